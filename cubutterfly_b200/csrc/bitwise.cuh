@@ -1,0 +1,242 @@
+// bitwise.cuh -- FWHT and subset/superset zeta kernels for sm_100a.
+//
+// Both transforms are products of commuting per-bit stages: stage b pairs the
+// elements whose indices differ in bit b.  The reference runs them stage by
+// stage (FwhtOperator / BooleanZetaOperator, src/operator_traits.cuh:88-112 and
+// :364-398; reference_fwht / reference_subset_zeta, butterfly_reference.cpp:349,
+// :475).  Because the stages commute, this kernel applies any set of index bits
+// in one pass over a TILE of 2^(LOGH+LOGW) elements: LOGH transformed "row"
+// bits over W = 2^LOGW contiguous, untouched "column" positions.  Each thread
+// holds E = 2^LOGE values in registers; the tile's bits are covered by a few
+// register groups: group 1 is loaded straight from HBM with 16-byte vectors
+// (bits 0..LOGV-1 plus the top bits), later groups are reached through one
+// shared-memory exchange each.  A transform longer than one tile runs as
+// several tile passes (a contiguous pass over the low bits, then strided
+// passes over the high bits with coalesced column blocks), each pass reading
+// and writing HBM once.
+#pragma once
+
+#include "common.cuh"
+
+namespace cubf::bw {
+
+// ---- operators --------------------------------------------------------------
+// apply(lo, hi): lo has the stage bit clear, hi has it set.
+struct FwhtOp {
+    template <typename T>
+    static CUBF_DEV void apply(T& lo, T& hi, int) {
+        const T a = lo, b = hi;
+        lo = a + b;
+        hi = a - b;
+    }
+};
+template <bool SUPERSET>
+struct ZetaOp {
+    // subset: f[S | bit] += f[S]; superset: f[S] += f[S | bit]; inverse subtracts.
+    template <typename T>
+    static CUBF_DEV void apply(T& lo, T& hi, int inverse) {
+        if constexpr (SUPERSET)
+            lo = inverse ? lo - hi : lo + hi;
+        else
+            hi = inverse ? hi - lo : hi + lo;
+    }
+};
+
+// ---- register-group plan (compile time) -------------------------------------
+struct Groups {
+    uint32_t reg[4];    // tile-index bits held in registers by each group
+    uint32_t stage[4];  // bits transformed while in that group
+    int count;
+};
+
+constexpr int log2_const(int x) {
+    int l = 0;
+    while ((1 << l) < x) ++l;
+    return l;
+}
+
+template <int LOGH, int LOGW, int LOGE, int LOGV>
+constexpr Groups make_groups() {
+    Groups g{};
+    constexpr int LT = LOGH + LOGW;
+    const uint32_t transform = lowmask(LOGH) << LOGW;
+    const uint32_t g1 = lowmask(LOGV) | (lowmask(LOGE - LOGV) << (LT - (LOGE - LOGV)));
+    g.reg[0] = g1;
+    g.stage[0] = g1 & transform;
+    uint32_t done = g.stage[0];
+    int k = 1;
+    while ((transform & ~done) != 0u && k < 4) {
+        const uint32_t rem = transform & ~done;
+        uint32_t take = 0;
+        int cnt = 0;
+        for (int b = 0; b < LT && cnt < LOGE; ++b)
+            if ((rem >> b) & 1u) {
+                take |= 1u << b;
+                ++cnt;
+            }
+        uint32_t reg = take;
+        // Fill the group with low bits first so the final store can vectorise.
+        for (int b = 0; b < LT && cnt < LOGE; ++b)
+            if (!((reg >> b) & 1u)) {
+                reg |= 1u << b;
+                ++cnt;
+            }
+        g.reg[k] = reg;
+        g.stage[k] = take;
+        done |= take;
+        ++k;
+    }
+    g.count = k;
+    return g;
+}
+
+template <typename TS_, typename TC_, int LOGH_, int LOGW_, int LOGE_>
+struct TileShape {
+    using TS = TS_;
+    using TC = TC_;
+    static constexpr int LOGH = LOGH_;
+    static constexpr int LOGW = LOGW_;
+    static constexpr int LT = LOGH + LOGW;
+    static constexpr int LOGE = LOGE_ < LT ? LOGE_ : LT;
+    static constexpr int E = 1 << LOGE;
+    static constexpr int TPT = 1 << (LT - LOGE);  // threads per tile
+    static constexpr int VEC_BITS = log2_const(16 / sizeof(TS));
+    // Vector loads need bits 0..LOGV-1 contiguous in memory.
+    // 16-byte vectors only: bits 0..VEC_BITS-1 must be register bits and be
+    // contiguous in memory (contiguous tiles, or at least that many columns).
+    static constexpr int LOGV = (LOGE >= VEC_BITS && (LOGW == 0 || LOGW >= VEC_BITS)) ? VEC_BITS : 0;
+    static constexpr int V = 1 << LOGV;
+    static constexpr Groups G = make_groups<LOGH, LOGW, LOGE, LOGV>();
+    static constexpr int TPB = TPT >= 128 ? TPT : 128;
+    static constexpr int TILES = TPB / TPT;  // tiles per CTA
+    static constexpr int BANK_SHIFT = sizeof(TC) == 8 ? 4 : 5;
+    static constexpr int PADDED = (1 << LT) + ((1 << LT) >> BANK_SHIFT);
+    static constexpr int SMEM_BYTES = G.count > 1 ? TILES * PADDED * static_cast<int>(sizeof(TC)) : 0;
+    static CUBF_DEV int pad(uint32_t e) { return static_cast<int>(e + (e >> BANK_SHIFT)); }
+    // Final group stores 16-byte vectors when it holds bits 0..LOGV-1.
+    static constexpr bool VEC_STORE = LOGV > 0 && (G.reg[G.count - 1] & lowmask(LOGV)) == lowmask(LOGV);
+};
+
+// Apply the stages STAGE (tile-index bits) of a group whose registers hold the
+// tile-index bits REG: register bit j pairs v[r] with v[r | 1 << j].
+template <typename Op, int LOGE, uint32_t REG, uint32_t STAGE, typename TC>
+CUBF_DEV void apply_group(TC (&v)[1 << LOGE], int inverse) {
+    constexpr uint32_t RSTAGE = extract(STAGE, REG);
+#pragma unroll
+    for (int j = 0; j < LOGE; ++j) {
+        if ((RSTAGE >> j) & 1u) {
+#pragma unroll
+            for (int r = 0; r < (1 << LOGE); ++r)
+                if (!((r >> j) & 1)) Op::apply(v[r], v[r | (1 << j)], inverse);
+        }
+    }
+}
+
+// Shared-memory exchange into group K and its stages, then the rest.
+template <typename Op, typename S, int K>
+CUBF_DEV void exchange_groups(typename S::TC (&v)[S::E], typename S::TC* tbuf, uint32_t t, int inverse) {
+    if constexpr (K < S::G.count) {
+        constexpr uint32_t RP = S::G.reg[K - 1];
+        constexpr uint32_t RN = S::G.reg[K];
+        constexpr Offsets<S::E> OP = make_offsets<S::E>(RP);
+        constexpr Offsets<S::E> ON = make_offsets<S::E>(RN);
+        if constexpr (K > 1) __syncthreads();  // previous exchange's reads are done
+        const uint32_t tp = deposit_rt<lowmask(S::LT) & ~RP, S::LT>(t);
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) tbuf[S::pad(tp | OP.v[r])] = v[r];
+        __syncthreads();
+        const uint32_t tn = deposit_rt<lowmask(S::LT) & ~RN, S::LT>(t);
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) v[r] = tbuf[S::pad(tn | ON.v[r])];
+        apply_group<Op, S::LOGE, RN, S::G.stage[K]>(v, inverse);
+        exchange_groups<Op, S, K + 1>(v, tbuf, t, inverse);
+    }
+}
+
+// One tile pass.  The input is `outer` independent arrays of H x 2^log_inner
+// elements (H = 2^LOGH transformed rows, row stride 2^log_inner); a tile is H
+// rows by W = 2^LOGW adjacent columns.  LOGW == 0 is the contiguous case (row
+// stride 1, log_inner ignored).  `in` and `out` may alias (every tile reads all its elements before
+// writing any).  Floating-point results are multiplied by `scale` before the
+// final narrowing (the FINAL_STORAGE epilogue).
+template <typename Op, typename TS, typename TC, int LOGH, int LOGW, int LOGE>
+__global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
+    bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale) {
+    using S = TileShape<TS, TC, LOGH, LOGW, LOGE>;
+    constexpr Groups G = S::G;
+    constexpr int LT = S::LT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    TC* smem = reinterpret_cast<TC*>(smem_raw);
+
+    const int local = threadIdx.x / S::TPT;
+    const uint32_t t = threadIdx.x % S::TPT;
+    // Contiguous tiles (LOGW == 0) have row stride 1; strided tiles 2^log_inner.
+    const int li = LOGW == 0 ? 0 : log_inner;
+    const size_t col_blocks = size_t{1} << (li - LOGW);
+    const size_t tile = static_cast<size_t>(blockIdx.x) * S::TILES + local;
+    const bool active = tile < outer * col_blocks;
+    const size_t o = active ? tile >> (li - LOGW) : 0;
+    const size_t cb = active ? tile & (col_blocks - 1) : 0;
+    const size_t base = (o << (li + LOGH)) + (cb << LOGW);
+    const TS* tin = in + base;
+    TS* tout = out + base;
+    // Offset of tile element e from the tile base (32-bit: tiles are < 2^31 elements apart only in base).
+    auto addr = [&](uint32_t e) -> size_t {
+        if constexpr (LOGW == 0)
+            return e;
+        else
+            return (static_cast<size_t>(e >> LOGW) << li) + (e & lowmask(LOGW));
+    };
+    TC* tbuf = smem + local * S::PADDED;
+
+    TC v[S::E];
+    {  // group 1: 16-byte vector loads along bits 0..LOGV-1
+        constexpr uint32_t R0 = G.reg[0];
+        constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
+        const uint32_t te = deposit_rt<lowmask(LT) & ~R0, LT>(t);
+#pragma unroll
+        for (int q = 0; q < S::E / S::V; ++q) {
+            const uint32_t e = te | O0.v[q * S::V];
+            if constexpr (S::V > 1) {
+                Vec16<TS> x;
+                if (active) {
+                    x = ldg_stream(reinterpret_cast<const Vec16<TS>*>(tin + addr(e)));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < S::V; ++i) x.v[i] = TS{};
+                }
+#pragma unroll
+                for (int i = 0; i < S::V; ++i) v[q * S::V + i] = Convert<TS, TC>::load(x.v[i]);
+            } else {
+                v[q] = Convert<TS, TC>::load(active ? tin[addr(e)] : TS{});
+            }
+        }
+    }
+    apply_group<Op, S::LOGE, G.reg[0], G.stage[0]>(v, inverse);
+    exchange_groups<Op, S, 1>(v, tbuf, t, inverse);
+
+    if (!active) return;
+    constexpr uint32_t RF = G.reg[G.count - 1];
+    constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
+    const uint32_t tf = deposit_rt<lowmask(LT) & ~RF, LT>(t);
+    auto narrow = [&](TC x) -> TS {
+        if constexpr (std::is_floating_point<TC>::value)
+            return Convert<TS, TC>::store(x * scale);
+        else
+            return Convert<TS, TC>::store(x);
+    };
+    if constexpr (S::VEC_STORE) {
+#pragma unroll
+        for (int q = 0; q < S::E / S::V; ++q) {
+            Vec16<TS> x;
+#pragma unroll
+            for (int i = 0; i < S::V; ++i) x.v[i] = narrow(v[q * S::V + i]);
+            stg_stream(reinterpret_cast<Vec16<TS>*>(tout + addr(tf | OF.v[q * S::V])), x);
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) tout[addr(tf | OF.v[r])] = narrow(v[r]);
+    }
+}
+
+}  // namespace cubf::bw

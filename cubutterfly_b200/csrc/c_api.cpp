@@ -1,0 +1,771 @@
+// c_api.cpp -- the cubutterfly* C ABI over the B200 planner and kernels.
+//
+// Contract (reference src/c_api.cpp): exceptions never cross the ABI;
+// protect() maps them to status codes with a thread-local last error
+// (reference c_api.cpp:121-163); string queries use the two-call NULL-buffer
+// protocol (:497-520); workspace is caller-owned (:4890-4995); execution is
+// asynchronous on the handle stream, allocation-free, with the in-place /
+// out-of-place pointer rule (:5002-5004).
+#include <cubutterfly/cubutterfly.h>
+#include <cubutterfly/cubutterfly_b200.h>
+
+#include "descriptor.hpp"
+#include "kernels.hpp"
+#include "planner.hpp"
+
+#include <cuda_runtime_api.h>
+#include <fcntl.h>
+#include <sys/file.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <mutex>
+#include <new>
+#include <sstream>
+#include <string>
+#include <vector>
+
+struct cubutterflyHandle {
+    cudaStream_t stream = nullptr;
+    cubutterflyLogCallback_t logger = nullptr;
+    void* logger_data = nullptr;
+    std::string cache_path;
+};
+
+struct cubutterflyPlan {
+    cubf::Descriptor desc;
+    cubf::PlanRequest req;
+    cubf::Mapping mapping;
+    cubf::HardwareProfile hw;
+    cubutterflySelectionSource_t source = CUBUTTERFLY_SELECTION_STATIC_MODEL;
+    std::string reason;
+    std::size_t input_bytes = 0;
+    std::size_t output_bytes = 0;
+    void* workspace = nullptr;
+    std::size_t workspace_size = 0;
+    void* twiddles = nullptr;  // FFT: W_N^k, k < N, complex fp32
+    int device = 0;
+    cudaStream_t steady_stream = nullptr;
+    bool steady_ready = false;
+    ~cubutterflyPlan() {
+        if (twiddles) cudaFree(twiddles);
+    }
+};
+
+namespace {
+
+thread_local std::string last_error;
+
+struct CudaFailure : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+void check_cuda(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        throw CudaFailure(std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+template <typename F>
+cubutterflyStatus_t protect(F&& body) noexcept {
+    try {
+        last_error.clear();
+        body();
+        return CUBUTTERFLY_STATUS_SUCCESS;
+    } catch (const cubf::Unsupported& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_NOT_SUPPORTED;
+    } catch (const CudaFailure& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_CUDA_ERROR;
+    } catch (const std::invalid_argument& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_INVALID_VALUE;
+    } catch (const std::overflow_error& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_INVALID_VALUE;
+    } catch (const std::bad_alloc& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_ALLOC_FAILED;
+    } catch (const nlohmann::json::exception& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_INVALID_VALUE;
+    } catch (const std::logic_error& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_INTERNAL_ERROR;
+    } catch (const std::runtime_error& e) {
+        last_error = e.what();
+        return CUBUTTERFLY_STATUS_BACKEND_ERROR;
+    } catch (...) {
+        last_error = "unrecognized exception";
+        return CUBUTTERFLY_STATUS_INTERNAL_ERROR;
+    }
+}
+
+using cubf::require;
+
+void copy_text(const std::string& value, char* dst, std::size_t* bytes) {
+    require(bytes != nullptr, "size query pointer must be non-null");
+    const std::size_t need = value.size() + 1;
+    if (dst == nullptr) {
+        *bytes = need;
+        return;
+    }
+    require(*bytes >= need, "destination string buffer is too small");
+    std::memcpy(dst, value.c_str(), need);
+    *bytes = need;
+}
+
+cubf::Descriptor& desc_of(cubutterflyDescriptor_t d) {
+    require(d != nullptr, "descriptor must be non-null");
+    return *d;
+}
+
+void log_event(const cubutterflyHandle* h, cubutterflyLogLevel_t level, const char* event, const std::string& msg) {
+    if (h && h->logger) h->logger(level, event, msg.c_str(), h->logger_data);
+}
+
+// ---- plan cache: {"schema", "entries": {key: mapping-json}} ------------------
+std::string workload_key(const cubutterflyPlan& p) {
+    std::ostringstream o;
+    o << cubf::semantic_json(p.desc).dump() << "|" << p.hw.fingerprint();
+    return o.str();
+}
+
+class FileLock {
+  public:
+    explicit FileLock(const std::string& path) {
+        fd_ = ::open((path + ".lock").c_str(), O_CREAT | O_RDWR, 0644);
+        if (fd_ >= 0) ::flock(fd_, LOCK_EX);
+    }
+    ~FileLock() {
+        if (fd_ >= 0) {
+            ::flock(fd_, LOCK_UN);
+            ::close(fd_);
+        }
+    }
+
+  private:
+    int fd_ = -1;
+};
+
+cubf::Json read_cache(const std::string& path) {
+    std::ifstream in(path);
+    if (!in) return {{"schema", "cubutterfly-b200-plan-cache-v1"}, {"entries", cubf::Json::object()}};
+    cubf::Json j;
+    in >> j;
+    require(j.is_object() && j.value("schema", "") == "cubutterfly-b200-plan-cache-v1" && j.contains("entries"),
+            "plan cache file has an unknown format: " + path);
+    return j;
+}
+
+bool lookup_cache(const std::string& path, const std::string& key, std::string& mapping) {
+    if (path.empty()) return false;
+    FileLock lock(path);
+    const cubf::Json j = read_cache(path);
+    const auto& e = j.at("entries");
+    if (!e.contains(key)) return false;
+    mapping = e.at(key).at("mapping").dump();
+    return true;
+}
+
+void store_cache(const std::string& path, const std::string& key, const cubf::Mapping& m, double us) {
+    if (path.empty()) return;
+    FileLock lock(path);
+    cubf::Json j = read_cache(path);
+    j["entries"][key] = {{"mapping", m.to_json()}, {"measured_us", us}};
+    const std::string tmp = path + ".tmp";
+    {
+        std::ofstream out(tmp, std::ios::trunc);
+        require(static_cast<bool>(out), "cannot write plan cache " + path);
+        out << j.dump(1) << "\n";
+    }
+    require(std::rename(tmp.c_str(), path.c_str()) == 0, "cannot publish plan cache " + path);
+}
+
+// ---- execution ----------------------------------------------------------------
+void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
+                    cudaStream_t stream) {
+    const auto& d = p.desc;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    const std::size_t n = d.extents[0];
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
+        const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
+        check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream),
+                   "FFT launch");
+        return;
+    }
+    // Bitwise tile passes: the first reads the input, the rest run in place.
+    double scale = 1.0;
+    if (d.op == CUBUTTERFLY_OPERATOR_FWHT) {
+        scale = d.output_scale;
+        if (inverse && d.normalize_inverse) scale /= static_cast<double>(n);
+    }
+    const void* src = in;
+    for (std::size_t i = 0; i < m.passes.size(); ++i) {
+        const auto& ps = m.passes[i];
+        const bool last = i + 1 == m.passes.size();
+        const std::size_t inner = std::size_t{1} << ps.log_inner;
+        const std::size_t outer = d.batch * (n >> (ps.log_inner + ps.log_h));
+        const std::size_t inner_arg = ps.log_w == 0 ? 1 : inner;
+        const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
+        check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, out, outer_arg, inner_arg,
+                                   inverse, last ? static_cast<float>(scale) : 1.0f, stream),
+                   "tile pass launch");
+        src = out;
+    }
+}
+
+double time_mapping(cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream,
+                    int reps) {
+    cudaEvent_t a, b;
+    check_cuda(cudaEventCreate(&a), "event");
+    check_cuda(cudaEventCreate(&b), "event");
+    launch_mapping(p, m, in, out, stream);  // warm-up
+    check_cuda(cudaEventRecord(a, stream), "event record");
+    for (int i = 0; i < reps; ++i) launch_mapping(p, m, in, out, stream);
+    check_cuda(cudaEventRecord(b, stream), "event record");
+    check_cuda(cudaEventSynchronize(b), "event sync");
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    return 1000.0 * ms / reps;
+}
+
+void build_tables(cubutterflyPlan& p) {
+    if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
+    const std::size_t n = p.desc.extents[0];
+    std::vector<float> tw(2 * n);
+    constexpr double kPi = 3.141592653589793238462643383279502884;
+    for (std::size_t k = 0; k < n; ++k) {
+        // exp(-2 pi i k / N) in double, rounded once (reference butterfly.cu:1502-1514)
+        const double a = -2.0 * kPi * static_cast<double>(k) / static_cast<double>(n);
+        tw[2 * k] = static_cast<float>(std::cos(a));
+        tw[2 * k + 1] = static_cast<float>(std::sin(a));
+    }
+    check_cuda(cudaMalloc(&p.twiddles, tw.size() * sizeof(float)), "twiddle table allocation");
+    check_cuda(cudaMemcpy(p.twiddles, tw.data(), tw.size() * sizeof(float), cudaMemcpyHostToDevice),
+               "twiddle table upload");
+}
+
+cubf::PlanRequest make_request(const cubf::Descriptor& d) {
+    cubf::PlanRequest r;
+    r.d = d;
+    r.log_n = static_cast<int>(cubf::log2_exact(d.extents[0]));
+    switch (d.op) {
+        case CUBUTTERFLY_OPERATOR_FWHT:
+            r.bw_op = cubf::BwOp::Fwht;
+            r.bw_type = d.storage == CUBUTTERFLY_DATA_BF16   ? cubf::BwType::BF16
+                        : d.storage == CUBUTTERFLY_DATA_FP16 ? cubf::BwType::F16
+                                                             : cubf::BwType::F32;
+            break;
+        case CUBUTTERFLY_OPERATOR_SUBSET_ZETA:
+        case CUBUTTERFLY_OPERATOR_SUPERSET_ZETA:
+            r.bw_op = d.op == CUBUTTERFLY_OPERATOR_SUBSET_ZETA ? cubf::BwOp::ZetaSubset : cubf::BwOp::ZetaSuperset;
+            r.bw_type = d.storage == CUBUTTERFLY_DATA_UINT64 ? cubf::BwType::U64 : cubf::BwType::U32;
+            break;
+        default:
+            break;
+    }
+    return r;
+}
+
+void select_mapping(cubutterflyHandle* h, cubutterflyPlan& p) {
+    const auto& d = p.desc;
+    if (d.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
+        p.mapping = cubf::parse_explicit_mapping(p.req, p.hw, d.explicit_algorithm);
+        p.source = CUBUTTERFLY_SELECTION_EXPLICIT;
+        p.reason = "explicit mapping " + p.mapping.name();
+        return;
+    }
+    auto ranked = cubf::enumerate_mappings(p.req, p.hw);
+    if (d.algorithm_policy == CUBUTTERFLY_ALGORITHM_DEFAULT) {
+        std::string cached;
+        if (h && lookup_cache(h->cache_path, workload_key(p), cached)) {
+            p.mapping = cubf::parse_explicit_mapping(p.req, p.hw, cached);
+            p.source = CUBUTTERFLY_SELECTION_USER_CACHE;
+            p.reason = "plan cache hit " + p.mapping.name();
+            return;
+        }
+        p.mapping = ranked.front();
+        p.source = CUBUTTERFLY_SELECTION_STATIC_MODEL;
+        std::ostringstream o;
+        o << "static roofline model over " << ranked.size() << " partitions on " << p.hw.name << " ("
+          << p.hw.source << "): " << p.mapping.name() << " predicted " << p.mapping.predicted_us << " us";
+        p.reason = o.str();
+        return;
+    }
+    // MEASURE: time up to four finalists on private device buffers.
+    const std::size_t finalists = std::min<std::size_t>(4, ranked.size());
+    const std::size_t bytes = std::max(p.input_bytes, p.output_bytes);
+    void* a = nullptr;
+    void* b = nullptr;
+    check_cuda(cudaMalloc(&a, bytes), "measure buffer");
+    std::unique_ptr<void, void (*)(void*)> ga(a, [](void* x) { cudaFree(x); });
+    check_cuda(cudaMalloc(&b, bytes), "measure buffer");
+    std::unique_ptr<void, void (*)(void*)> gb(b, [](void* x) { cudaFree(x); });
+    check_cuda(cudaMemset(a, 0, bytes), "measure buffer init");
+    cudaStream_t s = h ? h->stream : nullptr;
+    double best = 1e300;
+    std::size_t best_i = 0;
+    for (std::size_t i = 0; i < finalists; ++i) {
+        const double us = time_mapping(p, ranked[i], a, b, s, 5);
+        if (us < best) {
+            best = us;
+            best_i = i;
+        }
+    }
+    p.mapping = ranked[best_i];
+    p.source = CUBUTTERFLY_SELECTION_RUNTIME_MEASURED;
+    std::ostringstream o;
+    o << "measured " << finalists << " finalists: " << p.mapping.name() << " " << best << " us";
+    p.reason = o.str();
+    if (h) store_cache(h->cache_path, workload_key(p), p.mapping, best);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cubutterflyGetStatusString(cubutterflyStatus_t status) {
+    switch (status) {
+        case CUBUTTERFLY_STATUS_SUCCESS: return "CUBUTTERFLY_STATUS_SUCCESS";
+        case CUBUTTERFLY_STATUS_INVALID_VALUE: return "CUBUTTERFLY_STATUS_INVALID_VALUE";
+        case CUBUTTERFLY_STATUS_INVALID_TYPE: return "CUBUTTERFLY_STATUS_INVALID_TYPE";
+        case CUBUTTERFLY_STATUS_NOT_SUPPORTED: return "CUBUTTERFLY_STATUS_NOT_SUPPORTED";
+        case CUBUTTERFLY_STATUS_ALLOC_FAILED: return "CUBUTTERFLY_STATUS_ALLOC_FAILED";
+        case CUBUTTERFLY_STATUS_CUDA_ERROR: return "CUBUTTERFLY_STATUS_CUDA_ERROR";
+        case CUBUTTERFLY_STATUS_BACKEND_ERROR: return "CUBUTTERFLY_STATUS_BACKEND_ERROR";
+        case CUBUTTERFLY_STATUS_INTERNAL_ERROR: return "CUBUTTERFLY_STATUS_INTERNAL_ERROR";
+    }
+    return "CUBUTTERFLY_STATUS_UNKNOWN";
+}
+
+const char* cubutterflyGetLastErrorString(void) { return last_error.c_str(); }
+
+cubutterflyStatus_t cubutterflyGetVersion(int* major, int* minor, int* patch) {
+    return protect([&] {
+        require(major && minor && patch, "version pointers must be non-null");
+        *major = CUBUTTERFLY_VERSION_MAJOR;
+        *minor = CUBUTTERFLY_VERSION_MINOR;
+        *patch = CUBUTTERFLY_VERSION_PATCH;
+    });
+}
+
+cubutterflyStatus_t cubutterflyCreate(cubutterflyHandle_t* handle) {
+    return protect([&] {
+        require(handle != nullptr, "handle pointer must be non-null");
+        *handle = new cubutterflyHandle();
+    });
+}
+
+cubutterflyStatus_t cubutterflyDestroy(cubutterflyHandle_t handle) {
+    return protect([&] { delete handle; });
+}
+
+cubutterflyStatus_t cubutterflySetStream(cubutterflyHandle_t handle, cudaStream_t stream) {
+    return protect([&] {
+        require(handle != nullptr, "handle must be non-null");
+        handle->stream = stream;
+    });
+}
+
+cubutterflyStatus_t cubutterflyGetStream(cubutterflyHandle_t handle, cudaStream_t* stream) {
+    return protect([&] {
+        require(handle != nullptr && stream != nullptr, "handle and stream pointer must be non-null");
+        *stream = handle->stream;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetLogCallback(cubutterflyHandle_t handle, cubutterflyLogCallback_t callback,
+                                              void* user_data) {
+    return protect([&] {
+        require(handle != nullptr, "handle must be non-null");
+        handle->logger = callback;
+        handle->logger_data = user_data;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetCachePath(cubutterflyHandle_t handle, const char* path) {
+    return protect([&] {
+        require(handle != nullptr, "handle must be non-null");
+        handle->cache_path = path ? path : "";
+    });
+}
+
+int cubutterflyPackRealFp32(const float*, void*, size_t, float, uint64_t) {
+    last_error = "real-FFT packing is not built in cubutterfly_b200";
+    return CUBUTTERFLY_STATUS_NOT_SUPPORTED;
+}
+
+int cubutterflyExpandHermitianFp32(const void*, void*, uint32_t, uint32_t, size_t, uint64_t) {
+    last_error = "Hermitian expansion is not built in cubutterfly_b200";
+    return CUBUTTERFLY_STATUS_NOT_SUPPORTED;
+}
+
+cubutterflyStatus_t cubutterflyCreateDescriptor(cubutterflyDescriptor_t* descriptor) {
+    return protect([&] {
+        require(descriptor != nullptr, "descriptor pointer must be non-null");
+        *descriptor = new cubutterflyDescriptor();
+    });
+}
+
+cubutterflyStatus_t cubutterflyDestroyDescriptor(cubutterflyDescriptor_t descriptor) {
+    return protect([&] { delete descriptor; });
+}
+
+cubutterflyStatus_t cubutterflySetOperator(cubutterflyDescriptor_t d, cubutterflyOperator_t op) {
+    return protect([&] {
+        require(static_cast<int>(op) >= 0 && static_cast<int>(op) <= 5, "invalid operator");
+        desc_of(d).op = op;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetDataType(cubutterflyDescriptor_t d, cubutterflyDataType_t storage,
+                                           cubutterflyComputeType_t compute) {
+    return protect([&] {
+        require(static_cast<int>(storage) >= 0 && static_cast<int>(storage) <= 9, "invalid storage type");
+        require(static_cast<int>(compute) >= 0 && static_cast<int>(compute) <= 4, "invalid compute type");
+        desc_of(d).storage = storage;
+        desc_of(d).compute = compute;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetShape(cubutterflyDescriptor_t d, uint32_t rank, const size_t* extents,
+                                        size_t batch) {
+    return protect([&] {
+        require(rank > 0 && extents != nullptr, "rank must be positive and extents non-null");
+        require(batch > 0, "batch must be positive");
+        auto& x = desc_of(d);
+        x.rank = rank;
+        x.extents.assign(extents, extents + rank);
+        x.batch = batch;
+        x.input_strides.clear();
+        x.output_strides.clear();
+        x.input_orders.clear();
+        x.output_orders.clear();
+        x.stage_matrices.assign(std::max<std::size_t>(3, rank), {});
+    });
+}
+
+cubutterflyStatus_t cubutterflySetExecutionMode(cubutterflyDescriptor_t d, cubutterflyExecutionMode_t mode) {
+    return protect([&] {
+        require(static_cast<int>(mode) >= 0 && static_cast<int>(mode) <= 2, "invalid execution mode");
+        desc_of(d).execution_mode = mode;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetFftTransformType(cubutterflyDescriptor_t d, cubutterflyFftTransformType_t type) {
+    return protect([&] {
+        require(static_cast<int>(type) >= 0 && static_cast<int>(type) <= 2, "invalid FFT transform type");
+        desc_of(d).fft_type = type;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetFftOutputScale(cubutterflyDescriptor_t d, double scale) {
+    return protect([&] {
+        require(std::isfinite(scale), "FFT output scale must be finite");
+        desc_of(d).fft_output_scale = scale;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetOutputScale(cubutterflyDescriptor_t d, double scale) {
+    return protect([&] {
+        require(std::isfinite(scale), "output scale must be finite");
+        desc_of(d).output_scale = scale;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetArithmeticPolicy(cubutterflyDescriptor_t d, cubutterflyArithmeticPolicy_t policy) {
+    return protect([&] {
+        require(static_cast<int>(policy) >= 0 && static_cast<int>(policy) <= 1, "invalid arithmetic policy");
+        desc_of(d).arithmetic_policy = policy;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetOutputRounding(cubutterflyDescriptor_t d, cubutterflyOutputRounding_t rounding) {
+    return protect([&] {
+        require(static_cast<int>(rounding) >= 0 && static_cast<int>(rounding) <= 1, "invalid output rounding");
+        desc_of(d).output_rounding = rounding;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetStrides(cubutterflyDescriptor_t d, const size_t* input_strides,
+                                          size_t input_batch_stride, const size_t* output_strides,
+                                          size_t output_batch_stride) {
+    return protect([&] {
+        auto& x = desc_of(d);
+        const std::size_t rank = x.extents.size();
+        x.input_strides = input_strides ? std::vector<std::size_t>(input_strides, input_strides + rank)
+                                        : std::vector<std::size_t>{};
+        x.output_strides = output_strides ? std::vector<std::size_t>(output_strides, output_strides + rank)
+                                          : std::vector<std::size_t>{};
+        x.input_batch_stride = input_batch_stride;
+        x.output_batch_stride = output_batch_stride;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetLogicalOrders(cubutterflyDescriptor_t d, const cubutterflyLogicalOrder_t* in,
+                                                const cubutterflyLogicalOrder_t* out) {
+    return protect([&] {
+        auto& x = desc_of(d);
+        const std::size_t rank = x.extents.size();
+        x.input_orders = in ? std::vector<cubutterflyLogicalOrder_t>(in, in + rank)
+                            : std::vector<cubutterflyLogicalOrder_t>{};
+        x.output_orders = out ? std::vector<cubutterflyLogicalOrder_t>(out, out + rank)
+                              : std::vector<cubutterflyLogicalOrder_t>{};
+    });
+}
+
+cubutterflyStatus_t cubutterflyDescriptorValidate(cubutterflyDescriptor_t d) {
+    return protect([&] { (void)cubf::normalize(desc_of(d)); });
+}
+
+cubutterflyStatus_t cubutterflyDescriptorGetJson(cubutterflyDescriptor_t d, char* json, size_t* bytes) {
+    return protect([&] { copy_text(cubf::descriptor_json(desc_of(d)).dump(), json, bytes); });
+}
+
+cubutterflyStatus_t cubutterflyDescriptorSetJson(cubutterflyDescriptor_t d, const char* json) {
+    return protect([&] {
+        require(json != nullptr, "JSON text must be non-null");
+        auto& x = desc_of(d);
+        cubf::Descriptor parsed = cubf::descriptor_from_json(cubf::Json::parse(json));
+        x = cubutterflyDescriptor{parsed};  // atomic replacement
+    });
+}
+
+cubutterflyStatus_t cubutterflyDescriptorGetCapabilities(cubutterflyDescriptor_t d, char* json, size_t* bytes) {
+    return protect([&] { copy_text(cubf::capabilities(desc_of(d)).dump(), json, bytes); });
+}
+
+cubutterflyStatus_t cubutterflySetDirection(cubutterflyDescriptor_t d, cubutterflyDirection_t direction,
+                                            int normalize_inverse) {
+    return protect([&] {
+        require(static_cast<int>(direction) >= 0 && static_cast<int>(direction) <= 1, "invalid direction");
+        desc_of(d).direction = direction;
+        desc_of(d).normalize_inverse = normalize_inverse != 0;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetPlacement(cubutterflyDescriptor_t d, cubutterflyPlacement_t placement) {
+    return protect([&] {
+        require(static_cast<int>(placement) >= 0 && static_cast<int>(placement) <= 1, "invalid placement");
+        desc_of(d).placement = placement;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetLengthMode(cubutterflyDescriptor_t d, cubutterflyLengthMode_t mode) {
+    return protect([&] {
+        require(static_cast<int>(mode) >= 0 && static_cast<int>(mode) <= 1, "invalid length mode");
+        desc_of(d).length_mode = mode;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetAlgorithmPolicy(cubutterflyDescriptor_t d, cubutterflyAlgorithmPolicy_t policy,
+                                                  const char* explicit_algorithm) {
+    return protect([&] {
+        require(static_cast<int>(policy) >= 0 && static_cast<int>(policy) <= 2, "invalid algorithm policy");
+        auto& x = desc_of(d);
+        x.algorithm_policy = policy;
+        x.explicit_algorithm = explicit_algorithm ? explicit_algorithm : "";
+    });
+}
+
+cubutterflyStatus_t cubutterflySetModulus(cubutterflyDescriptor_t d, uint64_t modulus, uint32_t word_bits) {
+    return protect([&] {
+        require(word_bits == 32 || word_bits == 64, "word bits must be 32 or 64");
+        desc_of(d).modulus = modulus;
+        desc_of(d).word_bits = word_bits;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetNttLayouts(cubutterflyDescriptor_t d, cubutterflyNttLayout_t in,
+                                             cubutterflyNttLayout_t out) {
+    return protect([&] {
+        require(static_cast<int>(in) >= 0 && static_cast<int>(in) <= 2 && static_cast<int>(out) >= 0 &&
+                    static_cast<int>(out) <= 2,
+                "invalid NTT layout");
+        desc_of(d).input_ntt_layout = in;
+        desc_of(d).output_ntt_layout = out;
+    });
+}
+
+cubutterflyStatus_t cubutterflySetStageMatrices(cubutterflyDescriptor_t d, uint32_t axis,
+                                                const cubutterflyMatrix2x2_t* matrices, size_t count) {
+    return protect([&] {
+        auto& x = desc_of(d);
+        require(axis < x.rank, "matrix axis out of range");
+        require(count == 0 || matrices != nullptr, "matrices must be non-null");
+        if (x.stage_matrices.size() < std::max<std::size_t>(3, x.rank)) x.stage_matrices.resize(std::max<std::size_t>(3, x.rank));
+        x.stage_matrices[axis].assign(matrices, matrices + count);
+    });
+}
+
+cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterflyDescriptor_t descriptor,
+                                          cubutterflyPlan_t* plan) {
+    return protect([&] {
+        require(handle != nullptr && plan != nullptr, "handle and plan pointer must be non-null");
+        *plan = nullptr;
+        auto p = std::make_unique<cubutterflyPlan>();
+        p->desc = cubf::normalize(desc_of(descriptor));
+        const cubf::Json caps = cubf::capabilities(p->desc);
+        if (caps.at("status") != "eligible") {
+            const auto& gap = caps.at("gaps").at(0);
+            throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
+        }
+        const std::size_t esz = cubf::storage_bytes(p->desc.storage);
+        p->input_bytes = p->desc.batch * p->desc.input_batch_stride * esz;
+        p->output_bytes = p->desc.batch * p->desc.output_batch_stride * esz;
+        p->req = make_request(p->desc);
+        p->hw = cubf::resolve_profile();
+        check_cuda(cudaGetDevice(&p->device), "current device");
+        select_mapping(handle, *p);
+        build_tables(*p);
+        log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
+        *plan = p.release();
+    });
+}
+
+cubutterflyStatus_t cubutterflyDestroyPlan(cubutterflyPlan_t plan) {
+    return protect([&] { delete plan; });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetDescriptorJson(cubutterflyPlan_t plan, char* json, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr, "plan must be non-null");
+        copy_text(cubf::descriptor_json(plan->desc).dump(), json, bytes);
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetWorkspaceSize(cubutterflyPlan_t plan, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr && bytes != nullptr, "plan and size pointer must be non-null");
+        *bytes = plan->mapping.workspace_bytes;
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetInputSize(cubutterflyPlan_t plan, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr && bytes != nullptr, "plan and size pointer must be non-null");
+        *bytes = plan->input_bytes;
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetOutputSize(cubutterflyPlan_t plan, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr && bytes != nullptr, "plan and size pointer must be non-null");
+        *bytes = plan->output_bytes;
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetPhysicalExtents(cubutterflyPlan_t plan, size_t* extents, uint32_t capacity) {
+    return protect([&] {
+        require(plan != nullptr && extents != nullptr, "plan and extents must be non-null");
+        require(capacity >= plan->desc.rank, "extent capacity is smaller than the rank");
+        for (std::size_t a = 0; a < plan->desc.rank; ++a) extents[a] = plan->desc.extents[a];
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetSelectionSource(cubutterflyPlan_t plan, cubutterflySelectionSource_t* source) {
+    return protect([&] {
+        require(plan != nullptr && source != nullptr, "plan and source pointer must be non-null");
+        *source = plan->source;
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetAlgorithmName(cubutterflyPlan_t plan, char* name, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr, "plan must be non-null");
+        copy_text(plan->mapping.name(), name, bytes);
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetSelectionReason(cubutterflyPlan_t plan, char* reason, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr, "plan must be non-null");
+        copy_text(plan->reason, reason, bytes);
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetMappingJson(cubutterflyPlan_t plan, char* json, size_t* bytes) {
+    return protect([&] {
+        require(plan != nullptr, "plan must be non-null");
+        cubf::Json j = plan->mapping.to_json();
+        j["hardware"] = plan->hw.to_json();
+        copy_text(j.dump(), json, bytes);
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanGetNttLayoutInfo(cubutterflyPlan_t plan, cubutterflyNttLayoutInfo_t* info) {
+    return protect([&] {
+        require(plan != nullptr && info != nullptr, "plan and info must be non-null");
+        throw cubf::Unsupported("NTT layout info applies to main-ABI NTT plans, which this build serves through "
+                                "the RNS ABI");
+    });
+}
+
+cubutterflyStatus_t cubutterflyPlanSetWorkspace(cubutterflyPlan_t plan, void* workspace, size_t bytes) {
+    return protect([&] {
+        require(plan != nullptr, "plan must be non-null");
+        require(bytes >= plan->mapping.workspace_bytes, "workspace is smaller than the plan requires");
+        require(plan->mapping.workspace_bytes == 0 || workspace != nullptr, "workspace must be non-null");
+        require(reinterpret_cast<std::uintptr_t>(workspace) % 16 == 0, "workspace must be 16-byte aligned");
+        plan->workspace = workspace;
+        plan->workspace_size = bytes;
+    });
+}
+
+cubutterflyStatus_t cubutterflyExecute(cubutterflyHandle_t handle, cubutterflyPlan_t plan, const void* input,
+                                       void* output) {
+    return protect([&] {
+        require(handle != nullptr && plan != nullptr, "handle and plan must be non-null");
+        require(input != nullptr && output != nullptr, "input and output must be non-null");
+        const bool in_place = plan->desc.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
+        require(in_place == (input == output),
+                in_place ? "in-place plans require input == output" : "out-of-place plans require input != output");
+        require(plan->mapping.workspace_bytes == 0 || plan->workspace != nullptr, "plan workspace is not set");
+        require((reinterpret_cast<std::uintptr_t>(input) | reinterpret_cast<std::uintptr_t>(output)) % 16 == 0,
+                "input and output must be 16-byte aligned (the kernels move 16-byte vectors)");
+        launch_mapping(*plan, plan->mapping, input, output, handle->stream);
+        plan->steady_stream = handle->stream;
+        plan->steady_ready = true;
+    });
+}
+
+cubutterflyStatus_t cubutterflyExecuteSteady(cubutterflyHandle_t handle, cubutterflyPlan_t plan, const void* input,
+                                             void* output) {
+    if (!handle || !plan || !plan->steady_ready || plan->steady_stream != handle->stream)
+        return cubutterflyExecute(handle, plan, input, output);
+    return protect([&] {
+        const bool in_place = plan->desc.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
+        require(input != nullptr && output != nullptr && in_place == (input == output),
+                "pointer aliasing does not match the plan placement");
+        launch_mapping(*plan, plan->mapping, input, output, handle->stream);
+    });
+}
+
+cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descriptor, const char* hardware_json,
+                                               char* json, size_t* bytes) {
+    return protect([&] {
+        const cubf::Descriptor d = cubf::normalize(desc_of(descriptor));
+        const cubf::Json caps = cubf::capabilities(d);
+        if (caps.at("status") != "eligible") {
+            const auto& gap = caps.at("gaps").at(0);
+            throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
+        }
+        const cubf::HardwareProfile hw = hardware_json ? cubf::profile_from_json(cubf::Json::parse(hardware_json))
+                                                       : cubf::resolve_profile();
+        cubf::Json out = cubf::Json::array();
+        for (const auto& m : cubf::enumerate_mappings(make_request(d), hw)) out.push_back(m.to_json());
+        copy_text(out.dump(), json, bytes);
+    });
+}
+
+}  // extern "C"

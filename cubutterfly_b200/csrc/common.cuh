@@ -1,0 +1,134 @@
+// common.cuh -- device helpers shared by the sm_100a butterfly kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#define CUBF_DEV __device__ __forceinline__
+
+namespace cubf {
+
+// ---- compile-time bit helpers ------------------------------------------
+constexpr int popc32(uint32_t x) {
+    int c = 0;
+    for (int i = 0; i < 32; ++i) c += (x >> i) & 1u;
+    return c;
+}
+constexpr uint32_t lowmask(int n) { return n <= 0 ? 0u : (n >= 32 ? ~0u : ((1u << n) - 1u)); }
+// Bit position of the j-th set bit of m (j counted from the least significant).
+constexpr int nth_bit(uint32_t m, int j) {
+    for (int b = 0; b < 32; ++b)
+        if ((m >> b) & 1u) {
+            if (j == 0) return b;
+            --j;
+        }
+    return -1;
+}
+// Scatter the low bits of x into the set bits of m (parallel bit deposit).
+constexpr uint32_t deposit(uint32_t x, uint32_t m) {
+    uint32_t r = 0;
+    int src = 0;
+    for (int b = 0; b < 32; ++b)
+        if ((m >> b) & 1u) {
+            r |= ((x >> src) & 1u) << b;
+            ++src;
+        }
+    return r;
+}
+
+// Parallel bit extract: gather the bits of x selected by m into the low bits.
+constexpr uint32_t extract(uint32_t x, uint32_t m) {
+    uint32_t r = 0;
+    int dst = 0;
+    for (int b = 0; b < 32; ++b)
+        if ((m >> b) & 1u) {
+            r |= ((x >> b) & 1u) << dst;
+            ++dst;
+        }
+    return r;
+}
+
+// deposit(r, m) for every r < E, as a compile-time table (indexing it with an
+// unrolled loop counter folds to immediates).
+template <int E>
+struct Offsets {
+    uint32_t v[E];
+};
+template <int E>
+constexpr Offsets<E> make_offsets(uint32_t m) {
+    Offsets<E> o{};
+    for (int r = 0; r < E; ++r) o.v[r] = deposit(static_cast<uint32_t>(r), m);
+    return o;
+}
+
+// Runtime deposit of x into the compile-time mask M (unrolled; used once per
+// exchange group, not per element).
+template <uint32_t M, int BITS>
+CUBF_DEV uint32_t deposit_rt(uint32_t x) {
+    uint32_t r = 0;
+    int src = 0;
+#pragma unroll
+    for (int b = 0; b < BITS; ++b) {
+        if ((M >> b) & 1u) {
+            r |= ((x >> src) & 1u) << b;
+            ++src;
+        }
+    }
+    return r;
+}
+
+// ---- storage <-> compute conversions --------------------------------------
+template <typename S, typename C>
+struct Convert;
+template <>
+struct Convert<float, float> {
+    static CUBF_DEV float load(float x) { return x; }
+    static CUBF_DEV float store(float x) { return x; }
+};
+template <>
+struct Convert<__nv_bfloat16, float> {
+    static CUBF_DEV float load(__nv_bfloat16 x) { return __bfloat162float(x); }
+    static CUBF_DEV __nv_bfloat16 store(float x) { return __float2bfloat16_rn(x); }
+};
+template <>
+struct Convert<__half, float> {
+    static CUBF_DEV float load(__half x) { return __half2float(x); }
+    static CUBF_DEV __half store(float x) { return __float2half_rn(x); }
+};
+template <>
+struct Convert<uint32_t, uint32_t> {
+    static CUBF_DEV uint32_t load(uint32_t x) { return x; }
+    static CUBF_DEV uint32_t store(uint32_t x) { return x; }
+};
+template <>
+struct Convert<unsigned long long, unsigned long long> {
+    static CUBF_DEV unsigned long long load(unsigned long long x) { return x; }
+    static CUBF_DEV unsigned long long store(unsigned long long x) { return x; }
+};
+
+// 16-byte vector of storage elements.
+template <typename T>
+struct alignas(16) Vec16 {
+    static constexpr int N = 16 / sizeof(T);
+    T v[N];
+};
+
+// Streaming loads/stores: the transforms touch each byte once, so keep them
+// out of L1 and mark them evict-first in L2.
+template <typename T>
+CUBF_DEV Vec16<T> ldg_stream(const Vec16<T>* p) {
+    Vec16<T> r;
+    uint4 u = __ldcs(reinterpret_cast<const uint4*>(p));
+    *reinterpret_cast<uint4*>(&r) = u;
+    return r;
+}
+template <typename T>
+CUBF_DEV void stg_stream(Vec16<T>* p, const Vec16<T>& v) {
+    __stcs(reinterpret_cast<uint4*>(p), *reinterpret_cast<const uint4*>(&v));
+}
+
+}  // namespace cubf

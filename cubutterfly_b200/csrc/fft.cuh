@@ -1,0 +1,226 @@
+// fft.cuh -- complex fp32 FFT kernels for sm_100a (Stockham autosort).
+//
+// Semantics follow the reference FftOperator / reference_fft
+// (src/operator_traits.cuh:223-283, src/butterfly_reference.cpp:392-433):
+// X[k] = sum_n x[n] exp(-2 pi i n k / N) forward, +i inverse, optional 1/N.
+// The arithmetic organisation is new: Stockham autosort passes of radix 16
+// (register codelets built from radix-2 DIT splits with exact-rounded
+// constants), natural order in and out with no bit-reversal pass, one HBM
+// read and one HBM write per element, twiddles W_N^k from a table computed in
+// double on the host and rounded once to fp32 (as butterfly.cu:1502-1514).
+// The inverse transform is conj(FFT(conj(x))): the conjugation is folded into
+// the load and store so one set of forward kernels serves both directions.
+#pragma once
+
+#include "common.cuh"
+
+namespace cubf::fft {
+
+CUBF_DEV float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+CUBF_DEV float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+CUBF_DEV float2 cmul(float2 a, float2 b) {
+    return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+CUBF_DEV float2 conjf2(float2 a) { return make_float2(a.x, -a.y); }
+
+// W_16^k = exp(-2 pi i k / 16), k in [0, 16), as exact-rounded fp32 pairs.
+CUBF_DEV float2 w16(int k) {
+    constexpr float c1 = 0.923879532511286756128f;  // cos(pi/8)
+    constexpr float s1 = 0.382683432365089771728f;  // sin(pi/8)
+    constexpr float r2 = 0.707106781186547524401f;  // sqrt(2)/2
+    switch (k & 15) {
+        case 0: return make_float2(1.f, 0.f);
+        case 1: return make_float2(c1, -s1);
+        case 2: return make_float2(r2, -r2);
+        case 3: return make_float2(s1, -c1);
+        case 4: return make_float2(0.f, -1.f);
+        case 5: return make_float2(-s1, -c1);
+        case 6: return make_float2(-r2, -r2);
+        case 7: return make_float2(-c1, -s1);
+        case 8: return make_float2(-1.f, 0.f);
+        case 9: return make_float2(-c1, s1);
+        case 10: return make_float2(-r2, r2);
+        case 11: return make_float2(-s1, c1);
+        case 12: return make_float2(0.f, 1.f);
+        case 13: return make_float2(s1, c1);
+        case 14: return make_float2(r2, r2);
+        default: return make_float2(c1, s1);
+    }
+}
+
+// Multiply by W_16^k with the trivial cases free of multiplies.
+CUBF_DEV float2 mul_w16(float2 a, int k) {
+    switch (k & 15) {
+        case 0: return a;
+        case 4: return make_float2(a.y, -a.x);    // * -i
+        case 8: return make_float2(-a.x, -a.y);   // * -1
+        case 12: return make_float2(-a.y, a.x);   // * +i
+        default: return cmul(a, w16(k));
+    }
+}
+
+// In-register forward DFT of length R (R = 1, 2, 4, 8, 16) on v[0..R), natural
+// order in and out: X[k] = E[k] + W_R^k O[k], X[k + R/2] = E[k] - W_R^k O[k].
+template <int R>
+struct Dft {
+    static CUBF_DEV void run(float2* v) {
+        float2 e[R / 2], o[R / 2];
+#pragma unroll
+        for (int i = 0; i < R / 2; ++i) {
+            e[i] = v[2 * i];
+            o[i] = v[2 * i + 1];
+        }
+        Dft<R / 2>::run(e);
+        Dft<R / 2>::run(o);
+#pragma unroll
+        for (int k = 0; k < R / 2; ++k) {
+            const float2 t = mul_w16(o[k], k * (16 / R));
+            v[k] = cadd(e[k], t);
+            v[k + R / 2] = csub(e[k], t);
+        }
+    }
+};
+template <>
+struct Dft<2> {
+    static CUBF_DEV void run(float2* v) {
+        const float2 a = v[0], b = v[1];
+        v[0] = cadd(a, b);
+        v[1] = csub(a, b);
+    }
+};
+template <>
+struct Dft<1> {
+    static CUBF_DEV void run(float2*) {}
+};
+
+// Pass schedule of an in-CTA transform of 2^LOGN points: ceil(LOGN/4) passes,
+// radix bits balanced so every pass has radix <= 16.
+template <int LOGN>
+struct LocalShape {
+    static constexpr int N = 1 << LOGN;
+    static constexpr int LOGE = LOGN < 4 ? LOGN : 4;  // values held per thread (log)
+    static constexpr int E = 1 << LOGE;
+    static constexpr int T = N / E;  // threads per transform
+    static constexpr int NPASS = (LOGN + 3) / 4;
+    static constexpr int radix_bits(int p) { return LOGN / NPASS + (p < LOGN % NPASS ? 1 : 0); }
+    static constexpr int ns_bits(int p) {
+        int s = 0;
+        for (int i = 0; i < p; ++i) s += radix_bits(i);
+        return s;
+    }
+    // Shared-memory index with one float2 of padding per 16 (bank spread).
+    static CUBF_DEV int pad(int i) { return i + (i >> 4); }
+    static constexpr int PADDED = N + N / 16;
+    static constexpr int TPB = T >= 128 ? T : 128;  // threads per CTA
+    static constexpr int TPC = TPB / T;             // transforms per CTA
+    static constexpr bool DOUBLE_BUFFER = LOGN <= 12;
+    static constexpr int SMEM_BYTES = (DOUBLE_BUFFER ? 2 : 1) * TPC * PADDED * 8;
+};
+
+// One Stockham pass P of a 2^LOGN transform, split in two halves so the
+// caller can place a barrier between the reads and the writes of a pass:
+// load R values per sub-DFT, apply the inter-pass twiddle
+// W_{Ns R}^{(j mod Ns) r} = W_N^{(j mod Ns) r N/(Ns R)}, run the register DFT;
+// then store with the Stockham autosort index.
+template <int LOGN, int P, typename Load>
+CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const float2* __restrict__ tw, Load load) {
+    using S = LocalShape<LOGN>;
+    constexpr int RB = S::radix_bits(P);
+    constexpr int R = 1 << RB;
+    constexpr int NSB = S::ns_bits(P);
+    constexpr int NS = 1 << NSB;
+    constexpr int SUB = S::E / R;  // sub-DFTs per thread
+#pragma unroll
+    for (int u = 0; u < SUB; ++u) {
+        const int j = th + S::T * u;
+#pragma unroll
+        for (int r = 0; r < R; ++r) v[u * R + r] = load(j + r * (S::N / R));
+    }
+#pragma unroll
+    for (int u = 0; u < SUB; ++u) {
+        const int j = th + S::T * u;
+        if (NS > 1) {
+            const int jm = j & (NS - 1);
+#pragma unroll
+            for (int r = 1; r < R; ++r) {
+                const int k = (jm * r) << (LOGN - NSB - RB);
+                v[u * R + r] = cmul(v[u * R + r], __ldg(tw + k));
+            }
+        }
+        Dft<R>::run(&v[u * R]);
+    }
+}
+
+template <int LOGN, int P, typename Store>
+CUBF_DEV void pass_store(const float2 (&v)[LocalShape<LOGN>::E], int th, Store store) {
+    using S = LocalShape<LOGN>;
+    constexpr int RB = S::radix_bits(P);
+    constexpr int R = 1 << RB;
+    constexpr int NSB = S::ns_bits(P);
+    constexpr int NS = 1 << NSB;
+    constexpr int SUB = S::E / R;
+#pragma unroll
+    for (int u = 0; u < SUB; ++u) {
+        const int j = th + S::T * u;
+        const int base = ((j >> NSB) << (NSB + RB)) + (j & (NS - 1));
+#pragma unroll
+        for (int r = 0; r < R; ++r) store(base + r * NS, v[u * R + r]);
+    }
+}
+
+// Runs passes P..NPASS-1; pass 0 reads HBM, the last pass writes HBM, the
+// passes in between exchange through shared memory.
+template <int LOGN, int P>
+struct Passes {
+    template <typename GLoad, typename GStore>
+    static CUBF_DEV void run(float2 (&v)[LocalShape<LOGN>::E], int th, const float2* __restrict__ tw,
+                             float2* buf0, float2* buf1, GLoad gload, GStore gstore) {
+        using S = LocalShape<LOGN>;
+        if constexpr (P == 0) {
+            pass_load<LOGN, 0>(v, th, tw, gload);
+        } else {
+            const float2* rb = ((P - 1) & 1) ? buf1 : buf0;
+            pass_load<LOGN, P>(v, th, tw, [&](int i) { return rb[S::pad(i)]; });
+        }
+        if constexpr (P == S::NPASS - 1) {
+            pass_store<LOGN, P>(v, th, gstore);
+        } else {
+            if constexpr (!S::DOUBLE_BUFFER && P > 0) __syncthreads();  // reads done before overwrite
+            float2* wb = (P & 1) ? buf1 : buf0;
+            pass_store<LOGN, P>(v, th, [&](int i, float2 x) { wb[S::pad(i)] = x; });
+            __syncthreads();
+            Passes<LOGN, P + 1>::run(v, th, tw, buf0, buf1, gload, gstore);
+        }
+    }
+};
+
+// Whole transform in one CTA: batch rows of 2^LOGN packed complex64, natural
+// in/out.  `inverse` conjugates on load and store; `scale` multiplies outputs.
+template <int LOGN>
+__global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
+    fft_local_kernel(const float2* in, float2* out, size_t batch,
+                     const float2* __restrict__ tw, int inverse, float scale) {
+    using S = LocalShape<LOGN>;
+    extern __shared__ float2 smem[];
+    const int c = threadIdx.x / S::T;
+    const int th = threadIdx.x % S::T;
+    const size_t row = static_cast<size_t>(blockIdx.x) * S::TPC + c;
+    const bool active = row < batch;
+    const float2* src = in + row * S::N;
+    float2* dst = out + row * S::N;
+    float2* buf0 = smem + c * S::PADDED;
+    float2* buf1 = S::DOUBLE_BUFFER ? buf0 + S::TPC * S::PADDED : buf0;
+    const float sgn = inverse ? -1.f : 1.f;
+    float2 v[S::E];
+    auto gload = [&](int i) -> float2 {
+        float2 x = active ? __ldcs(src + i) : make_float2(0.f, 0.f);
+        x.y *= sgn;
+        return x;
+    };
+    auto gstore = [&](int i, float2 x) {
+        if (active) __stcs(dst + i, make_float2(x.x * scale, x.y * sgn * scale));
+    };
+    Passes<LOGN, 0>::run(v, th, tw, buf0, buf1, gload, gstore);
+}
+
+}  // namespace cubf::fft

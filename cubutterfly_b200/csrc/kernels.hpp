@@ -1,0 +1,81 @@
+// kernels.hpp -- host-side view of the compiled sm_100a kernel variants.
+//
+// Every kernel is a template instantiated for a fixed tile geometry; the
+// planner enumerates only the variants listed here and the executor launches
+// them through these functions.  No CUDA types beyond cudaStream_t appear.
+#pragma once
+
+#include <cuda_runtime_api.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+namespace cubf {
+
+struct LaunchShape {
+    int threads = 0;           // per CTA
+    int smem_bytes = 0;        // dynamic shared memory per CTA
+    int units_per_cta = 0;     // transforms / tiles handled by one CTA
+    int elems_per_thread = 0;  // register-resident values per thread
+    int exchanges = 0;         // shared-memory exchanges per tile
+};
+
+// ---- FFT (complex fp32) ------------------------------------------------------
+constexpr int kFftLocalMaxLog = 13;
+LaunchShape fft_local_shape(int log_n);
+cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
+                             bool inverse, float scale, cudaStream_t stream);
+
+// ---- FWHT / zeta tile passes --------------------------------------------------
+enum class BwOp { Fwht = 0, ZetaSubset = 1, ZetaSuperset = 2 };
+enum class BwType { F32 = 0, BF16 = 1, F16 = 2, U32 = 3, U64 = 4 };
+struct BwVariant {
+    BwOp op;
+    BwType type;
+    int log_h;  // transformed bits per tile
+    int log_w;  // adjacent columns per tile (0: contiguous rows)
+};
+const char* bw_type_name(BwType t);
+std::size_t bw_type_bytes(BwType t);
+// Fixed column width of strided passes for a storage type (64-byte segments).
+int bw_strided_log_w(BwType t);
+int bw_max_contiguous_log(BwType t);
+int bw_max_strided_log(BwType t);
+bool bw_available(const BwVariant& v);
+LaunchShape bw_shape(const BwVariant& v);
+// outer arrays of (2^log_h x inner) elements; the pass transforms the 2^log_h
+// axis.  in may equal out.
+cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
+                      bool inverse, float scale, cudaStream_t stream);
+
+// ---- RNS NTT tile passes --------------------------------------------------------
+struct NttPolyDesc {
+    std::uint64_t in_off;
+    std::uint64_t out_off;
+    std::uint32_t domain;
+    std::uint32_t pad_;
+};
+struct NttTables {
+    const std::uint64_t* roots;
+    const std::uint64_t* quotients;
+    const std::uint64_t* moduli;
+    const std::uint64_t* n_inv;
+    const std::uint64_t* n_inv_q;
+};
+struct NttVariant {
+    int log_n;     // transform length 2^log_n
+    bool strided;  // top bits (strided columns) or low bits (contiguous chunks)
+    bool inverse;
+};
+constexpr int kNttMinLog = 12;
+constexpr int kNttMaxLog = 20;
+inline int ntt_pass_bits(int log_n, bool strided) { return strided ? (log_n + 1) / 2 : log_n / 2; }
+bool ntt_available(const NttVariant& v);
+LaunchShape ntt_shape(const NttVariant& v);
+// One pass over all polynomials; polys is a DEVICE array of poly_count entries.
+cudaError_t launch_ntt_pass(const NttVariant& v, const std::uint64_t* in, std::uint64_t* out,
+                            const NttPolyDesc* polys, std::size_t poly_count, const NttTables& tables,
+                            bool in_is_out, bool final_scale, cudaStream_t stream);
+
+}  // namespace cubf

@@ -1,0 +1,137 @@
+// launch_bitwise.cu -- instantiations and launchers of the FWHT / zeta tile kernels.
+//
+// Compiled once per (operator, storage) pair: the translation unit is built
+// with CUBF_BW_OP and CUBF_BW_TYPE defined, so the instantiation sets compile
+// in parallel.  launch_bitwise_dispatch.cpp routes a BwVariant to the unit.
+#include "bitwise.cuh"
+#include "kernels.hpp"
+
+#ifndef CUBF_BW_OP
+#error "CUBF_BW_OP must be defined (0 fwht, 1 subset zeta, 2 superset zeta)"
+#endif
+#ifndef CUBF_BW_TYPE
+#error "CUBF_BW_TYPE must be defined (0 f32, 1 bf16, 2 f16, 3 u32, 4 u64)"
+#endif
+
+namespace cubf {
+namespace {
+
+#if CUBF_BW_OP == 0
+using Op = bw::FwhtOp;
+#elif CUBF_BW_OP == 1
+using Op = bw::ZetaOp<false>;
+#else
+using Op = bw::ZetaOp<true>;
+#endif
+
+#if CUBF_BW_TYPE == 0
+using TS = float;
+using TC = float;
+#elif CUBF_BW_TYPE == 1
+using TS = __nv_bfloat16;
+using TC = float;
+#elif CUBF_BW_TYPE == 2
+using TS = __half;
+using TC = float;
+#elif CUBF_BW_TYPE == 3
+using TS = uint32_t;
+using TC = uint32_t;
+#else
+using TS = unsigned long long;
+using TC = unsigned long long;
+#endif
+
+// Values per thread: 64 (LOGE 6) for 4-byte compute, 32 for 8-byte compute.
+constexpr int kLogE = sizeof(TC) == 8 ? 5 : 6;
+constexpr int kLogW = sizeof(TS) == 8 ? 3 : (sizeof(TS) == 4 ? 4 : 5);  // 64-byte column blocks
+constexpr int kMaxContig = sizeof(TC) == 8 ? 13 : 14;
+constexpr int kMaxStrided = sizeof(TC) == 8 ? 9 : 10;
+
+template <int LOGH, int LOGW>
+struct Entry {
+    using S = bw::TileShape<TS, TC, LOGH, LOGW, kLogE>;
+    static LaunchShape shape() {
+        LaunchShape s;
+        s.threads = S::TPB;
+        s.smem_bytes = S::SMEM_BYTES;
+        s.units_per_cta = S::TILES;
+        s.elems_per_thread = S::E;
+        s.exchanges = S::G.count - 1;
+        return s;
+    }
+    static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
+                              float scale, cudaStream_t stream) {
+        auto kernel = bw::bitwise_tile_kernel<Op, TS, TC, LOGH, LOGW, kLogE>;
+        static bool configured = false;
+        if (!configured && S::SMEM_BYTES > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+        }
+        configured = true;
+        if ((inner >> LOGW) == 0 || (inner & (inner - 1)) != 0) return cudaErrorInvalidValue;
+        if (LOGW == 0 && inner != 1) return cudaErrorInvalidValue;
+        int log_inner = 0;
+        while ((std::size_t{1} << log_inner) < inner) ++log_inner;
+        const std::size_t tiles = outer * (inner >> LOGW);
+        const std::size_t blocks = (tiles + S::TILES - 1) / S::TILES;
+        if (blocks == 0) return cudaSuccess;
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+            static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0, scale);
+        return cudaGetLastError();
+    }
+};
+
+using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, cudaStream_t);
+using ShapeFn = LaunchShape (*)();
+
+template <int... H>
+struct Contig {
+    static constexpr LaunchFn launch[] = {Entry<H, 0>::launch...};
+    static constexpr ShapeFn shape[] = {Entry<H, 0>::shape...};
+};
+template <int... H>
+struct Strided {
+    static constexpr LaunchFn launch[] = {Entry<H, kLogW>::launch...};
+    static constexpr ShapeFn shape[] = {Entry<H, kLogW>::shape...};
+};
+
+#if CUBF_BW_OP == 0
+// FWHT: one contiguous pass per row (N <= 2^14).
+using C = Contig<1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14>;
+using T = Strided<1>;
+constexpr bool kHasStrided = false;
+#else
+#if CUBF_BW_TYPE == 4
+using C = Contig<1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13>;
+using T = Strided<1, 2, 3, 4, 5, 6, 7, 8, 9>;
+#else
+using C = Contig<1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14>;
+using T = Strided<1, 2, 3, 4, 5, 6, 7, 8, 9, 10>;
+#endif
+constexpr bool kHasStrided = true;
+#endif
+
+}  // namespace
+
+#define CUBF_CAT2(a, b) a##b
+#define CUBF_CAT(a, b) CUBF_CAT2(a, b)
+#define CUBF_UNIT CUBF_CAT(CUBF_CAT(bw_unit_, CUBF_BW_OP), CUBF_CAT(_, CUBF_BW_TYPE))
+
+// Unit entry points (named per operator/type so all units link together).
+LaunchShape CUBF_CAT(CUBF_UNIT, _shape)(int log_h, int log_w) {
+    if (log_w == 0 && log_h >= 1 && log_h <= kMaxContig) return C::shape[log_h - 1]();
+    if (kHasStrided && log_w == kLogW && log_h >= 1 && log_h <= kMaxStrided) return T::shape[log_h - 1]();
+    return {};
+}
+
+cudaError_t CUBF_CAT(CUBF_UNIT, _launch)(int log_h, int log_w, const void* in, void* out, std::size_t outer,
+                                         std::size_t inner, bool inverse, float scale, cudaStream_t stream) {
+    if (log_w == 0 && log_h >= 1 && log_h <= kMaxContig)
+        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, stream);
+    if (kHasStrided && log_w == kLogW && log_h >= 1 && log_h <= kMaxStrided)
+        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, stream);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace cubf

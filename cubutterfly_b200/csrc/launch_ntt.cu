@@ -1,0 +1,88 @@
+// launch_ntt.cu -- instantiations and launchers of the RNS NTT tile passes.
+#include "kernels.hpp"
+#include "ntt.cuh"
+
+namespace cubf {
+namespace {
+
+template <int L, bool STRIDED, bool INV>
+struct Entry {
+    using S = ntt::PassShape<L, STRIDED, INV>;
+    static LaunchShape shape() {
+        LaunchShape s;
+        s.threads = S::TPB;
+        s.smem_bytes = S::SMEM_BYTES;
+        s.units_per_cta = S::COLS;
+        s.elems_per_thread = S::E;
+        s.exchanges = S::Gs::COUNT - 1;
+        return s;
+    }
+    static cudaError_t launch(const std::uint64_t* in, std::uint64_t* out, const NttPolyDesc* polys,
+                              std::size_t poly_count, const NttTables& t, bool in_is_out, bool final_scale,
+                              cudaStream_t stream) {
+        auto kernel = ntt::ntt_pass_kernel<L, STRIDED, INV>;
+        static bool configured = false;
+        if (!configured && S::SMEM_BYTES > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+        }
+        configured = true;
+        constexpr std::size_t groups = (std::size_t{1} << (L - S::B)) / S::COLS;
+        const std::size_t blocks = poly_count * groups;
+        if (blocks == 0) return cudaSuccess;
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        ntt::DomainTables tab{reinterpret_cast<const ntt::u64*>(t.roots),
+                              reinterpret_cast<const ntt::u64*>(t.quotients),
+                              reinterpret_cast<const ntt::u64*>(t.moduli), reinterpret_cast<const ntt::u64*>(t.n_inv),
+                              reinterpret_cast<const ntt::u64*>(t.n_inv_q)};
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+            reinterpret_cast<const ntt::u64*>(in), reinterpret_cast<ntt::u64*>(out),
+            reinterpret_cast<const ntt::PolyDesc*>(polys), tab, in_is_out ? 1 : 0, final_scale ? 1 : 0);
+        return cudaGetLastError();
+    }
+};
+
+using LaunchFn = cudaError_t (*)(const std::uint64_t*, std::uint64_t*, const NttPolyDesc*, std::size_t,
+                                 const NttTables&, bool, bool, cudaStream_t);
+using ShapeFn = LaunchShape (*)();
+
+template <bool STRIDED, bool INV, int... L>
+struct Row {
+    static constexpr LaunchFn launch[] = {Entry<L, STRIDED, INV>::launch...};
+    static constexpr ShapeFn shape[] = {Entry<L, STRIDED, INV>::shape...};
+};
+#define CUBF_NTT_LOGS 12, 13, 14, 15, 16, 17, 18, 19, 20
+using FwdStrided = Row<true, false, CUBF_NTT_LOGS>;
+using FwdContig = Row<false, false, CUBF_NTT_LOGS>;
+using InvStrided = Row<true, true, CUBF_NTT_LOGS>;
+using InvContig = Row<false, true, CUBF_NTT_LOGS>;
+
+static_assert(sizeof(NttPolyDesc) == sizeof(ntt::PolyDesc), "poly descriptor layout");
+
+int slot(const NttVariant& v) {
+    if (v.log_n < kNttMinLog || v.log_n > kNttMaxLog) return -1;
+    return v.log_n - kNttMinLog;
+}
+
+}  // namespace
+
+bool ntt_available(const NttVariant& v) { return slot(v) >= 0; }
+
+LaunchShape ntt_shape(const NttVariant& v) {
+    const int s = slot(v);
+    if (s < 0) return {};
+    if (!v.inverse) return v.strided ? FwdStrided::shape[s]() : FwdContig::shape[s]();
+    return v.strided ? InvStrided::shape[s]() : InvContig::shape[s]();
+}
+
+cudaError_t launch_ntt_pass(const NttVariant& v, const std::uint64_t* in, std::uint64_t* out,
+                            const NttPolyDesc* polys, std::size_t poly_count, const NttTables& tables,
+                            bool in_is_out, bool final_scale, cudaStream_t stream) {
+    const int s = slot(v);
+    if (s < 0) return cudaErrorInvalidValue;
+    LaunchFn fn = !v.inverse ? (v.strided ? FwdStrided::launch[s] : FwdContig::launch[s])
+                             : (v.strided ? InvStrided::launch[s] : InvContig::launch[s]);
+    return fn(in, out, polys, poly_count, tables, in_is_out, final_scale, stream);
+}
+
+}  // namespace cubf

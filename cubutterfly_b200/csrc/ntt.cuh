@@ -1,0 +1,257 @@
+// ntt.cuh -- RNS word64 NTT kernels for sm_100a.
+//
+// Forward negacyclic NTT, natural input, bit-reversed output, one modulus per
+// polynomial, as served by the reference's RNS ABI (RnsPlan, include/cuntt/
+// rns_ntt.hpp:97-131; fused CT core src/rns_fused_ctgs.cuh:55-224).  The
+// negacyclic twist is folded into the Cooley-Tukey stages: stage s pairs
+// elements j and j + N/2^(s+1) and multiplies by psi^bitrev(2^s + (j >> (L-s)))
+// (the "psi_rev" root schedule), so output is bit-reversed with no extra pass.
+// The inverse (Gentleman-Sande with psi^-bitrev, natural output from a
+// bit-reversed input, scaled by N^-1) uses the same tile machinery.
+//
+// The L = log2 N stages are split into two tile passes: pass 1 transforms the
+// top L1 index bits of every column (strided tiles, C adjacent columns per CTA
+// for coalescing), pass 2 the low L2 bits of contiguous chunks.  Inside a tile
+// each thread keeps 2^LOGE residues in registers; successive register groups
+// of LOGE index bits are reached through shared memory.  Products use Shoup's
+// method with per-root precomputed quotients floor(w 2^64 / q), so a modular
+// multiply is one 64-bit high product and two low products; q < 2^63.
+#pragma once
+
+#include "common.cuh"
+
+namespace cubf::ntt {
+
+using u64 = unsigned long long;
+
+CUBF_DEV u64 mul_shoup(u64 a, u64 w, u64 wq, u64 q) {
+    const u64 hi = __umul64hi(a, wq);
+    const u64 r = a * w - hi * q;  // in [0, 2q)
+    return r >= q ? r - q : r;
+}
+CUBF_DEV u64 add_mod(u64 a, u64 b, u64 q) {
+    const u64 s = a + b;
+    return s >= q ? s - q : s;
+}
+CUBF_DEV u64 sub_mod(u64 a, u64 b, u64 q) { return a >= b ? a - b : a + q - b; }
+
+// Per-polynomial binding of an RNS plan: offsets into the caller's buffers and
+// the domain whose modulus and root tables it uses.
+struct PolyDesc {
+    u64 in_off;
+    u64 out_off;
+    uint32_t domain;
+    uint32_t pad_;
+};
+
+struct DomainTables {
+    const u64* roots;     // [domains][N] forward: psi^bitrev(i); inverse: psi^-bitrev(i)
+    const u64* quotients; // Shoup quotients of `roots`
+    const u64* moduli;    // [domains]
+    const u64* n_inv;     // [domains] N^-1 mod q (inverse only)
+    const u64* n_inv_q;   // Shoup quotient of n_inv
+};
+
+// Register group g of a tile with B index bits: registers hold the LOGE
+// consecutive bits starting at lo(g); the stage bits of the group are the
+// not-yet-processed ones.  Forward processes bits top-down, inverse bottom-up.
+template <int B, int LOGE, bool INV>
+struct NttGroups {
+    static constexpr int E = 1 << LOGE;
+    static constexpr int COUNT = (B + LOGE - 1) / LOGE;
+    static constexpr int lo(int g) {
+        if (!INV) {
+            const int top = B - g * LOGE;  // exclusive top of new bits
+            return top - LOGE < 0 ? 0 : top - LOGE;
+        }
+        const int start = g * LOGE;
+        return start + LOGE > B ? B - LOGE : start;
+    }
+    // new (stage) bits of group g, as a mask of tile bits
+    static constexpr uint32_t stage(int g) {
+        if (!INV) {
+            const int top = B - g * LOGE;
+            const int bot = top - LOGE < 0 ? 0 : top - LOGE;
+            return lowmask(top) & ~lowmask(bot);
+        }
+        const int bot = g * LOGE;
+        const int top = bot + LOGE > B ? B : bot + LOGE;
+        return lowmask(top) & ~lowmask(bot);
+    }
+    static constexpr uint32_t reg(int g) { return lowmask(LOGE) << lo(g); }
+};
+
+template <int B_, int LOGE_, int COLS_, bool STRIDED_, bool INV_>
+struct NttShape {
+    static constexpr int B = B_;
+    static constexpr int LOGE = LOGE_;
+    static constexpr int E = 1 << LOGE;
+    static constexpr int COLS = COLS_;  // tiles per CTA
+    static constexpr bool STRIDED = STRIDED_;
+    static constexpr bool INV = INV_;
+    static constexpr int TPT = 1 << (B - LOGE);
+    static constexpr int TPB = TPT * COLS;
+    using Gs = NttGroups<B, LOGE, INV>;
+    static constexpr int TILE = 1 << B;
+    // strided tiles live column-interleaved ([row][col]); contiguous tiles
+    // row-major with one word of padding per 16.
+    static CUBF_DEV int sidx(int col, uint32_t i) {
+        if constexpr (STRIDED)
+            return static_cast<int>(i) * COLS + col;
+        else
+            return col * (TILE + TILE / 16) + static_cast<int>(i + (i >> 4));
+    }
+    static constexpr int SMEM_BYTES = (STRIDED ? TILE * COLS : COLS * (TILE + TILE / 16)) * 8;
+};
+
+// Butterflies of group G on the registers of one thread.  i = tpart | (r << lo)
+// is the tile row of register r; the root of the pair at tile bit b (local
+// stage ls = B-1-b forward) is roots[2^(off+ls) + (hi << ls) + (i >> (b+1))].
+template <typename S, int G>
+CUBF_DEV void ntt_group(u64 (&v)[S::E], uint32_t tpart, u64 hi, int off, const u64* __restrict__ roots,
+                        const u64* __restrict__ quots, u64 q) {
+    using Gs = typename S::Gs;
+    constexpr int LO = Gs::lo(G);
+    constexpr uint32_t STAGE = Gs::stage(G);
+#pragma unroll
+    for (int jj = 0; jj < S::LOGE; ++jj) {
+        const int j = S::INV ? jj : S::LOGE - 1 - jj;  // forward: top-down
+        const int b = LO + j;
+        if ((STAGE >> b) & 1u) {
+            const int ls = S::B - 1 - b;
+            const u64 head = (u64{1} << (off + ls)) + (hi << ls) + (tpart >> (b + 1));
+#pragma unroll
+            for (int rh = 0; rh < (S::E >> (j + 1)); ++rh) {
+                const u64 k = head + static_cast<u64>(rh);
+                const u64 w = __ldg(roots + k);
+                const u64 wq = __ldg(quots + k);
+#pragma unroll
+                for (int rl = 0; rl < (1 << j); ++rl) {
+                    const int r0 = (rh << (j + 1)) | rl;
+                    const int r1 = r0 | (1 << j);
+                    if constexpr (!S::INV) {
+                        // Cooley-Tukey: (a + w b, a - w b)
+                        const u64 t = mul_shoup(v[r1], w, wq, q);
+                        const u64 a = v[r0];
+                        v[r0] = add_mod(a, t, q);
+                        v[r1] = sub_mod(a, t, q);
+                    } else {
+                        // Gentleman-Sande: (a + b, (a - b) w)
+                        const u64 a = v[r0], c = v[r1];
+                        v[r0] = add_mod(a, c, q);
+                        v[r1] = mul_shoup(sub_mod(a, c, q), w, wq, q);
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <typename S, int G>
+CUBF_DEV void ntt_groups(u64 (&v)[S::E], u64* sbuf, int col, uint32_t t, u64 hi, int off,
+                         const u64* __restrict__ roots, const u64* __restrict__ quots, u64 q) {
+    using Gs = typename S::Gs;
+    if constexpr (G < Gs::COUNT) {
+        if constexpr (G > 0) {
+            constexpr uint32_t RP = Gs::reg(G - 1), RN = Gs::reg(G);
+            constexpr Offsets<S::E> OP = make_offsets<S::E>(RP);
+            constexpr Offsets<S::E> ON = make_offsets<S::E>(RN);
+            if constexpr (G > 1) __syncthreads();
+            const uint32_t tp = deposit_rt<lowmask(S::B) & ~RP, S::B>(t);
+#pragma unroll
+            for (int r = 0; r < S::E; ++r) sbuf[S::sidx(col, tp | OP.v[r])] = v[r];
+            __syncthreads();
+            const uint32_t tn = deposit_rt<lowmask(S::B) & ~RN, S::B>(t);
+#pragma unroll
+            for (int r = 0; r < S::E; ++r) v[r] = sbuf[S::sidx(col, tn | ON.v[r])];
+        }
+        const uint32_t tpart = deposit_rt<lowmask(S::B) & ~Gs::reg(G), S::B>(t);
+        ntt_group<S, G>(v, tpart, hi, off, roots, quots, q);
+        ntt_groups<S, G + 1>(v, sbuf, col, t, hi, off, roots, quots, q);
+    }
+}
+
+// Tile geometry of the two passes of a 2^L transform: the strided pass covers
+// the top ceil(L/2) index bits, the contiguous pass the low floor(L/2) bits.
+constexpr int strided_bits(int L) { return (L + 1) / 2; }
+constexpr int contiguous_bits(int L) { return L / 2; }
+constexpr int log_e_for(int b) { return b <= 6 ? 3 : (b <= 8 ? 4 : 5); }
+// Strided passes keep 16 adjacent columns (128-byte rows of uint64) per CTA;
+// contiguous passes pack tiles up to 256 threads.
+constexpr int cols_for(int b, bool strided) {
+    return strided ? 16 : ((256 >> (b - log_e_for(b))) > 0 ? (256 >> (b - log_e_for(b))) : 1);
+}
+template <int L, bool STRIDED, bool INV>
+using PassShape = NttShape<STRIDED ? strided_bits(L) : contiguous_bits(L),
+                           log_e_for(STRIDED ? strided_bits(L) : contiguous_bits(L)),
+                           cols_for(STRIDED ? strided_bits(L) : contiguous_bits(L), STRIDED), STRIDED, INV>;
+
+// One tile pass over every polynomial of a 2^L transform.  Forward runs the
+// strided pass (stages 0..B1-1) then the contiguous pass; inverse runs them in
+// the opposite order.  `in_is_out` makes the pass read the output buffer (the
+// second pass is in place); the final inverse pass scales by N^-1.
+template <int L, bool STRIDED, bool INV>
+__global__ void __launch_bounds__(PassShape<L, STRIDED, INV>::TPB)
+    ntt_pass_kernel(const u64* in, u64* out, const PolyDesc* __restrict__ polys, DomainTables tab, int in_is_out,
+                    int final_scale) {
+    using S = PassShape<L, STRIDED, INV>;
+    using Gs = typename S::Gs;
+    constexpr int B = S::B;
+    constexpr int COLS = S::COLS;
+    constexpr int LOWB = STRIDED ? L - B : 0;  // index bits below this pass's bits
+    constexpr size_t N = size_t{1} << L;
+    constexpr size_t GROUPS = (N >> B) / COLS;  // CTAs per polynomial
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    u64* sbuf = reinterpret_cast<u64*>(smem_raw);
+
+    const size_t p = blockIdx.x / GROUPS;
+    const uint32_t g = static_cast<uint32_t>(blockIdx.x % GROUPS);
+    const PolyDesc pd = polys[p];
+    const u64 q = tab.moduli[pd.domain];
+    const u64* roots = tab.roots + static_cast<size_t>(pd.domain) * N;
+    const u64* quots = tab.quotients + static_cast<size_t>(pd.domain) * N;
+    const u64* src = in_is_out ? static_cast<const u64*>(out) + pd.out_off : in + pd.in_off;
+    u64* dst = out + pd.out_off;
+
+    int col;
+    uint32_t t;
+    if constexpr (STRIDED) {
+        col = threadIdx.x % COLS;  // adjacent threads -> adjacent columns (coalesced)
+        t = threadIdx.x / COLS;
+    } else {
+        col = threadIdx.x / S::TPT;
+        t = threadIdx.x % S::TPT;
+    }
+    const uint32_t tile = g * COLS + col;
+    // Tile row i lives at (i << LOWB) | tile (strided) or (tile << B) | i.
+    const u64* tsrc = src + (STRIDED ? tile : (static_cast<size_t>(tile) << B));
+    u64* tdst = dst + (STRIDED ? tile : (static_cast<size_t>(tile) << B));
+    constexpr int SHIFT = STRIDED ? LOWB : 0;
+    const int off = STRIDED ? 0 : L - B;
+    const u64 hi = STRIDED ? 0 : static_cast<u64>(tile);
+
+    u64 v[S::E];
+    {
+        constexpr uint32_t R0 = Gs::reg(0);
+        constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
+        const uint32_t tp = deposit_rt<lowmask(B) & ~R0, B>(t);
+        const u64* ts = tsrc + (static_cast<size_t>(tp) << SHIFT);
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) v[r] = ts[static_cast<size_t>(O0.v[r]) << SHIFT];
+    }
+    ntt_groups<S, 0>(v, sbuf, col, t, hi, off, roots, quots, q);
+    constexpr uint32_t RF = Gs::reg(Gs::COUNT - 1);
+    constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
+    const uint32_t tf = deposit_rt<lowmask(B) & ~RF, B>(t);
+    u64* td = tdst + (static_cast<size_t>(tf) << SHIFT);
+    if (INV && final_scale) {
+        const u64 ni = tab.n_inv[pd.domain], niq = tab.n_inv_q[pd.domain];
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) td[static_cast<size_t>(OF.v[r]) << SHIFT] = mul_shoup(v[r], ni, niq, q);
+    } else {
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) td[static_cast<size_t>(OF.v[r]) << SHIFT] = v[r];
+    }
+}
+
+}  // namespace cubf::ntt

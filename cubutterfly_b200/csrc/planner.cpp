@@ -1,0 +1,283 @@
+// planner.cpp -- hardware profile, pass partitioning and static ranking.
+#include "planner.hpp"
+
+#include <cuda_runtime_api.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <fstream>
+#include <functional>
+#include <sstream>
+
+namespace cubf {
+
+Json HardwareProfile::to_json() const {
+    return {{"schema", "cubutterfly-b200-hardware-v1"},
+            {"name", name},
+            {"cc_major", cc_major},
+            {"cc_minor", cc_minor},
+            {"sm_count", sm_count},
+            {"smem_per_block_optin", smem_per_block_optin},
+            {"smem_per_sm", smem_per_sm},
+            {"regs_per_sm", regs_per_sm},
+            {"max_threads_per_sm", max_threads_per_sm},
+            {"l2_bytes", l2_bytes},
+            {"global_bytes", global_bytes},
+            {"hbm_gbs", hbm_gbs},
+            {"sm_clock_ghz", sm_clock_ghz},
+            {"launch_us", launch_us},
+            {"source", source}};
+}
+
+std::string HardwareProfile::fingerprint() const {
+    std::ostringstream o;
+    o << name << "|sm_" << cc_major << cc_minor << "|" << sm_count << "SM|" << smem_per_block_optin << "|"
+      << global_bytes;
+    return o.str();
+}
+
+HardwareProfile profile_from_json(const Json& j) {
+    HardwareProfile p;
+    require(j.is_object(), "hardware profile must be a JSON object");
+    auto get = [&](const char* k, auto& field) {
+        if (j.contains(k)) field = j.at(k).get<std::decay_t<decltype(field)>>();
+    };
+    get("name", p.name);
+    get("cc_major", p.cc_major);
+    get("cc_minor", p.cc_minor);
+    get("sm_count", p.sm_count);
+    get("smem_per_block_optin", p.smem_per_block_optin);
+    get("smem_per_sm", p.smem_per_sm);
+    get("regs_per_sm", p.regs_per_sm);
+    get("max_threads_per_sm", p.max_threads_per_sm);
+    get("l2_bytes", p.l2_bytes);
+    get("global_bytes", p.global_bytes);
+    get("hbm_gbs", p.hbm_gbs);
+    get("sm_clock_ghz", p.sm_clock_ghz);
+    get("launch_us", p.launch_us);
+    require(p.sm_count > 0 && p.smem_per_block_optin > 0 && p.hbm_gbs > 0 && p.sm_clock_ghz > 0,
+            "hardware profile capacities must be positive");
+    p.source = "file";
+    return p;
+}
+
+HardwareProfile resolve_profile() {
+    if (const char* path = std::getenv("CUBUTTERFLY_HARDWARE_MODEL"); path && *path) {
+        std::ifstream in(path);
+        require(static_cast<bool>(in), std::string("cannot read CUBUTTERFLY_HARDWARE_MODEL file ") + path);
+        Json j;
+        in >> j;
+        HardwareProfile p = profile_from_json(j);
+        p.source = std::string("file:") + path;
+        return p;
+    }
+    HardwareProfile p;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+        cudaGetLastError();
+        return p;  // builtin B200 profile
+    }
+    int dev = 0;
+    cudaDeviceProp prop{};
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return p;
+    }
+    p.name = prop.name;
+    p.cc_major = prop.major;
+    p.cc_minor = prop.minor;
+    p.sm_count = prop.multiProcessorCount;
+    p.smem_per_block_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    p.smem_per_sm = static_cast<int>(prop.sharedMemPerMultiprocessor);
+    p.regs_per_sm = prop.regsPerMultiprocessor;
+    p.max_threads_per_sm = prop.maxThreadsPerMultiProcessor;
+    p.l2_bytes = static_cast<std::size_t>(prop.l2CacheSize);
+    p.global_bytes = prop.totalGlobalMem;
+    // Bandwidth: the B200 figure measured on this platform unless the device
+    // is not a B200, then the bus-width x clock estimate at 80 %.
+    int mem_clock_khz = 0, bus_bits = 0;
+    cudaDeviceGetAttribute(&mem_clock_khz, cudaDevAttrMemoryClockRate, dev);
+    cudaDeviceGetAttribute(&bus_bits, cudaDevAttrGlobalMemoryBusWidth, dev);
+    if (p.cc_major != 10 && mem_clock_khz > 0 && bus_bits > 0)
+        p.hbm_gbs = 0.8 * 2.0 * mem_clock_khz * 1e3 * (bus_bits / 8.0) / 1e9;
+    p.source = "device";
+    return p;
+}
+
+// ---------------------------------------------------------------------------
+namespace {
+
+struct Cost {
+    double us = 0;
+};
+
+double pass_time_us(const HardwareProfile& hw, double elems, double store_bytes, double compute_bytes,
+                    int stages, int exchanges, double alu_ops_per_elem_stage, double eff) {
+    const double bytes = 2.0 * elems * store_bytes;
+    const double t_mem = bytes / (hw.hbm_gbs * 1e3 * eff);
+    const double lanes = hw.sm_count * 128.0 * hw.sm_clock_ghz * 1e3;  // ops per us
+    const double t_alu = elems * stages * alu_ops_per_elem_stage / lanes;
+    const double smem_bpus = hw.sm_count * 128.0 * hw.sm_clock_ghz * 1e3;  // bytes per us
+    const double t_smem = elems * exchanges * 2.0 * compute_bytes / smem_bpus;
+    return std::max({t_mem, t_alu, t_smem}) + hw.launch_us;
+}
+
+bool fits(const LaunchShape& s, const HardwareProfile& hw) {
+    return s.threads > 0 && s.threads <= 1024 && s.smem_bytes <= hw.smem_per_block_optin;
+}
+
+std::size_t compute_bytes_of(BwType t) { return t == BwType::U64 ? 8 : 4; }
+
+double bw_alu_cost(BwOp op, BwType t) {
+    // adds per element per stage (FWHT: one add or sub; zeta: half the
+    // elements update; 64-bit integer adds take two issue slots)
+    const double base = op == BwOp::Fwht ? 1.0 : 0.5;
+    return t == BwType::U64 ? 2.0 * base : base;
+}
+
+Mapping bitwise_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts) {
+    Mapping m;
+    m.family = r.bw_op == BwOp::Fwht ? "fwht-tile" : "zeta-tile";
+    const double elems = static_cast<double>(r.d.batch) * std::ldexp(1.0, r.log_n);
+    int done = 0;
+    for (std::size_t i = 0; i < parts.size(); ++i) {
+        Pass p;
+        p.kind = PassKind::BitwiseTile;
+        p.log_h = parts[i];
+        p.log_w = i == 0 ? 0 : bw_strided_log_w(r.bw_type);
+        p.log_inner = done;
+        require(p.log_h >= 1, "mapping pass must transform at least one bit");
+        if (i > 0 && p.log_inner < p.log_w)
+            throw Unsupported("strided pass needs at least " + std::to_string(p.log_w) + " lower index bits");
+        p.shape = bw_shape({r.bw_op, r.bw_type, p.log_h, p.log_w});
+        if (!fits(p.shape, hw))
+            throw Unsupported("no compiled tile kernel for pass of " + std::to_string(p.log_h) + " bits");
+        m.predicted_us += pass_time_us(hw, elems, static_cast<double>(bw_type_bytes(r.bw_type)),
+                                       static_cast<double>(compute_bytes_of(r.bw_type)), p.log_h, p.shape.exchanges,
+                                       bw_alu_cost(r.bw_op, r.bw_type), i == 0 ? 0.92 : 0.85);
+        m.passes.push_back(p);
+        done += parts[i];
+    }
+    require(done == r.log_n, "mapping passes must cover every stage exactly once");
+    return m;
+}
+
+void compositions(int total, int first_max, int rest_max, int max_parts, std::vector<int>& cur,
+                  std::vector<std::vector<int>>& out) {
+    if (total == 0) {
+        out.push_back(cur);
+        return;
+    }
+    if (static_cast<int>(cur.size()) == max_parts) return;
+    const int lim = cur.empty() ? first_max : rest_max;
+    for (int h = std::min(lim, total); h >= 1; --h) {
+        cur.push_back(h);
+        compositions(total - h, first_max, rest_max, max_parts, cur, out);
+        cur.pop_back();
+    }
+}
+
+}  // namespace
+
+std::string Mapping::name() const {
+    std::ostringstream o;
+    o << family << "[";
+    for (std::size_t i = 0; i < passes.size(); ++i) {
+        if (i) o << "+";
+        o << passes[i].log_h;
+    }
+    o << "]";
+    return o.str();
+}
+
+Json Mapping::to_json() const {
+    Json ps = Json::array();
+    for (const auto& p : passes) {
+        ps.push_back({{"kernel", p.kind == PassKind::FftLocal ? "fft_local" : "bitwise_tile"},
+                      {"log_h", p.log_h},
+                      {"log_w", p.log_w},
+                      {"log_inner", p.log_inner},
+                      {"threads", p.shape.threads},
+                      {"smem_bytes", p.shape.smem_bytes},
+                      {"units_per_cta", p.shape.units_per_cta},
+                      {"elems_per_thread", p.shape.elems_per_thread},
+                      {"exchanges", p.shape.exchanges}});
+    }
+    return {{"schema", "cubutterfly-b200-mapping-v1"},
+            {"family", family},
+            {"name", name()},
+            {"passes", ps},
+            {"workspace_bytes", workspace_bytes},
+            {"predicted_us", predicted_us}};
+}
+
+std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw) {
+    std::vector<Mapping> out;
+    const Descriptor& d = r.d;
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
+        if (r.log_n > kFftLocalMaxLog)
+            throw Unsupported("FFT lengths above 2^" + std::to_string(kFftLocalMaxLog) +
+                              " need the multi-pass FFT, which this build does not include yet");
+        Mapping m;
+        m.family = "fft-stockham-local";
+        Pass p;
+        p.kind = PassKind::FftLocal;
+        p.log_h = r.log_n;
+        p.shape = fft_local_shape(r.log_n);
+        require(fits(p.shape, hw), "FFT tile does not fit the device");
+        m.passes.push_back(p);
+        const double elems = static_cast<double>(d.batch) * std::ldexp(1.0, r.log_n);
+        // 5 N log N flops per transform on FMA lanes (2 flops per lane-op)
+        m.predicted_us = pass_time_us(hw, elems, 8.0, 8.0, r.log_n, p.shape.exchanges, 2.5 / 2.0, 0.9);
+        out.push_back(m);
+        return out;
+    }
+    // Bitwise operators: every composition of log N into tile passes.
+    std::vector<std::vector<int>> parts;
+    std::vector<int> cur;
+    const int first_max = std::min(bw_max_contiguous_log(r.bw_type), r.log_n);
+    const int rest_max = r.bw_op == BwOp::Fwht ? 0 : bw_max_strided_log(r.bw_type);
+    compositions(r.log_n, first_max, rest_max, 4, cur, parts);
+    for (const auto& p : parts) {
+        try {
+            out.push_back(bitwise_mapping(r, hw, p));
+        } catch (const Unsupported&) {
+        }
+    }
+    if (out.empty()) throw Unsupported("no tile partition of " + std::to_string(r.log_n) + " stages fits");
+    std::stable_sort(out.begin(), out.end(),
+                     [](const Mapping& a, const Mapping& b) { return a.predicted_us < b.predicted_us; });
+    return out;
+}
+
+Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::string& text) {
+    std::vector<int> parts;
+    if (!text.empty() && text.front() == '{') {
+        const Json j = Json::parse(text);
+        require(j.is_object() && j.value("schema", "") == "cubutterfly-b200-mapping-v1",
+                "explicit mapping must use schema cubutterfly-b200-mapping-v1");
+        require(j.at("passes").is_array(), "explicit mapping passes must be an array");
+        for (const auto& p : j.at("passes")) parts.push_back(p.at("log_h").get<int>());
+    } else {
+        std::string body = text;
+        const auto lb = body.find('['), rb = body.rfind(']');
+        if (lb != std::string::npos && rb != std::string::npos && rb > lb) body = body.substr(lb + 1, rb - lb - 1);
+        std::stringstream ss(body);
+        std::string item;
+        while (std::getline(ss, item, '+')) {
+            require(!item.empty() && item.find_first_not_of("0123456789") == std::string::npos,
+                    "explicit mapping must be JSON or a '+'-separated list of pass bit counts");
+            parts.push_back(std::stoi(item));
+        }
+    }
+    require(!parts.empty(), "explicit mapping has no passes");
+    if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
+        require(parts.size() == 1 && parts[0] == r.log_n, "FFT mapping must be one local pass of log N bits");
+        return enumerate_mappings(r, hw).front();
+    }
+    if (r.bw_op == BwOp::Fwht) require(parts.size() == 1, "FWHT executes as a single tile pass");
+    return bitwise_mapping(r, hw, parts);
+}
+
+}  // namespace cubf

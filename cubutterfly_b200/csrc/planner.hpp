@@ -1,0 +1,78 @@
+// planner.hpp -- B200 hardware profile, mappings and the stage partitioner.
+//
+// Replaces the reference's selection stack (mapping_selector.cpp:9-46 ->
+// plan_registry.cpp:551-1292 -> a Python static ranker subprocess) with a C++
+// planner: the stage set of a transform is partitioned into HBM passes, each
+// pass a compiled tile kernel whose on-chip footprint fits the hardware
+// profile; candidates are ranked by a roofline cost model (bytes moved per
+// pass against the profile's HBM bandwidth, integer/FP issue time and launch
+// latency), and the MEASURE policy times the best finalists on the device.
+#pragma once
+
+#include "descriptor.hpp"
+#include "kernels.hpp"
+
+#include <string>
+#include <vector>
+
+namespace cubf {
+
+// Capacity and throughput facts of the target (reference hardware_model.hpp:35-113).
+struct HardwareProfile {
+    std::string name = "NVIDIA B200";
+    int cc_major = 10;
+    int cc_minor = 0;
+    int sm_count = 148;
+    int smem_per_block_optin = 232448;  // 227 KB
+    int smem_per_sm = 233472;           // 228 KB
+    int regs_per_sm = 65536;
+    int max_threads_per_sm = 2048;
+    std::size_t l2_bytes = 126ull << 20;
+    std::size_t global_bytes = 0;
+    double hbm_gbs = 6450.0;     // measured STREAM-style copy on this platform
+    double sm_clock_ghz = 1.9;   // boost clock under memory-bound load
+    double launch_us = 2.5;      // per-kernel launch + drain
+    std::string source = "builtin";
+    Json to_json() const;
+    std::string fingerprint() const;
+};
+
+// The profile of the current device: env CUBUTTERFLY_HARDWARE_MODEL (a JSON
+// file) overrides; otherwise live device properties over B200 defaults; with
+// no device, the builtin B200 profile.
+HardwareProfile resolve_profile();
+HardwareProfile profile_from_json(const Json& j);
+
+enum class PassKind { FftLocal, BitwiseTile };
+
+struct Pass {
+    PassKind kind = PassKind::BitwiseTile;
+    int log_h = 0;      // transformed index bits
+    int log_w = 0;      // adjacent untouched columns per tile (bitwise)
+    int log_inner = 0;  // log2 of the row stride of this pass (bitwise)
+    LaunchShape shape;
+};
+
+struct Mapping {
+    std::string family;  // "fft-stockham-local", "fwht-tile", "zeta-tile"
+    std::vector<Pass> passes;
+    std::size_t workspace_bytes = 0;
+    double predicted_us = 0.0;
+    std::string name() const;
+    Json to_json() const;
+};
+
+struct PlanRequest {
+    Descriptor d;  // normalised
+    int log_n = 0;
+    BwType bw_type = BwType::F32;
+    BwOp bw_op = BwOp::Fwht;
+};
+
+// Every legal mapping of the request, ranked best first by the static model.
+std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw);
+// Parse an EXPLICIT mapping: the JSON of Mapping::to_json, or a pass list
+// "h0+h1+..." of transformed bits per pass (bitwise operators).
+Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::string& text);
+
+}  // namespace cubf

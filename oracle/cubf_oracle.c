@@ -1,0 +1,478 @@
+/*
+ * cubf_oracle.c -- CPU restatement of cuButterfly's reference algorithms.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the parity checker for the CUDA
+ * kernels of cubutterfly_b200; it is never linked into the product library and
+ * the product path never calls it.  Only tests/, __graft_entry__.smoke() and
+ * bench.py's cpu_baseline leg load it.
+ *
+ * Parity is pinned: tests/test_oracle.py checks every function here against
+ * (a) the known answers in the reference's own tests and (b) the reference's
+ * own CPU oracles (src/butterfly_reference.cpp, src/reference.cpp), compiled
+ * unchanged from the reference tree into oracle/_ref by oracle/Makefile, on
+ * seeded inputs (fixtures in tests/golden/, made by tests/golden/make_golden.py).
+ *
+ * Each function names the reference lines it restates.  Arithmetic order is
+ * kept identical to the reference so that results are bit-identical when both
+ * are compiled with -ffp-contract=off.
+ */
+#include <math.h>
+#include <stdlib.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <string.h>
+
+typedef unsigned __int128 u128;
+
+#define ORACLE_API __attribute__((visibility("default")))
+
+static int is_pow2(size_t n) { return n != 0 && (n & (n - 1)) == 0; }
+
+static unsigned log2_exact(size_t n) {
+    unsigned l = 0;
+    while (((size_t)1 << l) < n) ++l;
+    return l;
+}
+
+static size_t reverse_bits(size_t index, unsigned bits) {
+    size_t r = 0;
+    for (unsigned j = 0; j < bits; ++j, index >>= 1) r = (r << 1) | (index & 1u);
+    return r;
+}
+
+/* In-place bit-reversal permutation of n elements of `width` bytes, visiting
+ * indices in the same order as butterfly_reference.cpp:396-407. */
+static void bitrev_permute(void* data, size_t n, size_t width) {
+    unsigned char* p = (unsigned char*)data;
+    unsigned char tmp[16];
+    size_t reversed = 0;
+    for (size_t index = 1; index < n; ++index) {
+        size_t bit = n >> 1;
+        while ((reversed & bit) != 0) {
+            reversed ^= bit;
+            bit >>= 1;
+        }
+        reversed ^= bit;
+        if (index < reversed) {
+            memcpy(tmp, p + index * width, width);
+            memcpy(p + index * width, p + reversed * width, width);
+            memcpy(p + reversed * width, tmp, width);
+        }
+    }
+}
+
+/* ---------------------------------------------------------------- FFT ---- */
+
+/* Radix-2 DIT FFT over interleaved complex fp32, twiddles evaluated in double
+ * per butterfly and the product rounded to float, exactly as
+ * cuntt::reference_fft(std::vector<Complex32>&) in
+ * src/butterfly_reference.cpp:392-433.  `data` holds `batch` transforms of n
+ * complex values each (2n floats per transform). */
+ORACLE_API int cubf_oracle_fft_c32(float* data, size_t n, size_t batch, int inverse, int normalize) {
+    if (!is_pow2(n)) return 1;
+    const double kPi = 3.141592653589793238462643383279502884;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        float* v = data + 2 * n * b;
+        bitrev_permute(v, n, 2 * sizeof(float));
+        for (size_t half = 1; half < n; half <<= 1) {
+            for (size_t base = 0; base < n; base += 2 * half) {
+                for (size_t offset = 0; offset < half; ++offset) {
+                    const double direction = inverse ? 1.0 : -1.0;
+                    const double angle = direction * kPi * (double)offset / (double)half;
+                    const double wr = cos(angle);
+                    const double wi = sin(angle);
+                    float* a = v + 2 * (base + offset);
+                    float* c = v + 2 * (base + half + offset);
+                    const float ar = a[0], ai = a[1];
+                    const float br = c[0], bi = c[1];
+                    const float vr = (float)(br * wr - bi * wi);
+                    const float vi = (float)(br * wi + bi * wr);
+                    a[0] = ar + vr;
+                    a[1] = ai + vi;
+                    c[0] = ar - vr;
+                    c[1] = ai - vi;
+                }
+            }
+        }
+        if (inverse && normalize) {
+            const float scale = 1.0f / (float)n;
+            for (size_t i = 0; i < 2 * n; ++i) v[i] *= scale;
+        }
+    }
+    return 0;
+}
+
+/* Double-precision variant: cuntt::reference_fft(std::vector<Complex64>&),
+ * src/butterfly_reference.cpp:435-473.  Used as the truth for large-N checks. */
+ORACLE_API int cubf_oracle_fft_c64(double* data, size_t n, size_t batch, int inverse, int normalize) {
+    if (!is_pow2(n)) return 1;
+    const double kPi = 3.141592653589793238462643383279502884;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        double* v = data + 2 * n * b;
+        bitrev_permute(v, n, 2 * sizeof(double));
+        for (size_t half = 1; half < n; half <<= 1) {
+            for (size_t base = 0; base < n; base += 2 * half) {
+                for (size_t offset = 0; offset < half; ++offset) {
+                    const double angle = (inverse ? 1.0 : -1.0) * kPi * (double)offset / (double)half;
+                    const double wr = cos(angle);
+                    const double wi = sin(angle);
+                    double* a = v + 2 * (base + offset);
+                    double* c = v + 2 * (base + half + offset);
+                    const double ar = a[0], ai = a[1];
+                    const double br = c[0], bi = c[1];
+                    const double vr = br * wr - bi * wi;
+                    const double vi = br * wi + bi * wr;
+                    a[0] = ar + vr;
+                    a[1] = ai + vi;
+                    c[0] = ar - vr;
+                    c[1] = ai - vi;
+                }
+            }
+        }
+        if (inverse && normalize) {
+            const double scale = 1.0 / (double)n;
+            for (size_t i = 0; i < 2 * n; ++i) v[i] *= scale;
+        }
+    }
+    return 0;
+}
+
+/* Direct O(n) evaluation of selected DFT bins in long double, an independent
+ * truth for spot checks of very long transforms. */
+ORACLE_API void cubf_oracle_dft_bins(const float* data, size_t n, const size_t* bins, size_t count,
+                                     int inverse, double* out) {
+    const long double kPi = 3.141592653589793238462643383279502884L;
+#pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < count; ++i) {
+        const size_t k = bins[i];
+        long double sr = 0, si = 0;
+        for (size_t j = 0; j < n; ++j) {
+            /* reduce j*k mod n exactly before forming the angle */
+            const size_t m = (size_t)(((u128)j * k) % n);
+            const long double ang = (inverse ? 2.0L : -2.0L) * kPi * (long double)m / (long double)n;
+            const long double c = cosl(ang), s = sinl(ang);
+            const long double xr = data[2 * j], xi = data[2 * j + 1];
+            sr += xr * c - xi * s;
+            si += xr * s + xi * c;
+        }
+        out[2 * i] = (double)sr;
+        out[2 * i + 1] = (double)si;
+    }
+}
+
+/* --------------------------------------------------------------- FWHT ---- */
+
+/* cuntt::reference_fwht(std::vector<double>&), src/butterfly_reference.cpp:371-390. */
+static void fwht_f64_one(double* v, size_t n, int inverse, int normalize) {
+    for (size_t half = 1; half < n; half <<= 1) {
+        for (size_t base = 0; base < n; base += 2 * half) {
+            for (size_t offset = 0; offset < half; ++offset) {
+                const double left = v[base + offset];
+                const double right = v[base + half + offset];
+                v[base + offset] = left + right;
+                v[base + half + offset] = left - right;
+            }
+        }
+    }
+    if (inverse && normalize) {
+        const double scale = 1.0 / (double)n;
+        for (size_t i = 0; i < n; ++i) v[i] *= scale;
+    }
+}
+
+ORACLE_API int cubf_oracle_fwht_f64(double* data, size_t n, size_t batch, int inverse, int normalize) {
+    if (!is_pow2(n)) return 1;
+#pragma omp parallel for schedule(static)
+    for (size_t b = 0; b < batch; ++b) fwht_f64_one(data + n * b, n, inverse, normalize);
+    return 0;
+}
+
+/* cuntt::reference_fwht(std::vector<float>&), src/butterfly_reference.cpp:349-369. */
+ORACLE_API int cubf_oracle_fwht_f32(float* data, size_t n, size_t batch, int inverse, int normalize) {
+    if (!is_pow2(n)) return 1;
+#pragma omp parallel for schedule(static)
+    for (size_t b = 0; b < batch; ++b) {
+        float* v = data + n * b;
+        for (size_t half = 1; half < n; half <<= 1)
+            for (size_t base = 0; base < n; base += 2 * half)
+                for (size_t offset = 0; offset < half; ++offset) {
+                    const float left = v[base + offset];
+                    const float right = v[base + half + offset];
+                    v[base + offset] = left + right;
+                    v[base + half + offset] = left - right;
+                }
+        if (inverse && normalize) {
+            const float scale = 1.0f / (float)n;
+            for (size_t i = 0; i < n; ++i) v[i] *= scale;
+        }
+    }
+    return 0;
+}
+
+static double bf16_to_double(uint16_t h) {
+    uint32_t bits = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &bits, 4);
+    return (double)f;
+}
+
+/* Round a double to bfloat16, nearest-even (one rounding, no double rounding
+ * through float: the tie test is made on the exact double value). */
+static uint16_t double_to_bf16(double x) {
+    if (isnan(x)) return 0x7fc0;
+    float f = (float)x; /* exact when |x| has <= 24 significant bits */
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((double)f != x && isfinite(f)) {
+        /* Resolve directly from the double: truncate to bf16 then compare. */
+        uint32_t trunc = u & 0xffff0000u;
+        float lo_f, hi_f;
+        memcpy(&lo_f, &trunc, 4);
+        uint32_t next = trunc + 0x10000u;
+        memcpy(&hi_f, &next, 4);
+        /* lo_f and hi_f bracket x in magnitude order of the sign */
+        double dlo = fabs(x - (double)lo_f), dhi = fabs(x - (double)hi_f);
+        if (dlo < dhi) return (uint16_t)(trunc >> 16);
+        if (dhi < dlo) return (uint16_t)(next >> 16);
+        return (uint16_t)(((trunc >> 16) & 1u) ? (next >> 16) : (trunc >> 16));
+    }
+    /* f == x exactly (or overflow to inf): round the float's bits. */
+    uint32_t lsb = (u >> 16) & 1u;
+    uint32_t rounded = u + 0x7fffu + lsb;
+    return (uint16_t)(rounded >> 16);
+}
+
+/* FWHT with bf16 storage, wide compute and one final rounding:
+ * widen -> reference_fwht<double> -> x output_scale -> round to bf16.
+ * This is the final-storage contract of the reference's FP16 path
+ * (src/butterfly.cu:1451-1470, :1882-1897; tests/test_fwht_final_storage.py:25-38)
+ * applied to bf16 storage. */
+ORACLE_API int cubf_oracle_fwht_bf16_final(const uint16_t* in, uint16_t* out, size_t n, size_t batch,
+                                           int inverse, int normalize, double scale) {
+    if (!is_pow2(n)) return 1;
+    int failed = 0;
+#pragma omp parallel reduction(| : failed)
+    {
+        double* v = (double*)malloc(n * sizeof(double));
+        if (!v) failed = 1;
+#pragma omp for schedule(static)
+        for (size_t b = 0; b < batch; ++b) {
+            if (!v) continue;
+            for (size_t i = 0; i < n; ++i) v[i] = bf16_to_double(in[n * b + i]);
+            fwht_f64_one(v, n, inverse, normalize);
+            for (size_t i = 0; i < n; ++i) out[n * b + i] = double_to_bf16(v[i] * scale);
+        }
+        free(v);
+    }
+    return failed;
+}
+
+/* --------------------------------------------------------------- zeta ---- */
+
+/* cuntt::reference_subset_zeta(std::vector<uint32_t>&), butterfly_reference.cpp:475-490,
+ * and reference_superset_zeta :492-507.  Wrap-around mod 2^32. */
+ORACLE_API int cubf_oracle_zeta_u32(uint32_t* data, size_t n, size_t batch, int superset, int inverse) {
+    if (!is_pow2(n)) return 1;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        uint32_t* v = data + n * b;
+        for (size_t half = 1; half < n; half <<= 1)
+            for (size_t base = 0; base < n; base += 2 * half)
+                for (size_t offset = 0; offset < half; ++offset) {
+                    uint32_t* target = &v[base + offset + (superset ? 0 : half)];
+                    const uint32_t source = v[base + offset + (superset ? half : 0)];
+                    *target = inverse ? *target - source : *target + source;
+                }
+    }
+    return 0;
+}
+
+/* uint64 variants, butterfly_reference.cpp:513-538. */
+ORACLE_API int cubf_oracle_zeta_u64(uint64_t* data, size_t n, size_t batch, int superset, int inverse) {
+    if (!is_pow2(n)) return 1;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        uint64_t* v = data + n * b;
+        for (size_t half = 1; half < n; half <<= 1)
+            for (size_t base = 0; base < n; base += 2 * half)
+                for (size_t offset = 0; offset < half; ++offset) {
+                    uint64_t* target = &v[base + offset + (superset ? 0 : half)];
+                    const uint64_t source = v[base + offset + (superset ? half : 0)];
+                    *target = inverse ? *target - source : *target + source;
+                }
+    }
+    return 0;
+}
+
+/* ---------------------------------------------------------------- NTT ---- */
+
+static uint64_t mod_mul(uint64_t a, uint64_t b, uint64_t q) { return (uint64_t)(((u128)a * b) % q); }
+
+/* src/reference.cpp:506-520 */
+ORACLE_API uint64_t cubf_oracle_mod_pow(uint64_t base, uint64_t exponent, uint64_t q) {
+    uint64_t result = 1;
+    base %= q;
+    while (exponent) {
+        if (exponent & 1u) result = mod_mul(result, base, q);
+        base = mod_mul(base, base, q);
+        exponent >>= 1;
+    }
+    return result;
+}
+
+/* Deterministic Miller-Rabin with the 7-witness set valid for all 64-bit
+ * integers, as src/reference.cpp:522-562. */
+ORACLE_API int cubf_oracle_is_prime(uint64_t value) {
+    static const uint64_t small[12] = {2, 3, 5, 7, 11, 13, 17, 19, 23, 29, 31, 37};
+    static const uint64_t witnesses[7] = {2, 325, 9375, 28178, 450775, 9780504, 1795265022};
+    if (value < 2) return 0;
+    for (int i = 0; i < 12; ++i)
+        if (value % small[i] == 0) return value == small[i];
+    uint64_t d = value - 1;
+    unsigned s = 0;
+    while ((d & 1u) == 0) {
+        d >>= 1;
+        ++s;
+    }
+    for (int w = 0; w < 7; ++w) {
+        if (witnesses[w] % value == 0) continue;
+        uint64_t x = cubf_oracle_mod_pow(witnesses[w], d, value);
+        if (x == 1 || x == value - 1) continue;
+        int ok = 0;
+        for (unsigned r = 1; r < s; ++r) {
+            x = mod_mul(x, x, value);
+            if (x == value - 1) {
+                ok = 1;
+                break;
+            }
+        }
+        if (!ok) return 0;
+    }
+    return 1;
+}
+
+/* Smallest-candidate primitive 2^log_n-th root, src/reference.cpp:564-582.
+ * Returns 0 when the modulus is not prime or has no such root. */
+ORACLE_API uint64_t cubf_oracle_find_root(unsigned log_n, uint64_t q) {
+    if (log_n == 0 || log_n >= 63 || !cubf_oracle_is_prime(q)) return 0;
+    const uint64_t n = 1ull << log_n;
+    if ((q - 1) % n != 0) return 0;
+    for (uint64_t c = 2; c < (1ull << 20); ++c) {
+        const uint64_t root = cubf_oracle_mod_pow(c, (q - 1) / n, q);
+        if (cubf_oracle_mod_pow(root, n, q) == 1 && cubf_oracle_mod_pow(root, n >> 1, q) != 1) return root;
+    }
+    return 0;
+}
+
+/* The largest `count` primes q < 2^60 with q == 1 (mod 2^root_log), found by
+ * descending q = k * 2^root_log + 1 (the RNS limb generator of the benchmark). */
+ORACLE_API size_t cubf_oracle_rns_primes(unsigned root_log, size_t count, uint64_t* out) {
+    const uint64_t step = 1ull << root_log;
+    uint64_t k = ((1ull << 60) - 2) / step;
+    size_t found = 0;
+    while (found < count && k > 0) {
+        const uint64_t q = k * step + 1;
+        if (q < (1ull << 60) && cubf_oracle_is_prime(q)) out[found++] = q;
+        --k;
+    }
+    return found;
+}
+
+/* Cyclic radix-2 DIT NTT, src/reference.cpp:584-630: natural in, natural out,
+ * root = find_primitive_power_of_two_root(log n, q). */
+ORACLE_API int cubf_oracle_ntt_cyclic(uint64_t* values, size_t n, uint64_t q, int inverse) {
+    if (n < 2 || !is_pow2(n) || q >= (1ull << 63)) return 1;
+    const unsigned log_n = log2_exact(n);
+    uint64_t root = cubf_oracle_find_root(log_n, q);
+    if (!root) return 1;
+    if (inverse) root = cubf_oracle_mod_pow(root, q - 2, q);
+    for (size_t i = 0; i < n; ++i) values[i] %= q;
+    bitrev_permute(values, n, sizeof(uint64_t));
+    for (size_t length = 2; length <= n; length <<= 1) {
+        const size_t half = length >> 1;
+        const uint64_t step_root = cubf_oracle_mod_pow(root, n / length, q);
+        for (size_t start = 0; start < n; start += length) {
+            uint64_t omega = 1;
+            for (size_t offset = 0; offset < half; ++offset) {
+                const size_t left = start + offset;
+                const uint64_t u = values[left];
+                const uint64_t v = mod_mul(values[left + half], omega, q);
+                const uint64_t sum = u + v;
+                values[left] = sum >= q ? sum - q : sum;
+                values[left + half] = u >= v ? u - v : q + u - v;
+                omega = mod_mul(omega, step_root, q);
+            }
+        }
+    }
+    if (inverse) {
+        const uint64_t inv_n = cubf_oracle_mod_pow((uint64_t)n, q - 2, q);
+        for (size_t i = 0; i < n; ++i) values[i] = mod_mul(values[i], inv_n, q);
+    }
+    return 0;
+}
+
+/* RNS NTT of one polynomial, restating the independent CPU reference of the
+ * reference's RNS tests (tests/test_rns_ntt.cu:61-110): optional input
+ * bit-reversal, negacyclic twist by root^j (forward), cyclic DIT with
+ * omega = root^2 (negacyclic) or root (cyclic), inverse scaling by n^-1 and
+ * untwist by root^-j, optional output bit-reversal.  `root` is the FORWARD
+ * primitive 2n-th (negacyclic) or n-th (cyclic) root. */
+ORACLE_API int cubf_oracle_rns_ntt(const uint64_t* physical, uint64_t* result, unsigned log_n, uint64_t q,
+                                   uint64_t root, int negacyclic, int inverse, int input_bitrev,
+                                   int output_bitrev) {
+    const size_t n = (size_t)1 << log_n;
+    uint64_t* values = result;
+    if (physical == result) return 1;
+    for (size_t j = 0; j < n; ++j) values[j] = physical[input_bitrev ? reverse_bits(j, log_n) : j];
+    if (negacyclic && !inverse) {
+        uint64_t twist = 1;
+        for (size_t j = 0; j < n; ++j) {
+            values[j] = mod_mul(values[j], twist, q);
+            twist = mod_mul(twist, root, q);
+        }
+    }
+    uint64_t omega = negacyclic ? mod_mul(root, root, q) : root;
+    if (inverse) omega = cubf_oracle_mod_pow(omega, q - 2, q);
+    bitrev_permute(values, n, sizeof(uint64_t));
+    for (size_t length = 2; length <= n; length *= 2) {
+        const uint64_t step = cubf_oracle_mod_pow(omega, n / length, q);
+        for (size_t base = 0; base < n; base += length) {
+            uint64_t tw = 1;
+            for (size_t j = 0; j < length / 2; ++j) {
+                const uint64_t a = values[base + j];
+                const uint64_t b = mod_mul(values[base + j + length / 2], tw, q);
+                values[base + j] = (uint64_t)(((u128)a + b) % q);
+                values[base + j + length / 2] = (uint64_t)(((u128)a + q - b) % q);
+                tw = mod_mul(tw, step, q);
+            }
+        }
+    }
+    if (inverse) {
+        uint64_t factor = cubf_oracle_mod_pow(n, q - 2, q);
+        const uint64_t step = negacyclic ? cubf_oracle_mod_pow(root, q - 2, q) : 1;
+        for (size_t j = 0; j < n; ++j) {
+            values[j] = mod_mul(values[j], factor, q);
+            factor = mod_mul(factor, step, q);
+        }
+    }
+    if (output_bitrev) bitrev_permute(values, n, sizeof(uint64_t));
+    return 0;
+}
+
+/* Batched RNS NTT over `count` polynomials stored contiguously (polynomial i
+ * at i*n), polynomial i using (moduli[i], roots[i]). */
+ORACLE_API int cubf_oracle_rns_ntt_batch(const uint64_t* input, uint64_t* output, unsigned log_n, size_t count,
+                                         const uint64_t* moduli, const uint64_t* roots, int negacyclic,
+                                         int inverse, int input_bitrev, int output_bitrev) {
+    const size_t n = (size_t)1 << log_n;
+    int status = 0;
+#pragma omp parallel for schedule(dynamic, 1) reduction(| : status)
+    for (size_t i = 0; i < count; ++i)
+        status |= cubf_oracle_rns_ntt(input + i * n, output + i * n, log_n, moduli[i], roots[i], negacyclic, inverse,
+                                      input_bitrev, output_bitrev);
+    return status;
+}
+
+ORACLE_API int cubf_oracle_abi_version(void) { return 1; }

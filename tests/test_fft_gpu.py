@@ -1,0 +1,73 @@
+"""FFT parity on the GPU through the C ABI: rel L2 <= 2e-6 against the oracle
+(reference_fft<Complex32> semantics), plus bit-level checks against the
+golden fixtures made by the reference's own compiled oracle."""
+import numpy as np
+import pytest
+
+import cubutterfly_b200 as cb
+from conftest import rel_l2
+from cubutterfly_b200 import workloads as w
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-6  # relative L2, fp32 FFT (north_star)
+
+
+def fft_transform(n, batch, inverse=False, normalize=True, in_place=False):
+    return cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=[n], batch=batch,
+                        inverse=inverse, normalize_inverse=normalize, in_place=in_place)
+
+
+@pytest.mark.parametrize("n", [2, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096, 8192])
+def test_fft_forward_sizes(lib, oracle, cuda, n):
+    from gpu_util import run
+
+    x = w.fft_input(n, 17, seed=n)
+    got, name = run(lib, fft_transform(n, 17), x, cuda)
+    assert rel_l2(got, oracle.fft_c32(x)) <= TOL, name
+
+
+@pytest.mark.parametrize("n", [16, 4096, 8192])
+@pytest.mark.parametrize("normalize", [False, True])
+def test_fft_inverse(lib, oracle, cuda, n, normalize):
+    from gpu_util import run
+
+    x = w.fft_input(n, 5, seed=3)
+    got, _ = run(lib, fft_transform(n, 5, inverse=True, normalize=normalize), x, cuda)
+    assert rel_l2(got, oracle.fft_c32(x, inverse=True, normalize=normalize)) <= TOL
+
+
+@pytest.mark.parametrize("n", [8, 64, 1024, 4096])
+def test_fft_golden(lib, golden, cuda, n):
+    from gpu_util import run
+
+    x = golden[f"fft_fwd_{n}_in"]
+    got, _ = run(lib, fft_transform(n, x.shape[0]), x, cuda)
+    assert rel_l2(got, golden[f"fft_fwd_{n}_out"]) <= TOL
+
+
+def test_fft_in_place_and_ragged_batch(lib, oracle, cuda):
+    from gpu_util import run
+
+    for batch in (1, 3, 129):
+        x = w.fft_input(4096, batch, seed=batch)
+        got, _ = run(lib, fft_transform(4096, batch, in_place=True), x, cuda)
+        assert rel_l2(got, oracle.fft_c32(x)) <= TOL
+
+
+def test_fft_config0_full_size(lib, oracle, cuda):
+    """Config 0: N = 4096, batch 1024, natural in/out, unnormalized."""
+    from gpu_util import run
+
+    x = w.fft_input()
+    got, name = run(lib, fft_transform(w.FFT_N, w.FFT_BATCH), x, cuda)
+    err = rel_l2(got, oracle.fft_c32(x))
+    assert err <= TOL, (name, err)
+
+
+def test_fft_round_trip(lib, cuda):
+    from gpu_util import run
+
+    x = w.fft_input(2048, 8, seed=1)
+    f, _ = run(lib, fft_transform(2048, 8), x, cuda)
+    back, _ = run(lib, fft_transform(2048, 8, inverse=True, normalize=True), f, cuda)
+    assert rel_l2(back, x) <= TOL

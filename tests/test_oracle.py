@@ -1,0 +1,109 @@
+"""The CPU oracle is pinned before anything is checked against it.
+
+oracle/cubf_oracle.c restates the reference algorithms; here it must agree
+bit for bit with (a) the golden fixtures computed by the reference's own
+compiled CPU oracles (tests/golden/make_golden.py) and (b) the known answers
+quoted from the reference's tests, and, where oracle/_ref is built, with the
+reference oracles on fresh random inputs.
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+from cubutterfly_b200 import workloads as w
+
+
+def test_fwht_known_answer(oracle, golden):
+    # reference tests/test_c_api.c:698
+    got = oracle.fwht_f32(golden["kat_fwht_8_in"])
+    assert np.array_equal(got, golden["kat_fwht_8_out"])
+
+
+@pytest.mark.parametrize("n", [8, 64, 1024, 4096])
+def test_fft_matches_golden_bitexact(oracle, golden, n):
+    got = oracle.fft_c32(golden[f"fft_fwd_{n}_in"])
+    assert np.array_equal(got.view(np.uint32), golden[f"fft_fwd_{n}_out"].view(np.uint32))
+
+
+def test_fft_inverse_normalized_matches_golden(oracle, golden):
+    got = oracle.fft_c32(golden["fft_inv_norm_256_in"], inverse=True, normalize=True)
+    assert np.array_equal(got.view(np.uint32), golden["fft_inv_norm_256_out"].view(np.uint32))
+
+
+def test_fft_oracle_is_a_dft(oracle):
+    x = w.fft_input(512, 3, seed=5)
+    got = oracle.fft_c32(x)
+    assert rel_l2(got, np.fft.fft(x.astype(np.complex128), axis=-1)) < 1e-6
+
+
+@pytest.mark.parametrize("n", [128, 4096])
+def test_fwht_bf16_final_matches_golden(oracle, golden, n):
+    got = oracle.fwht_bf16_final(golden[f"fwht_bf16_{n}_in"], float(golden[f"fwht_bf16_{n}_scale"][0]))
+    assert np.array_equal(got, golden[f"fwht_bf16_{n}_out"])
+
+
+def test_fwht_f32_matches_golden(oracle, golden):
+    assert np.array_equal(oracle.fwht_f32(golden["fwht_f32_32_in"]), golden["fwht_f32_32_out"])
+
+
+def test_zeta_matches_golden(oracle, golden):
+    assert np.array_equal(oracle.zeta(golden["zeta_subset_1024_in"]), golden["zeta_subset_1024_out"])
+    z = golden["zeta_superset_256_in"]
+    assert np.array_equal(oracle.zeta(z, superset=True), golden["zeta_superset_256_out"])
+    assert np.array_equal(oracle.zeta(z, inverse=True), golden["zeta_subset_inv_256_out"])
+
+
+def test_zeta_inverse_round_trip(oracle):
+    z = w.zeta_input(12, 3, seed=3)
+    for superset in (False, True):
+        f = oracle.zeta(z, superset=superset)
+        assert np.array_equal(oracle.zeta(f, superset=superset, inverse=True), z)
+
+
+def test_negacyclic_ntt_matches_golden(oracle, golden):
+    qs = [int(q) for q in golden["ntt_neg_4096_moduli"]]
+    roots = [int(r) for r in golden["ntt_neg_4096_roots"]]
+    got = oracle.rns_ntt(golden["ntt_neg_4096_in"], qs, roots)
+    assert np.array_equal(got, golden["ntt_neg_4096_out"])
+
+
+def test_negacyclic_ntt_round_trip_and_linearity(oracle):
+    qs = w.rns_primes(2, 12)
+    roots = [w.primitive_root_of_two_power(13, q) for q in qs]
+    x = w.ntt_input(qs, 12, seed=4)
+    f = oracle.rns_ntt(x, qs, roots)
+    back = oracle.rns_ntt(f, qs, roots, inverse=True, input_bitrev=True, output_bitrev=False)
+    assert np.array_equal(back, x)
+    y = w.ntt_input(qs, 12, seed=5)
+    s = np.stack([(x[i].astype(object) + y[i].astype(object)) % q for i, q in enumerate(qs)]).astype(np.uint64)
+    fs = oracle.rns_ntt(s, qs, roots)
+    fy = oracle.rns_ntt(y, qs, roots)
+    expect = np.stack([(f[i].astype(object) + fy[i].astype(object)) % q for i, q in enumerate(qs)]).astype(np.uint64)
+    assert np.array_equal(fs, expect)
+
+
+def test_rns_primes_and_roots(oracle):
+    qs = w.rns_primes()
+    assert qs == oracle.rns_primes(17, 32)
+    assert len(set(qs)) == 32 and all(q < 2**60 and q >= 2**59 and q % 2**17 == 1 for q in qs)
+    assert qs[0] == 1152921504606584833  # the reference's default NTT modulus (ntt.hpp:17)
+    for q in qs[:6]:
+        assert w.primitive_root_of_two_power(17, q) == oracle.find_root(17, q)
+
+
+# ---- against the reference's own compiled oracles, fresh inputs ----------------
+def test_restatement_matches_reference_random(oracle, reference):
+    for n in (2, 16, 512, 2048):
+        x = w.fft_input(n, 2, seed=n)
+        assert np.array_equal(oracle.fft_c32(x).view(np.uint32), reference.fft_c32(x).view(np.uint32))
+        assert np.array_equal(oracle.fft_c32(x, inverse=True).view(np.uint32),
+                              reference.fft_c32(x, inverse=True).view(np.uint32))
+    bits = w.fwht_input_bits(16, 2048, seed=3)
+    assert np.array_equal(oracle.fwht_bf16_final(bits, 0.3), reference.fwht_bf16_final(bits, 0.3))
+    z = w.zeta_input(13, 2, seed=2)
+    assert np.array_equal(oracle.zeta(z), reference.zeta_u32(z))
+    assert np.array_equal(oracle.zeta(z, superset=True, inverse=True), reference.zeta_u32(z, True, True))
+    qs = w.rns_primes(3, 13)
+    x = w.ntt_input(qs, 13, seed=9)
+    roots = [reference.find_root(14, q) for q in qs]
+    assert np.array_equal(oracle.rns_ntt(x, qs, roots), reference.negacyclic_ntt(x, qs))

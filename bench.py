@@ -37,11 +37,13 @@ MIB = 1 << 20
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=4000)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-ops", action="store_true", help="skip the per-op table (FFT, NTT, zeta)")
     p.add_argument("--cpu-baseline", choices=["auto", "skip"], default="auto")
+    p.add_argument("--only", choices=["fwht4096", "fwht128", "fft", "zeta", "ntt"],
+                   help="run just this operator's launches (profiling driver; prints a short JSON line)")
     return p.parse_args()
 
 
@@ -137,13 +139,20 @@ def reference_arm(args):
         from oracle.oracle import Oracle
         ref, kind = Oracle(), "port"
         fa = lambda x, s: ref.fwht_bf16_final(x, s)  # noqa: E731
-    # bounded sample of the workload: 2048 of the 16384 rows per step (1/8 of a
-    # step); throughput in the same algorithmic bytes per second
-    sample_rows = 2048
-    bits = w.fwht_input_bits(sample_rows, COLS, seed=0)
+    # bounded sample of the workload: each step transforms `sample_rows` of the
+    # 16384 rows (both passes), sized so all steps take about a minute;
+    # throughput in the same algorithmic bytes per second
+    bits = w.fwht_input_bits(2048, COLS, seed=0)
+    t0 = time.perf_counter()
+    fa(bits[:256], 1 / 64)
+    fa(bits[:256].reshape(-1, HEAD), 1 / math.sqrt(HEAD))
+    per_row = (time.perf_counter() - t0) / 256
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    sample_rows = int(max(16, min(2048, budget / max(per_row, 1e-9))))
+    bits = np.ascontiguousarray(bits[:sample_rows])
     blocks = bits.reshape(-1, HEAD)
-    for _ in range(max(1, min(args.warmup, 1))):
-        fa(bits[:256], 1 / 64)
+    for _ in range(args.warmup):
+        fa(bits, 1 / 64)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
@@ -168,10 +177,55 @@ def reference_arm(args):
 
 
 # ---- B200 arm ------------------------------------------------------------------------------------
+def only_op(args):
+    """Launch one operator `steps` times after `warmup` launches (ncu driver)."""
+    import torch
+
+    import cubutterfly_b200 as cb
+    from cubutterfly_b200 import rns
+    from cubutterfly_b200 import workloads as w
+
+    dev = torch.device("cuda", 0)
+    lib = cb.Library()
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    if args.only in ("fwht4096", "fwht128"):
+        x = w.torch_fwht_input(ROWS, COLS, dev)
+        y = torch.empty_like(x)
+        n = COLS if args.only == "fwht4096" else HEAD
+        p = cb.Plan(lib, fwht_transform(cb, n, ROWS * COLS // n, 1 / math.sqrt(n)), stream=sp)
+        fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), PASS_BYTES
+    elif args.only == "fft":
+        x = w.torch_fft_input(w.FFT_N, w.FFT_BATCH, dev)
+        y = torch.empty_like(x)
+        p = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[w.FFT_N], batch=w.FFT_BATCH), stream=sp)
+        fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), 2 * w.FFT_N * w.FFT_BATCH * 8
+    elif args.only == "zeta":
+        z = w.torch_zeta_input(w.ZETA_LOG_N, w.ZETA_BATCH, dev)
+        t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << w.ZETA_LOG_N],
+                         batch=w.ZETA_BATCH, in_place=True)
+        p = cb.Plan(lib, t, stream=sp)
+        fn, nbytes = (lambda i: p.execute(z.data_ptr(), z.data_ptr())), 2 * (1 << w.ZETA_LOG_N) * w.ZETA_BATCH * 4
+    else:
+        cfg = w.rns_config()
+        qs = [d["modulus"] for d in cfg["domains"]]
+        x = w.torch_ntt_input(qs, w.NTT_LOG_N, dev)
+        y = torch.empty_like(x)
+        p = rns.Plan(rns.Library(), cfg)
+        p.prepare(stream=sp, repetitions=1)
+        fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr(), stream=sp)), 2 * w.NTT_LIMBS * (1 << w.NTT_LOG_N) * 8
+    ms = time_launches(fn, stream, args.steps, args.warmup)
+    print(json.dumps({"only": args.only, "ms_per_launch": round(ms, 5), "gbs": round(nbytes / ms / 1e6, 1)}))
+    p.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.only:
+        return only_op(args)
     import numpy as np
     import torch
     import torch.distributed as dist

@@ -21,17 +21,51 @@
 namespace cubf::bw {
 
 // ---- operators --------------------------------------------------------------
-// apply(lo, hi): lo has the stage bit clear, hi has it set.
+// apply(lo, hi): lo has the stage bit clear, hi has it set.  apply2 does two
+// independent butterflies (lo0, hi0), (lo1, hi1) at once; for FWHT in fp32 it
+// issues Blackwell's packed add.f32x2 / sub.f32x2 (two lanes per instruction).
 struct FwhtOp {
+    static constexpr bool kPacked = true;
     template <typename T>
     static CUBF_DEV void apply(T& lo, T& hi, int) {
         const T a = lo, b = hi;
         lo = a + b;
         hi = a - b;
     }
+    static CUBF_DEV void apply2(float& lo0, float& lo1, float& hi0, float& hi1, int) {
+        float s0, s1, d0, d1;
+        asm("{\n\t.reg .b64 a, b, s, d;\n\t"
+            "mov.b64 a, {%4, %5};\n\t"
+            "mov.b64 b, {%6, %7};\n\t"
+            "add.rn.f32x2 s, a, b;\n\t"
+            "sub.rn.f32x2 d, a, b;\n\t"
+            "mov.b64 {%0, %1}, s;\n\t"
+            "mov.b64 {%2, %3}, d;\n\t}"
+            : "=f"(s0), "=f"(s1), "=f"(d0), "=f"(d1)
+            : "f"(lo0), "f"(lo1), "f"(hi0), "f"(hi1));
+        lo0 = s0;
+        lo1 = s1;
+        hi0 = d0;
+        hi1 = d1;
+    }
 };
+
+// x * scale for two fp32 values with one packed multiply.
+CUBF_DEV void scale2(float& a, float& b, float s) {
+    float o0, o1;
+    asm("{\n\t.reg .b64 x, y, z;\n\t"
+        "mov.b64 x, {%2, %3};\n\t"
+        "mov.b64 y, {%4, %4};\n\t"
+        "mul.rn.f32x2 z, x, y;\n\t"
+        "mov.b64 {%0, %1}, z;\n\t}"
+        : "=f"(o0), "=f"(o1)
+        : "f"(a), "f"(b), "f"(s));
+    a = o0;
+    b = o1;
+}
 template <bool SUPERSET>
 struct ZetaOp {
+    static constexpr bool kPacked = false;
     // subset: f[S | bit] += f[S]; superset: f[S] += f[S | bit]; inverse subtracts.
     template <typename T>
     static CUBF_DEV void apply(T& lo, T& hi, int inverse) {
@@ -109,12 +143,26 @@ struct TileShape {
     static constexpr Groups G = make_groups<LOGH, LOGW, LOGE, LOGV>();
     static constexpr int TPB = TPT >= 128 ? TPT : 128;
     static constexpr int TILES = TPB / TPT;  // tiles per CTA
-    static constexpr int BANK_SHIFT = sizeof(TC) == 8 ? 4 : 5;
-    static constexpr int PADDED = (1 << LT) + ((1 << LT) >> BANK_SHIFT);
-    static constexpr int SMEM_BYTES = G.count > 1 ? TILES * PADDED * static_cast<int>(sizeof(TC)) : 0;
-    static CUBF_DEV int pad(uint32_t e) { return static_cast<int>(e + (e >> BANK_SHIFT)); }
-    // Final group stores 16-byte vectors when it holds bits 0..LOGV-1.
+    // Final group stores 16-byte vectors when it holds bits 0..LOGV-1;
+    // otherwise the narrowed results go back through shared memory into the
+    // group-1 layout and leave as 16-byte vectors (STAGE_OUT).
     static constexpr bool VEC_STORE = LOGV > 0 && (G.reg[G.count - 1] & lowmask(LOGV)) == lowmask(LOGV);
+    static constexpr bool STAGE_OUT = LOGV > 0 && !VEC_STORE;
+    // Exchange layout ("reader-contiguous"): the E values a thread reads in
+    // the next group are contiguous (16-byte loads), rows of E padded by one
+    // 16-byte chunk so consecutive readers start in different banks.
+    static constexpr int PADC = 16 / static_cast<int>(sizeof(TC));
+    static constexpr int PADS = 16 / static_cast<int>(sizeof(TS));
+    static constexpr int XCH_BYTES = TPT * (E + PADC) * static_cast<int>(sizeof(TC));
+    static constexpr int OUT_BYTES = STAGE_OUT ? TPT * (E + PADS) * static_cast<int>(sizeof(TS)) : 0;
+    static constexpr int TILE_SMEM = G.count > 1 || STAGE_OUT ? (XCH_BYTES > OUT_BYTES ? XCH_BYTES : OUT_BYTES) : 0;
+    static constexpr int SMEM_BYTES = TILES * TILE_SMEM;
+    // Offset (in elements) of tile element e in a buffer laid out for a
+    // reader whose register bits are RN.
+    template <uint32_t RN, int PAD>
+    static CUBF_DEV int xaddr(uint32_t e) {
+        return static_cast<int>(extract(e, lowmask(LT) & ~RN) * (E + PAD) + extract(e, RN));
+    }
 };
 
 // Apply the stages STAGE (tile-index bits) of a group whose registers hold the
@@ -125,11 +173,27 @@ CUBF_DEV void apply_group(TC (&v)[1 << LOGE], int inverse) {
 #pragma unroll
     for (int j = 0; j < LOGE; ++j) {
         if ((RSTAGE >> j) & 1u) {
+            if constexpr (Op::kPacked && std::is_same<TC, float>::value && LOGE >= 2) {
+                // pair butterflies along register bit k (0, or 1 for the stage on bit 0)
+                const int k = j == 0 ? 1 : 0;
 #pragma unroll
-            for (int r = 0; r < (1 << LOGE); ++r)
-                if (!((r >> j) & 1)) Op::apply(v[r], v[r | (1 << j)], inverse);
+                for (int r = 0; r < (1 << LOGE); ++r)
+                    if (!((r >> j) & 1) && !((r >> k) & 1))
+                        Op::apply2(v[r], v[r | (1 << k)], v[r | (1 << j)], v[r | (1 << j) | (1 << k)], inverse);
+            } else {
+#pragma unroll
+                for (int r = 0; r < (1 << LOGE); ++r)
+                    if (!((r >> j) & 1)) Op::apply(v[r], v[r | (1 << j)], inverse);
+            }
         }
     }
+}
+
+// 16-byte shared-memory vector access of N elements of T.
+template <typename T>
+CUBF_DEV void lds16(const T* p, T* out) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    *reinterpret_cast<uint4*>(out) = u;
 }
 
 // Shared-memory exchange into group K and its stages, then the rest.
@@ -140,14 +204,21 @@ CUBF_DEV void exchange_groups(typename S::TC (&v)[S::E], typename S::TC* tbuf, u
         constexpr uint32_t RN = S::G.reg[K];
         constexpr Offsets<S::E> OP = make_offsets<S::E>(RP);
         constexpr Offsets<S::E> ON = make_offsets<S::E>(RN);
+        (void)ON;
         if constexpr (K > 1) __syncthreads();  // previous exchange's reads are done
         const uint32_t tp = deposit_rt<lowmask(S::LT) & ~RP, S::LT>(t);
 #pragma unroll
-        for (int r = 0; r < S::E; ++r) tbuf[S::pad(tp | OP.v[r])] = v[r];
+        for (int r = 0; r < S::E; ++r) tbuf[S::template xaddr<RN, S::PADC>(tp | OP.v[r])] = v[r];
         __syncthreads();
-        const uint32_t tn = deposit_rt<lowmask(S::LT) & ~RN, S::LT>(t);
+        // the reader's E values are contiguous: row t, padded
+        const typename S::TC* row = tbuf + static_cast<int>(t) * (S::E + S::PADC);
+        if constexpr (S::E >= S::PADC) {
 #pragma unroll
-        for (int r = 0; r < S::E; ++r) v[r] = tbuf[S::pad(tn | ON.v[r])];
+            for (int r = 0; r < S::E; r += S::PADC) lds16(row + r, &v[r]);
+        } else {
+#pragma unroll
+            for (int r = 0; r < S::E; ++r) v[r] = row[r];
+        }
         apply_group<Op, S::LOGE, RN, S::G.stage[K]>(v, inverse);
         exchange_groups<Op, S, K + 1>(v, tbuf, t, inverse);
     }
@@ -166,7 +237,6 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
     constexpr Groups G = S::G;
     constexpr int LT = S::LT;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    TC* smem = reinterpret_cast<TC*>(smem_raw);
 
     const int local = threadIdx.x / S::TPT;
     const uint32_t t = threadIdx.x % S::TPT;
@@ -187,7 +257,7 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
         else
             return (static_cast<size_t>(e >> LOGW) << li) + (e & lowmask(LOGW));
     };
-    TC* tbuf = smem + local * S::PADDED;
+    TC* tbuf = reinterpret_cast<TC*>(smem_raw + local * S::TILE_SMEM);
 
     TC v[S::E];
     {  // group 1: 16-byte vector loads along bits 0..LOGV-1
@@ -215,16 +285,38 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
     apply_group<Op, S::LOGE, G.reg[0], G.stage[0]>(v, inverse);
     exchange_groups<Op, S, 1>(v, tbuf, t, inverse);
 
-    if (!active) return;
     constexpr uint32_t RF = G.reg[G.count - 1];
     constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
     const uint32_t tf = deposit_rt<lowmask(LT) & ~RF, LT>(t);
-    auto narrow = [&](TC x) -> TS {
-        if constexpr (std::is_floating_point<TC>::value)
-            return Convert<TS, TC>::store(x * scale);
-        else
-            return Convert<TS, TC>::store(x);
-    };
+    if constexpr (std::is_same<TC, float>::value) {
+        if (scale != 1.0f) {
+#pragma unroll
+            for (int r = 0; r < S::E; r += 2) scale2(v[r], v[r + 1], scale);
+        }
+    }
+    auto narrow = [&](TC x) -> TS { return Convert<TS, TC>::store(x); };
+    if constexpr (S::STAGE_OUT) {
+        // narrowed values -> shared memory in the group-1 (vector) layout ->
+        // 16-byte stores; the buffer is the exchange buffer, reused
+        constexpr uint32_t R0 = G.reg[0];
+        TS* obuf = reinterpret_cast<TS*>(tbuf);
+        if constexpr (G.count > 1) __syncthreads();  // exchange reads are done
+#pragma unroll
+        for (int r = 0; r < S::E; ++r) obuf[S::template xaddr<R0, S::PADS>(tf | OF.v[r])] = narrow(v[r]);
+        __syncthreads();
+        if (!active) return;
+        constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
+        const uint32_t te = deposit_rt<lowmask(LT) & ~R0, LT>(t);
+        const TS* row = obuf + static_cast<int>(t) * (S::E + S::PADS);
+#pragma unroll
+        for (int q = 0; q < S::E / S::V; ++q) {
+            Vec16<TS> x;
+            lds16(row + q * S::V, x.v);
+            stg_stream(reinterpret_cast<Vec16<TS>*>(tout + addr(te | O0.v[q * S::V])), x);
+        }
+        return;
+    }
+    if (!active) return;
     if constexpr (S::VEC_STORE) {
 #pragma unroll
         for (int q = 0; q < S::E / S::V; ++q) {

@@ -49,11 +49,13 @@ struct cubutterflyPlan {
     void* workspace = nullptr;
     std::size_t workspace_size = 0;
     void* twiddles = nullptr;  // FFT: W_N^k, k < N, complex fp32
+    unsigned* device_status = nullptr;  // error word written by bounded device waits
     int device = 0;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
     ~cubutterflyPlan() {
         if (twiddles) cudaFree(twiddles);
+        if (device_status) cudaFree(device_status);
     }
 };
 
@@ -197,7 +199,8 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
     const std::size_t n = d.extents[0];
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
         const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
-        check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream),
+        check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream,
+                                          p.device_status),
                    "FFT launch");
         return;
     }
@@ -240,6 +243,8 @@ double time_mapping(cubutterflyPlan& p, const cubf::Mapping& m, const void* in, 
 }
 
 void build_tables(cubutterflyPlan& p) {
+    check_cuda(cudaMalloc(reinterpret_cast<void**>(&p.device_status), sizeof(unsigned)), "status word allocation");
+    check_cuda(cudaMemset(p.device_status, 0, sizeof(unsigned)), "status word init");
     if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
     const std::size_t n = p.desc.extents[0];
     std::vector<float> tw(2 * n);
@@ -765,6 +770,16 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         cubf::Json out = cubf::Json::array();
         for (const auto& m : cubf::enumerate_mappings(make_request(d), hw)) out.push_back(m.to_json());
         copy_text(out.dump(), json, bytes);
+    });
+}
+
+cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterflyHandle_t handle, cubutterflyPlan_t plan,
+                                                       unsigned* status, int reset) {
+    return protect([&] {
+        require(handle != nullptr && plan != nullptr && status != nullptr, "handle, plan and status must be non-null");
+        check_cuda(cudaStreamSynchronize(handle->stream), "stream synchronize");
+        check_cuda(cudaMemcpy(status, plan->device_status, sizeof(unsigned), cudaMemcpyDeviceToHost), "status read");
+        if (reset) check_cuda(cudaMemset(plan->device_status, 0, sizeof(unsigned)), "status reset");
     });
 }
 

@@ -24,8 +24,9 @@ struct LaunchShape {
 // ---- FFT (complex fp32) ------------------------------------------------------
 constexpr int kFftLocalMaxLog = 13;
 LaunchShape fft_local_shape(int log_n);
+// `err` is a device word that receives error codes from bounded waits (or null).
 cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
-                             bool inverse, float scale, cudaStream_t stream);
+                             bool inverse, float scale, cudaStream_t stream, unsigned* err);
 
 // ---- FWHT / zeta tile passes --------------------------------------------------
 enum class BwOp { Fwht = 0, ZetaSubset = 1, ZetaSuperset = 2 };

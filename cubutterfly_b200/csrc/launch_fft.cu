@@ -2,6 +2,8 @@
 #include "fft.cuh"
 #include "kernels.hpp"
 
+#include <cstdint>
+
 namespace cubf {
 namespace {
 
@@ -17,10 +19,43 @@ LaunchShape shape_of() {
     return s;
 }
 
+constexpr int kStages = 2;
+
+// Persistent TMA-pipelined variant for rows of at least 2 KB (LOGN >= 8).
+template <int LOGN>
+cudaError_t launch_tma(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
+                       cudaStream_t stream, unsigned* err) {
+    using S = fft::LocalShape<LOGN>;
+    using T = fft::TmaShape<LOGN, kStages>;
+    auto kernel = fft::fft_tma_kernel<LOGN, kStages>;
+    static int grid_cap = 0;
+    if (grid_cap == 0) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        int per_sm = 0, dev = 0, sms = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, S::TPB, T::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        grid_cap = (per_sm > 0 ? per_sm : 1) * sms;
+    }
+    const std::size_t tiles = (batch + S::TPC - 1) / S::TPC;
+    if (tiles == 0) return cudaSuccess;
+    const unsigned grid = static_cast<unsigned>(tiles < static_cast<std::size_t>(grid_cap) ? tiles : grid_cap);
+    kernel<<<grid, S::TPB, T::SMEM_BYTES, stream>>>(static_cast<const float2*>(in), static_cast<float2*>(out), batch,
+                                                    static_cast<const float2*>(tw), inverse ? 1 : 0, scale, err);
+    return cudaGetLastError();
+}
+
 template <int LOGN>
 cudaError_t launch(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, unsigned* err) {
     using S = fft::LocalShape<LOGN>;
+    if constexpr (LOGN >= 8 && LOGN <= 12) {
+        // bulk copies need 16-byte aligned rows (always: N * 8 bytes, N >= 2)
+        if ((reinterpret_cast<std::uintptr_t>(in) & 15) == 0)
+            return launch_tma<LOGN>(in, out, batch, tw, inverse, scale, stream, err);
+    }
     auto kernel = fft::fft_local_kernel<LOGN>;
     static bool configured = false;
     if (!configured) {
@@ -37,7 +72,7 @@ cudaError_t launch(const void* in, void* out, std::size_t batch, const void* tw,
     return cudaGetLastError();
 }
 
-using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, const void*, bool, float, cudaStream_t);
+using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, const void*, bool, float, cudaStream_t, unsigned*);
 using ShapeFn = LaunchShape (*)();
 
 template <int... L>
@@ -55,9 +90,9 @@ LaunchShape fft_local_shape(int log_n) {
 }
 
 cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
-                             bool inverse, float scale, cudaStream_t stream) {
+                             bool inverse, float scale, cudaStream_t stream, unsigned* err) {
     if (log_n < 1 || log_n > kFftLocalMaxLog) return cudaErrorInvalidValue;
-    return Local::launch_fns[log_n - 1](in, out, batch, twiddles, inverse, scale, stream);
+    return Local::launch_fns[log_n - 1](in, out, batch, twiddles, inverse, scale, stream, err);
 }
 
 }  // namespace cubf

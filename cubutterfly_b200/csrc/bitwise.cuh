@@ -231,8 +231,12 @@ CUBF_DEV void exchange_groups(typename S::TC (&v)[S::E], typename S::TC* tbuf, u
 // writing any).  Floating-point results are multiplied by `scale` before the
 // final narrowing (the FINAL_STORAGE epilogue).
 template <typename Op, typename TS, typename TC, int LOGH, int LOGW, int LOGE>
-__global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
-    bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale) {
+__global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
+                                  (512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB > 0
+                                       ? 512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB
+                                       : 1))
+    bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale,
+                        int cache_mode) {
     using S = TileShape<TS, TC, LOGH, LOGW, LOGE>;
     constexpr Groups G = S::G;
     constexpr int LT = S::LT;
@@ -259,6 +263,10 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
     };
     TC* tbuf = reinterpret_cast<TC*>(smem_raw + local * S::TILE_SMEM);
 
+    // L2 policies: the input of a chain's first pass and the last pass's
+    // output are not read again; chain intermediates are kept.
+    const uint64_t ld_pol = l2_policy(false);
+    const uint64_t st_pol = l2_policy(cache_mode == kChainFirst || cache_mode == kChainMiddle);
     TC v[S::E];
     {  // group 1: 16-byte vector loads along bits 0..LOGV-1
         constexpr uint32_t R0 = G.reg[0];
@@ -270,7 +278,8 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
             if constexpr (S::V > 1) {
                 Vec16<TS> x;
                 if (active) {
-                    x = ldg_stream(reinterpret_cast<const Vec16<TS>*>(tin + addr(e)));
+                    const uint4 w = ld16_hint(tin + addr(e), ld_pol);
+                    x = *reinterpret_cast<const Vec16<TS>*>(&w);
                 } else {
 #pragma unroll
                     for (int i = 0; i < S::V; ++i) x.v[i] = TS{};
@@ -312,7 +321,7 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
         for (int q = 0; q < S::E / S::V; ++q) {
             Vec16<TS> x;
             lds16(row + q * S::V, x.v);
-            stg_stream(reinterpret_cast<Vec16<TS>*>(tout + addr(te | O0.v[q * S::V])), x);
+            st16_hint(tout + addr(te | O0.v[q * S::V]), *reinterpret_cast<const uint4*>(&x), st_pol);
         }
         return;
     }
@@ -323,7 +332,7 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB)
             Vec16<TS> x;
 #pragma unroll
             for (int i = 0; i < S::V; ++i) x.v[i] = narrow(v[q * S::V + i]);
-            stg_stream(reinterpret_cast<Vec16<TS>*>(tout + addr(tf | OF.v[q * S::V])), x);
+            st16_hint(tout + addr(tf | OF.v[q * S::V]), *reinterpret_cast<const uint4*>(&x), st_pol);
         }
     } else {
 #pragma unroll

@@ -210,18 +210,31 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
         scale = d.output_scale;
         if (inverse && d.normalize_inverse) scale /= static_cast<double>(n);
     }
-    const void* src = in;
-    for (std::size_t i = 0; i < m.passes.size(); ++i) {
-        const auto& ps = m.passes[i];
-        const bool last = i + 1 == m.passes.size();
-        const std::size_t inner = std::size_t{1} << ps.log_inner;
-        const std::size_t outer = d.batch * (n >> (ps.log_inner + ps.log_h));
-        const std::size_t inner_arg = ps.log_w == 0 ? 1 : inner;
-        const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
-        check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, out, outer_arg, inner_arg,
-                                   inverse, last ? static_cast<float>(scale) : 1.0f, stream),
-                   "tile pass launch");
-        src = out;
+    // Multi-pass chains run chunk by chunk: every pass over a chunk of
+    // transforms sized to stay in L2, so the intermediate written by one pass
+    // is read by the next from L2 instead of HBM.
+    const std::size_t esz = cubf::bw_type_bytes(p.req.bw_type);
+    const std::size_t transform_bytes = n * esz;
+    const std::size_t budget = std::max<std::size_t>(p.hw.l2_bytes * 2 / 5, 1);
+    const bool chained = m.passes.size() > 1;
+    const std::size_t chunk = chained ? std::max<std::size_t>(1, budget / transform_bytes) : d.batch;
+    for (std::size_t b0 = 0; b0 < d.batch; b0 += chunk) {
+        const std::size_t nb = std::min(chunk, d.batch - b0);
+        const void* src = static_cast<const unsigned char*>(in) + b0 * transform_bytes;
+        void* dst = static_cast<unsigned char*>(out) + b0 * transform_bytes;
+        for (std::size_t i = 0; i < m.passes.size(); ++i) {
+            const auto& ps = m.passes[i];
+            const bool last = i + 1 == m.passes.size();
+            const std::size_t inner = std::size_t{1} << ps.log_inner;
+            const std::size_t outer = nb * (n >> (ps.log_inner + ps.log_h));
+            const std::size_t inner_arg = ps.log_w == 0 ? 1 : inner;
+            const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
+            const int mode = !chained ? 0 : (i == 0 ? 1 : (last ? 2 : 3));
+            check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, dst, outer_arg,
+                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream),
+                       "tile pass launch");
+            src = dst;
+        }
     }
 }
 

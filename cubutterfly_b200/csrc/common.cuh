@@ -117,6 +117,33 @@ struct alignas(16) Vec16 {
     T v[N];
 };
 
+// L2 residency hints for the tile passes.  A single-pass transform streams
+// (evict-first both ways); in a multi-pass chain run on an L2-sized chunk the
+// intermediate is stored evict-last so the next pass reads it from L2, and the
+// final pass streams its output.
+enum CacheMode : int { kStream = 0, kChainFirst = 1, kChainLast = 2, kChainMiddle = 3 };
+
+CUBF_DEV uint64_t l2_policy(bool keep) {
+    uint64_t p;
+    if (keep)
+        asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    else
+        asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+CUBF_DEV uint4 ld16_hint(const void* p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol));
+    return r;
+}
+CUBF_DEV void st16_hint(void* p, uint4 v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v4.u32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w), "l"(pol)
+                 : "memory");
+}
+
 // Streaming loads/stores: the transforms touch each byte once, so keep them
 // out of L1 and mark them evict-first in L2.
 template <typename T>

@@ -94,6 +94,30 @@ struct Dft<1> {
     static CUBF_DEV void run(float2*) {}
 };
 
+// Twiddles W_N^k from two small tables in shared memory: W_N^k =
+// hi[k >> 6] * lo[k & 63], both factors exact-rounded fp32 (one extra product
+// rounding, far below the fp32 FFT error).  N/64 + 64 entries.
+template <int LOGN>
+struct TwiddleTable {
+    static constexpr int LO_BITS = LOGN < 6 ? LOGN : 6;
+    static constexpr int NLO = 1 << LO_BITS;
+    static constexpr int NHI = 1 << (LOGN - LO_BITS);
+    static constexpr int ENTRIES = NLO + NHI;
+    static constexpr int BYTES = ENTRIES * 8;
+    const float2* lo;
+    const float2* hi;
+    // fill from the global table of W_N^k, k < N (all threads of the CTA)
+    static CUBF_DEV TwiddleTable load(float2* smem, const float2* __restrict__ tw) {
+        for (int i = threadIdx.x; i < NLO; i += blockDim.x) smem[i] = __ldg(tw + i);
+        for (int i = threadIdx.x; i < NHI; i += blockDim.x) smem[NLO + i] = __ldg(tw + (i << LO_BITS));
+        return TwiddleTable{smem, smem + NLO};
+    }
+    CUBF_DEV float2 operator()(int k) const {
+        if constexpr (NHI == 1) return lo[k];
+        else return cmul(hi[k >> LO_BITS], lo[k & (NLO - 1)]);
+    }
+};
+
 // Pass schedule of an in-CTA transform of 2^LOGN points: ceil(LOGN/4) passes,
 // radix bits balanced so every pass has radix <= 16.
 template <int LOGN>
@@ -115,7 +139,7 @@ struct LocalShape {
     static constexpr int TPB = T >= 128 ? T : 128;  // threads per CTA
     static constexpr int TPC = TPB / T;             // transforms per CTA
     static constexpr bool DOUBLE_BUFFER = LOGN <= 12;
-    static constexpr int SMEM_BYTES = (DOUBLE_BUFFER ? 2 : 1) * TPC * PADDED * 8;
+    static constexpr int SMEM_BYTES = (DOUBLE_BUFFER ? 2 : 1) * TPC * PADDED * 8 + TwiddleTable<LOGN>::BYTES;
 };
 
 // One Stockham pass P of a 2^LOGN transform, split in two halves so the
@@ -124,7 +148,7 @@ struct LocalShape {
 // W_{Ns R}^{(j mod Ns) r} = W_N^{(j mod Ns) r N/(Ns R)}, run the register DFT;
 // then store with the Stockham autosort index.
 template <int LOGN, int P, typename Load>
-CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const float2* __restrict__ tw, Load load) {
+CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const TwiddleTable<LOGN>& tw, Load load) {
     using S = LocalShape<LOGN>;
     constexpr int RB = S::radix_bits(P);
     constexpr int R = 1 << RB;
@@ -145,7 +169,7 @@ CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const float2* 
 #pragma unroll
             for (int r = 1; r < R; ++r) {
                 const int k = (jm * r) << (LOGN - NSB - RB);
-                v[u * R + r] = cmul(v[u * R + r], __ldg(tw + k));
+                v[u * R + r] = cmul(v[u * R + r], tw(k));
             }
         }
         Dft<R>::run(&v[u * R]);
@@ -174,7 +198,7 @@ CUBF_DEV void pass_store(const float2 (&v)[LocalShape<LOGN>::E], int th, Store s
 template <int LOGN, int P, bool DB = LocalShape<LOGN>::DOUBLE_BUFFER>
 struct Passes {
     template <typename GLoad, typename GStore>
-    static CUBF_DEV void run(float2 (&v)[LocalShape<LOGN>::E], int th, const float2* __restrict__ tw,
+    static CUBF_DEV void run(float2 (&v)[LocalShape<LOGN>::E], int th, const TwiddleTable<LOGN>& tw,
                              float2* buf0, float2* buf1, GLoad gload, GStore gstore) {
         using S = LocalShape<LOGN>;
         if constexpr (P == 0) {
@@ -211,6 +235,8 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
     float2* dst = out + row * S::N;
     float2* buf0 = smem + c * S::PADDED;
     float2* buf1 = S::DOUBLE_BUFFER ? buf0 + S::TPC * S::PADDED : buf0;
+    const auto twt = TwiddleTable<LOGN>::load(smem + (S::DOUBLE_BUFFER ? 2 : 1) * S::TPC * S::PADDED, tw);
+    __syncthreads();
     const float sgn = inverse ? -1.f : 1.f;
     float2 v[S::E];
     auto gload = [&](int i) -> float2 {
@@ -221,7 +247,7 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
     auto gstore = [&](int i, float2 x) {
         if (active) __stcs(dst + i, make_float2(x.x * scale, x.y * sgn * scale));
     };
-    Passes<LOGN, 0>::run(v, th, tw, buf0, buf1, gload, gstore);
+    Passes<LOGN, 0>::run(v, th, twt, buf0, buf1, gload, gstore);
 }
 
 // Persistent variant: each CTA walks tiles of TPC contiguous transforms,
@@ -234,7 +260,8 @@ struct TmaShape {
     static constexpr int TILE_ELEMS = S::TPC * S::N;
     static constexpr int TILE_BYTES = TILE_ELEMS * 8;
     static constexpr int XCH_ELEMS = S::NPASS > 1 ? S::TPC * S::PADDED : 0;
-    static constexpr int BAR_OFFSET = (STAGES * TILE_ELEMS + XCH_ELEMS) * 8;
+    static constexpr int TW_OFFSET = (STAGES * TILE_ELEMS + XCH_ELEMS) * 8;
+    static constexpr int BAR_OFFSET = TW_OFFSET + TwiddleTable<LOGN>::BYTES;
     static constexpr int SMEM_BYTES = BAR_OFFSET + STAGES * 8;
 };
 
@@ -255,6 +282,7 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
         for (int st = 0; st < STAGES; ++st) tma::mbar_init(&bar[st], 1);
         tma::fence_barrier_init();
     }
+    const auto twt = TwiddleTable<LOGN>::load(reinterpret_cast<float2*>(smem_raw + T::TW_OFFSET), tw);
     __syncthreads();
     auto issue = [&](int st, size_t tile) {
         const size_t first = tile * S::TPC;
@@ -293,7 +321,7 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
         auto gstore = [&](int i, float2 x) {
             if (active) __stcs(dst + i, make_float2(x.x * scale, x.y * sgn * scale));
         };
-        Passes<LOGN, 0, false>::run(v, th, tw, xb, xb, gload, gstore);
+        Passes<LOGN, 0, false>::run(v, th, twt, xb, xb, gload, gstore);
         __syncthreads();  // ring slot and exchange buffer are free
         if (threadIdx.x == 0) {
             const size_t next = tile + static_cast<size_t>(STAGES) * gridDim.x;

@@ -4,6 +4,7 @@
 // with CUBF_BW_OP and CUBF_BW_TYPE defined, so the instantiation sets compile
 // in parallel.  launch_bitwise_dispatch.cpp routes a BwVariant to the unit.
 #include "bitwise.cuh"
+#include "fwht.cuh"
 #include "kernels.hpp"
 
 #ifndef CUBF_BW_OP
@@ -47,6 +48,47 @@ constexpr int kLogW = sizeof(TS) == 8 ? 3 : (sizeof(TS) == 4 ? 4 : 5);  // 64-by
 constexpr int kMaxContig = sizeof(TC) == 8 ? 13 : 14;
 constexpr int kMaxStrided = sizeof(TC) == 8 ? 9 : 10;
 
+#if CUBF_BW_OP == 0
+// FWHT tiles: one thread per row up to 128 values (no exchange), then 64
+// values per thread; rows narrower than one 16-byte vector use the generic kernel.
+constexpr int fwht_log_e(int logh) { return logh <= 7 ? logh : 6; }
+constexpr bool fwht_pair_kernel(int logh) { return (1 << logh) * static_cast<int>(sizeof(TS)) >= 16; }
+
+template <int LOGH>
+struct FwhtEntry {
+    static constexpr int LOGE = fwht_log_e(LOGH);
+    using S = fwht::FwhtShape<TS, LOGH, LOGE>;
+    static LaunchShape shape() {
+        LaunchShape s;
+        s.threads = S::TPB;
+        s.smem_bytes = S::SMEM_BYTES;
+        s.units_per_cta = S::TILES;
+        s.elems_per_thread = S::E;
+        s.exchanges = S::G.count - 1 + (S::STAGE_OUT ? 1 : 0);
+        return s;
+    }
+    static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
+                              float scale, int cache_mode, cudaStream_t stream) {
+        (void)inverse;  // FWHT is its own inverse up to the scale
+        (void)cache_mode;
+        auto kernel = fwht::fwht_tile_kernel<TS, LOGH, LOGE>;
+        static bool configured = false;
+        if (!configured && S::SMEM_BYTES > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+        }
+        configured = true;
+        if (inner != 1) return cudaErrorInvalidValue;
+        const std::size_t blocks = (outer + S::TILES - 1) / S::TILES;
+        if (blocks == 0) return cudaSuccess;
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+            static_cast<const TS*>(in), static_cast<TS*>(out), outer, scale);
+        return cudaGetLastError();
+    }
+};
+#endif
+
 template <int LOGH, int LOGW>
 struct Entry {
     using S = bw::TileShape<TS, TC, LOGH, LOGW, kLogE>;
@@ -60,7 +102,7 @@ struct Entry {
         return s;
     }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
-                              float scale, cudaStream_t stream) {
+                              float scale, int cache_mode, cudaStream_t stream) {
         auto kernel = bw::bitwise_tile_kernel<Op, TS, TC, LOGH, LOGW, kLogE>;
         static bool configured = false;
         if (!configured && S::SMEM_BYTES > 48 * 1024) {
@@ -77,18 +119,36 @@ struct Entry {
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
         kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-            static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0, scale);
+            static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0, scale, cache_mode);
         return cudaGetLastError();
     }
 };
 
-using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, cudaStream_t);
+using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, int, cudaStream_t);
 using ShapeFn = LaunchShape (*)();
+
+#if CUBF_BW_OP == 0
+template <int H>
+constexpr LaunchFn contig_launch() {
+    if constexpr (fwht_pair_kernel(H)) return FwhtEntry<H>::launch;
+    else return Entry<H, 0>::launch;
+}
+template <int H>
+constexpr ShapeFn contig_shape() {
+    if constexpr (fwht_pair_kernel(H)) return FwhtEntry<H>::shape;
+    else return Entry<H, 0>::shape;
+}
+#else
+template <int H>
+constexpr LaunchFn contig_launch() { return Entry<H, 0>::launch; }
+template <int H>
+constexpr ShapeFn contig_shape() { return Entry<H, 0>::shape; }
+#endif
 
 template <int... H>
 struct Contig {
-    static constexpr LaunchFn launch[] = {Entry<H, 0>::launch...};
-    static constexpr ShapeFn shape[] = {Entry<H, 0>::shape...};
+    static constexpr LaunchFn launch[] = {contig_launch<H>()...};
+    static constexpr ShapeFn shape[] = {contig_shape<H>()...};
 };
 template <int... H>
 struct Strided {
@@ -126,11 +186,12 @@ LaunchShape CUBF_CAT(CUBF_UNIT, _shape)(int log_h, int log_w) {
 }
 
 cudaError_t CUBF_CAT(CUBF_UNIT, _launch)(int log_h, int log_w, const void* in, void* out, std::size_t outer,
-                                         std::size_t inner, bool inverse, float scale, cudaStream_t stream) {
+                                         std::size_t inner, bool inverse, float scale, int cache_mode,
+                                         cudaStream_t stream) {
     if (log_w == 0 && log_h >= 1 && log_h <= kMaxContig)
-        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, stream);
+        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream);
     if (kHasStrided && log_w == kLogW && log_h >= 1 && log_h <= kMaxStrided)
-        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, stream);
+        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream);
     return cudaErrorInvalidValue;
 }
 

@@ -48,13 +48,18 @@ struct cubutterflyPlan {
     std::size_t output_bytes = 0;
     void* workspace = nullptr;
     std::size_t workspace_size = 0;
-    void* twiddles = nullptr;  // FFT: W_N^k, k < N, complex fp32
+    void* twiddles = nullptr;  // FFT: W_N^k, k < N (local) or W_1024^k (global passes), complex fp32
+    void* outer_lo = nullptr;  // global FFT: double2 W_N^k, k < 2^split
+    void* outer_hi = nullptr;  // global FFT: double2 W_N^(k << split)
+    int outer_split = 0;
     unsigned* device_status = nullptr;  // error word written by bounded device waits
     int device = 0;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
     ~cubutterflyPlan() {
         if (twiddles) cudaFree(twiddles);
+        if (outer_lo) cudaFree(outer_lo);
+        if (outer_hi) cudaFree(outer_hi);
         if (device_status) cudaFree(device_status);
     }
 };
@@ -199,9 +204,35 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
     const std::size_t n = d.extents[0];
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
         const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
-        check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream,
-                                          p.device_status),
-                   "FFT launch");
+        if (m.passes.front().kind == cubf::PassKind::FftLocal) {
+            check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream,
+                                              p.device_status),
+                       "FFT launch");
+            return;
+        }
+        // Global passes ping-pong between the output and the workspace so the
+        // last pass lands in `out`; an in-place plan with an odd pass count
+        // starts in a second workspace half.
+        const std::size_t np = m.passes.size();
+        const std::size_t bytes = d.batch * n * 8;
+        unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+        const bool in_place = in == out;
+        const cubf::FftOuterTables outer{p.outer_lo, p.outer_hi, p.outer_split};
+        const void* src = in;
+        for (std::size_t i = 0; i < np; ++i) {
+            void* dst;
+            if ((np - 1 - i) % 2 == 0)
+                dst = (in_place && i == 0 && np > 1) ? ws + bytes : out;
+            else
+                dst = ws;
+            const bool last = i + 1 == np;
+            const auto& ps = m.passes[i];
+            check_cuda(cubf::launch_fft_global_pass(ps.log_h, src, dst, p.req.log_n, ps.log_inner, d.batch, p.twiddles,
+                                                    outer, inverse && i == 0, inverse && last, last ? scale : 1.0f,
+                                                    stream),
+                       "FFT pass launch");
+            src = dst;
+        }
         return;
     }
     // Bitwise tile passes: the first reads the input, the rest run in place.
@@ -259,9 +290,33 @@ void build_tables(cubutterflyPlan& p) {
     check_cuda(cudaMalloc(reinterpret_cast<void**>(&p.device_status), sizeof(unsigned)), "status word allocation");
     check_cuda(cudaMemset(p.device_status, 0, sizeof(unsigned)), "status word init");
     if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
-    const std::size_t n = p.desc.extents[0];
-    std::vector<float> tw(2 * n);
     constexpr double kPi = 3.141592653589793238462643383279502884;
+    const bool global = p.mapping.passes.front().kind == cubf::PassKind::FftGlobal;
+    if (global) {
+        // exp(-2 pi i k / N) for the outer twiddles, in double: lo k < 2^split, hi k << split
+        const int l = p.req.log_n;
+        const int split = (l + 1) / 2;
+        const std::size_t nlo = std::size_t{1} << split, nhi = std::size_t{1} << (l - split);
+        const double n_d = std::ldexp(1.0, l);
+        std::vector<double> lo(2 * nlo), hi(2 * nhi);
+        for (std::size_t k = 0; k < nlo; ++k) {
+            const double a = -2.0 * kPi * static_cast<double>(k) / n_d;
+            lo[2 * k] = std::cos(a);
+            lo[2 * k + 1] = std::sin(a);
+        }
+        for (std::size_t k = 0; k < nhi; ++k) {
+            const double a = -2.0 * kPi * static_cast<double>(k << split) / n_d;
+            hi[2 * k] = std::cos(a);
+            hi[2 * k + 1] = std::sin(a);
+        }
+        check_cuda(cudaMalloc(&p.outer_lo, lo.size() * 8), "twiddle table allocation");
+        check_cuda(cudaMalloc(&p.outer_hi, hi.size() * 8), "twiddle table allocation");
+        check_cuda(cudaMemcpy(p.outer_lo, lo.data(), lo.size() * 8, cudaMemcpyHostToDevice), "twiddle upload");
+        check_cuda(cudaMemcpy(p.outer_hi, hi.data(), hi.size() * 8, cudaMemcpyHostToDevice), "twiddle upload");
+        p.outer_split = split;
+    }
+    const std::size_t n = global ? 1024 : p.desc.extents[0];
+    std::vector<float> tw(2 * n);
     for (std::size_t k = 0; k < n; ++k) {
         // exp(-2 pi i k / N) in double, rounded once (reference butterfly.cu:1502-1514)
         const double a = -2.0 * kPi * static_cast<double>(k) / static_cast<double>(n);

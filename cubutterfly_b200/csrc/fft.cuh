@@ -106,10 +106,12 @@ struct TwiddleTable {
     static constexpr int BYTES = ENTRIES * 8;
     const float2* lo;
     const float2* hi;
-    // fill from the global table of W_N^k, k < N (all threads of the CTA)
-    static CUBF_DEV TwiddleTable load(float2* smem, const float2* __restrict__ tw) {
-        for (int i = threadIdx.x; i < NLO; i += blockDim.x) smem[i] = __ldg(tw + i);
-        for (int i = threadIdx.x; i < NHI; i += blockDim.x) smem[NLO + i] = __ldg(tw + (i << LO_BITS));
+    // fill from a global table of W_M^k (M = N << log_stride), so entry k of
+    // this table is tw[k << log_stride]; all threads of the CTA take part
+    static CUBF_DEV TwiddleTable load(float2* smem, const float2* __restrict__ tw, int log_stride = 0) {
+        for (int i = threadIdx.x; i < NLO; i += blockDim.x) smem[i] = __ldg(tw + (i << log_stride));
+        for (int i = threadIdx.x; i < NHI; i += blockDim.x)
+            smem[NLO + i] = __ldg(tw + ((i << LO_BITS) << log_stride));
         return TwiddleTable{smem, smem + NLO};
     }
     CUBF_DEV float2 operator()(int k) const {
@@ -327,6 +329,110 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
             const size_t next = tile + static_cast<size_t>(STAGES) * gridDim.x;
             if (next < tiles) issue(st, next);
         }
+    }
+}
+
+// ---- multi-pass global Stockham (N > 2^13) -----------------------------------
+//
+// Pass p of radix R = 2^LOGR over a length-N transform (Ns = 2^ns_bits is the
+// product of the earlier radices): for j < N/R, take x[j + n N/R] (n < R),
+// multiply by the outer twiddle W_{Ns R}^{(j mod Ns) n}, run the length-R DFT,
+// and write y[(j / Ns) Ns R + (j mod Ns) + k Ns].  A CTA takes C = 256/T
+// adjacent columns j (coalesced 8C-byte segments): it loads the C x R tile
+// into shared memory with the outer twiddle applied (fp64 two-level table,
+// rounded once), runs the in-CTA Stockham passes of LocalShape<LOGR> on each
+// column, and scatters the result with a mapping that keeps global stores
+// contiguous.
+template <int LOGR>
+struct GlobalPassShape {
+    using S = LocalShape<LOGR>;
+    static constexpr int R = 1 << LOGR;
+    static constexpr int TPB = 256;
+    static constexpr int C = TPB / S::T;         // columns per CTA
+    static constexpr int RS = S::PADDED + 1;     // padded row stride (float2)
+    static constexpr int TILE = C * R;
+    static constexpr int SMEM_BYTES = 2 * C * RS * 8 + TwiddleTable<LOGR>::BYTES;
+    static_assert(LOGR >= 4 && S::T * C == TPB, "global pass radix must be 16..4096 with whole columns");
+};
+
+struct OuterTwiddles {
+    const double2* lo;  // W_N^k, k < 2^split
+    const double2* hi;  // W_N^(k << split)
+    int split;
+};
+
+CUBF_DEV float2 outer_twiddle(const OuterTwiddles& t, size_t k) {
+    const double2 a = __ldg(t.lo + (k & ((size_t{1} << t.split) - 1)));
+    const double2 b = __ldg(t.hi + (k >> t.split));
+    return make_float2(static_cast<float>(a.x * b.x - a.y * b.y), static_cast<float>(a.x * b.y + a.y * b.x));
+}
+
+template <int LOGR>
+__global__ void __launch_bounds__(256, 2)
+    fft_global_pass_kernel(const float2* src, float2* dst, int log_n, int ns_bits, size_t batch,
+                           const float2* __restrict__ tw_r, int tw_log_stride, OuterTwiddles outer, int conj_in,
+                           int conj_out, float scale) {
+    using G = GlobalPassShape<LOGR>;
+    using S = typename G::S;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* a = reinterpret_cast<float2*>(smem_raw);
+    float2* b = a + G::C * G::RS;
+    const auto twt = TwiddleTable<LOGR>::load(b + G::C * G::RS, tw_r, tw_log_stride);
+    const size_t n = size_t{1} << log_n;
+    const size_t cols = n >> LOGR;                    // j range
+    const size_t ctas_per_batch = cols / G::C;
+    const size_t bidx = blockIdx.x / ctas_per_batch;
+    const size_t j0 = (blockIdx.x % ctas_per_batch) * G::C;
+    const size_t ns = size_t{1} << ns_bits;
+    const float2* sb = src + bidx * n;
+    float2* db = dst + bidx * n;
+    const float in_sgn = conj_in ? -1.f : 1.f;
+    const int tshift = log_n - ns_bits - LOGR;       // W_{Ns R}^m = W_N^(m << tshift)
+    // 1. coalesced tile load, outer twiddle applied
+    for (int idx = threadIdx.x; idx < G::TILE; idx += G::TPB) {
+        const int c = idx % G::C;
+        const int r = idx / G::C;
+        const size_t j = j0 + c;
+        float2 x = __ldcs(sb + j + static_cast<size_t>(r) * cols);
+        x.y *= in_sgn;
+        if (ns_bits > 0 && r > 0) {
+            const size_t m = (j & (ns - 1)) * static_cast<size_t>(r);
+            x = cmul(x, outer_twiddle(outer, m << tshift));
+        }
+        a[c * G::RS + S::pad(r)] = x;
+    }
+    __syncthreads();
+    // 2. length-R DFT of each column (in-CTA Stockham, b as exchange buffer)
+    {
+        const int c = threadIdx.x / S::T;
+        const int th = threadIdx.x % S::T;
+        float2* arow = a + c * G::RS;
+        float2* brow = b + c * G::RS;
+        float2 v[S::E];
+        auto load = [&](int i) { return arow[S::pad(i)]; };
+        auto store = [&](int i, float2 x) { arow[S::pad(i)] = x; };
+        if constexpr (S::NPASS == 1) {
+            // single in-register pass: every thread reads its values before any writes
+            pass_load<LOGR, 0>(v, th, twt, load);
+            __syncthreads();
+            pass_store<LOGR, 0>(v, th, store);
+        } else {
+            Passes<LOGR, 0, false>::run(v, th, twt, brow, brow, load, store);
+        }
+    }
+    __syncthreads();
+    // 3. scatter: element (c, k) -> y[((j)/Ns) Ns R + (j mod Ns) + k Ns], with
+    //    the fastest index chosen so consecutive threads write consecutive words
+    const int ne = ns < static_cast<size_t>(G::C) ? static_cast<int>(ns) : G::C;
+    const float out_sgn = conj_out ? -1.f : 1.f;
+    for (int idx = threadIdx.x; idx < G::TILE; idx += G::TPB) {
+        const int c_lo = idx % ne;
+        const int k = (idx / ne) % G::R;
+        const int c = (idx / (ne * G::R)) * ne + c_lo;
+        const size_t j = j0 + c;
+        const size_t o = ((j >> ns_bits) << (ns_bits + LOGR)) + (j & (ns - 1)) + static_cast<size_t>(k) * ns;
+        const float2 x = a[c * G::RS + S::pad(k)];
+        __stcs(db + o, make_float2(x.x * scale, x.y * out_sgn * scale));
     }
 }
 

@@ -69,8 +69,43 @@ struct PairIO<__half> {
     }
 };
 
+CUBF_DEV P fma2(P a, P b, P c) {
+    P r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
 template <typename TS, int LOGH, int LOGE>
 using FwhtShape = bw::TileShape<TS, float, LOGH, 0, LOGE>;
+
+// Rows of at most 4 threads finish their thread bits with warp shuffles: the
+// partner's value arrives over the lane crossbar and the butterfly is
+// own * (+1 | -1) + partner (exact), one packed FMA per pair.
+template <typename S>
+struct ShuffleFinish {
+    static constexpr bool value = S::TPT > 1 && S::TPT <= 4;
+};
+
+template <typename S>
+CUBF_DEV void shuffle_stages(P (&v)[S::E / 2], uint32_t t) {
+    constexpr uint32_t R0 = S::G.reg[0];
+    constexpr uint32_t THREAD_BITS = lowmask(S::LT) & ~R0;  // tile bits held across lanes
+#pragma unroll
+    for (int k = 0; k < S::LT - S::LOGE; ++k) {
+        // k-th thread bit <-> lane bit k of t (threads of a tile are adjacent lanes)
+        const float s = ((t >> k) & 1u) ? -1.f : 1.f;
+        const P sgn = pk(s, s);
+        (void)THREAD_BITS;
+#pragma unroll
+        for (int i = 0; i < S::E / 2; ++i) {
+            float a, b;
+            up(v[i], a, b);
+            const float pa = __shfl_xor_sync(0xffffffffu, a, 1 << k);
+            const float pb = __shfl_xor_sync(0xffffffffu, b, 1 << k);
+            v[i] = fma2(v[i], sgn, pk(pa, pb));
+        }
+    }
+}
 
 // Stages STAGE of a group with register bits REG on pair registers.
 template <int LOGE, uint32_t REG, uint32_t STAGE>
@@ -176,17 +211,21 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB,
         }
     }
     pair_stages<S::LOGE, G.reg[0], G.stage[0]>(v);
-    pair_exchanges<S, 1>(v, tbuf, t);
+    constexpr bool kShuffle = ShuffleFinish<S>::value;
+    if constexpr (kShuffle)
+        shuffle_stages<S>(v, t);
+    else
+        pair_exchanges<S, 1>(v, tbuf, t);
 
     if (scale != 1.0f) {
         const P s2 = pk(scale, scale);
 #pragma unroll
         for (int i = 0; i < NP; ++i) v[i] = mul2(v[i], s2);
     }
-    constexpr uint32_t RF = G.reg[G.count - 1];
+    constexpr uint32_t RF = kShuffle ? G.reg[0] : G.reg[G.count - 1];
     constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
     const uint32_t tf = deposit_rt<lowmask(LT) & ~RF, LT>(t);
-    if constexpr (S::VEC_STORE) {
+    if constexpr (kShuffle || S::VEC_STORE) {
         if (!active) return;
 #pragma unroll
         for (int q = 0; q < S::E / S::V; ++q) {

@@ -28,6 +28,20 @@ LaunchShape fft_local_shape(int log_n);
 cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
                              bool inverse, float scale, cudaStream_t stream, unsigned* err);
 
+// Multi-pass global Stockham for N > 2^13: radix 2^4..2^10 per pass.
+constexpr int kFftPassMinLog = 4;
+constexpr int kFftPassMaxLog = 10;
+struct FftOuterTables {
+    const void* lo;  // double2 W_N^k, k < 2^split
+    const void* hi;  // double2 W_N^(k << split)
+    int split;
+};
+LaunchShape fft_global_pass_shape(int log_r);
+// tw1024: float2 W_1024^k, k < 1024 (the in-CTA twiddles of every radix)
+cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
+                                   std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
+                                   bool conj_out, float scale, cudaStream_t stream);
+
 // ---- FWHT / zeta tile passes --------------------------------------------------
 enum class BwOp { Fwht = 0, ZetaSubset = 1, ZetaSuperset = 2 };
 enum class BwType { F32 = 0, BF16 = 1, F16 = 2, U32 = 3, U64 = 4 };

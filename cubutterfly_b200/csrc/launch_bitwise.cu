@@ -51,20 +51,21 @@ constexpr int kMaxStrided = sizeof(TC) == 8 ? 9 : 10;
 #if CUBF_BW_OP == 0
 // FWHT tiles: one thread per row up to 128 values (no exchange), then 64
 // values per thread; rows narrower than one 16-byte vector use the generic kernel.
-constexpr int fwht_log_e(int logh) { return logh <= 7 ? logh : 6; }
+constexpr int fwht_log_e(int logh) { return logh <= 6 ? logh : 6; }
 constexpr bool fwht_pair_kernel(int logh) { return (1 << logh) * static_cast<int>(sizeof(TS)) >= 16; }
 
 template <int LOGH>
 struct FwhtEntry {
     static constexpr int LOGE = fwht_log_e(LOGH);
     using S = fwht::FwhtShape<TS, LOGH, LOGE>;
+    static constexpr int SMEM = fwht::ShuffleFinish<S>::value ? 0 : S::SMEM_BYTES;
     static LaunchShape shape() {
         LaunchShape s;
         s.threads = S::TPB;
-        s.smem_bytes = S::SMEM_BYTES;
+        s.smem_bytes = SMEM;
         s.units_per_cta = S::TILES;
         s.elems_per_thread = S::E;
-        s.exchanges = S::G.count - 1 + (S::STAGE_OUT ? 1 : 0);
+        s.exchanges = fwht::ShuffleFinish<S>::value ? 0 : S::G.count - 1 + (S::STAGE_OUT ? 1 : 0);
         return s;
     }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
@@ -73,8 +74,8 @@ struct FwhtEntry {
         (void)cache_mode;
         auto kernel = fwht::fwht_tile_kernel<TS, LOGH, LOGE>;
         static bool configured = false;
-        if (!configured && S::SMEM_BYTES > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+        if (!configured && SMEM > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
             if (e != cudaSuccess) return e;
         }
         configured = true;
@@ -82,8 +83,8 @@ struct FwhtEntry {
         const std::size_t blocks = (outer + S::TILES - 1) / S::TILES;
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
-        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-            static_cast<const TS*>(in), static_cast<TS*>(out), outer, scale);
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, SMEM, stream>>>(static_cast<const TS*>(in),
+                                                                          static_cast<TS*>(out), outer, scale);
         return cudaGetLastError();
     }
 };

@@ -82,7 +82,64 @@ struct Table {
 };
 using Local = Table<1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13>;
 
+template <int LOGR>
+struct GlobalEntry {
+    using G = fft::GlobalPassShape<LOGR>;
+    static LaunchShape shape() {
+        LaunchShape s;
+        s.threads = G::TPB;
+        s.smem_bytes = G::SMEM_BYTES;
+        s.units_per_cta = G::C;
+        s.elems_per_thread = G::S::E;
+        s.exchanges = G::S::NPASS + 1;
+        return s;
+    }
+    static cudaError_t launch(const void* src, void* dst, int log_n, int ns_bits, std::size_t batch,
+                              const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out,
+                              float scale, cudaStream_t stream) {
+        auto kernel = fft::fft_global_pass_kernel<LOGR>;
+        static bool configured = false;
+        if (!configured) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+            configured = true;
+        }
+        if (log_n < LOGR || ((std::size_t{1} << (log_n - LOGR)) % G::C) != 0) return cudaErrorInvalidValue;
+        const std::size_t blocks = batch * ((std::size_t{1} << (log_n - LOGR)) / G::C);
+        if (blocks == 0) return cudaSuccess;
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        fft::OuterTwiddles ot{static_cast<const double2*>(outer.lo), static_cast<const double2*>(outer.hi),
+                              outer.split};
+        kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
+            static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits, batch,
+            static_cast<const float2*>(tw1024), 10 - LOGR, ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale);
+        return cudaGetLastError();
+    }
+};
+using GlobalLaunch = cudaError_t (*)(const void*, void*, int, int, std::size_t, const void*, const FftOuterTables&,
+                                     bool, bool, float, cudaStream_t);
+using GlobalShape = LaunchShape (*)();
+template <int... L>
+struct GlobalTable {
+    static constexpr GlobalLaunch launch_fns[] = {GlobalEntry<L>::launch...};
+    static constexpr GlobalShape shape_fns[] = {GlobalEntry<L>::shape...};
+};
+using Global = GlobalTable<4, 5, 6, 7, 8, 9, 10>;
+
 }  // namespace
+
+LaunchShape fft_global_pass_shape(int log_r) {
+    if (log_r < kFftPassMinLog || log_r > kFftPassMaxLog) return {};
+    return Global::shape_fns[log_r - kFftPassMinLog]();
+}
+
+cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
+                                   std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
+                                   bool conj_out, float scale, cudaStream_t stream) {
+    if (log_r < kFftPassMinLog || log_r > kFftPassMaxLog) return cudaErrorInvalidValue;
+    return Global::launch_fns[log_r - kFftPassMinLog](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in,
+                                                      conj_out, scale, stream);
+}
 
 LaunchShape fft_local_shape(int log_n) {
     if (log_n < 1 || log_n > kFftLocalMaxLog) return {};

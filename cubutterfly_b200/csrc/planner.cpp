@@ -194,7 +194,9 @@ std::string Mapping::name() const {
 Json Mapping::to_json() const {
     Json ps = Json::array();
     for (const auto& p : passes) {
-        ps.push_back({{"kernel", p.kind == PassKind::FftLocal ? "fft_local" : "bitwise_tile"},
+        ps.push_back({{"kernel", p.kind == PassKind::FftLocal    ? "fft_local"
+                                 : p.kind == PassKind::FftGlobal ? "fft_global_pass"
+                                                                 : "bitwise_tile"},
                       {"log_h", p.log_h},
                       {"log_w", p.log_w},
                       {"log_inner", p.log_inner},
@@ -215,10 +217,31 @@ Json Mapping::to_json() const {
 std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw) {
     std::vector<Mapping> out;
     const Descriptor& d = r.d;
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT && r.log_n > kFftLocalMaxLog) {
+        // Multi-pass global Stockham: ceil(L/10) passes, radix bits balanced.
+        Mapping m;
+        m.family = "fft-stockham-global";
+        const int np = (r.log_n + kFftPassMaxLog - 1) / kFftPassMaxLog;
+        const double elems = static_cast<double>(d.batch) * std::ldexp(1.0, r.log_n);
+        int ns = 0;
+        for (int i = 0; i < np; ++i) {
+            Pass p;
+            p.kind = PassKind::FftGlobal;
+            p.log_h = r.log_n / np + (i < r.log_n % np ? 1 : 0);
+            p.log_inner = ns;
+            p.shape = fft_global_pass_shape(p.log_h);
+            require(fits(p.shape, hw), "FFT pass tile does not fit the device");
+            m.passes.push_back(p);
+            m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, p.log_h, p.shape.exchanges, 2.5 / 2.0, 0.85);
+            ns += p.log_h;
+        }
+        const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
+        const std::size_t bytes = d.batch * (std::size_t{1} << r.log_n) * 8;
+        m.workspace_bytes = (np > 1 ? bytes : 0) * ((in_place && np % 2 == 1) ? 2 : 1);
+        out.push_back(m);
+        return out;
+    }
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
-        if (r.log_n > kFftLocalMaxLog)
-            throw Unsupported("FFT lengths above 2^" + std::to_string(kFftLocalMaxLog) +
-                              " need the multi-pass FFT, which this build does not include yet");
         Mapping m;
         m.family = "fft-stockham-local";
         Pass p;
@@ -273,8 +296,11 @@ Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, 
     }
     require(!parts.empty(), "explicit mapping has no passes");
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
-        require(parts.size() == 1 && parts[0] == r.log_n, "FFT mapping must be one local pass of log N bits");
-        return enumerate_mappings(r, hw).front();
+        const Mapping planned = enumerate_mappings(r, hw).front();
+        require(parts.size() == planned.passes.size(), "FFT mapping pass count does not match this build's plan");
+        for (std::size_t i = 0; i < parts.size(); ++i)
+            require(parts[i] == planned.passes[i].log_h, "FFT mapping radices do not match this build's plan");
+        return planned;
     }
     if (r.bw_op == BwOp::Fwht) require(parts.size() == 1, "FWHT executes as a single tile pass");
     return bitwise_mapping(r, hw, parts);

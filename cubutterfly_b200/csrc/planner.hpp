@@ -43,13 +43,13 @@ struct HardwareProfile {
 HardwareProfile resolve_profile();
 HardwareProfile profile_from_json(const Json& j);
 
-enum class PassKind { FftLocal, BitwiseTile };
+enum class PassKind { FftLocal, FftGlobal, BitwiseTile };
 
 struct Pass {
     PassKind kind = PassKind::BitwiseTile;
     int log_h = 0;      // transformed index bits
     int log_w = 0;      // adjacent untouched columns per tile (bitwise)
-    int log_inner = 0;  // log2 of the row stride of this pass (bitwise)
+    int log_inner = 0;  // log2 of the row stride of this pass (bitwise); Ns bits (global FFT)
     LaunchShape shape;
 };
 

@@ -71,3 +71,40 @@ def test_fft_round_trip(lib, cuda):
     f, _ = run(lib, fft_transform(2048, 8), x, cuda)
     back, _ = run(lib, fft_transform(2048, 8, inverse=True, normalize=True), f, cuda)
     assert rel_l2(back, x) <= TOL
+
+
+# ---- multi-pass global FFT (N > 2^13) ----------------------------------------------
+@pytest.mark.parametrize("log_n", [14, 15, 16, 18, 20])
+def test_fft_multipass_sizes(lib, oracle, cuda, log_n):
+    from gpu_util import run
+
+    batch = 3 if log_n <= 16 else 1
+    x = w.fft_input(1 << log_n, batch, seed=log_n)
+    got, name = run(lib, fft_transform(1 << log_n, batch), x, cuda)
+    assert name.startswith("fft-stockham-global"), name
+    assert rel_l2(got, oracle.fft_c32(x)) <= TOL, name
+
+
+@pytest.mark.parametrize("in_place", [False, True])
+@pytest.mark.parametrize("log_n", [17, 21])
+def test_fft_multipass_inverse_in_place(lib, oracle, cuda, log_n, in_place):
+    """Odd and even pass counts (2 and 3 passes), with the in-place workspace."""
+    from gpu_util import run
+
+    x = w.fft_input(1 << log_n, 2, seed=2)
+    got, _ = run(lib, fft_transform(1 << log_n, 2, inverse=True, normalize=True, in_place=in_place), x, cuda)
+    assert rel_l2(got, oracle.fft_c32(x, inverse=True, normalize=True)) <= TOL
+
+
+def test_fft_2_24_spot_bins_and_round_trip(lib, oracle, cuda):
+    """Large single transform: direct long-double DFT at 8 bins, plus inverse(forward(x)) == x."""
+    from gpu_util import run
+
+    n = 1 << 24
+    x = w.fft_input(n, 1, seed=24)
+    f, name = run(lib, fft_transform(n, 1), x, cuda)
+    bins = w.rng(77).integers(0, n, size=8)
+    ref = oracle.dft_bins(x[0], bins)
+    assert rel_l2(f[0][bins], ref) <= TOL, name
+    back, _ = run(lib, fft_transform(n, 1, inverse=True, normalize=True), f, cuda)
+    assert rel_l2(back, x) <= TOL

@@ -405,6 +405,10 @@ void select_mapping(cubutterflyHandle* h, cubutterflyPlan& p) {
 
 }  // namespace
 
+namespace cubf {
+void set_last_error(const std::string& message) { last_error = message; }
+}  // namespace cubf
+
 extern "C" {
 
 const char* cubutterflyGetStatusString(cubutterflyStatus_t status) {

@@ -32,6 +32,24 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterfl
                                                                      cubutterflyPlan_t plan, unsigned* status,
                                                                      int reset);
 
+/* Allocation-free complex fp32 FFT (no counterpart in the reference ABI).
+ * For callers that cannot allocate device memory -- fixed memory budgets or
+ * pools that own every byte, hosts that forbid cudaMalloc/cudaFree on their
+ * threads, latency-critical paths -- and so cannot provide the workspace a
+ * planned multi-pass FFT needs.  Runs the same multi-pass kernels as a
+ * cubutterflyCreatePlan/Execute FFT (forward or inverse, optional 1/N,
+ * natural order, in place when input == output) with scratch in a 16 MiB
+ * device array inside the library: n a power of two in [2^14, 2^21],
+ * n * batch <= 2^21 complex values (2^20 for in-place 2^21-point transforms);
+ * larger sizes return CUBUTTERFLY_STATUS_INVALID_VALUE.  Pointers 16-byte
+ * aligned.  Allocates nothing.  The first call on a device sets up that
+ * device (symbol addresses, twiddle upload) and should precede any stream
+ * capture.  Every call shares the scratch: calls that overlap on the GPU
+ * race, so serialise them on one stream. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FftC2CNoAlloc(const void* input, void* output, size_t n,
+                                                               size_t batch, int inverse, int normalize,
+                                                               cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

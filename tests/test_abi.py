@@ -1,0 +1,210 @@
+"""C ABI contract tests that need no GPU: exports, errors, descriptor JSON,
+capabilities, planner preview and RNS request validation (mirroring the
+reference's CPU-only contract tests, tests/test_semantic_contract.cpp and
+tests/test_c_api.c)."""
+import ctypes as ct
+import json
+import re
+from pathlib import Path
+
+import pytest
+
+import cubutterfly_b200 as cb
+from cubutterfly_b200 import rns
+from cubutterfly_b200 import workloads as w
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").rglob("*.h"):
+        text = h.read_text()
+        names |= set(re.findall(r"\b(cubutterfly\w+)\s*\(", text))
+    return sorted(n for n in names if not n.endswith("_t"))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_symbols()
+    assert len(names) >= 59  # 50 main ABI + 6 RNS ABI + 3 B200 extensions
+    missing = [n for n in names if not hasattr(lib._dll, n)]
+    assert not missing, missing
+
+
+def test_reference_abi_surface_is_complete():
+    """Every entry point of the reference header (SURVEY 8b list) is declared here."""
+    reference = """GetStatusString GetLastErrorString GetVersion Create Destroy SetStream GetStream SetLogCallback
+    SetCachePath PackRealFp32 ExpandHermitianFp32 CreateDescriptor DestroyDescriptor SetOperator SetDataType SetShape
+    SetExecutionMode SetFftTransformType SetFftOutputScale SetOutputScale SetArithmeticPolicy SetOutputRounding
+    SetStrides SetLogicalOrders DescriptorValidate DescriptorGetJson DescriptorSetJson DescriptorGetCapabilities
+    SetDirection SetPlacement SetLengthMode SetAlgorithmPolicy SetModulus SetNttLayouts SetStageMatrices CreatePlan
+    DestroyPlan PlanGetDescriptorJson PlanGetWorkspaceSize PlanGetInputSize PlanGetOutputSize PlanGetPhysicalExtents
+    PlanGetSelectionSource PlanGetAlgorithmName PlanGetSelectionReason PlanGetMappingJson PlanGetNttLayoutInfo
+    PlanSetWorkspace Execute ExecuteSteady""".split()
+    rns_names = "LastError Create Prepare Execute InfoJson Destroy".split()
+    declared = set(declared_symbols())
+    assert not [n for n in reference if "cubutterfly" + n not in declared]
+    assert not [n for n in rns_names if "cubutterflyRns" + n not in declared]
+
+
+def test_version_and_status_strings(lib):
+    assert lib.version() == (0, 9, 3)
+    f = lib._dll.cubutterflyGetStatusString
+    f.restype = ct.c_char_p
+    f.argtypes = [ct.c_int]
+    assert f(0) == b"CUBUTTERFLY_STATUS_SUCCESS"
+    assert f(3) == b"CUBUTTERFLY_STATUS_NOT_SUPPORTED"
+
+
+def config1_transform():
+    return cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32, extents=[4096],
+                        batch=16384, output_scale=1 / 64, output_rounding=cb.OutputRounding.FINAL_STORAGE)
+
+
+def test_descriptor_json_round_trip(lib):
+    with cb.Descriptor(lib, config1_transform()) as d:
+        text = d.json()
+    j = json.loads(text)
+    assert j["schema"] == "cubutterfly-descriptor-v1"
+    s = j["semantics"]
+    assert s["schema"] == "cubutterfly-semantic-v1"
+    assert s["shape"] == [4096] and s["batch"] == 16384 and s["storage"] == cb.DataType.BF16
+    assert s["output_rounding"] == 1 and s["output_scale"] == pytest.approx(1 / 64)
+    assert s["input_strides"] == [1] and s["input_batch_stride"] == 4096 and s["modulus"] is None
+    with cb.Descriptor.from_json(lib, text) as d2:
+        assert d2.json() == text
+
+
+def test_descriptor_json_rejects_unknown_fields(lib):
+    with cb.Descriptor(lib, config1_transform()) as d:
+        j = json.loads(d.json())
+    j["semantics"]["bogus"] = 1
+    with pytest.raises(cb.Error) as e:
+        cb.Descriptor.from_json(lib, j)
+    assert e.value.status == cb.Status.INVALID_VALUE
+
+
+@pytest.mark.parametrize("transform, message", [
+    (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, extents=[6]), "power of two"),
+    (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[8]), "incompatible"),
+    (cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.FP32, extents=[8]), "integer storage"),
+    (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, extents=[8], batch=0), "batch"),
+])
+def test_invalid_descriptors(lib, transform, message):
+    with pytest.raises(cb.Error) as e:
+        with cb.Descriptor(lib, transform) as d:
+            d.validate()
+    assert e.value.status == cb.Status.INVALID_VALUE
+    assert message in str(e.value)
+
+
+def test_overlapping_layout_is_invalid(lib):
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, extents=[8], batch=4, input_batch_stride=4)
+    with pytest.raises(cb.Error) as e:
+        with cb.Descriptor(lib, t) as d:
+            d.validate()
+    assert "overlaps" in str(e.value)
+
+
+def capabilities(lib, t):
+    with cb.Descriptor(lib, t) as d:
+        return json.loads(d.capabilities_json())
+
+
+def test_benchmark_configs_are_eligible(lib):
+    fft = cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=1024)
+    big = cb.Transform(op=cb.Operator.FFT, extents=[1 << 30], batch=1)
+    zeta = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << 24], batch=16)
+    for t in (fft, big, zeta, config1_transform()):
+        c = capabilities(lib, t)
+        assert c["status"] == "eligible", c["gaps"]
+
+
+@pytest.mark.parametrize("transform, code", [
+    (cb.Transform(op=cb.Operator.FFT, extents=[8, 8]), "rank-lowering"),
+    (cb.Transform(op=cb.Operator.FFT, extents=[12]), "length-lowering"),
+    (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, extents=[64]), "storage-lowering"),
+    (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, extents=[64]), "storage-lowering"),
+    (cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.FP32, extents=[64]), "storage-lowering"),
+    (cb.Transform(op=cb.Operator.STRUCTURED_2X2, storage=cb.DataType.FP32, extents=[4],
+                  stage_matrices=[[(1.0, 1.0, 1.0, -1.0)]]), "operator-lowering"),
+    (cb.Transform(op=cb.Operator.FFT, extents=[64], input_strides=[2]), "layout-lowering"),
+])
+def test_unsupported_descriptors_report_gaps(lib, transform, code):
+    c = capabilities(lib, transform)
+    assert c["status"] == "missing-lowering"
+    assert code in [g["code"] for g in c["gaps"]]
+
+
+def rank(lib, t, hardware=None):
+    fn = lib._dll.cubutterflyB200RankMappings
+    fn.argtypes = [ct.c_void_p, ct.c_char_p, ct.c_void_p, ct.POINTER(ct.c_size_t)]
+    fn.restype = ct.c_int
+    with cb.Descriptor(lib, t) as d:
+        size = ct.c_size_t()
+        hw = json.dumps(hardware).encode() if hardware else None
+        assert fn(d.native_handle, hw, None, ct.byref(size)) == 0, lib._dll.cubutterflyGetLastErrorString()
+        buf = ct.create_string_buffer(size.value)
+        assert fn(d.native_handle, hw, buf, ct.byref(size)) == 0
+        return json.loads(buf.value)
+
+
+def test_planner_partitions_zeta_2_24(lib):
+    t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << 24], batch=16)
+    ms = rank(lib, t)
+    assert len(ms) > 10
+    best = ms[0]
+    assert sum(p["log_h"] for p in best["passes"]) == 24
+    assert len(best["passes"]) == 2 and best["passes"][0]["log_w"] == 0 and best["passes"][1]["log_w"] == 4
+    assert all(sum(p["log_h"] for p in m["passes"]) == 24 for m in ms)
+    assert [m["predicted_us"] for m in ms] == sorted(m["predicted_us"] for m in ms)
+
+
+def test_planner_single_pass_fwht_and_multipass_fft(lib):
+    ms = rank(lib, config1_transform())
+    assert ms[0]["name"] == "fwht-tile[12]" and ms[0]["passes"][0]["elems_per_thread"] == 64
+    ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[1 << 30], batch=1))
+    assert ms[0]["name"] == "fft-stockham-global[10+10+10]" and ms[0]["workspace_bytes"] == 8 << 30
+    ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[1 << 21], batch=1, in_place=True))
+    assert ms[0]["workspace_bytes"] == 2 * (8 << 21)  # odd pass count in place: two halves
+
+
+def test_planner_respects_hardware_profile(lib):
+    """A device with little shared memory cannot take the 14-bit contiguous zeta tile."""
+    t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << 24], batch=16)
+    small = {"name": "small", "sm_count": 80, "smem_per_block_optin": 48 * 1024, "hbm_gbs": 2000.0}
+    ms = rank(lib, t, small)
+    assert all(p["smem_bytes"] <= 48 * 1024 for m in ms for p in m["passes"])
+    assert ms[0]["passes"][0]["log_h"] < 14
+
+
+def rns_create(config):
+    lib = rns.Library()
+    with pytest.raises(rns.Error) as e:
+        rns.Plan(lib, config)
+    return e.value
+
+
+@pytest.mark.parametrize("mutate, status, message", [
+    (lambda c: c.update(schema_version=2), 1, "schema_version"),
+    (lambda c: c.update(extra=1), 1, "unknown RNS JSON config field"),
+    (lambda c: c["domains"][0].update(modulus=c["domains"][0]["modulus"] + 2), 1, "prime"),
+    (lambda c: c["domains"][0].update(root=1), 1, "primitive"),
+    (lambda c: c["polynomials"][1].update(output_offset=0), 1, "disjoint"),
+    (lambda c: c["polynomials"][0].update(domain=7), 1, "missing domain"),
+    (lambda c: c.update(ring="bogus"), 1, "enum"),
+])
+def test_rns_request_validation(mutate, status, message):
+    cfg = w.rns_config(count=2, log_n=12)
+    mutate(cfg)
+    err = rns_create(cfg)
+    assert err.status == status and message in str(err)
+
+
+def test_rns_bad_json_text():
+    """Malformed JSON reaches the C ABI (the Python frontend parses first, as the reference's does)."""
+    lib = rns.Library()
+    handle = ct.c_void_p()
+    assert lib._dll.cubutterflyRnsCreate(b"{not json", ct.byref(handle)) == 1
+    assert handle.value is None
+    assert lib._dll.cubutterflyRnsLastError()

@@ -42,8 +42,12 @@ def parse():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-ops", action="store_true", help="skip the per-op table (FFT, NTT, zeta)")
     p.add_argument("--cpu-baseline", choices=["auto", "skip"], default="auto")
-    p.add_argument("--only", choices=["fwht4096", "fwht128", "fft", "zeta", "ntt"],
+    p.add_argument("--only", choices=["fwht4096", "fwht128", "fft", "zeta", "ntt", "fft1g"],
                    help="run just this operator's launches (profiling driver; prints a short JSON line)")
+    p.add_argument("--workload", choices=["fwht", "fft4step"], default="fwht",
+                   help="fwht: configs[1] (default, weak scaling); fft4step: config 4, one 2^30-point FFT "
+                        "split over all ranks (strong scaling)")
+    p.add_argument("--log-n", type=int, default=30, help="fft4step transform length (log2)")
     return p.parse_args()
 
 
@@ -200,6 +204,14 @@ def only_op(args):
         y = torch.empty_like(x)
         p = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[w.FFT_N], batch=w.FFT_BATCH), stream=sp)
         fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), 2 * w.FFT_N * w.FFT_BATCH * 8
+    elif args.only == "fft1g":
+        n = 1 << 24
+        x = w.torch_fft_input(n, 1, dev)
+        y = torch.empty_like(x)
+        p = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1), stream=sp)
+        ws = torch.empty(p.workspace_size(), dtype=torch.uint8, device=dev)
+        p.set_workspace(ws.data_ptr(), ws.numel())
+        fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), 2 * n * 8
     elif args.only == "zeta":
         z = w.torch_zeta_input(w.ZETA_LOG_N, w.ZETA_BATCH, dev)
         t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << w.ZETA_LOG_N],
@@ -220,12 +232,83 @@ def only_op(args):
     return 0
 
 
+def fft4step(args):
+    """Config 4: one complex fp32 FFT of 2^log_n points; on one GPU the
+    multi-pass plan, on P GPUs the four-step decomposition with NCCL
+    all-to-alls.  Strong scaling; algorithmic bytes = input + output once."""
+    import torch
+    import torch.distributed as dist
+
+    import cubutterfly_b200 as cb
+    from cubutterfly_b200 import workloads as w
+    from cubutterfly_b200.distributed import FourStepFFT
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    n = 1 << args.log_n
+    shard = n // world
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.rand((shard, 2), generator=g, device=dev, dtype=torch.float32) * 2 - 1
+    if world == 1:
+        lib = cb.load()
+        plan = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1), stream=stream.cuda_stream)
+        ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=dev)
+        plan.set_workspace(ws.data_ptr(), ws.numel())
+        y = torch.empty_like(x)
+        step = lambda: plan.execute(x.data_ptr(), y.data_ptr())  # noqa: E731
+        algo = plan.algorithm_name()
+    else:
+        fs = FourStepFFT(n, device=dev)
+        step = lambda: fs(x)  # noqa: E731
+        algo = f"four-step {fs.shape.n1}x{fs.shape.n2} over {world} ranks (NCCL all-to-all x3)"
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        gbs = 2 * n * 8 / (ms * 1e-3) / 1e9
+        peak, kind = peaks()
+        print(json.dumps({
+            "metric": f"transform HBM GB/s (complex fp32 FFT, N=2^{args.log_n}, one transform)",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"fft_c64_2^{args.log_n}_four_step", "algorithm": algo,
+                       "bytes_per_step": 2 * n * 8},
+            "frac_of_single_gpu_hbm_peak": round(gbs / peak, 4), "peak_kind": kind}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
     if args.only:
         return only_op(args)
+    if args.workload == "fft4step":
+        return fft4step(args)
     import numpy as np
     import torch
     import torch.distributed as dist

@@ -1,0 +1,162 @@
+"""Multi-GPU execution: batch sharding and the four-step FFT.
+
+One process per GPU, `torch.distributed` for the plumbing (NCCL on GPUs, gloo
+in CPU tests).
+
+* Batch sharding: independent transforms (FFT batches, FWHT rows, zeta
+  batches, RNS limbs) split into contiguous per-rank ranges; each rank runs
+  its own plan and no collective touches the data path (`shard_range`).
+
+* Four-step FFT: one complex fp32 transform of length N = N1 * N2 held as a
+  contiguous 1/P shard per rank (rank r owns x[r N/P : (r+1) N/P]):
+    1. all-to-all so each rank holds N2/P whole columns (length N1);
+    2. column FFTs of length N1 (this library's plan) and the twiddle
+       W_N^(n2 k1) (cubutterflyB200FourStepTwiddle, fp64-accurate);
+    3. all-to-all so each rank holds N1/P whole rows (length N2);
+    4. row FFTs of length N2;
+    5. all-to-all back to natural order: rank r owns X[r N/P : (r+1) N/P].
+  The exchanges are NCCL all-to-alls over NVLink; packing and unpacking are
+  strided tensor copies.  Inverse transforms use inverse plans and conjugate
+  twiddles, normalised by 1/N1 * 1/N2 when requested.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+import cubutterfly_b200 as cb
+
+
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, start + count) share of `total` units for `rank`."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+def _log2(n: int) -> int:
+    if n <= 0 or n & (n - 1):
+        raise ValueError("length must be a power of two")
+    return n.bit_length() - 1
+
+
+@dataclass
+class FourStepShape:
+    n: int
+    world: int
+
+    def __post_init__(self):
+        self.log_n = _log2(self.n)
+        self.log_n1 = (self.log_n + 1) // 2
+        self.n1 = 1 << self.log_n1            # column FFT length (rows of the N1 x N2 matrix)
+        self.n2 = self.n >> self.log_n1       # row FFT length
+        if self.n1 % self.world or self.n2 % self.world:
+            raise ValueError("both four-step factors must be divisible by the number of ranks")
+        self.local = self.n // self.world
+
+
+class _LibraryFft:
+    """Batched contiguous FFTs through the C ABI (plan + caller workspace)."""
+
+    def __init__(self, lib, n, batch, inverse, normalize, device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        self.plan = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=batch, inverse=inverse,
+                                              normalize_inverse=normalize), stream=stream)
+        size = self.plan.workspace_size()
+        self.ws = torch.empty(max(size, 16), dtype=torch.uint8, device=device)
+        if size:
+            self.plan.set_workspace(self.ws.data_ptr(), self.ws.numel())
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor) -> None:
+        self.plan.execute(x.data_ptr(), out.data_ptr())
+
+    def close(self):
+        self.plan.close()
+
+
+class _LibraryTwiddle:
+    def __init__(self, lib):
+        fn = lib._dll.cubutterflyB200FourStepTwiddle
+        fn.argtypes = [ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_int, ct.c_void_p]
+        fn.restype = ct.c_int
+        self.fn, self.lib = fn, lib
+
+    def __call__(self, data: torch.Tensor, rows: int, cols: int, row_offset: int, n: int, inverse: bool) -> None:
+        stream = torch.cuda.current_stream(data.device).cuda_stream
+        status = self.fn(data.data_ptr(), rows, cols, row_offset, n, int(inverse), stream)
+        if status:
+            raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
+
+
+class FourStepFFT:
+    """Distributed single-transform complex fp32 FFT (natural order in and out).
+
+    `x` is this rank's contiguous shard as a float32 tensor of shape
+    (N / P, 2) (interleaved complex).  `local_fft(n, batch)` and `twiddle`
+    may be replaced (CPU tests inject reference implementations); by default
+    they are this library's GPU kernels.
+    """
+
+    def __init__(self, n: int, group=None, inverse: bool = False, normalize: bool = True, lib=None,
+                 device: Optional[torch.device] = None,
+                 local_fft: Optional[Callable[[int, int], Callable]] = None,
+                 twiddle: Optional[Callable] = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.shape = FourStepShape(n, self.world)
+        self.inverse, self.normalize = inverse, normalize
+        s = self.shape
+        if local_fft is None:
+            lib = lib or cb.load()
+            device = device or torch.device("cuda", torch.cuda.current_device())
+            self._cols = _LibraryFft(lib, s.n1, s.n2 // self.world, inverse, normalize, device)
+            self._rows = _LibraryFft(lib, s.n2, s.n1 // self.world, inverse, normalize, device)
+            self._twiddle = _LibraryTwiddle(lib)
+        else:
+            self._cols = local_fft(s.n1, s.n2 // self.world)
+            self._rows = local_fft(s.n2, s.n1 // self.world)
+            self._twiddle = twiddle
+
+    def _exchange(self, send: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return send
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        return recv
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        s, p, r = self.shape, self.world, self.rank
+        if x.shape != (s.local, 2) or x.dtype != torch.float32:
+            raise ValueError(f"expected a float32 shard of shape ({s.local}, 2)")
+        n1p, n2p = s.n1 // p, s.n2 // p
+        # 1. rows n1 in [r N1/P, ...) -> columns n2 in [r N2/P, ...)
+        send = x.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous()
+        recv = self._exchange(send)                                  # [p][i][j] = A[p N1/P + i][r N2/P + j]
+        cols = recv.permute(2, 0, 1, 3).reshape(n2p, s.n1, 2).contiguous()
+        # 2. column FFTs (length N1) and the twiddle W_N^(n2 k1)
+        spec = torch.empty_like(cols)
+        self._cols(cols, spec)
+        self._twiddle(spec, n2p, s.n1, r * n2p, s.n, self.inverse)
+        # 3. columns -> rows k1 in [r N1/P, ...)
+        send = spec.view(n2p, p, n1p, 2).permute(1, 0, 2, 3).contiguous()
+        recv = self._exchange(send)                                  # [p][j][i] = C[p N2/P + j][r N1/P + i]
+        rows = recv.permute(2, 0, 1, 3).reshape(n1p, s.n2, 2).contiguous()
+        # 4. row FFTs (length N2): E[i][k2] = X[(r N1/P + i) + N1 k2]
+        out = torch.empty_like(rows)
+        self._rows(rows, out)
+        # 5. back to natural order: rank r owns k2 in [r N2/P, ...), all k1
+        send = out.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous()
+        recv = self._exchange(send)                                  # [p][i][j] = X[(p N1/P + i) + N1 (r N2/P + j)]
+        return recv.permute(2, 0, 1, 3).reshape(s.local, 2).contiguous()
+
+    def close(self):
+        for part in (self._cols, self._rows):
+            if hasattr(part, "close"):
+                part.close()

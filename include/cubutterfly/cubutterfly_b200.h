@@ -32,6 +32,16 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterfl
                                                                      cubutterflyPlan_t plan, unsigned* status,
                                                                      int reset);
 
+/* Twiddle step of the four-step FFT (no counterpart in the reference ABI;
+ * used by cubutterfly_b200.distributed for one transform split across GPUs).
+ * data: `rows` x `cols` complex fp32, row-major, 16-byte aligned;
+ * multiplies element (j, k) by W_n^((row_offset + j) k), W_n = exp(-2 pi i/n)
+ * (conjugated when `inverse`), with the twiddle formed in fp64 and rounded
+ * once.  The first call per (device, n) uploads its tables. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepTwiddle(void* data, size_t rows, size_t cols,
+                                                                 size_t row_offset, size_t n, int inverse,
+                                                                 cudaStream_t stream);
+
 /* Allocation-free complex fp32 FFT (no counterpart in the reference ABI).
  * For callers that cannot allocate device memory -- fixed memory budgets or
  * pools that own every byte, hosts that forbid cudaMalloc/cudaFree on their

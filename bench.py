@@ -48,6 +48,7 @@ def parse():
                    help="fwht: configs[1] (default, weak scaling); fft4step: config 4, one 2^30-point FFT "
                         "split over all ranks (strong scaling)")
     p.add_argument("--log-n", type=int, default=30, help="fft4step transform length (log2)")
+    p.add_argument("--mapping", default="", help="explicit mapping for --only fft1g / --workload fft4step (1 GPU)")
     return p.parse_args()
 
 
@@ -205,10 +206,11 @@ def only_op(args):
         p = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[w.FFT_N], batch=w.FFT_BATCH), stream=sp)
         fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), 2 * w.FFT_N * w.FFT_BATCH * 8
     elif args.only == "fft1g":
-        n = 1 << 24
+        n = 1 << args.log_n
         x = w.torch_fft_input(n, 1, dev)
         y = torch.empty_like(x)
-        p = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1), stream=sp)
+        opts = cb.PlanOptions(mapping=args.mapping) if args.mapping else None
+        p = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1), options=opts, stream=sp)
         ws = torch.empty(p.workspace_size(), dtype=torch.uint8, device=dev)
         p.set_workspace(ws.data_ptr(), ws.numel())
         fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), 2 * n * 8
@@ -227,7 +229,9 @@ def only_op(args):
         p.prepare(stream=sp, repetitions=1)
         fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr(), stream=sp)), 2 * w.NTT_LIMBS * (1 << w.NTT_LOG_N) * 8
     ms = time_launches(fn, stream, args.steps, args.warmup)
-    print(json.dumps({"only": args.only, "ms_per_launch": round(ms, 5), "gbs": round(nbytes / ms / 1e6, 1)}))
+    name = p.algorithm_name() if hasattr(p, "algorithm_name") else args.only
+    print(json.dumps({"only": args.only, "algorithm": name, "ms_per_launch": round(ms, 5),
+                      "gbs": round(nbytes / ms / 1e6, 1)}))
     p.close()
     return 0
 

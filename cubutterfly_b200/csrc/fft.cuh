@@ -337,22 +337,24 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
 // Pass p of radix R = 2^LOGR over a length-N transform (Ns = 2^ns_bits is the
 // product of the earlier radices): for j < N/R, take x[j + n N/R] (n < R),
 // multiply by the outer twiddle W_{Ns R}^{(j mod Ns) n}, run the length-R DFT,
-// and write y[(j / Ns) Ns R + (j mod Ns) + k Ns].  A CTA takes C = 256/T
-// adjacent columns j (coalesced 8C-byte segments): it loads the C x R tile
-// into shared memory with the outer twiddle applied (fp64 two-level table,
-// rounded once), runs the in-CTA Stockham passes of LocalShape<LOGR> on each
-// column, and scatters the result with a mapping that keeps global stores
-// contiguous.
+// and write y[(j / Ns) Ns R + (j mod Ns) + k Ns].  A CTA takes C >= 16
+// adjacent columns j, so every global access is a run of at least 128 bytes:
+// it loads the C x R tile into shared memory with the outer twiddle applied,
+// runs the in-CTA Stockham passes of LocalShape<LOGR> on each column in the
+// same buffer, and scatters the result with a mapping that keeps global
+// stores contiguous.  Outer twiddles come from a fp64 recurrence per column
+// (one two-level table lookup for the start and one for the step, then fp64
+// products), rounded once to fp32.
 template <int LOGR>
 struct GlobalPassShape {
     using S = LocalShape<LOGR>;
     static constexpr int R = 1 << LOGR;
-    static constexpr int TPB = 256;
-    static constexpr int C = TPB / S::T;         // columns per CTA
-    static constexpr int RS = S::PADDED + 1;     // padded row stride (float2)
+    static constexpr int C = S::T >= 16 ? 16 : 256 / S::T;  // columns per CTA (>= 16)
+    static constexpr int TPB = C * S::T;
+    static constexpr int RS = S::PADDED + 1;                 // padded row stride (float2)
     static constexpr int TILE = C * R;
-    static constexpr int SMEM_BYTES = 2 * C * RS * 8 + TwiddleTable<LOGR>::BYTES;
-    static_assert(LOGR >= 4 && S::T * C == TPB, "global pass radix must be 16..4096 with whole columns");
+    static constexpr int SMEM_BYTES = C * RS * 8 + TwiddleTable<LOGR>::BYTES;
+    static_assert(LOGR >= 4 && TPB <= 1024, "global pass radix must be 16..1024");
 };
 
 struct OuterTwiddles {
@@ -361,14 +363,37 @@ struct OuterTwiddles {
     int split;
 };
 
-CUBF_DEV float2 outer_twiddle(const OuterTwiddles& t, size_t k) {
+CUBF_DEV double2 outer_twiddle_d(const OuterTwiddles& t, size_t k) {
     const double2 a = __ldg(t.lo + (k & ((size_t{1} << t.split) - 1)));
     const double2 b = __ldg(t.hi + (k >> t.split));
-    return make_float2(static_cast<float>(a.x * b.x - a.y * b.y), static_cast<float>(a.x * b.y + a.y * b.x));
+    return make_double2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+CUBF_DEV float2 outer_twiddle(const OuterTwiddles& t, size_t k) {
+    const double2 w = outer_twiddle_d(t, k);
+    return make_float2(static_cast<float>(w.x), static_cast<float>(w.y));
+}
+CUBF_DEV double2 cmul_d(double2 a, double2 b) {
+    return make_double2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
+// In-place in-CTA passes on one shared-memory buffer: load, barrier, store,
+// barrier, per pass.
+template <int LOGR, int P>
+struct GlobalColumnPasses {
+    static CUBF_DEV void run(float2 (&v)[LocalShape<LOGR>::E], int th, const TwiddleTable<LOGR>& tw, float2* row) {
+        using S = LocalShape<LOGR>;
+        if constexpr (P < S::NPASS) {
+            pass_load<LOGR, P>(v, th, tw, [&](int i) { return row[S::pad(i)]; });
+            __syncthreads();
+            pass_store<LOGR, P>(v, th, [&](int i, float2 x) { row[S::pad(i)] = x; });
+            __syncthreads();
+            GlobalColumnPasses<LOGR, P + 1>::run(v, th, tw, row);
+        }
+    }
+};
+
 template <int LOGR>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
     fft_global_pass_kernel(const float2* src, float2* dst, int log_n, int ns_bits, size_t batch,
                            const float2* __restrict__ tw_r, int tw_log_stride, OuterTwiddles outer, int conj_in,
                            int conj_out, float scale) {
@@ -376,10 +401,9 @@ __global__ void __launch_bounds__(256, 2)
     using S = typename G::S;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float2* a = reinterpret_cast<float2*>(smem_raw);
-    float2* b = a + G::C * G::RS;
-    const auto twt = TwiddleTable<LOGR>::load(b + G::C * G::RS, tw_r, tw_log_stride);
+    const auto twt = TwiddleTable<LOGR>::load(a + G::C * G::RS, tw_r, tw_log_stride);
     const size_t n = size_t{1} << log_n;
-    const size_t cols = n >> LOGR;                    // j range
+    const size_t cols = n >> LOGR;  // j range
     const size_t ctas_per_batch = cols / G::C;
     const size_t bidx = blockIdx.x / ctas_per_batch;
     const size_t j0 = (blockIdx.x % ctas_per_batch) * G::C;
@@ -387,41 +411,40 @@ __global__ void __launch_bounds__(256, 2)
     const float2* sb = src + bidx * n;
     float2* db = dst + bidx * n;
     const float in_sgn = conj_in ? -1.f : 1.f;
-    const int tshift = log_n - ns_bits - LOGR;       // W_{Ns R}^m = W_N^(m << tshift)
-    // 1. coalesced tile load, outer twiddle applied
-    for (int idx = threadIdx.x; idx < G::TILE; idx += G::TPB) {
-        const int c = idx % G::C;
-        const int r = idx / G::C;
+    const int tshift = log_n - ns_bits - LOGR;  // W_{Ns R}^m = W_N^(m << tshift)
+    // 1. coalesced tile load (runs of C elements), outer twiddle applied.
+    //    Thread t handles column c = t % C and rows r = t / C + k (TPB / C).
+    {
+        constexpr int RSTEP = G::TPB / G::C;
+        const int c = threadIdx.x % G::C;
         const size_t j = j0 + c;
-        float2 x = __ldcs(sb + j + static_cast<size_t>(r) * cols);
-        x.y *= in_sgn;
-        if (ns_bits > 0 && r > 0) {
-            const size_t m = (j & (ns - 1)) * static_cast<size_t>(r);
-            x = cmul(x, outer_twiddle(outer, m << tshift));
+        const size_t jm = j & (ns - 1);
+        const int r0 = threadIdx.x / G::C;
+        double2 w = make_double2(1.0, 0.0), step = make_double2(1.0, 0.0);
+        if (ns_bits > 0) {
+            w = outer_twiddle_d(outer, ((jm * static_cast<size_t>(r0)) << tshift) & (n - 1));
+            step = outer_twiddle_d(outer, ((jm * static_cast<size_t>(RSTEP)) << tshift) & (n - 1));
         }
-        a[c * G::RS + S::pad(r)] = x;
+#pragma unroll 4
+        for (int r = r0; r < G::R; r += RSTEP) {
+            float2 x = __ldcs(sb + j + static_cast<size_t>(r) * cols);
+            x.y *= in_sgn;
+            if (ns_bits > 0) {
+                x = cmul(x, make_float2(static_cast<float>(w.x), static_cast<float>(w.y)));
+                w = cmul_d(w, step);
+            }
+            a[c * G::RS + S::pad(r)] = x;
+        }
     }
     __syncthreads();
-    // 2. length-R DFT of each column (in-CTA Stockham, b as exchange buffer)
+    // 2. length-R DFT of each column, in place in shared memory
     {
         const int c = threadIdx.x / S::T;
         const int th = threadIdx.x % S::T;
-        float2* arow = a + c * G::RS;
-        float2* brow = b + c * G::RS;
         float2 v[S::E];
-        auto load = [&](int i) { return arow[S::pad(i)]; };
-        auto store = [&](int i, float2 x) { arow[S::pad(i)] = x; };
-        if constexpr (S::NPASS == 1) {
-            // single in-register pass: every thread reads its values before any writes
-            pass_load<LOGR, 0>(v, th, twt, load);
-            __syncthreads();
-            pass_store<LOGR, 0>(v, th, store);
-        } else {
-            Passes<LOGR, 0, false>::run(v, th, twt, brow, brow, load, store);
-        }
+        GlobalColumnPasses<LOGR, 0>::run(v, th, twt, a + c * G::RS);
     }
-    __syncthreads();
-    // 3. scatter: element (c, k) -> y[((j)/Ns) Ns R + (j mod Ns) + k Ns], with
+    // 3. scatter: element (c, k) -> y[(j / Ns) Ns R + (j mod Ns) + k Ns], with
     //    the fastest index chosen so consecutive threads write consecutive words
     const int ne = ns < static_cast<size_t>(G::C) ? static_cast<int>(ns) : G::C;
     const float out_sgn = conj_out ? -1.f : 1.f;

@@ -180,6 +180,33 @@ void compositions(int total, int first_max, int rest_max, int max_parts, std::ve
 
 }  // namespace
 
+Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts) {
+    Mapping m;
+    m.family = "fft-stockham-global";
+    const Descriptor& d = r.d;
+    const double elems = static_cast<double>(d.batch) * std::ldexp(1.0, r.log_n);
+    int ns = 0;
+    for (int bits : parts) {
+        require(bits >= kFftPassMinLog && bits <= kFftPassMaxLog, "FFT pass radix must be 2^4 .. 2^10");
+        Pass p;
+        p.kind = PassKind::FftGlobal;
+        p.log_h = bits;
+        p.log_inner = ns;
+        p.shape = fft_global_pass_shape(bits);
+        require(fits(p.shape, hw), "FFT pass tile does not fit the device");
+        // one CTA per SM at 1024 threads leaves the memory pipe less busy
+        const double eff = p.shape.threads >= 1024 ? 0.6 : 0.85;
+        m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, eff);
+        m.passes.push_back(p);
+        ns += bits;
+    }
+    require(ns == r.log_n, "FFT passes must cover every stage exactly once");
+    const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
+    const std::size_t bytes = d.batch * (std::size_t{1} << r.log_n) * 8;
+    m.workspace_bytes = bytes * ((in_place && parts.size() % 2 == 1) ? 2 : 1);
+    return m;
+}
+
 std::string Mapping::name() const {
     std::ostringstream o;
     o << family << "[";
@@ -218,27 +245,19 @@ std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProf
     std::vector<Mapping> out;
     const Descriptor& d = r.d;
     if (d.op == CUBUTTERFLY_OPERATOR_FFT && r.log_n > kFftLocalMaxLog) {
-        // Multi-pass global Stockham: ceil(L/10) passes, radix bits balanced.
-        Mapping m;
-        m.family = "fft-stockham-global";
-        const int np = (r.log_n + kFftPassMaxLog - 1) / kFftPassMaxLog;
-        const double elems = static_cast<double>(d.batch) * std::ldexp(1.0, r.log_n);
-        int ns = 0;
-        for (int i = 0; i < np; ++i) {
-            Pass p;
-            p.kind = PassKind::FftGlobal;
-            p.log_h = r.log_n / np + (i < r.log_n % np ? 1 : 0);
-            p.log_inner = ns;
-            p.shape = fft_global_pass_shape(p.log_h);
-            require(fits(p.shape, hw), "FFT pass tile does not fit the device");
-            m.passes.push_back(p);
-            m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, p.log_h, p.shape.exchanges, 2.5 / 2.0, 0.85);
-            ns += p.log_h;
+        // Multi-pass global Stockham: for each cap on the radix bits of a
+        // pass, ceil(L / cap) passes with balanced radices.
+        for (int cap = kFftPassMaxLog; cap >= 7; --cap) {
+            const int np = (r.log_n + cap - 1) / cap;
+            std::vector<int> parts;
+            for (int i = 0; i < np; ++i) parts.push_back(r.log_n / np + (i < r.log_n % np ? 1 : 0));
+            bool dup = false;
+            for (const auto& m : out)
+                if (m.passes.size() == parts.size()) dup = true;
+            if (!dup) out.push_back(fft_global_mapping(r, hw, parts));
         }
-        const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
-        const std::size_t bytes = d.batch * (std::size_t{1} << r.log_n) * 8;
-        m.workspace_bytes = (np > 1 ? bytes : 0) * ((in_place && np % 2 == 1) ? 2 : 1);
-        out.push_back(m);
+        std::stable_sort(out.begin(), out.end(),
+                         [](const Mapping& a, const Mapping& b) { return a.predicted_us < b.predicted_us; });
         return out;
     }
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
@@ -296,11 +315,9 @@ Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, 
     }
     require(!parts.empty(), "explicit mapping has no passes");
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
-        const Mapping planned = enumerate_mappings(r, hw).front();
-        require(parts.size() == planned.passes.size(), "FFT mapping pass count does not match this build's plan");
-        for (std::size_t i = 0; i < parts.size(); ++i)
-            require(parts[i] == planned.passes[i].log_h, "FFT mapping radices do not match this build's plan");
-        return planned;
+        if (r.log_n > kFftLocalMaxLog) return fft_global_mapping(r, hw, parts);
+        require(parts.size() == 1 && parts[0] == r.log_n, "FFT up to 2^13 is one local pass of log N bits");
+        return enumerate_mappings(r, hw).front();
     }
     if (r.bw_op == BwOp::Fwht) require(parts.size() == 1, "FWHT executes as a single tile pass");
     return bitwise_mapping(r, hw, parts);

@@ -69,6 +69,8 @@ struct PlanRequest {
     BwOp bw_op = BwOp::Fwht;
 };
 
+// Multi-pass global FFT with the given radix bits per pass.
+Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts);
 // Every legal mapping of the request, ranked best first by the static model.
 std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw);
 // Parse an EXPLICIT mapping: the JSON of Mapping::to_json, or a pass list

@@ -164,7 +164,10 @@ def test_planner_single_pass_fwht_and_multipass_fft(lib):
     ms = rank(lib, config1_transform())
     assert ms[0]["name"] == "fwht-tile[12]" and ms[0]["passes"][0]["elems_per_thread"] == 64
     ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[1 << 30], batch=1))
-    assert ms[0]["name"] == "fft-stockham-global[10+10+10]" and ms[0]["workspace_bytes"] == 8 << 30
+    names = [m["name"] for m in ms]
+    assert "fft-stockham-global[10+10+10]" in names and "fft-stockham-global[8+8+7+7]" in names
+    assert all(m["workspace_bytes"] == 8 << 30 for m in ms)
+    assert all(p["units_per_cta"] >= 16 for m in ms for p in m["passes"])  # >= 128-byte global runs
     ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[1 << 21], batch=1, in_place=True))
     assert ms[0]["workspace_bytes"] == 2 * (8 << 21)  # odd pass count in place: two halves
 

@@ -17,6 +17,12 @@
 
 namespace cubf::fft {
 
+constexpr int log2_const(int x) {
+    int l = 0;
+    while ((1 << l) < x) ++l;
+    return l;
+}
+
 CUBF_DEV float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
 CUBF_DEV float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
 CUBF_DEV float2 cmul(float2 a, float2 b) {
@@ -446,16 +452,21 @@ __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
     }
     // 3. scatter: element (c, k) -> y[(j / Ns) Ns R + (j mod Ns) + k Ns], with
     //    the fastest index chosen so consecutive threads write consecutive words
-    const int ne = ns < static_cast<size_t>(G::C) ? static_cast<int>(ns) : G::C;
+    constexpr int LOG_C = log2_const(G::C);
+    const int log_ne = ns_bits < LOG_C ? ns_bits : LOG_C;  // runs of min(Ns, C) columns are contiguous
+    const int ne_mask = (1 << log_ne) - 1;
     const float out_sgn = conj_out ? -1.f : 1.f;
+    float2* dcol = db + ((j0 >> ns_bits) << (ns_bits + LOGR)) + (j0 & (ns - 1));
+#pragma unroll 4
     for (int idx = threadIdx.x; idx < G::TILE; idx += G::TPB) {
-        const int c_lo = idx % ne;
-        const int k = (idx / ne) % G::R;
-        const int c = (idx / (ne * G::R)) * ne + c_lo;
-        const size_t j = j0 + c;
-        const size_t o = ((j >> ns_bits) << (ns_bits + LOGR)) + (j & (ns - 1)) + static_cast<size_t>(k) * ns;
+        const int c_lo = idx & ne_mask;
+        const int k = (idx >> log_ne) & (G::R - 1);
+        const int c = ((idx >> (log_ne + LOGR)) << log_ne) | c_lo;
+        // j = j0 + c; j0 is a multiple of C, so (j mod Ns) and (j / Ns) split as below
+        const size_t o = (static_cast<size_t>(c >> ns_bits) << (ns_bits + LOGR)) + (c & (ns - 1)) +
+                         static_cast<size_t>(k) * ns;
         const float2 x = a[c * G::RS + S::pad(k)];
-        __stcs(db + o, make_float2(x.x * scale, x.y * out_sgn * scale));
+        __stcs(dcol + o, make_float2(x.x * scale, x.y * out_sgn * scale));
     }
 }
 

@@ -428,7 +428,7 @@ def main():
             "config": {"workload": "fwht_bf16_16384x4096_h4096_h128", "rows": ROWS, "cols": COLS, "head": HEAD,
                        "bytes_per_step": STEP_BYTES, "parallelism": f"batch-sharded x{world} (every rank its own batch)",
                        "l2": "inputs larger than L2 (2 rotating 128 MiB input buffers)"},
-            "roofline": {"bound": "hbm", "kernel": "bitwise_tile_kernel<FWHT,bf16,LOGH=12>",
+            "roofline": {"bound": "hbm", "kernel": "fwht_tile_kernel<bf16,LOGH=12,LOGE=6>",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": PASS_BYTES,

@@ -262,7 +262,8 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
             const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
             const int mode = !chained ? 0 : (i == 0 ? 1 : (last ? 2 : 3));
             check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, dst, outer_arg,
-                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream),
+                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream,
+                                       p.device_status),
                        "tile pass launch");
             src = dst;
         }

@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
         const int st = k % STAGES;
         const bool ok = tma::mbar_wait(&bar[st], static_cast<uint32_t>((k / STAGES) & 1));
         if (__syncthreads_or(!ok)) {
-            if (threadIdx.x == 0) tma::record_error(err, tma::kErrTimeout);
+            if (threadIdx.x == 0) tma::abort_ring<STAGES>(bar, k, blockIdx.x, gridDim.x, tiles, err);
             break;
         }
         const size_t row = tile * S::TPC + c;

@@ -12,6 +12,7 @@
 #pragma once
 
 #include "bitwise.cuh"
+#include "tma.cuh"
 
 namespace cubf::fwht {
 
@@ -169,27 +170,30 @@ CUBF_DEV void pair_exchanges(P (&v)[S::E / 2], float* tbuf, uint32_t t) {
     }
 }
 
-// Contiguous rows of 2^LOGH elements, `rows` of them; in may equal out.
+// Resident CTAs per SM the register allocation must allow: as many as the
+// exchange buffers fit in shared memory (1 KB per CTA is reserved by the
+// runtime), at most 8, and no fewer registers than 88 per thread (64 values
+// in 32 register pairs plus addressing; tighter bounds spill).
 template <typename TS, int LOGH, int LOGE>
-__global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB,
-                                  ((LOGE >= 7 ? 256 : 512) / FwhtShape<TS, LOGH, LOGE>::TPB > 0
-                                       ? (LOGE >= 7 ? 256 : 512) / FwhtShape<TS, LOGH, LOGE>::TPB
-                                       : 1))
-    fwht_tile_kernel(const TS* in, TS* out, size_t rows, float scale) {
+constexpr int fwht_min_blocks() {
+    using S = FwhtShape<TS, LOGH, LOGE>;
+    constexpr int smem = ShuffleFinish<S>::value ? 0 : S::SMEM_BYTES;
+    constexpr int by_smem = (228 * 1024) / (smem + 1024);
+    constexpr int by_regs = 65536 / (S::TPB * 88);
+    constexpr int b = by_smem < by_regs ? by_smem : by_regs;
+    return b > 8 ? 8 : (b < 1 ? 1 : b);
+}
+
+// One row of 2^LOGH elements (per thread-group of the CTA): `load16(e)`
+// returns the 16 bytes starting at row element e (a group-1 vector), results
+// go to `tout` (the row in HBM).  Every thread of the CTA must call it (it
+// contains barriers when the row spans several threads' exchanges).
+template <typename TS, int LOGH, int LOGE, typename Load16>
+CUBF_DEV void fwht_row(Load16 load16, TS* tout, bool active, uint32_t t, float* tbuf, float scale) {
     using S = FwhtShape<TS, LOGH, LOGE>;
     constexpr bw::Groups G = S::G;
     constexpr int LT = S::LT;
     constexpr int NP = S::E / 2;
-    static_assert(S::E >= 2 && S::V * sizeof(TS) == 16, "FWHT tiles move 16-byte vectors");
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int local = threadIdx.x / S::TPT;
-    const uint32_t t = threadIdx.x % S::TPT;
-    const size_t row = static_cast<size_t>(blockIdx.x) * S::TILES + local;
-    const bool active = row < rows;
-    const TS* tin = in + (active ? row : 0) * (size_t{1} << LOGH);
-    TS* tout = out + (active ? row : 0) * (size_t{1} << LOGH);
-    float* tbuf = reinterpret_cast<float*>(smem_raw + local * S::TILE_SMEM);
-
     P v[NP];
     {
         constexpr uint32_t R0 = G.reg[0];
@@ -197,8 +201,7 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB,
         const uint32_t te = deposit_rt<lowmask(LT) & ~R0, LT>(t);
 #pragma unroll
         for (int q = 0; q < S::E / S::V; ++q) {
-            uint4 w = make_uint4(0, 0, 0, 0);
-            if (active) w = __ldg(reinterpret_cast<const uint4*>(tin + (te | O0.v[q * S::V])));
+            const uint4 w = load16(te | O0.v[q * S::V]);
             if constexpr (sizeof(TS) == 4) {
                 v[q * 2] = (static_cast<P>(w.y) << 32) | w.x;
                 v[q * 2 + 1] = (static_cast<P>(w.w) << 32) | w.z;
@@ -271,6 +274,93 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB,
         for (int q = 0; q < S::E / S::V; ++q)
             __stcs(reinterpret_cast<uint4*>(tout + (te | O0.v[q * S::V])),
                    *reinterpret_cast<const uint4*>(orow + q * S::V));
+    }
+}
+
+// Contiguous rows of 2^LOGH elements, `rows` of them; in may equal out.
+template <typename TS, int LOGH, int LOGE>
+__global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_blocks<TS, LOGH, LOGE>())
+    fwht_tile_kernel(const TS* in, TS* out, size_t rows, float scale) {
+    using S = FwhtShape<TS, LOGH, LOGE>;
+    static_assert(S::E >= 2 && S::V * sizeof(TS) == 16, "FWHT tiles move 16-byte vectors");
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int local = threadIdx.x / S::TPT;
+    const uint32_t t = threadIdx.x % S::TPT;
+    const size_t row = static_cast<size_t>(blockIdx.x) * S::TILES + local;
+    const bool active = row < rows;
+    const TS* tin = in + (active ? row : 0) * (size_t{1} << LOGH);
+    TS* tout = out + (active ? row : 0) * (size_t{1} << LOGH);
+    float* tbuf = reinterpret_cast<float*>(smem_raw + local * S::TILE_SMEM);
+    auto load16 = [&](uint32_t e) -> uint4 {
+        return active ? __ldg(reinterpret_cast<const uint4*>(tin + e)) : make_uint4(0, 0, 0, 0);
+    };
+    fwht_row<TS, LOGH, LOGE>(load16, tout, active, t, tbuf, scale);
+}
+
+// Persistent variant: each CTA walks tiles of TILES contiguous rows and keeps
+// STAGES of them in flight with bulk (TMA) copies into a shared-memory ring
+// (mbarrier completion, bounded waits recorded in `err`); group-1 vectors
+// are read from the ring, the rest as above.
+template <typename TS, int LOGH, int LOGE, int STAGES, bool EXCHANGE>
+struct FwhtTmaShape {
+    using S = FwhtShape<TS, LOGH, LOGE>;
+    static constexpr int ROW_ELEMS = 1 << LOGH;
+    static constexpr int TILE_BYTES = S::TILES * ROW_ELEMS * static_cast<int>(sizeof(TS));
+    static constexpr int XCH_OFFSET = STAGES * TILE_BYTES;
+    static constexpr int BAR_OFFSET = XCH_OFFSET + (EXCHANGE ? S::SMEM_BYTES : 0);
+    static constexpr int SMEM_BYTES = BAR_OFFSET + STAGES * 8;
+};
+
+template <typename TS, int LOGH, int LOGE, int STAGES, bool EXCHANGE>
+__global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_blocks<TS, LOGH, LOGE>())
+    fwht_tma_kernel(const TS* in, TS* out, size_t rows, float scale, unsigned* err) {
+    using S = FwhtShape<TS, LOGH, LOGE>;
+    using T = FwhtTmaShape<TS, LOGH, LOGE, STAGES, EXCHANGE>;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    TS* ring = reinterpret_cast<TS*>(smem_raw);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + T::BAR_OFFSET);
+    const int local = threadIdx.x / S::TPT;
+    const uint32_t t = threadIdx.x % S::TPT;
+    float* tbuf = reinterpret_cast<float*>(smem_raw + T::XCH_OFFSET + local * S::TILE_SMEM);
+    const size_t tiles = (rows + S::TILES - 1) / S::TILES;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < STAGES; ++st) tma::mbar_init(&bar[st], 1);
+        tma::fence_barrier_init();
+    }
+    __syncthreads();
+    auto issue = [&](int st, size_t tile) {
+        const size_t first = tile * S::TILES;
+        const size_t cnt = rows - first < static_cast<size_t>(S::TILES) ? rows - first : S::TILES;
+        const uint32_t bytes = static_cast<uint32_t>(cnt * T::ROW_ELEMS * sizeof(TS));
+        tma::mbar_arrive_expect_tx(&bar[st], bytes);
+        tma::bulk_load(ring + static_cast<size_t>(st) * S::TILES * T::ROW_ELEMS, in + first * T::ROW_ELEMS, bytes,
+                       &bar[st]);
+    };
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < STAGES; ++st) {
+            const size_t tile = blockIdx.x + static_cast<size_t>(st) * gridDim.x;
+            if (tile < tiles) issue(st, tile);
+        }
+    }
+    for (int k = 0;; ++k) {
+        const size_t tile = blockIdx.x + static_cast<size_t>(k) * gridDim.x;
+        if (tile >= tiles) break;
+        const int st = k % STAGES;
+        const bool ok = tma::mbar_wait(&bar[st], static_cast<uint32_t>((k / STAGES) & 1));
+        if (__syncthreads_or(!ok)) {
+            if (threadIdx.x == 0) tma::abort_ring<STAGES>(bar, k, blockIdx.x, gridDim.x, tiles, err);
+            break;
+        }
+        const size_t row = tile * S::TILES + local;
+        const bool active = row < rows;
+        const TS* srow = ring + (static_cast<size_t>(st) * S::TILES + local) * T::ROW_ELEMS;
+        auto load16 = [&](uint32_t e) -> uint4 { return *reinterpret_cast<const uint4*>(srow + e); };
+        fwht_row<TS, LOGH, LOGE>(load16, out + (active ? row : 0) * T::ROW_ELEMS, active, t, tbuf, scale);
+        __syncthreads();  // ring slot and exchange buffer are free
+        if (threadIdx.x == 0) {
+            const size_t next = tile + static_cast<size_t>(STAGES) * gridDim.x;
+            if (next < tiles) issue(st, next);
+        }
     }
 }
 

@@ -62,8 +62,9 @@ LaunchShape bw_shape(const BwVariant& v);
 // outer arrays of (2^log_h x inner) elements; the pass transforms the 2^log_h
 // axis.  in may equal out.  cache_mode: 0 streaming single pass, 1 first pass
 // of a chain (output kept in L2), 2 last pass of a chain, 3 middle pass.
+// `err` is a device word that receives error codes from bounded waits (or null).
 cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
-                      bool inverse, float scale, int cache_mode, cudaStream_t stream);
+                      bool inverse, float scale, int cache_mode, cudaStream_t stream, unsigned* err = nullptr);
 
 // ---- RNS NTT tile passes --------------------------------------------------------
 struct NttPolyDesc {

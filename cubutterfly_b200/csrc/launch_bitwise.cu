@@ -6,6 +6,10 @@
 #include "bitwise.cuh"
 #include "fwht.cuh"
 #include "kernels.hpp"
+#include "launch_util.cuh"
+
+#include <cstdint>
+#include <cstdlib>
 
 #ifndef CUBF_BW_OP
 #error "CUBF_BW_OP must be defined (0 fwht, 1 subset zeta, 2 superset zeta)"
@@ -49,39 +53,114 @@ constexpr int kMaxContig = sizeof(TC) == 8 ? 13 : 14;
 constexpr int kMaxStrided = sizeof(TC) == 8 ? 9 : 10;
 
 #if CUBF_BW_OP == 0
-// FWHT tiles: one thread per row up to 128 values (no exchange), then 64
-// values per thread; rows narrower than one 16-byte vector use the generic kernel.
-constexpr int fwht_log_e(int logh) { return logh <= 6 ? logh : 6; }
+// FWHT tiles: one thread per row up to 64 values (no exchange), rows of 128
+// over 4 threads of 32 values (shuffle finish: fewer registers, more resident
+// warps), then 64 values per thread; rows narrower than one 16-byte vector
+// use the generic kernel.
+constexpr int fwht_log_e(int logh) { return logh <= 6 ? logh : (logh == 7 ? 5 : 6); }
 constexpr bool fwht_pair_kernel(int logh) { return (1 << logh) * static_cast<int>(sizeof(TS)) >= 16; }
+
+// Persistent TMA-ring variant for rows of at least 512 bytes, selected by
+// CUBUTTERFLY_FWHT_STAGES = ring depth (tiles in flight per CTA, clamped to
+// what fits in shared memory).  Off by default: on B200 the ring's shared
+// memory halves the resident warps and the non-persistent kernel, which keeps
+// 16-20 warps per SM issuing, is faster (5.16 vs 4.68 TB/s for bf16 rows of
+// 4096, 2 stages).
+constexpr int kFwhtTmaMinRowBytes = 512;
+constexpr int kFwhtDefaultStages = 0;
+constexpr int kFwhtMaxStages = 4;
+constexpr int kSmemLimit = 227 * 1024;
+
+int fwht_stages_setting() {
+    static const int stages = [] {
+        const char* e = std::getenv("CUBUTTERFLY_FWHT_STAGES");
+        if (!e || !*e) return kFwhtDefaultStages;
+        const int v = std::atoi(e);
+        return v < 0 ? 0 : (v > kFwhtMaxStages ? kFwhtMaxStages : v);
+    }();
+    return stages;
+}
 
 template <int LOGH>
 struct FwhtEntry {
     static constexpr int LOGE = fwht_log_e(LOGH);
     using S = fwht::FwhtShape<TS, LOGH, LOGE>;
-    static constexpr int SMEM = fwht::ShuffleFinish<S>::value ? 0 : S::SMEM_BYTES;
+    static constexpr bool kShuffle = fwht::ShuffleFinish<S>::value;
+    static constexpr int SMEM = kShuffle ? 0 : S::SMEM_BYTES;
+    static constexpr bool kTma = (1 << LOGH) * static_cast<int>(sizeof(TS)) >= kFwhtTmaMinRowBytes;
+    template <int ST>
+    using TmaShape = fwht::FwhtTmaShape<TS, LOGH, LOGE, ST, !kShuffle>;
+    template <int ST>
+    static constexpr bool fits() { return TmaShape<ST>::SMEM_BYTES <= kSmemLimit; }
+
     static LaunchShape shape() {
         LaunchShape s;
         s.threads = S::TPB;
         s.smem_bytes = SMEM;
+        if constexpr (kTma) {
+            const int st = clamp_stages(fwht_stages_setting());
+            if (st > 0) s.smem_bytes = tma_smem(st);
+        }
         s.units_per_cta = S::TILES;
         s.elems_per_thread = S::E;
-        s.exchanges = fwht::ShuffleFinish<S>::value ? 0 : S::G.count - 1 + (S::STAGE_OUT ? 1 : 0);
+        s.exchanges = kShuffle ? 0 : S::G.count - 1 + (S::STAGE_OUT ? 1 : 0);
         return s;
     }
+    static int clamp_stages(int want) {
+        if (want <= 0) return 0;
+        for (int st = want; st >= 2; --st) {
+            if (st == 4 && fits<4>()) return 4;
+            if (st == 3 && fits<3>()) return 3;
+            if (st == 2 && fits<2>()) return 2;
+        }
+        return 0;
+    }
+    static int tma_smem(int st) {
+        return st == 4 ? TmaShape<4>::SMEM_BYTES : (st == 3 ? TmaShape<3>::SMEM_BYTES : TmaShape<2>::SMEM_BYTES);
+    }
+    template <int ST>
+    static cudaError_t launch_tma(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream,
+                                  unsigned* err) {
+        if constexpr (!fits<ST>()) {
+            return cudaErrorInvalidConfiguration;
+        } else {
+            auto kernel = fwht::fwht_tma_kernel<TS, LOGH, LOGE, ST, !kShuffle>;
+            constexpr int smem = TmaShape<ST>::SMEM_BYTES;
+            static KernelSetup setup;
+            int grid_cap = 0;
+            cudaError_t e = setup_kernel(setup, kernel, S::TPB, smem, &grid_cap);
+            if (e != cudaSuccess) return e;
+            const std::size_t tiles = (rows + S::TILES - 1) / S::TILES;
+            const unsigned grid =
+                static_cast<unsigned>(tiles < static_cast<std::size_t>(grid_cap) ? tiles : grid_cap);
+            kernel<<<grid, S::TPB, smem, stream>>>(static_cast<const TS*>(in), static_cast<TS*>(out), rows, scale,
+                                                    err);
+            return cudaGetLastError();
+        }
+    }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
-                              float scale, int cache_mode, cudaStream_t stream) {
+                              float scale, int cache_mode, cudaStream_t stream, unsigned* err) {
         (void)inverse;  // FWHT is its own inverse up to the scale
         (void)cache_mode;
-        auto kernel = fwht::fwht_tile_kernel<TS, LOGH, LOGE>;
-        static bool configured = false;
-        if (!configured && SMEM > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-            if (e != cudaSuccess) return e;
-        }
-        configured = true;
         if (inner != 1) return cudaErrorInvalidValue;
+        if (outer == 0) return cudaSuccess;
+        if constexpr (kTma) {
+            // bulk copies need a 16-byte aligned source (rows are >= 512 bytes)
+            if ((reinterpret_cast<std::uintptr_t>(in) & 15) == 0) {
+                switch (clamp_stages(fwht_stages_setting())) {
+                    case 4: return launch_tma<4>(in, out, outer, scale, stream, err);
+                    case 3: return launch_tma<3>(in, out, outer, scale, stream, err);
+                    case 2: return launch_tma<2>(in, out, outer, scale, stream, err);
+                    default: break;
+                }
+            }
+        }
+        auto kernel = fwht::fwht_tile_kernel<TS, LOGH, LOGE>;
+        static KernelSetup setup;
+        int grid_cap = 0;
+        cudaError_t e = setup_kernel(setup, kernel, S::TPB, SMEM, &grid_cap);
+        if (e != cudaSuccess) return e;
         const std::size_t blocks = (outer + S::TILES - 1) / S::TILES;
-        if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
         kernel<<<static_cast<unsigned>(blocks), S::TPB, SMEM, stream>>>(static_cast<const TS*>(in),
                                                                           static_cast<TS*>(out), outer, scale);
@@ -103,14 +182,13 @@ struct Entry {
         return s;
     }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
-                              float scale, int cache_mode, cudaStream_t stream) {
+                              float scale, int cache_mode, cudaStream_t stream, unsigned* err) {
+        (void)err;
         auto kernel = bw::bitwise_tile_kernel<Op, TS, TC, LOGH, LOGW, kLogE>;
-        static bool configured = false;
-        if (!configured && S::SMEM_BYTES > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
-            if (e != cudaSuccess) return e;
-        }
-        configured = true;
+        static KernelSetup setup;
+        int grid_cap = 0;
+        cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
+        if (e != cudaSuccess) return e;
         if ((inner >> LOGW) == 0 || (inner & (inner - 1)) != 0) return cudaErrorInvalidValue;
         if (LOGW == 0 && inner != 1) return cudaErrorInvalidValue;
         int log_inner = 0;
@@ -125,7 +203,8 @@ struct Entry {
     }
 };
 
-using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, int, cudaStream_t);
+using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, int, cudaStream_t,
+                                 unsigned*);
 using ShapeFn = LaunchShape (*)();
 
 #if CUBF_BW_OP == 0
@@ -188,11 +267,11 @@ LaunchShape CUBF_CAT(CUBF_UNIT, _shape)(int log_h, int log_w) {
 
 cudaError_t CUBF_CAT(CUBF_UNIT, _launch)(int log_h, int log_w, const void* in, void* out, std::size_t outer,
                                          std::size_t inner, bool inverse, float scale, int cache_mode,
-                                         cudaStream_t stream) {
+                                         cudaStream_t stream, unsigned* err) {
     if (log_w == 0 && log_h >= 1 && log_h <= kMaxContig)
-        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream);
+        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream, err);
     if (kHasStrided && log_w == kLogW && log_h >= 1 && log_h <= kMaxStrided)
-        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream);
+        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream, err);
     return cudaErrorInvalidValue;
 }
 

@@ -1,6 +1,7 @@
 // launch_fft.cu -- instantiations and launchers of the FFT kernels.
 #include "fft.cuh"
 #include "kernels.hpp"
+#include "launch_util.cuh"
 
 #include <cstdint>
 
@@ -28,17 +29,10 @@ cudaError_t launch_tma(const void* in, void* out, std::size_t batch, const void*
     using S = fft::LocalShape<LOGN>;
     using T = fft::TmaShape<LOGN, kStages>;
     auto kernel = fft::fft_tma_kernel<LOGN, kStages>;
-    static int grid_cap = 0;
-    if (grid_cap == 0) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, T::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        int per_sm = 0, dev = 0, sms = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, S::TPB, T::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        grid_cap = (per_sm > 0 ? per_sm : 1) * sms;
-    }
+    static KernelSetup setup;
+    int grid_cap = 0;
+    cudaError_t e = setup_kernel(setup, kernel, S::TPB, T::SMEM_BYTES, &grid_cap);
+    if (e != cudaSuccess) return e;
     const std::size_t tiles = (batch + S::TPC - 1) / S::TPC;
     if (tiles == 0) return cudaSuccess;
     const unsigned grid = static_cast<unsigned>(tiles < static_cast<std::size_t>(grid_cap) ? tiles : grid_cap);
@@ -57,12 +51,10 @@ cudaError_t launch(const void* in, void* out, std::size_t batch, const void* tw,
             return launch_tma<LOGN>(in, out, batch, tw, inverse, scale, stream, err);
     }
     auto kernel = fft::fft_local_kernel<LOGN>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static KernelSetup setup;
+    int grid_cap = 0;
+    cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
+    if (e != cudaSuccess) return e;
     const std::size_t blocks = (batch + S::TPC - 1) / S::TPC;
     if (blocks == 0) return cudaSuccess;
     if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
@@ -98,12 +90,10 @@ struct GlobalEntry {
                               const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out,
                               float scale, cudaStream_t stream) {
         auto kernel = fft::fft_global_pass_kernel<LOGR>;
-        static bool configured = false;
-        if (!configured) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
-            if (e != cudaSuccess) return e;
-            configured = true;
-        }
+        static KernelSetup setup;
+        int grid_cap = 0;
+        cudaError_t e = setup_kernel(setup, kernel, G::TPB, G::SMEM_BYTES, &grid_cap);
+        if (e != cudaSuccess) return e;
         if (log_n < LOGR || ((std::size_t{1} << (log_n - LOGR)) % G::C) != 0) return cudaErrorInvalidValue;
         const std::size_t blocks = batch * ((std::size_t{1} << (log_n - LOGR)) / G::C);
         if (blocks == 0) return cudaSuccess;

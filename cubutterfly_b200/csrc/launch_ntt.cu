@@ -1,5 +1,6 @@
 // launch_ntt.cu -- instantiations and launchers of the RNS NTT tile passes.
 #include "kernels.hpp"
+#include "launch_util.cuh"
 #include "ntt.cuh"
 
 namespace cubf {
@@ -21,12 +22,10 @@ struct Entry {
                               std::size_t poly_count, const NttTables& t, bool in_is_out, bool final_scale,
                               cudaStream_t stream) {
         auto kernel = ntt::ntt_pass_kernel<L, STRIDED, INV>;
-        static bool configured = false;
-        if (!configured && S::SMEM_BYTES > 48 * 1024) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
-            if (e != cudaSuccess) return e;
-        }
-        configured = true;
+        static KernelSetup setup;
+        int grid_cap = 0;
+        cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
+        if (e != cudaSuccess) return e;
         constexpr std::size_t groups = (std::size_t{1} << (L - S::B)) / S::COLS;
         const std::size_t blocks = poly_count * groups;
         if (blocks == 0) return cudaSuccess;

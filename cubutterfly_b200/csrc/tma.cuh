@@ -76,4 +76,18 @@ CUBF_DEV void record_error(unsigned* err, unsigned code) {
     if (err) atomicOr(err, code);
 }
 
+// Abort path of a ring pipeline whose iteration k gave up waiting: records
+// the error and waits (bounded) for the copies still in flight -- iterations
+// k .. k+STAGES-1 that have a tile -- so that none lands after the CTA
+// leaves.  Called by the issuing thread only.
+template <int STAGES>
+CUBF_DEV void abort_ring(uint64_t* bar, int k, size_t first_tile, size_t tile_stride, size_t tiles,
+                         unsigned* err) {
+    record_error(err, kErrTimeout);
+    for (int j = k; j < k + STAGES; ++j) {
+        if (first_tile + static_cast<size_t>(j) * tile_stride >= tiles) break;
+        mbar_wait(&bar[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1));
+    }
+}
+
 }  // namespace cubf::tma

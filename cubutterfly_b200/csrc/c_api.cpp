@@ -316,14 +316,7 @@ void build_tables(cubutterflyPlan& p) {
         check_cuda(cudaMemcpy(p.outer_hi, hi.data(), hi.size() * 8, cudaMemcpyHostToDevice), "twiddle upload");
         p.outer_split = split;
     }
-    const std::size_t n = global ? 1024 : p.desc.extents[0];
-    std::vector<float> tw(2 * n);
-    for (std::size_t k = 0; k < n; ++k) {
-        // exp(-2 pi i k / N) in double, rounded once (reference butterfly.cu:1502-1514)
-        const double a = -2.0 * kPi * static_cast<double>(k) / static_cast<double>(n);
-        tw[2 * k] = static_cast<float>(std::cos(a));
-        tw[2 * k + 1] = static_cast<float>(std::sin(a));
-    }
+    const std::vector<float> tw = cubf::fft_local_twiddles(global ? 10 : p.req.log_n);
     check_cuda(cudaMalloc(&p.twiddles, tw.size() * sizeof(float)), "twiddle table allocation");
     check_cuda(cudaMemcpy(p.twiddles, tw.data(), tw.size() * sizeof(float), cudaMemcpyHostToDevice),
                "twiddle table upload");

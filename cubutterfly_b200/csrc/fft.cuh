@@ -13,7 +13,6 @@
 #pragma once
 
 #include "common.cuh"
-#include "tma.cuh"
 
 namespace cubf::fft {
 
@@ -256,86 +255,6 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
         if (active) __stcs(dst + i, make_float2(x.x * scale, x.y * sgn * scale));
     };
     Passes<LOGN, 0>::run(v, th, twt, buf0, buf1, gload, gstore);
-}
-
-// Persistent variant: each CTA walks tiles of TPC contiguous transforms,
-// keeping STAGES tiles in flight with bulk (TMA) copies into a shared-memory
-// ring; pass 0 reads the ring, the passes exchange through one padded
-// buffer, the last pass writes HBM directly (coalesced).
-template <int LOGN, int STAGES>
-struct TmaShape {
-    using S = LocalShape<LOGN>;
-    static constexpr int TILE_ELEMS = S::TPC * S::N;
-    static constexpr int TILE_BYTES = TILE_ELEMS * 8;
-    static constexpr int XCH_ELEMS = S::NPASS > 1 ? S::TPC * S::PADDED : 0;
-    static constexpr int TW_OFFSET = (STAGES * TILE_ELEMS + XCH_ELEMS) * 8;
-    static constexpr int BAR_OFFSET = TW_OFFSET + TwiddleTable<LOGN>::BYTES;
-    static constexpr int SMEM_BYTES = BAR_OFFSET + STAGES * 8;
-};
-
-template <int LOGN, int STAGES>
-__global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
-    fft_tma_kernel(const float2* in, float2* out, size_t batch, const float2* __restrict__ tw, int inverse,
-                   float scale, unsigned* err) {
-    using S = LocalShape<LOGN>;
-    using T = TmaShape<LOGN, STAGES>;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    float2* ring = reinterpret_cast<float2*>(smem_raw);
-    float2* xbuf = ring + STAGES * T::TILE_ELEMS;
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + T::BAR_OFFSET);
-    const int c = threadIdx.x / S::T;
-    const int th = threadIdx.x % S::T;
-    const size_t tiles = (batch + S::TPC - 1) / S::TPC;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < STAGES; ++st) tma::mbar_init(&bar[st], 1);
-        tma::fence_barrier_init();
-    }
-    const auto twt = TwiddleTable<LOGN>::load(reinterpret_cast<float2*>(smem_raw + T::TW_OFFSET), tw);
-    __syncthreads();
-    auto issue = [&](int st, size_t tile) {
-        const size_t first = tile * S::TPC;
-        const size_t cnt = batch - first < static_cast<size_t>(S::TPC) ? batch - first : S::TPC;
-        const uint32_t bytes = static_cast<uint32_t>(cnt * S::N * 8);
-        tma::mbar_arrive_expect_tx(&bar[st], bytes);
-        tma::bulk_load(ring + st * T::TILE_ELEMS, in + first * S::N, bytes, &bar[st]);
-    };
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < STAGES; ++st) {
-            const size_t tile = blockIdx.x + static_cast<size_t>(st) * gridDim.x;
-            if (tile < tiles) issue(st, tile);
-        }
-    }
-    const float sgn = inverse ? -1.f : 1.f;
-    float2* xb = xbuf + c * S::PADDED;
-    float2 v[S::E];
-    for (int k = 0;; ++k) {
-        const size_t tile = blockIdx.x + static_cast<size_t>(k) * gridDim.x;
-        if (tile >= tiles) break;
-        const int st = k % STAGES;
-        const bool ok = tma::mbar_wait(&bar[st], static_cast<uint32_t>((k / STAGES) & 1));
-        if (__syncthreads_or(!ok)) {
-            if (threadIdx.x == 0) tma::abort_ring<STAGES>(bar, k, blockIdx.x, gridDim.x, tiles, err);
-            break;
-        }
-        const size_t row = tile * S::TPC + c;
-        const bool active = row < batch;
-        const float2* src = ring + st * T::TILE_ELEMS + c * S::N;
-        float2* dst = out + row * S::N;
-        auto gload = [&](int i) -> float2 {
-            float2 x = src[i];
-            x.y *= sgn;
-            return x;
-        };
-        auto gstore = [&](int i, float2 x) {
-            if (active) __stcs(dst + i, make_float2(x.x * scale, x.y * sgn * scale));
-        };
-        Passes<LOGN, 0, false>::run(v, th, twt, xb, xb, gload, gstore);
-        __syncthreads();  // ring slot and exchange buffer are free
-        if (threadIdx.x == 0) {
-            const size_t next = tile + static_cast<size_t>(STAGES) * gridDim.x;
-            if (next < tiles) issue(st, next);
-        }
-    }
 }
 
 // ---- multi-pass global Stockham (N > 2^13) -----------------------------------

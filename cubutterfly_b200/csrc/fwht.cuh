@@ -12,33 +12,11 @@
 #pragma once
 
 #include "bitwise.cuh"
-#include "tma.cuh"
+#include "f32x2.cuh"
 
 namespace cubf::fwht {
 
-using P = unsigned long long;  // two fp32 lanes
-
-CUBF_DEV P pk(float lo, float hi) {
-    P r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-CUBF_DEV void up(P p, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(p)); }
-CUBF_DEV P add2(P a, P b) {
-    P r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-CUBF_DEV P sub2(P a, P b) {
-    P r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-CUBF_DEV P mul2(P a, P b) {
-    P r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
+using namespace cubf::f32x2;
 
 // Storage <-> pair conversions (16-bit types pack two elements per word).
 template <typename TS>
@@ -69,12 +47,6 @@ struct PairIO<__half> {
         return r;
     }
 };
-
-CUBF_DEV P fma2(P a, P b, P c) {
-    P r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
 
 template <typename TS, int LOGH, int LOGE>
 using FwhtShape = bw::TileShape<TS, float, LOGH, 0, LOGE>;
@@ -295,73 +267,6 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_block
         return active ? __ldg(reinterpret_cast<const uint4*>(tin + e)) : make_uint4(0, 0, 0, 0);
     };
     fwht_row<TS, LOGH, LOGE>(load16, tout, active, t, tbuf, scale);
-}
-
-// Persistent variant: each CTA walks tiles of TILES contiguous rows and keeps
-// STAGES of them in flight with bulk (TMA) copies into a shared-memory ring
-// (mbarrier completion, bounded waits recorded in `err`); group-1 vectors
-// are read from the ring, the rest as above.
-template <typename TS, int LOGH, int LOGE, int STAGES, bool EXCHANGE>
-struct FwhtTmaShape {
-    using S = FwhtShape<TS, LOGH, LOGE>;
-    static constexpr int ROW_ELEMS = 1 << LOGH;
-    static constexpr int TILE_BYTES = S::TILES * ROW_ELEMS * static_cast<int>(sizeof(TS));
-    static constexpr int XCH_OFFSET = STAGES * TILE_BYTES;
-    static constexpr int BAR_OFFSET = XCH_OFFSET + (EXCHANGE ? S::SMEM_BYTES : 0);
-    static constexpr int SMEM_BYTES = BAR_OFFSET + STAGES * 8;
-};
-
-template <typename TS, int LOGH, int LOGE, int STAGES, bool EXCHANGE>
-__global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_blocks<TS, LOGH, LOGE>())
-    fwht_tma_kernel(const TS* in, TS* out, size_t rows, float scale, unsigned* err) {
-    using S = FwhtShape<TS, LOGH, LOGE>;
-    using T = FwhtTmaShape<TS, LOGH, LOGE, STAGES, EXCHANGE>;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    TS* ring = reinterpret_cast<TS*>(smem_raw);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw + T::BAR_OFFSET);
-    const int local = threadIdx.x / S::TPT;
-    const uint32_t t = threadIdx.x % S::TPT;
-    float* tbuf = reinterpret_cast<float*>(smem_raw + T::XCH_OFFSET + local * S::TILE_SMEM);
-    const size_t tiles = (rows + S::TILES - 1) / S::TILES;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < STAGES; ++st) tma::mbar_init(&bar[st], 1);
-        tma::fence_barrier_init();
-    }
-    __syncthreads();
-    auto issue = [&](int st, size_t tile) {
-        const size_t first = tile * S::TILES;
-        const size_t cnt = rows - first < static_cast<size_t>(S::TILES) ? rows - first : S::TILES;
-        const uint32_t bytes = static_cast<uint32_t>(cnt * T::ROW_ELEMS * sizeof(TS));
-        tma::mbar_arrive_expect_tx(&bar[st], bytes);
-        tma::bulk_load(ring + static_cast<size_t>(st) * S::TILES * T::ROW_ELEMS, in + first * T::ROW_ELEMS, bytes,
-                       &bar[st]);
-    };
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < STAGES; ++st) {
-            const size_t tile = blockIdx.x + static_cast<size_t>(st) * gridDim.x;
-            if (tile < tiles) issue(st, tile);
-        }
-    }
-    for (int k = 0;; ++k) {
-        const size_t tile = blockIdx.x + static_cast<size_t>(k) * gridDim.x;
-        if (tile >= tiles) break;
-        const int st = k % STAGES;
-        const bool ok = tma::mbar_wait(&bar[st], static_cast<uint32_t>((k / STAGES) & 1));
-        if (__syncthreads_or(!ok)) {
-            if (threadIdx.x == 0) tma::abort_ring<STAGES>(bar, k, blockIdx.x, gridDim.x, tiles, err);
-            break;
-        }
-        const size_t row = tile * S::TILES + local;
-        const bool active = row < rows;
-        const TS* srow = ring + (static_cast<size_t>(st) * S::TILES + local) * T::ROW_ELEMS;
-        auto load16 = [&](uint32_t e) -> uint4 { return *reinterpret_cast<const uint4*>(srow + e); };
-        fwht_row<TS, LOGH, LOGE>(load16, out + (active ? row : 0) * T::ROW_ELEMS, active, t, tbuf, scale);
-        __syncthreads();  // ring slot and exchange buffer are free
-        if (threadIdx.x == 0) {
-            const size_t next = tile + static_cast<size_t>(STAGES) * gridDim.x;
-            if (next < tiles) issue(st, next);
-        }
-    }
 }
 
 }  // namespace cubf::fwht

@@ -10,6 +10,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <vector>
 
 namespace cubf {
 
@@ -23,6 +24,12 @@ struct LaunchShape {
 
 // ---- FFT (complex fp32) ------------------------------------------------------
 constexpr int kFftLocalMaxLog = 13;
+// Lengths served by the column-pair (f32x2) kernel.
+constexpr int kFftPairMinLog = 5;
+constexpr int kFftPairMaxLog = 13;
+// Twiddle table of a local plan: W_N^k (k < N, interleaved complex fp32),
+// followed for the column-pair lengths by its per-pass column-pair entries.
+std::vector<float> fft_local_twiddles(int log_n);
 LaunchShape fft_local_shape(int log_n);
 // `err` is a device word that receives error codes from bounded waits (or null).
 cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,

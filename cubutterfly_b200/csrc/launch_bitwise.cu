@@ -8,8 +8,6 @@
 #include "kernels.hpp"
 #include "launch_util.cuh"
 
-#include <cstdint>
-#include <cstdlib>
 
 #ifndef CUBF_BW_OP
 #error "CUBF_BW_OP must be defined (0 fwht, 1 subset zeta, 2 superset zeta)"
@@ -60,101 +58,28 @@ constexpr int kMaxStrided = sizeof(TC) == 8 ? 9 : 10;
 constexpr int fwht_log_e(int logh) { return logh <= 6 ? logh : (logh == 7 ? 5 : 6); }
 constexpr bool fwht_pair_kernel(int logh) { return (1 << logh) * static_cast<int>(sizeof(TS)) >= 16; }
 
-// Persistent TMA-ring variant for rows of at least 512 bytes, selected by
-// CUBUTTERFLY_FWHT_STAGES = ring depth (tiles in flight per CTA, clamped to
-// what fits in shared memory).  Off by default: on B200 the ring's shared
-// memory halves the resident warps and the non-persistent kernel, which keeps
-// 16-20 warps per SM issuing, is faster (5.16 vs 4.68 TB/s for bf16 rows of
-// 4096, 2 stages).
-constexpr int kFwhtTmaMinRowBytes = 512;
-constexpr int kFwhtDefaultStages = 0;
-constexpr int kFwhtMaxStages = 4;
-constexpr int kSmemLimit = 227 * 1024;
-
-int fwht_stages_setting() {
-    static const int stages = [] {
-        const char* e = std::getenv("CUBUTTERFLY_FWHT_STAGES");
-        if (!e || !*e) return kFwhtDefaultStages;
-        const int v = std::atoi(e);
-        return v < 0 ? 0 : (v > kFwhtMaxStages ? kFwhtMaxStages : v);
-    }();
-    return stages;
-}
-
 template <int LOGH>
 struct FwhtEntry {
     static constexpr int LOGE = fwht_log_e(LOGH);
     using S = fwht::FwhtShape<TS, LOGH, LOGE>;
     static constexpr bool kShuffle = fwht::ShuffleFinish<S>::value;
     static constexpr int SMEM = kShuffle ? 0 : S::SMEM_BYTES;
-    static constexpr bool kTma = (1 << LOGH) * static_cast<int>(sizeof(TS)) >= kFwhtTmaMinRowBytes;
-    template <int ST>
-    using TmaShape = fwht::FwhtTmaShape<TS, LOGH, LOGE, ST, !kShuffle>;
-    template <int ST>
-    static constexpr bool fits() { return TmaShape<ST>::SMEM_BYTES <= kSmemLimit; }
-
     static LaunchShape shape() {
         LaunchShape s;
         s.threads = S::TPB;
         s.smem_bytes = SMEM;
-        if constexpr (kTma) {
-            const int st = clamp_stages(fwht_stages_setting());
-            if (st > 0) s.smem_bytes = tma_smem(st);
-        }
         s.units_per_cta = S::TILES;
         s.elems_per_thread = S::E;
         s.exchanges = kShuffle ? 0 : S::G.count - 1 + (S::STAGE_OUT ? 1 : 0);
         return s;
     }
-    static int clamp_stages(int want) {
-        if (want <= 0) return 0;
-        for (int st = want; st >= 2; --st) {
-            if (st == 4 && fits<4>()) return 4;
-            if (st == 3 && fits<3>()) return 3;
-            if (st == 2 && fits<2>()) return 2;
-        }
-        return 0;
-    }
-    static int tma_smem(int st) {
-        return st == 4 ? TmaShape<4>::SMEM_BYTES : (st == 3 ? TmaShape<3>::SMEM_BYTES : TmaShape<2>::SMEM_BYTES);
-    }
-    template <int ST>
-    static cudaError_t launch_tma(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream,
-                                  unsigned* err) {
-        if constexpr (!fits<ST>()) {
-            return cudaErrorInvalidConfiguration;
-        } else {
-            auto kernel = fwht::fwht_tma_kernel<TS, LOGH, LOGE, ST, !kShuffle>;
-            constexpr int smem = TmaShape<ST>::SMEM_BYTES;
-            static KernelSetup setup;
-            int grid_cap = 0;
-            cudaError_t e = setup_kernel(setup, kernel, S::TPB, smem, &grid_cap);
-            if (e != cudaSuccess) return e;
-            const std::size_t tiles = (rows + S::TILES - 1) / S::TILES;
-            const unsigned grid =
-                static_cast<unsigned>(tiles < static_cast<std::size_t>(grid_cap) ? tiles : grid_cap);
-            kernel<<<grid, S::TPB, smem, stream>>>(static_cast<const TS*>(in), static_cast<TS*>(out), rows, scale,
-                                                    err);
-            return cudaGetLastError();
-        }
-    }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
                               float scale, int cache_mode, cudaStream_t stream, unsigned* err) {
         (void)inverse;  // FWHT is its own inverse up to the scale
         (void)cache_mode;
+        (void)err;  // no bounded waits in this kernel
         if (inner != 1) return cudaErrorInvalidValue;
         if (outer == 0) return cudaSuccess;
-        if constexpr (kTma) {
-            // bulk copies need a 16-byte aligned source (rows are >= 512 bytes)
-            if ((reinterpret_cast<std::uintptr_t>(in) & 15) == 0) {
-                switch (clamp_stages(fwht_stages_setting())) {
-                    case 4: return launch_tma<4>(in, out, outer, scale, stream, err);
-                    case 3: return launch_tma<3>(in, out, outer, scale, stream, err);
-                    case 2: return launch_tma<2>(in, out, outer, scale, stream, err);
-                    default: break;
-                }
-            }
-        }
         auto kernel = fwht::fwht_tile_kernel<TS, LOGH, LOGE>;
         static KernelSetup setup;
         int grid_cap = 0;

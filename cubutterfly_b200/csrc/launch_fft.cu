@@ -1,9 +1,12 @@
 // launch_fft.cu -- instantiations and launchers of the FFT kernels.
 #include "fft.cuh"
+#include "fft_pair.cuh"
 #include "kernels.hpp"
 #include "launch_util.cuh"
 
+#include <cmath>
 #include <cstdint>
+#include <vector>
 
 namespace cubf {
 namespace {
@@ -20,24 +23,23 @@ LaunchShape shape_of() {
     return s;
 }
 
-constexpr int kStages = 2;
-
-// Persistent TMA-pipelined variant for rows of at least 2 KB (LOGN >= 8).
+// Column-pair f32x2 kernel; its twiddle table follows the 2N floats of W_N.
 template <int LOGN>
-cudaError_t launch_tma(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
-                       cudaStream_t stream, unsigned* err) {
-    using S = fft::LocalShape<LOGN>;
-    using T = fft::TmaShape<LOGN, kStages>;
-    auto kernel = fft::fft_tma_kernel<LOGN, kStages>;
+cudaError_t launch_pair(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
+                        cudaStream_t stream, unsigned* err) {
+    (void)err;  // no bounded waits in this kernel
+    using S = fft::PairShape<LOGN>;
+    const float4* table = reinterpret_cast<const float4*>(static_cast<const float*>(tw) + 2 * S::N);
+    auto kernel = fft::fft_pair_kernel<LOGN>;
     static KernelSetup setup;
     int grid_cap = 0;
-    cudaError_t e = setup_kernel(setup, kernel, S::TPB, T::SMEM_BYTES, &grid_cap);
+    cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
     if (e != cudaSuccess) return e;
-    const std::size_t tiles = (batch + S::TPC - 1) / S::TPC;
-    if (tiles == 0) return cudaSuccess;
-    const unsigned grid = static_cast<unsigned>(tiles < static_cast<std::size_t>(grid_cap) ? tiles : grid_cap);
-    kernel<<<grid, S::TPB, T::SMEM_BYTES, stream>>>(static_cast<const float2*>(in), static_cast<float2*>(out), batch,
-                                                    static_cast<const float2*>(tw), inverse ? 1 : 0, scale, err);
+    const std::size_t blocks = (batch + S::TPC - 1) / S::TPC;
+    if (blocks == 0) return cudaSuccess;
+    if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+    kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+        static_cast<const float4*>(in), static_cast<float4*>(out), batch, table, inverse ? 1 : 0, scale);
     return cudaGetLastError();
 }
 
@@ -45,10 +47,9 @@ template <int LOGN>
 cudaError_t launch(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
                    cudaStream_t stream, unsigned* err) {
     using S = fft::LocalShape<LOGN>;
-    if constexpr (LOGN >= 8 && LOGN <= 12) {
-        // bulk copies need 16-byte aligned rows (always: N * 8 bytes, N >= 2)
-        if ((reinterpret_cast<std::uintptr_t>(in) & 15) == 0)
-            return launch_tma<LOGN>(in, out, batch, tw, inverse, scale, stream, err);
+    if constexpr (LOGN >= kFftPairMinLog && LOGN <= kFftPairMaxLog) {
+        if (((reinterpret_cast<std::uintptr_t>(in) | reinterpret_cast<std::uintptr_t>(out)) & 15) == 0)
+            return launch_pair<LOGN>(in, out, batch, tw, inverse, scale, stream, err);
     }
     auto kernel = fft::fft_local_kernel<LOGN>;
     static KernelSetup setup;
@@ -129,6 +130,41 @@ cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int lo
     if (log_r < kFftPassMinLog || log_r > kFftPassMaxLog) return cudaErrorInvalidValue;
     return Global::launch_fns[log_r - kFftPassMinLog](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in,
                                                       conj_out, scale, stream);
+}
+
+std::vector<float> fft_local_twiddles(int log_n) {
+    constexpr double kPi = 3.141592653589793238462643383279502884;
+    const std::size_t n = std::size_t{1} << log_n;
+    std::vector<float> tw(2 * n);
+    for (std::size_t k = 0; k < n; ++k) {
+        // exp(-2 pi i k / N) in double, rounded once (reference butterfly.cu:1502-1514)
+        const double a = -2.0 * kPi * static_cast<double>(k) / static_cast<double>(n);
+        tw[2 * k] = static_cast<float>(std::cos(a));
+        tw[2 * k + 1] = static_cast<float>(std::sin(a));
+    }
+    if (log_n >= kFftPairMinLog && log_n <= kFftPairMaxLog) {
+        // column-pair table: pass p >= 1, radix index r in [1, R), column pair
+        // jp < NS/2 -> (re, re, im, im) of W_{NS R}^{c r} for columns c = 2jp, 2jp+1
+        const int npass = (log_n + 3) / 4;
+        int ns_bits = 0;
+        for (int p = 0; p < npass; ++p) {
+            const int rb = log_n / npass + (p < log_n % npass ? 1 : 0);
+            if (p > 0) {
+                const std::size_t ns = std::size_t{1} << ns_bits, len = ns << rb;
+                for (std::size_t r = 1; r < (std::size_t{1} << rb); ++r)
+                    for (std::size_t jp = 0; jp < ns / 2; ++jp) {
+                        const double a0 = -2.0 * kPi * static_cast<double>((2 * jp * r) % len) / len;
+                        const double a1 = -2.0 * kPi * static_cast<double>(((2 * jp + 1) * r) % len) / len;
+                        tw.push_back(static_cast<float>(std::cos(a0)));
+                        tw.push_back(static_cast<float>(std::cos(a1)));
+                        tw.push_back(static_cast<float>(std::sin(a0)));
+                        tw.push_back(static_cast<float>(std::sin(a1)));
+                    }
+            }
+            ns_bits += rb;
+        }
+    }
+    return tw;
 }
 
 LaunchShape fft_local_shape(int log_n) {

@@ -89,10 +89,25 @@ constexpr int log2_const(int x) {
     return l;
 }
 
+constexpr int popcount_const(uint32_t x) {
+    int n = 0;
+    for (; x; x &= x - 1) ++n;
+    return n;
+}
+
+// Register groups of a tile of 2^(LOGH+LOGW) elements, LOGE register bits
+// per thread.  Group 1 holds the LOGV vector bits (16-byte loads) and the
+// top bits.  Each later group takes the remaining stage bits (the previous
+// group's lane bits first) and fills its register set with, in order: the
+// vector bits if it is the final group (16-byte stores), the previous
+// group's lane bits (its lowest five thread bits), then bits above those.
+// With the writer's lane bits as the reader's lowest register bits, the
+// scalar shared-memory stores of an exchange hit 32 distinct banks.
 template <int LOGH, int LOGW, int LOGE, int LOGV>
 constexpr Groups make_groups() {
     Groups g{};
     constexpr int LT = LOGH + LOGW;
+    const uint32_t full = lowmask(LT);
     const uint32_t transform = lowmask(LOGH) << LOGW;
     const uint32_t g1 = lowmask(LOGV) | (lowmask(LOGE - LOGV) << (LT - (LOGE - LOGV)));
     g.reg[0] = g1;
@@ -101,15 +116,45 @@ constexpr Groups make_groups() {
     int k = 1;
     while ((transform & ~done) != 0u && k < 4) {
         const uint32_t rem = transform & ~done;
+        const uint32_t thread_bits = full & ~g.reg[k - 1];
+        uint32_t lanes = 0;
+        int nl = 0, top = -1;
+        for (int b = 0; b < LT && nl < 5; ++b)
+            if ((thread_bits >> b) & 1u) {
+                lanes |= 1u << b;
+                ++nl;
+                top = b;
+            }
+        const bool last = popcount_const(rem) <= LOGE;
         uint32_t take = 0;
         int cnt = 0;
         for (int b = 0; b < LT && cnt < LOGE; ++b)
-            if ((rem >> b) & 1u) {
+            if (((rem & lanes) >> b) & 1u) {
+                take |= 1u << b;
+                ++cnt;
+            }
+        for (int b = 0; b < LT && cnt < LOGE; ++b)
+            if (((rem & ~take) >> b) & 1u) {
                 take |= 1u << b;
                 ++cnt;
             }
         uint32_t reg = take;
-        // Fill the group with low bits first so the final store can vectorise.
+        if (last)
+            for (int b = 0; b < LOGV && cnt < LOGE; ++b)
+                if (!((reg >> b) & 1u)) {
+                    reg |= 1u << b;
+                    ++cnt;
+                }
+        for (int b = 0; b < LT && cnt < LOGE; ++b)
+            if (((lanes & ~reg) >> b) & 1u) {
+                reg |= 1u << b;
+                ++cnt;
+            }
+        for (int b = top + 1; b < LT && cnt < LOGE; ++b)
+            if (!((reg >> b) & 1u)) {
+                reg |= 1u << b;
+                ++cnt;
+            }
         for (int b = 0; b < LT && cnt < LOGE; ++b)
             if (!((reg >> b) & 1u)) {
                 reg |= 1u << b;
@@ -122,6 +167,13 @@ constexpr Groups make_groups() {
     }
     g.count = k;
     return g;
+}
+
+template <int LOGH, int LOGW>
+constexpr bool covers(const Groups& g) {
+    uint32_t acc = 0;
+    for (int k = 0; k < g.count; ++k) acc |= g.stage[k];
+    return acc == (lowmask(LOGH) << LOGW);
 }
 
 template <typename TS_, typename TC_, int LOGH_, int LOGW_, int LOGE_>
@@ -141,6 +193,7 @@ struct TileShape {
     static constexpr int LOGV = (LOGE >= VEC_BITS && (LOGW == 0 || LOGW >= VEC_BITS)) ? VEC_BITS : 0;
     static constexpr int V = 1 << LOGV;
     static constexpr Groups G = make_groups<LOGH, LOGW, LOGE, LOGV>();
+    static_assert(covers<LOGH, LOGW>(G), "register groups must cover every transformed bit");
     static constexpr int TPB = TPT >= 128 ? TPT : 128;
     static constexpr int TILES = TPB / TPT;  // tiles per CTA
     // Final group stores 16-byte vectors when it holds bits 0..LOGV-1;

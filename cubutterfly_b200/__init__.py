@@ -220,7 +220,6 @@ class Library:
             "ExecuteSteady": [p, p, p, p],
             "PlanGetSelectionSource": [p, pi],
             "PlanGetPhysicalExtents": [p, pn, ct.c_uint32],
-            "B200PlanGetDeviceStatus": [p, p, ct.POINTER(ct.c_uint), i],
             "B200RankMappings": [p, ct.c_char_p, ct.c_void_p, pn],
         }
         for name in _STRING_QUERIES:
@@ -483,12 +482,6 @@ class Plan:
 
     def execute_steady(self, input, output):
         self.library._call("ExecuteSteady", self._context, self.native_handle, _pointer(input), _pointer(output))
-
-    def device_status(self, reset=False):
-        """Error word of the plan's bounded device waits (0 = healthy)."""
-        v = ct.c_uint()
-        self.library._call("B200PlanGetDeviceStatus", self._context, self.native_handle, ct.byref(v), int(reset))
-        return v.value
 
     def mapping_json(self):
         return self.library._query("PlanGetMappingJson", self.native_handle)

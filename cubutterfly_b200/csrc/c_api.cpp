@@ -52,7 +52,6 @@ struct cubutterflyPlan {
     void* outer_lo = nullptr;  // global FFT: double2 W_N^k, k < 2^split
     void* outer_hi = nullptr;  // global FFT: double2 W_N^(k << split)
     int outer_split = 0;
-    unsigned* device_status = nullptr;  // error word written by bounded device waits
     int device = 0;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
@@ -60,7 +59,6 @@ struct cubutterflyPlan {
         if (twiddles) cudaFree(twiddles);
         if (outer_lo) cudaFree(outer_lo);
         if (outer_hi) cudaFree(outer_hi);
-        if (device_status) cudaFree(device_status);
     }
 };
 
@@ -205,8 +203,7 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
         const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
         if (m.passes.front().kind == cubf::PassKind::FftLocal) {
-            check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream,
-                                              p.device_status),
+            check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream),
                        "FFT launch");
             return;
         }
@@ -262,8 +259,7 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
             const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
             const int mode = !chained ? 0 : (i == 0 ? 1 : (last ? 2 : 3));
             check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, dst, outer_arg,
-                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream,
-                                       p.device_status),
+                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream),
                        "tile pass launch");
             src = dst;
         }
@@ -288,8 +284,6 @@ double time_mapping(cubutterflyPlan& p, const cubf::Mapping& m, const void* in, 
 }
 
 void build_tables(cubutterflyPlan& p) {
-    check_cuda(cudaMalloc(reinterpret_cast<void**>(&p.device_status), sizeof(unsigned)), "status word allocation");
-    check_cuda(cudaMemset(p.device_status, 0, sizeof(unsigned)), "status word init");
     if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
     constexpr double kPi = 3.141592653589793238462643383279502884;
     const bool global = p.mapping.passes.front().kind == cubf::PassKind::FftGlobal;
@@ -836,16 +830,6 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         cubf::Json out = cubf::Json::array();
         for (const auto& m : cubf::enumerate_mappings(make_request(d), hw)) out.push_back(m.to_json());
         copy_text(out.dump(), json, bytes);
-    });
-}
-
-cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterflyHandle_t handle, cubutterflyPlan_t plan,
-                                                       unsigned* status, int reset) {
-    return protect([&] {
-        require(handle != nullptr && plan != nullptr && status != nullptr, "handle, plan and status must be non-null");
-        check_cuda(cudaStreamSynchronize(handle->stream), "stream synchronize");
-        check_cuda(cudaMemcpy(status, plan->device_status, sizeof(unsigned), cudaMemcpyDeviceToHost), "status read");
-        if (reset) check_cuda(cudaMemset(plan->device_status, 0, sizeof(unsigned)), "status reset");
     });
 }
 

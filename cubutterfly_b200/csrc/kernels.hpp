@@ -31,9 +31,8 @@ constexpr int kFftPairMaxLog = 13;
 // followed for the column-pair lengths by its per-pass column-pair entries.
 std::vector<float> fft_local_twiddles(int log_n);
 LaunchShape fft_local_shape(int log_n);
-// `err` is a device word that receives error codes from bounded waits (or null).
 cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
-                             bool inverse, float scale, cudaStream_t stream, unsigned* err);
+                             bool inverse, float scale, cudaStream_t stream);
 
 // Multi-pass global Stockham for N > 2^13: radix 2^4..2^10 per pass.
 constexpr int kFftPassMinLog = 4;
@@ -69,9 +68,8 @@ LaunchShape bw_shape(const BwVariant& v);
 // outer arrays of (2^log_h x inner) elements; the pass transforms the 2^log_h
 // axis.  in may equal out.  cache_mode: 0 streaming single pass, 1 first pass
 // of a chain (output kept in L2), 2 last pass of a chain, 3 middle pass.
-// `err` is a device word that receives error codes from bounded waits (or null).
 cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
-                      bool inverse, float scale, int cache_mode, cudaStream_t stream, unsigned* err = nullptr);
+                      bool inverse, float scale, int cache_mode, cudaStream_t stream);
 
 // ---- RNS NTT tile passes --------------------------------------------------------
 struct NttPolyDesc {

@@ -74,10 +74,9 @@ struct FwhtEntry {
         return s;
     }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
-                              float scale, int cache_mode, cudaStream_t stream, unsigned* err) {
+                              float scale, int cache_mode, cudaStream_t stream) {
         (void)inverse;  // FWHT is its own inverse up to the scale
         (void)cache_mode;
-        (void)err;  // no bounded waits in this kernel
         if (inner != 1) return cudaErrorInvalidValue;
         if (outer == 0) return cudaSuccess;
         auto kernel = fwht::fwht_tile_kernel<TS, LOGH, LOGE>;
@@ -107,8 +106,7 @@ struct Entry {
         return s;
     }
     static cudaError_t launch(const void* in, void* out, std::size_t outer, std::size_t inner, bool inverse,
-                              float scale, int cache_mode, cudaStream_t stream, unsigned* err) {
-        (void)err;
+                              float scale, int cache_mode, cudaStream_t stream) {
         auto kernel = bw::bitwise_tile_kernel<Op, TS, TC, LOGH, LOGW, kLogE>;
         static KernelSetup setup;
         int grid_cap = 0;
@@ -128,8 +126,7 @@ struct Entry {
     }
 };
 
-using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, int, cudaStream_t,
-                                 unsigned*);
+using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, std::size_t, bool, float, int, cudaStream_t);
 using ShapeFn = LaunchShape (*)();
 
 #if CUBF_BW_OP == 0
@@ -192,11 +189,11 @@ LaunchShape CUBF_CAT(CUBF_UNIT, _shape)(int log_h, int log_w) {
 
 cudaError_t CUBF_CAT(CUBF_UNIT, _launch)(int log_h, int log_w, const void* in, void* out, std::size_t outer,
                                          std::size_t inner, bool inverse, float scale, int cache_mode,
-                                         cudaStream_t stream, unsigned* err) {
+                                         cudaStream_t stream) {
     if (log_w == 0 && log_h >= 1 && log_h <= kMaxContig)
-        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream, err);
+        return C::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream);
     if (kHasStrided && log_w == kLogW && log_h >= 1 && log_h <= kMaxStrided)
-        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream, err);
+        return T::launch[log_h - 1](in, out, outer, inner, inverse, scale, cache_mode, stream);
     return cudaErrorInvalidValue;
 }
 

@@ -7,8 +7,7 @@ namespace cubf {
     LaunchShape bw_unit_##OP##_##TY##_shape(int log_h, int log_w);                                      \
     cudaError_t bw_unit_##OP##_##TY##_launch(int log_h, int log_w, const void* in, void* out,          \
                                              std::size_t outer, std::size_t inner, bool inverse,       \
-                                             float scale, int cache_mode, cudaStream_t stream, \
-                                             unsigned* err);
+                                             float scale, int cache_mode, cudaStream_t stream);
 CUBF_DECLARE_UNIT(0, 0)
 CUBF_DECLARE_UNIT(0, 1)
 CUBF_DECLARE_UNIT(0, 2)
@@ -21,7 +20,7 @@ CUBF_DECLARE_UNIT(2, 4)
 namespace {
 using ShapeFn = LaunchShape (*)(int, int);
 using LaunchFn = cudaError_t (*)(int, int, const void*, void*, std::size_t, std::size_t, bool, float, int,
-                                 cudaStream_t, unsigned*);
+                                 cudaStream_t);
 struct Unit {
     ShapeFn shape;
     LaunchFn launch;
@@ -78,10 +77,10 @@ LaunchShape bw_shape(const BwVariant& v) {
 }
 
 cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
-                      bool inverse, float scale, int cache_mode, cudaStream_t stream, unsigned* err) {
+                      bool inverse, float scale, int cache_mode, cudaStream_t stream) {
     const Unit u = unit_of(v.op, v.type);
     if (!u.launch) return cudaErrorInvalidValue;
-    return u.launch(v.log_h, v.log_w, in, out, outer, inner, inverse, scale, cache_mode, stream, err);
+    return u.launch(v.log_h, v.log_w, in, out, outer, inner, inverse, scale, cache_mode, stream);
 }
 
 }  // namespace cubf

@@ -26,8 +26,7 @@ LaunchShape shape_of() {
 // Column-pair f32x2 kernel; its twiddle table follows the 2N floats of W_N.
 template <int LOGN>
 cudaError_t launch_pair(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
-                        cudaStream_t stream, unsigned* err) {
-    (void)err;  // no bounded waits in this kernel
+                        cudaStream_t stream) {
     using S = fft::PairShape<LOGN>;
     const float4* table = reinterpret_cast<const float4*>(static_cast<const float*>(tw) + 2 * S::N);
     auto kernel = fft::fft_pair_kernel<LOGN>;
@@ -45,11 +44,11 @@ cudaError_t launch_pair(const void* in, void* out, std::size_t batch, const void
 
 template <int LOGN>
 cudaError_t launch(const void* in, void* out, std::size_t batch, const void* tw, bool inverse, float scale,
-                   cudaStream_t stream, unsigned* err) {
+                   cudaStream_t stream) {
     using S = fft::LocalShape<LOGN>;
     if constexpr (LOGN >= kFftPairMinLog && LOGN <= kFftPairMaxLog) {
         if (((reinterpret_cast<std::uintptr_t>(in) | reinterpret_cast<std::uintptr_t>(out)) & 15) == 0)
-            return launch_pair<LOGN>(in, out, batch, tw, inverse, scale, stream, err);
+            return launch_pair<LOGN>(in, out, batch, tw, inverse, scale, stream);
     }
     auto kernel = fft::fft_local_kernel<LOGN>;
     static KernelSetup setup;
@@ -65,7 +64,7 @@ cudaError_t launch(const void* in, void* out, std::size_t batch, const void* tw,
     return cudaGetLastError();
 }
 
-using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, const void*, bool, float, cudaStream_t, unsigned*);
+using LaunchFn = cudaError_t (*)(const void*, void*, std::size_t, const void*, bool, float, cudaStream_t);
 using ShapeFn = LaunchShape (*)();
 
 template <int... L>
@@ -173,9 +172,9 @@ LaunchShape fft_local_shape(int log_n) {
 }
 
 cudaError_t launch_fft_local(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
-                             bool inverse, float scale, cudaStream_t stream, unsigned* err) {
+                             bool inverse, float scale, cudaStream_t stream) {
     if (log_n < 1 || log_n > kFftLocalMaxLog) return cudaErrorInvalidValue;
-    return Local::launch_fns[log_n - 1](in, out, batch, twiddles, inverse, scale, stream, err);
+    return Local::launch_fns[log_n - 1](in, out, batch, twiddles, inverse, scale, stream);
 }
 
 }  // namespace cubf

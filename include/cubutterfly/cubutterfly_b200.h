@@ -23,15 +23,6 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescri
                                                               const char* hardware_json, char* json,
                                                               size_t* bytes);
 
-/* Device-side status of a plan (no counterpart in the reference ABI): the
- * persistent kernels wait on shared-memory barriers with bounded polls and,
- * instead of trapping, record a nonzero code (1 = a bulk-copy wait expired)
- * in a per-plan device word.  Reads the word after synchronising the
- * handle's stream; `reset` nonzero clears it. */
-CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterflyHandle_t handle,
-                                                                     cubutterflyPlan_t plan, unsigned* status,
-                                                                     int reset);
-
 /* Twiddle step of the four-step FFT (no counterpart in the reference ABI;
  * used by cubutterfly_b200.distributed for one transform split across GPUs).
  * data: `rows` x `cols` complex fp32, row-major, 16-byte aligned;

@@ -104,7 +104,7 @@ constexpr int popcount_const(uint32_t x) {
 // With the writer's lane bits as the reader's lowest register bits, the
 // scalar shared-memory stores of an exchange hit 32 distinct banks.
 template <int LOGH, int LOGW, int LOGE, int LOGV>
-constexpr Groups make_groups() {
+constexpr Groups lane_fill_groups() {
     Groups g{};
     constexpr int LT = LOGH + LOGW;
     const uint32_t full = lowmask(LT);
@@ -169,11 +169,191 @@ constexpr Groups make_groups() {
     return g;
 }
 
-template <int LOGH, int LOGW>
-constexpr bool covers(const Groups& g) {
+// A plan is well formed when every group holds exactly LOGE register bits,
+// each stage bit belongs to its group, and the stages cover every
+// transformed bit once.
+template <int LOGH, int LOGW, int LOGE>
+constexpr bool well_formed(const Groups& g) {
+    if (g.count < 1 || g.count > 4) return false;
     uint32_t acc = 0;
-    for (int k = 0; k < g.count; ++k) acc |= g.stage[k];
+    for (int k = 0; k < g.count; ++k) {
+        if (popcount_const(g.reg[k]) != LOGE || (g.stage[k] & ~g.reg[k]) != 0u || (acc & g.stage[k]) != 0u)
+            return false;
+        acc |= g.stage[k];
+    }
     return acc == (lowmask(LOGH) << LOGW);
+}
+
+// Alternative plan: every later group holds all of the previous group's
+// lane bits and takes stage bits only in the remaining slots, finishing
+// (with the vector bits) as soon as the rest fits.  Costs a group more on
+// some tiles but makes every exchange conflict free by construction.
+template <int LOGH, int LOGW, int LOGE, int LOGV>
+constexpr Groups lanes_first_groups() {
+    Groups g{};
+    constexpr int LT = LOGH + LOGW;
+    const uint32_t full = lowmask(LT);
+    const uint32_t transform = lowmask(LOGH) << LOGW;
+    const uint32_t g1 = lowmask(LOGV) | (lowmask(LOGE - LOGV) << (LT - (LOGE - LOGV)));
+    g.reg[0] = g1;
+    g.stage[0] = g1 & transform;
+    uint32_t done = g.stage[0];
+    int k = 1;
+    while ((transform & ~done) != 0u && k < 4) {
+        const uint32_t rem = transform & ~done;
+        const uint32_t thread_bits = full & ~g.reg[k - 1];
+        uint32_t reg = 0;
+        int nl = 0, top = -1;
+        for (int b = 0; b < LT && nl < 5; ++b)
+            if ((thread_bits >> b) & 1u) {
+                reg |= 1u << b;
+                ++nl;
+                top = b;
+            }
+        if (nl > LOGE) return Groups{};
+        const uint32_t need = (rem | lowmask(LOGV)) & ~reg;
+        if (popcount_const(need) + nl <= LOGE) {
+            reg |= need;
+            int cnt = popcount_const(reg);
+            for (int b = top + 1; b < LT && cnt < LOGE; ++b)
+                if (!((reg >> b) & 1u)) {
+                    reg |= 1u << b;
+                    ++cnt;
+                }
+            for (int b = 0; b < LT && cnt < LOGE; ++b)
+                if (!((reg >> b) & 1u)) {
+                    reg |= 1u << b;
+                    ++cnt;
+                }
+        } else {
+            int cnt = nl;
+            for (int b = 0; b < LT && cnt < LOGE; ++b)
+                if (((rem & ~reg) >> b) & 1u) {
+                    reg |= 1u << b;
+                    ++cnt;
+                }
+            for (int b = top + 1; b < LT && cnt < LOGE; ++b)
+                if (!((reg >> b) & 1u)) {
+                    reg |= 1u << b;
+                    ++cnt;
+                }
+            for (int b = 0; b < LT && cnt < LOGE; ++b)
+                if (!((reg >> b) & 1u)) {
+                    reg |= 1u << b;
+                    ++cnt;
+                }
+        }
+        if ((reg & rem) == 0u || popcount_const(reg) != LOGE) return Groups{};
+        g.reg[k] = reg;
+        g.stage[k] = reg & rem;
+        done |= reg & rem;
+        ++k;
+    }
+    g.count = (transform & ~done) == 0u ? k : 0;
+    return g;
+}
+
+// Shared-memory cost of a plan: (passes, wavefronts).  Passes are the
+// exchanges plus the output staging when the final group cannot store
+// 16-byte vectors.  Wavefronts are those of one warp's scalar stores and
+// 16-byte loads per pass, from an exact bank model of lanes 0..31 (banks
+// shift uniformly with the register index, so register 0 stands for all).
+struct SmemCost {
+    int passes;
+    int waves;
+};
+
+// Max distinct 32-bit words per bank among `n` lanes accessing `width`
+// bytes each at byte addresses a[] (wider accesses issue in phases of
+// 128 bytes).
+constexpr int bank_waves(const uint32_t (&a)[32], int width) {
+    const int per_phase = width <= 4 ? 32 : 128 / width;
+    int total = 0;
+    for (int p0 = 0; p0 < 32; p0 += per_phase) {
+        int worst = 0;
+        for (int bank = 0; bank < 32; ++bank) {
+            uint32_t words[32] = {};
+            int nw = 0;
+            for (int l = p0; l < p0 + per_phase; ++l)
+                for (int w = 0; w < (width <= 4 ? 1 : width / 4); ++w) {
+                    const uint32_t word = (a[l] >> 2) + static_cast<uint32_t>(w);
+                    if (static_cast<int>(word % 32u) != bank) continue;
+                    bool seen = false;
+                    for (int i = 0; i < nw; ++i) seen = seen || words[i] == word;
+                    if (!seen) words[nw++] = word;
+                }
+            worst = nw > worst ? nw : worst;
+        }
+        total += worst;
+    }
+    return total;
+}
+
+template <int LT, int LOGE>
+constexpr uint32_t layout_addr(uint32_t e, uint32_t rn, int pad, int tile, int tile_elems, int esize) {
+    const uint32_t row = extract(e, lowmask(LT) & ~rn);
+    const uint32_t j = extract(e, rn);
+    return (static_cast<uint32_t>(tile * tile_elems) + row * static_cast<uint32_t>((1 << LOGE) + pad) + j) *
+           static_cast<uint32_t>(esize);
+}
+
+template <int LT, int LOGE>
+constexpr int pass_waves(uint32_t writer, uint32_t reader, int pad, int tile_elems, int esize) {
+    constexpr int TPT = 1 << (LT - LOGE);
+    uint32_t a[32] = {};
+    for (int l = 0; l < 32; ++l) {
+        const int tile = l / TPT, t = l % TPT;
+        a[l] = layout_addr<LT, LOGE>(deposit(static_cast<uint32_t>(t), lowmask(LT) & ~writer), reader, pad, tile,
+                                     tile_elems, esize);
+    }
+    const int stores = (1 << LOGE) * bank_waves(a, esize);
+    for (int l = 0; l < 32; ++l) {
+        const int tile = l / TPT, t = l % TPT;
+        a[l] = layout_addr<LT, LOGE>(deposit(static_cast<uint32_t>(t), lowmask(LT) & ~reader), reader, pad, tile,
+                                     tile_elems, esize);
+    }
+    const int per_load = 16 / esize;
+    const int loads = ((1 << LOGE) >= per_load ? (1 << LOGE) / per_load : 1) * bank_waves(a, 16);
+    return stores + loads;
+}
+
+template <int LOGH, int LOGW, int LOGE, int LOGV, int TS_BYTES, int TC_BYTES>
+constexpr SmemCost smem_cost(const Groups& g) {
+    constexpr int LT = LOGH + LOGW;
+    constexpr int E = 1 << LOGE;
+    constexpr int TPT = 1 << (LT - LOGE);
+    SmemCost c{0, 0};
+    if (!well_formed<LOGH, LOGW, LOGE>(g)) return SmemCost{1 << 20, 1 << 20};
+    const int padc = 16 / TC_BYTES, pads = 16 / TS_BYTES;
+    const int xch_elems = TPT * (E + padc);
+    for (int k = 1; k < g.count; ++k) {
+        ++c.passes;
+        c.waves += pass_waves<LT, LOGE>(g.reg[k - 1], g.reg[k], padc, xch_elems, TC_BYTES);
+    }
+    const bool vec_final = LOGV > 0 && (g.reg[g.count - 1] & lowmask(LOGV)) == lowmask(LOGV);
+    if (LOGV > 0 && !vec_final) {
+        ++c.passes;
+        const int out_elems = TPT * (E + pads);
+        const int tile_elems = (xch_elems * TC_BYTES > out_elems * TS_BYTES ? xch_elems * TC_BYTES
+                                                                           : out_elems * TS_BYTES) /
+                               TS_BYTES;
+        c.waves += pass_waves<LT, LOGE>(g.reg[g.count - 1], g.reg[0], pads, tile_elems, TS_BYTES);
+    }
+    return c;
+}
+
+// The plan a tile uses: the fewer shared-memory passes, then the fewer
+// wavefronts.
+template <int LOGH, int LOGW, int LOGE, int LOGV, int TS_BYTES, int TC_BYTES>
+constexpr Groups make_groups() {
+    constexpr Groups a = lane_fill_groups<LOGH, LOGW, LOGE, LOGV>();
+    constexpr Groups b = lanes_first_groups<LOGH, LOGW, LOGE, LOGV>();
+    constexpr SmemCost ca = smem_cost<LOGH, LOGW, LOGE, LOGV, TS_BYTES, TC_BYTES>(a);
+    constexpr SmemCost cb = smem_cost<LOGH, LOGW, LOGE, LOGV, TS_BYTES, TC_BYTES>(b);
+    if constexpr (cb.passes < ca.passes || (cb.passes == ca.passes && cb.waves < ca.waves))
+        return b;
+    else
+        return a;
 }
 
 template <typename TS_, typename TC_, int LOGH_, int LOGW_, int LOGE_>
@@ -192,8 +372,8 @@ struct TileShape {
     // contiguous in memory (contiguous tiles, or at least that many columns).
     static constexpr int LOGV = (LOGE >= VEC_BITS && (LOGW == 0 || LOGW >= VEC_BITS)) ? VEC_BITS : 0;
     static constexpr int V = 1 << LOGV;
-    static constexpr Groups G = make_groups<LOGH, LOGW, LOGE, LOGV>();
-    static_assert(covers<LOGH, LOGW>(G), "register groups must cover every transformed bit");
+    static constexpr Groups G = make_groups<LOGH, LOGW, LOGE, LOGV, sizeof(TS), sizeof(TC)>();
+    static_assert(well_formed<LOGH, LOGW, LOGE>(G), "register groups must be well formed");
     static constexpr int TPB = TPT >= 128 ? TPT : 128;
     static constexpr int TILES = TPB / TPT;  // tiles per CTA
     // Final group stores 16-byte vectors when it holds bits 0..LOGV-1;

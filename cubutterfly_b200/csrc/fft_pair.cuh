@@ -17,6 +17,7 @@
 
 #include "f32x2.cuh"
 
+#include <type_traits>
 #include <utility>
 
 namespace cubf::fft {
@@ -117,13 +118,14 @@ struct PairShape {
     }
     static constexpr int TPB = T >= 128 ? T : 128;
     static constexpr int TPC = TPB / T;  // transforms per CTA
-    // One real and one imaginary plane of N floats per transform (plus two
-    // floats so the planes of adjacent transforms start in different banks).
-    static constexpr int PLANE = N + 2;
+    // One real and one imaginary plane per transform.  Element i lives at
+    // pad(i) = i + 2 (i / 32): two floats of padding per 32 spread the
+    // strided exchange stores over the banks while keeping 64-bit granules
+    // aligned, and pad(i + 32 m) = pad(i) + 34 m, so every access is a
+    // per-thread base plus a compile-time offset.
+    static CUBF_DEV int pad(int i) { return i + ((i >> 5) << 1); }
+    static constexpr int PLANE = N + N / 16 + 2;
     static constexpr int SMEM_BYTES = TPC * 2 * PLANE * 4;
-    // 64-bit granules of a plane are XOR-swizzled by the 32-float row index so
-    // that the strided exchange stores spread over the banks.
-    static CUBF_DEV int swz(int i) { return i ^ (((i >> 5) & 15) << 1); }
     // Twiddle table: for each pass p >= 1, (R_p - 1) x (NS_p / 2) entries.
     static constexpr int tw_offset(int p) {
         int o = 0;
@@ -134,18 +136,51 @@ struct PairShape {
     static_assert(LOGN >= 5 && LOGN <= 13, "column-pair kernel covers 2^5 .. 2^13 points");
 };
 
-template <int LOGN, int P, typename Load2>
-CUBF_DEV void pair_pass_load(CP (&v)[16], int q, const float4* __restrict__ tw, Load2 load2) {
+// Offset of element base + off in a padded plane, given pad(base); when
+// base's low five bits and off cannot carry into bit 5 the padding of off
+// adds on its own (off a multiple of 32, or base + off within one 32-block).
+template <int OFF, bool SAME_BLOCK>
+CUBF_DEV int pad_add(int pbase, int base) {
+    if constexpr (OFF % 32 == 0) return pbase + OFF + ((OFF >> 5) << 1);
+    else if constexpr (SAME_BLOCK) return pbase + OFF;
+    else return base + OFF + (((base + OFF) >> 5) << 1);
+}
+
+template <int N, int... I>
+struct Unroll {
+    template <typename F>
+    static CUBF_DEV void run(F&& f) {
+        if constexpr (sizeof...(I) < N) Unroll<N, I..., sizeof...(I)>::run(f);
+        else (f(std::integral_constant<int, I>{}), ...);
+    }
+};
+
+// Pass P, load half: the R inputs x[j + r N/R] of columns j, j+1 (j even),
+// the inter-pass twiddles, the radix-R codelets.  `gload(i)` reads HBM (pass
+// 0); later passes read the padded planes.
+template <int LOGN, int P, typename GLoad>
+CUBF_DEV void pair_pass_load(CP (&v)[16], int q, const float4* __restrict__ tw, const float* pre,
+                             const float* pim, GLoad gload) {
     using S = PairShape<LOGN>;
     constexpr int RB = S::radix_bits(P);
     constexpr int R = 1 << RB;
     constexpr int NS = 1 << S::ns_bits(P);
     constexpr int SUB = 16 / R;
+    constexpr int STEP = S::N / R;
 #pragma unroll
     for (int u = 0; u < SUB; ++u) {
         const int j = 2 * (q + S::T * u);
+        if constexpr (P == 0) {
 #pragma unroll
-        for (int r = 0; r < R; ++r) v[u * R + r] = load2(j + r * (S::N / R));
+            for (int r = 0; r < R; ++r) v[u * R + r] = gload(j + r * STEP);
+        } else {
+            const int pj = S::pad(j);
+            Unroll<R>::run([&](auto rc) {
+                constexpr int r = decltype(rc)::value;
+                const int a = pad_add<r * STEP, false>(pj, j);
+                v[u * R + r] = CP{*reinterpret_cast<const f32x2::P*>(pre + a), *reinterpret_cast<const f32x2::P*>(pim + a)};
+            });
+        }
     }
     if constexpr (NS > 1) {
 #pragma unroll
@@ -163,26 +198,55 @@ CUBF_DEV void pair_pass_load(CP (&v)[16], int q, const float4* __restrict__ tw, 
     for (int u = 0; u < SUB; ++u) PairDft<R>::run(&v[u * R]);
 }
 
-// Stockham store of pass P: output k of column j goes to
-// (j / NS) NS R + (j mod NS) + k NS.  Columns j and j+1 are adjacent there
-// when NS >= 2 (store2(i, x) writes both); in pass 0 they are R apart
-// (split(i0, i1, x)).
-template <int LOGN, int P, typename Store2, typename Split>
-CUBF_DEV void pair_pass_store(const CP (&v)[16], int q, Store2 store2, Split split) {
+// Pass P, store half: output k of column j goes to (j / NS) NS R + (j mod NS)
+// + k NS.  Columns j and j+1 are adjacent there when NS >= 2 (one 64-bit
+// store per plane); in pass 0 (NS = 1) they are R apart.  The last pass
+// writes HBM through `gstore(i, x)` (i even, both columns).
+template <int LOGN, int P, typename GStore>
+CUBF_DEV void pair_pass_store(const CP (&v)[16], int q, float* pre, float* pim, GStore gstore) {
     using S = PairShape<LOGN>;
     constexpr int RB = S::radix_bits(P);
     constexpr int R = 1 << RB;
     constexpr int NSB = S::ns_bits(P);
     constexpr int NS = 1 << NSB;
     constexpr int SUB = 16 / R;
+    constexpr bool LAST = P == S::NPASS - 1;
 #pragma unroll
     for (int u = 0; u < SUB; ++u) {
         const int j = 2 * (q + S::T * u);
-        const int base = ((j >> NSB) << (NSB + RB)) + (j & (NS - 1));
+        const int hi = (j >> NSB) << (NSB + RB);
+        const int base = hi + (j & (NS - 1));
+        if constexpr (LAST) {
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
-            if constexpr (NS >= 2) store2(base + k * NS, v[u * R + k]);
-            else split(base + k, base + R + k, v[u * R + k]);
+            for (int k = 0; k < R; ++k) gstore(base + k * NS, v[u * R + k]);
+        } else if constexpr (NS >= 2) {
+            // hi is a multiple of NS R >= 32; (j mod NS) + k NS stays inside a
+            // 32-block when NS < 32 (NS divides 32), else k NS is a multiple of 32
+            static_assert(NS * R >= 32, "exchange planes assume NS R >= 32");
+            const int pb = (NS >= 32) ? S::pad(base) : base + ((hi >> 5) << 1);
+            Unroll<R>::run([&](auto kc) {
+                constexpr int k = decltype(kc)::value;
+                constexpr int off = k * NS;
+                const int a = NS >= 32 ? pad_add<off, false>(pb, base) : pb + off + ((off >> 5) << 1);
+                *reinterpret_cast<f32x2::P*>(pre + a) = v[u * R + k].re;
+                *reinterpret_cast<f32x2::P*>(pim + a) = v[u * R + k].im;
+            });
+        } else {
+            // pass 0: column j at j R + k, column j + 1 at j R + R + k; with
+            // R >= 16 both stay in the 32-block of j R (j even)
+            const int pb = S::pad(base);
+            Unroll<R>::run([&](auto kc) {
+                constexpr int k = decltype(kc)::value;
+                float r0, r1, m0, m1;
+                up(v[u * R + k].re, r0, r1);
+                up(v[u * R + k].im, m0, m1);
+                const int a0 = R >= 16 ? pb + k : S::pad(base + k);
+                const int a1 = R >= 16 ? pb + R + k : S::pad(base + R + k);
+                pre[a0] = r0;
+                pre[a1] = r1;
+                pim[a0] = m0;
+                pim[a1] = m1;
+            });
         }
     }
 }
@@ -193,31 +257,12 @@ struct PairPasses {
     static CUBF_DEV void run(CP (&v)[16], int q, const float4* __restrict__ tw, float* pre, float* pim,
                              GLoad gload, GStore gstore) {
         using S = PairShape<LOGN>;
-        auto sload = [&](int i) -> CP {
-            const int a = S::swz(i);
-            return CP{*reinterpret_cast<const f32x2::P*>(pre + a), *reinterpret_cast<const f32x2::P*>(pim + a)};
-        };
-        if constexpr (P == 0) pair_pass_load<LOGN, 0>(v, q, tw, gload);
-        else pair_pass_load<LOGN, P>(v, q, tw, sload);
+        pair_pass_load<LOGN, P>(v, q, tw, pre, pim, gload);
         if constexpr (P == S::NPASS - 1) {
-            pair_pass_store<LOGN, P>(v, q, gstore, [](int, int, CP) {});
+            pair_pass_store<LOGN, P>(v, q, pre, pim, gstore);
         } else {
             if constexpr (P > 0) __syncthreads();  // every read of this pass is done
-            auto store2 = [&](int i, CP x) {
-                const int a = S::swz(i);
-                *reinterpret_cast<f32x2::P*>(pre + a) = x.re;
-                *reinterpret_cast<f32x2::P*>(pim + a) = x.im;
-            };
-            auto split = [&](int i0, int i1, CP x) {
-                float r0, r1, m0, m1;
-                up(x.re, r0, r1);
-                up(x.im, m0, m1);
-                pre[S::swz(i0)] = r0;
-                pre[S::swz(i1)] = r1;
-                pim[S::swz(i0)] = m0;
-                pim[S::swz(i1)] = m1;
-            };
-            pair_pass_store<LOGN, P>(v, q, store2, split);
+            pair_pass_store<LOGN, P>(v, q, pre, pim, gstore);
             __syncthreads();
             PairPasses<LOGN, P + 1>::run(v, q, tw, pre, pim, gload, gstore);
         }

@@ -89,6 +89,7 @@ struct NttVariant {
     int log_n;     // transform length 2^log_n
     bool strided;  // top bits (strided columns) or low bits (contiguous chunks)
     bool inverse;
+    bool lazy;     // Harvey lazy reduction (every modulus < 2^62)
 };
 constexpr int kNttMinLog = 12;
 constexpr int kNttMaxLog = 20;
@@ -98,6 +99,6 @@ LaunchShape ntt_shape(const NttVariant& v);
 // One pass over all polynomials; polys is a DEVICE array of poly_count entries.
 cudaError_t launch_ntt_pass(const NttVariant& v, const std::uint64_t* in, std::uint64_t* out,
                             const NttPolyDesc* polys, std::size_t poly_count, const NttTables& tables,
-                            bool in_is_out, bool final_scale, cudaStream_t stream);
+                            bool in_is_out, bool final_pass, bool final_scale, cudaStream_t stream);
 
 }  // namespace cubf

@@ -35,6 +35,14 @@ CUBF_DEV u64 add_mod(u64 a, u64 b, u64 q) {
 }
 CUBF_DEV u64 sub_mod(u64 a, u64 b, u64 q) { return a >= b ? a - b : a + q - b; }
 
+// Lazy (Harvey) arithmetic for q < 2^62: Shoup's product without its final
+// correction lands in [0, 2q) for any 64-bit input, and butterflies keep
+// values in [0, 4q) (forward) or [0, 2q) (inverse) so most conditional
+// subtractions disappear; outputs are reduced to [0, q) once, when written.
+CUBF_DEV u64 mul_shoup_lazy(u64 a, u64 w, u64 wq, u64 q) { return a * w - __umul64hi(a, wq) * q; }
+CUBF_DEV u64 reduce_2q(u64 a, u64 q2) { return a >= q2 ? a - q2 : a; }
+CUBF_DEV u64 canonical_4q(u64 a, u64 q) { return reduce_2q(reduce_2q(a, 2 * q), q); }
+
 // Per-polynomial binding of an RNS plan: offsets into the caller's buffers and
 // the domain whose modulus and root tables it uses.
 struct PolyDesc {
@@ -81,8 +89,9 @@ struct NttGroups {
     static constexpr uint32_t reg(int g) { return lowmask(LOGE) << lo(g); }
 };
 
-template <int B_, int LOGE_, int COLS_, bool STRIDED_, bool INV_>
+template <int B_, int LOGE_, int COLS_, bool STRIDED_, bool INV_, bool LAZY_>
 struct NttShape {
+    static constexpr bool LAZY = LAZY_;
     static constexpr int B = B_;
     static constexpr int LOGE = LOGE_;
     static constexpr int E = 1 << LOGE;
@@ -129,7 +138,18 @@ CUBF_DEV void ntt_group(u64 (&v)[S::E], uint32_t tpart, u64 hi, int off, const u
                 for (int rl = 0; rl < (1 << j); ++rl) {
                     const int r0 = (rh << (j + 1)) | rl;
                     const int r1 = r0 | (1 << j);
-                    if constexpr (!S::INV) {
+                    if constexpr (!S::INV && S::LAZY) {
+                        // Cooley-Tukey, inputs and outputs in [0, 4q)
+                        const u64 a = reduce_2q(v[r0], 2 * q);
+                        const u64 t = mul_shoup_lazy(v[r1], w, wq, q);
+                        v[r0] = a + t;
+                        v[r1] = a - t + 2 * q;
+                    } else if constexpr (S::INV && S::LAZY) {
+                        // Gentleman-Sande, inputs and outputs in [0, 2q)
+                        const u64 a = v[r0], c = v[r1];
+                        v[r0] = reduce_2q(a + c, 2 * q);
+                        v[r1] = mul_shoup_lazy(a - c + 2 * q, w, wq, q);
+                    } else if constexpr (!S::INV) {
                         // Cooley-Tukey: (a + w b, a - w b)
                         const u64 t = mul_shoup(v[r1], w, wq, q);
                         const u64 a = v[r0];
@@ -181,20 +201,22 @@ constexpr int log_e_for(int b) { return b <= 6 ? 3 : (b <= 8 ? 4 : 5); }
 constexpr int cols_for(int b, bool strided) {
     return strided ? 16 : ((256 >> (b - log_e_for(b))) > 0 ? (256 >> (b - log_e_for(b))) : 1);
 }
-template <int L, bool STRIDED, bool INV>
+template <int L, bool STRIDED, bool INV, bool LAZY>
 using PassShape = NttShape<STRIDED ? strided_bits(L) : contiguous_bits(L),
                            log_e_for(STRIDED ? strided_bits(L) : contiguous_bits(L)),
-                           cols_for(STRIDED ? strided_bits(L) : contiguous_bits(L), STRIDED), STRIDED, INV>;
+                           cols_for(STRIDED ? strided_bits(L) : contiguous_bits(L), STRIDED), STRIDED, INV, LAZY>;
 
 // One tile pass over every polynomial of a 2^L transform.  Forward runs the
 // strided pass (stages 0..B1-1) then the contiguous pass; inverse runs them in
 // the opposite order.  `in_is_out` makes the pass read the output buffer (the
-// second pass is in place); the final inverse pass scales by N^-1.
-template <int L, bool STRIDED, bool INV>
-__global__ void __launch_bounds__(PassShape<L, STRIDED, INV>::TPB)
+// second pass is in place); `final_pass` marks the pass that writes the
+// result (lazy variants reduce to [0, q) there), and with `final_scale` the
+// final inverse pass scales by N^-1.  LAZY requires every modulus < 2^62.
+template <int L, bool STRIDED, bool INV, bool LAZY>
+__global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB)
     ntt_pass_kernel(const u64* in, u64* out, const PolyDesc* __restrict__ polys, DomainTables tab, int in_is_out,
-                    int final_scale) {
-    using S = PassShape<L, STRIDED, INV>;
+                    int final_pass, int final_scale) {
+    using S = PassShape<L, STRIDED, INV, LAZY>;
     using Gs = typename S::Gs;
     constexpr int B = S::B;
     constexpr int COLS = S::COLS;
@@ -248,6 +270,10 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV>::TPB)
         const u64 ni = tab.n_inv[pd.domain], niq = tab.n_inv_q[pd.domain];
 #pragma unroll
         for (int r = 0; r < S::E; ++r) td[static_cast<size_t>(OF.v[r]) << SHIFT] = mul_shoup(v[r], ni, niq, q);
+    } else if (LAZY && final_pass) {
+#pragma unroll
+        for (int r = 0; r < S::E; ++r)
+            td[static_cast<size_t>(OF.v[r]) << SHIFT] = INV ? reduce_2q(v[r], q) : canonical_4q(v[r], q);
     } else {
 #pragma unroll
         for (int r = 0; r < S::E; ++r) td[static_cast<size_t>(OF.v[r]) << SHIFT] = v[r];

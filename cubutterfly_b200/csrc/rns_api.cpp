@@ -232,6 +232,7 @@ struct cubutterflyRnsPlanOpaque {
     bool prepared = false;
     bool in_place = false;
     bool needs_scratch = false;
+    bool lazy = false;  // every modulus < 2^62: Harvey lazy butterflies
     std::size_t scratch_bytes = 0;
     DeviceBuffer roots, quots, moduli, n_inv, n_inv_q, polys, polys_scratch, scratch;
     cubf::NttTables tables{};
@@ -254,7 +255,7 @@ struct cubutterflyRnsPlanOpaque {
                 {"strided_columns", s1.units_per_cta},
                 {"contiguous_tiles", s2.units_per_cta},
                 {"values_per_thread", s1.elems_per_thread},
-                {"arithmetic", "shoup"},
+                {"arithmetic", lazy ? "shoup-lazy" : "shoup"},
                 {"order", config.inverse ? "contiguous_then_strided" : "strided_then_contiguous"}};
     }
 
@@ -271,9 +272,11 @@ struct cubutterflyRnsPlanOpaque {
         const std::size_t n = std::size_t{1} << l;
         const std::size_t dn = c.domains.size();
         std::vector<u64> r(dn * n), rq(dn * n), m(dn), ni(dn), niq(dn);
+        lazy = true;
         for (std::size_t d = 0; d < dn; ++d) {
             const u64 q = c.domains[d].modulus;
             m[d] = q;
+            lazy = lazy && q < (u64{1} << 62);
             // Forward stage s, block i uses root table entry k = 2^s + i.
             //   negacyclic: psi^bitrev_L(k)
             //   cyclic:     omega^(bitrev_s(i) * 2^(L-1-s)), omega = root
@@ -327,20 +330,23 @@ struct cubutterflyRnsPlanOpaque {
         const int l = static_cast<int>(config.log_n);
         const std::size_t count = config.polynomials.size();
         const bool inv = config.inverse;
-        const cubf::NttVariant first{l, !inv, inv}, second{l, inv, inv};
+        const cubf::NttVariant first{l, !inv, inv, lazy}, second{l, inv, inv, lazy};
         if (needs_scratch) {
             u64* tmp = scratch.as<u64>();
             check(cubf::launch_ntt_pass(first, in, tmp, polys_scratch.as<cubf::NttPolyDesc>(), count, tables, false,
-                                        false, stream),
+                                        false, false, stream),
                   "pass 1 launch");
             // pass 2 reads scratch (its out_off) and writes the caller's output
-            check(cubf::launch_ntt_pass(second, tmp, out, polys_scratch_to_out(), count, tables, false, inv, stream),
+            check(cubf::launch_ntt_pass(second, tmp, out, polys_scratch_to_out(), count, tables, false, true, inv,
+                                        stream),
                   "pass 2 launch");
             return;
         }
-        check(cubf::launch_ntt_pass(first, in, out, polys.as<cubf::NttPolyDesc>(), count, tables, false, false, stream),
+        check(cubf::launch_ntt_pass(first, in, out, polys.as<cubf::NttPolyDesc>(), count, tables, false, false, false,
+                                    stream),
               "pass 1 launch");
-        check(cubf::launch_ntt_pass(second, out, out, polys.as<cubf::NttPolyDesc>(), count, tables, true, inv, stream),
+        check(cubf::launch_ntt_pass(second, out, out, polys.as<cubf::NttPolyDesc>(), count, tables, true, true, inv,
+                                    stream),
               "pass 2 launch");
     }
 

@@ -62,6 +62,34 @@ def test_sizes(oracle, cuda, log_n):
     assert np.array_equal(got.reshape(x.shape), oracle.rns_ntt(x, qs, roots))
 
 
+@pytest.mark.parametrize("inverse", [False, True])
+@pytest.mark.parametrize("bits", [[63, 63], [60, 63]])
+def test_wide_moduli_strict_path(oracle, cuda, inverse, bits):
+    """Moduli at or above 2^62 leave no headroom for lazy reduction (values up
+    to 4q): the plan falls back to fully reduced butterflies for every limb."""
+    log_n = 13
+    qs = [w.rns_primes(1, log_n, bits=b)[0] for b in bits]
+    roots = [w.primitive_root_of_two_power(log_n + 1, q) for q in qs]
+    n = 1 << log_n
+    cfg = {"schema_version": 1, "log_n": log_n, "inverse": inverse, "ring": "negacyclic",
+           "input_order": "bit_reversed" if inverse else "natural",
+           "output_order": "natural" if inverse else "bit_reversed",
+           "domains": [{"modulus": q, "root": r} for q, r in zip(qs, roots)],
+           "polynomials": [{"domain": i, "input_offset": i * n, "output_offset": i * n} for i in range(len(qs))]}
+    x = w.ntt_input(qs, log_n, seed=7)
+    got, info = run_rns(cfg, x.reshape(-1), x.size)
+    assert info["mapping"]["arithmetic"] == "shoup"
+    want = oracle.rns_ntt(x, qs, roots, inverse=inverse, input_bitrev=inverse, output_bitrev=not inverse)
+    assert np.array_equal(got.reshape(x.shape), want)
+
+
+def test_lazy_path_selected_for_60_bit_moduli(cuda):
+    cfg = w.rns_config(count=2, log_n=12)
+    x = w.ntt_input([d["modulus"] for d in cfg["domains"]], 12)
+    _, info = run_rns(cfg, x.reshape(-1), x.size)
+    assert info["mapping"]["arithmetic"] == "shoup-lazy"
+
+
 def reference_fixture_config(inverse):
     """The reference RNS test layout (tests/test_rns_ntt.cu:19, :122-139): two
     primes, roots primitive^3 / primitive^5, five polynomials with domains

@@ -224,9 +224,11 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
                 dst = ws;
             const bool last = i + 1 == np;
             const auto& ps = m.passes[i];
-            check_cuda(cubf::launch_fft_global_pass(ps.log_h, src, dst, p.req.log_n, ps.log_inner, d.batch, p.twiddles,
-                                                    outer, inverse && i == 0, inverse && last, last ? scale : 1.0f,
-                                                    stream),
+            // interleaved batches run as one array of N * batch values
+            const int lv = p.req.log_v;
+            check_cuda(cubf::launch_fft_global_pass(ps.log_h, src, dst, p.req.log_n + lv, ps.log_inner + lv,
+                                                    lv ? 1 : d.batch, p.twiddles, outer, inverse && i == 0,
+                                                    inverse && last, last ? scale : 1.0f, stream, lv),
                        "FFT pass launch");
             src = dst;
         }
@@ -320,6 +322,8 @@ cubf::PlanRequest make_request(const cubf::Descriptor& d) {
     cubf::PlanRequest r;
     r.d = d;
     r.log_n = static_cast<int>(cubf::log2_exact(d.extents[0]));
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT && cubf::interleaved_batches(d))
+        r.log_v = static_cast<int>(cubf::log2_exact(d.batch));
     switch (d.op) {
         case CUBUTTERFLY_OPERATOR_FWHT:
             r.bw_op = cubf::BwOp::Fwht;
@@ -686,8 +690,14 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
             throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
         }
         const std::size_t esz = cubf::storage_bytes(p->desc.storage);
-        p->input_bytes = p->desc.batch * p->desc.input_batch_stride * esz;
-        p->output_bytes = p->desc.batch * p->desc.output_batch_stride * esz;
+        // bytes spanned by a layout: its largest element offset + 1
+        auto span = [&](const std::vector<std::size_t>& ext, const std::vector<std::size_t>& str, std::size_t bs) {
+            std::size_t last = (p->desc.batch - 1) * bs;
+            for (std::size_t a = 0; a < ext.size(); ++a) last += (ext[a] - 1) * str[a];
+            return (last + 1) * esz;
+        };
+        p->input_bytes = span(cubf::input_extents(p->desc), p->desc.input_strides, p->desc.input_batch_stride);
+        p->output_bytes = span(cubf::output_extents(p->desc), p->desc.output_strides, p->desc.output_batch_stride);
         p->req = make_request(p->desc);
         p->hw = cubf::resolve_profile();
         check_cuda(cudaGetDevice(&p->device), "current device");

@@ -208,6 +208,13 @@ std::size_t storage_bytes(cubutterflyDataType_t t) {
 std::vector<std::size_t> input_extents(const Descriptor& d) { return side(d, true); }
 std::vector<std::size_t> output_extents(const Descriptor& d) { return side(d, false); }
 
+bool interleaved_batches(const Descriptor& d) {
+    return d.rank == 1 && d.batch >= 2 && (d.batch & (d.batch - 1)) == 0 && d.extents.size() == 1 &&
+           d.extents[0] >= 16 && d.extents[0] * d.batch >= 4096 && d.input_strides == std::vector<std::size_t>{d.batch} &&
+           d.output_strides == std::vector<std::size_t>{d.batch} && d.input_batch_stride == 1 &&
+           d.output_batch_stride == 1;
+}
+
 bool layout_nonoverlapping(const std::vector<std::size_t>& extents, const std::vector<std::size_t>& strides,
                            std::size_t batch, std::size_t batch_stride) {
     return prove_layout(extents, strides, batch, batch_stride) == Proof::Disjoint;
@@ -485,7 +492,10 @@ Json capabilities(const Descriptor& source) {
     const bool packed = d.rank == 1 && d.input_strides == std::vector<std::size_t>{1} &&
                         d.output_strides == std::vector<std::size_t>{1} && d.input_batch_stride == in[0] &&
                         d.output_batch_stride == out[0];
-    if (!packed) gap("layout-lowering", "strided or padded layouts are not built; use packed rank-one batches");
+    const bool interleaved = d.op == CUBUTTERFLY_OPERATOR_FFT && interleaved_batches(d);
+    if (!packed && !interleaved)
+        gap("layout-lowering", "strided or padded layouts are not built; use packed rank-one batches or, for FFT, "
+                               "batches interleaved element-wise (stride = batch, batch stride 1)");
     const bool natural_in = std::all_of(d.input_orders.begin(), d.input_orders.end(),
                                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; });
     const bool natural_out = std::all_of(d.output_orders.begin(), d.output_orders.end(),

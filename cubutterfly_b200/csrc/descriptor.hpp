@@ -80,6 +80,11 @@ Descriptor descriptor_from_json(const Json& j);
 Json capabilities(const Descriptor& d);
 std::vector<std::size_t> input_extents(const Descriptor& d);
 std::vector<std::size_t> output_extents(const Descriptor& d);
+// Rank-one batches interleaved element-wise: element n of transform b at
+// n * batch + b (stride = batch, batch stride 1), batch a power of two >= 2,
+// N >= 16 and N * batch >= 2^12 (a pass tile takes >= 16 columns).  The
+// layout of the columns of a row-major matrix.
+bool interleaved_batches(const Descriptor& d);
 bool layout_nonoverlapping(const std::vector<std::size_t>& extents, const std::vector<std::size_t>& strides,
                            std::size_t batch, std::size_t batch_stride);
 std::size_t storage_bytes(cubutterflyDataType_t t);

@@ -317,11 +317,17 @@ struct GlobalColumnPasses {
     }
 };
 
+// Interleaved batches (log_v > 0): 2^log_v transforms stored as vector
+// elements -- element n of transform l at n 2^log_v + l -- form one array of
+// 2^log_n = N 2^log_v values.  A pass over it is the same Stockham pass with
+// Ns scaled by 2^log_v (the caller passes ns_bits including log_v), except
+// that the outer twiddle depends on the transform index (j mod Ns) >> log_v
+// only and is a power of W_N (the outer tables hold W_N).
 template <int LOGR>
 __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
     fft_global_pass_kernel(const float2* src, float2* dst, int log_n, int ns_bits, size_t batch,
                            const float2* __restrict__ tw_r, int tw_log_stride, OuterTwiddles outer, int conj_in,
-                           int conj_out, float scale) {
+                           int conj_out, float scale, int log_v) {
     using G = GlobalPassShape<LOGR>;
     using S = typename G::S;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -337,24 +343,26 @@ __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
     float2* db = dst + bidx * n;
     const float in_sgn = conj_in ? -1.f : 1.f;
     const int tshift = log_n - ns_bits - LOGR;  // W_{Ns R}^m = W_N^(m << tshift)
+    const size_t tmask = (n >> log_v) - 1;      // exponents are taken mod N
     // 1. coalesced tile load (runs of C elements), outer twiddle applied.
     //    Thread t handles column c = t % C and rows r = t / C + k (TPB / C).
     {
         constexpr int RSTEP = G::TPB / G::C;
         const int c = threadIdx.x % G::C;
         const size_t j = j0 + c;
-        const size_t jm = j & (ns - 1);
+        const size_t jm = (j & (ns - 1)) >> log_v;
         const int r0 = threadIdx.x / G::C;
+        const bool twiddled = ns_bits > log_v;
         double2 w = make_double2(1.0, 0.0), step = make_double2(1.0, 0.0);
-        if (ns_bits > 0) {
-            w = outer_twiddle_d(outer, ((jm * static_cast<size_t>(r0)) << tshift) & (n - 1));
-            step = outer_twiddle_d(outer, ((jm * static_cast<size_t>(RSTEP)) << tshift) & (n - 1));
+        if (twiddled) {
+            w = outer_twiddle_d(outer, ((jm * static_cast<size_t>(r0)) << tshift) & tmask);
+            step = outer_twiddle_d(outer, ((jm * static_cast<size_t>(RSTEP)) << tshift) & tmask);
         }
 #pragma unroll 4
         for (int r = r0; r < G::R; r += RSTEP) {
             float2 x = __ldcs(sb + j + static_cast<size_t>(r) * cols);
             x.y *= in_sgn;
-            if (ns_bits > 0) {
+            if (twiddled) {
                 x = cmul(x, make_float2(static_cast<float>(w.x), static_cast<float>(w.y)));
                 w = cmul_d(w, step);
             }

@@ -43,10 +43,13 @@ struct FftOuterTables {
     int split;
 };
 LaunchShape fft_global_pass_shape(int log_r);
-// tw1024: float2 W_1024^k, k < 1024 (the in-CTA twiddles of every radix)
+// tw1024: float2 W_1024^k, k < 1024 (the in-CTA twiddles of every radix).
+// log_v > 0: 2^log_v interleaved transforms (element n of transform l at
+// n 2^log_v + l) treated as one array of 2^log_n values; ns_bits then
+// includes log_v and `outer` holds W for the transform length 2^(log_n-log_v).
 cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
                                    std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
-                                   bool conj_out, float scale, cudaStream_t stream);
+                                   bool conj_out, float scale, cudaStream_t stream, int log_v = 0);
 
 // ---- FWHT / zeta tile passes --------------------------------------------------
 enum class BwOp { Fwht = 0, ZetaSubset = 1, ZetaSuperset = 2 };

@@ -88,7 +88,7 @@ struct GlobalEntry {
     }
     static cudaError_t launch(const void* src, void* dst, int log_n, int ns_bits, std::size_t batch,
                               const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out,
-                              float scale, cudaStream_t stream) {
+                              float scale, cudaStream_t stream, int log_v) {
         auto kernel = fft::fft_global_pass_kernel<LOGR>;
         static KernelSetup setup;
         int grid_cap = 0;
@@ -102,12 +102,12 @@ struct GlobalEntry {
                               outer.split};
         kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
             static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits, batch,
-            static_cast<const float2*>(tw1024), 10 - LOGR, ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale);
+            static_cast<const float2*>(tw1024), 10 - LOGR, ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v);
         return cudaGetLastError();
     }
 };
 using GlobalLaunch = cudaError_t (*)(const void*, void*, int, int, std::size_t, const void*, const FftOuterTables&,
-                                     bool, bool, float, cudaStream_t);
+                                     bool, bool, float, cudaStream_t, int);
 using GlobalShape = LaunchShape (*)();
 template <int... L>
 struct GlobalTable {
@@ -125,10 +125,11 @@ LaunchShape fft_global_pass_shape(int log_r) {
 
 cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
                                    std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
-                                   bool conj_out, float scale, cudaStream_t stream) {
+                                   bool conj_out, float scale, cudaStream_t stream, int log_v) {
     if (log_r < kFftPassMinLog || log_r > kFftPassMaxLog) return cudaErrorInvalidValue;
+    if (log_v < 0 || log_v > log_n - log_r) return cudaErrorInvalidValue;
     return Global::launch_fns[log_r - kFftPassMinLog](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in,
-                                                      conj_out, scale, stream);
+                                                      conj_out, scale, stream, log_v);
 }
 
 std::vector<float> fft_local_twiddles(int log_n) {

@@ -194,6 +194,10 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
         p.log_inner = ns;
         p.shape = fft_global_pass_shape(bits);
         require(fits(p.shape, hw), "FFT pass tile does not fit the device");
+        // a CTA takes units_per_cta adjacent columns of the (N 2^log_v) / R
+        const std::size_t cols = std::size_t{1} << (r.log_n + r.log_v - bits);
+        if (cols % static_cast<std::size_t>(p.shape.units_per_cta) != 0)
+            throw Unsupported("FFT pass of " + std::to_string(bits) + " bits needs more columns than this transform has");
         // one CTA per SM at 1024 threads leaves the memory pipe less busy
         const double eff = p.shape.threads >= 1024 ? 0.6 : 0.85;
         m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, eff);
@@ -244,7 +248,9 @@ Json Mapping::to_json() const {
 std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw) {
     std::vector<Mapping> out;
     const Descriptor& d = r.d;
-    if (d.op == CUBUTTERFLY_OPERATOR_FFT && r.log_n > kFftLocalMaxLog) {
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT && (r.log_n > kFftLocalMaxLog || r.log_v > 0)) {
+        if (r.log_n < kFftPassMinLog)
+            throw Unsupported("interleaved FFT batches need at least 2^" + std::to_string(kFftPassMinLog) + " points");
         // Multi-pass global Stockham: for each cap on the radix bits of a
         // pass, ceil(L / cap) passes with balanced radices.
         for (int cap = kFftPassMaxLog; cap >= 7; --cap) {
@@ -254,8 +260,13 @@ std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProf
             bool dup = false;
             for (const auto& m : out)
                 if (m.passes.size() == parts.size()) dup = true;
-            if (!dup) out.push_back(fft_global_mapping(r, hw, parts));
+            if (dup) continue;
+            try {
+                out.push_back(fft_global_mapping(r, hw, parts));
+            } catch (const Unsupported&) {
+            }
         }
+        if (out.empty()) throw Unsupported("no global FFT pass partition fits this transform");
         std::stable_sort(out.begin(), out.end(),
                          [](const Mapping& a, const Mapping& b) { return a.predicted_us < b.predicted_us; });
         return out;
@@ -315,7 +326,7 @@ Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, 
     }
     require(!parts.empty(), "explicit mapping has no passes");
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
-        if (r.log_n > kFftLocalMaxLog) return fft_global_mapping(r, hw, parts);
+        if (r.log_n > kFftLocalMaxLog || r.log_v > 0) return fft_global_mapping(r, hw, parts);
         require(parts.size() == 1 && parts[0] == r.log_n, "FFT up to 2^13 is one local pass of log N bits");
         return enumerate_mappings(r, hw).front();
     }

@@ -65,6 +65,9 @@ struct Mapping {
 struct PlanRequest {
     Descriptor d;  // normalised
     int log_n = 0;
+    // FFT batches interleaved element-wise (element stride = batch, batch
+    // stride 1): log2 of the batch, else 0.  Always planned as global passes.
+    int log_v = 0;
     BwType bw_type = BwType::F32;
     BwOp bw_op = BwOp::Fwht;
 };

@@ -172,6 +172,26 @@ def test_planner_single_pass_fwht_and_multipass_fft(lib):
     assert ms[0]["workspace_bytes"] == 2 * (8 << 21)  # odd pass count in place: two halves
 
 
+def test_interleaved_fft_batches_are_planned_as_global_passes(lib):
+    """FFT batches interleaved element-wise (stride = batch, batch stride 1) are
+    eligible; they always run as global passes, and a plan spans N * batch values."""
+    t = cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=64, input_strides=[64], output_strides=[64],
+                     input_batch_stride=1, output_batch_stride=1)
+    assert capabilities(lib, t)["status"] == "eligible"
+    ms = rank(lib, t)
+    assert ms and all(m["family"] == "fft-stockham-global" for m in ms)
+    assert all(sum(p["log_h"] for p in m["passes"]) == 12 for m in ms)
+    small = cb.Transform(op=cb.Operator.FFT, extents=[8], batch=4, input_strides=[4], output_strides=[4],
+                         input_batch_stride=1, output_batch_stride=1)
+    assert capabilities(lib, small)["status"] == "missing-lowering"  # passes need >= 16 points
+    few = cb.Transform(op=cb.Operator.FFT, extents=[16], batch=64, input_strides=[64], output_strides=[64],
+                       input_batch_stride=1, output_batch_stride=1)
+    assert capabilities(lib, few)["status"] == "missing-lowering"  # and >= 2^12 values in all
+    odd = cb.Transform(op=cb.Operator.FFT, extents=[64], batch=6, input_strides=[6], output_strides=[6],
+                       input_batch_stride=1, output_batch_stride=1)
+    assert "layout-lowering" in [g["code"] for g in capabilities(lib, odd)["gaps"]]
+
+
 def test_planner_respects_hardware_profile(lib):
     """A device with little shared memory cannot take the 14-bit contiguous zeta tile."""
     t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << 24], batch=16)

@@ -108,3 +108,33 @@ def test_fft_2_24_spot_bins_and_round_trip(lib, oracle, cuda):
     assert rel_l2(f[0][bins], ref) <= TOL, name
     back, _ = run(lib, fft_transform(n, 1, inverse=True, normalize=True), f, cuda)
     assert rel_l2(back, x) <= TOL
+
+
+def interleaved_transform(n, batch, inverse=False, normalize=True, in_place=False):
+    """Batches interleaved element-wise: element k of transform b at k * batch + b
+    (the columns of a row-major n x batch matrix), through cubutterflySetStrides."""
+    return cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=[n], batch=batch,
+                        inverse=inverse, normalize_inverse=normalize, in_place=in_place, input_strides=[batch],
+                        output_strides=[batch], input_batch_stride=1, output_batch_stride=1)
+
+
+@pytest.mark.parametrize("n, batch", [(16, 256), (256, 32), (4096, 64), (1 << 15, 16), (1 << 14, 4), (8192, 512), (1024, 4)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_fft_interleaved_batches(lib, oracle, cuda, n, batch, inverse):
+    from gpu_util import run
+
+    x = w.fft_input(n, batch, seed=n + batch)
+    cols = np.ascontiguousarray(x.T)  # (n, batch): transform b is column b
+    got, name = run(lib, interleaved_transform(n, batch, inverse=inverse), cols, cuda)
+    assert name.startswith("fft-stockham-global"), name
+    want = oracle.fft_c32(x, inverse=inverse, normalize=True)
+    assert rel_l2(np.ascontiguousarray(got.reshape(n, batch).T), want) <= TOL, name
+
+
+def test_fft_interleaved_in_place(lib, oracle, cuda):
+    from gpu_util import run
+
+    n, batch = 1 << 13, 128
+    x = w.fft_input(n, batch, seed=5)
+    got, _ = run(lib, interleaved_transform(n, batch, in_place=True), np.ascontiguousarray(x.T), cuda)
+    assert rel_l2(np.ascontiguousarray(got.reshape(n, batch).T), oracle.fft_c32(x)) <= TOL

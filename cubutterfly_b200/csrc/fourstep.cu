@@ -1,11 +1,13 @@
-// fourstep.cu -- twiddle step of the four-step (distributed) FFT.
+// fourstep.cu -- twiddle and transpose steps of the four-step (distributed) FFT.
 //
 // A length-N = N1 * N2 FFT split over ranks runs column FFTs of length N1,
-// multiplies element (n2, k1) by W_N^(n2 k1), exchanges, and runs row FFTs of
-// length N2.  This kernel applies the middle multiply to a rank's block of
-// rows: data[j][k] *= W_N^((row_offset + j) k), the exponent reduced mod N in
-// integers and the twiddle formed in fp64 from two exact tables (W_N^e =
-// hi[e >> s] * lo[e & (2^s - 1)]) before one rounding to fp32.
+// multiplies element (k1, n2) by W_N^(k1 n2), exchanges, and runs row FFTs of
+// length N2.  The twiddle kernel applies the middle multiply to a rank's block:
+// data[i][j] *= W_N^((row_offset + i) (col_offset + j)), the exponent reduced
+// mod N in integers and the twiddle formed in fp64 from two exact tables
+// (W_N^e = hi[e >> s] * lo[e & (2^s - 1)]) before one rounding to fp32.  The
+// transpose kernel moves 32 x 32 tiles of complex64 through shared memory
+// (coalesced 256-byte row segments on both sides) for the final reordering.
 #include <cubutterfly/cubutterfly_b200.h>
 
 #include "fft.cuh"
@@ -27,19 +29,19 @@ void set_last_error(const std::string& message);
 
 namespace {
 
-__global__ void fourstep_twiddle_kernel(float4* data, size_t pairs, int log_cols, size_t row_offset, int log_n,
-                                        cubf::fft::OuterTwiddles tw, int conj) {
+// Generic path: two table-formed twiddles per float4 (any cols >= 2).
+__global__ void fourstep_twiddle_kernel(float4* data, size_t pairs, int log_cols, size_t row_offset,
+                                        size_t col_offset, int log_n, cubf::fft::OuterTwiddles tw, int conj) {
     const size_t nmask = (size_t{1} << log_n) - 1;
     const size_t cmask = (size_t{1} << log_cols) - 1;
     for (size_t p = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; p < pairs;
          p += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const size_t idx = 2 * p;  // two complex values per float4
-        const size_t j = idx >> log_cols;
-        const size_t k = idx & cmask;
-        const size_t row = row_offset + j;
+        const size_t row = row_offset + (idx >> log_cols);
+        const size_t col = col_offset + (idx & cmask);
         float4 v = __ldcs(data + p);
-        float2 w0 = cubf::fft::outer_twiddle(tw, (row * k) & nmask);
-        float2 w1 = cubf::fft::outer_twiddle(tw, (row * (k + 1)) & nmask);
+        float2 w0 = cubf::fft::outer_twiddle(tw, (row * col) & nmask);
+        float2 w1 = cubf::fft::outer_twiddle(tw, (row * (col + 1)) & nmask);
         if (conj) {
             w0.y = -w0.y;
             w1.y = -w1.y;
@@ -47,6 +49,59 @@ __global__ void fourstep_twiddle_kernel(float4* data, size_t pairs, int log_cols
         const float2 a = cubf::fft::cmul(make_float2(v.x, v.y), w0);
         const float2 b = cubf::fft::cmul(make_float2(v.z, v.w), w1);
         __stcs(data + p, make_float4(a.x, a.y, b.x, b.y));
+    }
+}
+
+// Rows of at least 64 columns: a warp covers 64 consecutive columns (32
+// float4, one coalesced 512-byte access) of one row per step and walks kSteps
+// steps along the row; each thread's two twiddles start from the tables and
+// advance by W^(64 row) in fp64 (one complex multiply each per step).
+constexpr int kTwiddleSteps = 16;
+__global__ void fourstep_twiddle_rows_kernel(float4* data, int log_cols, size_t rows, size_t row_offset,
+                                             size_t col_offset, int log_n, cubf::fft::OuterTwiddles tw, int conj,
+                                             int steps) {
+    const size_t nmask = (size_t{1} << log_n) - 1;
+    const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    const size_t warps_per_row = (size_t{1} << (log_cols - 6)) / static_cast<size_t>(steps);
+    const size_t r = warp / warps_per_row;
+    if (r >= rows) return;
+    const size_t c0 = (warp % warps_per_row) * static_cast<size_t>(steps) * 64 + 2 * static_cast<size_t>(lane);
+    const size_t row = row_offset + r;
+    const size_t col = col_offset + c0;
+    double2 wa = cubf::fft::outer_twiddle_d(tw, (row * col) & nmask);
+    double2 wb = cubf::fft::outer_twiddle_d(tw, (row * (col + 1)) & nmask);
+    const double2 step = cubf::fft::outer_twiddle_d(tw, (row * 64) & nmask);
+    const double sgn = conj ? -1.0 : 1.0;
+    float4* p = data + ((r << log_cols) + c0) / 2;
+    for (int s = 0; s < steps; ++s) {
+        const float4 v = __ldcs(p + 32 * s);
+        const float2 a = cubf::fft::cmul(make_float2(v.x, v.y),
+                                         make_float2(static_cast<float>(wa.x), static_cast<float>(sgn * wa.y)));
+        const float2 b = cubf::fft::cmul(make_float2(v.z, v.w),
+                                         make_float2(static_cast<float>(wb.x), static_cast<float>(sgn * wb.y)));
+        __stcs(p + 32 * s, make_float4(a.x, a.y, b.x, b.y));
+        wa = cubf::fft::cmul_d(wa, step);
+        wb = cubf::fft::cmul_d(wb, step);
+    }
+}
+
+// out[b][c][r] = in[b][r][c]; 32 x 32 tiles, 32 x 8 threads, batch in z.
+__global__ void transpose_c64_kernel(const float2* __restrict__ in, float2* __restrict__ out, size_t rows,
+                                     size_t cols) {
+    __shared__ float2 tile[32][33];
+    const size_t base = static_cast<size_t>(blockIdx.z) * rows * cols;
+    const size_t r0 = static_cast<size_t>(blockIdx.y) * 32, c0 = static_cast<size_t>(blockIdx.x) * 32;
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        const size_t r = r0 + threadIdx.y + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[threadIdx.y + i][threadIdx.x] = __ldcs(in + base + r * cols + c);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        const size_t c = c0 + threadIdx.y + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) __stcs(out + base + c * rows + r, tile[threadIdx.x][threadIdx.y + i]);
     }
 }
 
@@ -103,8 +158,8 @@ const Tables& tables_for(int log_n) {
 }  // namespace
 
 extern "C" cubutterflyStatus_t cubutterflyB200FourStepTwiddle(void* data, size_t rows, size_t cols,
-                                                             size_t row_offset, size_t n, int inverse,
-                                                             cudaStream_t stream) {
+                                                             size_t row_offset, size_t col_offset, size_t n,
+                                                             int inverse, cudaStream_t stream) {
     try {
         cubf::set_last_error("");
         if (!data || rows == 0 || cols < 2 || (cols & (cols - 1)) || n == 0 || (n & (n - 1)))
@@ -116,16 +171,51 @@ extern "C" cubutterflyStatus_t cubutterflyB200FourStepTwiddle(void* data, size_t
         while ((std::size_t{1} << log_cols) < cols) ++log_cols;
         if (log_n > 40) throw std::invalid_argument("four-step twiddle length is limited to 2^40");
         const Tables& t = tables_for(log_n);
-        const std::size_t pairs = rows * cols / 2;
-        int dev = 0, sms = 0;
-        check(cudaGetDevice(&dev), "current device");
-        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device attribute");
-        const std::size_t want = (pairs + 255) / 256;
-        const unsigned grid = static_cast<unsigned>(want < static_cast<std::size_t>(sms) * 16 ? want : sms * 16);
-        fourstep_twiddle_kernel<<<grid, 256, 0, stream>>>(static_cast<float4*>(data), pairs, log_cols, row_offset,
-                                                           log_n, cubf::fft::OuterTwiddles{t.lo, t.hi, t.split},
-                                                           inverse ? 1 : 0);
+        const cubf::fft::OuterTwiddles ot{t.lo, t.hi, t.split};
+        if (log_cols >= 6) {
+            const std::size_t chunks = cols / 64;
+            const int steps = static_cast<int>(chunks < kTwiddleSteps ? chunks : kTwiddleSteps);
+            const std::size_t warps = rows * (chunks / static_cast<std::size_t>(steps));
+            const std::size_t blocks = (warps * 32 + 255) / 256;
+            if (blocks > 0x7fffffffULL) throw std::invalid_argument("four-step twiddle grid is too large");
+            fourstep_twiddle_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+                static_cast<float4*>(data), log_cols, rows, row_offset, col_offset, log_n, ot, inverse ? 1 : 0, steps);
+        } else {
+            const std::size_t pairs = rows * cols / 2;
+            int dev = 0, sms = 0;
+            check(cudaGetDevice(&dev), "current device");
+            check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device attribute");
+            const std::size_t want = (pairs + 255) / 256;
+            const unsigned grid =
+                static_cast<unsigned>(want < static_cast<std::size_t>(sms) * 16 ? want : sms * 16);
+            fourstep_twiddle_kernel<<<grid, 256, 0, stream>>>(static_cast<float4*>(data), pairs, log_cols, row_offset,
+                                                               col_offset, log_n, ot, inverse ? 1 : 0);
+        }
         check(cudaGetLastError(), "four-step twiddle launch");
+        return CUBUTTERFLY_STATUS_SUCCESS;
+    } catch (const std::invalid_argument& e) {
+        cubf::set_last_error(e.what());
+        return CUBUTTERFLY_STATUS_INVALID_VALUE;
+    } catch (const std::exception& e) {
+        cubf::set_last_error(e.what());
+        return CUBUTTERFLY_STATUS_CUDA_ERROR;
+    }
+}
+
+extern "C" cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input, void* output, size_t batch, size_t rows,
+                                                          size_t cols, cudaStream_t stream) {
+    try {
+        cubf::set_last_error("");
+        if (!input || !output || batch == 0 || rows == 0 || cols == 0)
+            throw std::invalid_argument("transpose needs non-null buffers and nonzero batch, rows and cols");
+        if (input == output) throw std::invalid_argument("transpose must be out of place");
+        const std::size_t ty = (rows + 31) / 32, tx = (cols + 31) / 32;
+        if (tx > 0x7fffffffULL || ty > 65535 || batch > 65535)
+            throw std::invalid_argument("transpose grid exceeds the launch limits (rows/32 and batch <= 65535)");
+        transpose_c64_kernel<<<dim3(static_cast<unsigned>(tx), static_cast<unsigned>(ty), static_cast<unsigned>(batch)),
+                               dim3(32, 8), 0, stream>>>(static_cast<const float2*>(input), static_cast<float2*>(output),
+                                                         rows, cols);
+        check(cudaGetLastError(), "transpose launch");
         return CUBUTTERFLY_STATUS_SUCCESS;
     } catch (const std::invalid_argument& e) {
         cubf::set_last_error(e.what());

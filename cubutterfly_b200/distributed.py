@@ -8,15 +8,20 @@ in CPU tests).
   its own plan and no collective touches the data path (`shard_range`).
 
 * Four-step FFT: one complex fp32 transform of length N = N1 * N2 held as a
-  contiguous 1/P shard per rank (rank r owns x[r N/P : (r+1) N/P]):
-    1. all-to-all so each rank holds N2/P whole columns (length N1);
-    2. column FFTs of length N1 (this library's plan) and the twiddle
-       W_N^(n2 k1) (cubutterflyB200FourStepTwiddle, fp64-accurate);
-    3. all-to-all so each rank holds N1/P whole rows (length N2);
-    4. row FFTs of length N2;
-    5. all-to-all back to natural order: rank r owns X[r N/P : (r+1) N/P].
-  The exchanges are NCCL all-to-alls over NVLink; packing and unpacking are
-  strided tensor copies.  Inverse transforms use inverse plans and conjugate
+  contiguous 1/P shard per rank (rank r owns x[r N/P : (r+1) N/P]), viewed
+  as the row-major matrix A[n1][n2] (n = n1 N2 + n2), X[k1 + N1 k2] =
+  sum_n2 W_N2^(n2 k2) W_N^(n2 k1) sum_n1 A[n1][n2] W_N1^(n1 k1):
+    1. block permute + all-to-all: rank r receives its N2/P columns as an
+       N1 x N2/P row-major block (no unpacking);
+    2. column FFTs of length N1 run on that block directly, as interleaved
+       batches (element stride N2/P), then the twiddle W_N^(k1 n2);
+    3. all-to-all of k1 row blocks (sent as they lie) and a block permute:
+       rank r holds N1/P whole rows of length N2;
+    4. row FFTs of length N2 (contiguous batches);
+    5. block permute + all-to-all back to natural order and one tiled
+       transpose: rank r owns X[r N/P : (r+1) N/P].
+  The exchanges are NCCL all-to-alls over NVLink (received tiles land in
+  local HBM before use).  Inverse transforms use inverse plans and conjugate
   twiddles, normalised by 1/N1 * 1/N2 when requested.
 """
 from __future__ import annotations
@@ -62,12 +67,16 @@ class FourStepShape:
 
 
 class _LibraryFft:
-    """Batched contiguous FFTs through the C ABI (plan + caller workspace)."""
+    """Batched FFTs through the C ABI (plan + caller workspace): contiguous
+    rows, or batches interleaved element-wise (the columns of a row-major
+    n x batch matrix)."""
 
-    def __init__(self, lib, n, batch, inverse, normalize, device):
+    def __init__(self, lib, n, batch, inverse, normalize, device, interleaved=False):
         stream = torch.cuda.current_stream(device).cuda_stream
+        layout = dict(input_strides=[batch], output_strides=[batch], input_batch_stride=1,
+                      output_batch_stride=1) if interleaved else {}
         self.plan = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=batch, inverse=inverse,
-                                              normalize_inverse=normalize), stream=stream)
+                                              normalize_inverse=normalize, **layout), stream=stream)
         size = self.plan.workspace_size()
         self.ws = torch.empty(max(size, 16), dtype=torch.uint8, device=device)
         if size:
@@ -83,13 +92,29 @@ class _LibraryFft:
 class _LibraryTwiddle:
     def __init__(self, lib):
         fn = lib._dll.cubutterflyB200FourStepTwiddle
-        fn.argtypes = [ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_int, ct.c_void_p]
+        fn.argtypes = [ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_int,
+                       ct.c_void_p]
         fn.restype = ct.c_int
         self.fn, self.lib = fn, lib
 
-    def __call__(self, data: torch.Tensor, rows: int, cols: int, row_offset: int, n: int, inverse: bool) -> None:
+    def __call__(self, data: torch.Tensor, rows: int, cols: int, row_offset: int, col_offset: int, n: int,
+                 inverse: bool) -> None:
         stream = torch.cuda.current_stream(data.device).cuda_stream
-        status = self.fn(data.data_ptr(), rows, cols, row_offset, n, int(inverse), stream)
+        status = self.fn(data.data_ptr(), rows, cols, row_offset, col_offset, n, int(inverse), stream)
+        if status:
+            raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
+
+
+class _LibraryTranspose:
+    def __init__(self, lib):
+        fn = lib._dll.cubutterflyB200TransposeC64
+        fn.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_void_p]
+        fn.restype = ct.c_int
+        self.fn, self.lib = fn, lib
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor, rows: int, cols: int) -> None:
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        status = self.fn(x.data_ptr(), out.data_ptr(), 1, rows, cols, stream)
         if status:
             raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
 
@@ -98,15 +123,15 @@ class FourStepFFT:
     """Distributed single-transform complex fp32 FFT (natural order in and out).
 
     `x` is this rank's contiguous shard as a float32 tensor of shape
-    (N / P, 2) (interleaved complex).  `local_fft(n, batch)` and `twiddle`
-    may be replaced (CPU tests inject reference implementations); by default
-    they are this library's GPU kernels.
+    (N / P, 2) (interleaved complex).  `local_fft(n, batch, interleaved)`,
+    `twiddle` and `transpose` may be replaced (CPU tests inject reference
+    implementations); by default they are this library's GPU kernels.
     """
 
     def __init__(self, n: int, group=None, inverse: bool = False, normalize: bool = True, lib=None,
                  device: Optional[torch.device] = None,
-                 local_fft: Optional[Callable[[int, int], Callable]] = None,
-                 twiddle: Optional[Callable] = None):
+                 local_fft: Optional[Callable[[int, int, bool], Callable]] = None,
+                 twiddle: Optional[Callable] = None, transpose: Optional[Callable] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -116,13 +141,15 @@ class FourStepFFT:
         if local_fft is None:
             lib = lib or cb.load()
             device = device or torch.device("cuda", torch.cuda.current_device())
-            self._cols = _LibraryFft(lib, s.n1, s.n2 // self.world, inverse, normalize, device)
+            self._cols = _LibraryFft(lib, s.n1, s.n2 // self.world, inverse, normalize, device, interleaved=True)
             self._rows = _LibraryFft(lib, s.n2, s.n1 // self.world, inverse, normalize, device)
             self._twiddle = _LibraryTwiddle(lib)
+            self._transpose = _LibraryTranspose(lib)
         else:
-            self._cols = local_fft(s.n1, s.n2 // self.world)
-            self._rows = local_fft(s.n2, s.n1 // self.world)
+            self._cols = local_fft(s.n1, s.n2 // self.world, True)
+            self._rows = local_fft(s.n2, s.n1 // self.world, False)
             self._twiddle = twiddle
+            self._transpose = transpose
 
     def _exchange(self, send: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
@@ -136,25 +163,27 @@ class FourStepFFT:
         if x.shape != (s.local, 2) or x.dtype != torch.float32:
             raise ValueError(f"expected a float32 shard of shape ({s.local}, 2)")
         n1p, n2p = s.n1 // p, s.n2 // p
-        # 1. rows n1 in [r N1/P, ...) -> columns n2 in [r N2/P, ...)
-        send = x.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous()
-        recv = self._exchange(send)                                  # [p][i][j] = A[p N1/P + i][r N2/P + j]
-        cols = recv.permute(2, 0, 1, 3).reshape(n2p, s.n1, 2).contiguous()
-        # 2. column FFTs (length N1) and the twiddle W_N^(n2 k1)
-        spec = torch.empty_like(cols)
-        self._cols(cols, spec)
-        self._twiddle(spec, n2p, s.n1, r * n2p, s.n, self.inverse)
-        # 3. columns -> rows k1 in [r N1/P, ...)
-        send = spec.view(n2p, p, n1p, 2).permute(1, 0, 2, 3).contiguous()
-        recv = self._exchange(send)                                  # [p][j][i] = C[p N2/P + j][r N1/P + i]
-        rows = recv.permute(2, 0, 1, 3).reshape(n1p, s.n2, 2).contiguous()
+        # 1. my rows n1, every rank's column block -> recv[q][i][j] = A[q N1/P + i][r N2/P + j],
+        #    i.e. the N1 x N2/P block of my columns, row-major
+        send = x.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous() if p > 1 else x.view(s.n1, n2p, 2)
+        block = self._exchange(send).view(s.n1, n2p, 2)
+        # 2. column FFTs (length N1) on the block's columns, then W_N^(k1 n2), n2 = r N2/P + j
+        spec = torch.empty_like(block)
+        self._cols(block, spec)
+        self._twiddle(spec, s.n1, n2p, 0, r * n2p, s.n, self.inverse)
+        # 3. k1 row blocks as they lie -> recv[q][i][j] = C[r N1/P + i][q N2/P + j]; rows of length N2
+        recv = self._exchange(spec.view(p, n1p, n2p, 2))
+        rows = recv.permute(1, 0, 2, 3).contiguous().view(n1p, s.n2, 2) if p > 1 else recv.view(n1p, s.n2, 2)
         # 4. row FFTs (length N2): E[i][k2] = X[(r N1/P + i) + N1 k2]
         out = torch.empty_like(rows)
         self._rows(rows, out)
-        # 5. back to natural order: rank r owns k2 in [r N2/P, ...), all k1
-        send = out.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous()
-        recv = self._exchange(send)                                  # [p][i][j] = X[(p N1/P + i) + N1 (r N2/P + j)]
-        return recv.permute(2, 0, 1, 3).reshape(s.local, 2).contiguous()
+        # 5. column blocks k2 in [q N2/P, ...) to rank q: recv[q][i][j] = X[(q N1/P + i) + N1 (r N2/P + j)],
+        #    an N1 x N2/P block whose transpose is my natural-order shard X[r N/P + j N1 + k1]
+        send = out.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous() if p > 1 else out.view(s.n1, n2p, 2)
+        back = self._exchange(send).view(s.n1, n2p, 2)
+        result = torch.empty((s.local, 2), dtype=torch.float32, device=x.device)
+        self._transpose(back, result, s.n1, n2p)
+        return result
 
     def close(self):
         for part in (self._cols, self._rows):

@@ -25,13 +25,21 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescri
 
 /* Twiddle step of the four-step FFT (no counterpart in the reference ABI;
  * used by cubutterfly_b200.distributed for one transform split across GPUs).
- * data: `rows` x `cols` complex fp32, row-major, 16-byte aligned;
- * multiplies element (j, k) by W_n^((row_offset + j) k), W_n = exp(-2 pi i/n)
- * (conjugated when `inverse`), with the twiddle formed in fp64 and rounded
- * once.  The first call per (device, n) uploads its tables. */
+ * data: `rows` x `cols` complex fp32, row-major, 16-byte aligned, cols a
+ * power of two >= 2; multiplies element (i, j) by
+ * W_n^((row_offset + i) (col_offset + j)), W_n = exp(-2 pi i/n) (conjugated
+ * when `inverse`), with the twiddle formed in fp64 and rounded once.  The
+ * first call per (device, n) uploads its tables. */
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepTwiddle(void* data, size_t rows, size_t cols,
-                                                                 size_t row_offset, size_t n, int inverse,
-                                                                 cudaStream_t stream);
+                                                                 size_t row_offset, size_t col_offset, size_t n,
+                                                                 int inverse, cudaStream_t stream);
+
+/* Batched complex fp32 transpose (no counterpart in the reference ABI; the
+ * four-step FFT's final reordering): output[b][c][r] = input[b][r][c] for
+ * `batch` row-major rows x cols matrices, out of place, asynchronous on
+ * `stream`; rows / 32 and batch at most 65535. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input, void* output, size_t batch,
+                                                              size_t rows, size_t cols, cudaStream_t stream);
 
 /* Allocation-free complex fp32 FFT (no counterpart in the reference ABI).
  * For callers that cannot allocate device memory -- fixed memory budgets or

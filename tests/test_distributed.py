@@ -43,22 +43,31 @@ def test_four_step_shape():
 
 
 def numpy_fft_factory(inverse, normalize):
-    def factory(n, batch):
+    """Stand-in for the library's batched FFTs: contiguous rows (batch, n), or
+    batches interleaved element-wise, i.e. the columns of an (n, batch) array."""
+    def factory(n, batch, interleaved):
+        axis = 0 if interleaved else -1
+        shape = (n, batch) if interleaved else (batch, n)
+
         def run(x, out):
-            z = x.numpy().astype(np.float64).view(np.complex128).reshape(batch, n)
-            f = np.fft.ifft(z, axis=-1) * (1 if normalize else n) if inverse else np.fft.fft(z, axis=-1)
-            out.copy_(torch.from_numpy(f.astype(np.complex64).view(np.float32).reshape(batch, n, 2)))
+            z = x.numpy().astype(np.float64).view(np.complex128).reshape(shape)
+            f = np.fft.ifft(z, axis=axis) * (1 if normalize else n) if inverse else np.fft.fft(z, axis=axis)
+            out.copy_(torch.from_numpy(f.astype(np.complex64).view(np.float32).reshape(*shape, 2)))
         return run
     return factory
 
 
-def numpy_twiddle(data, rows, cols, row_offset, n, inverse):
-    j = np.arange(row_offset, row_offset + rows, dtype=np.float64)[:, None]
-    k = np.arange(cols, dtype=np.float64)[None, :]
-    e = np.mod(j * k, n)
+def numpy_twiddle(data, rows, cols, row_offset, col_offset, n, inverse):
+    i = np.arange(row_offset, row_offset + rows, dtype=np.float64)[:, None]
+    j = np.arange(col_offset, col_offset + cols, dtype=np.float64)[None, :]
+    e = np.mod(i * j, n)
     w = np.exp((2j if inverse else -2j) * np.pi * e / n)
     z = data.numpy().astype(np.float64).view(np.complex128).reshape(rows, cols) * w
     data.copy_(torch.from_numpy(z.astype(np.complex64).view(np.float32).reshape(rows, cols, 2)))
+
+
+def numpy_transpose(x, out, rows, cols):
+    out.copy_(x.reshape(rows, cols, 2).permute(1, 0, 2).reshape(out.shape))
 
 
 def _gloo_worker(rank, world, port, log_n, inverse, q):
@@ -71,7 +80,8 @@ def _gloo_worker(rank, world, port, log_n, inverse, q):
         x = (rng.uniform(-1, 1, n) + 1j * rng.uniform(-1, 1, n)).astype(np.complex64)
         lo, cnt = shard_range(n, world, rank)
         shard = torch.from_numpy(x[lo:lo + cnt].view(np.float32).reshape(cnt, 2).copy())
-        fs = FourStepFFT(n, inverse=inverse, local_fft=numpy_fft_factory(inverse, True), twiddle=numpy_twiddle)
+        fs = FourStepFFT(n, inverse=inverse, local_fft=numpy_fft_factory(inverse, True), twiddle=numpy_twiddle,
+                         transpose=numpy_transpose)
         got = fs(shard).numpy().view(np.complex64).reshape(-1)
         want = (np.fft.ifft(x.astype(np.complex128)) if inverse else np.fft.fft(x.astype(np.complex128)))[lo:lo + cnt]
         q.put((rank, float(np.linalg.norm(got - want) / np.linalg.norm(want))))
@@ -153,3 +163,45 @@ def test_four_step_two_gpus_nccl():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert all(err <= 2e-6 for err in results.values()), results
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows, cols, row_offset, col_offset, inverse", [
+    (64, 4096, 0, 8192, False),     # row path (>= 64 columns), 16 steps per warp
+    (32, 128, 7, 256, True),        # row path, 2 steps per warp
+    (16, 32, 3, 5, False),          # generic path (< 64 columns)
+])
+def test_four_step_twiddle_kernel(cuda, rows, cols, row_offset, col_offset, inverse):
+    """cubutterflyB200FourStepTwiddle: data[i][j] *= W_n^((row_offset + i) (col_offset + j))."""
+    from cubutterfly_b200 import load
+    from cubutterfly_b200.distributed import _LibraryTwiddle
+
+    n = 1 << 20
+    rng = np.random.default_rng(rows + cols)
+    x = (rng.uniform(-1, 1, (rows, cols)) + 1j * rng.uniform(-1, 1, (rows, cols))).astype(np.complex64)
+    d = torch.from_numpy(x.view(np.float32).reshape(rows, cols, 2).copy()).to(cuda)
+    _LibraryTwiddle(load())(d, rows, cols, row_offset, col_offset, n, inverse)
+    torch.cuda.synchronize()
+    i = np.arange(row_offset, row_offset + rows, dtype=np.int64)[:, None]
+    j = np.arange(col_offset, col_offset + cols, dtype=np.int64)[None, :]
+    w = np.exp((2j if inverse else -2j) * np.pi * ((i * j) % n) / n)
+    want = x.astype(np.complex128) * w
+    got = d.cpu().numpy().view(np.complex64).reshape(rows, cols)
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-7
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch, rows, cols", [(1, 2048, 1024), (3, 40, 72)])
+def test_transpose_kernel(cuda, batch, rows, cols):
+    from cubutterfly_b200 import load
+
+    lib = load()
+    fn = lib._dll.cubutterflyB200TransposeC64
+    import ctypes as ct
+    fn.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_void_p]
+    fn.restype = ct.c_int
+    x = torch.randn(batch, rows, cols, 2, device=cuda)
+    y = torch.empty(batch, cols, rows, 2, device=cuda)
+    assert fn(x.data_ptr(), y.data_ptr(), batch, rows, cols, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y, x.permute(0, 2, 1, 3))

@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <cstdint>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -102,6 +103,23 @@ __global__ void transpose_c64_kernel(const float2* __restrict__ in, float2* __re
     for (int i = 0; i < 32; i += 8) {
         const size_t c = c0 + threadIdx.y + i, r = r0 + threadIdx.x;
         if (r < rows && c < cols) __stcs(out + base + c * rows + r, tile[threadIdx.x][threadIdx.y + i]);
+    }
+}
+
+// out[b][a][c] = in[a][b][c] for (A, B, C) blocks of complex64, C a
+// multiple of 2 (16-byte moves).  When in_self / out_self are set, source
+// block a == self is read from in_self ([B][C]) and destination block
+// b == self is written to out_self ([A][C]) instead -- a rank's own block of
+// an all-to-all never has to pass through the exchange buffers.
+__global__ void permute_blocks_c64_kernel(const float4* __restrict__ in, const float4* __restrict__ in_self,
+                                          float4* __restrict__ out, float4* __restrict__ out_self, size_t self,
+                                          size_t A, size_t B, size_t c4) {
+    const size_t runs = A * B;
+    for (size_t run = blockIdx.x; run < runs; run += gridDim.x) {
+        const size_t a = run / B, b = run % B;
+        const float4* src = (in_self && a == self) ? in_self + b * c4 : in + run * c4;
+        float4* dst = (out_self && b == self) ? out_self + a * c4 : out + (b * A + a) * c4;
+        for (size_t i = threadIdx.x; i < c4; i += blockDim.x) __stcs(dst + i, __ldcs(src + i));
     }
 }
 
@@ -216,6 +234,36 @@ extern "C" cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input, vo
                                dim3(32, 8), 0, stream>>>(static_cast<const float2*>(input), static_cast<float2*>(output),
                                                          rows, cols);
         check(cudaGetLastError(), "transpose launch");
+        return CUBUTTERFLY_STATUS_SUCCESS;
+    } catch (const std::invalid_argument& e) {
+        cubf::set_last_error(e.what());
+        return CUBUTTERFLY_STATUS_INVALID_VALUE;
+    } catch (const std::exception& e) {
+        cubf::set_last_error(e.what());
+        return CUBUTTERFLY_STATUS_CUDA_ERROR;
+    }
+}
+
+extern "C" cubutterflyStatus_t cubutterflyB200PermuteBlocksC64(const void* input, const void* input_self,
+                                                              void* output, void* output_self, size_t self,
+                                                              size_t a, size_t b, size_t c, cudaStream_t stream) {
+    try {
+        cubf::set_last_error("");
+        if (!input || !output || a == 0 || b == 0 || c == 0 || c % 2)
+            throw std::invalid_argument("block permute needs non-null buffers, nonzero A and B and an even C");
+        for (const void* ptr : {input, input_self, static_cast<const void*>(output), static_cast<const void*>(output_self)})
+            if (reinterpret_cast<std::uintptr_t>(ptr) % 16)
+                throw std::invalid_argument("block permute buffers must be 16-byte aligned");
+        if (input == output) throw std::invalid_argument("block permute must be out of place");
+        int dev = 0, sms = 0;
+        check(cudaGetDevice(&dev), "current device");
+        check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "device attribute");
+        const std::size_t runs = a * b;
+        const unsigned grid = static_cast<unsigned>(runs < static_cast<std::size_t>(sms) * 8 ? runs : sms * 8);
+        permute_blocks_c64_kernel<<<grid, 256, 0, stream>>>(
+            static_cast<const float4*>(input), static_cast<const float4*>(input_self), static_cast<float4*>(output),
+            static_cast<float4*>(output_self), self, a, b, c / 2);
+        check(cudaGetLastError(), "block permute launch");
         return CUBUTTERFLY_STATUS_SUCCESS;
     } catch (const std::invalid_argument& e) {
         cubf::set_last_error(e.what());

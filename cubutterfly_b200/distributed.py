@@ -11,17 +11,19 @@ in CPU tests).
   contiguous 1/P shard per rank (rank r owns x[r N/P : (r+1) N/P]), viewed
   as the row-major matrix A[n1][n2] (n = n1 N2 + n2), X[k1 + N1 k2] =
   sum_n2 W_N2^(n2 k2) W_N^(n2 k1) sum_n1 A[n1][n2] W_N1^(n1 k1):
-    1. block permute + all-to-all: rank r receives its N2/P columns as an
+    1. block permute + exchange: rank r receives its N2/P columns as an
        N1 x N2/P row-major block (no unpacking);
     2. column FFTs of length N1 run on that block directly, as interleaved
        batches (element stride N2/P), then the twiddle W_N^(k1 n2);
-    3. all-to-all of k1 row blocks (sent as they lie) and a block permute:
+    3. exchange of k1 row blocks (sent as they lie) and a block permute:
        rank r holds N1/P whole rows of length N2;
     4. row FFTs of length N2 (contiguous batches);
-    5. block permute + all-to-all back to natural order and one tiled
+    5. block permute + exchange back to natural order and one tiled
        transpose: rank r owns X[r N/P : (r+1) N/P].
-  The exchanges are NCCL all-to-alls over NVLink (received tiles land in
-  local HBM before use).  Inverse transforms use inverse plans and conjugate
+  Each exchange is an all-to-all of P blocks: the P - 1 remote blocks move
+  as grouped NCCL send/recv over NVLink (received blocks land in local HBM
+  before use); a rank's own block never enters the exchange -- the block
+  permutes read it from, or write it to, its final place.  Inverse transforms use inverse plans and conjugate
   twiddles, normalised by 1/N1 * 1/N2 when requested.
 """
 from __future__ import annotations
@@ -105,6 +107,25 @@ class _LibraryTwiddle:
             raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
 
 
+class _LibraryPermute:
+    """out[b][a][:] = in[a][b][:] over A x B blocks of C complex values; block
+    a == self may come from `in_self`, block b == self may go to `out_self`."""
+
+    def __init__(self, lib):
+        fn = lib._dll.cubutterflyB200PermuteBlocksC64
+        fn.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t,
+                       ct.c_size_t, ct.c_void_p]
+        fn.restype = ct.c_int
+        self.fn, self.lib = fn, lib
+
+    def __call__(self, x, out, a, b, c, self_index=0, in_self=None, out_self=None):
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        status = self.fn(x.data_ptr(), ptr(in_self), out.data_ptr(), ptr(out_self), self_index, a, b, c, stream)
+        if status:
+            raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
+
+
 class _LibraryTranspose:
     def __init__(self, lib):
         fn = lib._dll.cubutterflyB200TransposeC64
@@ -124,14 +145,16 @@ class FourStepFFT:
 
     `x` is this rank's contiguous shard as a float32 tensor of shape
     (N / P, 2) (interleaved complex).  `local_fft(n, batch, interleaved)`,
-    `twiddle` and `transpose` may be replaced (CPU tests inject reference
-    implementations); by default they are this library's GPU kernels.
+    `twiddle`, `transpose` and `permute` may be replaced (CPU tests inject
+    reference implementations); by default they are this library's GPU
+    kernels.
     """
 
     def __init__(self, n: int, group=None, inverse: bool = False, normalize: bool = True, lib=None,
                  device: Optional[torch.device] = None,
                  local_fft: Optional[Callable[[int, int, bool], Callable]] = None,
-                 twiddle: Optional[Callable] = None, transpose: Optional[Callable] = None):
+                 twiddle: Optional[Callable] = None, transpose: Optional[Callable] = None,
+                 permute: Optional[Callable] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -145,42 +168,77 @@ class FourStepFFT:
             self._rows = _LibraryFft(lib, s.n2, s.n1 // self.world, inverse, normalize, device)
             self._twiddle = _LibraryTwiddle(lib)
             self._transpose = _LibraryTranspose(lib)
+            self._permute = _LibraryPermute(lib)
         else:
             self._cols = local_fft(s.n1, s.n2 // self.world, True)
             self._rows = local_fft(s.n2, s.n1 // self.world, False)
             self._twiddle = twiddle
             self._transpose = transpose
+            self._permute = permute
+        self._bufs = None
 
-    def _exchange(self, send: torch.Tensor) -> torch.Tensor:
-        if self.world == 1:
-            return send
-        recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=self.group)
-        return recv
+    def _exchange(self, send: torch.Tensor, recv: torch.Tensor) -> None:
+        """Block q of `send` goes to rank q, block q of `recv` comes from rank q,
+        for every q != this rank (grouped point-to-point; own blocks stay put)."""
+        ops = []
+        for q in range(self.world):
+            if q == self.rank:
+                continue
+            peer = q if self.group is None else dist.get_global_rank(self.group, q)
+            ops.append(dist.P2POp(dist.isend, send[q], peer, group=self.group))
+            ops.append(dist.P2POp(dist.irecv, recv[q], peer, group=self.group))
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+
+    def _buffers(self, device):
+        """Three shard-sized work buffers, allocated once and reused by every
+        call (allocating gigabyte temporaries per call lets the caching
+        allocator stall a step to return and re-reserve memory)."""
+        if self._bufs is None or self._bufs[0].device != device:
+            shape = (self.shape.local, 2)
+            self._bufs = [torch.empty(shape, dtype=torch.float32, device=device) for _ in range(3)]
+        return self._bufs
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         s, p, r = self.shape, self.world, self.rank
         if x.shape != (s.local, 2) or x.dtype != torch.float32:
             raise ValueError(f"expected a float32 shard of shape ({s.local}, 2)")
         n1p, n2p = s.n1 // p, s.n2 // p
-        # 1. my rows n1, every rank's column block -> recv[q][i][j] = A[q N1/P + i][r N2/P + j],
-        #    i.e. the N1 x N2/P block of my columns, row-major
-        send = x.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous() if p > 1 else x.view(s.n1, n2p, 2)
-        block = self._exchange(send).view(s.n1, n2p, 2)
+        buf_a, buf_b, buf_c = self._buffers(x.device)
+        # 1. my rows n1, every rank's column block: block[q][i][j] = A[q N1/P + i][r N2/P + j],
+        #    i.e. the N1 x N2/P block of my columns, row-major (my own block is permuted in place)
+        if p > 1:
+            send, block = buf_a.view(p, n1p, n2p, 2), buf_b.view(p, n1p, n2p, 2)
+            self._permute(x, send, n1p, p, n2p, r, out_self=block[r])
+            self._exchange(send, block)
+            block = block.view(s.n1, n2p, 2)
+        else:
+            block = x.view(s.n1, n2p, 2)
         # 2. column FFTs (length N1) on the block's columns, then W_N^(k1 n2), n2 = r N2/P + j
-        spec = torch.empty_like(block)
+        spec = buf_c.view(s.n1, n2p, 2)
         self._cols(block, spec)
         self._twiddle(spec, s.n1, n2p, 0, r * n2p, s.n, self.inverse)
-        # 3. k1 row blocks as they lie -> recv[q][i][j] = C[r N1/P + i][q N2/P + j]; rows of length N2
-        recv = self._exchange(spec.view(p, n1p, n2p, 2))
-        rows = recv.permute(1, 0, 2, 3).contiguous().view(n1p, s.n2, 2) if p > 1 else recv.view(n1p, s.n2, 2)
+        # 3. k1 row blocks as they lie: recv[q][i][j] = C[r N1/P + i][q N2/P + j], then rows of length N2
+        if p > 1:
+            blocks, recv = spec.view(p, n1p, n2p, 2), buf_a.view(p, n1p, n2p, 2)
+            self._exchange(blocks, recv)
+            rows = buf_b.view(n1p, p, n2p, 2)
+            self._permute(recv, rows, p, n1p, n2p, r, in_self=blocks[r])
+            rows = rows.view(n1p, s.n2, 2)
+            out = buf_c.view(n1p, s.n2, 2)
+        else:
+            rows, out = spec.view(n1p, s.n2, 2), buf_a.view(n1p, s.n2, 2)
         # 4. row FFTs (length N2): E[i][k2] = X[(r N1/P + i) + N1 k2]
-        out = torch.empty_like(rows)
         self._rows(rows, out)
-        # 5. column blocks k2 in [q N2/P, ...) to rank q: recv[q][i][j] = X[(q N1/P + i) + N1 (r N2/P + j)],
+        # 5. column blocks k2 in [q N2/P, ...) to rank q: back[q][i][j] = X[(q N1/P + i) + N1 (r N2/P + j)],
         #    an N1 x N2/P block whose transpose is my natural-order shard X[r N/P + j N1 + k1]
-        send = out.view(n1p, p, n2p, 2).permute(1, 0, 2, 3).contiguous() if p > 1 else out.view(s.n1, n2p, 2)
-        back = self._exchange(send).view(s.n1, n2p, 2)
+        if p > 1:
+            send, back = buf_a.view(p, n1p, n2p, 2), buf_b.view(p, n1p, n2p, 2)
+            self._permute(out, send, n1p, p, n2p, r, out_self=back[r])
+            self._exchange(send, back)
+            back = back.view(s.n1, n2p, 2)
+        else:
+            back = out.view(s.n1, n2p, 2)
         result = torch.empty((s.local, 2), dtype=torch.float32, device=x.device)
         self._transpose(back, result, s.n1, n2p)
         return result
@@ -189,3 +247,4 @@ class FourStepFFT:
         for part in (self._cols, self._rows):
             if hasattr(part, "close"):
                 part.close()
+        self._bufs = None

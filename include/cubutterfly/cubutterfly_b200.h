@@ -34,6 +34,17 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepTwiddle(void* data, si
                                                                  size_t row_offset, size_t col_offset, size_t n,
                                                                  int inverse, cudaStream_t stream);
 
+/* Block permute of complex fp32 data (no counterpart in the reference ABI;
+ * the four-step FFT's packing around its all-to-alls): output[b][a][:] =
+ * input[a][b][:] for A x B blocks of C values (C even, buffers 16-byte
+ * aligned, out of place).  If `input_self` is non-null, source block
+ * a == self is read from input_self ([B][C]) instead; if `output_self` is
+ * non-null, destination block b == self is written to output_self ([A][C]). */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PermuteBlocksC64(const void* input, const void* input_self,
+                                                                  void* output, void* output_self, size_t self,
+                                                                  size_t a, size_t b, size_t c,
+                                                                  cudaStream_t stream);
+
 /* Batched complex fp32 transpose (no counterpart in the reference ABI; the
  * four-step FFT's final reordering): output[b][c][r] = input[b][r][c] for
  * `batch` row-major rows x cols matrices, out of place, asynchronous on

@@ -70,6 +70,20 @@ def numpy_transpose(x, out, rows, cols):
     out.copy_(x.reshape(rows, cols, 2).permute(1, 0, 2).reshape(out.shape))
 
 
+def torch_permute(x, out, a, b, c, self_index=0, in_self=None, out_self=None):
+    """Stand-in for cubutterflyB200PermuteBlocksC64 (same block routing)."""
+    src = x.reshape(a, b, c, 2).clone()
+    if in_self is not None:
+        src[self_index] = in_self.reshape(b, c, 2)
+    res = src.permute(1, 0, 2, 3)
+    if out_self is not None:
+        out_self.copy_(res[self_index].reshape(out_self.shape))
+        keep = [q for q in range(b) if q != self_index]
+        out.reshape(b, a, c, 2)[keep] = res[keep]
+    else:
+        out.copy_(res.reshape(out.shape))
+
+
 def _gloo_worker(rank, world, port, log_n, inverse, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -81,7 +95,7 @@ def _gloo_worker(rank, world, port, log_n, inverse, q):
         lo, cnt = shard_range(n, world, rank)
         shard = torch.from_numpy(x[lo:lo + cnt].view(np.float32).reshape(cnt, 2).copy())
         fs = FourStepFFT(n, inverse=inverse, local_fft=numpy_fft_factory(inverse, True), twiddle=numpy_twiddle,
-                         transpose=numpy_transpose)
+                         transpose=numpy_transpose, permute=torch_permute)
         got = fs(shard).numpy().view(np.complex64).reshape(-1)
         want = (np.fft.ifft(x.astype(np.complex128)) if inverse else np.fft.fft(x.astype(np.complex128)))[lo:lo + cnt]
         q.put((rank, float(np.linalg.norm(got - want) / np.linalg.norm(want))))
@@ -205,3 +219,26 @@ def test_transpose_kernel(cuda, batch, rows, cols):
     assert fn(x.data_ptr(), y.data_ptr(), batch, rows, cols, torch.cuda.current_stream().cuda_stream) == 0
     torch.cuda.synchronize()
     assert torch.equal(y, x.permute(0, 2, 1, 3))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("route", ["plain", "out_self", "in_self"])
+def test_permute_blocks_kernel(cuda, route):
+    """cubutterflyB200PermuteBlocksC64 against the torch stand-in, own-block routing included."""
+    from cubutterfly_b200 import load
+    from cubutterfly_b200.distributed import _LibraryPermute
+
+    a, b, c, me = 6, 4, 34, 2
+    x = torch.randn(a, b, c, 2, device=cuda)
+    kw, want_kw = {}, {}
+    if route == "out_self":
+        kw["out_self"], want_kw["out_self"] = torch.zeros(a, c, 2, device=cuda), torch.zeros(a, c, 2, device=cuda)
+    if route == "in_self":
+        kw["in_self"] = want_kw["in_self"] = torch.randn(b, c, 2, device=cuda)
+    got, want = torch.zeros(b, a, c, 2, device=cuda), torch.zeros(b, a, c, 2, device=cuda)
+    _LibraryPermute(load())(x, got, a, b, c, me, **kw)
+    torch_permute(x, want, a, b, c, me, **want_kw)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    if route == "out_self":
+        assert torch.equal(kw["out_self"], want_kw["out_self"])

@@ -37,19 +37,25 @@ MIB = 1 << 20
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=4000)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default: 4000 for the FWHT workload and --only, 20 for fft4step / fftbatch)")
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-ops", action="store_true", help="skip the per-op table (FFT, NTT, zeta)")
     p.add_argument("--cpu-baseline", choices=["auto", "skip"], default="auto")
     p.add_argument("--only", choices=["fwht4096", "fwht128", "fft", "zeta", "ntt", "fft1g"],
                    help="run just this operator's launches (profiling driver; prints a short JSON line)")
-    p.add_argument("--workload", choices=["fwht", "fft4step"], default="fwht",
+    p.add_argument("--workload", choices=["fwht", "fft4step", "fftbatch"], default="fwht",
                    help="fwht: configs[1] (default, weak scaling); fft4step: config 4, one 2^30-point FFT "
-                        "split over all ranks (strong scaling)")
+                        "split over all ranks (strong scaling); fftbatch: config 4's batch sweep, 2^20 "
+                        "transforms of 4096 points split over the ranks (strong scaling)")
+    p.add_argument("--log-batch", type=int, default=20, help="fftbatch total batch (log2)")
     p.add_argument("--log-n", type=int, default=30, help="fft4step transform length (log2)")
     p.add_argument("--mapping", default="", help="explicit mapping for --only fft1g / --workload fft4step (1 GPU)")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.workload in ("fft4step", "fftbatch") and not args.only else 4000
+    return args
 
 
 def peaks():
@@ -305,6 +311,72 @@ def fft4step(args):
     return 0
 
 
+def fftbatch(args):
+    """Config 4's batch sweep: 2^log_batch independent 4096-point complex fp32
+    FFTs (config 0's shape), the total batch split over the ranks with no
+    communication (strong scaling).  At 2^20 the input is 32 GiB: far larger
+    than L2, so every step streams from HBM."""
+    import torch
+    import torch.distributed as dist
+
+    import cubutterfly_b200 as cb
+    from cubutterfly_b200.distributed import shard_range
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    n, total = 4096, 1 << args.log_batch
+    _, count = shard_range(total, world, rank)
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.rand((count, n, 2), generator=g, device=dev, dtype=torch.float32)
+    x.mul_(2).sub_(1)
+    y = torch.empty_like(x)
+    plan = cb.Plan(cb.load(), cb.Transform(op=cb.Operator.FFT, extents=[n], batch=count), stream=stream.cuda_stream)
+    step = lambda: plan.execute(x.data_ptr(), y.data_ptr())  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank == 0:
+        step_bytes = 2 * total * n * 8
+        gbs = step_bytes / (ms * 1e-3) / 1e9
+        peak, kind = peaks()
+        print(json.dumps({
+            "metric": f"transform HBM GB/s (complex fp32 FFT, N=4096, batch 2^{args.log_batch} split over ranks)",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"fft_c64_4096_batch_2^{args.log_batch}", "algorithm": plan.algorithm_name(),
+                       "bytes_per_step": step_bytes, "parallelism": f"batch-sharded x{world}",
+                       "l2": "input larger than L2 (32 GiB at batch 2^20)"},
+            "frac_of_aggregate_hbm_peak": round(gbs / (peak * world), 4), "peak_kind": kind,
+            "clocks": clocks.summary()}), flush=True)
+    plan.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -313,6 +385,8 @@ def main():
         return only_op(args)
     if args.workload == "fft4step":
         return fft4step(args)
+    if args.workload == "fftbatch":
+        return fftbatch(args)
     import numpy as np
     import torch
     import torch.distributed as dist

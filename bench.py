@@ -576,6 +576,19 @@ def measure_ops(cb, lib, dev, stream, peak, steps, warmup):
         b = 2 * w.NTT_LIMBS * (1 << w.NTT_LOG_N) * 8
         ops["rns_ntt_u64_32x2^16"] = {"gbs": round(b / ms / 1e6, 1), "frac": round(b / ms / 1e6 / peak, 4),
                                       "us": round(ms * 1e3, 2), "algorithm": "b200_two_pass_tile"}
+    del ins, out
+    # config 4 on one GPU: one 2^30-point FFT (8 GiB in, 8 GiB out, 8 GiB workspace), multi-pass plan
+    n = 1 << 30
+    x = w.torch_fft_input(n, 1, dev, seed=4)
+    y = torch.empty_like(x)
+    with cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1), stream=sp) as p:
+        ws = torch.empty(p.workspace_size(), dtype=torch.uint8, device=dev)
+        p.set_workspace(ws.data_ptr(), ws.numel())
+        ms = time_launches(lambda i: p.execute(x.data_ptr(), y.data_ptr()), stream, 3, 1)
+        b = 2 * n * 8
+        ops["fft_c64_2^30"] = {"gbs": round(b / ms / 1e6, 1), "frac": round(b / ms / 1e6 / peak, 4),
+                               "us": round(ms * 1e3, 2), "algorithm": p.algorithm_name()}
+    del x, y, ws
     return ops
 
 

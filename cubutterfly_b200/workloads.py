@@ -152,8 +152,8 @@ def zeta_input(log_n: int = ZETA_LOG_N, batch: int = ZETA_BATCH, seed: int = SEE
 def torch_fft_input(n: int, batch: int, device, seed: int = SEED):
     import torch
     g = torch.Generator(device=device).manual_seed(seed)
-    x = torch.rand((batch, n, 2), generator=g, device=device, dtype=torch.float32) * 2 - 1
-    return x
+    x = torch.rand((batch, n, 2), generator=g, device=device, dtype=torch.float32)
+    return x.mul_(2).sub_(1)  # in place: no gigabyte temporaries at the large configs
 
 
 def torch_fwht_input(rows: int, cols: int, device, seed: int = SEED):

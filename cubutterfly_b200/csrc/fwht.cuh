@@ -156,32 +156,43 @@ constexpr int fwht_min_blocks() {
     return b > 8 ? 8 : (b < 1 ? 1 : b);
 }
 
-// One row of 2^LOGH elements (per thread-group of the CTA): `load16(e)`
-// returns the 16 bytes starting at row element e (a group-1 vector), results
-// go to `tout` (the row in HBM).  Every thread of the CTA must call it (it
-// contains barriers when the row spans several threads' exchanges).
-template <typename TS, int LOGH, int LOGE, typename Load16>
-CUBF_DEV void fwht_row(Load16 load16, TS* tout, bool active, uint32_t t, float* tbuf, float scale) {
+// Group-1 input of one thread: the 16-byte vectors of row `tin` it holds
+// (zeros for an inactive row).
+template <typename TS, int LOGH, int LOGE>
+CUBF_DEV void fwht_load(const TS* tin, bool active, uint32_t t, uint4 (&w)[FwhtShape<TS, LOGH, LOGE>::E /
+                                                                          FwhtShape<TS, LOGH, LOGE>::V]) {
+    using S = FwhtShape<TS, LOGH, LOGE>;
+    constexpr uint32_t R0 = S::G.reg[0];
+    constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
+    const uint32_t te = deposit_rt<lowmask(S::LT) & ~R0, S::LT>(t);
+#pragma unroll
+    for (int q = 0; q < S::E / S::V; ++q)
+        w[q] = active ? __ldg(reinterpret_cast<const uint4*>(tin + (te | O0.v[q * S::V]))) : make_uint4(0, 0, 0, 0);
+}
+
+// One row of 2^LOGH elements (per thread-group of the CTA) from its loaded
+// group-1 vectors `w`; results go to `tout` (the row in HBM).  Every thread
+// of the CTA must call it (it contains barriers when the row spans several
+// threads' exchanges).
+template <typename TS, int LOGH, int LOGE>
+CUBF_DEV void fwht_row(const uint4 (&w)[FwhtShape<TS, LOGH, LOGE>::E / FwhtShape<TS, LOGH, LOGE>::V], TS* tout,
+                       bool active, uint32_t t, float* tbuf, float scale) {
     using S = FwhtShape<TS, LOGH, LOGE>;
     constexpr bw::Groups G = S::G;
     constexpr int LT = S::LT;
     constexpr int NP = S::E / 2;
     P v[NP];
     {
-        constexpr uint32_t R0 = G.reg[0];
-        constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
-        const uint32_t te = deposit_rt<lowmask(LT) & ~R0, LT>(t);
 #pragma unroll
         for (int q = 0; q < S::E / S::V; ++q) {
-            const uint4 w = load16(te | O0.v[q * S::V]);
             if constexpr (sizeof(TS) == 4) {
-                v[q * 2] = (static_cast<P>(w.y) << 32) | w.x;
-                v[q * 2 + 1] = (static_cast<P>(w.w) << 32) | w.z;
+                v[q * 2] = (static_cast<P>(w[q].y) << 32) | w[q].x;
+                v[q * 2 + 1] = (static_cast<P>(w[q].w) << 32) | w[q].z;
             } else {
-                v[q * 4 + 0] = PairIO<TS>::widen(w.x);
-                v[q * 4 + 1] = PairIO<TS>::widen(w.y);
-                v[q * 4 + 2] = PairIO<TS>::widen(w.z);
-                v[q * 4 + 3] = PairIO<TS>::widen(w.w);
+                v[q * 4 + 0] = PairIO<TS>::widen(w[q].x);
+                v[q * 4 + 1] = PairIO<TS>::widen(w[q].y);
+                v[q * 4 + 2] = PairIO<TS>::widen(w[q].z);
+                v[q * 4 + 3] = PairIO<TS>::widen(w[q].w);
             }
         }
     }
@@ -263,10 +274,9 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_block
     const TS* tin = in + (active ? row : 0) * (size_t{1} << LOGH);
     TS* tout = out + (active ? row : 0) * (size_t{1} << LOGH);
     float* tbuf = reinterpret_cast<float*>(smem_raw + local * S::TILE_SMEM);
-    auto load16 = [&](uint32_t e) -> uint4 {
-        return active ? __ldg(reinterpret_cast<const uint4*>(tin + e)) : make_uint4(0, 0, 0, 0);
-    };
-    fwht_row<TS, LOGH, LOGE>(load16, tout, active, t, tbuf, scale);
+    uint4 w[S::E / S::V];
+    fwht_load<TS, LOGH, LOGE>(tin, active, t, w);
+    fwht_row<TS, LOGH, LOGE>(w, tout, active, t, tbuf, scale);
 }
 
 }  // namespace cubf::fwht

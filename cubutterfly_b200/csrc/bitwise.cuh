@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
                                        ? 512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB
                                        : 1))
     bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale,
-                        int cache_mode) {
+                        int cache_mode, unsigned prefetch_stride) {
     using S = TileShape<TS, TC, LOGH, LOGW, LOGE>;
     constexpr Groups G = S::G;
     constexpr int LT = S::LT;
@@ -523,6 +523,11 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
                 v[q] = Convert<TS, TC>::load(active ? tin[addr(e)] : TS{});
             }
         }
+    }
+    if constexpr (LOGW == 0) {  // loads issued: prefetch the rows of the CTA one resident wave later
+        constexpr size_t row_bytes = (size_t{1} << LOGH) * sizeof(TS);
+        const size_t rem = outer % S::TILES;
+        prefetch_next_wave(in, S::TILES * row_bytes, (rem ? rem : S::TILES) * row_bytes, prefetch_stride);
     }
     apply_group<Op, S::LOGE, G.reg[0], G.stage[0]>(v, inverse);
     exchange_groups<Op, S, 1>(v, tbuf, t, inverse);

@@ -123,6 +123,28 @@ struct alignas(16) Vec16 {
 // final pass streams its output.
 enum CacheMode : int { kStream = 0, kChainFirst = 1, kChainLast = 2, kChainMiddle = 3 };
 
+// Bulk prefetch of [p, p + bytes) into L2 (one instruction; p 16-byte
+// aligned, bytes a multiple of 16).  One-shot kernels issue it for the tile
+// the CTA one resident wave later will read, so DRAM keeps streaming while
+// the current wave computes.
+CUBF_DEV void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetch of the rows [first, first + count) x row_bytes of the tile that
+// CTA blockIdx.x + stride will process (thread 0 only; stride 0 disables).
+CUBF_DEV void prefetch_next_wave(const void* base, size_t tile_bytes, size_t last_bytes, unsigned stride) {
+    if (stride == 0 || threadIdx.x != 0) return;
+    const size_t next = static_cast<size_t>(blockIdx.x) + stride;
+    if (next >= gridDim.x) return;
+    const size_t bytes = next + 1 == gridDim.x ? last_bytes : tile_bytes;
+    const unsigned char* p = static_cast<const unsigned char*>(base) + next * tile_bytes;
+    for (size_t off = 0; off < bytes; off += size_t{1} << 20) {
+        const size_t n = bytes - off < (size_t{1} << 20) ? bytes - off : (size_t{1} << 20);
+        prefetch_l2(p + off, static_cast<uint32_t>(n));
+    }
+}
+
 CUBF_DEV uint64_t l2_policy(bool keep) {
     uint64_t p;
     if (keep)

@@ -158,9 +158,9 @@ struct Unroll {
 // Pass P, load half: the R inputs x[j + r N/R] of columns j, j+1 (j even),
 // the inter-pass twiddles, the radix-R codelets.  `gload(i)` reads HBM (pass
 // 0); later passes read the padded planes.
-template <int LOGN, int P, typename GLoad>
+template <int LOGN, int P, typename GLoad, typename AfterLoad>
 CUBF_DEV void pair_pass_load(CP (&v)[16], int q, const float4* __restrict__ tw, const float* pre,
-                             const float* pim, GLoad gload) {
+                             const float* pim, GLoad gload, AfterLoad after_load) {
     using S = PairShape<LOGN>;
     constexpr int RB = S::radix_bits(P);
     constexpr int R = 1 << RB;
@@ -173,6 +173,7 @@ CUBF_DEV void pair_pass_load(CP (&v)[16], int q, const float4* __restrict__ tw, 
         if constexpr (P == 0) {
 #pragma unroll
             for (int r = 0; r < R; ++r) v[u * R + r] = gload(j + r * STEP);
+            if (u == SUB - 1) after_load();  // global loads of this thread are issued
         } else {
             const int pj = S::pad(j);
             Unroll<R>::run([&](auto rc) {
@@ -253,18 +254,18 @@ CUBF_DEV void pair_pass_store(const CP (&v)[16], int q, float* pre, float* pim, 
 
 template <int LOGN, int P>
 struct PairPasses {
-    template <typename GLoad, typename GStore>
+    template <typename GLoad, typename GStore, typename AfterLoad>
     static CUBF_DEV void run(CP (&v)[16], int q, const float4* __restrict__ tw, float* pre, float* pim,
-                             GLoad gload, GStore gstore) {
+                             GLoad gload, GStore gstore, AfterLoad after_load) {
         using S = PairShape<LOGN>;
-        pair_pass_load<LOGN, P>(v, q, tw, pre, pim, gload);
+        pair_pass_load<LOGN, P>(v, q, tw, pre, pim, gload, after_load);
         if constexpr (P == S::NPASS - 1) {
             pair_pass_store<LOGN, P>(v, q, pre, pim, gstore);
         } else {
             if constexpr (P > 0) __syncthreads();  // every read of this pass is done
             pair_pass_store<LOGN, P>(v, q, pre, pim, gstore);
             __syncthreads();
-            PairPasses<LOGN, P + 1>::run(v, q, tw, pre, pim, gload, gstore);
+            PairPasses<LOGN, P + 1>::run(v, q, tw, pre, pim, gload, gstore, after_load);
         }
     }
 };
@@ -282,7 +283,7 @@ constexpr int pair_min_blocks() {
 template <int LOGN>
 __global__ void __launch_bounds__(PairShape<LOGN>::TPB, pair_min_blocks<LOGN>())
     fft_pair_kernel(const float4* in, float4* out, size_t batch, const float4* __restrict__ tw, int inverse,
-                    float scale) {
+                    float scale, unsigned prefetch_stride) {
     using S = PairShape<LOGN>;
     extern __shared__ __align__(16) float smem_f[];
     const int c = threadIdx.x / S::T;
@@ -314,8 +315,14 @@ __global__ void __launch_bounds__(PairShape<LOGN>::TPB, pair_min_blocks<LOGN>())
         up(x.im, m0, m1);
         if (active) __stcs(dst + (i >> 1), make_float4(r0, m0, r1, m1));
     };
+    // once this CTA's loads are out, prefetch the tile of the CTA one wave later into L2
+    auto after_load = [&]() {
+        constexpr size_t tile_bytes = size_t{S::TPC} * S::N * 8;
+        const size_t rem = batch % S::TPC;
+        prefetch_next_wave(in, tile_bytes, rem ? rem * S::N * 8 : tile_bytes, prefetch_stride);
+    };
     CP v[16];
-    PairPasses<LOGN, 0>::run(v, q, tw, pre, pim, gload, gstore);
+    PairPasses<LOGN, 0>::run(v, q, tw, pre, pim, gload, gstore, after_load);
 }
 
 }  // namespace cubf::fft

@@ -263,7 +263,7 @@ CUBF_DEV void fwht_row(const uint4 (&w)[FwhtShape<TS, LOGH, LOGE>::E / FwhtShape
 // Contiguous rows of 2^LOGH elements, `rows` of them; in may equal out.
 template <typename TS, int LOGH, int LOGE>
 __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_blocks<TS, LOGH, LOGE>())
-    fwht_tile_kernel(const TS* in, TS* out, size_t rows, float scale) {
+    fwht_tile_kernel(const TS* in, TS* out, size_t rows, float scale, unsigned prefetch_stride) {
     using S = FwhtShape<TS, LOGH, LOGE>;
     static_assert(S::E >= 2 && S::V * sizeof(TS) == 16, "FWHT tiles move 16-byte vectors");
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -276,6 +276,11 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_block
     float* tbuf = reinterpret_cast<float*>(smem_raw + local * S::TILE_SMEM);
     uint4 w[S::E / S::V];
     fwht_load<TS, LOGH, LOGE>(tin, active, t, w);
+    {  // loads issued: prefetch the tile of the CTA one resident wave later into L2
+        constexpr size_t row_bytes = (size_t{1} << LOGH) * sizeof(TS);
+        const size_t rem = rows % S::TILES;
+        prefetch_next_wave(in, S::TILES * row_bytes, (rem ? rem : S::TILES) * row_bytes, prefetch_stride);
+    }
     fwht_row<TS, LOGH, LOGE>(w, tout, active, t, tbuf, scale);
 }
 

@@ -86,8 +86,9 @@ struct FwhtEntry {
         if (e != cudaSuccess) return e;
         const std::size_t blocks = (outer + S::TILES - 1) / S::TILES;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        const unsigned stride = blocks > static_cast<std::size_t>(grid_cap) ? grid_cap : 0;
         kernel<<<static_cast<unsigned>(blocks), S::TPB, SMEM, stream>>>(static_cast<const TS*>(in),
-                                                                          static_cast<TS*>(out), outer, scale);
+                                                                          static_cast<TS*>(out), outer, scale, stride);
         return cudaGetLastError();
     }
 };
@@ -120,8 +121,12 @@ struct Entry {
         const std::size_t blocks = (tiles + S::TILES - 1) / S::TILES;
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        // contiguous passes that stream from DRAM prefetch one resident wave ahead
+        const bool streams_in = LOGW == 0 && (cache_mode == kStream || cache_mode == kChainFirst);
+        const unsigned stride = streams_in && blocks > static_cast<std::size_t>(grid_cap) ? grid_cap : 0;
         kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-            static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0, scale, cache_mode);
+            static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0, scale, cache_mode,
+            stride);
         return cudaGetLastError();
     }
 };

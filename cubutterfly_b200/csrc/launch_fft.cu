@@ -37,8 +37,10 @@ cudaError_t launch_pair(const void* in, void* out, std::size_t batch, const void
     const std::size_t blocks = (batch + S::TPC - 1) / S::TPC;
     if (blocks == 0) return cudaSuccess;
     if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+    // prefetch one resident wave ahead when the grid has more than one wave
+    const unsigned stride = blocks > static_cast<std::size_t>(grid_cap) ? grid_cap : 0;
     kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-        static_cast<const float4*>(in), static_cast<float4*>(out), batch, table, inverse ? 1 : 0, scale);
+        static_cast<const float4*>(in), static_cast<float4*>(out), batch, table, inverse ? 1 : 0, scale, stride);
     return cudaGetLastError();
 }
 

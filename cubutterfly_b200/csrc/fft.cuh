@@ -327,7 +327,7 @@ template <int LOGR>
 __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
     fft_global_pass_kernel(const float2* src, float2* dst, int log_n, int ns_bits, size_t batch,
                            const float2* __restrict__ tw_r, int tw_log_stride, OuterTwiddles outer, int conj_in,
-                           int conj_out, float scale, int log_v) {
+                           int conj_out, float scale, int log_v, unsigned prefetch_stride) {
     using G = GlobalPassShape<LOGR>;
     using S = typename G::S;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -368,6 +368,13 @@ __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
             }
             a[c * G::RS + S::pad(r)] = x;
         }
+    }
+    // loads issued: prefetch the tile of the CTA one resident wave later into L2, one C-column row segment
+    // (a run of C * 8 bytes) per thread and row
+    if (prefetch_stride != 0 && blockIdx.x + static_cast<size_t>(prefetch_stride) < gridDim.x) {
+        const size_t nb = blockIdx.x + static_cast<size_t>(prefetch_stride);
+        const float2* nsrc = src + (nb / ctas_per_batch) * n + (nb % ctas_per_batch) * G::C;
+        for (int r = threadIdx.x; r < G::R; r += G::TPB) prefetch_l2(nsrc + static_cast<size_t>(r) * cols, G::C * 8);
     }
     __syncthreads();
     // 2. length-R DFT of each column, in place in shared memory

@@ -104,7 +104,8 @@ struct GlobalEntry {
                               outer.split};
         kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
             static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits, batch,
-            static_cast<const float2*>(tw1024), 10 - LOGR, ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v);
+            static_cast<const float2*>(tw1024), 10 - LOGR, ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v,
+            blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u);
         return cudaGetLastError();
     }
 };

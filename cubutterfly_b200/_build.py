@@ -43,10 +43,14 @@ def _units():
               "--expt-relaxed-constexpr", f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{_json_include()}"]
     units = []
     for name in ("c_api.cpp", "descriptor.cpp", "planner.cpp", "rns_api.cpp", "launch_bitwise_dispatch.cpp",
-                 "launch_fft.cu", "launch_ntt.cu", "noalloc.cu", "fourstep.cu"):
+                 "launch_ntt_dispatch.cpp", "launch_fft.cu", "noalloc.cu", "fourstep.cu", "bitrev.cu"):
         src = CSRC / name
         obj = OBJ / (src.stem + ".o")
         units.append((common + ["-c", str(src), "-o", str(obj)], src, obj))
+    for word in (64, 32):  # NTT storage words
+        src = CSRC / "launch_ntt.cu"
+        obj = OBJ / f"ntt_w{word}.o"
+        units.append((common + [f"-DCUBF_NTT_WORD={word}", "-c", str(src), "-o", str(obj)], src, obj))
     for op, ty in BW_UNITS:
         src = CSRC / "launch_bitwise.cu"
         obj = OBJ / f"bitwise_{op}_{ty}.o"

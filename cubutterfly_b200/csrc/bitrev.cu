@@ -1,0 +1,107 @@
+// bitrev.cu -- bit-reversal permutation of packed batches of 2^L elements.
+//
+// Serves the bit-reversed logical orders of the main ABI (semantic contract
+// src/semantic_contract.cpp:257-271: a bit-reversed axis stores logical index
+// i at position bitrev(i)).  For L >= 10 the index is split as (a, m, b) with
+// 5-bit a and b: element (a, m, b) moves to (rev b, rev m, rev a), so the
+// 32 x 32 tile of middle index m maps onto the tile of middle index rev(m) with
+// rows and columns exchanged and reversed.  One CTA loads both tiles m and
+// rev(m) through shared memory and writes both, so every CTA writes exactly
+// the addresses it read and the permutation runs in place as well; rows are
+// 32 consecutive elements, so loads and stores are coalesced.  Shorter
+// transforms swap element pairs directly.
+#include "common.cuh"
+#include "kernels.hpp"
+
+#include <cstdint>
+
+namespace cubf {
+namespace {
+
+constexpr int kTileBits = 5;
+constexpr int kTile = 1 << kTileBits;
+constexpr int kThreads = 256;
+
+CUBF_DEV uint32_t rev_bits(uint32_t x, int bits) { return bits ? __brev(x) >> (32 - bits) : 0u; }
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) bitrev_tiled_kernel(const T* in, T* out, int log_n) {
+    __shared__ T s[2][kTile][kTile + 1];  // +1 column: the transposed reads hit distinct banks
+    const int mid_bits = log_n - 2 * kTileBits;
+    const size_t blk = blockIdx.x;
+    const uint32_t m = static_cast<uint32_t>(blk & ((size_t{1} << mid_bits) - 1));
+    const uint32_t mr = rev_bits(m, mid_bits);
+    if (mr < m) return;  // the pair is handled by the CTA of the smaller index
+    const bool pair = mr != m;
+    const size_t n = size_t{1} << log_n;
+    const size_t base = (blk >> mid_bits) * n;
+    const size_t row = size_t{1} << (log_n - kTileBits);  // distance between rows a and a + 1
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const T* src = in + base;
+    T* dst = out + base;
+#pragma unroll
+    for (int a = warp; a < kTile; a += kThreads / 32) {
+        s[0][a][lane] = src[a * row + (static_cast<size_t>(m) << kTileBits) + lane];
+        if (pair) s[1][a][lane] = src[a * row + (static_cast<size_t>(mr) << kTileBits) + lane];
+    }
+    __syncthreads();
+    const uint32_t rl = rev_bits(lane, kTileBits);
+#pragma unroll
+    for (int a = warp; a < kTile; a += kThreads / 32) {
+        const uint32_t ra = rev_bits(a, kTileBits);
+        dst[a * row + (static_cast<size_t>(mr) << kTileBits) + lane] = s[0][rl][ra];
+        if (pair) dst[a * row + (static_cast<size_t>(m) << kTileBits) + lane] = s[1][rl][ra];
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) bitrev_small_kernel(const T* in, T* out, int log_n, size_t total) {
+    const size_t idx = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (idx >= total) return;
+    const size_t n = size_t{1} << log_n;
+    const size_t base = idx & ~(n - 1);
+    const uint32_t i = static_cast<uint32_t>(idx & (n - 1));
+    const uint32_t j = rev_bits(i, log_n);
+    if (j < i) return;  // each pair is swapped by its smaller index
+    const T a = in[base + i], b = in[base + j];
+    out[base + j] = a;
+    out[base + i] = b;
+}
+
+template <typename T>
+cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch, cudaStream_t stream) {
+    const T* src = static_cast<const T*>(in);
+    T* dst = static_cast<T*>(out);
+    if (log_n >= 2 * kTileBits) {
+        const std::size_t blocks = batch << (log_n - 2 * kTileBits);
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        bitrev_tiled_kernel<T><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(src, dst, log_n);
+    } else {
+        const std::size_t total = batch << log_n;
+        const std::size_t blocks = (total + kThreads - 1) / kThreads;
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        bitrev_small_kernel<T><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(src, dst, log_n, total);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
+                          cudaStream_t stream) {
+    if (log_n < 0 || log_n > 31) return cudaErrorInvalidValue;
+    if (batch == 0 || log_n == 0) {
+        if (in != out && batch != 0)
+            return cudaMemcpyAsync(out, in, batch * static_cast<std::size_t>(elem_bytes), cudaMemcpyDeviceToDevice,
+                                   stream);
+        return cudaSuccess;
+    }
+    switch (elem_bytes) {
+        case 2: return launch_typed<std::uint16_t>(log_n, in, out, batch, stream);
+        case 4: return launch_typed<std::uint32_t>(log_n, in, out, batch, stream);
+        case 8: return launch_typed<unsigned long long>(log_n, in, out, batch, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace cubf

@@ -11,6 +11,7 @@
 
 #include "descriptor.hpp"
 #include "kernels.hpp"
+#include "modarith.hpp"
 #include "planner.hpp"
 
 #include <cuda_runtime_api.h>
@@ -52,6 +53,11 @@ struct cubutterflyPlan {
     void* outer_lo = nullptr;  // global FFT: double2 W_N^k, k < 2^split
     void* outer_hi = nullptr;  // global FFT: double2 W_N^(k << split)
     int outer_split = 0;
+    // NTT: one allocation holding the root table, its Shoup quotients, the
+    // per-modulus constants and the per-transform offsets of the tile passes.
+    void* ntt_block = nullptr;
+    cubf::NttTables ntt_tables{};
+    const cubf::NttPolyDesc* ntt_polys = nullptr;
     int device = 0;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
@@ -59,6 +65,7 @@ struct cubutterflyPlan {
         if (twiddles) cudaFree(twiddles);
         if (outer_lo) cudaFree(outer_lo);
         if (outer_hi) cudaFree(outer_hi);
+        if (ntt_block) cudaFree(ntt_block);
     }
 };
 
@@ -195,11 +202,63 @@ void store_cache(const std::string& path, const std::string& key, const cubf::Ma
 }
 
 // ---- execution ----------------------------------------------------------------
+// Cyclic NTT (cuntt::Plan semantics, include/cuntt/ntt.hpp:432; reference_ntt
+// src/reference.cpp:584-630): input words reduced modulo q on load, the
+// inverse always scaled by N^-1.
+void launch_ntt(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    const int l = p.req.log_n;
+    const bool gs = p.req.ntt_gs;
+    cubf::NttLaunch a;
+    a.count = d.batch;
+    a.tables = p.ntt_tables;
+    a.polys = p.ntt_polys;
+    a.in = in;
+    a.out = out;
+    a.reduce_input = true;
+    if (m.passes.size() == 1) {
+        a.final_pass = true;
+        a.final_scale = inverse;
+        check_cuda(cubf::launch_ntt({l, false, gs, p.req.ntt_lazy, p.req.ntt_word32}, a, stream), "NTT launch");
+        return;
+    }
+    check_cuda(cubf::launch_ntt({l, !gs, gs, p.req.ntt_lazy, p.req.ntt_word32}, a, stream), "NTT pass 1 launch");
+    a.in = out;
+    a.in_is_out = true;
+    a.reduce_input = false;
+    a.final_pass = true;
+    a.final_scale = inverse;
+    check_cuda(cubf::launch_ntt({l, gs, gs, p.req.ntt_lazy, p.req.ntt_word32}, a, stream), "NTT pass 2 launch");
+}
+
+void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream);
+
+// The logical-order boundary around the core passes: a bit-reversed input is
+// permuted into the output buffer first (the core then runs in place there),
+// a bit-reversed output is permuted in place last.
 void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                     cudaStream_t stream) {
     const auto& d = p.desc;
+    const int esz = static_cast<int>(cubf::storage_bytes(d.storage));
+    const void* core_in = in;
+    if (m.permute_input) {
+        check_cuda(cubf::launch_bitrev(esz, p.req.log_n, in, out, d.batch, stream), "input permutation launch");
+        core_in = out;
+    }
+    launch_core(p, m, core_in, out, stream);
+    if (m.permute_output)
+        check_cuda(cubf::launch_bitrev(esz, p.req.log_n, out, out, d.batch, stream), "output permutation launch");
+}
+
+void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
     const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
     const std::size_t n = d.extents[0];
+    if (d.op == CUBUTTERFLY_OPERATOR_NTT) {
+        launch_ntt(p, m, in, out, stream);
+        return;
+    }
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
         const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
         if (m.passes.front().kind == cubf::PassKind::FftLocal) {
@@ -285,10 +344,54 @@ double time_mapping(cubutterflyPlan& p, const cubf::Mapping& m, const void* in, 
     return 1000.0 * ms / reps;
 }
 
+// Root table of the cyclic NTT with the reference's root convention
+// (find_primitive_power_of_two_root(log N, q); the inverse uses its modular
+// inverse, src/reference.cpp:597-600), followed by q, N^-1, its Shoup
+// quotient, floor(2^64 / q) and the per-transform offsets.
+void build_ntt_tables(cubutterflyPlan& p) {
+    namespace ma = cubf::modarith;
+    const auto& d = p.desc;
+    const int l = p.req.log_n;
+    const std::uint64_t q = d.modulus;
+    // validate_config of the reference's NTT plans (src/ntt.cu): a prime
+    // modulus below 2^63 with 2^log_n | q - 1 (the root search checks the rest)
+    require(q < (std::uint64_t{1} << 63), "NTT modulus must be below 2^63");
+    const std::size_t n = std::size_t{1} << l;
+    std::uint64_t root = ma::primitive_root_of_two_power(static_cast<unsigned>(l), q);
+    if (d.direction == CUBUTTERFLY_DIRECTION_INVERSE) root = ma::powmod(root, q - 2, q);
+    std::vector<std::uint64_t> words(2 * n + 4);
+    ma::cyclic_root_table(l, q, root, words.data(), words.data() + n);
+    const std::uint64_t ni = ma::powmod(static_cast<std::uint64_t>(n), q - 2, q);
+    words[2 * n + 0] = q;
+    words[2 * n + 1] = ni;
+    words[2 * n + 2] = ma::shoup(ni, q);
+    words[2 * n + 3] = static_cast<std::uint64_t>((static_cast<unsigned __int128>(1) << 64) / q);
+    std::vector<cubf::NttPolyDesc> polys;
+    if (!cubf::ntt_single_available(l)) {
+        polys.resize(d.batch);
+        for (std::size_t b = 0; b < d.batch; ++b) polys[b] = {b * n, b * n, 0, 0};
+    }
+    const std::size_t table_bytes = words.size() * 8, poly_bytes = polys.size() * sizeof(cubf::NttPolyDesc);
+    check_cuda(cudaMalloc(&p.ntt_block, table_bytes + poly_bytes), "NTT table allocation");
+    check_cuda(cudaMemcpy(p.ntt_block, words.data(), table_bytes, cudaMemcpyHostToDevice), "NTT table upload");
+    auto* base = static_cast<std::uint64_t*>(p.ntt_block);
+    if (poly_bytes) {
+        check_cuda(cudaMemcpy(base + words.size(), polys.data(), poly_bytes, cudaMemcpyHostToDevice),
+                   "NTT offsets upload");
+        p.ntt_polys = reinterpret_cast<const cubf::NttPolyDesc*>(base + words.size());
+    }
+    p.ntt_tables = {base, base + n, base + 2 * n, base + 2 * n + 1, base + 2 * n + 2, base + 2 * n + 3};
+}
+
 void build_tables(cubutterflyPlan& p) {
+    if (p.desc.op == CUBUTTERFLY_OPERATOR_NTT) {
+        build_ntt_tables(p);
+        return;
+    }
     if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
     constexpr double kPi = 3.141592653589793238462643383279502884;
-    const bool global = p.mapping.passes.front().kind == cubf::PassKind::FftGlobal;
+    // every candidate of a request is global or every one is local
+    const bool global = p.req.log_n > cubf::kFftLocalMaxLog || p.req.log_v > 0;
     if (global) {
         // exp(-2 pi i k / N) for the outer twiddles, in double: lo k < 2^split, hi k << split
         const int l = p.req.log_n;
@@ -339,6 +442,7 @@ cubf::PlanRequest make_request(const cubf::Descriptor& d) {
         default:
             break;
     }
+    cubf::resolve_orders(r);
     return r;
 }
 
@@ -377,6 +481,15 @@ void select_mapping(cubutterflyHandle* h, cubutterflyPlan& p) {
     check_cuda(cudaMalloc(&b, bytes), "measure buffer");
     std::unique_ptr<void, void (*)(void*)> gb(b, [](void* x) { cudaFree(x); });
     check_cuda(cudaMemset(a, 0, bytes), "measure buffer init");
+    // a private workspace for the finalists (the caller's is set after planning)
+    std::size_t ws_bytes = 0;
+    for (std::size_t i = 0; i < finalists; ++i) ws_bytes = std::max(ws_bytes, ranked[i].workspace_bytes);
+    void* ws = nullptr;
+    if (ws_bytes) check_cuda(cudaMalloc(&ws, ws_bytes), "measure workspace");
+    std::unique_ptr<void, void (*)(void*)> gws(ws, [](void* x) {
+        if (x) cudaFree(x);
+    });
+    p.workspace = ws;
     cudaStream_t s = h ? h->stream : nullptr;
     double best = 1e300;
     std::size_t best_i = 0;
@@ -387,6 +500,8 @@ void select_mapping(cubutterflyHandle* h, cubutterflyPlan& p) {
             best_i = i;
         }
     }
+    check_cuda(cudaStreamSynchronize(s), "measure drain");
+    p.workspace = nullptr;
     p.mapping = ranked[best_i];
     p.source = CUBUTTERFLY_SELECTION_RUNTIME_MEASURED;
     std::ostringstream o;
@@ -701,8 +816,8 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
         p->req = make_request(p->desc);
         p->hw = cubf::resolve_profile();
         check_cuda(cudaGetDevice(&p->device), "current device");
+        build_tables(*p);  // before selection: MEASURE executes the candidates
         select_mapping(handle, *p);
-        build_tables(*p);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
         *plan = p.release();
     });
@@ -781,8 +896,10 @@ cubutterflyStatus_t cubutterflyPlanGetMappingJson(cubutterflyPlan_t plan, char* 
 cubutterflyStatus_t cubutterflyPlanGetNttLayoutInfo(cubutterflyPlan_t plan, cubutterflyNttLayoutInfo_t* info) {
     return protect([&] {
         require(plan != nullptr && info != nullptr, "plan and info must be non-null");
-        throw cubf::Unsupported("NTT layout info applies to main-ABI NTT plans, which this build serves through "
-                                "the RNS ABI");
+        // The reference reports layout info only for its APPT static-layout
+        // NTT cores (src/c_api.cpp:4843-4870); this build executes natural
+        // and bit-reversed orders only.
+        throw cubf::Unsupported("NTT layout info describes APPT static layouts, which this build does not execute");
     });
 }
 

@@ -500,6 +500,9 @@ Json capabilities(const Descriptor& source) {
                                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; });
     const bool natural_out = std::all_of(d.output_orders.begin(), d.output_orders.end(),
                                          [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; });
+    // Bit-reversed orders run as bit-reversal permutations of packed batches.
+    if ((!natural_in || !natural_out) && !packed)
+        gap("order-lowering", "bit-reversed logical orders require packed rank-one batches");
     if (d.arithmetic_policy != CUBUTTERFLY_ARITHMETIC_STRICT)
         gap("arithmetic-policy", "FP16 MMA policy is not built");
     const bool epilogue = d.output_scale != 1.0 || d.output_rounding != CUBUTTERFLY_ROUNDING_STAGE_STORAGE;
@@ -507,7 +510,6 @@ Json capabilities(const Descriptor& source) {
         case CUBUTTERFLY_OPERATOR_FFT:
             if (d.storage != CUBUTTERFLY_DATA_COMPLEX_FP32 || d.compute != CUBUTTERFLY_COMPUTE_FP32)
                 gap("storage-lowering", "FFT executes complex FP32 storage with FP32 compute");
-            if (!natural_in || !natural_out) gap("order-lowering", "FFT executes natural logical orders");
             if (epilogue) gap("output-epilogue-lowering", "output epilogues apply to FWHT only");
             if (n > (std::size_t{1} << 30)) gap("length-lowering", "FFT length is limited to 2^30");
             break;
@@ -523,7 +525,6 @@ Json capabilities(const Descriptor& source) {
                 gap("output-epilogue-lowering", "output epilogue requires FP32 compute");
             if (!std::isfinite(static_cast<float>(d.output_scale)))
                 gap("output-scale-lowering", "output scale must be representable as finite FP32");
-            if (!natural_in || !natural_out) gap("order-lowering", "FWHT executes natural logical orders");
             if (n > (std::size_t{1} << 15)) gap("length-lowering", "FWHT length is limited to 2^15");
             break;
         }
@@ -531,13 +532,17 @@ Json capabilities(const Descriptor& source) {
         case CUBUTTERFLY_OPERATOR_SUPERSET_ZETA:
             if (d.storage != CUBUTTERFLY_DATA_UINT32 && d.storage != CUBUTTERFLY_DATA_UINT64)
                 gap("storage-lowering", "zeta kernels require uint32 or uint64 storage");
-            if (!natural_in || !natural_out) gap("order-lowering", "zeta executes natural logical orders");
             if (epilogue) gap("output-epilogue-lowering", "output epilogues apply to FWHT only");
             if (n > (std::size_t{1} << 30)) gap("length-lowering", "zeta length is limited to 2^30");
             break;
         case CUBUTTERFLY_OPERATOR_NTT:
-            gap("operator-lowering",
-                "single-modulus NTT is served by the RNS ABI (cubutterflyRnsCreate) in this build");
+            // Cyclic NTT over uint32 / uint64 words (word bits = storage
+            // bits, checked by normalize); modulus primality, q < 2^63 and
+            // 2^log_n | q - 1 are plan-time validation (INVALID_VALUE), as
+            // in the reference's plan constructor.
+            if (epilogue) gap("output-epilogue-lowering", "output epilogues apply to FWHT only");
+            if (n > (std::size_t{1} << 20))
+                gap("length-lowering", "NTT length is limited to 2^20 (the reference's direct NTT range)");
             break;
         case CUBUTTERFLY_OPERATOR_STRUCTURED_2X2:
             gap("operator-lowering", "structured 2x2 transforms are not built");

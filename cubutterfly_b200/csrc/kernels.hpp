@@ -74,7 +74,7 @@ LaunchShape bw_shape(const BwVariant& v);
 cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
                       bool inverse, float scale, int cache_mode, cudaStream_t stream);
 
-// ---- RNS NTT tile passes --------------------------------------------------------
+// ---- NTT tile passes (RNS ABI and the main-ABI cyclic NTT) ----------------------
 struct NttPolyDesc {
     std::uint64_t in_off;
     std::uint64_t out_off;
@@ -87,21 +87,46 @@ struct NttTables {
     const std::uint64_t* moduli;
     const std::uint64_t* n_inv;
     const std::uint64_t* n_inv_q;
+    const std::uint64_t* unit_q = nullptr;  // floor(2^64 / q); needed when input words are reduced
 };
 struct NttVariant {
-    int log_n;     // transform length 2^log_n
-    bool strided;  // top bits (strided columns) or low bits (contiguous chunks)
-    bool inverse;
-    bool lazy;     // Harvey lazy reduction (every modulus < 2^62)
+    int log_n;            // transform length 2^log_n
+    bool strided;         // top bits (strided columns) or low bits (contiguous chunks)
+    bool inverse;         // Gentleman-Sande (bit-reversed in, natural out) vs Cooley-Tukey
+    bool lazy;            // Harvey lazy reduction (every modulus < 2^62)
+    bool word32 = false;  // 32-bit storage words (moduli < 2^32, always lazy)
 };
+// One launch of a pass (2^12 .. 2^20: strided or contiguous tile pass over the
+// polynomials of `polys`, a DEVICE array of `count` entries) or of a
+// whole-transform tile (2^1 .. 2^11: `count` packed transforms, domain 0,
+// `polys` unused).
+struct NttLaunch {
+    const void* in = nullptr;
+    void* out = nullptr;
+    const NttPolyDesc* polys = nullptr;
+    std::size_t count = 0;
+    NttTables tables{};
+    bool in_is_out = false;     // read the output buffer at the output offsets
+    bool final_pass = false;    // this pass writes the result (lazy: reduce to [0, q))
+    bool final_scale = false;   // multiply the result by N^-1
+    bool reduce_input = false;  // reduce input words modulo q on load
+};
+constexpr int kNttSingleMaxLog = 11;
 constexpr int kNttMinLog = 12;
 constexpr int kNttMaxLog = 20;
 inline int ntt_pass_bits(int log_n, bool strided) { return strided ? (log_n + 1) / 2 : log_n / 2; }
+// Two tile passes exist for 2^12 .. 2^20.
 bool ntt_available(const NttVariant& v);
+// A whole-transform tile exists for 2^1 .. 2^11.
+bool ntt_single_available(int log_n);
 LaunchShape ntt_shape(const NttVariant& v);
-// One pass over all polynomials; polys is a DEVICE array of poly_count entries.
-cudaError_t launch_ntt_pass(const NttVariant& v, const std::uint64_t* in, std::uint64_t* out,
-                            const NttPolyDesc* polys, std::size_t poly_count, const NttTables& tables,
-                            bool in_is_out, bool final_pass, bool final_scale, cudaStream_t stream);
+cudaError_t launch_ntt(const NttVariant& v, const NttLaunch& a, cudaStream_t stream);
+
+// ---- bit-reversal permutation ------------------------------------------------------
+// out[b][rev(i)] = in[b][i] for `batch` packed transforms of 2^log_n elements
+// of elem_bytes (2, 4 or 8) each.  in may equal out (pairs of tiles are swapped
+// by one CTA).
+cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
+                          cudaStream_t stream);
 
 }  // namespace cubf

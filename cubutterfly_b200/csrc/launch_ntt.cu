@@ -1,10 +1,31 @@
-// launch_ntt.cu -- instantiations and launchers of the RNS NTT tile passes.
+// launch_ntt.cu -- instantiations and launchers of the NTT tile kernels for
+// one storage word, chosen by CUBF_NTT_WORD (32 or 64; one object each).
+// 64-bit words carry strict and lazy variants (lazy needs every modulus
+// < 2^62); 32-bit words always have q < 2^32 and use the lazy variants only.
 #include "kernels.hpp"
 #include "launch_util.cuh"
 #include "ntt.cuh"
 
+#ifndef CUBF_NTT_WORD
+#define CUBF_NTT_WORD 64
+#endif
+
 namespace cubf {
 namespace {
+
+#if CUBF_NTT_WORD == 64
+using Word = ntt::u64;
+constexpr bool kHasStrict = true;
+#else
+using Word = unsigned int;
+constexpr bool kHasStrict = false;
+#endif
+
+ntt::DomainTables device_tables(const NttTables& t) {
+    return {reinterpret_cast<const ntt::u64*>(t.roots),   reinterpret_cast<const ntt::u64*>(t.quotients),
+            reinterpret_cast<const ntt::u64*>(t.moduli),  reinterpret_cast<const ntt::u64*>(t.n_inv),
+            reinterpret_cast<const ntt::u64*>(t.n_inv_q), reinterpret_cast<const ntt::u64*>(t.unit_q)};
+}
 
 template <int L, bool STRIDED, bool INV, bool LAZY>
 struct Entry {
@@ -18,32 +39,53 @@ struct Entry {
         s.exchanges = S::Gs::COUNT - 1;
         return s;
     }
-    static cudaError_t launch(const std::uint64_t* in, std::uint64_t* out, const NttPolyDesc* polys,
-                              std::size_t poly_count, const NttTables& t, bool in_is_out, bool final_pass,
-                              bool final_scale, cudaStream_t stream) {
-        auto kernel = ntt::ntt_pass_kernel<L, STRIDED, INV, LAZY>;
+    static cudaError_t launch(const NttLaunch& a, cudaStream_t stream) {
+        auto kernel = ntt::ntt_pass_kernel<L, STRIDED, INV, LAZY, Word>;
         static KernelSetup setup;
         int grid_cap = 0;
         cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
         if (e != cudaSuccess) return e;
         constexpr std::size_t groups = (std::size_t{1} << (L - S::B)) / S::COLS;
-        const std::size_t blocks = poly_count * groups;
+        const std::size_t blocks = a.count * groups;
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
-        ntt::DomainTables tab{reinterpret_cast<const ntt::u64*>(t.roots),
-                              reinterpret_cast<const ntt::u64*>(t.quotients),
-                              reinterpret_cast<const ntt::u64*>(t.moduli), reinterpret_cast<const ntt::u64*>(t.n_inv),
-                              reinterpret_cast<const ntt::u64*>(t.n_inv_q)};
         kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-            reinterpret_cast<const ntt::u64*>(in), reinterpret_cast<ntt::u64*>(out),
-            reinterpret_cast<const ntt::PolyDesc*>(polys), tab, in_is_out ? 1 : 0, final_pass ? 1 : 0,
-            final_scale ? 1 : 0);
+            static_cast<const Word*>(a.in), static_cast<Word*>(a.out),
+            reinterpret_cast<const ntt::PolyDesc*>(a.polys), device_tables(a.tables), a.in_is_out ? 1 : 0,
+            a.final_pass ? 1 : 0, a.final_scale ? 1 : 0, a.reduce_input ? 1 : 0);
         return cudaGetLastError();
     }
 };
 
-using LaunchFn = cudaError_t (*)(const std::uint64_t*, std::uint64_t*, const NttPolyDesc*, std::size_t,
-                                 const NttTables&, bool, bool, bool, cudaStream_t);
+template <int L, bool INV, bool LAZY>
+struct SingleEntry {
+    using S = ntt::SingleShape<L, INV, LAZY>;
+    static LaunchShape shape() {
+        LaunchShape s;
+        s.threads = S::TPB;
+        s.smem_bytes = S::SMEM_BYTES;
+        s.units_per_cta = S::COLS;
+        s.elems_per_thread = S::E;
+        s.exchanges = S::Gs::COUNT - 1;
+        return s;
+    }
+    static cudaError_t launch(const NttLaunch& a, cudaStream_t stream) {
+        auto kernel = ntt::ntt_single_kernel<L, INV, LAZY, Word>;
+        static KernelSetup setup;
+        int grid_cap = 0;
+        cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
+        if (e != cudaSuccess) return e;
+        const std::size_t blocks = (a.count + S::COLS - 1) / S::COLS;
+        if (blocks == 0) return cudaSuccess;
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+            static_cast<const Word*>(a.in), static_cast<Word*>(a.out), a.count, device_tables(a.tables),
+            a.final_scale ? 1 : 0, a.reduce_input ? 1 : 0);
+        return cudaGetLastError();
+    }
+};
+
+using LaunchFn = cudaError_t (*)(const NttLaunch&, cudaStream_t);
 using ShapeFn = LaunchShape (*)();
 
 template <bool STRIDED, bool INV, bool LAZY, int... L>
@@ -51,51 +93,77 @@ struct Row {
     static constexpr LaunchFn launch[] = {Entry<L, STRIDED, INV, LAZY>::launch...};
     static constexpr ShapeFn shape[] = {Entry<L, STRIDED, INV, LAZY>::shape...};
 };
-#define CUBF_NTT_LOGS 12, 13, 14, 15, 16, 17, 18, 19, 20
-// [inverse][strided][lazy]
-template <bool INV, bool STRIDED>
-struct Rows {
-    using Strict = Row<STRIDED, INV, false, CUBF_NTT_LOGS>;
-    using Lazy = Row<STRIDED, INV, true, CUBF_NTT_LOGS>;
+template <bool INV, bool LAZY, int... L>
+struct SingleRow {
+    static constexpr LaunchFn launch[] = {SingleEntry<L, INV, LAZY>::launch...};
+    static constexpr ShapeFn shape[] = {SingleEntry<L, INV, LAZY>::shape...};
 };
+#define CUBF_NTT_LOGS 12, 13, 14, 15, 16, 17, 18, 19, 20
+#define CUBF_NTT_SINGLE_LOGS 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11
+static_assert(kNttSingleMaxLog == 11 && kNttMinLog == 12, "instantiated length ranges");
 
-static_assert(sizeof(NttPolyDesc) == sizeof(ntt::PolyDesc), "poly descriptor layout");
+// Pass tables [inverse][strided][lazy]; 32-bit words map strict requests to lazy.
+template <typename Fn, bool FOR_SHAPE>
+Fn pick_pass(const NttVariant& v) {
+    const bool lazy = v.lazy || !kHasStrict;
+    const int s = v.log_n - kNttMinLog;
+#define CUBF_PICK(INV, STR)                                                                              \
+    if (lazy) {                                                                                          \
+        if constexpr (FOR_SHAPE) return Row<STR, INV, true, CUBF_NTT_LOGS>::shape[s];                    \
+        else return Row<STR, INV, true, CUBF_NTT_LOGS>::launch[s];                                       \
+    } else {                                                                                             \
+        if constexpr (FOR_SHAPE) return Row<STR, INV, !kHasStrict, CUBF_NTT_LOGS>::shape[s];             \
+        else return Row<STR, INV, !kHasStrict, CUBF_NTT_LOGS>::launch[s];                                \
+    }
+    if (!v.inverse) {
+        if (v.strided) { CUBF_PICK(false, true) } else { CUBF_PICK(false, false) }
+    } else {
+        if (v.strided) { CUBF_PICK(true, true) } else { CUBF_PICK(true, false) }
+    }
+#undef CUBF_PICK
+}
 
-int slot(const NttVariant& v) {
-    if (v.log_n < kNttMinLog || v.log_n > kNttMaxLog) return -1;
-    return v.log_n - kNttMinLog;
+template <typename Fn, bool FOR_SHAPE>
+Fn pick_single(const NttVariant& v) {
+    const bool lazy = v.lazy || !kHasStrict;
+    const int s = v.log_n - 1;
+#define CUBF_PICK(INV)                                                                            \
+    if (lazy) {                                                                                   \
+        if constexpr (FOR_SHAPE) return SingleRow<INV, true, CUBF_NTT_SINGLE_LOGS>::shape[s];     \
+        else return SingleRow<INV, true, CUBF_NTT_SINGLE_LOGS>::launch[s];                        \
+    } else {                                                                                      \
+        if constexpr (FOR_SHAPE) return SingleRow<INV, !kHasStrict, CUBF_NTT_SINGLE_LOGS>::shape[s]; \
+        else return SingleRow<INV, !kHasStrict, CUBF_NTT_SINGLE_LOGS>::launch[s];                 \
+    }
+    if (!v.inverse) {
+        CUBF_PICK(false)
+    } else {
+        CUBF_PICK(true)
+    }
+#undef CUBF_PICK
 }
 
 }  // namespace
 
-bool ntt_available(const NttVariant& v) { return slot(v) >= 0; }
+namespace detail {
+#if CUBF_NTT_WORD == 64
+#define CUBF_NTT_FN(name) name##_w64
+#else
+#define CUBF_NTT_FN(name) name##_w32
+#endif
 
-LaunchShape ntt_shape(const NttVariant& v) {
-    const int s = slot(v);
-    if (s < 0) return {};
-    ShapeFn const* t;
-    if (!v.inverse)
-        t = v.strided ? (v.lazy ? Rows<false, true>::Lazy::shape : Rows<false, true>::Strict::shape)
-                      : (v.lazy ? Rows<false, false>::Lazy::shape : Rows<false, false>::Strict::shape);
-    else
-        t = v.strided ? (v.lazy ? Rows<true, true>::Lazy::shape : Rows<true, true>::Strict::shape)
-                      : (v.lazy ? Rows<true, false>::Lazy::shape : Rows<true, false>::Strict::shape);
-    return t[s]();
+LaunchShape CUBF_NTT_FN(ntt_shape)(const NttVariant& v) {
+    if (v.log_n >= kNttMinLog && v.log_n <= kNttMaxLog) return pick_pass<ShapeFn, true>(v)();
+    if (v.log_n >= 1 && v.log_n <= kNttSingleMaxLog) return pick_single<ShapeFn, true>(v)();
+    return {};
 }
 
-cudaError_t launch_ntt_pass(const NttVariant& v, const std::uint64_t* in, std::uint64_t* out,
-                            const NttPolyDesc* polys, std::size_t poly_count, const NttTables& tables,
-                            bool in_is_out, bool final_pass, bool final_scale, cudaStream_t stream) {
-    const int s = slot(v);
-    if (s < 0) return cudaErrorInvalidValue;
-    LaunchFn const* t;
-    if (!v.inverse)
-        t = v.strided ? (v.lazy ? Rows<false, true>::Lazy::launch : Rows<false, true>::Strict::launch)
-                      : (v.lazy ? Rows<false, false>::Lazy::launch : Rows<false, false>::Strict::launch);
-    else
-        t = v.strided ? (v.lazy ? Rows<true, true>::Lazy::launch : Rows<true, true>::Strict::launch)
-                      : (v.lazy ? Rows<true, false>::Lazy::launch : Rows<true, false>::Strict::launch);
-    return t[s](in, out, polys, poly_count, tables, in_is_out, final_pass, final_scale, stream);
+cudaError_t CUBF_NTT_FN(launch_ntt)(const NttVariant& v, const NttLaunch& a, cudaStream_t stream) {
+    if (v.log_n >= kNttMinLog && v.log_n <= kNttMaxLog) return pick_pass<LaunchFn, false>(v)(a, stream);
+    if (v.log_n >= 1 && v.log_n <= kNttSingleMaxLog) return pick_single<LaunchFn, false>(v)(a, stream);
+    return cudaErrorInvalidValue;
 }
+#undef CUBF_NTT_FN
+}  // namespace detail
 
 }  // namespace cubf

@@ -16,6 +16,14 @@
 // of LOGE index bits are reached through shared memory.  Products use Shoup's
 // method with per-root precomputed quotients floor(w 2^64 / q), so a modular
 // multiply is one 64-bit high product and two low products; q < 2^63.
+//
+// The same passes serve the cyclic single-modulus NTT of the main ABI
+// (cuntt::Plan, include/cuntt/ntt.hpp:432): with the cyclic root schedule the
+// Cooley-Tukey passes map natural input to bit-reversed output and the
+// Gentleman-Sande passes bit-reversed input to natural output, for either
+// direction (the root table carries omega or omega^-1).  Storage words may be
+// 32 or 64 bits wide; arithmetic is 64-bit throughout.  Transforms of at most
+// 2^11 points run as one tile per transform (ntt_single_kernel).
 #pragma once
 
 #include "common.cuh"
@@ -42,6 +50,11 @@ CUBF_DEV u64 sub_mod(u64 a, u64 b, u64 q) { return a >= b ? a - b : a + q - b; }
 CUBF_DEV u64 mul_shoup_lazy(u64 a, u64 w, u64 wq, u64 q) { return a * w - __umul64hi(a, wq) * q; }
 CUBF_DEV u64 reduce_2q(u64 a, u64 q2) { return a >= q2 ? a - q2 : a; }
 CUBF_DEV u64 canonical_4q(u64 a, u64 q) { return reduce_2q(reduce_2q(a, 2 * q), q); }
+// x mod q for any 64-bit x: Shoup's product with w = 1 and uq = floor(2^64 / q)
+// estimates the quotient to within one, so one conditional subtraction
+// remains.  The main-ABI NTT reduces its input words with it, as the
+// reference's reference_ntt does (src/reference.cpp:601-603).
+CUBF_DEV u64 reduce_word(u64 x, u64 uq, u64 q) { return reduce_2q(x - __umul64hi(x, uq) * q, q); }
 
 // Per-polynomial binding of an RNS plan: offsets into the caller's buffers and
 // the domain whose modulus and root tables it uses.
@@ -58,6 +71,7 @@ struct DomainTables {
     const u64* moduli;    // [domains]
     const u64* n_inv;     // [domains] N^-1 mod q (inverse only)
     const u64* n_inv_q;   // Shoup quotient of n_inv
+    const u64* unit_q;    // [domains] floor(2^64 / q), read when input words are reduced
 };
 
 // Register group g of a tile with B index bits: registers hold the LOGE
@@ -212,10 +226,21 @@ using PassShape = NttShape<STRIDED ? strided_bits(L) : contiguous_bits(L),
 // second pass is in place); `final_pass` marks the pass that writes the
 // result (lazy variants reduce to [0, q) there), and with `final_scale` the
 // final inverse pass scales by N^-1.  LAZY requires every modulus < 2^62.
-template <int L, bool STRIDED, bool INV, bool LAZY>
+// Results are written by store_result: reduced to [0, q) on the final pass of
+// a lazy variant, scaled by N^-1 when `final_scale` is set.
+template <bool INV, bool LAZY>
+CUBF_DEV u64 final_value(u64 v, u64 q, bool final_pass, bool scale, u64 ni, u64 niq) {
+    if (scale) return mul_shoup(v, ni, niq, q);  // exact for any 64-bit v
+    if (LAZY && final_pass) return INV ? reduce_2q(v, q) : canonical_4q(v, q);
+    return v;
+}
+
+// T is the storage word (unsigned int or u64); `reduce_input` reduces each
+// loaded word modulo q first, so any 64-bit input is accepted.
+template <int L, bool STRIDED, bool INV, bool LAZY, typename T>
 __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB)
-    ntt_pass_kernel(const u64* in, u64* out, const PolyDesc* __restrict__ polys, DomainTables tab, int in_is_out,
-                    int final_pass, int final_scale) {
+    ntt_pass_kernel(const T* in, T* out, const PolyDesc* __restrict__ polys, DomainTables tab, int in_is_out,
+                    int final_pass, int final_scale, int reduce_input) {
     using S = PassShape<L, STRIDED, INV, LAZY>;
     using Gs = typename S::Gs;
     constexpr int B = S::B;
@@ -232,8 +257,8 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB)
     const u64 q = tab.moduli[pd.domain];
     const u64* roots = tab.roots + static_cast<size_t>(pd.domain) * N;
     const u64* quots = tab.quotients + static_cast<size_t>(pd.domain) * N;
-    const u64* src = in_is_out ? static_cast<const u64*>(out) + pd.out_off : in + pd.in_off;
-    u64* dst = out + pd.out_off;
+    const T* src = in_is_out ? static_cast<const T*>(out) + pd.out_off : in + pd.in_off;
+    T* dst = out + pd.out_off;
 
     int col;
     uint32_t t;
@@ -246,8 +271,8 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB)
     }
     const uint32_t tile = g * COLS + col;
     // Tile row i lives at (i << LOWB) | tile (strided) or (tile << B) | i.
-    const u64* tsrc = src + (STRIDED ? tile : (static_cast<size_t>(tile) << B));
-    u64* tdst = dst + (STRIDED ? tile : (static_cast<size_t>(tile) << B));
+    const T* tsrc = src + (STRIDED ? tile : (static_cast<size_t>(tile) << B));
+    T* tdst = dst + (STRIDED ? tile : (static_cast<size_t>(tile) << B));
     constexpr int SHIFT = STRIDED ? LOWB : 0;
     const int off = STRIDED ? 0 : L - B;
     const u64 hi = STRIDED ? 0 : static_cast<u64>(tile);
@@ -257,27 +282,69 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB)
         constexpr uint32_t R0 = Gs::reg(0);
         constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
         const uint32_t tp = deposit_rt<lowmask(B) & ~R0, B>(t);
-        const u64* ts = tsrc + (static_cast<size_t>(tp) << SHIFT);
+        const T* ts = tsrc + (static_cast<size_t>(tp) << SHIFT);
 #pragma unroll
-        for (int r = 0; r < S::E; ++r) v[r] = ts[static_cast<size_t>(O0.v[r]) << SHIFT];
+        for (int r = 0; r < S::E; ++r) v[r] = static_cast<u64>(ts[static_cast<size_t>(O0.v[r]) << SHIFT]);
+        if (reduce_input) {
+            const u64 uq = tab.unit_q[pd.domain];
+#pragma unroll
+            for (int r = 0; r < S::E; ++r) v[r] = reduce_word(v[r], uq, q);
+        }
     }
     ntt_groups<S, 0>(v, sbuf, col, t, hi, off, roots, quots, q);
     constexpr uint32_t RF = Gs::reg(Gs::COUNT - 1);
     constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
     const uint32_t tf = deposit_rt<lowmask(B) & ~RF, B>(t);
-    u64* td = tdst + (static_cast<size_t>(tf) << SHIFT);
-    if (INV && final_scale) {
-        const u64 ni = tab.n_inv[pd.domain], niq = tab.n_inv_q[pd.domain];
+    T* td = tdst + (static_cast<size_t>(tf) << SHIFT);
+    const u64 ni = final_scale ? tab.n_inv[pd.domain] : 0, niq = final_scale ? tab.n_inv_q[pd.domain] : 0;
 #pragma unroll
-        for (int r = 0; r < S::E; ++r) td[static_cast<size_t>(OF.v[r]) << SHIFT] = mul_shoup(v[r], ni, niq, q);
-    } else if (LAZY && final_pass) {
+    for (int r = 0; r < S::E; ++r)
+        td[static_cast<size_t>(OF.v[r]) << SHIFT] =
+            static_cast<T>(final_value<INV, LAZY>(v[r], q, final_pass, final_scale, ni, niq));
+}
+
+// Whole transforms of 2^L <= 2^11 points as single tiles, COLS transforms
+// per CTA, packed batch (transform p at p * 2^L), one domain.
+constexpr int single_log_e(int L) { return L < log_e_for(L) ? L : log_e_for(L); }
+constexpr int single_cols(int L) { return 256 >> (L - single_log_e(L)); }
+template <int L, bool INV, bool LAZY>
+using SingleShape = NttShape<L, single_log_e(L), single_cols(L), false, INV, LAZY>;
+
+template <int L, bool INV, bool LAZY, typename T>
+__global__ void __launch_bounds__(SingleShape<L, INV, LAZY>::TPB)
+    ntt_single_kernel(const T* in, T* out, size_t count, DomainTables tab, int final_scale, int reduce_input) {
+    using S = SingleShape<L, INV, LAZY>;
+    using Gs = typename S::Gs;
+    constexpr size_t N = size_t{1} << L;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    u64* sbuf = reinterpret_cast<u64*>(smem_raw);
+    const int col = threadIdx.x / S::TPT;
+    const uint32_t t = threadIdx.x % S::TPT;
+    const size_t p = static_cast<size_t>(blockIdx.x) * S::COLS + col;
+    const bool active = p < count;  // idle columns still take part in the block barriers
+    const u64 q = tab.moduli[0];
+
+    u64 v[S::E];
+    {
+        constexpr uint32_t R0 = Gs::reg(0);
+        constexpr Offsets<S::E> O0 = make_offsets<S::E>(R0);
+        const T* ts = in + p * N + deposit_rt<lowmask(L) & ~R0, L>(t);
+        const u64 uq = reduce_input ? tab.unit_q[0] : 0;
 #pragma unroll
-        for (int r = 0; r < S::E; ++r)
-            td[static_cast<size_t>(OF.v[r]) << SHIFT] = INV ? reduce_2q(v[r], q) : canonical_4q(v[r], q);
-    } else {
-#pragma unroll
-        for (int r = 0; r < S::E; ++r) td[static_cast<size_t>(OF.v[r]) << SHIFT] = v[r];
+        for (int r = 0; r < S::E; ++r) {
+            v[r] = active ? static_cast<u64>(ts[O0.v[r]]) : 0;
+            if (reduce_input) v[r] = reduce_word(v[r], uq, q);
+        }
     }
+    ntt_groups<S, 0>(v, sbuf, col, t, 0, 0, tab.roots, tab.quotients, q);
+    if (!active) return;
+    constexpr uint32_t RF = Gs::reg(Gs::COUNT - 1);
+    constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
+    T* td = out + p * N + deposit_rt<lowmask(L) & ~RF, L>(t);
+    const u64 ni = final_scale ? tab.n_inv[0] : 0, niq = final_scale ? tab.n_inv_q[0] : 0;
+#pragma unroll
+    for (int r = 0; r < S::E; ++r)
+        td[OF.v[r]] = static_cast<T>(final_value<INV, LAZY>(v[r], q, true, final_scale, ni, niq));
 }
 
 }  // namespace cubf::ntt

@@ -180,6 +180,80 @@ void compositions(int total, int first_max, int rest_max, int max_parts, std::ve
 
 }  // namespace
 
+void resolve_orders(PlanRequest& r) {
+    const Descriptor& d = r.d;
+    const bool rin = !d.input_orders.empty() && d.input_orders[0] == CUBUTTERFLY_ORDER_BIT_REVERSED;
+    const bool rout = !d.output_orders.empty() && d.output_orders[0] == CUBUTTERFLY_ORDER_BIT_REVERSED;
+    r.permute_input = r.permute_output = r.ntt_gs = false;
+    switch (d.op) {
+        case CUBUTTERFLY_OPERATOR_FFT:
+            r.permute_input = rin;
+            r.permute_output = rout;
+            break;
+        case CUBUTTERFLY_OPERATOR_NTT:
+            // (N, R): CT.  (R, N): GS.  (N, N): permute, then bit-reversed
+            // input -> GS.  (R, R): permute, then natural input -> CT.
+            r.permute_input = rin == rout;
+            r.ntt_gs = rin != rout ? rin : !rin;
+            r.ntt_word32 = d.storage == CUBUTTERFLY_DATA_UINT32;
+            r.ntt_lazy = d.modulus < (std::uint64_t{1} << 62);
+            break;
+        default:
+            r.permute_output = rin != rout;
+            break;
+    }
+}
+
+namespace {
+double permutation_us(const PlanRequest& r, const HardwareProfile& hw, double elem_bytes) {
+    const double bytes = 2.0 * static_cast<double>(r.d.batch) * std::ldexp(1.0, r.log_n) * elem_bytes;
+    return bytes / (hw.hbm_gbs * 1e3 * 0.8) + hw.launch_us;
+}
+void add_boundary(Mapping& m, const PlanRequest& r, const HardwareProfile& hw) {
+    m.permute_input = r.permute_input;
+    m.permute_output = r.permute_output;
+    const double esz = static_cast<double>(storage_bytes(r.d.storage));
+    m.predicted_us += (m.permute_input ? permutation_us(r, hw, esz) : 0.0) +
+                      (m.permute_output ? permutation_us(r, hw, esz) : 0.0);
+}
+}  // namespace
+
+Mapping ntt_mapping(const PlanRequest& r, const HardwareProfile& hw) {
+    Mapping m;
+    m.family = r.ntt_gs ? "ntt-tile-gs" : "ntt-tile-ct";
+    const int l = r.log_n;
+    const double elems = static_cast<double>(r.d.batch) * std::ldexp(1.0, l);
+    const double esz = r.ntt_word32 ? 4.0 : 8.0;
+    // 64-bit Shoup butterflies: ~20 integer issue slots per element and stage
+    // on the half-rate integer pipe
+    const double alu = r.ntt_lazy ? 40.0 : 48.0;
+    auto add = [&](PassKind kind, int bits, int inner, bool strided) {
+        Pass p;
+        p.kind = kind;
+        p.log_h = bits;
+        p.log_inner = inner;
+        p.shape = ntt_shape({l, strided, r.ntt_gs, r.ntt_lazy, r.ntt_word32});
+        if (!fits(p.shape, hw)) throw Unsupported("NTT tile does not fit the device");
+        m.predicted_us += pass_time_us(hw, elems, esz, 8.0, bits, p.shape.exchanges, alu, 0.85);
+        m.passes.push_back(p);
+    };
+    if (ntt_single_available(l)) {
+        add(PassKind::NttSingle, l, 0, false);
+    } else if (ntt_available({l, true, r.ntt_gs, r.ntt_lazy, r.ntt_word32})) {
+        const int sb = ntt_pass_bits(l, true), cb = ntt_pass_bits(l, false);
+        if (!r.ntt_gs) {
+            add(PassKind::NttStrided, sb, cb, true);
+            add(PassKind::NttContiguous, cb, 0, false);
+        } else {
+            add(PassKind::NttContiguous, cb, 0, false);
+            add(PassKind::NttStrided, sb, cb, true);
+        }
+    } else {
+        throw Unsupported("NTT length must be 2^1 .. 2^" + std::to_string(kNttMaxLog) + " in this build");
+    }
+    return m;
+}
+
 Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts) {
     Mapping m;
     m.family = "fft-stockham-global";
@@ -205,7 +279,8 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
         ns += bits;
     }
     require(ns == r.log_n, "FFT passes must cover every stage exactly once");
-    const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
+    // a permuted input lands in the output buffer and the passes run in place
+    const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE || r.permute_input;
     const std::size_t bytes = d.batch * (std::size_t{1} << r.log_n) * 8;
     m.workspace_bytes = bytes * ((in_place && parts.size() % 2 == 1) ? 2 : 1);
     return m;
@@ -213,21 +288,30 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
 
 std::string Mapping::name() const {
     std::ostringstream o;
+    if (permute_input) o << "bitrev+";
     o << family << "[";
     for (std::size_t i = 0; i < passes.size(); ++i) {
         if (i) o << "+";
         o << passes[i].log_h;
     }
     o << "]";
+    if (permute_output) o << "+bitrev";
     return o.str();
 }
 
 Json Mapping::to_json() const {
     Json ps = Json::array();
     for (const auto& p : passes) {
-        ps.push_back({{"kernel", p.kind == PassKind::FftLocal    ? "fft_local"
-                                 : p.kind == PassKind::FftGlobal ? "fft_global_pass"
-                                                                 : "bitwise_tile"},
+        const char* kernel = "bitwise_tile";
+        switch (p.kind) {
+            case PassKind::FftLocal: kernel = "fft_local"; break;
+            case PassKind::FftGlobal: kernel = "fft_global_pass"; break;
+            case PassKind::NttStrided: kernel = "ntt_pass_strided"; break;
+            case PassKind::NttContiguous: kernel = "ntt_pass_contiguous"; break;
+            case PassKind::NttSingle: kernel = "ntt_single"; break;
+            default: break;
+        }
+        ps.push_back({{"kernel", kernel},
                       {"log_h", p.log_h},
                       {"log_w", p.log_w},
                       {"log_inner", p.log_inner},
@@ -241,12 +325,28 @@ Json Mapping::to_json() const {
             {"family", family},
             {"name", name()},
             {"passes", ps},
+            {"boundary", {{"input_bit_reversal", permute_input}, {"output_bit_reversal", permute_output}}},
             {"workspace_bytes", workspace_bytes},
             {"predicted_us", predicted_us}};
 }
 
+namespace {
+std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile& hw);
+}
+
 std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw) {
+    std::vector<Mapping> out = enumerate_core(r, hw);
+    for (auto& m : out) add_boundary(m, r, hw);
+    return out;
+}
+
+namespace {
+std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile& hw) {
     std::vector<Mapping> out;
+    if (r.d.op == CUBUTTERFLY_OPERATOR_NTT) {
+        out.push_back(ntt_mapping(r, hw));
+        return out;
+    }
     const Descriptor& d = r.d;
     if (d.op == CUBUTTERFLY_OPERATOR_FFT && (r.log_n > kFftLocalMaxLog || r.log_v > 0)) {
         if (r.log_n < kFftPassMinLog)
@@ -303,8 +403,20 @@ std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProf
                      [](const Mapping& a, const Mapping& b) { return a.predicted_us < b.predicted_us; });
     return out;
 }
+}  // namespace
+
+namespace {
+Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::string& text);
+}
 
 Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::string& text) {
+    Mapping m = parse_core(r, hw, text);
+    add_boundary(m, r, hw);
+    return m;
+}
+
+namespace {
+Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::string& text) {
     std::vector<int> parts;
     if (!text.empty() && text.front() == '{') {
         const Json j = Json::parse(text);
@@ -328,10 +440,18 @@ Mapping parse_explicit_mapping(const PlanRequest& r, const HardwareProfile& hw, 
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
         if (r.log_n > kFftLocalMaxLog || r.log_v > 0) return fft_global_mapping(r, hw, parts);
         require(parts.size() == 1 && parts[0] == r.log_n, "FFT up to 2^13 is one local pass of log N bits");
-        return enumerate_mappings(r, hw).front();
+        return enumerate_core(r, hw).front();
+    }
+    if (r.d.op == CUBUTTERFLY_OPERATOR_NTT) {
+        Mapping m = ntt_mapping(r, hw);
+        std::vector<int> planned;
+        for (const auto& p : m.passes) planned.push_back(p.log_h);
+        if (parts != planned) throw Unsupported("explicit NTT mapping must be the planned pass split " + m.name());
+        return m;
     }
     if (r.bw_op == BwOp::Fwht) require(parts.size() == 1, "FWHT executes as a single tile pass");
     return bitwise_mapping(r, hw, parts);
 }
+}  // namespace
 
 }  // namespace cubf

@@ -43,7 +43,7 @@ struct HardwareProfile {
 HardwareProfile resolve_profile();
 HardwareProfile profile_from_json(const Json& j);
 
-enum class PassKind { FftLocal, FftGlobal, BitwiseTile };
+enum class PassKind { FftLocal, FftGlobal, BitwiseTile, NttStrided, NttContiguous, NttSingle };
 
 struct Pass {
     PassKind kind = PassKind::BitwiseTile;
@@ -54,8 +54,12 @@ struct Pass {
 };
 
 struct Mapping {
-    std::string family;  // "fft-stockham-local", "fwht-tile", "zeta-tile"
+    std::string family;  // "fft-stockham-local", "fwht-tile", "zeta-tile", "ntt-tile-ct", ...
     std::vector<Pass> passes;
+    // Logical-order boundary: bit-reversal permutation of the input before
+    // the first pass and of the output after the last.
+    bool permute_input = false;
+    bool permute_output = false;
     std::size_t workspace_bytes = 0;
     double predicted_us = 0.0;
     std::string name() const;
@@ -70,8 +74,32 @@ struct PlanRequest {
     int log_v = 0;
     BwType bw_type = BwType::F32;
     BwOp bw_op = BwOp::Fwht;
+    // Bit-reversal permutations the logical orders require (see
+    // boundary_permutations); a permuted input makes the core run in place.
+    bool permute_input = false;
+    bool permute_output = false;
+    // NTT: Gentleman-Sande passes (bit-reversed input to natural output)
+    // instead of Cooley-Tukey (natural input to bit-reversed output).
+    bool ntt_gs = false;
+    bool ntt_word32 = false;  // uint32 storage
+    bool ntt_lazy = false;    // modulus < 2^62
 };
 
+// Fill the order-dependent fields of a request from its descriptor:
+//   FFT            bit-reversed input / output -> permute before / after;
+//   FWHT, zeta     both commute with bit reversal (H and the subset order are
+//                  invariant under reversing the bit positions), so equal
+//                  orders need nothing and unequal ones one permutation of
+//                  the output;
+//   NTT            natural -> bit-reversed runs Cooley-Tukey, bit-reversed ->
+//                  natural Gentleman-Sande; equal orders permute the input
+//                  and then run Gentleman-Sande (natural) or Cooley-Tukey
+//                  (bit-reversed).
+void resolve_orders(PlanRequest& r);
+
+// The NTT passes of the request (one whole-transform tile up to 2^11, else
+// the strided and contiguous passes in execution order).
+Mapping ntt_mapping(const PlanRequest& r, const HardwareProfile& hw);
 // Multi-pass global FFT with the given radix bits per pass.
 Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts);
 // Every legal mapping of the request, ranked best first by the static model.

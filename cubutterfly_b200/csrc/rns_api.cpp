@@ -11,6 +11,7 @@
 
 #include "descriptor.hpp"
 #include "kernels.hpp"
+#include "modarith.hpp"
 #include "planner.hpp"
 
 #include <cuda_runtime_api.h>
@@ -32,7 +33,6 @@
 namespace {
 
 using u64 = std::uint64_t;
-using u128 = unsigned __int128;
 using cubf::Json;
 
 thread_local std::string last_error;
@@ -47,47 +47,11 @@ void check(cudaError_t e, const char* what) {
     }
 }
 
-u64 mulmod(u64 a, u64 b, u64 q) { return static_cast<u64>(static_cast<u128>(a) * b % q); }
-u64 powmod(u64 b, u64 e, u64 q) {
-    u64 r = 1 % q;
-    b %= q;
-    for (; e; e >>= 1, b = mulmod(b, b, q))
-        if (e & 1) r = mulmod(r, b, q);
-    return r;
-}
-// Deterministic Miller-Rabin for 64-bit integers.
-bool is_prime(u64 n) {
-    if (n < 2) return false;
-    for (u64 p : {2ull, 3ull, 5ull, 7ull, 11ull, 13ull, 17ull, 19ull, 23ull, 29ull, 31ull, 37ull})
-        if (n % p == 0) return n == p;
-    u64 d = n - 1;
-    int s = 0;
-    while (!(d & 1)) {
-        d >>= 1;
-        ++s;
-    }
-    for (u64 a : {2ull, 325ull, 9375ull, 28178ull, 450775ull, 9780504ull, 1795265022ull}) {
-        if (a % n == 0) continue;
-        u64 x = powmod(a, d, n);
-        if (x == 1 || x == n - 1) continue;
-        bool ok = false;
-        for (int r = 1; r < s; ++r) {
-            x = mulmod(x, x, n);
-            if (x == n - 1) {
-                ok = true;
-                break;
-            }
-        }
-        if (!ok) return false;
-    }
-    return true;
-}
-u64 shoup(u64 w, u64 q) { return static_cast<u64>((static_cast<u128>(w) << 64) / q); }
-std::size_t bitrev(std::size_t x, int bits) {
-    std::size_t r = 0;
-    for (int i = 0; i < bits; ++i, x >>= 1) r = (r << 1) | (x & 1);
-    return r;
-}
+using cubf::modarith::bitrev;
+using cubf::modarith::is_prime;
+using cubf::modarith::mulmod;
+using cubf::modarith::powmod;
+using cubf::modarith::shoup;
 
 struct Domain {
     u64 modulus = 0;
@@ -331,23 +295,31 @@ struct cubutterflyRnsPlanOpaque {
         const std::size_t count = config.polynomials.size();
         const bool inv = config.inverse;
         const cubf::NttVariant first{l, !inv, inv, lazy}, second{l, inv, inv, lazy};
+        cubf::NttLaunch a1, a2;
+        a1.count = a2.count = count;
+        a1.tables = a2.tables = tables;
+        a2.final_pass = true;
+        a2.final_scale = inv;
         if (needs_scratch) {
+            // pass 1 into private scratch; pass 2 reads scratch (its out_off)
+            // and writes the caller's output
             u64* tmp = scratch.as<u64>();
-            check(cubf::launch_ntt_pass(first, in, tmp, polys_scratch.as<cubf::NttPolyDesc>(), count, tables, false,
-                                        false, false, stream),
-                  "pass 1 launch");
-            // pass 2 reads scratch (its out_off) and writes the caller's output
-            check(cubf::launch_ntt_pass(second, tmp, out, polys_scratch_to_out(), count, tables, false, true, inv,
-                                        stream),
-                  "pass 2 launch");
-            return;
+            a1.in = in;
+            a1.out = tmp;
+            a1.polys = polys_scratch.as<cubf::NttPolyDesc>();
+            a2.in = tmp;
+            a2.out = out;
+            a2.polys = polys_scratch_to_out();
+        } else {
+            a1.in = in;
+            a1.out = out;
+            a1.polys = a2.polys = polys.as<cubf::NttPolyDesc>();
+            a2.in = out;
+            a2.out = out;
+            a2.in_is_out = true;
         }
-        check(cubf::launch_ntt_pass(first, in, out, polys.as<cubf::NttPolyDesc>(), count, tables, false, false, false,
-                                    stream),
-              "pass 1 launch");
-        check(cubf::launch_ntt_pass(second, out, out, polys.as<cubf::NttPolyDesc>(), count, tables, true, true, inv,
-                                    stream),
-              "pass 2 launch");
+        check(cubf::launch_ntt(first, a1, stream), "pass 1 launch");
+        check(cubf::launch_ntt(second, a2, stream), "pass 2 launch");
     }
 
     DeviceBuffer polys_s2o;

@@ -149,9 +149,12 @@ class Oracle:
         return [int(v) for v in out[:got]]
 
     def ntt_cyclic(self, x: np.ndarray, q: int, inverse=False) -> np.ndarray:
+        """Cyclic NTT of every row of x (natural in, natural out)."""
         y = np.ascontiguousarray(x, dtype=np.uint64).copy()
-        if self.lib.cubf_oracle_ntt_cyclic(_ptr(y), y.shape[-1], q, int(inverse)):
-            raise ValueError("oracle NTT rejected its input")
+        n = y.shape[-1]
+        for row in y.reshape(-1, n):
+            if self.lib.cubf_oracle_ntt_cyclic(_ptr(row), n, q, int(inverse)):
+                raise ValueError("oracle NTT rejected its input")
         return y
 
     def rns_ntt(self, x: np.ndarray, moduli, roots, negacyclic=True, inverse=False,
@@ -188,6 +191,7 @@ class Reference:
         L.cubf_ref_find_root.argtypes = [ct.c_uint, _u64]
         L.cubf_ref_find_root.restype = _u64
         L.cubf_ref_negacyclic_ntt.argtypes = [_p, _p, ct.c_uint, _n, _p, _i]
+        L.cubf_ref_ntt_cyclic.argtypes = [_p, _n, _n, _u64, _i, _i]
 
     @staticmethod
     def available(path: os.PathLike | None = None) -> bool:
@@ -244,3 +248,11 @@ class Reference:
         if self.lib.cubf_ref_negacyclic_ntt(_ptr(x), _ptr(out), n.bit_length() - 1, count, _ptr(m), threads):
             raise ValueError("reference NTT failed")
         return out
+
+    def ntt_cyclic(self, x, q, inverse=False, threads=1):
+        """reference_ntt over the rows of x (natural in, natural out)."""
+        y = np.ascontiguousarray(x, dtype=np.uint64).copy()
+        n = y.shape[-1]
+        if self.lib.cubf_ref_ntt_cyclic(_ptr(y), n, y.size // n, q, int(inverse), threads):
+            raise ValueError("reference NTT failed")
+        return y

@@ -168,5 +168,22 @@ int cubf_ref_negacyclic_ntt(const std::uint64_t* in, std::uint64_t* out, unsigne
     return 0;
 }
 
-int cubf_ref_abi_version(void) { return 1; }
+// The reference's cyclic reference_ntt (src/reference.cpp:584-630) on each of
+// `batch` packed transforms: natural in, natural out, root
+// find_primitive_power_of_two_root(log n, q), inverse scaled by n^-1.
+int cubf_ref_ntt_cyclic(std::uint64_t* data, std::size_t n, std::size_t batch, std::uint64_t q, int inverse,
+                        int threads) {
+    try {
+        parallel_for(batch, threads, [&](std::size_t b) {
+            std::vector<std::uint64_t> v(data + n * b, data + n * (b + 1));
+            cuntt::reference_ntt(v, q, inverse != 0);
+            std::copy(v.begin(), v.end(), data + n * b);
+        });
+    } catch (...) {
+        return 1;
+    }
+    return 0;
+}
+
+int cubf_ref_abi_version(void) { return 2; }
 }

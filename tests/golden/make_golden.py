@@ -68,6 +68,20 @@ def main() -> None:
     out["ntt_neg_4096_in"] = xs
     out["ntt_neg_4096_out"] = ref.negacyclic_ntt(xs, qs)
 
+    # Cyclic single-modulus NTT, reference_ntt (reference.cpp:584-630): natural
+    # in, natural out, forward and inverse; the default modulus
+    # (include/cuntt/ntt.hpp:17) and the word32 / word64 workload moduli of the
+    # reference's NTT rows.  Inputs are full-width words, so the reduction of
+    # non-canonical input is pinned too.
+    for q, bits in ((1152921504606584833, 64), (576460756061519873, 64), (2013265921, 32), (998244353, 32)):
+        for n in (2, 16, 2048, 4096):
+            g = w.rng(20 + n + bits)
+            x = g.integers(0, 1 << bits, size=(3, n), dtype=np.uint64)
+            x[0, :2] = [q, (1 << bits) - 1]  # words at and above the modulus
+            out[f"ntt_cyc_{q}_{n}_in"] = x
+            out[f"ntt_cyc_{q}_{n}_fwd"] = ref.ntt_cyclic(x, q)
+            out[f"ntt_cyc_{q}_{n}_inv"] = ref.ntt_cyclic(x, q, inverse=True)
+
     # Known answers quoted from the reference's C ABI test (tests/test_c_api.c:698):
     # FWHT of 1..8 is {36, -4, -8, 0, -16, 0, 0, 0}.
     out["kat_fwht_8_in"] = np.arange(1, 9, dtype=np.float32)

@@ -192,6 +192,72 @@ def test_interleaved_fft_batches_are_planned_as_global_passes(lib):
     assert "layout-lowering" in [g["code"] for g in capabilities(lib, odd)["gaps"]]
 
 
+def ntt_transform(n, batch=1, modulus=cb.DEFAULT_MODULUS, inverse=False, word32=False, orders=None, **kw):
+    storage = cb.DataType.UINT32 if word32 else cb.DataType.UINT64
+    t = cb.Transform(op=cb.Operator.NTT, storage=storage, extents=[n], batch=batch, modulus=modulus,
+                     word_bits=32 if word32 else 64, inverse=inverse, **kw)
+    if orders is not None:
+        t.input_orders, t.output_orders = [orders[0]], [orders[1]]
+    return t
+
+
+N, R = cb.LogicalOrder.NATURAL, cb.LogicalOrder.BIT_REVERSED
+
+
+@pytest.mark.parametrize("orders, family, permute", [
+    ((N, R), "ntt-tile-ct", False), ((R, N), "ntt-tile-gs", False),
+    ((N, N), "ntt-tile-gs", True), ((R, R), "ntt-tile-ct", True)])
+def test_ntt_planner_orders(lib, orders, family, permute):
+    """Cooley-Tukey passes map natural to bit-reversed order, Gentleman-Sande
+    passes the reverse; equal orders permute the input first."""
+    t = ntt_transform(1 << 16, 4, orders=orders)
+    assert capabilities(lib, t)["status"] == "eligible"
+    (m,) = rank(lib, t)
+    assert m["family"] == family and m["boundary"]["input_bit_reversal"] == permute
+    assert not m["boundary"]["output_bit_reversal"] and m["workspace_bytes"] == 0
+    kinds = [p["kernel"] for p in m["passes"]]
+    assert kinds == (["ntt_pass_strided", "ntt_pass_contiguous"] if family.endswith("ct")
+                     else ["ntt_pass_contiguous", "ntt_pass_strided"])
+    assert sorted(p["log_h"] for p in m["passes"]) == [8, 8]
+
+
+def test_ntt_planner_lengths_and_words(lib):
+    for log_n in range(1, 12):
+        (m,) = rank(lib, ntt_transform(1 << log_n, 3))
+        assert [p["kernel"] for p in m["passes"]] == ["ntt_single"] and m["passes"][0]["log_h"] == log_n
+    (m,) = rank(lib, ntt_transform(1 << 17, 2, modulus=2013265921, word32=True))
+    # natural orders: permuted input, Gentleman-Sande (contiguous pass first)
+    assert m["name"] == "bitrev+ntt-tile-gs[8+9]"
+    big = capabilities(lib, ntt_transform(1 << 21))
+    assert "length-lowering" in [g["code"] for g in big["gaps"]]
+    strided = capabilities(lib, ntt_transform(64, input_strides=[2]))
+    assert "layout-lowering" in [g["code"] for g in strided["gaps"]]
+
+
+@pytest.mark.parametrize("op, storage, orders, boundary", [
+    (cb.Operator.FFT, cb.DataType.COMPLEX_FP32, (R, N), (True, False)),
+    (cb.Operator.FFT, cb.DataType.COMPLEX_FP32, (R, R), (True, True)),
+    (cb.Operator.FWHT, cb.DataType.FP32, (R, R), (False, False)),
+    (cb.Operator.FWHT, cb.DataType.FP32, (N, R), (False, True)),
+    (cb.Operator.SUBSET_ZETA, cb.DataType.UINT32, (R, N), (False, True)),
+    (cb.Operator.SUPERSET_ZETA, cb.DataType.UINT64, (R, R), (False, False))])
+def test_logical_order_boundary(lib, op, storage, orders, boundary):
+    """FFT permutes each bit-reversed side; FWHT and zeta commute with bit
+    reversal, so only unequal orders cost one output permutation."""
+    t = cb.Transform(op=op, storage=storage, extents=[1024], batch=2, input_orders=[orders[0]],
+                     output_orders=[orders[1]])
+    assert capabilities(lib, t)["status"] == "eligible"
+    m = rank(lib, t)[0]
+    assert (m["boundary"]["input_bit_reversal"], m["boundary"]["output_bit_reversal"]) == boundary
+    assert m["name"].startswith("bitrev+") == boundary[0] and m["name"].endswith("+bitrev") == boundary[1]
+
+
+def test_bit_reversed_orders_need_packed_batches(lib):
+    t = cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=64, input_strides=[64], output_strides=[64],
+                     input_batch_stride=1, output_batch_stride=1, output_orders=[R])
+    assert "order-lowering" in [g["code"] for g in capabilities(lib, t)["gaps"]]
+
+
 def test_planner_respects_hardware_profile(lib):
     """A device with little shared memory cannot take the 14-bit contiguous zeta tile."""
     t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << 24], batch=16)

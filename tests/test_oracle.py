@@ -82,6 +82,32 @@ def test_negacyclic_ntt_round_trip_and_linearity(oracle):
     assert np.array_equal(fs, expect)
 
 
+NTT_MODULI = (1152921504606584833, 576460756061519873, 2013265921, 998244353)
+
+
+@pytest.mark.parametrize("q", NTT_MODULI)
+@pytest.mark.parametrize("n", [2, 16, 2048, 4096])
+def test_cyclic_ntt_matches_golden(oracle, golden, q, n):
+    """The cyclic restatement equals the reference's reference_ntt bit for bit,
+    including the reduction of input words at and above the modulus."""
+    x = golden[f"ntt_cyc_{q}_{n}_in"]
+    assert np.array_equal(oracle.ntt_cyclic(x, q), golden[f"ntt_cyc_{q}_{n}_fwd"])
+    assert np.array_equal(oracle.ntt_cyclic(x, q, inverse=True), golden[f"ntt_cyc_{q}_{n}_inv"])
+
+
+def test_cyclic_ntt_round_trip_and_convolution(oracle):
+    q, n = 998244353, 64
+    g = w.rng(30)
+    a = g.integers(0, q, size=n, dtype=np.uint64)
+    b = g.integers(0, q, size=n, dtype=np.uint64)
+    assert np.array_equal(oracle.ntt_cyclic(oracle.ntt_cyclic(a, q), q, inverse=True), a)
+    # pointwise product of transforms = transform of the cyclic convolution
+    fa, fb = oracle.ntt_cyclic(a, q).astype(object), oracle.ntt_cyclic(b, q).astype(object)
+    conv = [sum(int(a[j]) * int(b[(k - j) % n]) for j in range(n)) % q for k in range(n)]
+    got = oracle.ntt_cyclic(np.array((fa * fb) % q, dtype=np.uint64), q, inverse=True)
+    assert [int(v) for v in got] == conv
+
+
 def test_rns_primes_and_roots(oracle):
     qs = w.rns_primes()
     assert qs == oracle.rns_primes(17, 32)
@@ -107,3 +133,7 @@ def test_restatement_matches_reference_random(oracle, reference):
     x = w.ntt_input(qs, 13, seed=9)
     roots = [reference.find_root(14, q) for q in qs]
     assert np.array_equal(oracle.rns_ntt(x, qs, roots), reference.negacyclic_ntt(x, qs))
+    for q in (NTT_MODULI[0], NTT_MODULI[3]):
+        x = w.rng(31).integers(0, 1 << 63, size=(2, 1024), dtype=np.uint64)
+        for inverse in (False, True):
+            assert np.array_equal(oracle.ntt_cyclic(x, q, inverse), reference.ntt_cyclic(x, q, inverse))

@@ -576,6 +576,19 @@ def measure_ops(cb, lib, dev, stream, peak, steps, warmup):
         b = 2 * w.NTT_LIMBS * (1 << w.NTT_LOG_N) * 8
         ops["rns_ntt_u64_32x2^16"] = {"gbs": round(b / ms / 1e6, 1), "frac": round(b / ms / 1e6 / peak, 4),
                                       "us": round(ms * 1e3, 2), "algorithm": "b200_two_pass_tile"}
+    # the same shape as one cyclic single-modulus NTT plan of the main ABI:
+    # natural -> bit-reversed (two passes) and natural -> natural (a
+    # bit-reversal permutation first)
+    q = 576460756061519873
+    for tag, out_order in (("nr", cb.LogicalOrder.BIT_REVERSED), ("nn", cb.LogicalOrder.NATURAL)):
+        t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[1 << w.NTT_LOG_N],
+                         batch=w.NTT_LIMBS, modulus=q, output_orders=[out_order])
+        with cb.Plan(lib, t, stream=sp) as p:
+            ms = time_launches(lambda i: p.execute(ins[i % 16].data_ptr(), out.data_ptr()), stream, steps * 4,
+                               warmup)
+            ops[f"ntt_cyclic_u64_32x2^16_{tag}"] = {"gbs": round(b / ms / 1e6, 1),
+                                                    "frac": round(b / ms / 1e6 / peak, 4),
+                                                    "us": round(ms * 1e3, 2), "algorithm": p.algorithm_name()}
     del ins, out
     # config 4 on one GPU: one 2^30-point FFT (8 GiB in, 8 GiB out, 8 GiB workspace), multi-pass plan
     n = 1 << 30

@@ -168,3 +168,21 @@ def test_fwht_and_zeta_bit_reversed_orders(lib, oracle, cuda, orders):
             assert rel_l2(got, want) <= 1e-6, name
         else:
             assert np.array_equal(got, want), name
+
+
+@pytest.mark.parametrize("q, bits", [(2013265921, 32), (576460756061519873, 64)])
+@pytest.mark.parametrize("inverse", [False, True])
+@pytest.mark.parametrize("layout", [cb.NttLayout.NATURAL, cb.NttLayout.BIT_REVERSED])
+def test_ntt_legacy_output_layout(lib, oracle, cuda, q, bits, inverse, layout):
+    """The reference C test's output-order case (N = 8, batch 2, word32 and
+    word64, forward and inverse) through the legacy SetNttLayouts call."""
+    from gpu_util import run
+
+    x = (np.arange(16, dtype=np.uint64).reshape(2, 8) * 12345 + 7) % q
+    t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT32 if bits == 32 else cb.DataType.UINT64,
+                     extents=[8], batch=2, modulus=q, word_bits=bits, inverse=inverse, output_order=layout)
+    got, _ = run(lib, t, x.astype(np.uint32 if bits == 32 else np.uint64), cuda)
+    want = oracle.ntt_cyclic(x, q, inverse)
+    if layout == cb.NttLayout.BIT_REVERSED:
+        want = permute(want, 8)
+    assert np.array_equal(got.astype(np.uint64), want)

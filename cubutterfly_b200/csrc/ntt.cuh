@@ -125,6 +125,10 @@ struct NttShape {
             return col * (TILE + TILE / 16) + static_cast<int>(i + (i >> 4));
     }
     static constexpr int SMEM_BYTES = (STRIDED ? TILE * COLS : COLS * (TILE + TILE / 16)) * 8;
+    // Up to 16 residues per thread fit in 64 registers: asking for
+    // 1024 / TPB resident CTAs caps the kernel there, so a 32 x 2^16 pass
+    // (131072 threads) runs as one wave instead of 1.15 (80 registers).
+    static constexpr int MINB = (E <= 16 && TPB <= 1024) ? 1024 / TPB : 1;
 };
 
 // Butterflies of group G on the registers of one thread.  i = tpart | (r << lo)
@@ -238,7 +242,7 @@ CUBF_DEV u64 final_value(u64 v, u64 q, bool final_pass, bool scale, u64 ni, u64 
 // T is the storage word (unsigned int or u64); `reduce_input` reduces each
 // loaded word modulo q first, so any 64-bit input is accepted.
 template <int L, bool STRIDED, bool INV, bool LAZY, typename T>
-__global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB)
+__global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB, PassShape<L, STRIDED, INV, LAZY>::MINB)
     ntt_pass_kernel(const T* in, T* out, const PolyDesc* __restrict__ polys, DomainTables tab, int in_is_out,
                     int final_pass, int final_scale, int reduce_input) {
     using S = PassShape<L, STRIDED, INV, LAZY>;
@@ -311,7 +315,7 @@ template <int L, bool INV, bool LAZY>
 using SingleShape = NttShape<L, single_log_e(L), single_cols(L), false, INV, LAZY>;
 
 template <int L, bool INV, bool LAZY, typename T>
-__global__ void __launch_bounds__(SingleShape<L, INV, LAZY>::TPB)
+__global__ void __launch_bounds__(SingleShape<L, INV, LAZY>::TPB, SingleShape<L, INV, LAZY>::MINB)
     ntt_single_kernel(const T* in, T* out, size_t count, DomainTables tab, int final_scale, int reduce_input) {
     using S = SingleShape<L, INV, LAZY>;
     using Gs = typename S::Gs;

@@ -51,7 +51,9 @@ def parse():
                         "transforms of 4096 points split over the ranks (strong scaling)")
     p.add_argument("--log-batch", type=int, default=20, help="fftbatch total batch (log2)")
     p.add_argument("--log-n", type=int, default=30, help="fft4step transform length (log2)")
-    p.add_argument("--mapping", default="", help="explicit mapping for --only fft1g / --workload fft4step (1 GPU)")
+    p.add_argument("--mapping", default="",
+                   help="explicit mapping for --only fwht4096 / fft1g and --workload fft4step (1 GPU), "
+                        "e.g. 'fwht-tcgen05[6+6]' for the tensor-core FWHT")
     args = p.parse_args()
     if args.steps is None:
         args.steps = 20 if args.workload in ("fft4step", "fftbatch") and not args.only else 4000
@@ -204,7 +206,8 @@ def only_op(args):
         x = w.torch_fwht_input(ROWS, COLS, dev)
         y = torch.empty_like(x)
         n = COLS if args.only == "fwht4096" else HEAD
-        p = cb.Plan(lib, fwht_transform(cb, n, ROWS * COLS // n, 1 / math.sqrt(n)), stream=sp)
+        opts = cb.PlanOptions(mapping=args.mapping) if args.mapping else None
+        p = cb.Plan(lib, fwht_transform(cb, n, ROWS * COLS // n, 1 / math.sqrt(n)), options=opts, stream=sp)
         fn, nbytes = (lambda i: p.execute(x.data_ptr(), y.data_ptr())), PASS_BYTES
     elif args.only == "fft":
         x = w.torch_fft_input(w.FFT_N, w.FFT_BATCH, dev)
@@ -545,6 +548,18 @@ def measure_ops(cb, lib, dev, stream, peak, steps, warmup):
 
     sp = stream.cuda_stream
     ops = {}
+    # config 1 pass A on the tensor cores (tcgen05 mapping, H_64 (x) H_64): two rotating 128 MiB inputs
+    xa = w.torch_fwht_input(ROWS, COLS, dev, seed=0)
+    xb = w.torch_fwht_input(ROWS, COLS, dev, seed=1)
+    y = torch.empty_like(xa)
+    with cb.Plan(lib, fwht_transform(cb, COLS, ROWS, 1 / 64), options=cb.PlanOptions(mapping="fwht-tcgen05[6+6]"),
+                 stream=sp) as p:
+        ms = time_launches(lambda i: p.execute((xb if i % 2 else xa).data_ptr(), y.data_ptr()), stream, steps,
+                           warmup)
+        ops["fwht_tcgen05_bf16_16384x4096"] = {"gbs": round(PASS_BYTES / ms / 1e6, 1),
+                                               "frac": round(PASS_BYTES / ms / 1e6 / peak, 4),
+                                               "us": round(ms * 1e3, 2), "algorithm": p.algorithm_name()}
+    del xa, xb, y
     # config 0: FFT c64 4096 x 1024 (32 MiB: rotate 8 buffers so each step reads cold data)
     xs = [w.torch_fft_input(w.FFT_N, w.FFT_BATCH, dev, seed=s) for s in range(8)]
     y = torch.empty_like(xs[0])

@@ -299,6 +299,10 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         scale = d.output_scale;
         if (inverse && d.normalize_inverse) scale /= static_cast<double>(n);
     }
+    if (m.passes.front().kind == cubf::PassKind::FwhtTensor) {
+        check_cuda(cubf::launch_fwht_tc(in, out, d.batch, static_cast<float>(scale), stream), "tensor FWHT launch");
+        return;
+    }
     // Multi-pass chains run chunk by chunk: every pass over a chunk of
     // transforms sized to stay in L2, so the intermediate written by one pass
     // is read by the next from L2 instead of HBM.

@@ -74,6 +74,15 @@ LaunchShape bw_shape(const BwVariant& v);
 cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
                       bool inverse, float scale, int cache_mode, cudaStream_t stream);
 
+// ---- FWHT on the tensor cores (tcgen05) ------------------------------------------
+// 4096-point bf16 rows as H_64 (x) H_64 contractions (csrc/fwht_tc.cu); in may
+// equal out.  fwht_tc_take_status returns (and clears) the kernel's error
+// word: nonzero when a bounded wait expired.
+bool fwht_tc_available(int log_n, BwType type);
+LaunchShape fwht_tc_shape();
+cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream);
+unsigned fwht_tc_take_status();
+
 // ---- NTT tile passes (RNS ABI and the main-ABI cyclic NTT) ----------------------
 struct NttPolyDesc {
     std::uint64_t in_off;

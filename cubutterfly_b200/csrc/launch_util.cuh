@@ -22,9 +22,13 @@ struct KernelSetup {
 };
 
 // `setup` must have static storage duration (zero-initialised).  On success
-// *grid_cap = resident CTAs per SM x SMs of the current device.
+// *grid_cap = resident CTAs per SM x SMs of the current device.  A kernel
+// whose residency is set by its shared memory (tensor-core tiles) passes
+// `max_carveout` to ask for the largest shared-memory carveout; without it the
+// occupancy the driver grants such a kernel can be a single CTA per SM.
 template <typename Kernel>
-cudaError_t setup_kernel(KernelSetup& setup, Kernel kernel, int threads, int smem_bytes, int* grid_cap) {
+cudaError_t setup_kernel(KernelSetup& setup, Kernel kernel, int threads, int smem_bytes, int* grid_cap,
+                         bool max_carveout = false) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
@@ -33,6 +37,11 @@ cudaError_t setup_kernel(KernelSetup& setup, Kernel kernel, int threads, int sme
     if (cap == 0) {
         if (smem_bytes > 48 * 1024) {
             e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+            if (e != cudaSuccess) return e;
+        }
+        if (max_carveout) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
         }
         int per_sm = 0, sms = 0;

@@ -218,6 +218,24 @@ void add_boundary(Mapping& m, const PlanRequest& r, const HardwareProfile& hw) {
 }
 }  // namespace
 
+Mapping fwht_tc_mapping(const PlanRequest& r, const HardwareProfile& hw) {
+    Mapping m;
+    m.family = "fwht-tcgen05";
+    const double elems = static_cast<double>(r.d.batch) * std::ldexp(1.0, r.log_n);
+    for (int i = 0; i < 2; ++i) {
+        Pass p;
+        p.kind = PassKind::FwhtTensor;
+        p.log_h = r.log_n / 2;
+        p.shape = fwht_tc_shape();
+        m.passes.push_back(p);
+    }
+    if (!fits(m.passes[0].shape, hw)) throw Unsupported("tensor-core FWHT tile does not fit the device");
+    // one HBM pass; ranked behind the single-pass SIMT tile by the static
+    // model (the MEASURE policy or an explicit mapping selects it)
+    m.predicted_us = 1.05 * pass_time_us(hw, elems, 2.0, 4.0, r.log_n, 1, 0.5, 0.92);
+    return m;
+}
+
 Mapping ntt_mapping(const PlanRequest& r, const HardwareProfile& hw) {
     Mapping m;
     m.family = r.ntt_gs ? "ntt-tile-gs" : "ntt-tile-ct";
@@ -309,6 +327,7 @@ Json Mapping::to_json() const {
             case PassKind::NttStrided: kernel = "ntt_pass_strided"; break;
             case PassKind::NttContiguous: kernel = "ntt_pass_contiguous"; break;
             case PassKind::NttSingle: kernel = "ntt_single"; break;
+            case PassKind::FwhtTensor: kernel = "fwht_tcgen05"; break;
             default: break;
         }
         ps.push_back({{"kernel", kernel},
@@ -386,6 +405,7 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         out.push_back(m);
         return out;
     }
+    if (r.bw_op == BwOp::Fwht && fwht_tc_available(r.log_n, r.bw_type)) out.push_back(fwht_tc_mapping(r, hw));
     // Bitwise operators: every composition of log N into tile passes.
     std::vector<std::vector<int>> parts;
     std::vector<int> cur;
@@ -424,6 +444,7 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
                 "explicit mapping must use schema cubutterfly-b200-mapping-v1");
         require(j.at("passes").is_array(), "explicit mapping passes must be an array");
         for (const auto& p : j.at("passes")) parts.push_back(p.at("log_h").get<int>());
+        if (j.value("family", "") == "fwht-tcgen05") return parse_core(r, hw, "fwht-tcgen05[6+6]");
     } else {
         std::string body = text;
         const auto lb = body.find('['), rb = body.rfind(']');
@@ -448,6 +469,11 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         for (const auto& p : m.passes) planned.push_back(p.log_h);
         if (parts != planned) throw Unsupported("explicit NTT mapping must be the planned pass split " + m.name());
         return m;
+    }
+    if (r.bw_op == BwOp::Fwht && text.find("tcgen05") != std::string::npos) {
+        if (!fwht_tc_available(r.log_n, r.bw_type))
+            throw Unsupported("the tensor-core FWHT serves 4096-point bf16 rows");
+        return fwht_tc_mapping(r, hw);
     }
     if (r.bw_op == BwOp::Fwht) require(parts.size() == 1, "FWHT executes as a single tile pass");
     return bitwise_mapping(r, hw, parts);

@@ -43,7 +43,7 @@ struct HardwareProfile {
 HardwareProfile resolve_profile();
 HardwareProfile profile_from_json(const Json& j);
 
-enum class PassKind { FftLocal, FftGlobal, BitwiseTile, NttStrided, NttContiguous, NttSingle };
+enum class PassKind { FftLocal, FftGlobal, BitwiseTile, NttStrided, NttContiguous, NttSingle, FwhtTensor };
 
 struct Pass {
     PassKind kind = PassKind::BitwiseTile;
@@ -97,6 +97,8 @@ struct PlanRequest {
 //                  (bit-reversed).
 void resolve_orders(PlanRequest& r);
 
+// The tensor-core FWHT (4096-point bf16 rows as H_64 (x) H_64 on tcgen05).
+Mapping fwht_tc_mapping(const PlanRequest& r, const HardwareProfile& hw);
 // The NTT passes of the request (one whole-transform tile up to 2^11, else
 // the strided and contiguous passes in execution order).
 Mapping ntt_mapping(const PlanRequest& r, const HardwareProfile& hw);

@@ -258,6 +258,19 @@ def test_bit_reversed_orders_need_packed_batches(lib):
     assert "order-lowering" in [g["code"] for g in capabilities(lib, t)["gaps"]]
 
 
+def test_tensor_core_fwht_is_offered_for_bf16_4096_only(lib):
+    def t(n):
+        return cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32,
+                            extents=[n], batch=8, output_rounding=cb.OutputRounding.FINAL_STORAGE)
+
+    ms = rank(lib, t(4096))
+    names = [m["name"] for m in ms]
+    assert names[0] == "fwht-tile[12]" and "fwht-tcgen05[6+6]" in names
+    tc = ms[names.index("fwht-tcgen05[6+6]")]
+    assert [p["kernel"] for p in tc["passes"]] == ["fwht_tcgen05"] * 2 and tc["passes"][0]["threads"] == 512
+    assert all("tcgen05" not in m["name"] for m in rank(lib, t(2048)))
+
+
 def test_planner_respects_hardware_profile(lib):
     """A device with little shared memory cannot take the 14-bit contiguous zeta tile."""
     t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << 24], batch=16)

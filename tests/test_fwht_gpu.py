@@ -99,3 +99,44 @@ def test_fwht_in_place_round_trip(lib, cuda):
     t.inverse = True
     back, _ = run(lib, t, f, cuda)
     assert rel_l2(back, x) <= 1e-6
+
+
+# ---- tensor-core FWHT (tcgen05, H_4096 = H_64 (x) H_64) ----------------------------
+TC = cb.PlanOptions(mapping="fwht-tcgen05[6+6]")
+
+
+@pytest.mark.parametrize("rows", [1, 2, 3, 64, 999, 4097])
+def test_fwht_tcgen05_matches_oracle(lib, oracle, cuda, rows):
+    """The tensor-core mapping: ragged row counts (odd rows zero-padded in the
+    last M = 128 tile), >99% bit-identical to the FP32 final-storage oracle."""
+    from gpu_util import run
+
+    bits = w.fwht_input_bits(rows, 4096, seed=rows)
+    got, name = run(lib, bf16_transform(4096, rows, 1 / 64), bits, cuda, options=TC)
+    assert name == "fwht-tcgen05[6+6]"
+    want = oracle.fwht_bf16_final(bits, 1 / 64)
+    assert rel_l2(f32(got), f32(want)) <= TOL_BF16
+    assert np.mean(got == want) > 0.99
+
+
+def test_fwht_tcgen05_inverse_in_place_and_golden(lib, oracle, golden, cuda):
+    from gpu_util import run
+
+    bits = w.fwht_input_bits(40, 4096, seed=5)
+    got, _ = run(lib, bf16_transform(4096, 40, 0.375, inverse=True, normalize=True, in_place=True), bits, cuda,
+                 options=TC)
+    want = oracle.fwht_bf16_final(bits, 0.375, inverse=True, normalize=True)
+    assert rel_l2(f32(got), f32(want)) <= TOL_BF16
+    x = golden["fwht_bf16_4096_in"]
+    got, _ = run(lib, bf16_transform(4096, x.shape[0], float(golden["fwht_bf16_4096_scale"][0])), x, cuda, options=TC)
+    assert rel_l2(f32(got), f32(golden["fwht_bf16_4096_out"])) <= TOL_BF16
+
+
+def test_fwht_tcgen05_config1_full_size(lib, oracle, cuda):
+    from gpu_util import run
+
+    bits = w.fwht_input_bits()
+    got, _ = run(lib, bf16_transform(4096, w.FWHT_ROWS, 1 / 64), bits, cuda, options=TC)
+    want = oracle.fwht_bf16_final(bits, 1 / 64)
+    assert rel_l2(f32(got), f32(want)) <= TOL_BF16
+    assert np.mean(got == want) > 0.99

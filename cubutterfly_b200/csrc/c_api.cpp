@@ -22,6 +22,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <memory>
@@ -61,11 +62,21 @@ struct cubutterflyPlan {
     int device = 0;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
+    // Chained multi-pass bitwise plans over several L2 chunks: the first pass
+    // of chunk c+1 runs on lanes[0] while the later passes of chunk c run on
+    // lanes[1] (fork/join through events on the caller's stream).
+    cudaStream_t lanes[2] = {nullptr, nullptr};
+    cudaEvent_t ev_fork = nullptr, ev_handoff = nullptr, ev_done[2] = {nullptr, nullptr};
+    cudaEvent_t ev_join[2] = {nullptr, nullptr};
     ~cubutterflyPlan() {
         if (twiddles) cudaFree(twiddles);
         if (outer_lo) cudaFree(outer_lo);
         if (outer_hi) cudaFree(outer_hi);
         if (ntt_block) cudaFree(ntt_block);
+        for (auto e : {ev_fork, ev_handoff, ev_done[0], ev_done[1], ev_join[0], ev_join[1]})
+            if (e) cudaEventDestroy(e);
+        for (auto l : lanes)
+            if (l) cudaStreamDestroy(l);
     }
 };
 
@@ -311,7 +322,14 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
     const std::size_t budget = std::max<std::size_t>(p.hw.l2_bytes * 2 / 5, 1);
     const bool chained = m.passes.size() > 1;
     const std::size_t chunk = chained ? std::max<std::size_t>(1, budget / transform_bytes) : d.batch;
-    for (std::size_t b0 = 0; b0 < d.batch; b0 += chunk) {
+    const bool overlap = chained && p.lanes[0] && d.batch > chunk;
+    if (overlap) {
+        check_cuda(cudaEventRecord(p.ev_fork, stream), "fork");
+        check_cuda(cudaStreamWaitEvent(p.lanes[0], p.ev_fork, 0), "fork");
+        check_cuda(cudaStreamWaitEvent(p.lanes[1], p.ev_fork, 0), "fork");
+    }
+    std::size_t c = 0;
+    for (std::size_t b0 = 0; b0 < d.batch; b0 += chunk, ++c) {
         const std::size_t nb = std::min(chunk, d.batch - b0);
         const void* src = static_cast<const unsigned char*>(in) + b0 * transform_bytes;
         void* dst = static_cast<unsigned char*>(out) + b0 * transform_bytes;
@@ -323,12 +341,37 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
             const std::size_t inner_arg = ps.log_w == 0 ? 1 : inner;
             const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
             const int mode = !chained ? 0 : (i == 0 ? 1 : (last ? 2 : 3));
+            cudaStream_t s = stream;
+            if (overlap) {
+                s = p.lanes[i == 0 ? 0 : 1];
+                // the first pass runs at most one chunk ahead of the others (L2 holds two chunks)
+                if (i == 0 && c >= 2) check_cuda(cudaStreamWaitEvent(s, p.ev_done[c & 1], 0), "chunk order");
+                if (i == 1) check_cuda(cudaStreamWaitEvent(s, p.ev_handoff, 0), "chunk handoff");
+            }
             check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, dst, outer_arg,
-                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream),
+                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, s),
                        "tile pass launch");
+            if (overlap && i == 0) check_cuda(cudaEventRecord(p.ev_handoff, s), "chunk handoff");
+            if (overlap && last) check_cuda(cudaEventRecord(p.ev_done[c & 1], s), "chunk done");
             src = dst;
         }
     }
+    if (overlap) {
+        check_cuda(cudaEventRecord(p.ev_join[0], p.lanes[0]), "join");
+        check_cuda(cudaEventRecord(p.ev_join[1], p.lanes[1]), "join");
+        check_cuda(cudaStreamWaitEvent(stream, p.ev_join[0], 0), "join");
+        check_cuda(cudaStreamWaitEvent(stream, p.ev_join[1], 0), "join");
+    }
+}
+
+// Streams and events of the chunk-overlapped execution (chained bitwise plans
+// whose batch spans several L2 chunks).
+void make_lanes(cubutterflyPlan& p) {
+    if (p.mapping.passes.size() < 2 || p.mapping.passes.front().kind != cubf::PassKind::BitwiseTile) return;
+    if (const char* v = std::getenv("CUBUTTERFLY_B200_CHUNK_OVERLAP"); v && std::string(v) == "0") return;
+    for (auto& l : p.lanes) check_cuda(cudaStreamCreateWithFlags(&l, cudaStreamNonBlocking), "lane stream");
+    for (auto* e : {&p.ev_fork, &p.ev_handoff, &p.ev_done[0], &p.ev_done[1], &p.ev_join[0], &p.ev_join[1]})
+        check_cuda(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "lane event");
 }
 
 double time_mapping(cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream,
@@ -822,6 +865,7 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
         check_cuda(cudaGetDevice(&p->device), "current device");
         build_tables(*p);  // before selection: MEASURE executes the candidates
         select_mapping(handle, *p);
+        make_lanes(*p);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
         *plan = p.release();
     });

@@ -1,4 +1,6 @@
-// bitrev.cu -- bit-reversal permutation of packed batches of 2^L elements.
+// bitrev.cu -- boundary kernels of the main ABI: the bit-reversal permutation
+// of packed batches of 2^L elements (logical orders) and the strided gather /
+// scatter that stages a strided or padded layout through a packed buffer.
 //
 // Serves the bit-reversed logical orders of the main ABI (semantic contract
 // src/semantic_contract.cpp:257-271: a bit-reversed axis stores logical index
@@ -85,7 +87,47 @@ cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch
     return cudaGetLastError();
 }
 
+// out[b * obs + i * os] = in[b * ibs + i * is] for i < n, b < batch.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) strided_copy_kernel(const T* in, size_t is, size_t ibs, T* out, size_t os,
+                                                                 size_t obs, size_t n, size_t total) {
+    for (size_t idx = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * kThreads) {
+        const size_t b = idx / n, i = idx - b * n;
+        out[b * obs + i * os] = in[b * ibs + i * is];
+    }
+}
+
+template <typename T>
+cudaError_t copy_typed(const void* in, std::size_t is, std::size_t ibs, void* out, std::size_t os, std::size_t obs,
+                       std::size_t n, std::size_t batch, cudaStream_t stream) {
+    const std::size_t total = n * batch;
+    std::size_t blocks = (total + kThreads - 1) / kThreads;
+    if (blocks > 148 * 64) blocks = 148 * 64;  // grid-stride beyond 64 blocks per SM
+    strided_copy_kernel<T><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
+        static_cast<const T*>(in), is, ibs, static_cast<T*>(out), os, obs, n, total);
+    return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_strided_copy(int elem_bytes, const void* in, std::size_t in_stride, std::size_t in_batch_stride,
+                                void* out, std::size_t out_stride, std::size_t out_batch_stride, std::size_t n,
+                                std::size_t batch, cudaStream_t stream) {
+    if (n == 0 || batch == 0) return cudaSuccess;
+    switch (elem_bytes) {
+        case 2:
+            return copy_typed<std::uint16_t>(in, in_stride, in_batch_stride, out, out_stride, out_batch_stride, n,
+                                             batch, stream);
+        case 4:
+            return copy_typed<std::uint32_t>(in, in_stride, in_batch_stride, out, out_stride, out_batch_stride, n,
+                                             batch, stream);
+        case 8:
+            return copy_typed<unsigned long long>(in, in_stride, in_batch_stride, out, out_stride, out_batch_stride,
+                                                  n, batch, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
 
 cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
                           cudaStream_t stream) {

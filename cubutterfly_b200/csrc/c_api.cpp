@@ -243,13 +243,15 @@ void launch_ntt(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in
     check_cuda(cubf::launch_ntt({l, gs, gs, p.req.ntt_lazy, p.req.ntt_word32}, a, stream), "NTT pass 2 launch");
 }
 
-void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream);
+void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* ws,
+                 cudaStream_t stream);
 
-// The logical-order boundary around the core passes: a bit-reversed input is
-// permuted into the output buffer first (the core then runs in place there),
-// a bit-reversed output is permuted in place last.
-void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
-                    cudaStream_t stream) {
+// The boundary around the core passes, on packed batches: a bit-reversed
+// input is permuted into the output buffer first (the core then runs in place
+// there), a bit-reversed output is permuted in place last.  `ws` is the
+// core's workspace.
+void launch_packed(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* ws,
+                   cudaStream_t stream) {
     const auto& d = p.desc;
     const int esz = static_cast<int>(cubf::storage_bytes(d.storage));
     const void* core_in = in;
@@ -257,12 +259,35 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
         check_cuda(cubf::launch_bitrev(esz, p.req.log_n, in, out, d.batch, stream), "input permutation launch");
         core_in = out;
     }
-    launch_core(p, m, core_in, out, stream);
+    launch_core(p, m, core_in, out, ws, stream);
     if (m.permute_output)
         check_cuda(cubf::launch_bitrev(esz, p.req.log_n, out, out, d.batch, stream), "output permutation launch");
 }
 
-void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream) {
+// A strided or padded layout is gathered into the packed buffer at the start
+// of the workspace, transformed there in place and scattered to the output
+// layout (the reference's general strided boundary, src/general_kernels.cu).
+void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
+                    cudaStream_t stream) {
+    if (!m.staged) {
+        launch_packed(p, m, in, out, p.workspace, stream);
+        return;
+    }
+    const auto& d = p.desc;
+    const int esz = static_cast<int>(cubf::storage_bytes(d.storage));
+    const std::size_t n = d.extents[0];
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    check_cuda(cubf::launch_strided_copy(esz, in, d.input_strides[0], d.input_batch_stride, ws, 1, n, n, d.batch,
+                                         stream),
+               "layout gather launch");
+    launch_packed(p, m, ws, ws, ws + m.staged_bytes, stream);
+    check_cuda(cubf::launch_strided_copy(esz, ws, 1, n, out, d.output_strides[0], d.output_batch_stride, n, d.batch,
+                                         stream),
+               "layout scatter launch");
+}
+
+void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
+                 cudaStream_t stream) {
     const auto& d = p.desc;
     const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
     const std::size_t n = d.extents[0];
@@ -282,7 +307,7 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         // starts in a second workspace half.
         const std::size_t np = m.passes.size();
         const std::size_t bytes = d.batch * n * 8;
-        unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+        unsigned char* ws = static_cast<unsigned char*>(core_ws);
         const bool in_place = in == out;
         const cubf::FftOuterTables outer{p.outer_lo, p.outer_hi, p.outer_split};
         const void* src = in;
@@ -490,6 +515,7 @@ cubf::PlanRequest make_request(const cubf::Descriptor& d) {
             break;
     }
     cubf::resolve_orders(r);
+    r.staged = !cubf::packed_layout(d) && r.log_v == 0;
     return r;
 }
 

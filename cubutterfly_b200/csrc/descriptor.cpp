@@ -215,6 +215,12 @@ bool interleaved_batches(const Descriptor& d) {
            d.output_batch_stride == 1;
 }
 
+bool packed_layout(const Descriptor& d) {
+    return d.rank == 1 && d.extents.size() == 1 && d.input_strides == std::vector<std::size_t>{1} &&
+           d.output_strides == std::vector<std::size_t>{1} && d.input_batch_stride == d.extents[0] &&
+           d.output_batch_stride == d.extents[0];
+}
+
 bool layout_nonoverlapping(const std::vector<std::size_t>& extents, const std::vector<std::size_t>& strides,
                            std::size_t batch, std::size_t batch_stride) {
     return prove_layout(extents, strides, batch, batch_stride) == Proof::Disjoint;
@@ -492,17 +498,17 @@ Json capabilities(const Descriptor& source) {
     const bool packed = d.rank == 1 && d.input_strides == std::vector<std::size_t>{1} &&
                         d.output_strides == std::vector<std::size_t>{1} && d.input_batch_stride == in[0] &&
                         d.output_batch_stride == out[0];
+    // Other rank-one strided or padded layouts are staged through a packed
+    // workspace buffer (gather, packed passes, scatter); FFT batches
+    // interleaved element-wise run natively.
     const bool interleaved = d.op == CUBUTTERFLY_OPERATOR_FFT && interleaved_batches(d);
-    if (!packed && !interleaved)
-        gap("layout-lowering", "strided or padded layouts are not built; use packed rank-one batches or, for FFT, "
-                               "batches interleaved element-wise (stride = batch, batch stride 1)");
     const bool natural_in = std::all_of(d.input_orders.begin(), d.input_orders.end(),
                                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; });
     const bool natural_out = std::all_of(d.output_orders.begin(), d.output_orders.end(),
                                          [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; });
     // Bit-reversed orders run as bit-reversal permutations of packed batches.
-    if ((!natural_in || !natural_out) && !packed)
-        gap("order-lowering", "bit-reversed logical orders require packed rank-one batches");
+    if ((!natural_in || !natural_out) && interleaved && !packed)
+        gap("order-lowering", "bit-reversed logical orders are not built for interleaved FFT batches");
     if (d.arithmetic_policy != CUBUTTERFLY_ARITHMETIC_STRICT)
         gap("arithmetic-policy", "FP16 MMA policy is not built");
     const bool epilogue = d.output_scale != 1.0 || d.output_rounding != CUBUTTERFLY_ROUNDING_STAGE_STORAGE;

@@ -85,6 +85,8 @@ std::vector<std::size_t> output_extents(const Descriptor& d);
 // N >= 16 and N * batch >= 2^12 (a pass tile takes >= 16 columns).  The
 // layout of the columns of a row-major matrix.
 bool interleaved_batches(const Descriptor& d);
+// Rank one, element stride 1, batch stride N on both sides.
+bool packed_layout(const Descriptor& d);
 bool layout_nonoverlapping(const std::vector<std::size_t>& extents, const std::vector<std::size_t>& strides,
                            std::size_t batch, std::size_t batch_stride);
 std::size_t storage_bytes(cubutterflyDataType_t t);

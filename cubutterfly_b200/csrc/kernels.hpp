@@ -137,5 +137,10 @@ cudaError_t launch_ntt(const NttVariant& v, const NttLaunch& a, cudaStream_t str
 // by one CTA).
 cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
                           cudaStream_t stream);
+// out[b * out_batch_stride + i * out_stride] = in[b * in_batch_stride + i * in_stride]
+// for i < n, b < batch (elements of elem_bytes 2, 4 or 8; strides in elements).
+cudaError_t launch_strided_copy(int elem_bytes, const void* in, std::size_t in_stride, std::size_t in_batch_stride,
+                                void* out, std::size_t out_stride, std::size_t out_batch_stride, std::size_t n,
+                                std::size_t batch, cudaStream_t stream);
 
 }  // namespace cubf

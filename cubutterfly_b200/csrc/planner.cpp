@@ -215,6 +215,13 @@ void add_boundary(Mapping& m, const PlanRequest& r, const HardwareProfile& hw) {
     const double esz = static_cast<double>(storage_bytes(r.d.storage));
     m.predicted_us += (m.permute_input ? permutation_us(r, hw, esz) : 0.0) +
                       (m.permute_output ? permutation_us(r, hw, esz) : 0.0);
+    m.staged = r.staged;
+    if (m.staged) {
+        const std::size_t bytes = r.d.batch * (std::size_t{1} << r.log_n) * storage_bytes(r.d.storage);
+        m.staged_bytes = (bytes + 255) / 256 * 256;  // the core's own workspace follows, 256-byte aligned
+        m.workspace_bytes += m.staged_bytes;
+        m.predicted_us += 2.0 * permutation_us(r, hw, esz);  // gather + scatter
+    }
 }
 }  // namespace
 
@@ -298,7 +305,7 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
     }
     require(ns == r.log_n, "FFT passes must cover every stage exactly once");
     // a permuted input lands in the output buffer and the passes run in place
-    const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE || r.permute_input;
+    const bool in_place = d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE || r.permute_input || r.staged;
     const std::size_t bytes = d.batch * (std::size_t{1} << r.log_n) * 8;
     m.workspace_bytes = bytes * ((in_place && parts.size() % 2 == 1) ? 2 : 1);
     return m;
@@ -306,6 +313,7 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
 
 std::string Mapping::name() const {
     std::ostringstream o;
+    if (staged) o << "gather+";
     if (permute_input) o << "bitrev+";
     o << family << "[";
     for (std::size_t i = 0; i < passes.size(); ++i) {
@@ -314,6 +322,7 @@ std::string Mapping::name() const {
     }
     o << "]";
     if (permute_output) o << "+bitrev";
+    if (staged) o << "+scatter";
     return o.str();
 }
 
@@ -344,7 +353,11 @@ Json Mapping::to_json() const {
             {"family", family},
             {"name", name()},
             {"passes", ps},
-            {"boundary", {{"input_bit_reversal", permute_input}, {"output_bit_reversal", permute_output}}},
+            {"boundary",
+             {{"input_bit_reversal", permute_input},
+              {"output_bit_reversal", permute_output},
+              {"staged_layout", staged},
+              {"staged_bytes", staged_bytes}}},
             {"workspace_bytes", workspace_bytes},
             {"predicted_us", predicted_us}};
 }

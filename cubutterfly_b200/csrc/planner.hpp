@@ -60,6 +60,10 @@ struct Mapping {
     // the first pass and of the output after the last.
     bool permute_input = false;
     bool permute_output = false;
+    // Strided or padded layout: gathered into a packed buffer at the start of
+    // the workspace (staged_bytes), transformed there in place, scattered out.
+    bool staged = false;
+    std::size_t staged_bytes = 0;
     std::size_t workspace_bytes = 0;
     double predicted_us = 0.0;
     std::string name() const;
@@ -75,9 +79,12 @@ struct PlanRequest {
     BwType bw_type = BwType::F32;
     BwOp bw_op = BwOp::Fwht;
     // Bit-reversal permutations the logical orders require (see
-    // boundary_permutations); a permuted input makes the core run in place.
+    // resolve_orders); a permuted input makes the core run in place.
     bool permute_input = false;
     bool permute_output = false;
+    // A strided or padded layout runs staged through a packed buffer (the
+    // core then runs in place on it).
+    bool staged = false;
     // NTT: Gentleman-Sande passes (bit-reversed input to natural output)
     // instead of Cooley-Tukey (natural input to bit-reversed output).
     bool ntt_gs = false;

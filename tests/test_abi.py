@@ -128,7 +128,6 @@ def test_benchmark_configs_are_eligible(lib):
     (cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.FP32, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.STRUCTURED_2X2, storage=cb.DataType.FP32, extents=[4],
                   stage_matrices=[[(1.0, 1.0, 1.0, -1.0)]]), "operator-lowering"),
-    (cb.Transform(op=cb.Operator.FFT, extents=[64], input_strides=[2]), "layout-lowering"),
 ])
 def test_unsupported_descriptors_report_gaps(lib, transform, code):
     c = capabilities(lib, transform)
@@ -181,15 +180,19 @@ def test_interleaved_fft_batches_are_planned_as_global_passes(lib):
     ms = rank(lib, t)
     assert ms and all(m["family"] == "fft-stockham-global" for m in ms)
     assert all(sum(p["log_h"] for p in m["passes"]) == 12 for m in ms)
+    # interleaved shapes the global passes cannot take natively (fewer than 16
+    # points, fewer than 2^12 values, a batch that is not a power of two) run
+    # staged through a packed buffer instead
     small = cb.Transform(op=cb.Operator.FFT, extents=[8], batch=4, input_strides=[4], output_strides=[4],
                          input_batch_stride=1, output_batch_stride=1)
-    assert capabilities(lib, small)["status"] == "missing-lowering"  # passes need >= 16 points
     few = cb.Transform(op=cb.Operator.FFT, extents=[16], batch=64, input_strides=[64], output_strides=[64],
                        input_batch_stride=1, output_batch_stride=1)
-    assert capabilities(lib, few)["status"] == "missing-lowering"  # and >= 2^12 values in all
     odd = cb.Transform(op=cb.Operator.FFT, extents=[64], batch=6, input_strides=[6], output_strides=[6],
                        input_batch_stride=1, output_batch_stride=1)
-    assert "layout-lowering" in [g["code"] for g in capabilities(lib, odd)["gaps"]]
+    for x in (small, few, odd):
+        assert capabilities(lib, x)["status"] == "eligible"
+        assert rank(lib, x)[0]["boundary"]["staged_layout"]
+    assert not ms[0]["boundary"]["staged_layout"]
 
 
 def ntt_transform(n, batch=1, modulus=cb.DEFAULT_MODULUS, inverse=False, word32=False, orders=None, **kw):
@@ -230,8 +233,7 @@ def test_ntt_planner_lengths_and_words(lib):
     assert m["name"] == "bitrev+ntt-tile-gs[8+9]"
     big = capabilities(lib, ntt_transform(1 << 21))
     assert "length-lowering" in [g["code"] for g in big["gaps"]]
-    strided = capabilities(lib, ntt_transform(64, input_strides=[2]))
-    assert "layout-lowering" in [g["code"] for g in strided["gaps"]]
+    assert rank(lib, ntt_transform(64, input_strides=[2]))[0]["boundary"]["staged_layout"]
 
 
 @pytest.mark.parametrize("op, storage, orders, boundary", [
@@ -250,6 +252,25 @@ def test_logical_order_boundary(lib, op, storage, orders, boundary):
     m = rank(lib, t)[0]
     assert (m["boundary"]["input_bit_reversal"], m["boundary"]["output_bit_reversal"]) == boundary
     assert m["name"].startswith("bitrev+") == boundary[0] and m["name"].endswith("+bitrev") == boundary[1]
+
+
+@pytest.mark.parametrize("transform", [
+    cb.Transform(op=cb.Operator.FFT, extents=[64], batch=3, input_strides=[2], output_strides=[1],
+                 input_batch_stride=128, output_batch_stride=64),
+    cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[1024], batch=4,
+                 input_strides=[1], output_strides=[1], input_batch_stride=1100, output_batch_stride=1030),
+    cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[4096], batch=2, input_strides=[3],
+                 output_strides=[2], input_batch_stride=3 * 4096, output_batch_stride=2 * 4096 + 1)])
+def test_strided_layouts_are_staged(lib, transform):
+    """Strided or padded rank-one layouts run through a packed staging buffer
+    at the start of the workspace (gather, packed passes in place, scatter)."""
+    assert capabilities(lib, transform)["status"] == "eligible"
+    m = rank(lib, transform)[0]
+    n, b = transform.extents[0], transform.batch
+    esz = {cb.DataType.COMPLEX_FP32: 8, cb.DataType.FP32: 4, cb.DataType.UINT64: 8}[transform.storage]
+    assert m["boundary"]["staged_layout"] and m["boundary"]["staged_bytes"] >= n * b * esz
+    assert m["workspace_bytes"] >= m["boundary"]["staged_bytes"]
+    assert m["name"].startswith("gather+") and m["name"].endswith("+scatter")
 
 
 def test_bit_reversed_orders_need_packed_batches(lib):

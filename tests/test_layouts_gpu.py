@@ -1,0 +1,123 @@
+"""Strided and padded rank-one layouts on the GPU through the C ABI: the plan
+gathers the input layout into a packed workspace buffer, runs the packed
+passes there and scatters into the output layout.  Results equal the oracle
+on the logical values (bit-exact for zeta / NTT), and output padding keeps its
+sentinel."""
+import numpy as np
+import pytest
+import torch
+
+import cubutterfly_b200 as cb
+from conftest import rel_l2
+from cubutterfly_b200 import workloads as w
+
+pytestmark = pytest.mark.gpu
+
+
+def layout_view(buf, n, batch, stride, batch_stride):
+    """Indices of logical element (b, i) in a flat buffer."""
+    b = np.arange(batch)[:, None]
+    i = np.arange(n)[None, :]
+    return b * batch_stride + i * stride
+
+
+def run_layout(lib, t, logical, sentinel, cuda):
+    """Place `logical` (batch, n) in t's input layout, execute, return the
+    logical output and the raw output buffer (host)."""
+    from gpu_util import stream_ptr
+
+    n, batch = t.extents[0], t.batch
+    dtype = logical.dtype
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        esz = dtype.itemsize
+        in_span, out_span = plan.input_size() // esz, plan.output_size() // esz
+        host_in = np.full(in_span, sentinel, dtype=dtype)
+        host_in[layout_view(host_in, n, batch, t.input_strides[0], t.input_batch_stride)] = logical
+        din = torch.from_numpy(host_in.view(np.uint8).copy()).to(cuda)
+        if t.in_place:
+            dout = din
+        else:
+            dout = torch.from_numpy(np.full(out_span, sentinel, dtype=dtype).view(np.uint8).copy()).to(cuda)
+        ws = None
+        if plan.workspace_size():
+            ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=cuda)
+            plan.set_workspace(ws.data_ptr(), ws.numel())
+        assert plan.mapping_json().find('"staged_layout":true') >= 0
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        raw = dout.cpu().numpy().view(dtype)
+    idx = layout_view(raw, n, batch, t.output_strides[0], t.output_batch_stride)
+    return raw[idx], raw, idx
+
+
+def padding_untouched(raw, idx, sentinel, equal=np.array_equal):
+    mask = np.ones(raw.shape, dtype=bool)
+    mask[idx.reshape(-1)] = False
+    return equal(raw[mask], np.full(mask.sum(), sentinel, dtype=raw.dtype))
+
+
+@pytest.mark.parametrize("n", [64, 4096, 1 << 15])
+def test_fft_strided_input_padded_output(lib, oracle, cuda, n):
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=[n], batch=3,
+                     input_strides=[2], output_strides=[1], input_batch_stride=2 * n + 5, output_batch_stride=n + 8)
+    x = w.fft_input(n, 3, seed=n)
+    got, raw, idx = run_layout(lib, t, x, np.complex64(7 + 7j), cuda)
+    assert rel_l2(got, oracle.fft_c32(x)) <= 2e-6
+    assert padding_untouched(raw, idx, np.complex64(7 + 7j))
+
+
+def test_fft_column_layout_with_bit_reversed_output(lib, oracle, cuda):
+    """Batches as columns of a row-major N x 6 matrix (not a power-of-two batch,
+    so not the native interleaved path), output bit-reversed and packed."""
+    n, batch = 256, 6
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=[n], batch=batch,
+                     input_strides=[batch], output_strides=[1], input_batch_stride=1, output_batch_stride=n,
+                     output_orders=[cb.LogicalOrder.BIT_REVERSED])
+    x = w.fft_input(n, batch, seed=2)
+    got, _, _ = run_layout(lib, t, x, np.complex64(0), cuda)
+    rev = np.array([int(format(i, "08b")[::-1], 2) for i in range(n)])
+    assert rel_l2(got, oracle.fft_c32(x)[:, rev]) <= 2e-6
+
+
+def test_fwht_fp32_padded_rows_in_place(lib, oracle, cuda):
+    n, batch = 1024, 5
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[n],
+                     batch=batch, input_strides=[1], output_strides=[1], input_batch_stride=n + 16,
+                     output_batch_stride=n + 16, in_place=True)
+    x = w.rng(3).uniform(-1, 1, size=(batch, n)).astype(np.float32)
+    got, raw, idx = run_layout(lib, t, x, np.float32(-3.5), cuda)
+    assert rel_l2(got, oracle.fwht_f32(x, normalize=False)) <= 1e-6
+    assert padding_untouched(raw, idx, np.float32(-3.5))
+
+
+def test_bf16_fwht_strided(lib, oracle, cuda):
+    n, batch = 4096, 4
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32, extents=[n],
+                     batch=batch, output_scale=1 / 64, output_rounding=cb.OutputRounding.FINAL_STORAGE,
+                     input_strides=[3], output_strides=[1], input_batch_stride=3 * n, output_batch_stride=n)
+    bits = w.fwht_input_bits(batch, n, seed=4)
+    got, _, _ = run_layout(lib, t, bits, np.uint16(0), cuda)
+    want = oracle.fwht_bf16_final(bits, 1 / 64)
+    assert rel_l2(w.bf16_bits_to_f32(got), w.bf16_bits_to_f32(want)) <= 4e-3
+
+
+@pytest.mark.parametrize("op", [cb.Operator.SUBSET_ZETA, cb.Operator.SUPERSET_ZETA])
+def test_zeta_strided_both_sides(lib, oracle, cuda, op):
+    n, batch = 1 << 14, 3
+    t = cb.Transform(op=op, storage=cb.DataType.UINT32, extents=[n], batch=batch, input_strides=[2],
+                     output_strides=[3], input_batch_stride=2 * n + 1, output_batch_stride=3 * n + 7)
+    z = w.zeta_input(14, batch, seed=6)
+    got, raw, idx = run_layout(lib, t, z, np.uint32(0xDEADBEEF), cuda)
+    assert np.array_equal(got, oracle.zeta(z, superset=op == cb.Operator.SUPERSET_ZETA))
+    assert padding_untouched(raw, idx, np.uint32(0xDEADBEEF))
+
+
+@pytest.mark.parametrize("n", [256, 1 << 16])
+def test_ntt_strided(lib, oracle, cuda, n):
+    q = 576460756061519873
+    t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[n], batch=2, modulus=q,
+                     input_strides=[2], output_strides=[1], input_batch_stride=2 * n, output_batch_stride=n + 3)
+    x = w.rng(7).integers(0, q, size=(2, n), dtype=np.uint64)
+    got, raw, idx = run_layout(lib, t, x, np.uint64(12345), cuda)
+    assert np.array_equal(got, oracle.ntt_cyclic(x, q))
+    assert padding_untouched(raw, idx, np.uint64(12345))

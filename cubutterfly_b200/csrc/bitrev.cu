@@ -98,6 +98,42 @@ __global__ void __launch_bounds__(kThreads) strided_copy_kernel(const T* in, siz
     }
 }
 
+// Up to three axes and a batch: element (b, i0, i1, i2) moves from
+// b * ibs + sum_k i_k * is_k to b * obs + sum_k i_k * os_k.
+struct NdLayout {
+    size_t ext[3];
+    size_t is[3];
+    size_t os[3];
+    size_t ibs, obs;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) strided_copy_nd_kernel(const T* in, T* out, NdLayout l, size_t total) {
+    for (size_t idx = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * kThreads) {
+        size_t r = idx;
+        const size_t i2 = r % l.ext[2];
+        r /= l.ext[2];
+        const size_t i1 = r % l.ext[1];
+        r /= l.ext[1];
+        const size_t i0 = r % l.ext[0];
+        const size_t b = r / l.ext[0];
+        out[b * l.obs + i0 * l.os[0] + i1 * l.os[1] + i2 * l.os[2]] =
+            in[b * l.ibs + i0 * l.is[0] + i1 * l.is[1] + i2 * l.is[2]];
+    }
+}
+
+template <typename T>
+cudaError_t copy_nd_typed(const void* in, void* out, const NdLayout& l, size_t batch, cudaStream_t stream) {
+    const std::size_t total = batch * l.ext[0] * l.ext[1] * l.ext[2];
+    if (total == 0) return cudaSuccess;
+    std::size_t blocks = (total + kThreads - 1) / kThreads;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    strided_copy_nd_kernel<T><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(static_cast<const T*>(in),
+                                                                                        static_cast<T*>(out), l, total);
+    return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t copy_typed(const void* in, std::size_t is, std::size_t ibs, void* out, std::size_t os, std::size_t obs,
                        std::size_t n, std::size_t batch, cudaStream_t stream) {
@@ -125,6 +161,29 @@ cudaError_t launch_strided_copy(int elem_bytes, const void* in, std::size_t in_s
         case 8:
             return copy_typed<unsigned long long>(in, in_stride, in_batch_stride, out, out_stride, out_batch_stride,
                                                   n, batch, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_strided_copy_nd(int elem_bytes, int dims, const std::size_t* extents, const void* in,
+                                   const std::size_t* in_strides, std::size_t in_batch_stride, void* out,
+                                   const std::size_t* out_strides, std::size_t out_batch_stride, std::size_t batch,
+                                   cudaStream_t stream) {
+    if (dims < 1 || dims > 3) return cudaErrorInvalidValue;
+    NdLayout l{};
+    const int pad = 3 - dims;  // leading unit axes
+    for (int k = 0; k < 3; ++k) {
+        const int a = k - pad;
+        l.ext[k] = a >= 0 ? extents[a] : 1;
+        l.is[k] = a >= 0 ? in_strides[a] : 0;
+        l.os[k] = a >= 0 ? out_strides[a] : 0;
+    }
+    l.ibs = in_batch_stride;
+    l.obs = out_batch_stride;
+    switch (elem_bytes) {
+        case 2: return copy_nd_typed<std::uint16_t>(in, out, l, batch, stream);
+        case 4: return copy_nd_typed<std::uint32_t>(in, out, l, batch, stream);
+        case 8: return copy_nd_typed<unsigned long long>(in, out, l, batch, stream);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -68,6 +68,19 @@ struct cubutterflyPlan {
     cudaStream_t lanes[2] = {nullptr, nullptr};
     cudaEvent_t ev_fork = nullptr, ev_handoff = nullptr, ev_done[2] = {nullptr, nullptr};
     cudaEvent_t ev_join[2] = {nullptr, nullptr};
+    // Rank two and three: packed rank-one child plans.  FFT / NTT: one per
+    // axis, innermost first, each run in place on a packed copy of the tensor
+    // (axes other than the innermost transposed innermost through a second
+    // buffer).  FWHT / zeta: one child over the flattened index, on the
+    // caller's buffers when both layouts are packed (`flat`).
+    struct Axis {
+        std::unique_ptr<cubutterflyPlan> plan;
+        std::size_t n = 0, outer = 0, inner = 0;  // length; blocks before and elements after the axis
+        std::size_t ws_offset = 0;                // child workspace inside this plan's workspace
+    };
+    std::vector<Axis> axes;
+    bool flat = false;
+    std::size_t packed_bytes = 0;  // one packed copy of the tensor (256-byte aligned)
     ~cubutterflyPlan() {
         if (twiddles) cudaFree(twiddles);
         if (outer_lo) cudaFree(outer_lo);
@@ -264,11 +277,68 @@ void launch_packed(const cubutterflyPlan& p, const cubf::Mapping& m, const void*
         check_cuda(cubf::launch_bitrev(esz, p.req.log_n, out, out, d.batch, stream), "output permutation launch");
 }
 
+void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
+                    cudaStream_t stream);
+
+// Row-major packed strides of the extents.
+std::vector<std::size_t> packed_strides(const std::vector<std::size_t>& ext) {
+    std::vector<std::size_t> st(ext.size(), 1);
+    for (std::size_t k = ext.size(); k-- > 1;) st[k - 1] = st[k] * ext[k];
+    return st;
+}
+
+// Rank two and three (reference composite execution, src/c_api.cpp:4533-4650:
+// one axis plan per dimension, innermost first).
+void launch_composite(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    if (p.flat) {
+        auto& c = *p.axes.front().plan;
+        c.workspace = ws + p.axes.front().ws_offset;
+        launch_mapping(c, c.mapping, in, out, stream);
+        return;
+    }
+    const int esz = static_cast<int>(cubf::storage_bytes(d.storage));
+    const int dims = static_cast<int>(d.rank);
+    const auto ps = packed_strides(d.extents);
+    std::size_t volume = 1;
+    for (auto e : d.extents) volume *= e;
+    unsigned char* a = ws;
+    unsigned char* b = ws + p.packed_bytes;
+    check_cuda(cubf::launch_strided_copy_nd(esz, dims, d.extents.data(), in, d.input_strides.data(),
+                                            d.input_batch_stride, a, ps.data(), volume, d.batch, stream),
+               "composite gather launch");
+    for (const auto& ax : p.axes) {
+        auto& c = *ax.plan;
+        c.workspace = ws + ax.ws_offset;
+        if (ax.inner == 1) {
+            launch_mapping(c, c.mapping, a, a, stream);
+            continue;
+        }
+        // [outer][n][inner] <-> [outer][inner][n]
+        const std::size_t ext[2] = {ax.n, ax.inner};
+        const std::size_t by_axis[2] = {ax.inner, 1}, axis_last[2] = {1, ax.n};
+        const std::size_t block = ax.n * ax.inner;
+        check_cuda(cubf::launch_strided_copy_nd(esz, 2, ext, a, by_axis, block, b, axis_last, block, ax.outer, stream),
+                   "composite transpose launch");
+        launch_mapping(c, c.mapping, b, b, stream);
+        check_cuda(cubf::launch_strided_copy_nd(esz, 2, ext, b, axis_last, block, a, by_axis, block, ax.outer, stream),
+                   "composite transpose launch");
+    }
+    check_cuda(cubf::launch_strided_copy_nd(esz, dims, d.extents.data(), a, ps.data(), volume, out,
+                                            d.output_strides.data(), d.output_batch_stride, d.batch, stream),
+               "composite scatter launch");
+}
+
 // A strided or padded layout is gathered into the packed buffer at the start
 // of the workspace, transformed there in place and scattered to the output
 // layout (the reference's general strided boundary, src/general_kernels.cu).
 void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                     cudaStream_t stream) {
+    if (!p.axes.empty()) {
+        launch_composite(p, in, out, stream);
+        return;
+    }
     if (!m.staged) {
         launch_packed(p, m, in, out, p.workspace, stream);
         return;
@@ -586,6 +656,140 @@ void select_mapping(cubutterflyHandle* h, cubutterflyPlan& p) {
 }  // namespace
 
 namespace cubf {
+}  // namespace cubf
+
+namespace {
+
+// Bytes spanned by a layout: its largest element offset + 1.
+std::size_t layout_span(const cubf::Descriptor& d, const std::vector<std::size_t>& ext,
+                        const std::vector<std::size_t>& str, std::size_t bs) {
+    std::size_t last = (d.batch - 1) * bs;
+    for (std::size_t a = 0; a < ext.size(); ++a) last += (ext[a] - 1) * str[a];
+    return (last + 1) * cubf::storage_bytes(d.storage);
+}
+
+std::unique_ptr<cubutterflyPlan> create_rank1(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride);
+    p->req = make_request(d);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    build_tables(*p);  // before selection: MEASURE executes the candidates
+    select_mapping(handle, *p);
+    make_lanes(*p);
+    return p;
+}
+
+// The rank-one child descriptors of a rank-two or rank-three descriptor.
+struct AxisSpec {
+    cubf::Descriptor d;
+    std::size_t n, outer, inner;
+};
+std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat) {
+    cubf::Descriptor c = d;
+    c.rank = 1;
+    c.input_orders = c.output_orders = {CUBUTTERFLY_ORDER_NATURAL};
+    c.input_ntt_layout = c.output_ntt_layout = CUBUTTERFLY_NTT_LAYOUT_NATURAL;
+    c.input_strides = c.output_strides = {1};
+    c.stage_matrices.assign(3, {});
+    if (c.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {  // a pass list names one rank-one plan
+        c.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+        c.explicit_algorithm.clear();
+    }
+    std::size_t volume = 1;
+    for (auto e : d.extents) volume *= e;
+    const bool packed_in = d.input_strides == packed_strides(d.extents) && d.input_batch_stride == volume;
+    const bool packed_out = d.output_strides == packed_strides(d.extents) && d.output_batch_stride == volume;
+    std::vector<AxisSpec> axes;
+    if (d.op == CUBUTTERFLY_OPERATOR_FWHT || d.op == CUBUTTERFLY_OPERATOR_SUBSET_ZETA ||
+        d.op == CUBUTTERFLY_OPERATOR_SUPERSET_ZETA) {
+        // H_N0 (x) H_N1 (x) ... = H_(N0 N1 ...) on the row-major index, and
+        // likewise for the subset / superset order: one transform of the
+        // concatenated index bits
+        flat = packed_in && packed_out;
+        c.extents = {volume};
+        c.input_batch_stride = c.output_batch_stride = volume;
+        if (!flat) c.placement = CUBUTTERFLY_PLACEMENT_IN_PLACE;
+        axes.push_back({c, volume, d.batch, 1});
+        return axes;
+    }
+    flat = false;
+    c.placement = CUBUTTERFLY_PLACEMENT_IN_PLACE;  // children run in place on the workspace copies
+    for (std::size_t k = d.rank; k-- > 0;) {
+        std::size_t outer = d.batch, inner = 1;
+        for (std::size_t j = 0; j < k; ++j) outer *= d.extents[j];
+        for (std::size_t j = k + 1; j < d.rank; ++j) inner *= d.extents[j];
+        AxisSpec a{c, d.extents[k], outer, inner};
+        a.d.extents = {d.extents[k]};
+        a.d.batch = outer * inner;
+        a.d.input_batch_stride = a.d.output_batch_stride = d.extents[k];
+        axes.push_back(a);
+    }
+    return axes;
+}
+
+std::size_t align256(std::size_t v) { return (v + 255) / 256 * 256; }
+
+std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    std::size_t volume = 1;
+    for (auto e : d.extents) volume *= e;
+    p->packed_bytes = align256(d.batch * volume * cubf::storage_bytes(d.storage));
+    bool flat = false;
+    const auto specs = composite_axes(d, flat);
+    p->flat = flat;
+    const bool two_buffers = d.op == CUBUTTERFLY_OPERATOR_FFT || d.op == CUBUTTERFLY_OPERATOR_NTT;
+    std::size_t offset = flat ? 0 : p->packed_bytes * (two_buffers ? 2 : 1);
+    std::ostringstream name, reason;
+    name << "composite[";
+    cubutterflySelectionSource_t source = CUBUTTERFLY_SELECTION_STATIC_MODEL;
+    for (std::size_t i = 0; i < specs.size(); ++i) {
+        cubutterflyPlan::Axis ax;
+        ax.plan = create_rank1(handle, cubf::normalize(specs[i].d));
+        ax.n = specs[i].n;
+        ax.outer = specs[i].outer;
+        ax.inner = specs[i].inner;
+        ax.ws_offset = offset;
+        offset += align256(ax.plan->mapping.workspace_bytes);
+        const std::string label = flat || specs.size() == 1 ? "flat" : "axis" + std::to_string(d.rank - 1 - i);
+        name << (i ? "," : "") << label << ":" << ax.plan->mapping.name();
+        reason << (i ? "; " : "") << label << ": " << ax.plan->reason;
+        if (ax.plan->source != CUBUTTERFLY_SELECTION_STATIC_MODEL) source = ax.plan->source;
+        p->axes.push_back(std::move(ax));
+    }
+    name << "]";
+    p->mapping.family = "composite";
+    p->mapping.label = name.str();
+    p->mapping.workspace_bytes = offset;
+    p->source = source;
+    p->reason = "rank-" + std::to_string(d.rank) + " composition of rank-one plans: " + reason.str();
+    return p;
+}
+
+// Mapping JSON of a composite plan: its children, in execution order.
+cubf::Json composite_json(const cubutterflyPlan& p) {
+    cubf::Json axes = cubf::Json::array();
+    for (const auto& ax : p.axes)
+        axes.push_back({{"length", ax.n}, {"outer", ax.outer}, {"inner", ax.inner},
+                        {"mapping", ax.plan->mapping.to_json()}});
+    return {{"schema", "cubutterfly-b200-mapping-v1"},
+            {"family", "composite"},
+            {"name", p.mapping.name()},
+            {"flat", p.flat},
+            {"axes", axes},
+            {"workspace_bytes", p.mapping.workspace_bytes}};
+}
+
+}  // namespace
+
+namespace cubf {
 void set_last_error(const std::string& message) { last_error = message; }
 }  // namespace cubf
 
@@ -870,28 +1074,13 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
     return protect([&] {
         require(handle != nullptr && plan != nullptr, "handle and plan pointer must be non-null");
         *plan = nullptr;
-        auto p = std::make_unique<cubutterflyPlan>();
-        p->desc = cubf::normalize(desc_of(descriptor));
-        const cubf::Json caps = cubf::capabilities(p->desc);
+        const cubf::Descriptor d = cubf::normalize(desc_of(descriptor));
+        const cubf::Json caps = cubf::capabilities(d);
         if (caps.at("status") != "eligible") {
             const auto& gap = caps.at("gaps").at(0);
             throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
         }
-        const std::size_t esz = cubf::storage_bytes(p->desc.storage);
-        // bytes spanned by a layout: its largest element offset + 1
-        auto span = [&](const std::vector<std::size_t>& ext, const std::vector<std::size_t>& str, std::size_t bs) {
-            std::size_t last = (p->desc.batch - 1) * bs;
-            for (std::size_t a = 0; a < ext.size(); ++a) last += (ext[a] - 1) * str[a];
-            return (last + 1) * esz;
-        };
-        p->input_bytes = span(cubf::input_extents(p->desc), p->desc.input_strides, p->desc.input_batch_stride);
-        p->output_bytes = span(cubf::output_extents(p->desc), p->desc.output_strides, p->desc.output_batch_stride);
-        p->req = make_request(p->desc);
-        p->hw = cubf::resolve_profile();
-        check_cuda(cudaGetDevice(&p->device), "current device");
-        build_tables(*p);  // before selection: MEASURE executes the candidates
-        select_mapping(handle, *p);
-        make_lanes(*p);
+        auto p = d.rank == 1 ? create_rank1(handle, d) : create_composite(handle, d);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
         *plan = p.release();
     });
@@ -961,7 +1150,7 @@ cubutterflyStatus_t cubutterflyPlanGetSelectionReason(cubutterflyPlan_t plan, ch
 cubutterflyStatus_t cubutterflyPlanGetMappingJson(cubutterflyPlan_t plan, char* json, size_t* bytes) {
     return protect([&] {
         require(plan != nullptr, "plan must be non-null");
-        cubf::Json j = plan->mapping.to_json();
+        cubf::Json j = plan->axes.empty() ? plan->mapping.to_json() : composite_json(*plan);
         j["hardware"] = plan->hw.to_json();
         copy_text(j.dump(), json, bytes);
     });
@@ -1029,7 +1218,20 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         const cubf::HardwareProfile hw = hardware_json ? cubf::profile_from_json(cubf::Json::parse(hardware_json))
                                                        : cubf::resolve_profile();
         cubf::Json out = cubf::Json::array();
-        for (const auto& m : cubf::enumerate_mappings(make_request(d), hw)) out.push_back(m.to_json());
+        if (d.rank == 1) {
+            for (const auto& m : cubf::enumerate_mappings(make_request(d), hw)) out.push_back(m.to_json());
+        } else {
+            // a composite: the best mapping of every child, in execution order
+            bool flat = false;
+            cubf::Json axes = cubf::Json::array();
+            for (const auto& a : composite_axes(d, flat)) {
+                const cubf::Descriptor c = cubf::normalize(a.d);
+                axes.push_back({{"length", a.n}, {"outer", a.outer}, {"inner", a.inner},
+                                {"mapping", cubf::enumerate_mappings(make_request(c), hw).front().to_json()}});
+            }
+            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"}, {"family", "composite"}, {"flat", flat},
+                           {"axes", axes}});
+        }
         copy_text(out.dump(), json, bytes);
     });
 }

@@ -484,7 +484,11 @@ Json capabilities(const Descriptor& source) {
     const Descriptor d = normalize(source);
     Json gaps = Json::array();
     auto gap = [&](const char* code, const char* reason) { gaps.push_back({{"code", code}, {"reason", reason}}); };
-    if (d.rank != 1) gap("rank-lowering", "this build executes rank-one transforms only");
+    // Ranks two and three run as compositions of rank-one plans: FFT and NTT
+    // one per axis (innermost first, the other axes transposed innermost
+    // through the workspace), FWHT and zeta as one transform over the
+    // concatenated index bits (the tensor product of the per-axis transforms).
+    if (d.rank > 3) gap("rank-lowering", "ranks above three are not built");
     if (d.execution_mode == CUBUTTERFLY_EXECUTION_XD) gap("execution-policy", "xD execution is not built");
     if (d.length_mode != CUBUTTERFLY_LENGTH_STANDARD)
         gap("length-lowering", "zero-extended embedding is not built");
@@ -494,7 +498,20 @@ Json capabilities(const Descriptor& source) {
     if (d.fft_type == CUBUTTERFLY_FFT_C2C && d.fft_output_scale != 1.0)
         gap("fft-scale-lowering", "additional FFT output scaling requires R2C/C2R");
     const auto in = input_extents(d), out = output_extents(d);
-    const std::size_t n = d.extents[0];
+    // FWHT and zeta of rank > 1 transform the flattened index; FFT and NTT
+    // each axis (bounded by the largest axis)
+    std::size_t n = 1, longest = 1;
+    for (auto e : d.extents) {
+        n *= e;
+        longest = std::max(longest, e);
+    }
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT || d.op == CUBUTTERFLY_OPERATOR_NTT) n = longest;
+    if (d.rank > 1 && !std::all_of(d.input_orders.begin(), d.input_orders.end(),
+                                   [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
+        gap("order-lowering", "bit-reversed logical orders are built for rank-one transforms");
+    if (d.rank > 1 && !std::all_of(d.output_orders.begin(), d.output_orders.end(),
+                                   [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
+        gap("order-lowering", "bit-reversed logical orders are built for rank-one transforms");
     const bool packed = d.rank == 1 && d.input_strides == std::vector<std::size_t>{1} &&
                         d.output_strides == std::vector<std::size_t>{1} && d.input_batch_stride == in[0] &&
                         d.output_batch_stride == out[0];

@@ -142,5 +142,10 @@ cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, 
 cudaError_t launch_strided_copy(int elem_bytes, const void* in, std::size_t in_stride, std::size_t in_batch_stride,
                                 void* out, std::size_t out_stride, std::size_t out_batch_stride, std::size_t n,
                                 std::size_t batch, cudaStream_t stream);
+// The same over dims = 1..3 axes (extents, per-axis strides in elements).
+cudaError_t launch_strided_copy_nd(int elem_bytes, int dims, const std::size_t* extents, const void* in,
+                                   const std::size_t* in_strides, std::size_t in_batch_stride, void* out,
+                                   const std::size_t* out_strides, std::size_t out_batch_stride, std::size_t batch,
+                                   cudaStream_t stream);
 
 }  // namespace cubf

@@ -312,6 +312,7 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
 }
 
 std::string Mapping::name() const {
+    if (!label.empty()) return label;
     std::ostringstream o;
     if (staged) o << "gather+";
     if (permute_input) o << "bitrev+";

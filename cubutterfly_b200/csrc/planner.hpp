@@ -66,6 +66,7 @@ struct Mapping {
     std::size_t staged_bytes = 0;
     std::size_t workspace_bytes = 0;
     double predicted_us = 0.0;
+    std::string label;  // replaces the derived name when set (composite plans)
     std::string name() const;
     Json to_json() const;
 };

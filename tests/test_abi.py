@@ -121,7 +121,7 @@ def test_benchmark_configs_are_eligible(lib):
 
 
 @pytest.mark.parametrize("transform, code", [
-    (cb.Transform(op=cb.Operator.FFT, extents=[8, 8]), "rank-lowering"),
+    (cb.Transform(op=cb.Operator.FFT, extents=[8, 8], output_orders=[1, 1]), "order-lowering"),
     (cb.Transform(op=cb.Operator.FFT, extents=[12]), "length-lowering"),
     (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, extents=[64]), "storage-lowering"),
@@ -271,6 +271,25 @@ def test_strided_layouts_are_staged(lib, transform):
     assert m["boundary"]["staged_layout"] and m["boundary"]["staged_bytes"] >= n * b * esz
     assert m["workspace_bytes"] >= m["boundary"]["staged_bytes"]
     assert m["name"].startswith("gather+") and m["name"].endswith("+scatter")
+
+
+def test_rank_two_and_three_compose_rank_one_plans(lib):
+    """FFT / NTT: one rank-one child per axis, innermost first; FWHT / zeta:
+    one child over the flattened index (the tensor product of the per-axis
+    transforms)."""
+    (m,) = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[64, 1024], batch=3))
+    assert m["family"] == "composite" and not m["flat"]
+    assert [(a["length"], a["outer"], a["inner"]) for a in m["axes"]] == [(1024, 192, 1), (64, 3, 1024)]
+    (m,) = rank(lib, cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[16, 32, 64], batch=2,
+                                  modulus=998244353, word_bits=64))
+    assert [a["length"] for a in m["axes"]] == [64, 32, 16]
+    assert all(a["mapping"]["name"].startswith("bitrev+ntt-tile-gs") for a in m["axes"])
+    (m,) = rank(lib, cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32,
+                                  extents=[2, 2, 2]))
+    assert m["flat"] and m["axes"][0]["length"] == 8
+    (m,) = rank(lib, cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1024, 1024],
+                                  batch=2, input_strides=[2048, 1], input_batch_stride=1024 * 2048))
+    assert not m["flat"] and m["axes"][0]["length"] == 1 << 20
 
 
 def test_bit_reversed_orders_need_packed_batches(lib):

@@ -1,0 +1,112 @@
+"""Rank-two and rank-three transforms on the GPU through the C ABI (composite
+plans of rank-one children): FFT and NTT against the oracle applied along
+every axis, FWHT and zeta against the oracle on the flattened index, and the
+reference C test's rank-three FWHT known answer."""
+import numpy as np
+import pytest
+import torch
+
+import cubutterfly_b200 as cb
+from conftest import rel_l2
+from cubutterfly_b200 import workloads as w
+
+pytestmark = pytest.mark.gpu
+
+
+def run_nd(lib, t, x, cuda, sentinel=0):
+    """x: (batch, *extents) logical values placed in t's input layout."""
+    from gpu_util import stream_ptr
+
+    dims = len(t.extents)
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        esz = x.dtype.itemsize
+        istr = t.input_strides or list(np.cumprod([1] + t.extents[::-1][:-1])[::-1])
+        ostr = t.output_strides or istr
+        vol = int(np.prod(t.extents))
+        ibs = t.input_batch_stride or vol
+        obs = t.output_batch_stride or vol
+        host = np.full(plan.input_size() // esz, sentinel, dtype=x.dtype)
+        grids = np.indices((t.batch, *t.extents)).reshape(dims + 1, -1)
+        off_in = grids[0] * ibs + sum(grids[k + 1] * istr[k] for k in range(dims))
+        off_out = grids[0] * obs + sum(grids[k + 1] * ostr[k] for k in range(dims))
+        host[off_in] = x.reshape(-1)
+        din = torch.from_numpy(host.view(np.uint8).copy()).to(cuda)
+        dout = din if t.in_place else torch.zeros(plan.output_size(), dtype=torch.uint8, device=cuda)
+        ws = None
+        if plan.workspace_size():
+            ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=cuda)
+            plan.set_workspace(ws.data_ptr(), ws.numel())
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        raw = dout.cpu().numpy().view(x.dtype)
+        return raw[off_out].reshape(x.shape), plan.algorithm_name()
+
+
+def along_axes(fn, x):
+    """Apply a rank-one batched transform (rows of the last axis) along every
+    transformed axis of x (batch, *extents)."""
+    y = x
+    for axis in range(1, x.ndim):
+        moved = np.moveaxis(y, axis, -1)
+        shape = moved.shape
+        out = fn(np.ascontiguousarray(moved).reshape(-1, shape[-1])).reshape(shape)
+        y = np.moveaxis(out, -1, axis)
+    return y
+
+
+def test_rank_three_fwht_known_answer(lib, cuda):
+    """tests/test_c_api.c:698 of the reference: FWHT of 1..8 as 2 x 2 x 2."""
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[2, 2, 2])
+    got, name = run_nd(lib, t, np.arange(1, 9, dtype=np.float32).reshape(1, 2, 2, 2), cuda)
+    assert name.startswith("composite[flat:")
+    assert np.array_equal(got.reshape(-1), np.array([36, -4, -8, 0, -16, 0, 0, 0], dtype=np.float32))
+
+
+@pytest.mark.parametrize("extents, batch", [([64, 128], 3), ([8, 16, 32], 2), ([4, 1 << 14], 1), ([2, 4096], 2)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_fft_composite(lib, oracle, cuda, extents, batch, inverse):
+    vol = int(np.prod(extents))
+    x = w.fft_input(vol, batch, seed=vol).reshape(batch, *extents)
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=extents, batch=batch,
+                     inverse=inverse, normalize_inverse=True)
+    got, name = run_nd(lib, t, x, cuda)
+    want = along_axes(lambda r: oracle.fft_c32(r, inverse=inverse, normalize=True), x)
+    assert name.startswith("composite[")
+    assert rel_l2(got, want) <= 2e-6, name
+
+
+def test_fft_composite_padded_layout_in_place(lib, oracle, cuda):
+    extents, batch = [32, 64], 2
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=extents, batch=batch,
+                     input_strides=[80, 1], output_strides=[80, 1], input_batch_stride=32 * 80 + 16,
+                     output_batch_stride=32 * 80 + 16, in_place=True)
+    x = w.fft_input(2048, batch, seed=3).reshape(batch, *extents)
+    got, _ = run_nd(lib, t, x, cuda, sentinel=np.complex64(1 + 2j))
+    assert rel_l2(got, along_axes(lambda r: oracle.fft_c32(r), x)) <= 2e-6
+
+
+@pytest.mark.parametrize("inverse", [False, True])
+def test_ntt_composite(lib, oracle, cuda, inverse):
+    q = 998244353
+    extents, batch = [16, 256], 2
+    x = w.rng(5).integers(0, q, size=(batch, *extents), dtype=np.uint64)
+    t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=extents, batch=batch, modulus=q,
+                     inverse=inverse)
+    got, _ = run_nd(lib, t, x, cuda)
+    assert np.array_equal(got, along_axes(lambda r: oracle.ntt_cyclic(r, q, inverse), x))
+
+
+def test_zeta_and_fwht_composite(lib, oracle, cuda):
+    z = w.zeta_input(12, 2, seed=7).reshape(2, 64, 64)
+    t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[64, 64], batch=2,
+                     input_strides=[128, 2], output_strides=[64, 1], input_batch_stride=64 * 128,
+                     output_batch_stride=4096)
+    got, name = run_nd(lib, t, z, cuda)
+    assert np.array_equal(got.reshape(2, -1), oracle.zeta(z.reshape(2, -1)))
+    bits = w.fwht_input_bits(4, 4096, seed=8)
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32, extents=[64, 64],
+                     batch=4, output_scale=1 / 64, output_rounding=cb.OutputRounding.FINAL_STORAGE)
+    got, name = run_nd(lib, t, bits.reshape(4, 64, 64), cuda)
+    assert name.startswith("composite[flat:")
+    want = oracle.fwht_bf16_final(bits, 1 / 64)
+    assert rel_l2(w.bf16_bits_to_f32(got.reshape(4, -1)), w.bf16_bits_to_f32(want)) <= 4e-3

@@ -861,15 +861,7 @@ cubutterflyStatus_t cubutterflySetCachePath(cubutterflyHandle_t handle, const ch
     });
 }
 
-int cubutterflyPackRealFp32(const float*, void*, size_t, float, uint64_t) {
-    last_error = "real-FFT packing is not built in cubutterfly_b200";
-    return CUBUTTERFLY_STATUS_NOT_SUPPORTED;
-}
-
-int cubutterflyExpandHermitianFp32(const void*, void*, uint32_t, uint32_t, size_t, uint64_t) {
-    last_error = "Hermitian expansion is not built in cubutterfly_b200";
-    return CUBUTTERFLY_STATUS_NOT_SUPPORTED;
-}
+// cubutterflyPackRealFp32 and cubutterflyExpandHermitianFp32 live in real_adapter.cu.
 
 cubutterflyStatus_t cubutterflyCreateDescriptor(cubutterflyDescriptor_t* descriptor) {
     return protect([&] {

@@ -110,3 +110,36 @@ def test_zeta_and_fwht_composite(lib, oracle, cuda):
     assert name.startswith("composite[flat:")
     want = oracle.fwht_bf16_final(bits, 1 / 64)
     assert rel_l2(w.bf16_bits_to_f32(got.reshape(4, -1)), w.bf16_bits_to_f32(want)) <= 4e-3
+
+
+def test_legacy_real_fft_adapters(lib, oracle, cuda):
+    """cubutterflyPackRealFp32 and cubutterflyExpandHermitianFp32 (reference
+    src/real_fft_adapter.cu): real input -> complex (scaled) -> rank-two FFT
+    -> half spectrum -> full spectrum rebuilt from Hermitian symmetry."""
+    import ctypes as ct
+
+    from gpu_util import stream_ptr
+
+    dll = lib._dll
+    dll.cubutterflyPackRealFp32.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_float, ct.c_uint64]
+    dll.cubutterflyExpandHermitianFp32.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_uint32, ct.c_uint32, ct.c_size_t,
+                                                   ct.c_uint64]
+    batch, h, wd = 2, 16, 32
+    real = w.rng(9).uniform(-1, 1, size=(batch, h, wd)).astype(np.float32)
+    din = torch.from_numpy(real.copy()).to(cuda)
+    packed = torch.empty((batch, h, wd, 2), dtype=torch.float32, device=cuda)
+    assert dll.cubutterflyPackRealFp32(din.data_ptr(), packed.data_ptr(), real.size, 0.5, stream_ptr()) == 0
+    torch.cuda.synchronize()
+    got = packed.cpu().numpy()
+    assert np.array_equal(got[..., 0], real * np.float32(0.5)) and not got[..., 1].any()
+    assert dll.cubutterflyPackRealFp32(None, packed.data_ptr(), 4, 1.0, stream_ptr()) == 1
+
+    x = (real * np.float32(0.5)).astype(np.complex64)
+    spectrum = along_axes(lambda r: oracle.fft_c32(r), x)
+    half = np.ascontiguousarray(spectrum[..., : wd // 2 + 1])
+    dh = torch.from_numpy(half.view(np.float32).copy()).to(cuda)
+    full = torch.empty((batch, h, wd, 2), dtype=torch.float32, device=cuda)
+    assert dll.cubutterflyExpandHermitianFp32(dh.data_ptr(), full.data_ptr(), h, wd, batch, stream_ptr()) == 0
+    torch.cuda.synchronize()
+    rebuilt = full.cpu().numpy().view(np.complex64).reshape(batch, h, wd)
+    assert rel_l2(rebuilt, spectrum) <= 1e-6

@@ -81,11 +81,16 @@ struct cubutterflyPlan {
     std::vector<Axis> axes;
     bool flat = false;
     std::size_t packed_bytes = 0;  // one packed copy of the tensor (256-byte aligned)
+    // R2C / C2R: axes[0] is the N/2-point complex FFT; the half-length
+    // spectrum lives at the start of the workspace (packed_bytes).
+    cubutterflyFftTransformType_t real_kind = CUBUTTERFLY_FFT_C2C;
+    void* real_tw = nullptr;  // W_N^k, k = 0..N/2, complex fp32
     ~cubutterflyPlan() {
         if (twiddles) cudaFree(twiddles);
         if (outer_lo) cudaFree(outer_lo);
         if (outer_hi) cudaFree(outer_hi);
         if (ntt_block) cudaFree(ntt_block);
+        if (real_tw) cudaFree(real_tw);
         for (auto e : {ev_fork, ev_handoff, ev_done[0], ev_done[1], ev_join[0], ev_join[1]})
             if (e) cudaEventDestroy(e);
         for (auto l : lanes)
@@ -333,8 +338,36 @@ void launch_composite(const cubutterflyPlan& p, const void* in, void* out, cudaS
 // A strided or padded layout is gathered into the packed buffer at the start
 // of the workspace, transformed there in place and scattered to the output
 // layout (the reference's general strided boundary, src/general_kernels.cu).
+// R2C: the real input read as N/2 complex values -> complex FFT into the
+// workspace -> split into N/2 + 1 bins.  C2R: bins -> N/2 complex values in
+// the workspace -> inverse complex FFT written as the real output.
+void launch_real(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const std::size_t half = d.extents[0] / 2;
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    auto& c = *p.axes.front().plan;
+    c.workspace = ws + p.axes.front().ws_offset;
+    if (p.real_kind == CUBUTTERFLY_FFT_R2C) {
+        launch_mapping(c, c.mapping, in, ws, stream);
+        check_cuda(cubf::launch_r2c_post(ws, out, p.real_tw, half, d.batch, d.output_batch_stride,
+                                         static_cast<float>(d.fft_output_scale), stream),
+                   "R2C split launch");
+        return;
+    }
+    double scale = 2.0 * d.fft_output_scale;  // the half-length inverse yields (N/2) z
+    if (d.normalize_inverse) scale /= static_cast<double>(d.extents[0]);
+    check_cuda(cubf::launch_c2r_pre(in, ws, p.real_tw, half, d.batch, d.input_batch_stride, static_cast<float>(scale),
+                                    stream),
+               "C2R merge launch");
+    launch_mapping(c, c.mapping, ws, out, stream);
+}
+
 void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                     cudaStream_t stream) {
+    if (p.real_kind != CUBUTTERFLY_FFT_C2C) {
+        launch_real(p, in, out, stream);
+        return;
+    }
     if (!p.axes.empty()) {
         launch_composite(p, in, out, stream);
         return;
@@ -773,6 +806,66 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
     return p;
 }
 
+// The N/2-point complex FFT under an R2C / C2R descriptor.
+cubf::Descriptor real_child(const cubf::Descriptor& d) {
+    cubf::Descriptor c = d;
+    c.fft_type = CUBUTTERFLY_FFT_C2C;
+    c.storage = CUBUTTERFLY_DATA_COMPLEX_FP32;
+    c.compute = CUBUTTERFLY_COMPUTE_FP32;
+    c.extents = {d.extents[0] / 2};
+    c.input_strides = c.output_strides = {1};
+    c.input_batch_stride = c.output_batch_stride = d.extents[0] / 2;
+    c.normalize_inverse = false;  // C2R folds 2 / N into its merge step
+    c.fft_output_scale = 1.0;
+    c.placement = CUBUTTERFLY_PLACEMENT_OUT_OF_PLACE;
+    if (c.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
+        c.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+        c.explicit_algorithm.clear();
+    }
+    return cubf::normalize(c);
+}
+
+// R2C / C2R over an N/2-point complex FFT child plan.
+std::unique_ptr<cubutterflyPlan> create_real(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->real_kind = d.fft_type;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride) *
+                     (d.fft_type == CUBUTTERFLY_FFT_C2R ? 2 : 1);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride) *
+                      (d.fft_type == CUBUTTERFLY_FFT_R2C ? 2 : 1);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    const std::size_t n = d.extents[0], half = n / 2;
+    const cubf::Descriptor c = real_child(d);
+    p->packed_bytes = align256(d.batch * half * 8);
+    cubutterflyPlan::Axis ax;
+    ax.plan = create_rank1(handle, c);
+    ax.n = half;
+    ax.outer = d.batch;
+    ax.inner = 1;
+    ax.ws_offset = p->packed_bytes;
+    p->mapping.family = d.fft_type == CUBUTTERFLY_FFT_R2C ? "fft-r2c" : "fft-c2r";
+    p->mapping.label = p->mapping.family + "[" + ax.plan->mapping.name() + "]";
+    p->mapping.workspace_bytes = p->packed_bytes + align256(ax.plan->mapping.workspace_bytes);
+    p->source = ax.plan->source;
+    p->reason = std::string(d.fft_type == CUBUTTERFLY_FFT_R2C ? "R2C" : "C2R") + " over an N/2-point complex FFT: " +
+                ax.plan->reason;
+    p->axes.push_back(std::move(ax));
+    // W_N^k = exp(-2 pi i k / N), k = 0..N/2, computed in double, rounded once
+    constexpr double kPi = 3.141592653589793238462643383279502884;
+    std::vector<float> tw(2 * (half + 1));
+    for (std::size_t k = 0; k <= half; ++k) {
+        const double a = -2.0 * kPi * static_cast<double>(k) / static_cast<double>(n);
+        tw[2 * k] = static_cast<float>(std::cos(a));
+        tw[2 * k + 1] = static_cast<float>(std::sin(a));
+    }
+    check_cuda(cudaMalloc(&p->real_tw, tw.size() * sizeof(float)), "real twiddle allocation");
+    check_cuda(cudaMemcpy(p->real_tw, tw.data(), tw.size() * sizeof(float), cudaMemcpyHostToDevice),
+               "real twiddle upload");
+    return p;
+}
+
 // Mapping JSON of a composite plan: its children, in execution order.
 cubf::Json composite_json(const cubutterflyPlan& p) {
     cubf::Json axes = cubf::Json::array();
@@ -780,7 +873,7 @@ cubf::Json composite_json(const cubutterflyPlan& p) {
         axes.push_back({{"length", ax.n}, {"outer", ax.outer}, {"inner", ax.inner},
                         {"mapping", ax.plan->mapping.to_json()}});
     return {{"schema", "cubutterfly-b200-mapping-v1"},
-            {"family", "composite"},
+            {"family", p.mapping.family},
             {"name", p.mapping.name()},
             {"flat", p.flat},
             {"axes", axes},
@@ -1072,7 +1165,9 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
             const auto& gap = caps.at("gaps").at(0);
             throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
         }
-        auto p = d.rank == 1 ? create_rank1(handle, d) : create_composite(handle, d);
+        auto p = d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C ? create_real(handle, d)
+                 : d.rank == 1                                                        ? create_rank1(handle, d)
+                                                                                      : create_composite(handle, d);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
         *plan = p.release();
     });
@@ -1210,7 +1305,15 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         const cubf::HardwareProfile hw = hardware_json ? cubf::profile_from_json(cubf::Json::parse(hardware_json))
                                                        : cubf::resolve_profile();
         cubf::Json out = cubf::Json::array();
-        if (d.rank == 1) {
+        if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C) {
+            const cubf::Descriptor c = real_child(d);
+            cubf::Json axes = cubf::Json::array();
+            axes.push_back({{"length", c.extents[0]}, {"outer", d.batch}, {"inner", 1},
+                            {"mapping", cubf::enumerate_mappings(make_request(c), hw).front().to_json()}});
+            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"},
+                           {"family", d.fft_type == CUBUTTERFLY_FFT_R2C ? "fft-r2c" : "fft-c2r"},
+                           {"axes", axes}});
+        } else if (d.rank == 1) {
             for (const auto& m : cubf::enumerate_mappings(make_request(d), hw)) out.push_back(m.to_json());
         } else {
             // a composite: the best mapping of every child, in execution order

@@ -494,7 +494,23 @@ Json capabilities(const Descriptor& source) {
         gap("length-lowering", "zero-extended embedding is not built");
     for (auto n : d.extents)
         if (!is_pow2(n) || n < 2) gap("length-lowering", "extents must be powers of two of at least two");
-    if (d.fft_type != CUBUTTERFLY_FFT_C2C) gap("real-fft-lowering", "R2C/C2R transforms are not built");
+    // R2C / C2R: rank one, fp32, packed, out of place, over an N/2-point
+    // complex FFT (N >= 4)
+    const bool real_fft = d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C;
+    if (real_fft) {
+        if (d.rank != 1) gap("real-fft-lowering", "R2C/C2R transforms are built for rank one");
+        if (d.storage != CUBUTTERFLY_DATA_FP32)
+            gap("real-fft-lowering", "R2C/C2R transforms execute FP32 real storage");
+        if (d.extents[0] < 4) gap("real-fft-lowering", "R2C/C2R transforms need at least four points");
+        if (d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE)
+            gap("real-fft-lowering", "R2C/C2R transforms execute out of place");
+        const auto ri = side(d, true), ro = side(d, false);
+        if (d.input_strides != std::vector<std::size_t>{1} || d.output_strides != std::vector<std::size_t>{1} ||
+            d.input_batch_stride != ri[0] || d.output_batch_stride != ro[0])
+            gap("layout-lowering", "R2C/C2R transforms execute packed batches");
+        if (!std::isfinite(static_cast<float>(d.fft_output_scale)))
+            gap("fft-scale-lowering", "FFT output scale must be representable as finite FP32");
+    }
     if (d.fft_type == CUBUTTERFLY_FFT_C2C && d.fft_output_scale != 1.0)
         gap("fft-scale-lowering", "additional FFT output scaling requires R2C/C2R");
     const auto in = input_extents(d), out = output_extents(d);
@@ -531,8 +547,8 @@ Json capabilities(const Descriptor& source) {
     const bool epilogue = d.output_scale != 1.0 || d.output_rounding != CUBUTTERFLY_ROUNDING_STAGE_STORAGE;
     switch (d.op) {
         case CUBUTTERFLY_OPERATOR_FFT:
-            if (d.storage != CUBUTTERFLY_DATA_COMPLEX_FP32 || d.compute != CUBUTTERFLY_COMPUTE_FP32)
-                gap("storage-lowering", "FFT executes complex FP32 storage with FP32 compute");
+            if ((d.storage != CUBUTTERFLY_DATA_COMPLEX_FP32 && !real_fft) || d.compute != CUBUTTERFLY_COMPUTE_FP32)
+                gap("storage-lowering", "FFT executes complex FP32 storage (FP32 for R2C/C2R) with FP32 compute");
             if (epilogue) gap("output-epilogue-lowering", "output epilogues apply to FWHT only");
             if (n > (std::size_t{1} << 30)) gap("length-lowering", "FFT length is limited to 2^30");
             break;

@@ -83,6 +83,16 @@ LaunchShape fwht_tc_shape();
 cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream);
 unsigned fwht_tc_take_status();
 
+// ---- real FFTs over an N/2-point complex FFT (csrc/real_fft.cu) -------------------
+// twiddles: W_N^k (complex fp32), k = 0..half.  R2C: z (batch x half, packed)
+// -> x (half + 1 per transform at out_batch_stride), times scale.  C2R: x ->
+// z with the factor 2 of the half-length inverse and the caller's scales in
+// `scale`.
+cudaError_t launch_r2c_post(const void* z, void* x, const void* twiddles, std::size_t half, std::size_t batch,
+                            std::size_t out_batch_stride, float scale, cudaStream_t stream);
+cudaError_t launch_c2r_pre(const void* x, void* z, const void* twiddles, std::size_t half, std::size_t batch,
+                           std::size_t in_batch_stride, float scale, cudaStream_t stream);
+
 // ---- NTT tile passes (RNS ABI and the main-ABI cyclic NTT) ----------------------
 struct NttPolyDesc {
     std::uint64_t in_off;

@@ -292,6 +292,21 @@ def test_rank_two_and_three_compose_rank_one_plans(lib):
     assert not m["flat"] and m["axes"][0]["length"] == 1 << 20
 
 
+def test_real_fft_plans_and_gaps(lib):
+    r2c = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[1 << 16], batch=2,
+                       fft_type=cb.FftType.R2C)
+    (m,) = rank(lib, r2c)
+    assert m["family"] == "fft-r2c" and m["axes"][0]["length"] == 1 << 15
+    assert m["axes"][0]["mapping"]["family"] == "fft-stockham-global"
+    for bad, code in ((cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[64], fft_type=1,
+                                    in_place=True), "real-fft-lowering"),
+                      (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[8, 8], fft_type=1),
+                       "real-fft-lowering"),
+                      (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[64], fft_type=1,
+                                    input_strides=[2], output_strides=[1]), "layout-lowering")):
+        assert code in [g["code"] for g in capabilities(lib, bad)["gaps"]]
+
+
 def test_bit_reversed_orders_need_packed_batches(lib):
     t = cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=64, input_strides=[64], output_strides=[64],
                      input_batch_stride=1, output_batch_stride=1, output_orders=[R])

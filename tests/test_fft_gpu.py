@@ -138,3 +138,48 @@ def test_fft_interleaved_in_place(lib, oracle, cuda):
     x = w.fft_input(n, batch, seed=5)
     got, _ = run(lib, interleaved_transform(n, batch, in_place=True), np.ascontiguousarray(x.T), cuda)
     assert rel_l2(np.ascontiguousarray(got.reshape(n, batch).T), oracle.fft_c32(x)) <= TOL
+
+
+# ---- R2C / C2R (over an N/2-point complex FFT) --------------------------------------
+def run_real(lib, t, x, out_shape, out_dtype, cuda):
+    import torch
+
+    from gpu_util import from_device, stream_ptr, to_device
+
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        din = to_device(x, cuda)
+        assert plan.input_size() == din.numel()
+        dout = torch.empty(plan.output_size(), dtype=torch.uint8, device=cuda)
+        ws = torch.empty(max(plan.workspace_size(), 1), dtype=torch.uint8, device=cuda)
+        plan.set_workspace(ws.data_ptr(), plan.workspace_size())
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        return from_device(dout, out_dtype, out_shape), plan.algorithm_name()
+
+
+@pytest.mark.parametrize("n", [4, 64, 4096, 1 << 15])
+@pytest.mark.parametrize("scale", [1.0, 0.5])
+def test_r2c(lib, oracle, cuda, n, scale):
+    x = w.rng(n).uniform(-1, 1, size=(3, n)).astype(np.float32)
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[n], batch=3, fft_type=cb.FftType.R2C,
+                     fft_output_scale=scale)
+    got, name = run_real(lib, t, x, (3, n // 2 + 1), np.complex64, cuda)
+    want = oracle.fft_c32(x.astype(np.complex64))[:, : n // 2 + 1] * np.float32(scale)
+    assert name.startswith("fft-r2c[")
+    assert rel_l2(got, want) <= TOL, name
+
+
+@pytest.mark.parametrize("n", [4, 64, 4096, 1 << 15])
+@pytest.mark.parametrize("normalize", [True, False])
+def test_c2r(lib, oracle, cuda, n, normalize):
+    real = w.rng(n + 1).uniform(-1, 1, size=(3, n)).astype(np.float32)
+    half = np.ascontiguousarray(oracle.fft_c32(real.astype(np.complex64))[:, : n // 2 + 1])  # Hermitian half
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[n], batch=3, fft_type=cb.FftType.C2R,
+                     inverse=True, normalize_inverse=normalize)
+    got, name = run_real(lib, t, half, (3, n), np.float32, cuda)
+    full = np.concatenate([half, np.conj(half[:, 1:-1][:, ::-1])], axis=1)
+    want = oracle.fft_c32(full, inverse=True, normalize=normalize).real
+    assert name.startswith("fft-c2r[")
+    assert rel_l2(got, want) <= TOL, name
+    if normalize:
+        assert rel_l2(got, real) <= TOL  # round trip R2C -> C2R

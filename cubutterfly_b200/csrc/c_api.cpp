@@ -83,6 +83,7 @@ struct cubutterflyPlan {
     std::size_t packed_bytes = 0;  // one packed copy of the tensor (256-byte aligned)
     // R2C / C2R: axes[0] is the N/2-point complex FFT; the half-length
     // spectrum lives at the start of the workspace (packed_bytes).
+    bool embedded = false;  // zero-extended embedding: axes[0] transforms the padded rows in place
     cubutterflyFftTransformType_t real_kind = CUBUTTERFLY_FFT_C2C;
     void* real_tw = nullptr;  // W_N^k, k = 0..N/2, complex fp32
     ~cubutterflyPlan() {
@@ -362,8 +363,34 @@ void launch_real(const cubutterflyPlan& p, const void* in, void* out, cudaStream
     launch_mapping(c, c.mapping, ws, out, stream);
 }
 
+// Zero-extended embedding: rows of N logical elements in a packed buffer of
+// P = next_pow2(N) per row.  Forward: zero the buffer, gather the N inputs,
+// transform, write all P outputs.  Inverse: gather the P inputs, transform,
+// write the first N outputs of each row.
+void launch_embedded(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const int esz = static_cast<int>(cubf::storage_bytes(d.storage));
+    const std::size_t n = d.extents[0], pn = p.axes.front().n;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    auto& c = *p.axes.front().plan;
+    c.workspace = ws + p.axes.front().ws_offset;
+    if (!inverse) check_cuda(cudaMemsetAsync(ws, 0, d.batch * pn * esz, stream), "embedding zero fill");
+    check_cuda(cubf::launch_strided_copy(esz, in, d.input_strides[0], d.input_batch_stride, ws, 1, pn,
+                                         inverse ? pn : n, d.batch, stream),
+               "embedding gather launch");
+    launch_mapping(c, c.mapping, ws, ws, stream);
+    check_cuda(cubf::launch_strided_copy(esz, ws, 1, pn, out, d.output_strides[0], d.output_batch_stride,
+                                         inverse ? n : pn, d.batch, stream),
+               "embedding scatter launch");
+}
+
 void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                     cudaStream_t stream) {
+    if (p.embedded) {
+        launch_embedded(p, in, out, stream);
+        return;
+    }
     if (p.real_kind != CUBUTTERFLY_FFT_C2C) {
         launch_real(p, in, out, stream);
         return;
@@ -866,6 +893,44 @@ std::unique_ptr<cubutterflyPlan> create_real(cubutterflyHandle* handle, const cu
     return p;
 }
 
+// Zero-extended embedding over a packed plan of the padded length.
+std::unique_ptr<cubutterflyPlan> create_embedded(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->embedded = true;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    std::size_t pn = 1;
+    while (pn < d.extents[0]) pn <<= 1;
+    cubf::Descriptor c = d;
+    c.length_mode = CUBUTTERFLY_LENGTH_STANDARD;
+    c.extents = {pn};
+    c.input_strides = c.output_strides = {1};
+    c.input_batch_stride = c.output_batch_stride = pn;
+    c.placement = CUBUTTERFLY_PLACEMENT_IN_PLACE;
+    if (c.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
+        c.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+        c.explicit_algorithm.clear();
+    }
+    p->packed_bytes = align256(d.batch * pn * cubf::storage_bytes(d.storage));
+    cubutterflyPlan::Axis ax;
+    ax.plan = create_rank1(handle, cubf::normalize(c));
+    ax.n = pn;
+    ax.outer = d.batch;
+    ax.inner = 1;
+    ax.ws_offset = p->packed_bytes;
+    p->mapping.family = "zero-extended";
+    p->mapping.label = "zero-extended[" + ax.plan->mapping.name() + "]";
+    p->mapping.workspace_bytes = p->packed_bytes + align256(ax.plan->mapping.workspace_bytes);
+    p->source = ax.plan->source;
+    p->reason = "zero-extended embedding of " + std::to_string(d.extents[0]) + " points into " + std::to_string(pn) +
+                ": " + ax.plan->reason;
+    p->axes.push_back(std::move(ax));
+    return p;
+}
+
 // Mapping JSON of a composite plan: its children, in execution order.
 cubf::Json composite_json(const cubutterflyPlan& p) {
     cubf::Json axes = cubf::Json::array();
@@ -1165,7 +1230,8 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
             const auto& gap = caps.at("gaps").at(0);
             throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
         }
-        auto p = d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C ? create_real(handle, d)
+        auto p = d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING ? create_embedded(handle, d)
+                 : d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C ? create_real(handle, d)
                  : d.rank == 1                                                        ? create_rank1(handle, d)
                                                                                       : create_composite(handle, d);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
@@ -1305,7 +1371,23 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         const cubf::HardwareProfile hw = hardware_json ? cubf::profile_from_json(cubf::Json::parse(hardware_json))
                                                        : cubf::resolve_profile();
         cubf::Json out = cubf::Json::array();
-        if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C) {
+        if (d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING) {
+            cubf::Descriptor c = d;
+            std::size_t pn = 1;
+            while (pn < d.extents[0]) pn <<= 1;
+            c.length_mode = CUBUTTERFLY_LENGTH_STANDARD;
+            c.extents = {pn};
+            c.input_strides = c.output_strides = {1};
+            c.input_batch_stride = c.output_batch_stride = pn;
+            c.placement = CUBUTTERFLY_PLACEMENT_IN_PLACE;
+            c.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+            c.explicit_algorithm.clear();
+            c = cubf::normalize(c);
+            cubf::Json axes = cubf::Json::array();
+            axes.push_back({{"length", pn}, {"outer", d.batch}, {"inner", 1},
+                            {"mapping", cubf::enumerate_mappings(make_request(c), hw).front().to_json()}});
+            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"}, {"family", "zero-extended"}, {"axes", axes}});
+        } else if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C) {
             const cubf::Descriptor c = real_child(d);
             cubf::Json axes = cubf::Json::array();
             axes.push_back({{"length", c.extents[0]}, {"outer", d.batch}, {"inner", 1},

@@ -490,10 +490,24 @@ Json capabilities(const Descriptor& source) {
     // concatenated index bits (the tensor product of the per-axis transforms).
     if (d.rank > 3) gap("rank-lowering", "ranks above three are not built");
     if (d.execution_mode == CUBUTTERFLY_EXECUTION_XD) gap("execution-policy", "xD execution is not built");
-    if (d.length_mode != CUBUTTERFLY_LENGTH_STANDARD)
-        gap("length-lowering", "zero-extended embedding is not built");
+    // Zero-extended embedding (the forward input / inverse output zero-padded
+    // to the next power of two) runs staged through a packed buffer of the
+    // padded length: rank one, out of place.
+    const bool embedded = d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING;
+    if (embedded) {
+        if (d.rank != 1) gap("length-lowering", "zero-extended embedding is built for rank one");
+        if (d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE)
+            gap("length-lowering", "zero-extended embedding executes out of place");
+        if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C)
+            gap("length-lowering", "zero-extended embedding is built for complex FFTs");
+        if (!std::all_of(d.input_orders.begin(), d.input_orders.end(),
+                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }) ||
+            !std::all_of(d.output_orders.begin(), d.output_orders.end(),
+                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
+            gap("order-lowering", "zero-extended embedding executes natural logical orders");
+    }
     for (auto n : d.extents)
-        if (!is_pow2(n) || n < 2) gap("length-lowering", "extents must be powers of two of at least two");
+        if ((!is_pow2(n) && !embedded) || n < 2) gap("length-lowering", "extents must be powers of two of at least two");
     // R2C / C2R: rank one, fp32, packed, out of place, over an N/2-point
     // complex FFT (N >= 4)
     const bool real_fft = d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C;
@@ -518,6 +532,7 @@ Json capabilities(const Descriptor& source) {
     // each axis (bounded by the largest axis)
     std::size_t n = 1, longest = 1;
     for (auto e : d.extents) {
+        if (embedded) e = next_pow2(e);  // the padded (physical) length
         n *= e;
         longest = std::max(longest, e);
     }

@@ -307,6 +307,18 @@ def test_real_fft_plans_and_gaps(lib):
         assert code in [g["code"] for g in capabilities(lib, bad)["gaps"]]
 
 
+def test_zero_extended_embedding_pads_to_a_power_of_two(lib):
+    t = cb.Transform(op=cb.Operator.FFT, extents=[1000], batch=2, length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    assert capabilities(lib, t)["status"] == "eligible"
+    (m,) = rank(lib, t)
+    assert m["family"] == "zero-extended" and m["axes"][0]["length"] == 1024
+    bad = cb.Transform(op=cb.Operator.FFT, extents=[1000], in_place=True,
+                       length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    assert "length-lowering" in [g["code"] for g in capabilities(lib, bad)["gaps"]]
+    std = cb.Transform(op=cb.Operator.FFT, extents=[1000])
+    assert "length-lowering" in [g["code"] for g in capabilities(lib, std)["gaps"]]
+
+
 def test_bit_reversed_orders_need_packed_batches(lib):
     t = cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=64, input_strides=[64], output_strides=[64],
                      input_batch_stride=1, output_batch_stride=1, output_orders=[R])

@@ -121,3 +121,59 @@ def test_ntt_strided(lib, oracle, cuda, n):
     got, raw, idx = run_layout(lib, t, x, np.uint64(12345), cuda)
     assert np.array_equal(got, oracle.ntt_cyclic(x, q))
     assert padding_untouched(raw, idx, np.uint64(12345))
+
+
+# ---- zero-extended embedding (non-power-of-two logical lengths) ---------------------
+def run_sides(lib, t, x, out_len, out_dtype, cuda):
+    from gpu_util import from_device, stream_ptr, to_device
+
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        din = to_device(x, cuda)
+        assert plan.input_size() == din.numel()
+        dout = torch.empty(plan.output_size(), dtype=torch.uint8, device=cuda)
+        ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=cuda)
+        plan.set_workspace(ws.data_ptr(), ws.numel())
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        return from_device(dout, out_dtype, (t.batch, out_len)), plan.algorithm_name()
+
+
+def test_zero_extended_fft_forward_and_inverse(lib, oracle, cuda):
+    n, p = 1000, 1024
+    x = w.fft_input(n, 3, seed=10)
+    t = cb.Transform(op=cb.Operator.FFT, extents=[n], batch=3, length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    got, name = run_sides(lib, t, x, p, np.complex64, cuda)
+    padded = np.zeros((3, p), dtype=np.complex64)
+    padded[:, :n] = x
+    assert name.startswith("zero-extended[")
+    assert rel_l2(got, oracle.fft_c32(padded)) <= 2e-6
+    spec = w.fft_input(p, 3, seed=11)
+    t = cb.Transform(op=cb.Operator.FFT, extents=[n], batch=3, inverse=True,
+                     length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    got, _ = run_sides(lib, t, spec, n, np.complex64, cuda)
+    assert rel_l2(got, oracle.fft_c32(spec, inverse=True)[:, :n]) <= 2e-6
+
+
+def test_zero_extended_fwht_zeta_ntt(lib, oracle, cuda):
+    x = w.rng(12).uniform(-1, 1, size=(2, 100)).astype(np.float32)
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[100],
+                     batch=2, length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    got, _ = run_sides(lib, t, x, 128, np.float32, cuda)
+    padded = np.zeros((2, 128), dtype=np.float32)
+    padded[:, :100] = x
+    assert rel_l2(got, oracle.fwht_f32(padded, normalize=False)) <= 1e-6
+    z = w.rng(13).integers(0, 1 << 20, size=(2, 3000), dtype=np.uint32)
+    t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[3000], batch=2,
+                     length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    got, _ = run_sides(lib, t, z, 4096, np.uint32, cuda)
+    zp = np.zeros((2, 4096), dtype=np.uint32)
+    zp[:, :3000] = z
+    assert np.array_equal(got, oracle.zeta(zp))
+    q = 998244353
+    v = w.rng(14).integers(0, q, size=(2, 1000), dtype=np.uint64)
+    t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[1000], batch=2, modulus=q,
+                     length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
+    got, _ = run_sides(lib, t, v, 1024, np.uint64, cuda)
+    vp = np.zeros((2, 1024), dtype=np.uint64)
+    vp[:, :1000] = v
+    assert np.array_equal(got, oracle.ntt_cyclic(vp, q))

@@ -84,6 +84,7 @@ struct cubutterflyPlan {
     // R2C / C2R: axes[0] is the N/2-point complex FFT; the half-length
     // spectrum lives at the start of the workspace (packed_bytes).
     bool embedded = false;  // zero-extended embedding: axes[0] transforms the padded rows in place
+    cubf::StructuredStages structured{};  // structured 2x2: per-stage matrices (inverted for an inverse plan)
     cubutterflyFftTransformType_t real_kind = CUBUTTERFLY_FFT_C2C;
     void* real_tw = nullptr;  // W_N^k, k = 0..N/2, complex fp32
     ~cubutterflyPlan() {
@@ -425,6 +426,12 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         launch_ntt(p, m, in, out, stream);
         return;
     }
+    if (d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) {
+        check_cuda(cubf::launch_structured(static_cast<int>(cubf::storage_bytes(d.storage)), p.req.log_n, in, out,
+                                           d.batch, p.structured, stream),
+                   "structured launch");
+        return;
+    }
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
         const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
         if (m.passes.front().kind == cubf::PassKind::FftLocal) {
@@ -585,9 +592,41 @@ void build_ntt_tables(cubutterflyPlan& p) {
     p.ntt_tables = {base, base + n, base + 2 * n, base + 2 * n + 1, base + 2 * n + 2, base + 2 * n + 3};
 }
 
+// Per-stage matrices of a structured 2x2 plan: one shared matrix or one per
+// stage; an inverse plan uses each matrix's inverse, computed in double as the
+// reference does (src/butterfly_reference.cpp:560-570).
+void build_structured(cubutterflyPlan& p) {
+    const auto& ms = p.desc.stage_matrices.at(0);
+    const int l = p.req.log_n;
+    require(ms.size() == 1 || ms.size() == static_cast<std::size_t>(l),
+            "structured 2x2 requires one matrix or one matrix per stage");
+    require(l <= cubf::kStructuredMaxLog, "structured 2x2 length is limited to 2^30");
+    for (int s = 0; s < l; ++s) {
+        const auto& m = ms.size() == 1 ? ms[0] : ms[s];
+        double a = m.m00, b = m.m01, c = m.m10, e = m.m11;
+        if (p.desc.direction == CUBUTTERFLY_DIRECTION_INVERSE) {
+            const double det = m.m00 * m.m11 - m.m01 * m.m10;
+            require(std::isfinite(det) && det != 0.0, "structured 2x2 inverse requires nonsingular matrices");
+            a = m.m11 / det;
+            b = -m.m01 / det;
+            c = -m.m10 / det;
+            e = m.m00 / det;
+        }
+        const double v[4] = {a, b, c, e};
+        for (int k = 0; k < 4; ++k) {
+            p.structured.f64[s][k] = v[k];
+            p.structured.f32[s][k] = static_cast<float>(v[k]);
+        }
+    }
+}
+
 void build_tables(cubutterflyPlan& p) {
     if (p.desc.op == CUBUTTERFLY_OPERATOR_NTT) {
         build_ntt_tables(p);
+        return;
+    }
+    if (p.desc.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) {
+        build_structured(p);
         return;
     }
     if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
@@ -763,8 +802,21 @@ std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat) {
     const bool packed_in = d.input_strides == packed_strides(d.extents) && d.input_batch_stride == volume;
     const bool packed_out = d.output_strides == packed_strides(d.extents) && d.output_batch_stride == volume;
     std::vector<AxisSpec> axes;
+    if (d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) {
+        // the structured transform of a row-major tensor is the one of the
+        // flattened index whose stages are the innermost axis's, then the next
+        std::vector<cubutterflyMatrix2x2_t> flat_stages;
+        for (std::size_t k = d.rank; k-- > 0;) {
+            const auto& ms = d.stage_matrices.at(k);
+            const unsigned bits = cubf::log2_exact(d.extents[k]);
+            require(ms.size() == 1 || ms.size() == bits, "structured axis requires one matrix or one per stage");
+            for (unsigned s = 0; s < bits; ++s) flat_stages.push_back(ms.size() == 1 ? ms[0] : ms[s]);
+        }
+        c.stage_matrices.assign(3, {});
+        c.stage_matrices[0] = flat_stages;
+    }
     if (d.op == CUBUTTERFLY_OPERATOR_FWHT || d.op == CUBUTTERFLY_OPERATOR_SUBSET_ZETA ||
-        d.op == CUBUTTERFLY_OPERATOR_SUPERSET_ZETA) {
+        d.op == CUBUTTERFLY_OPERATOR_SUPERSET_ZETA || d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) {
         // H_N0 (x) H_N1 (x) ... = H_(N0 N1 ...) on the row-major index, and
         // likewise for the subset / superset order: one transform of the
         // concatenated index bits

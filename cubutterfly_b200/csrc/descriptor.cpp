@@ -599,7 +599,15 @@ Json capabilities(const Descriptor& source) {
                 gap("length-lowering", "NTT length is limited to 2^20 (the reference's direct NTT range)");
             break;
         case CUBUTTERFLY_OPERATOR_STRUCTURED_2X2:
-            gap("operator-lowering", "structured 2x2 transforms are not built");
+            // fp32 / fp64 storage computed in its own precision; ranks two and
+            // three run over the flattened index with the axes' stage lists
+            // concatenated (innermost axis = lowest bits)
+            if ((d.storage != CUBUTTERFLY_DATA_FP32 || d.compute != CUBUTTERFLY_COMPUTE_FP32) &&
+                (d.storage != CUBUTTERFLY_DATA_FP64 || d.compute != CUBUTTERFLY_COMPUTE_FP64))
+                gap("storage-lowering", "structured 2x2 executes FP32 or FP64 storage in its own precision");
+            if (!natural_in || !natural_out) gap("order-lowering", "structured 2x2 executes natural logical orders");
+            if (epilogue) gap("output-epilogue-lowering", "output epilogues apply to FWHT only");
+            if (n > (std::size_t{1} << 30)) gap("length-lowering", "structured 2x2 length is limited to 2^30");
             break;
     }
     if (!layout_nonoverlapping(in, d.input_strides, d.batch, d.input_batch_stride) ||

@@ -83,6 +83,19 @@ LaunchShape fwht_tc_shape();
 cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream);
 unsigned fwht_tc_take_status();
 
+// ---- structured 2x2 butterfly (csrc/structured.cu) ---------------------------------
+constexpr int kStructuredMaxLog = 30;
+// Per-stage matrices (m00, m01, m10, m11), already inverted for an inverse
+// transform, in both storage precisions (fp32 values are the fp64 ones cast).
+struct StructuredStages {
+    float f32[kStructuredMaxLog][4];
+    double f64[kStructuredMaxLog][4];
+};
+// `batch` packed transforms of 2^log_n fp32 (elem_bytes 4) or fp64 (8)
+// values; in may equal out.  One tile pass plus one pass per stage >= 12.
+cudaError_t launch_structured(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
+                              const StructuredStages& stages, cudaStream_t stream);
+
 // ---- real FFTs over an N/2-point complex FFT (csrc/real_fft.cu) -------------------
 // twiddles: W_N^k (complex fp32), k = 0..half.  R2C: z (batch x half, packed)
 // -> x (half + 1 per transform at out_batch_stride), times scale.  C2R: x ->

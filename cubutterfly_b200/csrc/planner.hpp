@@ -43,7 +43,17 @@ struct HardwareProfile {
 HardwareProfile resolve_profile();
 HardwareProfile profile_from_json(const Json& j);
 
-enum class PassKind { FftLocal, FftGlobal, BitwiseTile, NttStrided, NttContiguous, NttSingle, FwhtTensor };
+enum class PassKind {
+    FftLocal,
+    FftGlobal,
+    BitwiseTile,
+    NttStrided,
+    NttContiguous,
+    NttSingle,
+    FwhtTensor,
+    StructuredTile,
+    StructuredStage
+};
 
 struct Pass {
     PassKind kind = PassKind::BitwiseTile;

@@ -289,6 +289,76 @@ ORACLE_API int cubf_oracle_zeta_u32(uint32_t* data, size_t n, size_t batch, int 
     return 0;
 }
 
+/* cuntt::reference_structured_2x2 (butterfly_reference.cpp:541-591): stage s
+ * (s = 0 .. log n - 1, in that order) maps each pair (left, right) at index
+ * bit s clear / set to (m00 left + m01 right, m10 left + m11 right) with the
+ * stage's matrix (one shared matrix, or one per stage) cast to the storage
+ * precision; the inverse uses each matrix's inverse computed in double.
+ * mats: 4 doubles (m00, m01, m10, m11) per matrix.  Products and sums are
+ * rounded separately (the oracle is compiled with -ffp-contract=off). */
+static int structured_mats(const double* mats, size_t count, unsigned log_n, int inverse, double* out) {
+    if (count != 1 && count != log_n) return 1;
+    for (unsigned s = 0; s < log_n; ++s) {
+        const double* m = mats + 4 * (count == 1 ? 0 : s);
+        double m00 = m[0], m01 = m[1], m10 = m[2], m11 = m[3];
+        if (!isfinite(m00) || !isfinite(m01) || !isfinite(m10) || !isfinite(m11)) return 1;
+        if (inverse) {
+            const double det = m00 * m11 - m01 * m10;
+            if (!isfinite(det) || det == 0.0) return 1;
+            const double a = m[3] / det, b = -m[1] / det, c = -m[2] / det, d = m[0] / det;
+            m00 = a; m01 = b; m10 = c; m11 = d;
+        }
+        out[4 * s] = m00; out[4 * s + 1] = m01; out[4 * s + 2] = m10; out[4 * s + 3] = m11;
+    }
+    return 0;
+}
+
+ORACLE_API int cubf_oracle_structured_f32(float* data, size_t n, size_t batch, const double* mats, size_t count,
+                                          int inverse) {
+    if (!is_pow2(n)) return 1;
+    const unsigned log_n = log2_exact(n);
+    double m[4 * 64];
+    if (log_n > 64 || structured_mats(mats, count, log_n, inverse, m)) return 1;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        float* v = data + b * n;
+        for (unsigned s = 0; s < log_n; ++s) {
+            const float m00 = (float)m[4 * s], m01 = (float)m[4 * s + 1], m10 = (float)m[4 * s + 2],
+                        m11 = (float)m[4 * s + 3];
+            const size_t half = (size_t)1 << s;
+            for (size_t base = 0; base < n; base += 2 * half)
+                for (size_t o = 0; o < half; ++o) {
+                    const float l = v[base + o], r = v[base + half + o];
+                    v[base + o] = m00 * l + m01 * r;
+                    v[base + half + o] = m10 * l + m11 * r;
+                }
+        }
+    }
+    return 0;
+}
+
+ORACLE_API int cubf_oracle_structured_f64(double* data, size_t n, size_t batch, const double* mats, size_t count,
+                                          int inverse) {
+    if (!is_pow2(n)) return 1;
+    const unsigned log_n = log2_exact(n);
+    double m[4 * 64];
+    if (log_n > 64 || structured_mats(mats, count, log_n, inverse, m)) return 1;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        double* v = data + b * n;
+        for (unsigned s = 0; s < log_n; ++s) {
+            const size_t half = (size_t)1 << s;
+            for (size_t base = 0; base < n; base += 2 * half)
+                for (size_t o = 0; o < half; ++o) {
+                    const double l = v[base + o], r = v[base + half + o];
+                    v[base + o] = m[4 * s] * l + m[4 * s + 1] * r;
+                    v[base + half + o] = m[4 * s + 2] * l + m[4 * s + 3] * r;
+                }
+        }
+    }
+    return 0;
+}
+
 /* uint64 variants, butterfly_reference.cpp:513-538. */
 ORACLE_API int cubf_oracle_zeta_u64(uint64_t* data, size_t n, size_t batch, int superset, int inverse) {
     if (!is_pow2(n)) return 1;

@@ -73,6 +73,8 @@ class Oracle:
         L.cubf_oracle_rns_primes.argtypes = [ct.c_uint, _n, _p]
         L.cubf_oracle_rns_primes.restype = _n
         L.cubf_oracle_ntt_cyclic.argtypes = [_p, _n, _u64, _i]
+        L.cubf_oracle_structured_f32.argtypes = [_p, _n, _n, _p, _n, _i]
+        L.cubf_oracle_structured_f64.argtypes = [_p, _n, _n, _p, _n, _i]
         L.cubf_oracle_rns_ntt_batch.argtypes = [_p, _p, ct.c_uint, _n, _p, _p, _i, _i, _i, _i]
 
     # -- FFT ---------------------------------------------------------------
@@ -148,6 +150,17 @@ class Oracle:
         got = self.lib.cubf_oracle_rns_primes(root_log, count, _ptr(out))
         return [int(v) for v in out[:got]]
 
+    def structured(self, x: np.ndarray, matrices, inverse=False) -> np.ndarray:
+        """Structured 2x2 butterfly of every row (float32 or float64); matrices:
+        one (m00, m01, m10, m11) or one per stage."""
+        y = np.ascontiguousarray(x).copy()
+        m = np.ascontiguousarray(np.asarray(matrices, dtype=np.float64).reshape(-1, 4))
+        n = y.shape[-1]
+        fn = self.lib.cubf_oracle_structured_f32 if y.dtype == np.float32 else self.lib.cubf_oracle_structured_f64
+        if fn(_ptr(y), n, y.size // n, _ptr(m), m.shape[0], int(inverse)):
+            raise ValueError("oracle structured transform rejected its input")
+        return y
+
     def ntt_cyclic(self, x: np.ndarray, q: int, inverse=False) -> np.ndarray:
         """Cyclic NTT of every row of x (natural in, natural out)."""
         y = np.ascontiguousarray(x, dtype=np.uint64).copy()
@@ -192,6 +205,7 @@ class Reference:
         L.cubf_ref_find_root.restype = _u64
         L.cubf_ref_negacyclic_ntt.argtypes = [_p, _p, ct.c_uint, _n, _p, _i]
         L.cubf_ref_ntt_cyclic.argtypes = [_p, _n, _n, _u64, _i, _i]
+        L.cubf_ref_structured_f32.argtypes = [_p, _n, _n, _p, _n, _i]
 
     @staticmethod
     def available(path: os.PathLike | None = None) -> bool:
@@ -255,4 +269,12 @@ class Reference:
         n = y.shape[-1]
         if self.lib.cubf_ref_ntt_cyclic(_ptr(y), n, y.size // n, q, int(inverse), threads):
             raise ValueError("reference NTT failed")
+        return y
+
+    def structured_f32(self, x, matrices, inverse=False):
+        y = np.ascontiguousarray(x, dtype=np.float32).copy()
+        m = np.ascontiguousarray(np.asarray(matrices, dtype=np.float64).reshape(-1, 4))
+        n = y.shape[-1]
+        if self.lib.cubf_ref_structured_f32(_ptr(y), n, y.size // n, _ptr(m), m.shape[0], int(inverse)):
+            raise ValueError("reference structured transform failed")
         return y

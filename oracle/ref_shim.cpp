@@ -185,5 +185,23 @@ int cubf_ref_ntt_cyclic(std::uint64_t* data, std::size_t n, std::size_t batch, s
     return 0;
 }
 
-int cubf_ref_abi_version(void) { return 2; }
+// The reference's structured 2x2 butterfly (reference_structured_2x2,
+// src/butterfly_reference.cpp:541-591); mats: 4 doubles per matrix.
+int cubf_ref_structured_f32(float* data, std::size_t n, std::size_t batch, const double* mats, std::size_t count,
+                            int inverse) {
+    try {
+        std::vector<cuntt::ButterflyMatrix2x2> ms(count);
+        for (std::size_t i = 0; i < count; ++i) ms[i] = {mats[4 * i], mats[4 * i + 1], mats[4 * i + 2], mats[4 * i + 3]};
+        for (std::size_t b = 0; b < batch; ++b) {
+            std::vector<float> v(data + n * b, data + n * (b + 1));
+            cuntt::reference_structured_2x2(v, ms, inverse != 0);
+            std::copy(v.begin(), v.end(), data + n * b);
+        }
+    } catch (...) {
+        return 1;
+    }
+    return 0;
+}
+
+int cubf_ref_abi_version(void) { return 3; }
 }

@@ -82,6 +82,18 @@ def main() -> None:
             out[f"ntt_cyc_{q}_{n}_fwd"] = ref.ntt_cyclic(x, q)
             out[f"ntt_cyc_{q}_{n}_inv"] = ref.ntt_cyclic(x, q, inverse=True)
 
+    # Structured 2x2 butterfly (reference_structured_2x2, butterfly_reference.cpp:541-591):
+    # one shared matrix and one matrix per stage, forward and inverse, fp32.
+    xs = w.rng(40).uniform(-1, 1, size=(3, 256)).astype(np.float32)
+    per_stage = w.rng(41).uniform(-1.5, 1.5, size=(8, 4))
+    shared = np.array([[0.75, -0.5, 0.25, 1.25]])
+    out["structured_256_in"] = xs
+    out["structured_256_per_stage"] = per_stage
+    out["structured_256_shared"] = shared
+    out["structured_256_fwd_per_stage"] = ref.structured_f32(xs, per_stage)
+    out["structured_256_inv_per_stage"] = ref.structured_f32(xs, per_stage, inverse=True)
+    out["structured_256_fwd_shared"] = ref.structured_f32(xs, shared)
+
     # Known answers quoted from the reference's C ABI test (tests/test_c_api.c:698):
     # FWHT of 1..8 is {36, -4, -8, 0, -16, 0, 0, 0}.
     out["kat_fwht_8_in"] = np.arange(1, 9, dtype=np.float32)

@@ -126,8 +126,8 @@ def test_benchmark_configs_are_eligible(lib):
     (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.FP32, extents=[64]), "storage-lowering"),
-    (cb.Transform(op=cb.Operator.STRUCTURED_2X2, storage=cb.DataType.FP32, extents=[4],
-                  stage_matrices=[[(1.0, 1.0, 1.0, -1.0)]]), "operator-lowering"),
+    (cb.Transform(op=cb.Operator.STRUCTURED_2X2, storage=cb.DataType.BF16, extents=[4],
+                  stage_matrices=[[(1.0, 1.0, 1.0, -1.0)]]), "storage-lowering"),
 ])
 def test_unsupported_descriptors_report_gaps(lib, transform, code):
     c = capabilities(lib, transform)

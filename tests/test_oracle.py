@@ -108,6 +108,17 @@ def test_cyclic_ntt_round_trip_and_convolution(oracle):
     assert [int(v) for v in got] == conv
 
 
+def test_structured_matches_golden(oracle, golden):
+    """The structured 2x2 restatement equals reference_structured_2x2 bit for bit."""
+    x = golden["structured_256_in"]
+    per_stage, shared = golden["structured_256_per_stage"], golden["structured_256_shared"]
+    assert np.array_equal(oracle.structured(x, per_stage), golden["structured_256_fwd_per_stage"])
+    assert np.array_equal(oracle.structured(x, per_stage, inverse=True), golden["structured_256_inv_per_stage"])
+    assert np.array_equal(oracle.structured(x, shared), golden["structured_256_fwd_shared"])
+    # H_2 in every stage is the unnormalised FWHT
+    assert np.array_equal(oracle.structured(x, [[1.0, 1.0, 1.0, -1.0]]), oracle.fwht_f32(x, normalize=False))
+
+
 def test_rns_primes_and_roots(oracle):
     qs = w.rns_primes()
     assert qs == oracle.rns_primes(17, 32)

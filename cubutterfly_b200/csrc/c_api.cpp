@@ -945,6 +945,25 @@ std::unique_ptr<cubutterflyPlan> create_real(cubutterflyHandle* handle, const cu
     return p;
 }
 
+// FP64 FWHT as the structured 2x2 butterfly: H_2 = [[1, 1], [1, -1]] in every
+// stage (1 * x is exact, so each stage is (l + r, l - r) as in the reference's
+// double FWHT); an inverse normalised by 1/N halves every stage instead, which
+// is exact for a power-of-two N.
+std::unique_ptr<cubutterflyPlan> create_fwht64(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    cubf::Descriptor s = d;
+    s.op = CUBUTTERFLY_OPERATOR_STRUCTURED_2X2;
+    const bool halve = d.direction == CUBUTTERFLY_DIRECTION_INVERSE && d.normalize_inverse;
+    const double h = halve ? 0.5 : 1.0;
+    s.direction = CUBUTTERFLY_DIRECTION_FORWARD;
+    s.normalize_inverse = false;
+    s.stage_matrices.assign(3, {});
+    for (std::size_t k = 0; k < d.rank; ++k) s.stage_matrices[k] = {cubutterflyMatrix2x2_t{h, h, h, -h}};
+    s = cubf::normalize(s);
+    auto p = s.rank == 1 ? create_rank1(handle, s) : create_composite(handle, s);
+    p->mapping.label = "fwht-f64:" + p->mapping.name();
+    return p;
+}
+
 // Zero-extended embedding over a packed plan of the padded length.
 std::unique_ptr<cubutterflyPlan> create_embedded(cubutterflyHandle* handle, const cubf::Descriptor& d) {
     auto p = std::make_unique<cubutterflyPlan>();
@@ -1282,7 +1301,9 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
             const auto& gap = caps.at("gaps").at(0);
             throw cubf::Unsupported(gap.at("code").get<std::string>() + ": " + gap.at("reason").get<std::string>());
         }
-        auto p = d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING ? create_embedded(handle, d)
+        auto p = d.op == CUBUTTERFLY_OPERATOR_FWHT && d.storage == CUBUTTERFLY_DATA_FP64
+                     ? create_fwht64(handle, d)
+                 : d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING ? create_embedded(handle, d)
                  : d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C ? create_real(handle, d)
                  : d.rank == 1                                                        ? create_rank1(handle, d)
                                                                                       : create_composite(handle, d);

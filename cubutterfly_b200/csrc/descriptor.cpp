@@ -489,7 +489,11 @@ Json capabilities(const Descriptor& source) {
     // through the workspace), FWHT and zeta as one transform over the
     // concatenated index bits (the tensor product of the per-axis transforms).
     if (d.rank > 3) gap("rank-lowering", "ranks above three are not built");
-    if (d.execution_mode == CUBUTTERFLY_EXECUTION_XD) gap("execution-policy", "xD execution is not built");
+    // xD execution (reference src/c_api.cpp:4289-4365) needs rank two or
+    // more; where its lowering is unavailable the reference itself runs the
+    // composite path, which is what ranks two and three execute here.
+    if (d.execution_mode == CUBUTTERFLY_EXECUTION_XD && d.rank < 2)
+        gap("execution-policy", "xD execution requires rank at least two");
     // Zero-extended embedding (the forward input / inverse output zero-padded
     // to the next power of two) runs staged through a packed buffer of the
     // padded length: rank one, out of place.
@@ -557,8 +561,10 @@ Json capabilities(const Descriptor& source) {
     // Bit-reversed orders run as bit-reversal permutations of packed batches.
     if ((!natural_in || !natural_out) && interleaved && !packed)
         gap("order-lowering", "bit-reversed logical orders are not built for interleaved FFT batches");
-    if (d.arithmetic_policy != CUBUTTERFLY_ARITHMETIC_STRICT)
-        gap("arithmetic-policy", "FP16 MMA policy is not built");
+    // ALLOW_FP16_MMA only permits tensor-core arithmetic: the reference keeps
+    // its strict selection when no calibrated MMA candidate wins
+    // (src/mapping_selector.cpp:13-42), so the policy itself is no gap here
+    // (normalize limits it to native FP16 FWHT, a storage gap of this build).
     const bool epilogue = d.output_scale != 1.0 || d.output_rounding != CUBUTTERFLY_ROUNDING_STAGE_STORAGE;
     switch (d.op) {
         case CUBUTTERFLY_OPERATOR_FFT:
@@ -568,6 +574,14 @@ Json capabilities(const Descriptor& source) {
             if (n > (std::size_t{1} << 30)) gap("length-lowering", "FFT length is limited to 2^30");
             break;
         case CUBUTTERFLY_OPERATOR_FWHT: {
+            // FP64 runs as the structured 2x2 butterfly with H_2 in every stage
+            // (bit-identical to the reference's double FWHT), no epilogue
+            const bool f64 = d.storage == CUBUTTERFLY_DATA_FP64 && d.compute == CUBUTTERFLY_COMPUTE_FP64;
+            if (f64) {
+                if (epilogue) gap("output-epilogue-lowering", "FP64 FWHT takes no output epilogue");
+                if (!natural_in || !natural_out) gap("order-lowering", "FP64 FWHT executes natural logical orders");
+                break;
+            }
             const bool f32 = d.storage == CUBUTTERFLY_DATA_FP32 && d.compute == CUBUTTERFLY_COMPUTE_FP32;
             const bool low = (d.storage == CUBUTTERFLY_DATA_BF16 || d.storage == CUBUTTERFLY_DATA_FP16) &&
                              d.compute == CUBUTTERFLY_COMPUTE_FP32 &&

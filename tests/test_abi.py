@@ -319,6 +319,23 @@ def test_zero_extended_embedding_pads_to_a_power_of_two(lib):
     assert "length-lowering" in [g["code"] for g in capabilities(lib, std)["gaps"]]
 
 
+def test_execution_and_arithmetic_policies(lib):
+    """xD at rank >= 2 runs the composite path (the reference's own fallback);
+    rank one cannot be xD."""
+    xd = cb.Transform(op=cb.Operator.FFT, extents=[64, 64], execution_mode=cb.ExecutionMode.XD)
+    assert capabilities(lib, xd)["status"] == "eligible"
+    one = cb.Transform(op=cb.Operator.FFT, extents=[64], execution_mode=cb.ExecutionMode.XD)
+    assert "execution-policy" in [g["code"] for g in capabilities(lib, one)["gaps"]]
+    # the descriptor contract limits the policy to native (stage-storage) FP16
+    # FWHT, which this build does not execute: a storage gap, not a policy gap
+    mma = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP16, extents=[4096], batch=8,
+                       arithmetic_policy=cb.ArithmeticPolicy.ALLOW_FP16_MMA)
+    codes = [g["code"] for g in capabilities(lib, mma)["gaps"]]
+    assert "arithmetic-policy" not in codes and "storage-lowering" in codes
+    f64 = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP64, compute=cb.ComputeType.FP64, extents=[1024])
+    assert capabilities(lib, f64)["status"] == "eligible"
+
+
 def test_bit_reversed_orders_need_packed_batches(lib):
     t = cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=64, input_strides=[64], output_strides=[64],
                      input_batch_stride=1, output_batch_stride=1, output_orders=[R])

@@ -58,3 +58,17 @@ def test_structured_rank_two(lib, oracle, cuda):
     got, name = run(lib, structured(0, 2, [outer, inner], extents=[8, 16]), x, cuda)
     assert name.startswith("composite[flat:structured-2x2")
     assert np.array_equal(got, oracle.structured(x, inner + outer))
+
+
+@pytest.mark.parametrize("inverse, normalize", [(False, False), (True, True), (True, False)])
+def test_fwht_fp64_runs_as_structured(lib, oracle, cuda, inverse, normalize):
+    """FP64 FWHT = structured 2x2 with H_2 per stage; the normalised inverse
+    halves every stage (exact for power-of-two N)."""
+    from gpu_util import run
+
+    x = w.rng(30).uniform(-1, 1, size=(3, 1 << 14))
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP64, compute=cb.ComputeType.FP64, extents=[1 << 14],
+                     batch=3, inverse=inverse, normalize_inverse=normalize)
+    got, name = run(lib, t, x, cuda)
+    assert name.startswith("fwht-f64:structured-2x2")
+    assert np.array_equal(got, oracle.fwht_f64(x, inverse=inverse, normalize=normalize))

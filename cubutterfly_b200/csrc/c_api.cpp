@@ -426,6 +426,12 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         launch_ntt(p, m, in, out, stream);
         return;
     }
+    if (p.req.fwht_native) {
+        check_cuda(cubf::launch_fwht_native(d.storage == CUBUTTERFLY_DATA_BF16, p.req.log_n, in, out, d.batch,
+                                            inverse && d.normalize_inverse, stream),
+                   "native FWHT launch");
+        return;
+    }
     if (d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) {
         check_cuda(cubf::launch_structured(static_cast<int>(cubf::storage_bytes(d.storage)), p.req.log_n, in, out,
                                            d.batch, p.structured, stream),
@@ -685,6 +691,9 @@ cubf::PlanRequest make_request(const cubf::Descriptor& d) {
     }
     cubf::resolve_orders(r);
     r.staged = !cubf::packed_layout(d) && r.log_v == 0;
+    r.fwht_native = d.op == CUBUTTERFLY_OPERATOR_FWHT &&
+                    (d.storage == CUBUTTERFLY_DATA_BF16 || d.storage == CUBUTTERFLY_DATA_FP16) &&
+                    d.compute == CUBUTTERFLY_COMPUTE_NATIVE;
     return r;
 }
 

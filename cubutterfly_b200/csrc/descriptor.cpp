@@ -582,6 +582,18 @@ Json capabilities(const Descriptor& source) {
                 if (!natural_in || !natural_out) gap("order-lowering", "FP64 FWHT executes natural logical orders");
                 break;
             }
+            // bf16 / fp16 with NATIVE compute: stage-storage rounding (the
+            // reference's default low-precision FWHT), no epilogue
+            const bool native_low = (d.storage == CUBUTTERFLY_DATA_BF16 || d.storage == CUBUTTERFLY_DATA_FP16) &&
+                                    d.compute == CUBUTTERFLY_COMPUTE_NATIVE &&
+                                    d.output_rounding == CUBUTTERFLY_ROUNDING_STAGE_STORAGE;
+            if (native_low) {
+                if (d.output_scale != 1.0)
+                    gap("output-epilogue-lowering", "native low-precision FWHT takes no output scale");
+                if (!natural_in || !natural_out)
+                    gap("order-lowering", "native low-precision FWHT executes natural logical orders");
+                break;
+            }
             const bool f32 = d.storage == CUBUTTERFLY_DATA_FP32 && d.compute == CUBUTTERFLY_COMPUTE_FP32;
             const bool low = (d.storage == CUBUTTERFLY_DATA_BF16 || d.storage == CUBUTTERFLY_DATA_FP16) &&
                              d.compute == CUBUTTERFLY_COMPUTE_FP32 &&

@@ -96,6 +96,12 @@ struct StructuredStages {
 cudaError_t launch_structured(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
                               const StructuredStages& stages, cudaStream_t stream);
 
+// ---- FWHT with native bf16 / fp16 stage storage (csrc/fwht_native.cu) -------------
+// Every stage rounds to the storage type; `normalize` halves each stage (an
+// inverse normalised by 1/N).  in may equal out.
+cudaError_t launch_fwht_native(bool bf16, int log_n, const void* in, void* out, std::size_t batch, bool normalize,
+                               cudaStream_t stream);
+
 // ---- real FFTs over an N/2-point complex FFT (csrc/real_fft.cu) -------------------
 // twiddles: W_N^k (complex fp32), k = 0..half.  R2C: z (batch x half, packed)
 // -> x (half + 1 per transform at out_batch_stride), times scale.  C2R: x ->

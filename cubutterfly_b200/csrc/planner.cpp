@@ -340,6 +340,8 @@ Json Mapping::to_json() const {
             case PassKind::FwhtTensor: kernel = "fwht_tcgen05"; break;
             case PassKind::StructuredTile: kernel = "structured_tile"; break;
             case PassKind::StructuredStage: kernel = "structured_stage"; break;
+            case PassKind::NativeTile: kernel = "fwht_native_tile"; break;
+            case PassKind::NativeStage: kernel = "fwht_native_stage"; break;
             default: break;
         }
         ps.push_back({{"kernel", kernel},
@@ -382,15 +384,16 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         out.push_back(ntt_mapping(r, hw));
         return out;
     }
-    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) {
+    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native) {
         // one shared-memory tile pass for the low 12 stages, one pass per higher stage
+        const bool native = r.fwht_native;
         Mapping m;
-        m.family = "structured-2x2";
+        m.family = native ? "fwht-native" : "structured-2x2";
         const int tile = std::min(r.log_n, 12);
         const double esz = static_cast<double>(storage_bytes(r.d.storage));
         const double elems = static_cast<double>(r.d.batch) * std::ldexp(1.0, r.log_n);
         Pass t;
-        t.kind = PassKind::StructuredTile;
+        t.kind = native ? PassKind::NativeTile : PassKind::StructuredTile;
         t.log_h = tile;
         t.shape.threads = 256;
         t.shape.smem_bytes = static_cast<int>(esz) << tile;
@@ -399,7 +402,7 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         m.predicted_us += pass_time_us(hw, elems, esz, esz, tile, tile, 3.0, 0.7);
         for (int s = tile; s < r.log_n; ++s) {
             Pass g;
-            g.kind = PassKind::StructuredStage;
+            g.kind = native ? PassKind::NativeStage : PassKind::StructuredStage;
             g.log_h = 1;
             g.log_inner = s;
             g.shape.threads = 256;
@@ -513,7 +516,7 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         if (parts != planned) throw Unsupported("explicit NTT mapping must be the planned pass split " + m.name());
         return m;
     }
-    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2) return enumerate_core(r, hw).front();
+    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native) return enumerate_core(r, hw).front();
     if (r.bw_op == BwOp::Fwht && text.find("tcgen05") != std::string::npos) {
         if (!fwht_tc_available(r.log_n, r.bw_type))
             throw Unsupported("the tensor-core FWHT serves 4096-point bf16 rows");

@@ -52,7 +52,9 @@ enum class PassKind {
     NttSingle,
     FwhtTensor,
     StructuredTile,
-    StructuredStage
+    StructuredStage,
+    NativeTile,
+    NativeStage
 };
 
 struct Pass {
@@ -101,6 +103,8 @@ struct PlanRequest {
     bool ntt_gs = false;
     bool ntt_word32 = false;  // uint32 storage
     bool ntt_lazy = false;    // modulus < 2^62
+    // FWHT on bf16 / fp16 with NATIVE compute: every stage rounds to storage
+    bool fwht_native = false;
 };
 
 // Fill the order-dependent fields of a request from its descriptor:

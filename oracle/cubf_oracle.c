@@ -359,6 +359,85 @@ ORACLE_API int cubf_oracle_structured_f64(double* data, size_t n, size_t batch, 
     return 0;
 }
 
+/* FWHT with native bf16 / fp16 stage storage: the semantics of the reference's
+ * LowFwhtOperator<Storage, Native = true> (src/operator_traits.cuh:114-154)
+ * applied in stage order 0 .. log n - 1: every add / sub / halving is the
+ * correctly rounded storage-precision result (computed exactly in double,
+ * then rounded to nearest even, subnormals included); a normalised inverse
+ * halves after the butterfly when both operands' magnitude bits are within
+ * 0x7e7f (bf16) / 0x73ff (fp16), before it otherwise.  The reference has no
+ * CPU function for this path, so this restatement is checked against the
+ * FP32 final-storage oracle within the bf16 / fp16 tolerance. */
+static double low_decode(uint16_t b, int bf16) {
+    if (bf16) {
+        const uint32_t u = (uint32_t)b << 16;
+        float f;
+        memcpy(&f, &u, 4);
+        return (double)f;
+    }
+    const int sign = b >> 15, exp = (b >> 10) & 31, mant = b & 1023;
+    double v;
+    if (exp == 0) v = ldexp((double)mant, -24);
+    else if (exp == 31) v = mant ? NAN : INFINITY;
+    else v = ldexp((double)(1024 + mant), exp - 25);
+    return sign ? -v : v;
+}
+static uint16_t low_encode(double x, int bf16) {
+    const uint16_t sign = signbit(x) ? 0x8000 : 0;
+    if (isnan(x)) return bf16 ? 0x7fc0 : 0x7e00;
+    double a = fabs(x);
+    const int digits = bf16 ? 8 : 11, min_q = bf16 ? -133 : -24;
+    const double max = bf16 ? ldexp(255.0, 120) : 65504.0;
+    if (a != 0.0 && !isinf(a)) {
+        int e;
+        frexp(a, &e);
+        const int q = e - digits > min_q ? e - digits : min_q;
+        a = ldexp(nearbyint(ldexp(a, -q)), q);  /* round to nearest even at quantum 2^q */
+        if (a > max) a = INFINITY;
+    }
+    if (bf16) {
+        const float f = (float)a;  /* exact: a is a bf16 value */
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        return sign | (uint16_t)(u >> 16);
+    }
+    if (isinf(a)) return sign | 0x7c00;
+    if (a == 0.0) return sign;
+    if (a < ldexp(1.0, -14)) return sign | (uint16_t)ldexp(a, 24);
+    int e;
+    const double m = frexp(a, &e); /* a = m 2^e, m in [0.5, 1) */
+    return sign | (uint16_t)((e - 1 + 15) << 10) | (uint16_t)(ldexp(m, 11) - 1024.0);
+}
+
+ORACLE_API int cubf_oracle_fwht_native(uint16_t* data, size_t n, size_t batch, int bf16, int normalize) {
+    if (!is_pow2(n)) return 1;
+    const uint16_t limit = bf16 ? 0x7e7f : 0x73ff;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t b = 0; b < batch; ++b) {
+        uint16_t* v = data + b * n;
+        for (size_t half = 1; half < n; half <<= 1)
+            for (size_t base = 0; base < n; base += 2 * half)
+                for (size_t o = 0; o < half; ++o) {
+                    uint16_t l = v[base + o], r = v[base + half + o];
+                    const int after = normalize && (l & 0x7fff) <= limit && (r & 0x7fff) <= limit;
+                    if (normalize && !after) {
+                        l = low_encode(low_decode(l, bf16) * 0.5, bf16);
+                        r = low_encode(low_decode(r, bf16) * 0.5, bf16);
+                    }
+                    const double a = low_decode(l, bf16), c = low_decode(r, bf16);
+                    l = low_encode(a + c, bf16);
+                    r = low_encode(a - c, bf16);
+                    if (after) {
+                        l = low_encode(low_decode(l, bf16) * 0.5, bf16);
+                        r = low_encode(low_decode(r, bf16) * 0.5, bf16);
+                    }
+                    v[base + o] = l;
+                    v[base + half + o] = r;
+                }
+    }
+    return 0;
+}
+
 /* uint64 variants, butterfly_reference.cpp:513-538. */
 ORACLE_API int cubf_oracle_zeta_u64(uint64_t* data, size_t n, size_t batch, int superset, int inverse) {
     if (!is_pow2(n)) return 1;

@@ -74,6 +74,7 @@ class Oracle:
         L.cubf_oracle_rns_primes.restype = _n
         L.cubf_oracle_ntt_cyclic.argtypes = [_p, _n, _u64, _i]
         L.cubf_oracle_structured_f32.argtypes = [_p, _n, _n, _p, _n, _i]
+        L.cubf_oracle_fwht_native.argtypes = [_p, _n, _n, _i, _i]
         L.cubf_oracle_structured_f64.argtypes = [_p, _n, _n, _p, _n, _i]
         L.cubf_oracle_rns_ntt_batch.argtypes = [_p, _p, ct.c_uint, _n, _p, _p, _i, _i, _i, _i]
 
@@ -149,6 +150,14 @@ class Oracle:
         out = np.zeros(count, dtype=np.uint64)
         got = self.lib.cubf_oracle_rns_primes(root_log, count, _ptr(out))
         return [int(v) for v in out[:got]]
+
+    def fwht_native(self, bits: np.ndarray, bf16=True, normalize=False) -> np.ndarray:
+        """FWHT of bf16 / fp16 payloads (uint16) with every stage rounded to storage."""
+        y = np.ascontiguousarray(bits, dtype=np.uint16).copy()
+        n = y.shape[-1]
+        if self.lib.cubf_oracle_fwht_native(_ptr(y), n, y.size // n, int(bf16), int(normalize)):
+            raise ValueError("oracle FWHT rejected its input")
+        return y
 
     def structured(self, x: np.ndarray, matrices, inverse=False) -> np.ndarray:
         """Structured 2x2 butterfly of every row (float32 or float64); matrices:

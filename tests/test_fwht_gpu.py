@@ -140,3 +140,27 @@ def test_fwht_tcgen05_config1_full_size(lib, oracle, cuda):
     want = oracle.fwht_bf16_final(bits, 1 / 64)
     assert rel_l2(f32(got), f32(want)) <= TOL_BF16
     assert np.mean(got == want) > 0.99
+
+
+# ---- native stage-storage FWHT (bf16 / fp16 NATIVE compute) --------------------------
+@pytest.mark.parametrize("storage", [cb.DataType.BF16, cb.DataType.FP16])
+@pytest.mark.parametrize("n", [2, 256, 4096, 1 << 14])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_fwht_native_stage_storage(lib, oracle, cuda, storage, n, inverse):
+    """Every stage rounded to bf16 / fp16 (the reference's default low-precision
+    FWHT): bit-identical to the restated stage-storage semantics, and within
+    the looser stage-storage distance of the FP32 final-storage oracle."""
+    from gpu_util import run
+
+    bf16 = storage == cb.DataType.BF16
+    x = w.rng(n).standard_normal((5, n)).astype(np.float32)
+    bits = w.f32_to_bf16_bits(x) if bf16 else x.astype(np.float16).view(np.uint16)
+    t = cb.Transform(op=cb.Operator.FWHT, storage=storage, extents=[n], batch=5, inverse=inverse,
+                     normalize_inverse=True)
+    got, name = run(lib, t, bits, cuda)
+    assert name.startswith("fwht-native")
+    want = oracle.fwht_native(bits, bf16=bf16, normalize=inverse)
+    assert np.array_equal(got, want), name
+    if bf16:
+        f32 = oracle.fwht_f32(w.bf16_bits_to_f32(bits), inverse=inverse, normalize=True)
+        assert rel_l2(w.bf16_bits_to_f32(got), f32) <= 3e-2

@@ -161,6 +161,9 @@ cudaError_t launch_strided_copy(int elem_bytes, const void* in, std::size_t in_s
         case 8:
             return copy_typed<unsigned long long>(in, in_stride, in_batch_stride, out, out_stride, out_batch_stride,
                                                   n, batch, stream);
+        case 16:
+            return copy_typed<uint4>(in, in_stride, in_batch_stride, out, out_stride, out_batch_stride, n, batch,
+                                     stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -184,6 +187,7 @@ cudaError_t launch_strided_copy_nd(int elem_bytes, int dims, const std::size_t* 
         case 2: return copy_nd_typed<std::uint16_t>(in, out, l, batch, stream);
         case 4: return copy_nd_typed<std::uint32_t>(in, out, l, batch, stream);
         case 8: return copy_nd_typed<unsigned long long>(in, out, l, batch, stream);
+        case 16: return copy_nd_typed<uint4>(in, out, l, batch, stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -201,6 +205,7 @@ cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, 
         case 2: return launch_typed<std::uint16_t>(log_n, in, out, batch, stream);
         case 4: return launch_typed<std::uint32_t>(log_n, in, out, batch, stream);
         case 8: return launch_typed<unsigned long long>(log_n, in, out, batch, stream);
+        case 16: return launch_typed<uint4>(log_n, in, out, batch, stream);
         default: return cudaErrorInvalidValue;
     }
 }

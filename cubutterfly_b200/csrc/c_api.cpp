@@ -438,6 +438,11 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
                    "structured launch");
         return;
     }
+    if (p.req.fft64) {
+        const double scale = (inverse && d.normalize_inverse) ? 1.0 / static_cast<double>(n) : 1.0;
+        check_cuda(cubf::launch_fft64(p.req.log_n, in, out, d.batch, p.twiddles, scale, stream), "FP64 FFT launch");
+        return;
+    }
     if (d.op == CUBUTTERFLY_OPERATOR_FFT) {
         const float scale = (inverse && d.normalize_inverse) ? 1.0f / static_cast<float>(n) : 1.0f;
         if (m.passes.front().kind == cubf::PassKind::FftLocal) {
@@ -637,6 +642,23 @@ void build_tables(cubutterflyPlan& p) {
     }
     if (p.desc.op != CUBUTTERFLY_OPERATOR_FFT) return;
     constexpr double kPi = 3.141592653589793238462643383279502884;
+    if (p.req.fft64) {
+        // W_N^k, k < N/2, with the reference's angle rounding: ((+-pi) * o) / half
+        // for stage half and offset o equals ((+-pi) * 2k) / N exactly (powers of two)
+        const std::size_t n = p.desc.extents[0];
+        const double sign = p.desc.direction == CUBUTTERFLY_DIRECTION_INVERSE ? 1.0 : -1.0;
+        std::vector<double> tw(n);  // n / 2 complex entries
+        for (std::size_t k = 0; k < n / 2; ++k) {
+            const double angle = sign * kPi * static_cast<double>(2 * k) / static_cast<double>(n);
+            tw[2 * k] = std::cos(angle);
+            tw[2 * k + 1] = std::sin(angle);
+        }
+        check_cuda(cudaMalloc(&p.twiddles, std::max<std::size_t>(tw.size(), 2) * sizeof(double)),
+                   "twiddle table allocation");
+        check_cuda(cudaMemcpy(p.twiddles, tw.data(), tw.size() * sizeof(double), cudaMemcpyHostToDevice),
+                   "twiddle table upload");
+        return;
+    }
     // every candidate of a request is global or every one is local
     const bool global = p.req.log_n > cubf::kFftLocalMaxLog || p.req.log_v > 0;
     if (global) {
@@ -672,8 +694,9 @@ cubf::PlanRequest make_request(const cubf::Descriptor& d) {
     cubf::PlanRequest r;
     r.d = d;
     r.log_n = static_cast<int>(cubf::log2_exact(d.extents[0]));
-    if (d.op == CUBUTTERFLY_OPERATOR_FFT && cubf::interleaved_batches(d))
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.storage == CUBUTTERFLY_DATA_COMPLEX_FP32 && cubf::interleaved_batches(d))
         r.log_v = static_cast<int>(cubf::log2_exact(d.batch));
+    r.fft64 = d.op == CUBUTTERFLY_OPERATOR_FFT && d.storage == CUBUTTERFLY_DATA_COMPLEX_FP64;
     switch (d.op) {
         case CUBUTTERFLY_OPERATOR_FWHT:
             r.bw_op = cubf::BwOp::Fwht;

@@ -553,7 +553,8 @@ Json capabilities(const Descriptor& source) {
     // Other rank-one strided or padded layouts are staged through a packed
     // workspace buffer (gather, packed passes, scatter); FFT batches
     // interleaved element-wise run natively.
-    const bool interleaved = d.op == CUBUTTERFLY_OPERATOR_FFT && interleaved_batches(d);
+    const bool interleaved = d.op == CUBUTTERFLY_OPERATOR_FFT && d.storage == CUBUTTERFLY_DATA_COMPLEX_FP32 &&
+                             interleaved_batches(d);
     const bool natural_in = std::all_of(d.input_orders.begin(), d.input_orders.end(),
                                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; });
     const bool natural_out = std::all_of(d.output_orders.begin(), d.output_orders.end(),
@@ -568,8 +569,10 @@ Json capabilities(const Descriptor& source) {
     const bool epilogue = d.output_scale != 1.0 || d.output_rounding != CUBUTTERFLY_ROUNDING_STAGE_STORAGE;
     switch (d.op) {
         case CUBUTTERFLY_OPERATOR_FFT:
-            if ((d.storage != CUBUTTERFLY_DATA_COMPLEX_FP32 && !real_fft) || d.compute != CUBUTTERFLY_COMPUTE_FP32)
-                gap("storage-lowering", "FFT executes complex FP32 storage (FP32 for R2C/C2R) with FP32 compute");
+            if (!(d.storage == CUBUTTERFLY_DATA_COMPLEX_FP64 && d.compute == CUBUTTERFLY_COMPUTE_FP64 && !real_fft) &&
+                ((d.storage != CUBUTTERFLY_DATA_COMPLEX_FP32 && !real_fft) || d.compute != CUBUTTERFLY_COMPUTE_FP32))
+                gap("storage-lowering",
+                    "FFT executes complex FP32 (FP32 for R2C/C2R) with FP32 compute, or complex FP64 with FP64 compute");
             if (epilogue) gap("output-epilogue-lowering", "output epilogues apply to FWHT only");
             if (n > (std::size_t{1} << 30)) gap("length-lowering", "FFT length is limited to 2^30");
             break;

@@ -96,6 +96,12 @@ struct StructuredStages {
 cudaError_t launch_structured(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
                               const StructuredStages& stages, cudaStream_t stream);
 
+// ---- complex fp64 FFT, radix 2 (csrc/fft64.cu) ---------------------------------------
+// twiddles: W_N^k (double2), k < N/2, conjugated for an inverse; scale: 1 or
+// 1/N (normalised inverse).  in may equal out.
+cudaError_t launch_fft64(int log_n, const void* in, void* out, std::size_t batch, const void* twiddles,
+                         double scale, cudaStream_t stream);
+
 // ---- FWHT with native bf16 / fp16 stage storage (csrc/fwht_native.cu) -------------
 // Every stage rounds to the storage type; `normalize` halves each stage (an
 // inverse normalised by 1/N).  in may equal out.
@@ -162,7 +168,7 @@ cudaError_t launch_ntt(const NttVariant& v, const NttLaunch& a, cudaStream_t str
 
 // ---- bit-reversal permutation ------------------------------------------------------
 // out[b][rev(i)] = in[b][i] for `batch` packed transforms of 2^log_n elements
-// of elem_bytes (2, 4 or 8) each.  in may equal out (pairs of tiles are swapped
+// of elem_bytes (2, 4, 8 or 16) each.  in may equal out (pairs of tiles are swapped
 // by one CTA).
 cudaError_t launch_bitrev(int elem_bytes, int log_n, const void* in, void* out, std::size_t batch,
                           cudaStream_t stream);

@@ -342,6 +342,8 @@ Json Mapping::to_json() const {
             case PassKind::StructuredStage: kernel = "structured_stage"; break;
             case PassKind::NativeTile: kernel = "fwht_native_tile"; break;
             case PassKind::NativeStage: kernel = "fwht_native_stage"; break;
+            case PassKind::Fft64Tile: kernel = "fft64_tile"; break;
+            case PassKind::Fft64Stage: kernel = "fft64_stage"; break;
             default: break;
         }
         ps.push_back({{"kernel", kernel},
@@ -384,16 +386,16 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         out.push_back(ntt_mapping(r, hw));
         return out;
     }
-    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native) {
-        // one shared-memory tile pass for the low 12 stages, one pass per higher stage
+    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native || r.fft64) {
+        // one shared-memory tile pass for the low 12 (fp64 FFT: 11) stages, one pass per higher stage
         const bool native = r.fwht_native;
         Mapping m;
-        m.family = native ? "fwht-native" : "structured-2x2";
-        const int tile = std::min(r.log_n, 12);
+        m.family = r.fft64 ? "fft64-radix2" : native ? "fwht-native" : "structured-2x2";
+        const int tile = std::min(r.log_n, r.fft64 ? 11 : 12);
         const double esz = static_cast<double>(storage_bytes(r.d.storage));
         const double elems = static_cast<double>(r.d.batch) * std::ldexp(1.0, r.log_n);
         Pass t;
-        t.kind = native ? PassKind::NativeTile : PassKind::StructuredTile;
+        t.kind = r.fft64 ? PassKind::Fft64Tile : native ? PassKind::NativeTile : PassKind::StructuredTile;
         t.log_h = tile;
         t.shape.threads = 256;
         t.shape.smem_bytes = static_cast<int>(esz) << tile;
@@ -402,7 +404,7 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         m.predicted_us += pass_time_us(hw, elems, esz, esz, tile, tile, 3.0, 0.7);
         for (int s = tile; s < r.log_n; ++s) {
             Pass g;
-            g.kind = native ? PassKind::NativeStage : PassKind::StructuredStage;
+            g.kind = r.fft64 ? PassKind::Fft64Stage : native ? PassKind::NativeStage : PassKind::StructuredStage;
             g.log_h = 1;
             g.log_inner = s;
             g.shape.threads = 256;
@@ -504,6 +506,8 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         }
     }
     require(!parts.empty(), "explicit mapping has no passes");
+    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native || r.fft64)
+        return enumerate_core(r, hw).front();
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
         if (r.log_n > kFftLocalMaxLog || r.log_v > 0) return fft_global_mapping(r, hw, parts);
         require(parts.size() == 1 && parts[0] == r.log_n, "FFT up to 2^13 is one local pass of log N bits");
@@ -516,7 +520,6 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         if (parts != planned) throw Unsupported("explicit NTT mapping must be the planned pass split " + m.name());
         return m;
     }
-    if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native) return enumerate_core(r, hw).front();
     if (r.bw_op == BwOp::Fwht && text.find("tcgen05") != std::string::npos) {
         if (!fwht_tc_available(r.log_n, r.bw_type))
             throw Unsupported("the tensor-core FWHT serves 4096-point bf16 rows");

@@ -54,7 +54,9 @@ enum class PassKind {
     StructuredTile,
     StructuredStage,
     NativeTile,
-    NativeStage
+    NativeStage,
+    Fft64Tile,
+    Fft64Stage
 };
 
 struct Pass {
@@ -105,6 +107,7 @@ struct PlanRequest {
     bool ntt_lazy = false;    // modulus < 2^62
     // FWHT on bf16 / fp16 with NATIVE compute: every stage rounds to storage
     bool fwht_native = false;
+    bool fft64 = false;  // complex fp64 FFT (radix-2 passes)
 };
 
 // Fill the order-dependent fields of a request from its descriptor:

@@ -123,7 +123,7 @@ def test_benchmark_configs_are_eligible(lib):
 @pytest.mark.parametrize("transform, code", [
     (cb.Transform(op=cb.Operator.FFT, extents=[8, 8], output_orders=[1, 1]), "order-lowering"),
     (cb.Transform(op=cb.Operator.FFT, extents=[12]), "length-lowering"),
-    (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, extents=[64]), "storage-lowering"),
+    (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP16, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32, extents=[64]),
      "storage-lowering"),  # bf16 with FP32 compute needs FINAL_STORAGE rounding
     (cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.FP32, extents=[64]), "storage-lowering"),

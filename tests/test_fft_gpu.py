@@ -183,3 +183,36 @@ def test_c2r(lib, oracle, cuda, n, normalize):
     assert rel_l2(got, want) <= TOL, name
     if normalize:
         assert rel_l2(got, real) <= TOL  # round trip R2C -> C2R
+
+
+# ---- complex fp64 FFT (radix 2, bit-identical to reference_fft<Complex64>) -----------
+@pytest.mark.parametrize("n", [2, 64, 2048, 1 << 14])
+@pytest.mark.parametrize("inverse, normalize", [(False, False), (True, True), (True, False)])
+def test_fft_fp64(lib, oracle, cuda, n, inverse, normalize):
+    from gpu_util import run
+
+    x = w.fft_input(n, 3, seed=n).astype(np.complex128)
+    x += 1e-9 * w.fft_input(n, 3, seed=n + 1)  # low-order bits beyond fp32
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, compute=cb.ComputeType.FP64,
+                     extents=[n], batch=3, inverse=inverse, normalize_inverse=normalize)
+    got, name = run(lib, t, x, cuda)
+    assert name.startswith("fft64-radix2")
+    assert np.array_equal(got, oracle.fft_c64(x, inverse=inverse, normalize=normalize)), name
+
+
+def test_fft_fp64_matches_reference_and_composite(lib, oracle, reference, cuda):
+    """Pinned to the reference's own reference_fft<Complex64>; a rank-two fp64
+    FFT runs per axis through the composite path."""
+    from gpu_util import run
+
+    x = w.fft_input(4096, 2, seed=5).astype(np.complex128)
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, compute=cb.ComputeType.FP64,
+                     extents=[4096], batch=2)
+    got, _ = run(lib, t, x, cuda)
+    assert np.array_equal(got, reference.fft_c64(x))
+    x2 = w.fft_input(32 * 64, 2, seed=6).astype(np.complex128).reshape(2, 32, 64)
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, compute=cb.ComputeType.FP64,
+                     extents=[32, 64], batch=2)
+    got, name = run(lib, t, x2.reshape(2, -1), cuda)
+    want = oracle.fft_c64(np.swapaxes(oracle.fft_c64(x2), 1, 2).copy())
+    assert rel_l2(got.reshape(2, 32, 64), np.swapaxes(want, 1, 2)) <= 1e-13, name

@@ -69,3 +69,44 @@ def test_zeta_config3_full_size(lib, oracle, cuda):
     t, _ = zeta_transform(1 << w.ZETA_LOG_N, w.ZETA_BATCH, in_place=True)
     got, name = run(lib, t, z, cuda)
     assert np.array_equal(got, oracle.zeta(z)), name
+
+
+def test_zeta_chunk_overlap_graph_replay(lib, oracle, cuda):
+    """A chained plan whose batch spans several L2 chunks, executed again and
+    again: the first call on a buffer pair runs directly, the second captures
+    the chain into a CUDA graph and later calls replay it.  Alternating
+    buffers, and a caller that captures its own stream around the call, give
+    the same bits."""
+    import json
+
+    import torch
+
+    from gpu_util import stream_ptr
+
+    log_n, batch = 20, 16
+    z = w.zeta_input(log_n, batch, seed=21)
+    want = oracle.zeta(z)
+    t, _ = zeta_transform(1 << log_n, batch, in_place=True)
+    src = torch.from_numpy(z.view(np.int32).copy()).to(cuda)
+    bufs = [torch.empty_like(src) for _ in range(2)]
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        assert len(json.loads(plan.mapping_json())["passes"]) == 2
+        for k in (0, 0, 0, 1, 0, 1, 1, 1, 0):
+            bufs[k].copy_(src)
+            plan.execute(bufs[k].data_ptr(), bufs[k].data_ptr())
+            torch.cuda.synchronize()
+            assert np.array_equal(bufs[k].cpu().numpy().view(np.uint32), want), k
+    side = torch.cuda.Stream()
+    with cb.Plan(lib, t, stream=side.cuda_stream) as plan:
+        with torch.cuda.stream(side):
+            bufs[0].copy_(src)
+            plan.execute(bufs[0].data_ptr(), bufs[0].data_ptr())
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            plan.execute(bufs[0].data_ptr(), bufs[0].data_ptr())
+        for _ in range(2):
+            bufs[0].copy_(src)
+            graph.replay()
+            torch.cuda.synchronize()
+            assert np.array_equal(bufs[0].cpu().numpy().view(np.uint32), want)

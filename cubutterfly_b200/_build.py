@@ -43,7 +43,8 @@ def _units():
               "--expt-relaxed-constexpr", f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{_json_include()}"]
     units = []
     for name in ("c_api.cpp", "descriptor.cpp", "planner.cpp", "rns_api.cpp", "launch_bitwise_dispatch.cpp",
-                 "launch_ntt_dispatch.cpp", "launch_fft.cu", "noalloc.cu", "fourstep.cu", "bitrev.cu", "fwht_tc.cu", "real_adapter.cu", "real_fft.cu", "structured.cu", "fwht_native.cu", "fft64.cu"):
+                 "launch_ntt_dispatch.cpp", "launch_fft.cu", "noalloc.cu", "fourstep.cu", "bitrev.cu", "fwht_tc.cu", "real_adapter.cu", "real_fft.cu", "structured.cu", "fwht_native.cu", "fft64.cu",
+                 "heongpu_adapter.cpp"):
         src = CSRC / name
         obj = OBJ / (src.stem + ".o")
         units.append((common + ["-c", str(src), "-o", str(obj)], src, obj))
@@ -63,7 +64,7 @@ def _stale(obj: Path) -> bool:
     if not obj.exists():
         return True
     t = obj.stat().st_mtime
-    deps = list(CSRC.glob("*")) + list((ROOT / "include").rglob("*.h")) + [Path(__file__)]
+    deps = list(CSRC.glob("*")) + list((ROOT / "include").rglob("*.h*")) + [Path(__file__)]
     return any(d.stat().st_mtime > t for d in deps)
 
 

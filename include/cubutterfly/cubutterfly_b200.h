@@ -70,6 +70,32 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FftC2CNoAlloc(const void* inpu
                                                                size_t batch, int inverse, int normalize,
                                                                cudaStream_t stream);
 
+/* The HEonGPU NTT adapter (reference adapters/heongpu/ntt_adapter.hpp, C++
+ * API in cubutterfly/heongpu/ntt_adapter.hpp) driven with plain pointers:
+ * cubutterfly_heongpu::transform of `batch` negacyclic word64 polynomials of
+ * 2^n_power coefficients.  Device arrays: moduli, modulus_count records of
+ * three 64-bit words {value, bit, mu} (GPU-NTT's Modulus64); roots,
+ * modulus_count tables of 2^n_power words whose entry bitrev(j) is psi^j
+ * (forward) or psi^-j (inverse); mod_inverse, N^-1 per modulus (inverse
+ * only); order (orderings 1 and 2).  ordering: 0 contiguous, 1 modulus
+ * order, 2 polynomial order; execution: 0 one RNS plan (native-rns), 1 one
+ * plan per modulus (grouped).  The first call of a request prepares plans
+ * (device metadata reads, a stream synchronisation); later calls only
+ * launch. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200HeongpuTransform(const uint64_t* input, uint64_t* output,
+                                                                  const uint64_t* roots, const void* moduli,
+                                                                  const uint64_t* mod_inverse, int n_power,
+                                                                  int inverse, int batch, int modulus_count,
+                                                                  int ordering, const int* order, int execution,
+                                                                  cudaStream_t stream);
+/* Adapter switches of the calling thread: clear_cache (non-zero) drops every
+ * prepared plan and unfreezes; freeze 1 / 0 sets the frozen state (a plan
+ * miss then fails instead of preparing), -1 leaves it; calls / polynomials
+ * (optional) receive the counters, then reset_counters (non-zero) zeroes
+ * them. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200HeongpuControl(int freeze, int clear_cache, int reset_counters,
+                                                                size_t* calls, size_t* polynomials);
+
 #ifdef __cplusplus
 }
 #endif

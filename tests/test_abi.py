@@ -395,3 +395,71 @@ def test_rns_bad_json_text():
     assert lib._dll.cubutterflyRnsCreate(b"{not json", ct.byref(handle)) == 1
     assert handle.value is None
     assert lib._dll.cubutterflyRnsLastError()
+
+
+def test_heongpu_adapter_rejects_without_device(lib):
+    """The HEonGPU adapter's request checks run before any device work: an
+    unsupported length, ordering, layout or missing pointer is INVALID_VALUE,
+    and the switches answer on a host without a GPU."""
+    import ctypes as ct
+
+    dll = lib._dll
+    dll.cubutterflyB200HeongpuTransform.argtypes = [ct.c_void_p] * 5 + [ct.c_int] * 5 + [ct.c_void_p, ct.c_int,
+                                                                                          ct.c_void_p]
+    dll.cubutterflyB200HeongpuControl.argtypes = [ct.c_int, ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p]
+    dll.cubutterflyGetLastErrorString.restype = ct.c_char_p
+    p = 0x1000
+    invalid = 1  # CUBUTTERFLY_STATUS_INVALID_VALUE
+    cases = [
+        ((p, p, p, p, p, 11, 0, 2, 2, 0, None, 0, None), "12..20"),
+        ((p, p, p, p, p, 21, 0, 2, 2, 0, None, 0, None), "12..20"),
+        ((p, p, p, p, p, 12, 0, 2, 2, 3, None, 0, None), "ordering"),
+        ((p, p, p, p, p, 12, 0, 2, 2, 1, None, 0, None), "invalid HEonGPU NTT adapter request"),
+        ((p, p, None, p, p, 12, 0, 2, 2, 0, None, 0, None), "invalid HEonGPU NTT adapter request"),
+        ((p, p, p, p, None, 12, 1, 2, 2, 0, None, 0, None), "invalid HEonGPU NTT adapter request"),
+        ((p, p, p, p, p, 12, 0, 0, 2, 0, None, 0, None), "invalid HEonGPU NTT adapter request"),
+        ((p, p, p, p, p, 12, 0, 2, 2, 0, None, 2, None), "execution"),
+    ]
+    for args, text in cases:
+        assert dll.cubutterflyB200HeongpuTransform(*args) == invalid, args
+        assert text in dll.cubutterflyGetLastErrorString().decode(), args
+    calls, polys = ct.c_size_t(7), ct.c_size_t(7)
+    assert dll.cubutterflyB200HeongpuControl(0, 1, 1, ct.byref(calls), ct.byref(polys)) == 0
+    assert (calls.value, polys.value) == (0, 0)
+
+
+def test_heongpu_adapter_header_compiles_and_links(tmp_path):
+    """A HEonGPU-side translation unit: the adapter header's gpuntt wrappers
+    compile against the GPU-NTT stand-in names, link with the library, throw
+    when disabled (GPU-NTT not linked) and route to the adapter when enabled."""
+    import shutil
+    import subprocess
+
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("g++ not available")
+    src = tmp_path / "use.cpp"
+    src.write_text(r'''
+#include <cubutterfly/heongpu/ntt_adapter.hpp>
+#include <cstdio>
+int main() {
+    gpuntt::ntt_rns_configuration<Data64> cfg;
+    cfg.n_power = 12;
+    int seen = 0;
+    cubutterfly_heongpu::set_enabled(false);
+    try { gpuntt::cubutterfly_GPU_INTT_Inplace(nullptr, nullptr, nullptr, cfg, 1, 1); }
+    catch (const std::logic_error& e) { seen |= std::string(e.what()).find("GPU-NTT") != std::string::npos; }
+    cubutterfly_heongpu::set_enabled(true);
+    try { gpuntt::cubutterfly_GPU_NTT(nullptr, nullptr, nullptr, nullptr, cfg, 1, 1); }
+    catch (const std::invalid_argument&) { seen |= 2; }
+    cubutterfly_heongpu::set_execution(cubutterfly_heongpu::Execution::Grouped);
+    std::printf("%d %s\n", seen, cubutterfly_heongpu::execution_name(cubutterfly_heongpu::get_execution()));
+    return 0;
+}
+''')
+    libdir = ROOT / "cubutterfly_b200" / "lib"
+    exe = tmp_path / "use"
+    subprocess.run([gxx, "-std=c++17", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", str(src),
+                    f"-L{libdir}", "-lcubutterfly_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert out == ["3", "grouped"]

@@ -475,6 +475,14 @@ class Plan:
 
     def set_workspace(self, pointer, bytes):
         self.library._call("PlanSetWorkspace", self.native_handle, _pointer(pointer), bytes)
+
+    def physical_extents(self, rank):
+        """Extents the plan transforms physically: the padded length of a
+        zero-extended embedding, the convolution length of a non-power-of-two
+        FFT axis, else the logical extent."""
+        out = (ct.c_size_t * rank)()
+        self.library._call("PlanGetPhysicalExtents", self.native_handle, out, rank)
+        return list(out)
         self._workspace = pointer
 
     def execute(self, input, output):

@@ -106,12 +106,23 @@ struct cubutterflyPlan {
     cubf::StructuredStages structured{};  // structured 2x2: per-stage matrices (inverted for an inverse plan)
     cubutterflyFftTransformType_t real_kind = CUBUTTERFLY_FFT_C2C;
     void* real_tw = nullptr;  // W_N^k, k = 0..N/2, complex fp32
+    // Arbitrary-length FFT (Bluestein): axes[0] / axes[1] are the forward and
+    // unnormalised inverse conv-point FFTs, in place on the work buffer at the
+    // start of the workspace; bluestein_tables holds the chirp (n values) and,
+    // 256-byte aligned after it, the scaled convolution spectrum (conv values).
+    bool bluestein = false;
+    std::size_t conv = 0;
+    void* bluestein_tables = nullptr;
+    // Extents the plan transforms physically (padded or convolution lengths),
+    // when they differ from the descriptor's.
+    std::vector<std::size_t> physical;
     ~cubutterflyPlan() {
         if (twiddles) cudaFree(twiddles);
         if (outer_lo) cudaFree(outer_lo);
         if (outer_hi) cudaFree(outer_hi);
         if (ntt_block) cudaFree(ntt_block);
         if (real_tw) cudaFree(real_tw);
+        if (bluestein_tables) cudaFree(bluestein_tables);
         for (auto e : {ev_fork, ev_handoff, ev_done[0], ev_done[1], ev_join[0], ev_join[1]})
             if (e) cudaEventDestroy(e);
         for (const auto& g : chain_graphs.entries) cudaGraphExecDestroy(g.exec);
@@ -135,6 +146,8 @@ void check_cuda(cudaError_t e, const char* what) {
         throw CudaFailure(std::string(what) + ": " + cudaGetErrorString(e));
     }
 }
+
+std::size_t align256(std::size_t v) { return (v + 255) / 256 * 256; }
 
 template <typename F>
 cubutterflyStatus_t protect(F&& body) noexcept {
@@ -407,8 +420,38 @@ void launch_embedded(const cubutterflyPlan& p, const void* in, void* out, cudaSt
                "embedding scatter launch");
 }
 
+// Bluestein: pack (input x chirp, zero-padded) -> forward conv-point FFT ->
+// x spectrum -> inverse conv-point FFT -> unpack (x chirp) into the output
+// layout.  Input and output may alias: the pack completes before the unpack.
+void launch_bluestein(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const bool f64 = d.storage == CUBUTTERFLY_DATA_COMPLEX_FP64;
+    const std::size_t n = d.extents[0], m = p.conv, esz = cubf::storage_bytes(d.storage);
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    const unsigned char* chirp = static_cast<const unsigned char*>(p.bluestein_tables);
+    const unsigned char* spectrum = chirp + align256(n * esz);
+    check_cuda(cubf::launch_bluestein_pack(f64, in, d.input_strides[0], d.input_batch_stride, ws, chirp, n, m,
+                                           d.batch, stream),
+               "Bluestein pack launch");
+    for (std::size_t i = 0; i < 2; ++i) {
+        auto& c = *p.axes[i].plan;
+        c.workspace = ws + p.axes[i].ws_offset;
+        launch_mapping(c, c.mapping, ws, ws, stream);
+        if (i == 0)
+            check_cuda(cubf::launch_bluestein_multiply(f64, ws, spectrum, m, d.batch, stream),
+                       "Bluestein multiply launch");
+    }
+    check_cuda(cubf::launch_bluestein_unpack(f64, ws, out, d.output_strides[0], d.output_batch_stride, chirp, n, m,
+                                             d.batch, stream),
+               "Bluestein unpack launch");
+}
+
 void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                     cudaStream_t stream) {
+    if (p.bluestein) {
+        launch_bluestein(p, in, out, stream);
+        return;
+    }
     if (p.embedded) {
         launch_embedded(p, in, out, stream);
         return;
@@ -910,6 +953,129 @@ std::unique_ptr<cubutterflyPlan> create_rank1(cubutterflyHandle* handle, const c
     return p;
 }
 
+// A complex FFT whose length is not a power of two (standard length mode).
+bool arbitrary_fft(const cubf::Descriptor& d) {
+    return d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type == CUBUTTERFLY_FFT_C2C &&
+           d.length_mode == CUBUTTERFLY_LENGTH_STANDARD &&
+           std::any_of(d.extents.begin(), d.extents.end(), [](std::size_t e) { return !cubf::is_pow2(e); });
+}
+
+// The least power of two >= 2n - 1.
+std::size_t bluestein_length(std::size_t n) {
+    std::size_t m = 1;
+    while (m < 2 * n - 1) m <<= 1;
+    return m;
+}
+
+// The forward power-of-two child of a rank-one Bluestein plan: the packed
+// batch of convolution-length transforms, in place on the work buffer.
+cubf::Descriptor bluestein_child(const cubf::Descriptor& d) {
+    cubf::Descriptor c = d;
+    const std::size_t m = bluestein_length(d.extents[0]);
+    c.extents = {m};
+    c.input_strides = c.output_strides = {1};
+    c.input_batch_stride = c.output_batch_stride = m;
+    c.input_orders = c.output_orders = {CUBUTTERFLY_ORDER_NATURAL};
+    c.placement = CUBUTTERFLY_PLACEMENT_IN_PLACE;
+    c.direction = CUBUTTERFLY_DIRECTION_FORWARD;
+    c.normalize_inverse = false;
+    if (c.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
+        c.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+        c.explicit_algorithm.clear();
+    }
+    return cubf::normalize(c);
+}
+
+struct DeviceTemp {
+    void* ptr = nullptr;
+    explicit DeviceTemp(std::size_t bytes) { check_cuda(cudaMalloc(&ptr, bytes), "Bluestein set-up allocation"); }
+    ~DeviceTemp() {
+        if (ptr) cudaFree(ptr);
+    }
+    DeviceTemp(const DeviceTemp&) = delete;
+    DeviceTemp& operator=(const DeviceTemp&) = delete;
+};
+
+// Rank-one arbitrary-length complex FFT (reference src/bluestein_fft.cu with
+// its own power-of-two core): conv = the least power of two >= 2n - 1; the
+// convolution spectrum is computed once here in fp64 (taps on the device,
+// an fp64 conv-point FFT plan of this library, scaled by 1 / conv and, for a
+// normalised inverse, 1 / n) and rounded once to the storage precision.
+std::unique_ptr<cubutterflyPlan> create_bluestein(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->bluestein = true;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    const std::size_t n = d.extents[0];
+    const std::size_t m = bluestein_length(n);
+    p->conv = m;
+    p->physical = {m};
+    const bool f64 = d.storage == CUBUTTERFLY_DATA_COMPLEX_FP64;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    const std::size_t esz = cubf::storage_bytes(d.storage);
+    const std::size_t work_bytes = align256(m * d.batch * esz);
+    cubf::Descriptor c = bluestein_child(d);
+    std::size_t child_ws = 0;
+    for (auto dir : {CUBUTTERFLY_DIRECTION_FORWARD, CUBUTTERFLY_DIRECTION_INVERSE}) {
+        c.direction = dir;
+        cubutterflyPlan::Axis ax;
+        ax.plan = create_rank1(handle, cubf::normalize(c));
+        ax.n = m;
+        ax.outer = d.batch;
+        ax.inner = 1;
+        ax.ws_offset = work_bytes;
+        child_ws = std::max(child_ws, ax.plan->mapping.workspace_bytes);
+        p->axes.push_back(std::move(ax));
+    }
+    p->mapping.family = "bluestein";
+    p->mapping.label = "bluestein[" + std::to_string(m) + ":" + p->axes[0].plan->mapping.name() + "]";
+    p->mapping.workspace_bytes = work_bytes + align256(child_ws);
+    p->source = p->axes[0].plan->source;
+    p->reason = "non-power-of-two FFT of " + std::to_string(n) + " points as a " + std::to_string(m) +
+                "-point cyclic convolution (Bluestein): " + p->axes[0].plan->reason;
+
+    // per-plan tables
+    check_cuda(cudaMalloc(&p->bluestein_tables, align256(n * esz) + m * esz), "Bluestein table allocation");
+    unsigned char* chirp = static_cast<unsigned char*>(p->bluestein_tables);
+    cubf::Descriptor k = c;
+    k.storage = CUBUTTERFLY_DATA_COMPLEX_FP64;
+    k.compute = CUBUTTERFLY_COMPUTE_FP64;
+    k.batch = 1;
+    k.direction = CUBUTTERFLY_DIRECTION_FORWARD;
+    k.placement = CUBUTTERFLY_PLACEMENT_OUT_OF_PLACE;
+    k.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+    auto kp = create_rank1(handle, cubf::normalize(k));
+    DeviceTemp temp(2 * align256(m * 16) + align256(kp->mapping.workspace_bytes) + 256);
+    unsigned char* taps = static_cast<unsigned char*>(temp.ptr);
+    unsigned char* taps_spectrum = taps + align256(m * 16);
+    kp->workspace = taps_spectrum + align256(m * 16);
+    cudaStream_t s = nullptr;
+    check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "Bluestein set-up stream");
+    try {
+        check_cuda(cubf::launch_bluestein_tables(f64, n, m, inverse, chirp, taps, s), "Bluestein table launch");
+        launch_mapping(*kp, kp->mapping, taps, taps_spectrum, s);
+        const double scale = (1.0 / static_cast<double>(m)) *
+                             (inverse && d.normalize_inverse ? 1.0 / static_cast<double>(n) : 1.0);
+        check_cuda(cubf::launch_bluestein_spectrum(f64, taps_spectrum, chirp + align256(n * esz), m, scale, s),
+                   "Bluestein spectrum launch");
+        check_cuda(cudaStreamSynchronize(s), "Bluestein set-up");
+    } catch (...) {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+        throw;
+    }
+    cudaStreamDestroy(s);
+    return p;
+}
+
+// A rank-one plan of any supported length.
+std::unique_ptr<cubutterflyPlan> create_axis(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    return arbitrary_fft(d) ? create_bluestein(handle, d) : create_rank1(handle, d);
+}
+
 // The rank-one child descriptors of a rank-two or rank-three descriptor.
 struct AxisSpec {
     cubf::Descriptor d;
@@ -971,8 +1137,6 @@ std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat) {
     return axes;
 }
 
-std::size_t align256(std::size_t v) { return (v + 255) / 256 * 256; }
-
 std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, const cubf::Descriptor& d) {
     auto p = std::make_unique<cubutterflyPlan>();
     p->desc = d;
@@ -993,7 +1157,7 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
     cubutterflySelectionSource_t source = CUBUTTERFLY_SELECTION_STATIC_MODEL;
     for (std::size_t i = 0; i < specs.size(); ++i) {
         cubutterflyPlan::Axis ax;
-        ax.plan = create_rank1(handle, cubf::normalize(specs[i].d));
+        ax.plan = create_axis(handle, cubf::normalize(specs[i].d));
         ax.n = specs[i].n;
         ax.outer = specs[i].outer;
         ax.inner = specs[i].inner;
@@ -1006,6 +1170,11 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
         p->axes.push_back(std::move(ax));
     }
     name << "]";
+    if (!flat && p->axes.size() == d.rank) {  // per-axis children, innermost first
+        p->physical = d.extents;
+        for (std::size_t i = 0; i < p->axes.size(); ++i)
+            if (!p->axes[i].plan->physical.empty()) p->physical[d.rank - 1 - i] = p->axes[i].plan->physical[0];
+    }
     p->mapping.family = "composite";
     p->mapping.label = name.str();
     p->mapping.workspace_bytes = offset;
@@ -1118,6 +1287,7 @@ std::unique_ptr<cubutterflyPlan> create_embedded(cubutterflyHandle* handle, cons
     cubutterflyPlan::Axis ax;
     ax.plan = create_rank1(handle, cubf::normalize(c));
     ax.n = pn;
+    p->physical = {pn};
     ax.outer = d.batch;
     ax.inner = 1;
     ax.ws_offset = p->packed_bytes;
@@ -1434,7 +1604,7 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
                      ? create_fwht64(handle, d)
                  : d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING ? create_embedded(handle, d)
                  : d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C ? create_real(handle, d)
-                 : d.rank == 1                                                        ? create_rank1(handle, d)
+                 : d.rank == 1                                                        ? create_axis(handle, d)
                                                                                       : create_composite(handle, d);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
         *plan = p.release();
@@ -1477,7 +1647,8 @@ cubutterflyStatus_t cubutterflyPlanGetPhysicalExtents(cubutterflyPlan_t plan, si
     return protect([&] {
         require(plan != nullptr && extents != nullptr, "plan and extents must be non-null");
         require(capacity >= plan->desc.rank, "extent capacity is smaller than the rank");
-        for (std::size_t a = 0; a < plan->desc.rank; ++a) extents[a] = plan->desc.extents[a];
+        for (std::size_t a = 0; a < plan->desc.rank; ++a)
+            extents[a] = plan->physical.empty() ? plan->desc.extents[a] : plan->physical[a];
     });
 }
 
@@ -1573,7 +1744,20 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         const cubf::HardwareProfile hw = hardware_json ? cubf::profile_from_json(cubf::Json::parse(hardware_json))
                                                        : cubf::resolve_profile();
         cubf::Json out = cubf::Json::array();
-        if (d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING) {
+        // the best mapping of a rank-one child (its power-of-two core for a
+        // Bluestein axis)
+        auto child_mapping = [&](const cubf::Descriptor& c) -> cubf::Json {
+            if (!arbitrary_fft(c)) return cubf::enumerate_mappings(make_request(c), hw).front().to_json();
+            const cubf::Descriptor k = bluestein_child(c);
+            return {{"family", "bluestein"},
+                    {"convolution_length", k.extents[0]},
+                    {"core", cubf::enumerate_mappings(make_request(k), hw).front().to_json()}};
+        };
+        if (arbitrary_fft(d) && d.rank == 1) {
+            cubf::Json axes = cubf::Json::array();
+            axes.push_back({{"length", d.extents[0]}, {"outer", d.batch}, {"inner", 1}, {"mapping", child_mapping(d)}});
+            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"}, {"family", "bluestein"}, {"axes", axes}});
+        } else if (d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING) {
             cubf::Descriptor c = d;
             std::size_t pn = 1;
             while (pn < d.extents[0]) pn <<= 1;
@@ -1605,8 +1789,7 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
             cubf::Json axes = cubf::Json::array();
             for (const auto& a : composite_axes(d, flat)) {
                 const cubf::Descriptor c = cubf::normalize(a.d);
-                axes.push_back({{"length", a.n}, {"outer", a.outer}, {"inner", a.inner},
-                                {"mapping", cubf::enumerate_mappings(make_request(c), hw).front().to_json()}});
+                axes.push_back({{"length", a.n}, {"outer", a.outer}, {"inner", a.inner}, {"mapping", child_mapping(c)}});
             }
             out.push_back({{"schema", "cubutterfly-b200-mapping-v1"}, {"family", "composite"}, {"flat", flat},
                            {"axes", axes}});

@@ -510,8 +510,27 @@ Json capabilities(const Descriptor& source) {
                          [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
             gap("order-lowering", "zero-extended embedding executes natural logical orders");
     }
+    // Standard-length complex FFTs of other lengths run as Bluestein
+    // convolutions over power-of-two FFTs (reference src/bluestein_fft.cu):
+    // C2C, ranks one and two, natural orders, any layout.
+    const bool arbitrary = d.length_mode == CUBUTTERFLY_LENGTH_STANDARD &&
+                           std::any_of(d.extents.begin(), d.extents.end(), [](std::size_t e) { return !is_pow2(e); });
+    if (arbitrary) {
+        if (d.op == CUBUTTERFLY_OPERATOR_NTT)
+            gap("arbitrary-length-lowering", "non-power-of-two NTT lengths (Bluestein NTT) are not built");
+        if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C)
+            gap("arbitrary-length-lowering", "non-power-of-two R2C/C2R transforms are not built");
+        if (d.rank > 2) gap("rank-bluestein-lowering", "rank-three Bluestein composition is not built");
+        if (!std::all_of(d.input_orders.begin(), d.input_orders.end(),
+                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }) ||
+            !std::all_of(d.output_orders.begin(), d.output_orders.end(),
+                         [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
+            gap("order-lowering", "non-power-of-two FFTs execute natural logical orders");
+    }
+    const bool bluestein = arbitrary && d.op == CUBUTTERFLY_OPERATOR_FFT;
     for (auto n : d.extents)
-        if ((!is_pow2(n) && !embedded) || n < 2) gap("length-lowering", "extents must be powers of two of at least two");
+        if ((!is_pow2(n) && !embedded && !bluestein) || n < 2)
+            gap("length-lowering", "extents must be powers of two of at least two");
     // R2C / C2R: rank one, fp32, packed, out of place, over an N/2-point
     // complex FFT (N >= 4)
     const bool real_fft = d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C;
@@ -537,6 +556,7 @@ Json capabilities(const Descriptor& source) {
     std::size_t n = 1, longest = 1;
     for (auto e : d.extents) {
         if (embedded) e = next_pow2(e);  // the padded (physical) length
+        if (bluestein && !is_pow2(e)) e = next_pow2(2 * e - 1);  // the convolution length
         n *= e;
         longest = std::max(longest, e);
     }

@@ -108,6 +108,28 @@ cudaError_t launch_fft64(int log_n, const void* in, void* out, std::size_t batch
 cudaError_t launch_fwht_native(bool bf16, int log_n, const void* in, void* out, std::size_t batch, bool normalize,
                                cudaStream_t stream);
 
+// ---- arbitrary-length complex FFT (Bluestein, csrc/bluestein.cu) ------------------
+// f64 selects complex fp64 (double2) buffers, else complex fp32 (float2).
+// tables: chirp_table[j] = exp(s i pi j^2 / n), j < n (s = -1 forward, +1
+// inverse), in the storage precision; taps (fp64, m values) = the wrapped
+// conj(chirp) of the m-point cyclic convolution.
+cudaError_t launch_bluestein_tables(bool f64, std::size_t n, std::size_t m, bool inverse, void* chirp_table,
+                                    void* taps, cudaStream_t stream);
+// spectrum = taps_spectrum (fp64) * scale, in the storage precision
+cudaError_t launch_bluestein_spectrum(bool f64, const void* taps_spectrum, void* spectrum, std::size_t m,
+                                      double scale, cudaStream_t stream);
+// work (m per transform, packed) = input * chirp, zero-padded
+cudaError_t launch_bluestein_pack(bool f64, const void* in, std::size_t in_stride, std::size_t in_batch_stride,
+                                  void* work, const void* chirp_table, std::size_t n, std::size_t m, std::size_t batch,
+                                  cudaStream_t stream);
+// work *= spectrum (per transform)
+cudaError_t launch_bluestein_multiply(bool f64, void* work, const void* spectrum, std::size_t m, std::size_t batch,
+                                      cudaStream_t stream);
+// output = work[0 .. n) * chirp
+cudaError_t launch_bluestein_unpack(bool f64, const void* work, void* out, std::size_t out_stride,
+                                    std::size_t out_batch_stride, const void* chirp_table, std::size_t n,
+                                    std::size_t m, std::size_t batch, cudaStream_t stream);
+
 // ---- real FFTs over an N/2-point complex FFT (csrc/real_fft.cu) -------------------
 // twiddles: W_N^k (complex fp32), k = 0..half.  R2C: z (batch x half, packed)
 // -> x (half + 1 per transform at out_batch_stride), times scale.  C2R: x ->

@@ -162,6 +162,44 @@ ORACLE_API void cubf_oracle_dft_bins(const float* data, size_t n, const size_t* 
     }
 }
 
+/* Direct DFT of any length in long double, rows of n complex doubles:
+ * X[k] = sum_j x[j] exp(-+2 pi i j k / n) (1/n on a normalised inverse), the
+ * definition the reference's arbitrary-length FFT plans (src/bluestein_fft.cu)
+ * are held to by tests/test_c_api.c:49-108.  j k is reduced mod n exactly
+ * before the angle is formed; one table of n unit roots serves every term. */
+ORACLE_API int cubf_oracle_dft_c128(const double* in, double* out, size_t n, size_t batch, int inverse,
+                                    int normalize) {
+    if (n == 0) return 1;
+    const long double kPi = 3.141592653589793238462643383279502884L;
+    long double* tw = (long double*)malloc(2 * n * sizeof(long double));
+    if (!tw) return 1;
+    for (size_t m = 0; m < n; ++m) {
+        const long double ang = (inverse ? 2.0L : -2.0L) * kPi * (long double)m / (long double)n;
+        tw[2 * m] = cosl(ang);
+        tw[2 * m + 1] = sinl(ang);
+    }
+    const long double scale = (inverse && normalize) ? 1.0L / (long double)n : 1.0L;
+    for (size_t b = 0; b < batch; ++b) {
+        const double* x = in + 2 * b * n;
+        double* y = out + 2 * b * n;
+        for (size_t k = 0; k < n; ++k) {
+            long double sr = 0, si = 0;
+            size_t m = 0; /* j k mod n */
+            for (size_t j = 0; j < n; ++j) {
+                const long double c = tw[2 * m], s = tw[2 * m + 1];
+                sr += x[2 * j] * c - x[2 * j + 1] * s;
+                si += x[2 * j] * s + x[2 * j + 1] * c;
+                m += k;
+                if (m >= n) m -= n;
+            }
+            y[2 * k] = (double)(sr * scale);
+            y[2 * k + 1] = (double)(si * scale);
+        }
+    }
+    free(tw);
+    return 0;
+}
+
 /* --------------------------------------------------------------- FWHT ---- */
 
 /* cuntt::reference_fwht(std::vector<double>&), src/butterfly_reference.cpp:371-390. */

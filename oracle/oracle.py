@@ -60,6 +60,7 @@ class Oracle:
         L.cubf_oracle_fft_c64.argtypes = [_p, _n, _n, _i, _i]
         L.cubf_oracle_dft_bins.argtypes = [_p, _n, _p, _n, _i, _p]
         L.cubf_oracle_dft_bins.restype = None
+        L.cubf_oracle_dft_c128.argtypes = [_p, _p, _n, _n, _i, _i]
         L.cubf_oracle_fwht_f64.argtypes = [_p, _n, _n, _i, _i]
         L.cubf_oracle_fwht_f32.argtypes = [_p, _n, _n, _i, _i]
         L.cubf_oracle_fwht_bf16_final.argtypes = [_p, _p, _n, _n, _i, _i, _d]
@@ -93,6 +94,15 @@ class Oracle:
         if self.lib.cubf_oracle_fft_c64(_ptr(y), n, y.size // n, int(inverse), int(normalize)):
             raise ValueError("oracle FFT rejected its input")
         return y
+
+    def dft(self, x: np.ndarray, inverse=False, normalize=True) -> np.ndarray:
+        """Direct DFT of any length along the last axis (complex128 result)."""
+        y = np.ascontiguousarray(x, dtype=np.complex128)
+        n = y.shape[-1]
+        out = np.empty_like(y)
+        if self.lib.cubf_oracle_dft_c128(_ptr(y), _ptr(out), n, y.size // n, int(inverse), int(normalize)):
+            raise ValueError("oracle DFT rejected its input")
+        return out
 
     def dft_bins(self, x: np.ndarray, bins, inverse=False) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.complex64)

@@ -122,7 +122,8 @@ def test_benchmark_configs_are_eligible(lib):
 
 @pytest.mark.parametrize("transform, code", [
     (cb.Transform(op=cb.Operator.FFT, extents=[8, 8], output_orders=[1, 1]), "order-lowering"),
-    (cb.Transform(op=cb.Operator.FFT, extents=[12]), "length-lowering"),
+    (cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[12]), "arbitrary-length-lowering"),
+    (cb.Transform(op=cb.Operator.FFT, extents=[3, 5, 7]), "rank-bluestein-lowering"),
     (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP16, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32, extents=[64]),
      "storage-lowering"),  # bf16 with FP32 compute needs FINAL_STORAGE rounding
@@ -316,8 +317,10 @@ def test_zero_extended_embedding_pads_to_a_power_of_two(lib):
     bad = cb.Transform(op=cb.Operator.FFT, extents=[1000], in_place=True,
                        length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING)
     assert "length-lowering" in [g["code"] for g in capabilities(lib, bad)["gaps"]]
+    # the standard length mode runs the same length as a Bluestein convolution
     std = cb.Transform(op=cb.Operator.FFT, extents=[1000])
-    assert "length-lowering" in [g["code"] for g in capabilities(lib, std)["gaps"]]
+    assert capabilities(lib, std)["status"] == "eligible"
+    assert rank(lib, std)[0]["family"] == "bluestein"
 
 
 def test_execution_and_arithmetic_policies(lib):
@@ -463,3 +466,28 @@ int main() {
                     f"-L{libdir}", "-lcubutterfly_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
     assert out == ["3", "grouped"]
+
+
+@pytest.mark.parametrize("extents, storage", [([5], cb.DataType.COMPLEX_FP32), ([1000], cb.DataType.COMPLEX_FP64),
+                                              ([6, 10], cb.DataType.COMPLEX_FP32), ([12, 64], cb.DataType.COMPLEX_FP32)])
+def test_arbitrary_length_fft_is_eligible(lib, extents, storage):
+    """Standard-length complex FFTs whose extents are not powers of two run as
+    Bluestein convolutions (reference src/bluestein_fft.cu): ranks one and
+    two, complex FP32 / FP64, in or out of place."""
+    compute = cb.ComputeType.FP64 if storage == cb.DataType.COMPLEX_FP64 else cb.ComputeType.FP32
+    for in_place in (False, True):
+        t = cb.Transform(op=cb.Operator.FFT, storage=storage, compute=compute, extents=extents, batch=3,
+                         in_place=in_place)
+        c = capabilities(lib, t)
+        assert c["status"] == "eligible", c["gaps"]
+
+
+def test_bluestein_preview_names_the_convolution_core(lib):
+    """reference tests/test_c_api.c:49-74: a 5-point FFT convolves over 16
+    points (the least power of two >= 2N - 1)."""
+    ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[5], batch=2))
+    axis = ms[0]["axes"][0]
+    assert ms[0]["family"] == "bluestein" and axis["mapping"]["convolution_length"] == 16
+    ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[100, 64], batch=1))
+    lengths = [a["mapping"].get("convolution_length") for a in ms[0]["axes"]]
+    assert lengths == [None, 256]  # innermost axis (64) first, then the 100-point axis

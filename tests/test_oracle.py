@@ -148,3 +148,26 @@ def test_restatement_matches_reference_random(oracle, reference):
         x = w.rng(31).integers(0, 1 << 63, size=(2, 1024), dtype=np.uint64)
         for inverse in (False, True):
             assert np.array_equal(oracle.ntt_cyclic(x, q, inverse), reference.ntt_cyclic(x, q, inverse))
+
+
+def test_dft_known_answer_and_round_trip(oracle):
+    """reference tests/test_c_api.c:49-108: the 5-point FFT of an impulse at
+    index 1 is exp(-2 pi i k / 5), and the normalised inverse recovers it."""
+    x = np.zeros((1, 5), dtype=np.complex128)
+    x[0, 1] = 1
+    y = oracle.dft(x)
+    k = np.arange(5)
+    assert np.allclose(y[0], np.exp(-2j * np.pi * k / 5), atol=1e-15)
+    assert np.allclose(oracle.dft(y, inverse=True, normalize=True), x, atol=1e-15)
+
+
+@pytest.mark.parametrize("n", [3, 7, 12, 100, 1000])
+def test_dft_matches_numpy(oracle, n):
+    x = w.rng(50, n).uniform(-1, 1, size=(2, n)) + 1j * w.rng(51, n).uniform(-1, 1, size=(2, n))
+    assert np.abs(oracle.dft(x) - np.fft.fft(x)).max() < 1e-12 * n
+    assert np.abs(oracle.dft(x, inverse=True, normalize=False) - n * np.fft.ifft(x)).max() < 1e-12 * n
+
+
+def test_dft_matches_reference_fft_at_power_of_two(oracle, reference):
+    x = w.fft_input(256, 3, seed=52).astype(np.complex128)
+    assert np.abs(oracle.dft(x) - reference.fft_c64(x, normalize=False)).max() < 1e-12

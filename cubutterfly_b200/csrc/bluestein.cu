@@ -10,6 +10,14 @@
 // fp64; the two M-point transforms are the library's own power-of-two FFT
 // plans, in place in the workspace.  Chirp angles reduce j^2 mod 2N in
 // integers, so pi (j^2 mod 2N) / N stays in [0, 2 pi) for every length.
+//
+// The NTT of any length N (u64 words, prime q with 2N | q - 1 and M | q - 1)
+// is the same identity over Z_q with psi a primitive 2N-th root in place of
+// exp(-i pi / N): c[j] = psi^(j^2 mod 2N), b[j] = c[j]^-1, and
+// X[k] = c[k] sum_n x[n] c[n] b[k - n] = sum_n x[n] (psi^2)^(nk) exactly; the
+// M-point cyclic convolution runs on the library's power-of-two NTT plans
+// (natural -> bit-reversed forward, bit-reversed -> natural inverse with
+// 1/M, so the product needs no reordering).
 #include "kernels.hpp"
 
 #include <cuda_runtime.h>
@@ -115,7 +123,80 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// ---- NTT (u64 words, prime q < 2^63) ----------------------------------------
+// Shoup product a w mod q for any 64-bit a and w < q (wq = floor(w 2^64 / q)):
+// the remainder estimate lies in [0, 2q).
+__device__ __forceinline__ std::uint64_t mul_shoup(std::uint64_t a, std::uint64_t w, std::uint64_t wq,
+                                                   std::uint64_t q) {
+    const std::uint64_t r = a * w - __umul64hi(a, wq) * q;
+    return r >= q ? r - q : r;
+}
+
+// work[b][j] = (x[b][j] mod q) c[j] (j < n), 0 (n <= j < M)
+__global__ void __launch_bounds__(kThreads)
+    ntt_pack_kernel(const std::uint64_t* in, std::size_t is, std::size_t ibs, std::uint64_t* work,
+                    const std::uint64_t* chirp, const std::uint64_t* chirp_q, std::size_t n, std::size_t m,
+                    std::size_t batch, std::uint64_t q, std::uint64_t unit_q) {
+    const std::size_t total = m * batch;
+    for (std::size_t idx = static_cast<std::size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
+         idx += static_cast<std::size_t>(gridDim.x) * kThreads) {
+        const std::size_t b = idx / m, j = idx - b * m;
+        std::uint64_t v = 0;
+        if (j < n) v = mul_shoup(mul_shoup(in[b * ibs + j * is], 1, unit_q, q), chirp[j], chirp_q[j], q);
+        work[idx] = v;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    ntt_multiply_kernel(std::uint64_t* work, const std::uint64_t* spectrum, const std::uint64_t* spectrum_q,
+                        std::size_t m, std::size_t batch, std::uint64_t q) {
+    const std::size_t total = m * batch;
+    for (std::size_t idx = static_cast<std::size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
+         idx += static_cast<std::size_t>(gridDim.x) * kThreads) {
+        const std::size_t k = idx & (m - 1);
+        work[idx] = mul_shoup(work[idx], spectrum[k], spectrum_q[k], q);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    ntt_unpack_kernel(const std::uint64_t* work, std::uint64_t* out, std::size_t os, std::size_t obs,
+                      const std::uint64_t* chirp, const std::uint64_t* chirp_q, std::size_t n, std::size_t m,
+                      std::size_t batch, std::uint64_t q) {
+    const std::size_t total = n * batch;
+    for (std::size_t idx = static_cast<std::size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
+         idx += static_cast<std::size_t>(gridDim.x) * kThreads) {
+        const std::size_t b = idx / n, k = idx - b * n;
+        out[b * obs + k * os] = mul_shoup(work[b * m + k], chirp[k], chirp_q[k], q);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_bluestein_ntt_pack(const void* in, std::size_t is, std::size_t ibs, void* work, const void* chirp,
+                                      const void* chirp_q, std::size_t n, std::size_t m, std::size_t batch,
+                                      std::uint64_t q, std::uint64_t unit_q, cudaStream_t stream) {
+    ntt_pack_kernel<<<grid_for(m * batch), kThreads, 0, stream>>>(
+        static_cast<const std::uint64_t*>(in), is, ibs, static_cast<std::uint64_t*>(work),
+        static_cast<const std::uint64_t*>(chirp), static_cast<const std::uint64_t*>(chirp_q), n, m, batch, q, unit_q);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bluestein_ntt_multiply(void* work, const void* spectrum, const void* spectrum_q, std::size_t m,
+                                          std::size_t batch, std::uint64_t q, cudaStream_t stream) {
+    ntt_multiply_kernel<<<grid_for(m * batch), kThreads, 0, stream>>>(
+        static_cast<std::uint64_t*>(work), static_cast<const std::uint64_t*>(spectrum),
+        static_cast<const std::uint64_t*>(spectrum_q), m, batch, q);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_bluestein_ntt_unpack(const void* work, void* out, std::size_t os, std::size_t obs,
+                                        const void* chirp, const void* chirp_q, std::size_t n, std::size_t m,
+                                        std::size_t batch, std::uint64_t q, cudaStream_t stream) {
+    ntt_unpack_kernel<<<grid_for(n * batch), kThreads, 0, stream>>>(
+        static_cast<const std::uint64_t*>(work), static_cast<std::uint64_t*>(out), os, obs,
+        static_cast<const std::uint64_t*>(chirp), static_cast<const std::uint64_t*>(chirp_q), n, m, batch, q);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_bluestein_tables(bool f64, std::size_t n, std::size_t m, bool inverse, void* chirp_table,
                                     void* taps, cudaStream_t stream) {

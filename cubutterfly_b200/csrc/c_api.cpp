@@ -423,8 +423,55 @@ void launch_embedded(const cubutterflyPlan& p, const void* in, void* out, cudaSt
 // Bluestein: pack (input x chirp, zero-padded) -> forward conv-point FFT ->
 // x spectrum -> inverse conv-point FFT -> unpack (x chirp) into the output
 // layout.  Input and output may alias: the pack completes before the unpack.
+// Table layout of a Bluestein NTT plan: pack chirp, its Shoup quotients,
+// unpack chirp (x N^-1 for an inverse), its quotients (n words each), then
+// the convolution spectrum and its quotients (conv words each), every part
+// 256-byte aligned.
+struct NttChirpTables {
+    std::size_t pack, pack_q, unpack, unpack_q, spectrum, spectrum_q, bytes;
+    NttChirpTables(std::size_t n, std::size_t m) {
+        const std::size_t a = align256(n * 8), b = align256(m * 8);
+        pack = 0;
+        pack_q = a;
+        unpack = 2 * a;
+        unpack_q = 3 * a;
+        spectrum = 4 * a;
+        spectrum_q = 4 * a + b;
+        bytes = 4 * a + 2 * b;
+    }
+};
+
+void launch_bluestein_ntt(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const std::size_t n = d.extents[0], m = p.conv;
+    const std::uint64_t q = d.modulus;
+    const NttChirpTables t(n, m);
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    const unsigned char* tb = static_cast<const unsigned char*>(p.bluestein_tables);
+    const std::uint64_t unit_q = static_cast<std::uint64_t>((static_cast<unsigned __int128>(1) << 64) / q);
+    check_cuda(cubf::launch_bluestein_ntt_pack(in, d.input_strides[0], d.input_batch_stride, ws, tb + t.pack,
+                                               tb + t.pack_q, n, m, d.batch, q, unit_q, stream),
+               "Bluestein NTT pack launch");
+    for (std::size_t i = 0; i < 2; ++i) {
+        auto& c = *p.axes[i].plan;
+        c.workspace = ws + p.axes[i].ws_offset;
+        launch_mapping(c, c.mapping, ws, ws, stream);
+        if (i == 0)
+            check_cuda(cubf::launch_bluestein_ntt_multiply(ws, tb + t.spectrum, tb + t.spectrum_q, m, d.batch, q,
+                                                           stream),
+                       "Bluestein NTT multiply launch");
+    }
+    check_cuda(cubf::launch_bluestein_ntt_unpack(ws, out, d.output_strides[0], d.output_batch_stride, tb + t.unpack,
+                                                 tb + t.unpack_q, n, m, d.batch, q, stream),
+               "Bluestein NTT unpack launch");
+}
+
 void launch_bluestein(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
     const auto& d = p.desc;
+    if (d.op == CUBUTTERFLY_OPERATOR_NTT) {
+        launch_bluestein_ntt(p, in, out, stream);
+        return;
+    }
     const bool f64 = d.storage == CUBUTTERFLY_DATA_COMPLEX_FP64;
     const std::size_t n = d.extents[0], m = p.conv, esz = cubf::storage_bytes(d.storage);
     unsigned char* ws = static_cast<unsigned char*>(p.workspace);
@@ -1071,9 +1118,119 @@ std::unique_ptr<cubutterflyPlan> create_bluestein(cubutterflyHandle* handle, con
     return p;
 }
 
+// A u64 NTT whose length is not a power of two.
+bool arbitrary_ntt(const cubf::Descriptor& d) {
+    return d.op == CUBUTTERFLY_OPERATOR_NTT && d.length_mode == CUBUTTERFLY_LENGTH_STANDARD &&
+           std::any_of(d.extents.begin(), d.extents.end(), [](std::size_t e) { return !cubf::is_pow2(e); });
+}
+
+// Rank-one arbitrary-length NTT over u64 words (reference
+// src/bluestein_ntt.cu): psi = the reference's primitive 2n-th root (its
+// inverse for an inverse plan), chirps psi^(j^2 mod 2n), the wrapped inverse
+// chirps as convolution taps, the conv-point cyclic convolution on this
+// library's power-of-two NTT plans.  X[k] = sum_j x[j] (psi^2)^(jk) exactly,
+// times n^-1 for an inverse.  Needs a prime q < 2^63 with 2n | q - 1 and
+// conv | q - 1 (INVALID_VALUE otherwise, as the reference).
+std::unique_ptr<cubutterflyPlan> create_bluestein_ntt(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    namespace ma = cubf::modarith;
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->bluestein = true;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    const std::size_t n = d.extents[0];
+    const std::size_t m = bluestein_length(n);
+    const std::uint64_t q = d.modulus;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    p->conv = m;
+    p->physical = {m};
+    require(q < (std::uint64_t{1} << 63), "NTT modulus must be below 2^63");
+    std::uint64_t psi = ma::primitive_root_of_order(2 * n, q);  // validates q and 2n | q - 1
+    require((q - 1) % m == 0, "modulus does not admit the power-of-two Bluestein convolution root");
+    if (inverse) psi = ma::powmod(psi, q - 2, q);
+    // children: forward natural -> bit-reversed, inverse bit-reversed -> natural (x conv^-1)
+    cubf::Descriptor c = bluestein_child(d);
+    c.output_orders = {CUBUTTERFLY_ORDER_BIT_REVERSED};
+    const std::size_t work_bytes = align256(m * d.batch * 8);
+    std::size_t child_ws = 0;
+    for (int i = 0; i < 2; ++i) {
+        cubf::Descriptor ci = c;
+        if (i == 1) {
+            ci.direction = CUBUTTERFLY_DIRECTION_INVERSE;
+            ci.input_orders = {CUBUTTERFLY_ORDER_BIT_REVERSED};
+            ci.output_orders = {CUBUTTERFLY_ORDER_NATURAL};
+        }
+        cubutterflyPlan::Axis ax;
+        ax.plan = create_rank1(handle, cubf::normalize(ci));
+        ax.n = m;
+        ax.outer = d.batch;
+        ax.inner = 1;
+        ax.ws_offset = work_bytes;
+        child_ws = std::max(child_ws, ax.plan->mapping.workspace_bytes);
+        p->axes.push_back(std::move(ax));
+    }
+    p->mapping.family = "bluestein-ntt";
+    p->mapping.label = "bluestein-ntt[" + std::to_string(m) + ":" + p->axes[0].plan->mapping.name() + "]";
+    p->mapping.workspace_bytes = work_bytes + align256(child_ws);
+    p->source = p->axes[0].plan->source;
+    p->reason = "non-power-of-two NTT of " + std::to_string(n) + " points as a " + std::to_string(m) +
+                "-point cyclic convolution (Bluestein) over power-of-two NTT plans";
+
+    // host tables
+    const NttChirpTables t(n, m);
+    std::vector<std::uint64_t> host(t.bytes / 8, 0);
+    const std::uint64_t n_inv = inverse ? ma::powmod(n % q, q - 2, q) : 1;
+    std::vector<std::uint64_t> taps(m, 0);
+    for (std::size_t j = 0; j < n; ++j) {
+        const auto e = static_cast<std::uint64_t>((static_cast<unsigned __int128>(j) * j) % (2 * n));
+        const std::uint64_t cj = ma::powmod(psi, e, q);
+        const std::uint64_t uj = ma::mulmod(cj, n_inv, q);
+        host[t.pack / 8 + j] = cj;
+        host[t.pack_q / 8 + j] = ma::shoup(cj, q);
+        host[t.unpack / 8 + j] = uj;
+        host[t.unpack_q / 8 + j] = ma::shoup(uj, q);
+        const std::uint64_t bj = ma::powmod(cj, q - 2, q);
+        taps[j] = bj;
+        if (j) taps[m - j] = bj;
+    }
+    check_cuda(cudaMalloc(&p->bluestein_tables, t.bytes), "Bluestein NTT table allocation");
+    unsigned char* tb = static_cast<unsigned char*>(p->bluestein_tables);
+    // the taps' spectrum, in the forward child's (bit-reversed) order
+    cubf::Descriptor k = c;
+    k.batch = 1;
+    k.input_batch_stride = k.output_batch_stride = m;
+    k.placement = CUBUTTERFLY_PLACEMENT_OUT_OF_PLACE;
+    auto kp = create_rank1(handle, cubf::normalize(k));
+    DeviceTemp temp(align256(m * 8) + align256(kp->mapping.workspace_bytes) + 256);
+    unsigned char* dtaps = static_cast<unsigned char*>(temp.ptr);
+    kp->workspace = dtaps + align256(m * 8);
+    cudaStream_t s = nullptr;
+    check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "Bluestein set-up stream");
+    try {
+        check_cuda(cudaMemcpyAsync(dtaps, taps.data(), m * 8, cudaMemcpyHostToDevice, s), "Bluestein taps upload");
+        launch_mapping(*kp, kp->mapping, dtaps, tb + t.spectrum, s);
+        check_cuda(cudaMemcpyAsync(host.data() + t.spectrum / 8, tb + t.spectrum, m * 8, cudaMemcpyDeviceToHost, s),
+                   "Bluestein spectrum read");
+        check_cuda(cudaStreamSynchronize(s), "Bluestein set-up");
+        for (std::size_t j = 0; j < m; ++j) host[t.spectrum_q / 8 + j] = ma::shoup(host[t.spectrum / 8 + j], q);
+        check_cuda(cudaMemcpyAsync(tb, host.data(), t.bytes, cudaMemcpyHostToDevice, s), "Bluestein table upload");
+        check_cuda(cudaStreamSynchronize(s), "Bluestein set-up");
+    } catch (...) {
+        cudaStreamSynchronize(s);
+        cudaStreamDestroy(s);
+        throw;
+    }
+    cudaStreamDestroy(s);
+    return p;
+}
+
 // A rank-one plan of any supported length.
 std::unique_ptr<cubutterflyPlan> create_axis(cubutterflyHandle* handle, const cubf::Descriptor& d) {
-    return arbitrary_fft(d) ? create_bluestein(handle, d) : create_rank1(handle, d);
+    if (arbitrary_fft(d)) return create_bluestein(handle, d);
+    if (arbitrary_ntt(d)) return create_bluestein_ntt(handle, d);
+    return create_rank1(handle, d);
 }
 
 // The rank-one child descriptors of a rank-two or rank-three descriptor.
@@ -1747,16 +1904,23 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
         // the best mapping of a rank-one child (its power-of-two core for a
         // Bluestein axis)
         auto child_mapping = [&](const cubf::Descriptor& c) -> cubf::Json {
-            if (!arbitrary_fft(c)) return cubf::enumerate_mappings(make_request(c), hw).front().to_json();
-            const cubf::Descriptor k = bluestein_child(c);
-            return {{"family", "bluestein"},
+            if (!arbitrary_fft(c) && !arbitrary_ntt(c))
+                return cubf::enumerate_mappings(make_request(c), hw).front().to_json();
+            cubf::Descriptor k = bluestein_child(c);
+            if (c.op == CUBUTTERFLY_OPERATOR_NTT) {
+                k.output_orders = {CUBUTTERFLY_ORDER_BIT_REVERSED};
+                k = cubf::normalize(k);
+            }
+            return {{"family", c.op == CUBUTTERFLY_OPERATOR_NTT ? "bluestein-ntt" : "bluestein"},
                     {"convolution_length", k.extents[0]},
                     {"core", cubf::enumerate_mappings(make_request(k), hw).front().to_json()}};
         };
-        if (arbitrary_fft(d) && d.rank == 1) {
+        if ((arbitrary_fft(d) || arbitrary_ntt(d)) && d.rank == 1) {
             cubf::Json axes = cubf::Json::array();
             axes.push_back({{"length", d.extents[0]}, {"outer", d.batch}, {"inner", 1}, {"mapping", child_mapping(d)}});
-            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"}, {"family", "bluestein"}, {"axes", axes}});
+            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"},
+                           {"family", d.op == CUBUTTERFLY_OPERATOR_NTT ? "bluestein-ntt" : "bluestein"},
+                           {"axes", axes}});
         } else if (d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING) {
             cubf::Descriptor c = d;
             std::size_t pn = 1;

@@ -510,14 +510,15 @@ Json capabilities(const Descriptor& source) {
                          [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
             gap("order-lowering", "zero-extended embedding executes natural logical orders");
     }
-    // Standard-length complex FFTs of other lengths run as Bluestein
-    // convolutions over power-of-two FFTs (reference src/bluestein_fft.cu):
-    // C2C, ranks one and two, natural orders, any layout.
+    // Standard-length complex FFTs and u64 NTTs of other lengths run as
+    // Bluestein convolutions over power-of-two transforms (reference
+    // src/bluestein_fft.cu, src/bluestein_ntt.cu): C2C / u64, ranks one and
+    // two, natural orders, any layout.
     const bool arbitrary = d.length_mode == CUBUTTERFLY_LENGTH_STANDARD &&
                            std::any_of(d.extents.begin(), d.extents.end(), [](std::size_t e) { return !is_pow2(e); });
     if (arbitrary) {
-        if (d.op == CUBUTTERFLY_OPERATOR_NTT)
-            gap("arbitrary-length-lowering", "non-power-of-two NTT lengths (Bluestein NTT) are not built");
+        if (d.op == CUBUTTERFLY_OPERATOR_NTT && d.storage != CUBUTTERFLY_DATA_UINT64)
+            gap("arbitrary-word-lowering", "Bluestein NTT executes uint64 words");
         if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C)
             gap("arbitrary-length-lowering", "non-power-of-two R2C/C2R transforms are not built");
         if (d.rank > 2) gap("rank-bluestein-lowering", "rank-three Bluestein composition is not built");
@@ -527,7 +528,7 @@ Json capabilities(const Descriptor& source) {
                          [](auto o) { return o == CUBUTTERFLY_ORDER_NATURAL; }))
             gap("order-lowering", "non-power-of-two FFTs execute natural logical orders");
     }
-    const bool bluestein = arbitrary && d.op == CUBUTTERFLY_OPERATOR_FFT;
+    const bool bluestein = arbitrary && (d.op == CUBUTTERFLY_OPERATOR_FFT || d.op == CUBUTTERFLY_OPERATOR_NTT);
     for (auto n : d.extents)
         if ((!is_pow2(n) && !embedded && !bluestein) || n < 2)
             gap("length-lowering", "extents must be powers of two of at least two");

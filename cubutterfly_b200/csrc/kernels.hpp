@@ -125,6 +125,19 @@ cudaError_t launch_bluestein_pack(bool f64, const void* in, std::size_t in_strid
 // work *= spectrum (per transform)
 cudaError_t launch_bluestein_multiply(bool f64, void* work, const void* spectrum, std::size_t m, std::size_t batch,
                                       cudaStream_t stream);
+// NTT over u64 words: pack reduces the input mod q (unit_q = floor(2^64 / q))
+// and multiplies by the chirp; multiply by the convolution spectrum; unpack
+// multiplies by the output chirp.  Every multiplier comes with its Shoup
+// quotient table.
+cudaError_t launch_bluestein_ntt_pack(const void* in, std::size_t in_stride, std::size_t in_batch_stride, void* work,
+                                      const void* chirp, const void* chirp_q, std::size_t n, std::size_t m,
+                                      std::size_t batch, std::uint64_t q, std::uint64_t unit_q, cudaStream_t stream);
+cudaError_t launch_bluestein_ntt_multiply(void* work, const void* spectrum, const void* spectrum_q, std::size_t m,
+                                          std::size_t batch, std::uint64_t q, cudaStream_t stream);
+cudaError_t launch_bluestein_ntt_unpack(const void* work, void* out, std::size_t out_stride,
+                                        std::size_t out_batch_stride, const void* chirp, const void* chirp_q,
+                                        std::size_t n, std::size_t m, std::size_t batch, std::uint64_t q,
+                                        cudaStream_t stream);
 // output = work[0 .. n) * chirp
 cudaError_t launch_bluestein_unpack(bool f64, const void* work, void* out, std::size_t out_stride,
                                     std::size_t out_batch_stride, const void* chirp_table, std::size_t n,

@@ -70,6 +70,32 @@ inline u64 primitive_root_of_two_power(unsigned log_n, u64 q) {
 }
 
 // Shoup quotient floor(w 2^64 / q) of a constant w < q.
+// The primitive root of an arbitrary order the reference's Bluestein NTT
+// uses (src/bluestein_ntt.cu:42-57): the first candidate c = 2, 3, ... below
+// 2^20 whose power c^((q - 1) / order) has exactly that order (checked
+// against every prime factor of the order).
+inline u64 primitive_root_of_order(u64 order, u64 q) {
+    if (!is_prime(q)) throw std::invalid_argument("Bluestein NTT modulus must be prime");
+    if (order < 2 || (q - 1) % order != 0)
+        throw std::invalid_argument("modulus does not admit the required 2N-th Bluestein root");
+    u64 factors[64];
+    int nf = 0;
+    u64 v = order;
+    for (u64 f = 2; f <= v / f; ++f) {
+        if (v % f) continue;
+        factors[nf++] = f;
+        while (v % f == 0) v /= f;
+    }
+    if (v > 1) factors[nf++] = v;
+    for (u64 c = 2; c < (u64{1} << 20); ++c) {
+        const u64 r = powmod(c, (q - 1) / order, q);
+        bool primitive = powmod(r, order, q) == 1;
+        for (int i = 0; i < nf && primitive; ++i) primitive = powmod(r, order / factors[i], q) != 1;
+        if (primitive) return r;
+    }
+    throw std::runtime_error("could not find the required Bluestein NTT root");
+}
+
 inline u64 shoup(u64 w, u64 q) { return static_cast<u64>((static_cast<u128>(w) << 64) / q); }
 
 inline std::size_t bitrev(std::size_t x, int bits) {

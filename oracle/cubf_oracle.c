@@ -662,4 +662,62 @@ ORACLE_API int cubf_oracle_rns_ntt_batch(const uint64_t* input, uint64_t* output
     return status;
 }
 
+/* NTT of any length n over a prime q with 2n | q - 1, as the reference's
+ * non-power-of-two NTT plans define it (src/bluestein_ntt.cu:42-57, :222-239):
+ * psi = c^((q - 1) / 2n) for the first c = 2, 3, ... that makes it a
+ * primitive 2n-th root, omega = psi^2 (its inverse for an inverse transform),
+ * X[k] = sum_j (x[j] mod q) omega^(jk), times n^-1 for an inverse.  Rows of n
+ * words, in place.  Returns 1 for an unusable modulus. */
+ORACLE_API int cubf_oracle_ntt_any(uint64_t* values, size_t n, size_t batch, uint64_t q, int inverse) {
+    if (n < 2 || !cubf_oracle_is_prime(q) || (q - 1) % (2 * n) != 0) return 1;
+    const uint64_t order = 2 * n;
+    uint64_t factors[64];
+    int nf = 0;
+    uint64_t v = order;
+    for (uint64_t f = 2; f <= v / f; ++f) {
+        if (v % f) continue;
+        factors[nf++] = f;
+        while (v % f == 0) v /= f;
+    }
+    if (v > 1) factors[nf++] = v;
+    uint64_t psi = 0;
+    for (uint64_t c = 2; c < (1ull << 20) && !psi; ++c) {
+        const uint64_t r = cubf_oracle_mod_pow(c, (q - 1) / order, q);
+        int primitive = cubf_oracle_mod_pow(r, order, q) == 1;
+        for (int i = 0; i < nf && primitive; ++i) primitive = cubf_oracle_mod_pow(r, order / factors[i], q) != 1;
+        if (primitive) psi = r;
+    }
+    if (!psi) return 1;
+    uint64_t omega = mod_mul(psi, psi, q);
+    if (inverse) omega = cubf_oracle_mod_pow(omega, q - 2, q);
+    const uint64_t scale = inverse ? cubf_oracle_mod_pow(n % q, q - 2, q) : 1;
+    uint64_t* pw = (uint64_t*)malloc(n * sizeof(uint64_t));
+    uint64_t* x = (uint64_t*)malloc(n * sizeof(uint64_t));
+    if (!pw || !x) {
+        free(pw);
+        free(x);
+        return 1;
+    }
+    pw[0] = 1;
+    for (size_t m = 1; m < n; ++m) pw[m] = mod_mul(pw[m - 1], omega, q);
+    for (size_t b = 0; b < batch; ++b) {
+        uint64_t* row = values + b * n;
+        for (size_t j = 0; j < n; ++j) x[j] = row[j] % q;
+        for (size_t k = 0; k < n; ++k) {
+            u128 acc = 0;
+            size_t m = 0; /* j k mod n */
+            for (size_t j = 0; j < n; ++j) {
+                acc += (u128)x[j] * pw[m];
+                acc %= q;
+                m += k;
+                if (m >= n) m -= n;
+            }
+            row[k] = mod_mul((uint64_t)acc, scale, q);
+        }
+    }
+    free(pw);
+    free(x);
+    return 0;
+}
+
 ORACLE_API int cubf_oracle_abi_version(void) { return 1; }

@@ -61,6 +61,7 @@ class Oracle:
         L.cubf_oracle_dft_bins.argtypes = [_p, _n, _p, _n, _i, _p]
         L.cubf_oracle_dft_bins.restype = None
         L.cubf_oracle_dft_c128.argtypes = [_p, _p, _n, _n, _i, _i]
+        L.cubf_oracle_ntt_any.argtypes = [_p, _n, _n, _u64, _i]
         L.cubf_oracle_fwht_f64.argtypes = [_p, _n, _n, _i, _i]
         L.cubf_oracle_fwht_f32.argtypes = [_p, _n, _n, _i, _i]
         L.cubf_oracle_fwht_bf16_final.argtypes = [_p, _p, _n, _n, _i, _i, _d]
@@ -103,6 +104,16 @@ class Oracle:
         if self.lib.cubf_oracle_dft_c128(_ptr(y), _ptr(out), n, y.size // n, int(inverse), int(normalize)):
             raise ValueError("oracle DFT rejected its input")
         return out
+
+    def ntt_any(self, x: np.ndarray, q: int, inverse=False) -> np.ndarray:
+        """NTT of any length along the last axis with the reference's
+        non-power-of-two root convention (omega = psi^2, psi its primitive
+        2n-th root)."""
+        y = np.ascontiguousarray(x, dtype=np.uint64).copy()
+        n = y.shape[-1]
+        if self.lib.cubf_oracle_ntt_any(_ptr(y), n, y.size // n, q, int(inverse)):
+            raise ValueError("oracle NTT rejected its input")
+        return y
 
     def dft_bins(self, x: np.ndarray, bins, inverse=False) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.complex64)

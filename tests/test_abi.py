@@ -122,7 +122,8 @@ def test_benchmark_configs_are_eligible(lib):
 
 @pytest.mark.parametrize("transform, code", [
     (cb.Transform(op=cb.Operator.FFT, extents=[8, 8], output_orders=[1, 1]), "order-lowering"),
-    (cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[12]), "arbitrary-length-lowering"),
+    (cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT32, extents=[12], modulus=998244353, word_bits=32),
+     "arbitrary-word-lowering"),
     (cb.Transform(op=cb.Operator.FFT, extents=[3, 5, 7]), "rank-bluestein-lowering"),
     (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP16, extents=[64]), "storage-lowering"),
     (cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.FP32, extents=[64]),
@@ -491,3 +492,15 @@ def test_bluestein_preview_names_the_convolution_core(lib):
     ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[100, 64], batch=1))
     lengths = [a["mapping"].get("convolution_length") for a in ms[0]["axes"]]
     assert lengths == [None, 256]  # innermost axis (64) first, then the 100-point axis
+
+
+def test_arbitrary_length_ntt_is_eligible(lib):
+    """u64 NTTs of non-power-of-two lengths run as Bluestein convolutions over
+    the power-of-two NTT (reference src/bluestein_ntt.cu); the 3-point NTT of
+    the reference C test convolves over 8 points."""
+    t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[3], batch=1)
+    assert capabilities(lib, t)["status"] == "eligible"
+    ms = rank(lib, t)
+    assert ms[0]["family"] == "bluestein-ntt" and ms[0]["axes"][0]["mapping"]["convolution_length"] == 8
+    big = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[600000], batch=1)
+    assert "length-lowering" in [g["code"] for g in capabilities(lib, big)["gaps"]]

@@ -110,3 +110,76 @@ def test_rank_two_against_direct_dft(lib, oracle, cuda, extents):
     with cb.Plan(lib, transform(extents, 2)) as plan:
         assert plan.physical_extents(2) == [e if (e & (e - 1)) == 0 else 1 << (2 * e - 2).bit_length()
                                             for e in extents]
+
+
+# ---- NTT of non-power-of-two lengths (u64 words), bit-exact ---------------------
+DEFAULT_Q = 1152921504606584833  # q - 1 = 2^18 3^2 7^2 43 127 337 5419
+
+
+def ntt_transform(n, batch, inverse=False, q=DEFAULT_Q, **kw):
+    return cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=n if isinstance(n, list) else [n],
+                        batch=batch, modulus=q, inverse=inverse, **kw)
+
+
+def test_ntt_reference_round_trip(lib, oracle, cuda):
+    """reference tests/test_c_api.c:332-383: {7, 11, 19} under the default
+    modulus, forward then inverse."""
+    from gpu_util import run
+
+    x = np.array([[7, 11, 19]], dtype=np.uint64)
+    y, name = run(lib, ntt_transform(3, 1), x, cuda)
+    assert name.startswith("bluestein-ntt[8:")
+    assert np.array_equal(y, oracle.ntt_any(x, DEFAULT_Q))
+    back, _ = run(lib, ntt_transform(3, 1, inverse=True), y, cuda)
+    assert np.array_equal(back, x)
+
+
+@pytest.mark.parametrize("n", [3, 7, 12, 63, 127, 903, 5419])
+def test_ntt_against_oracle(lib, oracle, cuda, n):
+    """Full 64-bit input words (reduced on load), forward and inverse."""
+    from gpu_util import run
+
+    x = w.rng(71, n).integers(0, 2**64, size=(3, n), dtype=np.uint64)
+    for inverse in (False, True):
+        got, _ = run(lib, ntt_transform(n, 3, inverse), x, cuda)
+        assert np.array_equal(got, oracle.ntt_any(x, DEFAULT_Q, inverse)), (n, inverse)
+
+
+def test_ntt_layouts_rank_two_and_bad_modulus(lib, oracle, cuda):
+    from gpu_util import run
+    from test_composite_gpu import along_axes, run_nd
+
+    n, batch = 63, 4
+    x = w.rng(72).integers(0, DEFAULT_Q, size=(batch, n), dtype=np.uint64)
+    got, _ = run(lib, ntt_transform(n, batch, in_place=True), x, cuda)
+    assert np.array_equal(got, oracle.ntt_any(x, DEFAULT_Q))
+    from test_layouts_gpu import padding_untouched
+
+    t = ntt_transform(n, batch, input_strides=[3], output_strides=[2], input_batch_stride=3 * n + 1,
+                      output_batch_stride=2 * n + 5)
+    import test_layouts_gpu as tl
+
+    from gpu_util import stream_ptr
+
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        host = np.full(plan.input_size() // 8, 99, dtype=np.uint64)
+        host[tl.layout_view(host, n, batch, 3, 3 * n + 1)] = x
+        din = torch.from_numpy(host.view(np.uint8).copy()).to(cuda)
+        dout = torch.from_numpy(np.full(plan.output_size() // 8, 77, dtype=np.uint64).view(np.uint8).copy()).to(cuda)
+        ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=cuda)
+        plan.set_workspace(ws.data_ptr(), ws.numel())
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        raw = dout.cpu().numpy().view(np.uint64)
+    idx = tl.layout_view(raw, n, batch, 2, 2 * n + 5)
+    assert np.array_equal(raw[idx], oracle.ntt_any(x, DEFAULT_Q))
+    assert padding_untouched(raw, idx, np.uint64(77))
+    # rank two: 7 x 12, each axis its own length
+    x2 = w.rng(73).integers(0, DEFAULT_Q, size=(2, 7, 12), dtype=np.uint64)
+    got2, name = run_nd(lib, ntt_transform([7, 12], 2), x2, cuda)
+    assert "bluestein-ntt" in name
+    assert np.array_equal(got2, along_axes(lambda r: oracle.ntt_any(r, DEFAULT_Q), x2))
+    # 2n must divide q - 1: 11 does not divide the default modulus's q - 1
+    with pytest.raises(cb.Error) as e:
+        cb.Plan(lib, ntt_transform(11, 1))
+    assert "2N-th Bluestein root" in str(e.value)

@@ -171,3 +171,34 @@ def test_dft_matches_numpy(oracle, n):
 def test_dft_matches_reference_fft_at_power_of_two(oracle, reference):
     x = w.fft_input(256, 3, seed=52).astype(np.complex128)
     assert np.abs(oracle.dft(x) - reference.fft_c64(x, normalize=False)).max() < 1e-12
+
+
+DEFAULT_Q = 1152921504606584833  # the reference's default NTT modulus (include/cuntt/ntt.hpp:17)
+
+
+def test_ntt_any_known_answer_round_trip(oracle):
+    """reference tests/test_c_api.c:332-383: a 3-point NTT of {7, 11, 19} under
+    the default modulus, inverted, gives the input back."""
+    x = np.array([[7, 11, 19]], dtype=np.uint64)
+    y = oracle.ntt_any(x, DEFAULT_Q)
+    assert not np.array_equal(y, x)
+    assert np.array_equal(oracle.ntt_any(y, DEFAULT_Q, inverse=True), x)
+
+
+@pytest.mark.parametrize("n", [3, 6, 12])
+def test_ntt_any_matches_its_definition(oracle, n):
+    """Pure-Python restatement of the same definition: psi the first
+    c^((q-1)/2n) of exact order 2n (reference src/bluestein_ntt.cu:42-57),
+    omega = psi^2, X[k] = sum_j x[j] omega^(jk)."""
+    q = DEFAULT_Q
+    order = 2 * n
+    primes = [p for p in range(2, order + 1) if order % p == 0 and all(p % d for d in range(2, p))]
+    psi = next(r for c in range(2, 1 << 20) for r in [pow(c, (q - 1) // order, q)]
+               if pow(r, order, q) == 1 and all(pow(r, order // p, q) != 1 for p in primes))
+    omega = psi * psi % q
+    x = w.rng(70, n).integers(0, 2**63, size=(2, n), dtype=np.uint64)
+    want = np.array([[sum(int(v) % q * pow(omega, j * k, q) for j, v in enumerate(row)) % q for k in range(n)]
+                     for row in x], dtype=np.uint64)
+    assert np.array_equal(oracle.ntt_any(x, q), want)
+    back = oracle.ntt_any(want, q, inverse=True)
+    assert np.array_equal(back, x % np.uint64(q))

@@ -907,8 +907,25 @@ cubf::PlanRequest make_request(const cubf::Descriptor& d) {
     return r;
 }
 
+// An algorithm name of the reference's own catalogue ("ntt-shared-iterative",
+// "bluestein-cufft-power2-core", ...): lower-case words joined by '-', no
+// pass list, bracketed family or JSON.  Those name kernels of the reference
+// build; a plan that asks for one here runs this build's best mapping.
+bool reference_algorithm_name(const std::string& s) {
+    if (s.empty() || s.front() < 'a' || s.front() > 'z' || s.find('-') == std::string::npos) return false;
+    return std::all_of(s.begin(), s.end(), [](char c) { return (c >= 'a' && c <= 'z') || (c >= '0' && c <= '9') || c == '-'; });
+}
+
 void select_mapping(cubutterflyHandle* h, cubutterflyPlan& p) {
     const auto& d = p.desc;
+    if (d.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT && reference_algorithm_name(d.explicit_algorithm)) {
+        p.mapping = cubf::enumerate_mappings(p.req, p.hw).front();
+        p.source = CUBUTTERFLY_SELECTION_STATIC_MODEL;
+        p.reason = "explicit reference algorithm '" + d.explicit_algorithm +
+                   "' names a kernel family of the reference build; the static model's " + p.mapping.name() +
+                   " executes it here";
+        return;
+    }
     if (d.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
         p.mapping = cubf::parse_explicit_mapping(p.req, p.hw, d.explicit_algorithm);
         p.source = CUBUTTERFLY_SELECTION_EXPLICIT;
@@ -1333,7 +1350,9 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
             if (!p->axes[i].plan->physical.empty()) p->physical[d.rank - 1 - i] = p->axes[i].plan->physical[0];
     }
     p->mapping.family = "composite";
-    p->mapping.label = name.str();
+    // xD execution requests run as this composite (the reference's own path
+    // where its xD lowering does not apply); the name keeps the xD prefix
+    p->mapping.label = d.execution_mode == CUBUTTERFLY_EXECUTION_XD ? "xd[" + name.str() + "]" : name.str();
     p->mapping.workspace_bytes = offset;
     p->source = source;
     p->reason = "rank-" + std::to_string(d.rank) + " composition of rank-one plans: " + reason.str();

@@ -143,3 +143,52 @@ def test_legacy_real_fft_adapters(lib, oracle, cuda):
     torch.cuda.synchronize()
     rebuilt = full.cpu().numpy().view(np.complex64).reshape(batch, h, wd)
     assert rel_l2(rebuilt, spectrum) <= 1e-6
+
+
+@pytest.mark.parametrize("extents, batch", [([128, 128], 1), ([32, 32, 32], 4), ([64, 64, 64], 2)])
+def test_xd_uint32_ntt_measure(lib, oracle, cuda, extents, batch):
+    """reference tests/test_c_api.c:298-330: rank-two and rank-three uint32 NTTs
+    mod 257 in xD execution mode with the MEASURE policy plan under an
+    "xd[" algorithm name; results equal the oracle along every axis."""
+    q = 257
+    x = w.rng(80, sum(extents)).integers(0, q, size=(batch, *extents), dtype=np.uint32)
+    for inverse in (False, True):
+        t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT32, extents=extents, batch=batch, modulus=q,
+                         word_bits=32, inverse=inverse, execution_mode=cb.ExecutionMode.XD)
+        got, name = run_nd_opts(lib, t, x, cuda, cb.PlanOptions(policy=cb.AlgorithmPolicy.MEASURE))
+        assert name.startswith("xd["), name
+        want = along_axes(lambda r: oracle.ntt_cyclic(r.astype(np.uint64), q, inverse), x.astype(np.uint64))
+        assert np.array_equal(got.astype(np.uint64), want), (extents, inverse)
+
+
+def run_nd_opts(lib, t, x, cuda, options):
+    from gpu_util import stream_ptr
+
+    with cb.Plan(lib, t, options=options, stream=stream_ptr()) as plan:
+        din = torch.from_numpy(np.ascontiguousarray(x).view(np.uint8).reshape(-1).copy()).to(cuda)
+        dout = torch.zeros(plan.output_size(), dtype=torch.uint8, device=cuda)
+        if plan.workspace_size():
+            ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=cuda)
+            plan.set_workspace(ws.data_ptr(), ws.numel())
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        return dout.cpu().numpy().view(x.dtype).reshape(x.shape), plan.algorithm_name()
+
+
+@pytest.mark.parametrize("word_bits", [32, 64])
+def test_reference_algorithm_name_runs_this_builds_mapping(lib, oracle, cuda, word_bits):
+    """reference tests/test_c_api.c:920-975 asks for its "ntt-shared-iterative"
+    kernels by name: here the name is accepted, this build's mapping runs, and
+    the natural and bit-reversed output layouts agree up to the permutation."""
+    q = 998244353 if word_bits == 32 else 576460756061519873
+    dt = np.uint32 if word_bits == 32 else np.uint64
+    x = (np.arange(16, dtype=np.uint64) * 17 + 3).astype(dt).reshape(2, 8)
+    outs = []
+    for order in (cb.NttLayout.NATURAL, cb.NttLayout.BIT_REVERSED):
+        t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT32 if word_bits == 32 else cb.DataType.UINT64,
+                         extents=[8], batch=2, modulus=q, word_bits=word_bits, output_order=order)
+        got, _ = run_nd_opts(lib, t, x, cuda, cb.PlanOptions(mapping="ntt-shared-iterative"))
+        outs.append(got)
+    rev = [int(format(i, "03b")[::-1], 2) for i in range(8)]
+    assert np.array_equal(outs[1], outs[0][:, rev])
+    assert np.array_equal(outs[0].astype(np.uint64), oracle.ntt_cyclic(x.astype(np.uint64), q))

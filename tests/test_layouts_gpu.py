@@ -177,3 +177,31 @@ def test_zero_extended_fwht_zeta_ntt(lib, oracle, cuda):
     vp = np.zeros((2, 1024), dtype=np.uint64)
     vp[:, :1000] = v
     assert np.array_equal(got, oracle.ntt_cyclic(vp, q))
+
+
+def test_reference_strided_embedding_fwht(lib, cuda):
+    """reference tests/test_c_api.c:791-841: a 6-point FP32 FWHT zero-extended
+    to 8 points, written with output stride 2 into 15 floats."""
+    from gpu_util import stream_ptr
+
+    t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[6],
+                     batch=1, length_mode=cb.LengthMode.ZERO_EXTENDED_EMBEDDING, input_strides=[1],
+                     output_strides=[2], input_batch_stride=6, output_batch_stride=15)
+    expected = np.array([1, 2, 3, 4, 5, 6, 0, 0], dtype=np.float64)
+    width = 1
+    while width < 8:
+        for base in range(0, 8, 2 * width):
+            for o in range(width):
+                a, b = expected[base + o], expected[base + o + width]
+                expected[base + o], expected[base + o + width] = a + b, a - b
+        width *= 2
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        assert plan.output_size() == 15 * 4
+        din = torch.arange(1, 7, dtype=torch.float32, device=cuda)
+        dout = torch.zeros(15, dtype=torch.float32, device=cuda)
+        ws = torch.empty(max(plan.workspace_size(), 16), dtype=torch.uint8, device=cuda)
+        plan.set_workspace(ws.data_ptr(), ws.numel())
+        plan.execute(din.data_ptr(), dout.data_ptr())
+        torch.cuda.synchronize()
+        got = dout.cpu().numpy()
+    assert np.abs(got[0::2] - expected).max() <= 1e-5

@@ -105,6 +105,7 @@ struct cubutterflyPlan {
     bool embedded = false;  // zero-extended embedding: axes[0] transforms the padded rows in place
     cubf::StructuredStages structured{};  // structured 2x2: per-stage matrices (inverted for an inverse plan)
     cubutterflyFftTransformType_t real_kind = CUBUTTERFLY_FFT_C2C;
+    bool real_nd = false;  // rank-two / rank-three R2C / C2R: axes[0] rows, axes[1] outer axes
     void* real_tw = nullptr;  // W_N^k, k = 0..N/2, complex fp32
     // Arbitrary-length FFT (Bluestein): axes[0] / axes[1] are the forward and
     // unnormalised inverse conv-point FFTs, in place on the work buffer at the
@@ -493,8 +494,26 @@ void launch_bluestein(const cubutterflyPlan& p, const void* in, void* out, cudaS
                "Bluestein unpack launch");
 }
 
+void launch_real_nd(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
+    unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    auto& rows = *p.axes[0].plan;
+    auto& axes = *p.axes[1].plan;
+    rows.workspace = axes.workspace = ws + p.axes[0].ws_offset;
+    if (p.desc.fft_type == CUBUTTERFLY_FFT_R2C) {
+        launch_mapping(rows, rows.mapping, in, ws, stream);
+        launch_mapping(axes, axes.mapping, ws, out, stream);
+    } else {
+        launch_mapping(axes, axes.mapping, in, ws, stream);
+        launch_mapping(rows, rows.mapping, ws, out, stream);
+    }
+}
+
 void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                     cudaStream_t stream) {
+    if (p.real_nd) {
+        launch_real_nd(p, in, out, stream);
+        return;
+    }
     if (p.bluestein) {
         launch_bluestein(p, in, out, stream);
         return;
@@ -1254,8 +1273,11 @@ std::unique_ptr<cubutterflyPlan> create_axis(cubutterflyHandle* handle, const cu
 struct AxisSpec {
     cubf::Descriptor d;
     std::size_t n, outer, inner;
+    std::size_t axis = 0;  // descriptor axis (FFT / NTT children)
 };
-std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat) {
+// skip_innermost: leave the innermost axis untransformed (the outer axes of a
+// multi-rank real FFT, whose innermost axis is the half spectrum).
+std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat, bool skip_innermost = false) {
     cubf::Descriptor c = d;
     c.rank = 1;
     c.input_orders = c.output_orders = {CUBUTTERFLY_ORDER_NATURAL};
@@ -1299,10 +1321,11 @@ std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat) {
     flat = false;
     c.placement = CUBUTTERFLY_PLACEMENT_IN_PLACE;  // children run in place on the workspace copies
     for (std::size_t k = d.rank; k-- > 0;) {
+        if (skip_innermost && k + 1 == d.rank) continue;
         std::size_t outer = d.batch, inner = 1;
         for (std::size_t j = 0; j < k; ++j) outer *= d.extents[j];
         for (std::size_t j = k + 1; j < d.rank; ++j) inner *= d.extents[j];
-        AxisSpec a{c, d.extents[k], outer, inner};
+        AxisSpec a{c, d.extents[k], outer, inner, k};
         a.d.extents = {d.extents[k]};
         a.d.batch = outer * inner;
         a.d.input_batch_stride = a.d.output_batch_stride = d.extents[k];
@@ -1311,7 +1334,8 @@ std::vector<AxisSpec> composite_axes(const cubf::Descriptor& d, bool& flat) {
     return axes;
 }
 
-std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, const cubf::Descriptor& d,
+                                                  bool skip_innermost = false) {
     auto p = std::make_unique<cubutterflyPlan>();
     p->desc = d;
     p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride);
@@ -1322,7 +1346,7 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
     for (auto e : d.extents) volume *= e;
     p->packed_bytes = align256(d.batch * volume * cubf::storage_bytes(d.storage));
     bool flat = false;
-    const auto specs = composite_axes(d, flat);
+    const auto specs = composite_axes(d, flat, skip_innermost);
     p->flat = flat;
     const bool two_buffers = d.op == CUBUTTERFLY_OPERATOR_FFT || d.op == CUBUTTERFLY_OPERATOR_NTT;
     std::size_t offset = flat ? 0 : p->packed_bytes * (two_buffers ? 2 : 1);
@@ -1337,7 +1361,8 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
         ax.inner = specs[i].inner;
         ax.ws_offset = offset;
         offset += align256(ax.plan->mapping.workspace_bytes);
-        const std::string label = flat || specs.size() == 1 ? "flat" : "axis" + std::to_string(d.rank - 1 - i);
+        const std::string label = flat || (specs.size() == 1 && !skip_innermost) ? "flat"
+                                                                                 : "axis" + std::to_string(specs[i].axis);
         name << (i ? "," : "") << label << ":" << ax.plan->mapping.name();
         reason << (i ? "; " : "") << label << ": " << ax.plan->reason;
         if (ax.plan->source != CUBUTTERFLY_SELECTION_STATIC_MODEL) source = ax.plan->source;
@@ -1416,6 +1441,102 @@ std::unique_ptr<cubutterflyPlan> create_real(cubutterflyHandle* handle, const cu
     check_cuda(cudaMalloc(&p->real_tw, tw.size() * sizeof(float)), "real twiddle allocation");
     check_cuda(cudaMemcpy(p->real_tw, tw.data(), tw.size() * sizeof(float), cudaMemcpyHostToDevice),
                "real twiddle upload");
+    return p;
+}
+
+// The row transform of a rank-two / rank-three real FFT: the rank-one real
+// transform of every innermost line, packed, carrying the output scale (and
+// the outer axes' share of a normalised inverse's 1 / N).
+cubf::Descriptor real_rows(const cubf::Descriptor& d) {
+    const bool r2c = d.fft_type == CUBUTTERFLY_FFT_R2C;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    const std::size_t nl = d.extents.back(), h = nl / 2 + 1;
+    std::size_t outer = 1;
+    for (std::size_t k = 0; k + 1 < d.rank; ++k) outer *= d.extents[k];
+    cubf::Descriptor r = d;
+    r.rank = 1;
+    r.extents = {nl};
+    r.batch = d.batch * outer;
+    r.input_strides = r.output_strides = {1};
+    r.input_batch_stride = r2c ? nl : h;
+    r.output_batch_stride = r2c ? h : nl;
+    r.input_orders = r.output_orders = {CUBUTTERFLY_ORDER_NATURAL};
+    r.stage_matrices.assign(3, {});
+    r.execution_mode = CUBUTTERFLY_EXECUTION_AUTO;
+    r.fft_output_scale = d.fft_output_scale * (inverse && d.normalize_inverse ? 1.0 / static_cast<double>(outer) : 1.0);
+    if (r.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
+        r.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+        r.explicit_algorithm.clear();
+    }
+    return cubf::normalize(r);
+}
+
+// The outer axes of a rank-two / rank-three real FFT: C2C over the packed
+// half-spectrum tensor, whose innermost axis the composite leaves untouched.
+cubf::Descriptor real_outer(const cubf::Descriptor& d) {
+    const std::size_t h = d.extents.back() / 2 + 1;
+    std::size_t outer = 1;
+    for (std::size_t k = 0; k + 1 < d.rank; ++k) outer *= d.extents[k];
+    cubf::Descriptor c = d;
+    c.fft_type = CUBUTTERFLY_FFT_C2C;
+    c.storage = CUBUTTERFLY_DATA_COMPLEX_FP32;
+    c.compute = CUBUTTERFLY_COMPUTE_FP32;
+    c.extents.back() = h;
+    c.input_strides = c.output_strides = packed_strides(c.extents);
+    c.input_batch_stride = c.output_batch_stride = outer * h;
+    c.input_orders = c.output_orders = std::vector<cubutterflyLogicalOrder_t>(d.rank, CUBUTTERFLY_ORDER_NATURAL);
+    c.normalize_inverse = false;
+    c.fft_output_scale = 1.0;
+    c.placement = CUBUTTERFLY_PLACEMENT_OUT_OF_PLACE;
+    c.execution_mode = CUBUTTERFLY_EXECUTION_AUTO;
+    if (c.algorithm_policy == CUBUTTERFLY_ALGORITHM_EXPLICIT) {
+        c.algorithm_policy = CUBUTTERFLY_ALGORITHM_DEFAULT;
+        c.explicit_algorithm.clear();
+    }
+    return cubf::normalize(c);
+}
+
+// Rank-two and rank-three R2C / C2R (the reference's RealFFT,
+// python/cubutterfly/real_fft.py): axes[0] the rank-one real transform of
+// the innermost axis over every row, axes[1] a C2C composite over the outer
+// axes of the half-spectrum tensor (its innermost axis untouched).  R2C runs
+// rows then outer axes, C2R the reverse, through a packed half tensor at the
+// start of the workspace; the output scale (and a normalised inverse's 1 / N)
+// is applied once, by the row transform.
+std::unique_ptr<cubutterflyPlan> create_real_nd(cubutterflyHandle* handle, const cubf::Descriptor& d) {
+    auto p = std::make_unique<cubutterflyPlan>();
+    p->desc = d;
+    p->real_nd = true;
+    p->input_bytes = layout_span(d, cubf::input_extents(d), d.input_strides, d.input_batch_stride) *
+                     (d.fft_type == CUBUTTERFLY_FFT_C2R ? 2 : 1);
+    p->output_bytes = layout_span(d, cubf::output_extents(d), d.output_strides, d.output_batch_stride) *
+                      (d.fft_type == CUBUTTERFLY_FFT_R2C ? 2 : 1);
+    p->hw = cubf::resolve_profile();
+    check_cuda(cudaGetDevice(&p->device), "current device");
+    const bool r2c = d.fft_type == CUBUTTERFLY_FFT_R2C;
+    const std::size_t nl = d.extents.back(), h = nl / 2 + 1;
+    std::size_t outer = 1;
+    for (std::size_t k = 0; k + 1 < d.rank; ++k) outer *= d.extents[k];
+    const cubf::Descriptor r = real_rows(d), c = real_outer(d);
+    p->packed_bytes = align256(d.batch * outer * h * 8);
+    cubutterflyPlan::Axis rows, axes;
+    rows.plan = create_real(handle, r);
+    axes.plan = create_composite(handle, c, true);
+    rows.n = nl;
+    axes.n = h;
+    rows.outer = axes.outer = d.batch;
+    rows.inner = axes.inner = 1;
+    rows.ws_offset = axes.ws_offset = p->packed_bytes;
+    p->mapping.family = r2c ? "fft-r2c" : "fft-c2r";
+    p->mapping.label = p->mapping.family + "-rank" + std::to_string(d.rank) + "[rows:" + rows.plan->mapping.name() +
+                       "," + axes.plan->mapping.name() + "]";
+    p->mapping.workspace_bytes =
+        p->packed_bytes + align256(std::max(rows.plan->mapping.workspace_bytes, axes.plan->mapping.workspace_bytes));
+    p->source = rows.plan->source;
+    p->reason = std::string(r2c ? "R2C" : "C2R") + " of rank " + std::to_string(d.rank) +
+                ": rank-one real rows, then C2C outer axes of the half spectrum: " + rows.plan->reason;
+    p->axes.push_back(std::move(rows));
+    p->axes.push_back(std::move(axes));
     return p;
 }
 
@@ -1779,7 +1900,8 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
         auto p = d.op == CUBUTTERFLY_OPERATOR_FWHT && d.storage == CUBUTTERFLY_DATA_FP64
                      ? create_fwht64(handle, d)
                  : d.length_mode == CUBUTTERFLY_LENGTH_ZERO_EXTENDED_EMBEDDING ? create_embedded(handle, d)
-                 : d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C ? create_real(handle, d)
+                 : d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C
+                     ? (d.rank == 1 ? create_real(handle, d) : create_real_nd(handle, d))
                  : d.rank == 1                                                        ? create_axis(handle, d)
                                                                                       : create_composite(handle, d);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
@@ -1956,6 +2078,19 @@ cubutterflyStatus_t cubutterflyB200RankMappings(cubutterflyDescriptor_t descript
             axes.push_back({{"length", pn}, {"outer", d.batch}, {"inner", 1},
                             {"mapping", cubf::enumerate_mappings(make_request(c), hw).front().to_json()}});
             out.push_back({{"schema", "cubutterfly-b200-mapping-v1"}, {"family", "zero-extended"}, {"axes", axes}});
+        } else if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C && d.rank > 1) {
+            const cubf::Descriptor r = real_rows(d), c = real_outer(d);
+            cubf::Json axes = cubf::Json::array();
+            axes.push_back({{"length", d.extents.back()}, {"outer", r.batch}, {"inner", 1},
+                            {"mapping", cubf::enumerate_mappings(make_request(real_child(r)), hw).front().to_json()}});
+            bool flat = false;
+            for (const auto& a : composite_axes(c, flat, true)) {
+                const cubf::Descriptor ca = cubf::normalize(a.d);
+                axes.push_back({{"length", a.n}, {"outer", a.outer}, {"inner", a.inner}, {"mapping", child_mapping(ca)}});
+            }
+            out.push_back({{"schema", "cubutterfly-b200-mapping-v1"},
+                           {"family", d.fft_type == CUBUTTERFLY_FFT_R2C ? "fft-r2c" : "fft-c2r"},
+                           {"axes", axes}});
         } else if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C) {
             const cubf::Descriptor c = real_child(d);
             cubf::Json axes = cubf::Json::array();

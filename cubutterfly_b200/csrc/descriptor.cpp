@@ -535,16 +535,28 @@ Json capabilities(const Descriptor& source) {
     // R2C / C2R: rank one, fp32, packed, out of place, over an N/2-point
     // complex FFT (N >= 4)
     const bool real_fft = d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C;
+    // (ranks two and three: real rows of the innermost axis, then C2C over
+    // the outer axes of the half spectrum, as the reference's RealFFT)
     if (real_fft) {
-        if (d.rank != 1) gap("real-fft-lowering", "R2C/C2R transforms are built for rank one");
+        if (d.rank > 3) gap("real-fft-lowering", "R2C/C2R transforms are built for ranks one to three");
         if (d.storage != CUBUTTERFLY_DATA_FP32)
             gap("real-fft-lowering", "R2C/C2R transforms execute FP32 real storage");
-        if (d.extents[0] < 4) gap("real-fft-lowering", "R2C/C2R transforms need at least four points");
+        if (d.extents.back() < 4) gap("real-fft-lowering", "R2C/C2R transforms need at least four points");
         if (d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE)
             gap("real-fft-lowering", "R2C/C2R transforms execute out of place");
         const auto ri = side(d, true), ro = side(d, false);
-        if (d.input_strides != std::vector<std::size_t>{1} || d.output_strides != std::vector<std::size_t>{1} ||
-            d.input_batch_stride != ri[0] || d.output_batch_stride != ro[0])
+        auto packed = [](const std::vector<std::size_t>& e) {
+            std::vector<std::size_t> st(e.size(), 1);
+            for (std::size_t k = e.size() - 1; k-- > 0;) st[k] = st[k + 1] * e[k + 1];
+            return st;
+        };
+        auto volume = [](const std::vector<std::size_t>& e) {
+            std::size_t v = 1;
+            for (auto x : e) v *= x;
+            return v;
+        };
+        if (d.input_strides != packed(ri) || d.output_strides != packed(ro) || d.input_batch_stride != volume(ri) ||
+            d.output_batch_stride != volume(ro))
             gap("layout-lowering", "R2C/C2R transforms execute packed batches");
         if (!std::isfinite(static_cast<float>(d.fft_output_scale)))
             gap("fft-scale-lowering", "FFT output scale must be representable as finite FP32");

@@ -303,8 +303,10 @@ def test_real_fft_plans_and_gaps(lib):
     assert m["axes"][0]["mapping"]["family"] == "fft-stockham-global"
     for bad, code in ((cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[64], fft_type=1,
                                     in_place=True), "real-fft-lowering"),
-                      (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[8, 8], fft_type=1),
+                      (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[2, 2, 2, 8], fft_type=1),
                        "real-fft-lowering"),
+                      (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[6, 8], fft_type=1),
+                       "arbitrary-length-lowering"),
                       (cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, extents=[64], fft_type=1,
                                     input_strides=[2], output_strides=[1]), "layout-lowering")):
         assert code in [g["code"] for g in capabilities(lib, bad)["gaps"]]
@@ -504,3 +506,18 @@ def test_arbitrary_length_ntt_is_eligible(lib):
     assert ms[0]["family"] == "bluestein-ntt" and ms[0]["axes"][0]["mapping"]["convolution_length"] == 8
     big = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[600000], batch=1)
     assert "length-lowering" in [g["code"] for g in capabilities(lib, big)["gaps"]]
+
+
+def test_rank_two_and_three_real_fft_plans(lib):
+    """R2C / C2R of ranks two and three (the reference's RealFFT): real rows of
+    the innermost axis, then C2C over the outer axes of the half spectrum."""
+    for extents in ([64, 128], [8, 16, 32]):
+        for fft_type in (cb.FftType.R2C, cb.FftType.C2R):
+            t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32,
+                             extents=extents, batch=3, fft_type=fft_type, inverse=fft_type == cb.FftType.C2R)
+            assert capabilities(lib, t)["status"] == "eligible", capabilities(lib, t)["gaps"]
+            (m,) = rank(lib, t)
+            half = extents[-1] // 2 + 1
+            assert m["axes"][0]["length"] == extents[-1]
+            assert [a["length"] for a in m["axes"][1:]] == extents[-2::-1]
+            assert all(a["inner"] % half == 0 for a in m["axes"][1:])

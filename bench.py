@@ -45,6 +45,8 @@ def parse():
     p.add_argument("--cpu-baseline", choices=["auto", "skip"], default="auto")
     p.add_argument("--only", choices=["fwht4096", "fwht128", "fft", "zeta", "ntt", "fft1g"],
                    help="run just this operator's launches (profiling driver; prints a short JSON line)")
+    p.add_argument("--inventory", action="store_true",
+                   help="time every other kernel family once per operator on moderate sizes (one JSON line each)")
     p.add_argument("--workload", choices=["fwht", "fft4step", "fftbatch"], default="fwht",
                    help="fwht: configs[1] (default, weak scaling); fft4step: config 4, one 2^30-point FFT "
                         "split over all ranks (strong scaling); fftbatch: config 4's batch sweep, 2^20 "
@@ -56,7 +58,7 @@ def parse():
                         "e.g. 'fwht-tcgen05[6+6]' for the tensor-core FWHT")
     args = p.parse_args()
     if args.steps is None:
-        args.steps = 20 if args.workload in ("fft4step", "fftbatch") and not args.only else 4000
+        args.steps = 20 if (args.workload in ("fft4step", "fftbatch") and not args.only) or args.inventory else 4000
     return args
 
 
@@ -187,6 +189,77 @@ def reference_arm(args):
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- kernel inventory ----------------------------------------------------------------------------
+def inventory(args):
+    """One line per operator outside the headline and per-op table: device
+    time per execution (CUDA events over `steps` executions after `warmup`)
+    and algorithmic bytes (input + output once) per execution.  Sizes are
+    moderate (a few hundred MiB at most) so that the same command can run
+    under an ncu launch list."""
+    import torch
+
+    import cubutterfly_b200 as cb
+
+    dev = torch.device("cuda", 0)
+    lib = cb.Library()
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    steps = args.steps
+    g = torch.Generator(device=dev).manual_seed(7)
+
+    def fill(nbytes):
+        return torch.randint(0, 1 << 20, (nbytes // 4,), dtype=torch.int32, device=dev, generator=g)
+
+    def case(label, t, in_bytes, out_bytes, make_input=None):
+        with cb.Plan(lib, t, stream=sp) as p:
+            x = make_input() if make_input else fill(p.input_size())
+            y = x if t.in_place else torch.empty(p.output_size() // 4 + 1, dtype=torch.int32, device=dev)
+            ws = torch.empty(max(p.workspace_size(), 16), dtype=torch.uint8, device=dev)
+            if p.workspace_size():
+                p.set_workspace(ws.data_ptr(), ws.numel())
+            ms = time_launches(lambda i: p.execute(x.data_ptr(), y.data_ptr()), stream, steps, args.warmup)
+            nbytes = in_bytes + out_bytes
+            print(json.dumps({"inventory": label, "algorithm": p.algorithm_name(), "us": round(ms * 1e3, 2),
+                              "gbs": round(nbytes / ms / 1e6, 1), "bytes": nbytes}), flush=True)
+
+    n, b = 1 << 20, 64
+    mats = [[(0.6, 0.8, -0.8, 0.6)]]
+    case("structured_2x2_f32_2^20x64",
+         cb.Transform(op=cb.Operator.STRUCTURED_2X2, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32,
+                      extents=[n], batch=b, stage_matrices=mats), 4 * n * b, 4 * n * b,
+         lambda: torch.randn(n * b, dtype=torch.float32, device=dev))
+    case("fwht_native_bf16_16384x4096",
+         cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.BF16, compute=cb.ComputeType.NATIVE, extents=[4096],
+                      batch=16384), 2 * 4096 * 16384, 2 * 4096 * 16384,
+         lambda: torch.randn(4096 * 16384, dtype=torch.float32, device=dev).to(torch.bfloat16))
+    case("fft_c128_2^16x256",
+         cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, compute=cb.ComputeType.FP64,
+                      extents=[1 << 16], batch=256), 16 * (1 << 16) * 256, 16 * (1 << 16) * 256,
+         lambda: torch.randn(2 * (1 << 16) * 256, dtype=torch.float64, device=dev))
+    q = 576460756061519873
+    case("ntt_cyclic_u64_2^16x32_natural",
+         cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[1 << 16], batch=32, modulus=q),
+         8 * (1 << 16) * 32, 8 * (1 << 16) * 32)
+    case("fft_r2c_f32_2^20x64",
+         cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[n], batch=b,
+                      fft_type=cb.FftType.R2C), 4 * n * b, 8 * (n // 2 + 1) * b,
+         lambda: torch.randn(n * b, dtype=torch.float32, device=dev))
+    case("fft_c64_4096x1024_strided_in",
+         cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=1024, input_strides=[2], output_strides=[1],
+                      input_batch_stride=8192, output_batch_stride=4096), 8 * 4096 * 1024, 8 * 4096 * 1024,
+         lambda: torch.randn(2 * 8192 * 1024, dtype=torch.float32, device=dev))
+    case("fft_c64_bluestein_4095x1024",
+         cb.Transform(op=cb.Operator.FFT, extents=[4095], batch=1024), 8 * 4095 * 1024, 8 * 4095 * 1024,
+         lambda: torch.randn(2 * 4095 * 1024, dtype=torch.float32, device=dev))
+    case("ntt_u64_bluestein_5419x64",
+         cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[5419], batch=64,
+                      modulus=1152921504606584833), 8 * 5419 * 64, 8 * 5419 * 64)
+    case("fft_c64_rank2_1024x1024",
+         cb.Transform(op=cb.Operator.FFT, extents=[1024, 1024], batch=16), 8 * (1 << 20) * 16, 8 * (1 << 20) * 16,
+         lambda: torch.randn(2 * (1 << 20) * 16, dtype=torch.float32, device=dev))
     return 0
 
 
@@ -387,6 +460,8 @@ def main():
         return reference_arm(args)
     if args.only:
         return only_op(args)
+    if args.inventory:
+        return inventory(args)
     if args.workload == "fft4step":
         return fft4step(args)
     if args.workload == "fftbatch":

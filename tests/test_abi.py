@@ -521,3 +521,43 @@ def test_rank_two_and_three_real_fft_plans(lib):
             assert m["axes"][0]["length"] == extents[-1]
             assert [a["length"] for a in m["axes"][1:]] == extents[-2::-1]
             assert all(a["inner"] % half == 0 for a in m["axes"][1:])
+
+
+def test_command_line_inspects_a_descriptor(lib, tmp_path):
+    """python -m cubutterfly_b200 DESCRIPTOR.json validates on the CPU and
+    prints the normalised descriptor with its capabilities."""
+    import subprocess
+    import sys
+
+    with cb.Descriptor(lib, cb.Transform(op=cb.Operator.FFT, extents=[12], batch=2)) as d:
+        path = tmp_path / "d.json"
+        path.write_text(d.json())
+    out = subprocess.run([sys.executable, "-m", "cubutterfly_b200", str(path)], cwd=ROOT, capture_output=True,
+                         text=True, check=True).stdout
+    j = json.loads(out)
+    assert j["capabilities"]["status"] == "eligible" and j["descriptor"]["semantics"]["batch"] == 2
+
+
+def compile_cpp(source, exe):
+    """g++ a consumer of include/cubutterfly against the in-tree library."""
+    import shutil
+    import subprocess
+
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.skip("g++ not available")
+    libdir = ROOT / "cubutterfly_b200" / "lib"
+    subprocess.run([gxx, "-std=c++17", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include", str(source),
+                    f"-L{libdir}", "-lcubutterfly_b200", "-L/usr/local/cuda/lib64", "-lcudart",
+                    f"-Wl,-rpath,{libdir}", "-Wl,-rpath,/usr/local/cuda/lib64", "-o", str(exe)], check=True)
+    return exe
+
+
+def test_cpp_owner_header_on_cpu(tmp_path):
+    """include/cubutterfly/plan.hpp (the reference's C++ interface): descriptor
+    construction, JSON round trip, capabilities and exceptions, no device."""
+    import subprocess
+
+    exe = compile_cpp(ROOT / "tests" / "cpp" / "plan_api_cpu.cpp", tmp_path / "plan_api_cpu")
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr

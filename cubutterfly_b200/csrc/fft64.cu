@@ -7,8 +7,9 @@
 // double with the same angle rounding (k = o N / (2 half)).  Products and sums
 // round separately in the reference's order, so results are bit-identical to
 // it.  The low min(L, 11) stages run in one shared-memory tile pass over
-// 2^11-point blocks; each higher stage is one in-place pass; a normalised
-// inverse scales by 1/N (exact) in the last pass.
+// 2^11-point blocks; higher stages in groups of up to eight per in-place
+// column pass (128-byte column runs of the rows those stages pair); a
+// normalised inverse scales by 1/N (exact) in the last stage.
 #include "kernels.hpp"
 
 #include <cuda_runtime.h>
@@ -49,15 +50,37 @@ __global__ void __launch_bounds__(kThreads)
     for (size_t i = threadIdx.x; i < n; i += kThreads) block[i] = tile[i];
 }
 
+// Stages s0 .. s0 + g - 1 (s0 >= 11, g <= 8) in one in-place pass: a CTA
+// takes kCols adjacent columns (128-byte runs) of the 2^g rows 2^s0 apart
+// that those stages pair and applies them in order in shared memory, with the
+// per-stage twiddles and arithmetic of the single-stage form.
+constexpr int kColGroup = 8;
+constexpr int kCols = 8;
 __global__ void __launch_bounds__(kThreads)
-    fft64_stage_kernel(double2* data, const double2* __restrict__ tw, int log_n, int s, size_t pairs, double scale) {
-    const size_t half = size_t{1} << s;
-    for (size_t p = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; p < pairs;
-         p += static_cast<size_t>(gridDim.x) * kThreads) {
-        const size_t o = p & (half - 1);
-        const size_t lo = ((p >> s) << (s + 1)) | o;
-        butterfly(data[lo], data[lo + half], __ldg(tw + (o << (log_n - 1 - s))), scale);
+    fft64_column_kernel(double2* data, const double2* __restrict__ tw, int log_n, int s0, int g, double last_scale) {
+    extern __shared__ __align__(16) unsigned char raw[];
+    double2* tile = reinterpret_cast<double2*>(raw);  // [2^g rows][kCols]
+    const size_t tiles_per_block = (size_t{1} << s0) / kCols;
+    const size_t blk = blockIdx.x / tiles_per_block;
+    const size_t c0 = (blockIdx.x % tiles_per_block) * kCols;
+    double2* base = data + (blk << (s0 + g)) + c0;
+    const int n = kCols << g;
+    for (int i = threadIdx.x; i < n; i += kThreads) tile[i] = base[(static_cast<size_t>(i / kCols) << s0) + i % kCols];
+    __syncthreads();
+    for (int k = 0; k < g; ++k) {
+        const int st = s0 + k;
+        const double scale = st + 1 == log_n ? last_scale : 1.0;
+        const int half = 1 << k;
+        for (int p = threadIdx.x; p < n / 2; p += kThreads) {
+            const int c = p % kCols, q = p / kCols;
+            const int r = ((q >> k) << (k + 1)) | (q & (half - 1));
+            // offset of the pair's low element within its 2^(st+1) group
+            const size_t o = (static_cast<size_t>(r & (half - 1)) << s0) | (c0 + c);
+            butterfly(tile[r * kCols + c], tile[(r + half) * kCols + c], __ldg(tw + (o << (log_n - 1 - st))), scale);
+        }
+        __syncthreads();
     }
+    for (int i = threadIdx.x; i < n; i += kThreads) base[(static_cast<size_t>(i / kCols) << s0) + i % kCols] = tile[i];
 }
 
 }  // namespace
@@ -75,13 +98,14 @@ cudaError_t launch_fft64(int log_n, const void* in, void* out, std::size_t batch
     const int smem = 16 << tile_log;
     fft64_tile_kernel<<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(data, tw, log_n, tile_log, scale);
     e = cudaGetLastError();
-    const std::size_t pairs = (batch << log_n) / 2;
-    std::size_t grid = (pairs + kThreads - 1) / kThreads;
-    if (grid > 148 * 32) grid = 148 * 32;
-    for (int s = tile_log; s < log_n && e == cudaSuccess; ++s) {
-        fft64_stage_kernel<<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(data, tw, log_n, s, pairs,
-                                                                               s + 1 == log_n ? scale : 1.0);
+    for (int s0 = tile_log; s0 < log_n && e == cudaSuccess;) {
+        const int g = log_n - s0 < kColGroup ? log_n - s0 : kColGroup;
+        const std::size_t ctas = (batch << (log_n - s0 - g)) * ((std::size_t{1} << s0) / kCols);
+        if (ctas > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        fft64_column_kernel<<<static_cast<unsigned>(ctas), kThreads, 16 * (kCols << g), stream>>>(data, tw, log_n, s0,
+                                                                                                g, scale);
         e = cudaGetLastError();
+        s0 += g;
     }
     return e;
 }

@@ -339,11 +339,11 @@ Json Mapping::to_json() const {
             case PassKind::NttSingle: kernel = "ntt_single"; break;
             case PassKind::FwhtTensor: kernel = "fwht_tcgen05"; break;
             case PassKind::StructuredTile: kernel = "structured_tile"; break;
-            case PassKind::StructuredStage: kernel = "structured_stage"; break;
+            case PassKind::StructuredStage: kernel = "structured_column"; break;
             case PassKind::NativeTile: kernel = "fwht_native_tile"; break;
             case PassKind::NativeStage: kernel = "fwht_native_stage"; break;
             case PassKind::Fft64Tile: kernel = "fft64_tile"; break;
-            case PassKind::Fft64Stage: kernel = "fft64_stage"; break;
+            case PassKind::Fft64Stage: kernel = "fft64_column"; break;
             default: break;
         }
         ps.push_back({{"kernel", kernel},
@@ -387,7 +387,7 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         return out;
     }
     if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native || r.fft64) {
-        // one shared-memory tile pass for the low 12 (fp64 FFT: 11) stages, one pass per higher stage
+        // one shared-memory tile pass for the low 12 (fp64 FFT: 11) stages
         const bool native = r.fwht_native;
         Mapping m;
         m.family = r.fft64 ? "fft64-radix2" : native ? "fwht-native" : "structured-2x2";
@@ -402,14 +402,18 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         t.shape.units_per_cta = 1;
         m.passes.push_back(t);
         m.predicted_us += pass_time_us(hw, elems, esz, esz, tile, tile, 3.0, 0.7);
-        for (int s = tile; s < r.log_n; ++s) {
+        // higher stages: one pass each (native), or column passes of up to
+        // eight stages (structured, fp64 FFT)
+        const int group = native ? 1 : 8;
+        for (int s = tile; s < r.log_n;) {
             Pass g;
             g.kind = r.fft64 ? PassKind::Fft64Stage : native ? PassKind::NativeStage : PassKind::StructuredStage;
-            g.log_h = 1;
+            g.log_h = std::min(group, r.log_n - s);
             g.log_inner = s;
             g.shape.threads = 256;
             m.passes.push_back(g);
-            m.predicted_us += pass_time_us(hw, elems, esz, esz, 1, 0, 3.0, 0.7);
+            m.predicted_us += pass_time_us(hw, elems, esz, esz, g.log_h, 0, 3.0, 0.7);
+            s += g.log_h;
         }
         out.push_back(m);
         return out;

@@ -4,8 +4,8 @@
 // Stage s (s = 0 .. L-1, applied in that order) maps every pair (l, r) whose
 // indices differ in bit s to (m00 l + m01 r, m10 l + m11 r) with the stage's
 // matrix.  The low min(L, 12) stages run in one shared-memory tile pass per
-// 2^12-element block; each higher stage is one in-place pass over pairs
-// 2^s apart.  Products and sums round separately (no fused multiply-add), in
+// 2^12-element block; higher stages in groups of up to eight per in-place
+// column pass (64-byte column runs of the rows those stages pair).  Products and sums round separately (no fused multiply-add), in
 // the reference's stage order, so results are bit-identical to it.
 #include "kernels.hpp"
 
@@ -64,16 +64,35 @@ __global__ void __launch_bounds__(kThreads)
     for (size_t i = threadIdx.x; i < n; i += kThreads) dst[i] = tile[i];
 }
 
-// Stage s >= kTileLog over `pairs` pairs of the whole batch, in place.
+// Stages s0 .. s0 + g - 1 (s0 >= 12, g <= 8) in one in-place pass: a CTA
+// takes kCols adjacent columns (64-byte runs) of the 2^g rows 2^s0 apart that
+// those stages pair, applies the stages in order in shared memory and writes
+// the tile back.
+constexpr int kColGroup = 8;
 template <typename T>
-__global__ void __launch_bounds__(kThreads) structured_stage_kernel(T* data, int s, size_t pairs, T m00, T m01, T m10,
-                                                                     T m11) {
-    const size_t half = size_t{1} << s;
-    for (size_t p = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; p < pairs;
-         p += static_cast<size_t>(gridDim.x) * kThreads) {
-        const size_t lo = ((p >> s) << (s + 1)) | (p & (half - 1));
-        stage_pair(data[lo], data[lo + half], m00, m01, m10, m11);
+__global__ void __launch_bounds__(kThreads) structured_column_kernel(T* data, int s0, int g, StructuredStages m) {
+    constexpr int kCols = 64 / static_cast<int>(sizeof(T));
+    extern __shared__ __align__(16) unsigned char raw[];
+    T* tile = reinterpret_cast<T*>(raw);  // [2^g rows][kCols]
+    const size_t tiles_per_block = (size_t{1} << s0) / kCols;
+    const size_t blk = blockIdx.x / tiles_per_block;
+    T* base = data + (blk << (s0 + g)) + (blockIdx.x % tiles_per_block) * kCols;
+    const int n = kCols << g;
+    for (int i = threadIdx.x; i < n; i += kThreads) tile[i] = base[(static_cast<size_t>(i / kCols) << s0) + i % kCols];
+    __syncthreads();
+    for (int k = 0; k < g; ++k) {
+        const int st = s0 + k;
+        const T m00 = Coef<T>::get(m, st, 0), m01 = Coef<T>::get(m, st, 1), m10 = Coef<T>::get(m, st, 2),
+                m11 = Coef<T>::get(m, st, 3);
+        const int half = 1 << k;
+        for (int p = threadIdx.x; p < n / 2; p += kThreads) {
+            const int c = p % kCols, q = p / kCols;
+            const int r = ((q >> k) << (k + 1)) | (q & (half - 1));
+            stage_pair(tile[r * kCols + c], tile[(r + half) * kCols + c], m00, m01, m10, m11);
+        }
+        __syncthreads();
     }
+    for (int i = threadIdx.x; i < n; i += kThreads) base[(static_cast<size_t>(i / kCols) << s0) + i % kCols] = tile[i];
 }
 
 template <typename T>
@@ -92,14 +111,16 @@ cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch
     structured_tile_kernel<T><<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(
         static_cast<const T*>(in), static_cast<T*>(out), tile_log, m);
     cudaError_t e = cudaGetLastError();
-    const std::size_t pairs = (batch << log_n) / 2;
-    std::size_t grid = (pairs + kThreads - 1) / kThreads;
-    if (grid > 148 * 32) grid = 148 * 32;
-    for (int s = tile_log; s < log_n && e == cudaSuccess; ++s) {
-        structured_stage_kernel<T><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(
-            static_cast<T*>(out), s, pairs, Coef<T>::get(m, s, 0), Coef<T>::get(m, s, 1), Coef<T>::get(m, s, 2),
-            Coef<T>::get(m, s, 3));
+    // higher stages in groups of up to kColGroup per in-place column pass
+    constexpr int kCols = 64 / static_cast<int>(sizeof(T));
+    for (int s0 = tile_log; s0 < log_n && e == cudaSuccess;) {
+        const int g = log_n - s0 < kColGroup ? log_n - s0 : kColGroup;
+        const std::size_t ctas = (batch << (log_n - s0 - g)) * ((std::size_t{1} << s0) / kCols);
+        if (ctas > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        structured_column_kernel<T><<<static_cast<unsigned>(ctas), kThreads, static_cast<int>(sizeof(T)) * (kCols << g),
+                                      stream>>>(static_cast<T*>(out), s0, g, m);
         e = cudaGetLastError();
+        s0 += g;
     }
     return e;
 }

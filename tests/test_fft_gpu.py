@@ -186,7 +186,7 @@ def test_c2r(lib, oracle, cuda, n, normalize):
 
 
 # ---- complex fp64 FFT (radix 2, bit-identical to reference_fft<Complex64>) -----------
-@pytest.mark.parametrize("n", [2, 64, 2048, 1 << 14])
+@pytest.mark.parametrize("n", [2, 64, 2048, 1 << 14, 1 << 20])
 @pytest.mark.parametrize("inverse, normalize", [(False, False), (True, True), (True, False)])
 def test_fft_fp64(lib, oracle, cuda, n, inverse, normalize):
     from gpu_util import run

@@ -20,7 +20,7 @@ def mats(log_n, seed):
     return [tuple(r) for r in w.rng(seed).uniform(-1.2, 1.2, size=(log_n, 4))]
 
 
-@pytest.mark.parametrize("log_n", [1, 5, 12, 16])
+@pytest.mark.parametrize("log_n", [1, 5, 12, 16, 21])
 @pytest.mark.parametrize("inverse", [False, True])
 def test_structured_fp32_per_stage(lib, oracle, cuda, log_n, inverse):
     from gpu_util import run

@@ -106,6 +106,12 @@ struct cubutterflyPlan {
     cubf::StructuredStages structured{};  // structured 2x2: per-stage matrices (inverted for an inverse plan)
     cubutterflyFftTransformType_t real_kind = CUBUTTERFLY_FFT_C2C;
     bool real_nd = false;  // rank-two / rank-three R2C / C2R: axes[0] rows, axes[1] outer axes
+    // FFT composites of packed tensors whose outer axes qualify as
+    // interleaved batches (`direct`): the innermost axis runs from the input
+    // into the output, every other axis in place there as `groups` blocks of
+    // interleaved transforms -- no gather, transposes or scatter.
+    bool direct = false;
+    std::size_t groups = 1;
     void* real_tw = nullptr;  // W_N^k, k = 0..N/2, complex fp32
     // Arbitrary-length FFT (Bluestein): axes[0] / axes[1] are the forward and
     // unnormalised inverse conv-point FFTs, in place on the work buffer at the
@@ -334,6 +340,16 @@ std::vector<std::size_t> packed_strides(const std::vector<std::size_t>& ext) {
 void launch_composite(const cubutterflyPlan& p, const void* in, void* out, cudaStream_t stream) {
     const auto& d = p.desc;
     unsigned char* ws = static_cast<unsigned char*>(p.workspace);
+    if (p.direct) {
+        const void* src = in;
+        for (const auto& ax : p.axes) {
+            auto& c = *ax.plan;
+            c.workspace = ws + ax.ws_offset;
+            launch_mapping(c, c.mapping, src, out, stream);
+            src = out;
+        }
+        return;
+    }
     if (p.flat) {
         auto& c = *p.axes.front().plan;
         c.workspace = ws + p.axes.front().ws_offset;
@@ -703,7 +719,7 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         // last pass lands in `out`; an in-place plan with an odd pass count
         // starts in a second workspace half.
         const std::size_t np = m.passes.size();
-        const std::size_t bytes = d.batch * n * 8;
+        const std::size_t bytes = d.batch * n * 8 * p.groups;
         unsigned char* ws = static_cast<unsigned char*>(core_ws);
         const bool in_place = in == out;
         const cubf::FftOuterTables outer{p.outer_lo, p.outer_hi, p.outer_split};
@@ -719,7 +735,7 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
             // interleaved batches run as one array of N * batch values
             const int lv = p.req.log_v;
             check_cuda(cubf::launch_fft_global_pass(ps.log_h, src, dst, p.req.log_n + lv, ps.log_inner + lv,
-                                                    lv ? 1 : d.batch, p.twiddles, outer, inverse && i == 0,
+                                                    lv ? p.groups : d.batch, p.twiddles, outer, inverse && i == 0,
                                                     inverse && last, last ? scale : 1.0f, stream, lv),
                        "FFT pass launch");
             src = dst;
@@ -1346,8 +1362,54 @@ std::unique_ptr<cubutterflyPlan> create_composite(cubutterflyHandle* handle, con
     for (auto e : d.extents) volume *= e;
     p->packed_bytes = align256(d.batch * volume * cubf::storage_bytes(d.storage));
     bool flat = false;
-    const auto specs = composite_axes(d, flat, skip_innermost);
+    auto specs = composite_axes(d, flat, skip_innermost);
     p->flat = flat;
+    // direct FFT composite: packed complex fp32 tensors, power-of-two axes,
+    // every outer axis an interleaved batch (n >= 16, n * inner >= 2^12)
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.storage == CUBUTTERFLY_DATA_COMPLEX_FP32 && !flat && !skip_innermost &&
+        d.input_strides == packed_strides(d.extents) && d.output_strides == packed_strides(d.extents) &&
+        d.input_batch_stride == volume && d.output_batch_stride == volume &&
+        std::all_of(d.extents.begin(), d.extents.end(), [](std::size_t e) { return cubf::is_pow2(e); }) &&
+        std::all_of(specs.begin(), specs.end(),
+                    [](const AxisSpec& a) {
+                        return a.inner == 1 ||
+                               (a.n >= 16 && a.n * a.inner >= 4096 && a.n * a.inner <= (std::size_t{1} << 30));
+                    })) {
+        p->direct = true;
+        std::size_t ws_bytes = 0;
+        std::ostringstream name;
+        name << "composite-direct[";
+        for (std::size_t i = 0; i < specs.size(); ++i) {
+            cubf::Descriptor c = specs[i].d;
+            if (specs[i].inner > 1) {  // interleaved: element stride = inner, transforms 1 apart
+                c.batch = specs[i].inner;
+                c.input_strides = c.output_strides = {specs[i].inner};
+                c.input_batch_stride = c.output_batch_stride = 1;
+            }
+            cubutterflyPlan::Axis ax;
+            ax.plan = create_rank1(handle, cubf::normalize(c));
+            if (specs[i].inner > 1) {
+                ax.plan->groups = specs[i].outer;
+                ax.plan->mapping.workspace_bytes *= specs[i].outer;
+            }
+            ax.n = specs[i].n;
+            ax.outer = specs[i].outer;
+            ax.inner = specs[i].inner;
+            ax.ws_offset = 0;
+            ws_bytes = std::max(ws_bytes, ax.plan->mapping.workspace_bytes);
+            name << (i ? "," : "") << "axis" << specs[i].axis << ":" << ax.plan->mapping.name();
+            p->axes.push_back(std::move(ax));
+        }
+        name << "]";
+        p->mapping.family = "composite";
+        p->mapping.label =
+            d.execution_mode == CUBUTTERFLY_EXECUTION_XD ? "xd[" + name.str() + "]" : name.str();
+        p->mapping.workspace_bytes = ws_bytes;
+        p->source = p->axes.front().plan->source;
+        p->reason = "rank-" + std::to_string(d.rank) +
+                    " FFT: the innermost axis from the input, every outer axis in place as interleaved batches";
+        return p;
+    }
     const bool two_buffers = d.op == CUBUTTERFLY_OPERATOR_FFT || d.op == CUBUTTERFLY_OPERATOR_NTT;
     std::size_t offset = flat ? 0 : p->packed_bytes * (two_buffers ? 2 : 1);
     std::ostringstream name, reason;

@@ -71,7 +71,7 @@ def test_fft_composite(lib, oracle, cuda, extents, batch, inverse):
                      inverse=inverse, normalize_inverse=True)
     got, name = run_nd(lib, t, x, cuda)
     want = along_axes(lambda r: oracle.fft_c32(r, inverse=inverse, normalize=True), x)
-    assert name.startswith("composite[")
+    assert name.startswith("composite")
     assert rel_l2(got, want) <= 2e-6, name
 
 
@@ -192,3 +192,21 @@ def test_reference_algorithm_name_runs_this_builds_mapping(lib, oracle, cuda, wo
     rev = [int(format(i, "03b")[::-1], 2) for i in range(8)]
     assert np.array_equal(outs[1], outs[0][:, rev])
     assert np.array_equal(outs[0].astype(np.uint64), oracle.ntt_cyclic(x.astype(np.uint64), q))
+
+
+@pytest.mark.parametrize("extents, batch, in_place", [([1024, 1024], 2, False), ([256, 64, 64], 2, False),
+                                                     ([64, 128], 3, True), ([16, 8192], 1, False)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_fft_composite_direct(lib, oracle, cuda, extents, batch, in_place, inverse):
+    """Packed power-of-two FFTs whose outer axes qualify as interleaved batches
+    run without gather, transposes or scatter: the innermost axis from the
+    input into the output, each outer axis in place as blocks of interleaved
+    transforms."""
+    vol = int(np.prod(extents))
+    x = w.fft_input(vol, batch, seed=vol + 5).reshape(batch, *extents)
+    t = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP32, extents=extents, batch=batch,
+                     inverse=inverse, normalize_inverse=True, in_place=in_place)
+    got, name = run_nd(lib, t, x, cuda)
+    assert name.startswith("composite-direct["), name
+    want = along_axes(lambda r: oracle.fft_c32(r, inverse=inverse, normalize=True), x)
+    assert rel_l2(got, want) <= 2e-6, name

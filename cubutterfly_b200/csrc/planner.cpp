@@ -297,8 +297,10 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
         const std::size_t cols = std::size_t{1} << (r.log_n + r.log_v - bits);
         if (cols % static_cast<std::size_t>(p.shape.units_per_cta) != 0)
             throw Unsupported("FFT pass of " + std::to_string(bits) + " bits needs more columns than this transform has");
-        // one CTA per SM at 1024 threads leaves the memory pipe less busy
-        const double eff = p.shape.threads >= 1024 ? 0.6 : 0.85;
+        // large radices run few, large CTAs whose load, exchange and store
+        // phases overlap poorly (measured: a radix-2^10 pass of 2^30 points
+        // takes 1.5x a radix-2^8 pass, radix-2^9 passes 1.3x)
+        const double eff = p.shape.threads >= 1024 ? 0.45 : (p.shape.threads >= 512 ? 0.6 : 0.85);
         m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, eff);
         m.passes.push_back(p);
         ns += bits;

@@ -23,36 +23,51 @@ __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
     return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
 }
 
+// Bin k of the half spectrum from Z[k] and conj Z[N/2 - k] (indices mod N/2).
+__device__ __forceinline__ float2 r2c_bin(float2 zk, float2 zm, float2 w, float scale) {
+    const float2 e = make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y - zm.y));
+    const float2 d = make_float2(0.5f * (zk.x - zm.x), 0.5f * (zk.y + zm.y));  // (Z[k] - conj Z[-k]) / 2
+    const float2 o = make_float2(d.y, -d.x);                                      // -i d
+    const float2 t = cmul(w, o);
+    return make_float2((e.x + t.x) * scale, (e.y + t.y) * scale);
+}
+
+// Bins k and N/2 - k read the same two values, so one thread makes both
+// (k = 0 .. N/4): every spectrum value is read once.
 __global__ void __launch_bounds__(kThreads) r2c_post_kernel(const float2* z, float2* x, const float2* tw, size_t half,
                                                             size_t batch, size_t out_bs, float scale) {
-    const size_t per = half + 1, total = per * batch;
+    const size_t per = half / 2 + 1, total = per * batch;
     for (size_t idx = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * kThreads) {
         const size_t b = idx / per, k = idx - b * per;
         const float2* zb = z + b * half;
-        const float2 zk = zb[k == half ? 0 : k];
-        const float2 zm = zb[k == 0 ? 0 : half - k];  // conj taken below
-        const float2 e = make_float2(0.5f * (zk.x + zm.x), 0.5f * (zk.y - zm.y));
-        const float2 d = make_float2(0.5f * (zk.x - zm.x), 0.5f * (zk.y + zm.y));  // (Z[k] - conj Z[-k]) / 2
-        const float2 o = make_float2(d.y, -d.x);                                      // -i d
-        const float2 t = cmul(tw[k], o);
-        x[b * out_bs + k] = make_float2((e.x + t.x) * scale, (e.y + t.y) * scale);
+        float2* xb = x + b * out_bs;
+        const float2 a = zb[k];
+        const float2 m = zb[k == 0 ? 0 : half - k];
+        xb[k] = r2c_bin(a, m, tw[k], scale);
+        if (half - k != k) xb[half - k] = r2c_bin(m, a, tw[half - k], scale);
     }
+}
+
+// z[k] from X[k] and conj X[N/2 - k]; z[k] and z[N/2 - k] share their reads.
+__device__ __forceinline__ float2 c2r_value(float2 xk, float2 xm, float2 w, float scale) {
+    const float2 e = make_float2(0.5f * (xk.x + xm.x), 0.5f * (xk.y - xm.y));
+    const float2 d = make_float2(0.5f * (xk.x - xm.x), 0.5f * (xk.y + xm.y));
+    const float2 o = cmul(make_float2(w.x, -w.y), d);  // W^-k d
+    return make_float2((e.x - o.y) * scale, (e.y + o.x) * scale);  // E + i O
 }
 
 __global__ void __launch_bounds__(kThreads) c2r_pre_kernel(const float2* x, float2* z, const float2* tw, size_t half,
                                                            size_t batch, size_t in_bs, float scale) {
-    const size_t total = half * batch;
+    const size_t per = half / 2 + 1, total = per * batch;
     for (size_t idx = static_cast<size_t>(blockIdx.x) * kThreads + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * kThreads) {
-        const size_t b = idx / half, k = idx - b * half;
+        const size_t b = idx / per, k = idx - b * per;
         const float2* xb = x + b * in_bs;
-        const float2 xk = xb[k], xm = xb[half - k];  // conj of xm taken below
-        const float2 e = make_float2(0.5f * (xk.x + xm.x), 0.5f * (xk.y - xm.y));
-        const float2 d = make_float2(0.5f * (xk.x - xm.x), 0.5f * (xk.y + xm.y));
-        const float2 w = tw[k];
-        const float2 o = cmul(make_float2(w.x, -w.y), d);  // W^-k d
-        z[idx] = make_float2((e.x - o.y) * scale, (e.y + o.x) * scale);  // E + i O
+        float2* zb = z + b * half;
+        const float2 xk = xb[k], xm = xb[half - k];  // conj of xm taken in c2r_value
+        zb[k] = c2r_value(xk, xm, tw[k], scale);
+        if (k != 0 && half - k != k) zb[half - k] = c2r_value(xm, xk, tw[half - k], scale);
     }
 }
 
@@ -66,7 +81,7 @@ unsigned grid_for(size_t work) {
 
 cudaError_t launch_r2c_post(const void* z, void* x, const void* twiddles, std::size_t half, std::size_t batch,
                             std::size_t out_batch_stride, float scale, cudaStream_t stream) {
-    r2c_post_kernel<<<grid_for((half + 1) * batch), kThreads, 0, stream>>>(
+    r2c_post_kernel<<<grid_for((half / 2 + 1) * batch), kThreads, 0, stream>>>(
         static_cast<const float2*>(z), static_cast<float2*>(x), static_cast<const float2*>(twiddles), half, batch,
         out_batch_stride, scale);
     return cudaGetLastError();
@@ -74,7 +89,7 @@ cudaError_t launch_r2c_post(const void* z, void* x, const void* twiddles, std::s
 
 cudaError_t launch_c2r_pre(const void* x, void* z, const void* twiddles, std::size_t half, std::size_t batch,
                            std::size_t in_batch_stride, float scale, cudaStream_t stream) {
-    c2r_pre_kernel<<<grid_for(half * batch), kThreads, 0, stream>>>(
+    c2r_pre_kernel<<<grid_for((half / 2 + 1) * batch), kThreads, 0, stream>>>(
         static_cast<const float2*>(x), static_cast<float2*>(z), static_cast<const float2*>(twiddles), half, batch,
         in_batch_stride, scale);
     return cudaGetLastError();

@@ -64,6 +64,65 @@ __global__ void __launch_bounds__(kThreads)
     for (size_t i = threadIdx.x; i < n; i += kThreads) dst[i] = tile[i];
 }
 
+// COUNT stages from FIRST on the 32 register values of a thread, stage
+// FIRST + i pairing registers whose index differs in bit REGBIT + i.
+template <typename T, int FIRST, int COUNT, int REGBIT>
+__device__ __forceinline__ void row_stages(T (&v)[32], const StructuredStages& m) {
+#pragma unroll
+    for (int i = 0; i < COUNT; ++i) {
+        const T m00 = Coef<T>::get(m, FIRST + i, 0), m01 = Coef<T>::get(m, FIRST + i, 1),
+                m10 = Coef<T>::get(m, FIRST + i, 2), m11 = Coef<T>::get(m, FIRST + i, 3);
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+            if (!(k & (1 << (REGBIT + i)))) stage_pair(v[k], v[k | (1 << (REGBIT + i))], m00, m01, m10, m11);
+    }
+}
+
+// Stages 0 .. 11 of 4096-element blocks, 128 threads per block, 32 values per
+// thread in registers: stages 0-4 on the thread's 32 consecutive values,
+// 5-9 and 10-11 after exchanges through shared memory (one word of padding
+// per 32 keeps every exchange access conflict free for 4-byte values), in the
+// reference's order with its roundings.
+template <typename T>
+__global__ void __launch_bounds__(128) structured_row4096_kernel(const T* in, T* out, StructuredStages m) {
+    __shared__ __align__(16) T tile[4096 + 128];
+    const int t = threadIdx.x;
+    const T* src = in + static_cast<size_t>(blockIdx.x) * 4096;
+    T* dst = out + static_cast<size_t>(blockIdx.x) * 4096;
+    auto at = [](int j) { return j + (j >> 5); };
+    T v[32];
+    // phase A: values t * 32 + e (bits 0-4)
+#pragma unroll
+    for (int q = 0; q < 32 * static_cast<int>(sizeof(T)) / 16; ++q) {
+        const uint4 w = reinterpret_cast<const uint4*>(src + t * 32)[q];
+        memcpy(&v[q * 16 / sizeof(T)], &w, 16);
+    }
+    row_stages<T, 0, 5, 0>(v, m);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) tile[at(t * 32 + e)] = v[e];
+    __syncthreads();
+    // phase B: thread (hi, lo) = index bits (10-11, 0-4); register k = bits 5-9
+    const int lo = t & 31, hi = t >> 5;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = tile[at((hi << 10) | (k << 5) | lo)];
+    row_stages<T, 5, 5, 0>(v, m);
+#pragma unroll
+    for (int k = 0; k < 32; ++k) tile[at((hi << 10) | (k << 5) | lo)] = v[k];
+    __syncthreads();
+    // phase C: thread t = index bits 3-9; register k = (bits 10-11) << 3 | bits 0-2
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = tile[at(((k >> 3) << 10) | (t << 3) | (k & 7))];
+    row_stages<T, 10, 2, 3>(v, m);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 8 * static_cast<int>(sizeof(T)) / 16; ++q) {
+            uint4 w;
+            memcpy(&w, &v[c * 8 + q * 16 / sizeof(T)], 16);
+            reinterpret_cast<uint4*>(dst + ((c << 10) | (t << 3)))[q] = w;
+        }
+}
+
 // Stages s0 .. s0 + g - 1 (s0 >= 12, g <= 8) in one in-place pass: a CTA
 // takes kCols adjacent columns (64-byte runs) of the 2^g rows 2^s0 apart that
 // those stages pair, applies the stages in order in shared memory and writes
@@ -96,12 +155,8 @@ __global__ void __launch_bounds__(kThreads) structured_column_kernel(T* data, in
 }
 
 template <typename T>
-cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch, const StructuredStages& m,
-                         cudaStream_t stream) {
-    const int tile_log = log_n < kTileLog ? log_n : kTileLog;
-    const std::size_t blocks = batch << (log_n - tile_log);
-    if (blocks == 0) return cudaSuccess;
-    if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+cudaError_t launch_tile(int tile_log, const void* in, void* out, std::size_t blocks, const StructuredStages& m,
+                        cudaStream_t stream) {
     const int smem = static_cast<int>(sizeof(T)) << tile_log;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(structured_tile_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -110,7 +165,24 @@ cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch
     }
     structured_tile_kernel<T><<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(
         static_cast<const T*>(in), static_cast<T*>(out), tile_log, m);
-    cudaError_t e = cudaGetLastError();
+    return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch, const StructuredStages& m,
+                         cudaStream_t stream) {
+    const int tile_log = log_n < kTileLog ? log_n : kTileLog;
+    const std::size_t blocks = batch << (log_n - tile_log);
+    if (blocks == 0) return cudaSuccess;
+    if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaSuccess;
+    if (tile_log == 12) {
+        structured_row4096_kernel<T><<<static_cast<unsigned>(blocks), 128, 0, stream>>>(static_cast<const T*>(in),
+                                                                                        static_cast<T*>(out), m);
+        e = cudaGetLastError();
+    } else {
+        e = launch_tile<T>(tile_log, in, out, blocks, m, stream);
+    }
     // higher stages in groups of up to kColGroup per in-place column pass
     constexpr int kCols = 64 / static_cast<int>(sizeof(T));
     for (int s0 = tile_log; s0 < log_n && e == cudaSuccess;) {

@@ -50,6 +50,63 @@ __global__ void __launch_bounds__(kThreads)
     for (size_t i = threadIdx.x; i < n; i += kThreads) block[i] = tile[i];
 }
 
+// COUNT stages from FIRST on a thread's 16 register values: stage FIRST + i
+// pairs registers whose index differs in bit REGBIT + i; `index(k)` is the
+// transform index of register k (for the pair's twiddle offset).
+template <int FIRST, int COUNT, int REGBIT, typename Index>
+__device__ __forceinline__ void row_stages(double2 (&v)[16], const double2* __restrict__ tw, int log_n,
+                                           double last_scale, Index index) {
+#pragma unroll
+    for (int i = 0; i < COUNT; ++i) {
+        const int st = FIRST + i;
+        const double scale = st + 1 == log_n ? last_scale : 1.0;
+        const size_t half = size_t{1} << st;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (!(k & (1 << (REGBIT + i)))) {
+                const size_t o = index(k) & (half - 1);
+                butterfly(v[k], v[k | (1 << (REGBIT + i))], __ldg(tw + (o << (log_n - 1 - st))), scale);
+            }
+    }
+}
+
+// Stages 0 .. 10 of 2048-point blocks (in place), 128 threads per block, 16
+// values per thread in registers: stages 0-3 on the thread's 16 consecutive
+// values, 4-7 and 8-10 after exchanges through shared memory (one value of
+// padding per 16), with the twiddles, order and roundings of the per-stage
+// form.
+__global__ void __launch_bounds__(128)
+    fft64_row2048_kernel(double2* data, const double2* __restrict__ tw, int log_n, double last_scale) {
+    __shared__ __align__(16) double2 tile[2048 + 128];
+    const int t = threadIdx.x;
+    double2* block = data + static_cast<size_t>(blockIdx.x) * 2048;
+    auto at = [](int j) { return j + (j >> 4); };
+    double2 v[16];
+    // phase A: values t * 16 + e (bits 0-3)
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = block[t * 16 + e];
+    row_stages<0, 4, 0>(v, tw, log_n, last_scale, [&](int k) { return static_cast<size_t>(t * 16 + k); });
+#pragma unroll
+    for (int e = 0; e < 16; ++e) tile[at(t * 16 + e)] = v[e];
+    __syncthreads();
+    // phase B: thread (hi, lo) = index bits (8-10, 0-3); register k = bits 4-7
+    const int lo = t & 15, hi = t >> 4;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = tile[at((hi << 8) | (k << 4) | lo)];
+    row_stages<4, 4, 0>(v, tw, log_n, last_scale,
+                        [&](int k) { return static_cast<size_t>((hi << 8) | (k << 4) | lo); });
+#pragma unroll
+    for (int k = 0; k < 16; ++k) tile[at((hi << 8) | (k << 4) | lo)] = v[k];
+    __syncthreads();
+    // phase C: thread t = index bits 1-7; register k = (bits 8-10) << 1 | bit 0
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = tile[at(((k >> 1) << 8) | (t << 1) | (k & 1))];
+    row_stages<8, 3, 1>(v, tw, log_n, last_scale,
+                        [&](int k) { return static_cast<size_t>(((k >> 1) << 8) | (t << 1) | (k & 1)); });
+#pragma unroll
+    for (int k = 0; k < 16; ++k) block[((k >> 1) << 8) | (t << 1) | (k & 1)] = v[k];
+}
+
 // Stages s0 .. s0 + g - 1 (s0 >= 11, g <= 8) in one in-place pass: a CTA
 // takes kCols adjacent columns (128-byte runs) of the 2^g rows 2^s0 apart
 // that those stages pair and applies them in order in shared memory, with the
@@ -95,8 +152,12 @@ cudaError_t launch_fft64(int log_n, const void* in, void* out, std::size_t batch
     const int tile_log = log_n < kTileLog ? log_n : kTileLog;
     const std::size_t blocks = batch << (log_n - tile_log);
     if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
-    const int smem = 16 << tile_log;
-    fft64_tile_kernel<<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(data, tw, log_n, tile_log, scale);
+    if (tile_log == 11) {
+        fft64_row2048_kernel<<<static_cast<unsigned>(blocks), 128, 0, stream>>>(data, tw, log_n, scale);
+    } else {
+        const int smem = 16 << tile_log;
+        fft64_tile_kernel<<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(data, tw, log_n, tile_log, scale);
+    }
     e = cudaGetLastError();
     for (int s0 = tile_log; s0 < log_n && e == cudaSuccess;) {
         const int g = log_n - s0 < kColGroup ? log_n - s0 : kColGroup;

@@ -554,10 +554,23 @@ void launch_mapping(const cubutterflyPlan& p, const cubf::Mapping& m, const void
     const int esz = static_cast<int>(cubf::storage_bytes(d.storage));
     const std::size_t n = d.extents[0];
     unsigned char* ws = static_cast<unsigned char*>(p.workspace);
-    check_cuda(cubf::launch_strided_copy(esz, in, d.input_strides[0], d.input_batch_stride, ws, 1, n, n, d.batch,
-                                         stream),
-               "layout gather launch");
-    launch_packed(p, m, ws, ws, ws + m.staged_bytes, stream);
+    // Out of place, a packed side needs no copy: the core reads the packed
+    // input or writes the packed output directly (every core also runs out of
+    // place, and its workspace was sized for the in-place form).
+    const bool packed_in = d.input_strides[0] == 1 && d.input_batch_stride == n;
+    const bool packed_out = d.output_strides[0] == 1 && d.output_batch_stride == n;
+    if (in != out && packed_in) {
+        launch_packed(p, m, in, ws, ws + m.staged_bytes, stream);
+    } else {
+        check_cuda(cubf::launch_strided_copy(esz, in, d.input_strides[0], d.input_batch_stride, ws, 1, n, n, d.batch,
+                                             stream),
+                   "layout gather launch");
+        if (in != out && packed_out) {
+            launch_packed(p, m, ws, out, ws + m.staged_bytes, stream);
+            return;
+        }
+        launch_packed(p, m, ws, ws, ws + m.staged_bytes, stream);
+    }
     check_cuda(cubf::launch_strided_copy(esz, ws, 1, n, out, d.output_strides[0], d.output_batch_stride, n, d.batch,
                                          stream),
                "layout scatter launch");

@@ -205,3 +205,45 @@ def test_reference_strided_embedding_fwht(lib, cuda):
         torch.cuda.synchronize()
         got = dout.cpu().numpy()
     assert np.abs(got[0::2] - expected).max() <= 1e-5
+
+
+@pytest.mark.parametrize("side", ["strided_in", "strided_out"])
+@pytest.mark.parametrize("op", ["fft", "fwht", "zeta", "ntt", "ntt_rev"])
+def test_one_packed_side_skips_its_copy(lib, oracle, cuda, side, op):
+    """Out of place with one packed side: the core reads the packed input (or
+    writes the packed output) directly; results and padding as with both
+    sides staged."""
+    n, batch = 4096, 3
+    strided = dict(input_strides=[2], input_batch_stride=2 * n + 1, output_strides=[1], output_batch_stride=n) \
+        if side == "strided_in" else \
+        dict(input_strides=[1], input_batch_stride=n, output_strides=[3], output_batch_stride=3 * n + 5)
+    q = 576460756061519873
+    if op == "fft":
+        t = cb.Transform(op=cb.Operator.FFT, extents=[n], batch=batch, **strided)
+        x = w.fft_input(n, batch, seed=41)
+        want, sentinel = oracle.fft_c32(x), np.complex64(5 - 5j)
+    elif op == "fwht":
+        t = cb.Transform(op=cb.Operator.FWHT, storage=cb.DataType.FP32, compute=cb.ComputeType.FP32, extents=[n],
+                         batch=batch, **strided)
+        x = w.rng(42).uniform(-1, 1, size=(batch, n)).astype(np.float32)
+        want, sentinel = oracle.fwht_f32(x, normalize=False), np.float32(-9)
+    elif op == "zeta":
+        t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[n], batch=batch, **strided)
+        x = w.zeta_input(12, batch, seed=43)
+        want, sentinel = oracle.zeta(x), np.uint32(0xCAFEBABE)
+    else:
+        orders = dict(output_orders=[cb.LogicalOrder.BIT_REVERSED]) if op == "ntt_rev" else {}
+        t = cb.Transform(op=cb.Operator.NTT, storage=cb.DataType.UINT64, extents=[n], batch=batch, modulus=q,
+                         **orders, **strided)
+        x = w.rng(44).integers(0, q, size=(batch, n), dtype=np.uint64)
+        want, sentinel = oracle.ntt_cyclic(x, q), np.uint64(31337)
+        if op == "ntt_rev":
+            want = want[:, [int(format(i, "012b")[::-1], 2) for i in range(n)]]
+    got, raw, idx = run_layout(lib, t, x, sentinel, cuda)
+    if op == "fft":
+        assert rel_l2(got, want) <= 2e-6
+    elif op == "fwht":
+        assert rel_l2(got, want) <= 1e-6
+    else:
+        assert np.array_equal(got, want)
+    assert padding_untouched(raw, idx, sentinel)

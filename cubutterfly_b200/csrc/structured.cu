@@ -154,6 +154,44 @@ __global__ void __launch_bounds__(kThreads) structured_column_kernel(T* data, in
     for (int i = threadIdx.x; i < n; i += kThreads) base[(static_cast<size_t>(i / kCols) << s0) + i % kCols] = tile[i];
 }
 
+// Eight stages s0 .. s0 + 7 (s0 >= 12) in one in-place pass with the values
+// in registers: a CTA of 16 x kCols threads takes kCols adjacent columns
+// (64-byte runs) of the 256 rows 2^s0 apart; thread (group g, column c) holds
+// rows 16 g + i (stages s0 .. s0 + 3 in registers), then, after one exchange
+// through padded shared memory, rows 16 i + g (stages s0 + 4 .. s0 + 7).
+template <typename T>
+__global__ void __launch_bounds__(16 * (64 / sizeof(T))) structured_column8_kernel(T* data, int s0, StructuredStages m) {
+    constexpr int kCols = 64 / static_cast<int>(sizeof(T));
+    __shared__ T tile[256 * (kCols + 1)];
+    const size_t tiles_per_block = (size_t{1} << s0) / kCols;
+    const size_t blk = blockIdx.x / tiles_per_block;
+    T* base = data + (blk << (s0 + 8)) + (blockIdx.x % tiles_per_block) * kCols;
+    const int c = threadIdx.x % kCols, g = threadIdx.x / kCols;
+    T v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = base[(static_cast<size_t>(16 * g + i) << s0) + c];
+    auto stages = [&](int first) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int st = first + b;
+            const T m00 = Coef<T>::get(m, st, 0), m01 = Coef<T>::get(m, st, 1), m10 = Coef<T>::get(m, st, 2),
+                    m11 = Coef<T>::get(m, st, 3);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (!(i & (1 << b))) stage_pair(v[i], v[i | (1 << b)], m00, m01, m10, m11);
+        }
+    };
+    stages(s0);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tile[(16 * g + i) * (kCols + 1) + c] = v[i];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = tile[(16 * i + g) * (kCols + 1) + c];
+    stages(s0 + 4);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) base[(static_cast<size_t>(16 * i + g) << s0) + c] = v[i];
+}
+
 template <typename T>
 cudaError_t launch_tile(int tile_log, const void* in, void* out, std::size_t blocks, const StructuredStages& m,
                         cudaStream_t stream) {
@@ -189,6 +227,13 @@ cudaError_t launch_typed(int log_n, const void* in, void* out, std::size_t batch
         const int g = log_n - s0 < kColGroup ? log_n - s0 : kColGroup;
         const std::size_t ctas = (batch << (log_n - s0 - g)) * ((std::size_t{1} << s0) / kCols);
         if (ctas > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        if (g == kColGroup) {
+            structured_column8_kernel<T><<<static_cast<unsigned>(ctas), 16 * kCols, 0, stream>>>(static_cast<T*>(out),
+                                                                                               s0, m);
+            e = cudaGetLastError();
+            s0 += g;
+            continue;
+        }
         structured_column_kernel<T><<<static_cast<unsigned>(ctas), kThreads, static_cast<int>(sizeof(T)) * (kCols << g),
                                       stream>>>(static_cast<T*>(out), s0, g, m);
         e = cudaGetLastError();

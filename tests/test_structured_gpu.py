@@ -72,3 +72,17 @@ def test_fwht_fp64_runs_as_structured(lib, oracle, cuda, inverse, normalize):
     got, name = run(lib, t, x, cuda)
     assert name.startswith("fwht-f64:structured-2x2")
     assert np.array_equal(got, oracle.fwht_f64(x, inverse=inverse, normalize=normalize))
+
+
+@pytest.mark.parametrize("log_n", [20, 22])
+def test_structured_fp64_per_stage_long_rows(lib, oracle, cuda, log_n):
+    """FP64 rows long enough for the eight-stage register column pass (and a
+    shorter tail pass), bit-identical to the oracle."""
+    from gpu_util import run
+
+    n = 1 << log_n
+    x = w.rng(log_n).uniform(-1, 1, size=(2, n))
+    m = mats(log_n, 200 + log_n)
+    for inverse in (False, True):
+        got, name = run(lib, structured(n, 2, [m], storage=cb.DataType.FP64, inverse=inverse), x, cuda)
+        assert np.array_equal(got, oracle.structured(x, m, inverse)), name

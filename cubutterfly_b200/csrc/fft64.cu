@@ -113,6 +113,48 @@ __global__ void __launch_bounds__(128)
 // per-stage twiddles and arithmetic of the single-stage form.
 constexpr int kColGroup = 8;
 constexpr int kCols = 8;
+// Eight stages s0 .. s0 + 7 (s0 >= 11) in one in-place pass with the values
+// in registers: 128 threads take kCols adjacent columns of the 256 rows 2^s0
+// apart; thread (group g, column c) holds rows 16 g + i for stages s0 ..
+// s0 + 3 and, after one exchange through padded shared memory, rows 16 i + g
+// for stages s0 + 4 .. s0 + 7, with the twiddles of the per-stage form.
+__global__ void __launch_bounds__(128)
+    fft64_column8_kernel(double2* data, const double2* __restrict__ tw, int log_n, int s0, double last_scale) {
+    __shared__ __align__(16) double2 tile[256 * (kCols + 1)];
+    const size_t tiles_per_block = (size_t{1} << s0) / kCols;
+    const size_t blk = blockIdx.x / tiles_per_block;
+    const size_t col = (blockIdx.x % tiles_per_block) * kCols + threadIdx.x % kCols;
+    double2* base = data + (blk << (s0 + 8)) + col;
+    const int g = threadIdx.x / kCols, c = threadIdx.x % kCols;
+    double2 v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = base[static_cast<size_t>(16 * g + i) << s0];
+    // row(i): the row of register i; stage s0 + first + b pairs registers differing in bit b
+    auto stages = [&](int first, auto row) {
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int st = s0 + first + b;
+            const double scale = st + 1 == log_n ? last_scale : 1.0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (!(i & (1 << b))) {
+                    const size_t r = static_cast<size_t>(row(i));
+                    const size_t o = ((r & ((size_t{1} << (first + b)) - 1)) << s0) | col;
+                    butterfly(v[i], v[i | (1 << b)], __ldg(tw + (o << (log_n - 1 - st))), scale);
+                }
+        }
+    };
+    stages(0, [&](int i) { return 16 * g + i; });
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tile[(16 * g + i) * (kCols + 1) + c] = v[i];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = tile[(16 * i + g) * (kCols + 1) + c];
+    stages(4, [&](int i) { return 16 * i + g; });
+#pragma unroll
+    for (int i = 0; i < 16; ++i) base[static_cast<size_t>(16 * i + g) << s0] = v[i];
+}
+
 __global__ void __launch_bounds__(kThreads)
     fft64_column_kernel(double2* data, const double2* __restrict__ tw, int log_n, int s0, int g, double last_scale) {
     extern __shared__ __align__(16) unsigned char raw[];
@@ -163,6 +205,12 @@ cudaError_t launch_fft64(int log_n, const void* in, void* out, std::size_t batch
         const int g = log_n - s0 < kColGroup ? log_n - s0 : kColGroup;
         const std::size_t ctas = (batch << (log_n - s0 - g)) * ((std::size_t{1} << s0) / kCols);
         if (ctas > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        if (g == kColGroup) {
+            fft64_column8_kernel<<<static_cast<unsigned>(ctas), 128, 0, stream>>>(data, tw, log_n, s0, scale);
+            e = cudaGetLastError();
+            s0 += g;
+            continue;
+        }
         fft64_column_kernel<<<static_cast<unsigned>(ctas), kThreads, 16 * (kCols << g), stream>>>(data, tw, log_n, s0,
                                                                                                 g, scale);
         e = cudaGetLastError();

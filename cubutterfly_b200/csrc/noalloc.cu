@@ -10,9 +10,10 @@
 // that loads this library holds until the process exits.
 //
 // Set-up: the first call on a device (with that device current) resolves the
-// arrays' device addresses with cudaGetSymbolAddress and uploads the twiddle
-// tables once; make that first call before any stream capture.  Calls after it
-// issue kernel launches only.  All calls share one scratch array and it keeps
+// arrays' device addresses with cudaGetSymbolAddress, uploads the twiddle
+// tables once and waits for that upload to land (so the first call's kernels
+// read complete tables on any stream, blocking or not); make that first call
+// before any stream capture.  Calls after it issue kernel launches only.  All calls share one scratch array and it keeps
 // the previous call's contents; nothing in it needs to start at zero (every
 // scratch word is written by a pass before any pass reads it).  Calls whose
 // execution overlaps on the GPU (different streams, or other host threads)
@@ -33,8 +34,10 @@
 namespace {
 
 // Largest scratch this entry point offers: 16 MiB, i.e. n * batch <= 2^21
-// complex values (half that for an in-place transform with an odd number of
-// passes, n = 2^21, which ping-pongs through two scratch halves).
+// complex values.  Passes alternate between the scratch and the output so the
+// last one lands in the output; an in-place transform therefore needs an even
+// pass count (n <= 2^20, two passes of at most 2^10), and n = 2^21 (three
+// passes) runs out of place only.
 constexpr std::size_t kScratchBytes = std::size_t{16} << 20;
 constexpr int kMinLog = 14;  // below this the single-kernel FFT needs no scratch
 constexpr int kMaxLog = 21;
@@ -127,6 +130,9 @@ const DeviceSlots& device_setup() {
     s.tw1024 = static_cast<float2*>(p);
     check(cudaMemcpyToSymbol(g_fft_outer, h_outer, sizeof(h_outer)), "twiddle upload");
     check(cudaMemcpyToSymbol(g_fft_tw1024, h_tw1024, sizeof(h_tw1024)), "twiddle upload");
+    // A pageable-source copy may return before its DMA lands, and kernels on a
+    // non-blocking stream do not wait for the legacy stream it ran on.
+    check(cudaStreamSynchronize(cudaStreamLegacy), "twiddle upload wait");
     s.ready = true;
     return s;
 }
@@ -159,14 +165,25 @@ extern "C" cubutterflyStatus_t cubutterflyB200FftC2CNoAlloc(const void* input, v
         if (batch == 0) throw Failure(CUBUTTERFLY_STATUS_INVALID_VALUE, "batch must be positive");
         const int np = (l + cubf::kFftPassMaxLog - 1) / cubf::kFftPassMaxLog;
         const bool in_place = input == output;
-        const bool two_halves = in_place && np % 2 == 1;
-        const std::size_t bytes = n * 8;
-        if (batch > kScratchBytes / (bytes * (two_halves ? 2 : 1)))
+        if (in_place && np % 2 == 1)
             throw Failure(CUBUTTERFLY_STATUS_INVALID_VALUE,
-                          "n * batch exceeds the 16 MiB allocation-free scratch (2^21 complex values; 2^20 for "
-                          "in-place 2^21-point transforms)");
-        const DeviceSlots& s = device_setup();
+                          "in-place allocation-free FFTs go up to 2^20 points; run 2^21 points out of place");
+        const std::size_t bytes = n * 8;
+        if (batch > kScratchBytes / bytes)
+            throw Failure(CUBUTTERFLY_STATUS_INVALID_VALUE,
+                          "n * batch exceeds the 16 MiB allocation-free scratch (2^21 complex values)");
         const std::size_t total = bytes * batch;
+        {
+            // pass 0 writes while it reads: partly overlapping buffers would
+            // corrupt the input before every element of it is read
+            const auto a = reinterpret_cast<std::uintptr_t>(input);
+            const auto b = reinterpret_cast<std::uintptr_t>(output);
+            if (!in_place && a < b + total && b < a + total)
+                throw Failure(CUBUTTERFLY_STATUS_INVALID_VALUE,
+                              "input and output overlap: pass the same pointer for an in-place transform or "
+                              "disjoint buffers");
+        }
+        const DeviceSlots& s = device_setup();
         const cubf::FftOuterTables outer{s.outer + offset_of(l), s.outer + offset_of(l) + (1 << split_of(l)),
                                          split_of(l)};
         const float scale = (inverse && normalize) ? 1.0f / static_cast<float>(n) : 1.0f;
@@ -176,11 +193,7 @@ extern "C" cubutterflyStatus_t cubutterflyB200FftC2CNoAlloc(const void* input, v
         int ns = 0;
         for (int i = 0; i < np; ++i) {
             const int log_r = l / np + (i < l % np ? 1 : 0);
-            void* dst;
-            if ((np - 1 - i) % 2 == 0)
-                dst = (in_place && i == 0) ? static_cast<void*>(s.scratch + total) : output;
-            else
-                dst = s.scratch;
+            void* dst = (np - 1 - i) % 2 == 0 ? output : static_cast<void*>(s.scratch);
             const bool last = i + 1 == np;
             check(cubf::launch_fft_global_pass(log_r, src, dst, l, ns, batch, s.tw1024, outer, inverse && i == 0,
                                                inverse && last, last ? scale : 1.0f, stream),

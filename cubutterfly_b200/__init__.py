@@ -1,26 +1,36 @@
-"""ctypes frontend of cubutterfly_b200 (mirrors the reference's python/cubutterfly).
+"""Python frontend of libcubutterfly_b200.so (B200 planner + sm_100a kernels).
 
-The names, enum values, dataclasses and call protocol match the reference's
-Python package (python/cubutterfly/__init__.py:32-450) so that code written
-against it runs unchanged: ``Library(path)``, ``Transform``, ``PlanOptions``,
-``Descriptor``, ``Plan(library, transform).execute(in_ptr, out_ptr)``.  The
-library behind it is libcubutterfly_b200.so (B200 planner + sm_100a kernels).
+Public names, enum values and the call protocol are those of the reference's
+Python package (python/cubutterfly/__init__.py: ``Library``, ``Transform``,
+``PlanOptions``, ``Descriptor``, ``Plan``, ``Error`` and the enums), so code
+written against it runs unchanged: ``Plan(Library(), Transform(...))`` then
+``plan.execute(in_ptr, out_ptr)``.
 
-``Library()`` with no argument loads the in-tree build; it fails loudly when
-the shared library is missing -- there is no CPU fallback.  Importing this
-package loads nothing.  Workspace is caller-allocated and bound with
-``Plan.set_workspace``; inputs, outputs, workspace and stream must outlive the
-asynchronous execution.
+How it is put together:
+
+* ``_ABI`` is the one table of every C entry point this frontend binds (the
+  reference ABI and the ``cubutterflyB200*`` extensions); ``Library`` binds it
+  once at load time.
+* A ``Transform`` (plus ``PlanOptions``) is first checked and normalised into a
+  flat ``_Request`` by ``_request``; ``_SETTERS`` then lists, as data, the
+  descriptor setters that configure it and the ``_Request`` fields each takes.
+
+``Library()`` without a path loads ``$CUBUTTERFLY_LIBRARY`` or the in-tree
+build and raises when neither exists: there is no CPU fallback.  Importing the
+package loads nothing.  Execution is asynchronous; inputs, outputs, workspace
+and stream must stay alive until it completes.
 """
 from __future__ import annotations
 
 import ctypes as ct
 import json as _json
-import operator
 import os
 from dataclasses import dataclass, field
 from enum import IntEnum
 from pathlib import Path
+from types import SimpleNamespace
+
+from . import _abi
 
 __all__ = [
     "Operator", "DataType", "ComputeType", "LogicalOrder", "NttLayout", "ExecutionMode", "AlgorithmPolicy",
@@ -33,9 +43,11 @@ DEFAULT_LIBRARY = _PKG / "lib" / "libcubutterfly_b200.so"
 
 
 def default_library_path() -> Path:
-    return Path(os.environ.get("CUBUTTERFLY_LIBRARY", DEFAULT_LIBRARY))
+    """$CUBUTTERFLY_LIBRARY when set, else the in-tree build."""
+    return Path(os.environ.get("CUBUTTERFLY_LIBRARY") or DEFAULT_LIBRARY)
 
 
+# ---- enums: integer values fixed by include/cubutterfly/cubutterfly.h --------------------------
 class Operator(IntEnum):
     FFT = 0
     NTT = 1
@@ -130,12 +142,13 @@ class Status(IntEnum):
     INTERNAL_ERROR = 7
 
 
-DEFAULT_MODULUS = 1152921504606584833
+DEFAULT_MODULUS = 1152921504606584833  # cuntt::kDefaultModulus
 
 
+# ---- request records (field names and defaults are the reference's) ---------------------------
 @dataclass
 class Transform:
-    """One batched transform request (field meanings as the reference's Transform)."""
+    """One batched transform request."""
     op: int = Operator.FFT
     storage: int = DataType.COMPLEX_FP32
     compute: int = ComputeType.NATIVE
@@ -166,241 +179,277 @@ class Transform:
 
 @dataclass
 class PlanOptions:
+    """Mapping selection: a policy, or an explicit mapping / algorithm name."""
     policy: int = AlgorithmPolicy.DEFAULT
     mapping: str = ""
     execution_mode: int = ExecutionMode.AUTO
 
 
 class Error(RuntimeError):
+    """A failed ABI call; `status` is the cubutterflyStatus_t value (None for frontend errors)."""
+
     def __init__(self, message, status=None):
         super().__init__(message)
         self.status = status
 
 
 class _Matrix(ct.Structure):
-    _fields_ = [(name, ct.c_double) for name in ("m00", "m01", "m10", "m11")]
+    """cubutterflyMatrix2x2_t: [[m00, m01], [m10, m11]] applied to (left, right)."""
+    _fields_ = [("m00", ct.c_double), ("m01", ct.c_double), ("m10", ct.c_double), ("m11", ct.c_double)]
 
 
-_STRING_QUERIES = ("DescriptorGetJson", "DescriptorGetCapabilities", "PlanGetMappingJson", "PlanGetDescriptorJson",
-                   "PlanGetAlgorithmName", "PlanGetSelectionReason")
-_SIZE_QUERIES = ("PlanGetWorkspaceSize", "PlanGetInputSize", "PlanGetOutputSize")
+# ---- the C ABI ---------------------------------------------------------------------------------
+# suffix of cubutterfly<suffix>, then argument codes (_abi.ARG; "m": matrix array)
+_ABI = """
+GetStatusString            i
+GetLastErrorString
+GetVersion                 I I I
+Create                     P
+Destroy                    p
+SetStream                  p p
+GetStream                  p P
+SetCachePath               p s
+CreateDescriptor           P
+DestroyDescriptor          p
+SetOperator                p i
+SetDataType                p i i
+SetShape                   p u Z z
+SetExecutionMode           p i
+SetFftTransformType        p i
+SetFftOutputScale          p d
+SetOutputScale             p d
+SetArithmeticPolicy        p i
+SetOutputRounding          p i
+SetStrides                 p Z z Z z
+SetLogicalOrders           p I I
+SetDirection               p i i
+SetPlacement               p i
+SetLengthMode              p i
+SetAlgorithmPolicy         p i s
+SetModulus                 p q u
+SetNttLayouts              p i i
+SetStageMatrices           p u m z
+DescriptorValidate         p
+DescriptorGetJson          p p Z
+DescriptorSetJson          p s
+DescriptorGetCapabilities  p p Z
+CreatePlan                 p p P
+DestroyPlan                p
+PlanGetDescriptorJson      p p Z
+PlanGetWorkspaceSize       p Z
+PlanGetInputSize           p Z
+PlanGetOutputSize          p Z
+PlanGetPhysicalExtents     p Z u
+PlanGetSelectionSource     p I
+PlanGetAlgorithmName       p p Z
+PlanGetSelectionReason     p p Z
+PlanGetMappingJson         p p Z
+PlanSetWorkspace           p p z
+Execute                    p p p p
+ExecuteSteady              p p p p
+# extensions of this build (include/cubutterfly/cubutterfly_b200.h)
+B200RankMappings           p s p Z
+B200PlanGetDeviceStatus    p U
+B200PlanInjectDeviceStatus p w
+B200FourStepTwiddle        p z z z z z i p
+B200PermuteBlocksC64       p p p p z z z z p
+B200TransposeC64           p p z z z p
+B200FftC2CNoAlloc          p p z z i i p
+"""
 
 
 class Library:
-    """The loaded C ABI.  Every bound symbol is resolved once at load time."""
+    """libcubutterfly_b200.so with every entry point of `_ABI` bound."""
 
     def __init__(self, path=None):
         path = Path(path) if path else default_library_path()
-        if not path.exists():
+        if not path.is_file():
             raise FileNotFoundError(
-                f"{path} is missing: build it with `python -m cubutterfly_b200._build` (no CPU fallback exists)")
+                f"no cuButterfly library at {path}; build it with `python -m cubutterfly_b200._build` "
+                "(this frontend has no CPU fallback)")
         self.path = path
         self._dll = ct.CDLL(os.fspath(path))
-        p, n, i = ct.c_void_p, ct.c_size_t, ct.c_int
-        pn, pi = ct.POINTER(n), ct.POINTER(i)
-        sig = {
-            "GetStatusString": [i], "GetLastErrorString": [],
-            "GetVersion": [pi, pi, pi],
-            "CreateDescriptor": [ct.POINTER(p)], "DestroyDescriptor": [p],
-            "SetOperator": [p, i], "SetDataType": [p, i, i],
-            "SetShape": [p, ct.c_uint32, pn, n], "SetExecutionMode": [p, i],
-            "SetFftTransformType": [p, i], "SetFftOutputScale": [p, ct.c_double],
-            "SetOutputScale": [p, ct.c_double],
-            "SetOutputRounding": [p, i], "SetArithmeticPolicy": [p, i],
-            "SetStrides": [p, pn, n, pn, n], "SetLogicalOrders": [p, pi, pi],
-            "SetDirection": [p, i, i], "SetPlacement": [p, i], "SetLengthMode": [p, i],
-            "SetAlgorithmPolicy": [p, i, ct.c_char_p],
-            "SetModulus": [p, ct.c_uint64, ct.c_uint32], "SetNttLayouts": [p, i, i],
-            "SetStageMatrices": [p, ct.c_uint32, ct.POINTER(_Matrix), n],
-            "DescriptorValidate": [p], "DescriptorSetJson": [p, ct.c_char_p],
-            "Create": [ct.POINTER(p)], "Destroy": [p], "SetStream": [p, p], "GetStream": [p, ct.POINTER(p)],
-            "SetCachePath": [p, ct.c_char_p],
-            "CreatePlan": [p, p, ct.POINTER(p)], "DestroyPlan": [p],
-            "PlanSetWorkspace": [p, p, n], "Execute": [p, p, p, p],
-            "ExecuteSteady": [p, p, p, p],
-            "PlanGetSelectionSource": [p, pi],
-            "PlanGetPhysicalExtents": [p, pn, ct.c_uint32],
-            "B200RankMappings": [p, ct.c_char_p, ct.c_void_p, pn],
-        }
-        for name in _STRING_QUERIES:
-            sig[name] = [p, ct.c_void_p, pn]
-        for name in _SIZE_QUERIES:
-            sig[name] = [p, pn]
-        self._functions = {}
-        for name, args in sig.items():
-            fn = getattr(self._dll, "cubutterfly" + name, None)
-            if fn is None:
-                raise AttributeError("library is missing cubutterfly" + name)
-            fn.argtypes = args
-            fn.restype = ct.c_char_p if name in ("GetStatusString", "GetLastErrorString") else i
-            self._functions[name] = fn
+        self.fn = _abi.bind(self._dll, "cubutterfly", _ABI, text=("GetStatusString", "GetLastErrorString"),
+                            extra={"m": ct.POINTER(_Matrix)})
 
-    def _call(self, name, *args):
-        status = self._functions[name](*args)
-        if status:
-            detail = (self._dll.cubutterflyGetLastErrorString() or b"").decode("utf-8", errors="replace")
-            summary = self._functions["GetStatusString"](status).decode("utf-8", errors="replace")
-            raise Error(summary + (": " + detail if detail else ""), status)
+    def invoke(self, name, *args):
+        """Call cubutterfly<name>; a nonzero status raises Error(status text: last error text)."""
+        status = self.fn[name](*args)
+        if status != Status.SUCCESS:
+            raise Error(self.describe(status), status)
 
-    def _query(self, name, handle):
-        size = ct.c_size_t()
-        self._call(name, handle, None, ct.byref(size))
-        buf = ct.create_string_buffer(size.value)
-        self._call(name, handle, buf, ct.byref(size))
-        return buf.value.decode("utf-8")
+    def describe(self, status) -> str:
+        text = (self.fn["GetStatusString"](int(status)) or b"").decode("utf-8", "replace")
+        detail = (self.fn["GetLastErrorString"]() or b"").decode("utf-8", "replace")
+        return f"{text}: {detail}" if detail else text
+
+    def text(self, name, handle) -> str:
+        """A two-call string query of `handle`."""
+        return _abi.two_call_text(lambda *a: self.invoke(name, *a), handle)
 
     def version(self):
-        a, b, c = ct.c_int(), ct.c_int(), ct.c_int()
-        self._call("GetVersion", ct.byref(a), ct.byref(b), ct.byref(c))
-        return a.value, b.value, c.value
+        v = [ct.c_int() for _ in range(3)]
+        self.invoke("GetVersion", *(ct.byref(x) for x in v))
+        return tuple(x.value for x in v)
 
 
-_LIBRARY = None
+_SHARED = {}
 
 
 def load(path=None) -> Library:
-    """Process-wide Library of the in-tree build (or `path`)."""
-    global _LIBRARY
-    if path is not None:
-        return Library(path)
-    if _LIBRARY is None:
-        _LIBRARY = Library()
-    return _LIBRARY
+    """A process-wide Library of `path` (default: the in-tree build)."""
+    key = os.fspath(path) if path is not None else None
+    if key not in _SHARED:
+        _SHARED[key] = Library(path)
+    return _SHARED[key]
 
 
-def _array(kind, values):
-    return (kind * len(values))(*values) if values else None
+# ---- Transform -> descriptor -----------------------------------------------------------------
+_ENUM_FIELDS = ("op", "storage", "compute", "fft_type", "output_rounding", "arithmetic_policy", "length_mode",
+                "input_order", "output_order", "execution_mode")
+_SCALE_FIELDS = ("fft_output_scale", "output_scale")
+_PER_AXIS = ("input_strides", "output_strides", "input_orders", "output_orders")
 
 
-def _integer(value, name, kind):
-    if isinstance(value, bool):
-        raise TypeError(f"{name} must be an integer, not bool")
-    try:
-        result = operator.index(value)
-    except TypeError as exc:
-        raise TypeError(f"{name} must be an integer") from exc
-    bits = ct.sizeof(kind) * 8
-    maximum = (1 << (bits - 1)) - 1 if kind is ct.c_int else (1 << bits) - 1
-    if result < 0 or result > maximum:
-        raise ValueError(f"{name} is outside the {kind.__name__} ABI range")
-    return result
+def _request(t: Transform, o: PlanOptions) -> SimpleNamespace:
+    """Check a Transform + PlanOptions and flatten them into setter arguments."""
+    r = SimpleNamespace()
+    for flag in ("inverse", "normalize_inverse", "in_place"):
+        if not isinstance(getattr(t, flag), bool):
+            raise TypeError(f"Transform.{flag} takes True or False, got {getattr(t, flag)!r}")
+    for name in _ENUM_FIELDS:
+        setattr(r, name, _abi.unsigned(getattr(t, name), f"Transform.{name}", ct.c_int))
+    for name in _SCALE_FIELDS:
+        setattr(r, name, float(getattr(t, name)))
+    for flag in ("inverse", "normalize_inverse", "in_place"):
+        setattr(r, flag, getattr(t, flag))
+    r.rank = _abi.unsigned(len(t.extents), "number of extents", ct.c_uint32)
+    r.extents = [_abi.unsigned(e, "Transform.extents", ct.c_size_t) for e in t.extents]
+    r.batch = _abi.unsigned(t.batch, "Transform.batch", ct.c_size_t)
+    for name in _PER_AXIS:
+        values = list(getattr(t, name))
+        if values and len(values) != r.rank:
+            raise ValueError(f"Transform.{name} has {len(values)} entries for {r.rank} axes (one per axis, or none)")
+        kind = ct.c_size_t if name.endswith("strides") else ct.c_int
+        setattr(r, name, [_abi.unsigned(v, f"Transform.{name}", kind) for v in values])
+    r.input_batch_stride = _abi.unsigned(t.input_batch_stride, "Transform.input_batch_stride")
+    r.output_batch_stride = _abi.unsigned(t.output_batch_stride, "Transform.output_batch_stride")
+    r.modulus = _abi.unsigned(t.modulus, "Transform.modulus", ct.c_uint64)
+    r.word_bits = _abi.unsigned(t.word_bits, "Transform.word_bits", ct.c_uint32)
+    r.ntt = r.op == Operator.NTT
+    # the legacy rank-one NTT layouts and per-axis logical orders are two ways
+    # of saying the same thing: a request may use one of them
+    r.legacy_layouts = (r.input_order, r.output_order) != (NttLayout.NATURAL, NttLayout.NATURAL)
+    if r.legacy_layouts and not r.ntt:
+        raise ValueError("input_order / output_order (NTT layouts) apply to NTT transforms only; "
+                         "use input_orders / output_orders")
+    if r.legacy_layouts and (r.input_orders or r.output_orders):
+        raise ValueError("give either NTT layouts (input_order / output_order) or logical orders "
+                         "(input_orders / output_orders), not both")
+    if not r.ntt and (r.modulus, r.word_bits) != (DEFAULT_MODULUS, 64):
+        raise ValueError(f"modulus / word_bits are NTT parameters; {Operator(r.op).name if r.op in set(Operator) else r.op} "
+                         "transforms take the defaults")
+    r.matrices = []
+    for axis, stages in enumerate(t.stage_matrices):
+        _abi.unsigned(axis, "stage matrix axis", ct.c_uint32)
+        if stages:
+            r.matrices.append((axis, [_Matrix(*m) for m in stages]))
+    r.policy = _abi.unsigned(o.policy, "PlanOptions.policy", ct.c_int)
+    r.mapping = o.mapping.encode("utf-8")
+    if r.mapping:
+        r.policy = AlgorithmPolicy.EXPLICIT
+    r.mode = _abi.unsigned(o.execution_mode, "PlanOptions.execution_mode", ct.c_int) or r.execution_mode
+    return r
 
 
-def _pointer(value):
-    if hasattr(value, "data_ptr"):
-        value = value.data_ptr()
-    return value if isinstance(value, ct.c_void_p) else ct.c_void_p(value)
+def _arr(kind, values):
+    return _abi.c_array(kind, values)
+
+
+# Descriptor setters in call order, each with a predicate (None: always) and
+# the arguments it takes from a _Request.  SetShape clears strides, orders and
+# stage matrices, so everything per-axis follows it.
+_SETTERS = (
+    ("SetOperator", None, lambda r: (r.op,)),
+    ("SetShape", None, lambda r: (r.rank, _arr(ct.c_size_t, r.extents), r.batch)),
+    ("SetDataType", None, lambda r: (r.storage, r.compute)),
+    ("SetDirection", None, lambda r: (int(r.inverse), int(r.normalize_inverse))),
+    ("SetPlacement", None, lambda r: (int(r.in_place),)),
+    ("SetExecutionMode", None, lambda r: (r.mode,)),
+    ("SetLengthMode", None, lambda r: (r.length_mode,)),
+    ("SetFftTransformType", None, lambda r: (r.fft_type,)),
+    ("SetFftOutputScale", None, lambda r: (r.fft_output_scale,)),
+    ("SetOutputScale", None, lambda r: (r.output_scale,)),
+    ("SetOutputRounding", None, lambda r: (r.output_rounding,)),
+    ("SetArithmeticPolicy", None, lambda r: (r.arithmetic_policy,)),
+    ("SetStrides", None, lambda r: (_arr(ct.c_size_t, r.input_strides), r.input_batch_stride,
+                                    _arr(ct.c_size_t, r.output_strides), r.output_batch_stride)),
+    ("SetModulus", lambda r: r.ntt, lambda r: (r.modulus, r.word_bits)),
+    ("SetNttLayouts", lambda r: r.ntt, lambda r: (r.input_order, r.output_order)),
+    ("SetLogicalOrders", lambda r: not r.legacy_layouts,
+     lambda r: (_arr(ct.c_int, r.input_orders), _arr(ct.c_int, r.output_orders))),
+    ("SetAlgorithmPolicy", None, lambda r: (r.policy, r.mapping)),
+)
 
 
 class Descriptor:
-    """Owned cubutterflyDescriptor_t configured from a Transform."""
+    """An owned cubutterflyDescriptor_t, configured from a Transform or loaded from JSON."""
 
     def __init__(self, library, transform, options=None):
         self.library = library
         self._handle = ct.c_void_p()
-        library._call("CreateDescriptor", ct.byref(self._handle))
+        library.invoke("CreateDescriptor", ct.byref(self._handle))
         try:
-            self._configure(transform, options or PlanOptions())
+            self._apply(_request(transform, options or PlanOptions()))
         except BaseException:
             self.close()
             raise
 
-    def _configure(self, t, options):
-        for name in ("inverse", "normalize_inverse", "in_place"):
-            if not isinstance(getattr(t, name), bool):
-                raise TypeError(f"{name} must be bool")
-        enum_names = ("op", "storage", "compute", "fft_type", "length_mode", "input_order", "output_order",
-                      "execution_mode", "output_rounding", "arithmetic_policy")
-        e = {name: _integer(getattr(t, name), name, ct.c_int) for name in enum_names}
-        policy = _integer(options.policy, "policy", ct.c_int)
-        mode = _integer(options.execution_mode, "options.execution_mode", ct.c_int)
-        extents = [_integer(v, "extents", ct.c_size_t) for v in t.extents]
-        strides_in = [_integer(v, "input_strides", ct.c_size_t) for v in t.input_strides]
-        strides_out = [_integer(v, "output_strides", ct.c_size_t) for v in t.output_strides]
-        orders_in = [_integer(v, "input_orders", ct.c_int) for v in t.input_orders]
-        orders_out = [_integer(v, "output_orders", ct.c_int) for v in t.output_orders]
-        batch = _integer(t.batch, "batch", ct.c_size_t)
-        batch_in = _integer(t.input_batch_stride, "input_batch_stride", ct.c_size_t)
-        batch_out = _integer(t.output_batch_stride, "output_batch_stride", ct.c_size_t)
-        modulus = _integer(t.modulus, "modulus", ct.c_uint64)
-        word_bits = _integer(t.word_bits, "word_bits", ct.c_uint32)
-        rank = len(t.extents)
-        _integer(rank, "rank", ct.c_uint32)
-        for values in (t.input_strides, t.output_strides, t.input_orders, t.output_orders):
-            if values and len(values) != rank:
-                raise ValueError("one entry is required per axis")
-        legacy = e["input_order"] != NttLayout.NATURAL or e["output_order"] != NttLayout.NATURAL
-        if legacy and e["op"] != Operator.NTT:
-            raise ValueError("legacy NTT layouts require an NTT operator")
-        if e["op"] != Operator.NTT and (modulus != DEFAULT_MODULUS or word_bits != 64):
-            raise ValueError("modulus and word_bits require an NTT operator")
-        if legacy and (t.input_orders or t.output_orders):
-            raise ValueError("legacy NTT layouts and logical orders are ambiguous")
-        call = lambda name, *args: self.library._call(name, self._handle, *args)  # noqa: E731
-        call("SetOperator", e["op"])
-        call("SetDataType", e["storage"], e["compute"])
-        call("SetShape", rank, _array(ct.c_size_t, extents), batch)
-        call("SetExecutionMode", mode or e["execution_mode"])
-        call("SetFftTransformType", e["fft_type"])
-        call("SetFftOutputScale", t.fft_output_scale)
-        call("SetOutputScale", t.output_scale)
-        call("SetOutputRounding", e["output_rounding"])
-        call("SetArithmeticPolicy", e["arithmetic_policy"])
-        call("SetStrides", _array(ct.c_size_t, strides_in), batch_in, _array(ct.c_size_t, strides_out), batch_out)
-        call("SetDirection", int(t.inverse), int(t.normalize_inverse))
-        call("SetPlacement", int(t.in_place))
-        call("SetLengthMode", e["length_mode"])
-        call("SetAlgorithmPolicy", AlgorithmPolicy.EXPLICIT if options.mapping else policy,
-             options.mapping.encode("utf-8"))
-        if e["op"] == Operator.NTT:
-            call("SetModulus", modulus, word_bits)
-            call("SetNttLayouts", e["input_order"], e["output_order"])
-        if not legacy:
-            call("SetLogicalOrders", _array(ct.c_int, orders_in), _array(ct.c_int, orders_out))
-        for axis, matrices in enumerate(t.stage_matrices):
-            _integer(axis, "matrix axis", ct.c_uint32)
-            if not matrices:
-                continue
-            values = [_Matrix(*m) for m in matrices]
-            call("SetStageMatrices", axis, _array(_Matrix, values), len(values))
+    def _apply(self, r):
+        for name, when, args in _SETTERS:
+            if when is None or when(r):
+                self.library.invoke(name, self._handle, *args(r))
+        for axis, stages in r.matrices:
+            self.library.invoke("SetStageMatrices", self._handle, axis, _arr(_Matrix, stages), len(stages))
 
     @classmethod
     def from_json(cls, library, value):
-        result = cls.__new__(cls)
-        result.library, result._handle = library, ct.c_void_p()
-        library._call("CreateDescriptor", ct.byref(result._handle))
+        """A descriptor from its JSON document (a str, or a dict serialised here)."""
+        self = cls.__new__(cls)
+        self.library, self._handle = library, ct.c_void_p()
+        library.invoke("CreateDescriptor", ct.byref(self._handle))
         try:
             text = value if isinstance(value, str) else _json.dumps(value)
-            library._call("DescriptorSetJson", result._handle, text.encode("utf-8"))
+            library.invoke("DescriptorSetJson", self._handle, text.encode("utf-8"))
         except BaseException:
-            result.close()
+            self.close()
             raise
-        return result
+        return self
 
     @property
     def native_handle(self):
         if not self._handle.value:
-            raise Error("descriptor is closed")
+            raise Error("this Descriptor has been closed")
         return self._handle
 
     def validate(self):
-        self.library._call("DescriptorValidate", self.native_handle)
+        self.library.invoke("DescriptorValidate", self.native_handle)
 
     def json(self):
-        return self.library._query("DescriptorGetJson", self.native_handle)
+        return self.library.text("DescriptorGetJson", self.native_handle)
 
     def capabilities_json(self):
-        return self.library._query("DescriptorGetCapabilities", self.native_handle)
+        return self.library.text("DescriptorGetCapabilities", self.native_handle)
 
     def close(self):
-        if self._handle.value:
-            handle, self._handle = self._handle, ct.c_void_p()
-            self.library._call("DestroyDescriptor", handle)
+        handle, self._handle = self._handle, ct.c_void_p()
+        if handle.value:
+            self.library.invoke("DestroyDescriptor", handle)
 
     def __enter__(self):
         return self
 
-    def __exit__(self, *args):
+    def __exit__(self, *exc):
         self.close()
 
     def __del__(self):
@@ -411,10 +460,13 @@ class Descriptor:
 
 
 class Plan:
-    """GPU plan with an owned handle (stream context) and caller workspace.
+    """An immutable plan and the handle (stream context) it executes on.
 
-    execute() is asynchronous on the plan's stream; pointers may be integers,
-    c_void_p, or objects with data_ptr() (torch tensors).
+    `transform` is a Transform (with optional PlanOptions) or a Descriptor of
+    the same Library.  The stream is fixed at construction.  Workspace is the
+    caller's: query workspace_size(), allocate, bind with set_workspace(),
+    which also keeps the passed object alive.  execute() is asynchronous;
+    pointers may be ints, c_void_p or objects with data_ptr() (torch tensors).
     """
 
     def __init__(self, library, transform, options=None, stream=None, cache_path=None):
@@ -422,98 +474,125 @@ class Plan:
         self._context, self._handle = ct.c_void_p(), ct.c_void_p()
         self._workspace = None
         try:
-            library._call("Create", ct.byref(self._context))
-            if cache_path is None:
-                cache_path = os.environ.get("CUBUTTERFLY_PLAN_CACHE")
-            if cache_path:
-                library._call("SetCachePath", self._context, os.fsencode(cache_path))
+            library.invoke("Create", ct.byref(self._context))
+            cache = os.environ.get("CUBUTTERFLY_PLAN_CACHE") if cache_path is None else cache_path
+            if cache:
+                library.invoke("SetCachePath", self._context, os.fsencode(cache))
             if stream is not None:
-                library._call("SetStream", self._context, _pointer(stream))
+                library.invoke("SetStream", self._context, _abi.address(stream, "stream"))
             if isinstance(transform, Descriptor):
                 if options is not None:
-                    raise ValueError("selection options must be set when constructing the Descriptor")
+                    raise ValueError("a Descriptor carries its own selection; pass options when building it")
                 if transform.library is not library:
-                    raise ValueError("descriptor and plan must use the same Library")
-                library._call("CreatePlan", self._context, transform.native_handle, ct.byref(self._handle))
+                    raise ValueError("the Descriptor was created by a different Library")
+                self._create(transform)
             else:
-                with Descriptor(library, transform, options) as descriptor:
-                    library._call("CreatePlan", self._context, descriptor.native_handle, ct.byref(self._handle))
+                with Descriptor(library, transform, options) as d:
+                    self._create(d)
         except BaseException:
             self.close()
             raise
 
+    def _create(self, descriptor):
+        self.library.invoke("CreatePlan", self._context, descriptor.native_handle, ct.byref(self._handle))
+
     @property
     def native_handle(self):
         if not self._handle.value:
-            raise Error("plan is closed")
+            raise Error("this Plan has been closed")
         return self._handle
 
     @property
     def native_context(self):
         if not self._context.value:
-            raise Error("plan context is closed")
+            raise Error("this Plan has been closed")
         return self._context
 
-    def _size(self, name):
-        size = ct.c_size_t()
-        self.library._call(name, self.native_handle, ct.byref(size))
-        return size.value
+    def set_stream(self, stream):
+        raise Error("a plan's stream is fixed when it is created: pass stream= to Plan()")
+
+    def _bytes(self, query):
+        v = ct.c_size_t()
+        self.library.invoke(query, self.native_handle, ct.byref(v))
+        return v.value
 
     def workspace_size(self):
-        return self._size("PlanGetWorkspaceSize")
+        return self._bytes("PlanGetWorkspaceSize")
 
     def input_size(self):
-        return self._size("PlanGetInputSize")
+        return self._bytes("PlanGetInputSize")
 
     def output_size(self):
-        return self._size("PlanGetOutputSize")
+        return self._bytes("PlanGetOutputSize")
 
     def selection_source(self):
         v = ct.c_int()
-        self.library._call("PlanGetSelectionSource", self.native_handle, ct.byref(v))
+        self.library.invoke("PlanGetSelectionSource", self.native_handle, ct.byref(v))
         return SelectionSource(v.value)
 
     def set_workspace(self, pointer, bytes):
-        self.library._call("PlanSetWorkspace", self.native_handle, _pointer(pointer), bytes)
+        self.library.invoke("PlanSetWorkspace", self.native_handle, _abi.address(pointer, "workspace"),
+                            _abi.unsigned(bytes, "workspace bytes"))
+        self._workspace = pointer
 
     def physical_extents(self, rank):
         """Extents the plan transforms physically: the padded length of a
         zero-extended embedding, the convolution length of a non-power-of-two
         FFT axis, else the logical extent."""
         out = (ct.c_size_t * rank)()
-        self.library._call("PlanGetPhysicalExtents", self.native_handle, out, rank)
+        self.library.invoke("PlanGetPhysicalExtents", self.native_handle, out, rank)
         return list(out)
-        self._workspace = pointer
 
     def execute(self, input, output):
-        self.library._call("Execute", self._context, self.native_handle, _pointer(input), _pointer(output))
+        self.library.invoke("Execute", self.native_context, self.native_handle, _abi.address(input, "input"),
+                            _abi.address(output, "output"))
 
     def execute_steady(self, input, output):
-        self.library._call("ExecuteSteady", self._context, self.native_handle, _pointer(input), _pointer(output))
+        self.library.invoke("ExecuteSteady", self.native_context, self.native_handle, _abi.address(input, "input"),
+                            _abi.address(output, "output"))
+
+    def device_status(self) -> int:
+        """Failure bits recorded on the device by earlier launches (0: none);
+        final once the plan's stream has been synchronised."""
+        v = ct.c_uint()
+        self.library.invoke("B200PlanGetDeviceStatus", self.native_handle, ct.byref(v))
+        return v.value
+
+    def inject_device_status(self, bits: int):
+        """Test hook: record `bits` as a failing launch would."""
+        self.library.invoke("B200PlanInjectDeviceStatus", self.native_handle, _abi.unsigned(bits, "bits", ct.c_uint))
 
     def mapping_json(self):
-        return self.library._query("PlanGetMappingJson", self.native_handle)
+        return self.library.text("PlanGetMappingJson", self.native_handle)
 
     def descriptor_json(self):
-        return self.library._query("PlanGetDescriptorJson", self.native_handle)
+        return self.library.text("PlanGetDescriptorJson", self.native_handle)
 
     def algorithm_name(self):
-        return self.library._query("PlanGetAlgorithmName", self.native_handle)
+        return self.library.text("PlanGetAlgorithmName", self.native_handle)
 
     def selection_reason(self):
-        return self.library._query("PlanGetSelectionReason", self.native_handle)
+        return self.library.text("PlanGetSelectionReason", self.native_handle)
 
     def close(self):
+        handle, self._handle = self._handle, ct.c_void_p()
+        context, self._context = self._context, ct.c_void_p()
+        self._workspace = None
         try:
-            if self._handle.value:
-                handle, self._handle = self._handle, ct.c_void_p()
-                self.library._call("DestroyPlan", handle)
+            if handle.value:
+                self.library.invoke("DestroyPlan", handle)
         finally:
-            if self._context.value:
-                context, self._context = self._context, ct.c_void_p()
-                self.library._call("Destroy", context)
-            self._workspace = None
+            if context.value:
+                self.library.invoke("Destroy", context)
 
-    __enter__ = Descriptor.__enter__
-    __exit__ = Descriptor.__exit__
-    __del__ = Descriptor.__del__
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

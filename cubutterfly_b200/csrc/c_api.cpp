@@ -60,6 +60,11 @@ struct cubutterflyPlan {
     cubf::NttTables ntt_tables{};
     const cubf::NttPolyDesc* ntt_polys = nullptr;
     int device = 0;
+    // Device-side status word of plans whose kernels wait on the device (the
+    // tensor-core FWHT): mapped pinned host memory the kernel ORs failure
+    // bits into, read (and cleared) by the next Execute without a sync.
+    unsigned int* status_host = nullptr;
+    unsigned int* status_dev = nullptr;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
     // Chained multi-pass bitwise plans over several L2 chunks: the first pass
@@ -136,6 +141,7 @@ struct cubutterflyPlan {
         for (auto l : lanes)
             if (l) cudaStreamDestroy(l);
         if (capture) cudaStreamDestroy(capture);
+        if (status_host) cudaFreeHost(status_host);
     }
 };
 
@@ -761,7 +767,8 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         if (inverse && d.normalize_inverse) scale /= static_cast<double>(n);
     }
     if (m.passes.front().kind == cubf::PassKind::FwhtTensor) {
-        check_cuda(cubf::launch_fwht_tc(in, out, d.batch, static_cast<float>(scale), stream), "tensor FWHT launch");
+        check_cuda(cubf::launch_fwht_tc(in, out, d.batch, static_cast<float>(scale), p.status_dev, stream),
+                   "tensor FWHT launch");
         return;
     }
     if (!launch_chain_graph(p, m, in, out, stream, scale)) enqueue_chain(p, m, in, out, stream, scale);
@@ -1059,6 +1066,15 @@ std::unique_ptr<cubutterflyPlan> create_rank1(cubutterflyHandle* handle, const c
     p->req = make_request(d);
     p->hw = cubf::resolve_profile();
     check_cuda(cudaGetDevice(&p->device), "current device");
+    if (d.op == CUBUTTERFLY_OPERATOR_FWHT && cubf::fwht_tc_available(p->req.log_n, p->req.bw_type)) {
+        void* host = nullptr;
+        check_cuda(cudaHostAlloc(&host, sizeof(unsigned int), cudaHostAllocMapped), "device status word");
+        p->status_host = static_cast<unsigned int*>(host);
+        *p->status_host = 0;
+        void* dev = nullptr;
+        check_cuda(cudaHostGetDevicePointer(&dev, host, 0), "device status word address");
+        p->status_dev = static_cast<unsigned int*>(dev);
+    }
     build_tables(*p);  // before selection: MEASURE executes the candidates
     select_mapping(handle, *p);
     make_lanes(*p);
@@ -2076,10 +2092,41 @@ cubutterflyStatus_t cubutterflyPlanSetWorkspace(cubutterflyPlan_t plan, void* wo
     });
 }
 
+namespace {
+// The device-status words of a plan and of its child plans, OR-ed.
+unsigned int device_status(const cubutterflyPlan& p) {
+    unsigned int bits = p.status_host ? *reinterpret_cast<volatile unsigned int*>(p.status_host) : 0u;
+    for (const auto& a : p.axes)
+        if (a.plan) bits |= device_status(*a.plan);
+    return bits;
+}
+
+void clear_device_status(cubutterflyPlan& p) {
+    if (p.status_host) *reinterpret_cast<volatile unsigned int*>(p.status_host) = 0u;
+    for (auto& a : p.axes)
+        if (a.plan) clear_device_status(*a.plan);
+}
+
+// A failure that an earlier launch of this plan recorded on the device (a
+// bounded wait that expired: that launch's output is invalid) is the status
+// of the next call on the plan; reporting it clears it.
+void report_device_status(cubutterflyPlan& p) {
+    const unsigned int bits = device_status(p);
+    if (bits == 0) return;
+    clear_device_status(p);
+    std::ostringstream o;
+    o << "an earlier launch of this plan failed on the device (status bits 0x" << std::hex << bits
+      << "): " << ((bits & 1u) ? "a tensor-core completion wait expired" : "kernel launch invariant violated")
+      << "; that launch's output is invalid";
+    throw std::runtime_error(o.str());
+}
+}  // namespace
+
 cubutterflyStatus_t cubutterflyExecute(cubutterflyHandle_t handle, cubutterflyPlan_t plan, const void* input,
                                        void* output) {
     return protect([&] {
         require(handle != nullptr && plan != nullptr, "handle and plan must be non-null");
+        report_device_status(*plan);
         require(input != nullptr && output != nullptr, "input and output must be non-null");
         const bool in_place = plan->desc.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
         require(in_place == (input == output),
@@ -2098,10 +2145,31 @@ cubutterflyStatus_t cubutterflyExecuteSteady(cubutterflyHandle_t handle, cubutte
     if (!handle || !plan || !plan->steady_ready || plan->steady_stream != handle->stream)
         return cubutterflyExecute(handle, plan, input, output);
     return protect([&] {
+        report_device_status(*plan);
         const bool in_place = plan->desc.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
         require(input != nullptr && output != nullptr && in_place == (input == output),
                 "pointer aliasing does not match the plan placement");
+        require((reinterpret_cast<std::uintptr_t>(input) | reinterpret_cast<std::uintptr_t>(output)) % 16 == 0,
+                "input and output must be 16-byte aligned (the kernels move 16-byte vectors)");
         launch_mapping(*plan, plan->mapping, input, output, handle->stream);
+    });
+}
+
+cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterflyPlan_t plan, unsigned int* bits) {
+    return protect([&] {
+        require(plan != nullptr && bits != nullptr, "plan and bits must be non-null");
+        *bits = device_status(*plan);
+    });
+}
+
+cubutterflyStatus_t cubutterflyB200PlanInjectDeviceStatus(cubutterflyPlan_t plan, unsigned int bits) {
+    return protect([&] {
+        require(plan != nullptr, "plan must be non-null");
+        cubutterflyPlan* p = plan;
+        while (p->status_host == nullptr && p->axes.size() == 1 && p->axes[0].plan) p = p->axes[0].plan.get();
+        if (p->status_host == nullptr)
+            throw cubf::Unsupported("plan has no device status word (only tensor-core FWHT plans wait on the device)");
+        *reinterpret_cast<volatile unsigned int*>(p->status_host) |= bits;
     });
 }
 

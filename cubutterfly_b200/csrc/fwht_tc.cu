@@ -87,7 +87,15 @@ struct Smem {
     uint32_t tmem_base;
 };
 
-__device__ unsigned int g_status;  // nonzero: a wait expired (see fwht_tc_take_status)
+
+// Failure report to the plan's status word (mapped pinned host memory): a
+// plain system-visible store, not an atomic -- atomics on mapped host memory
+// are not atomic from the host's side, and any nonzero value is a failure.
+CUBF_DEV void record_status(unsigned int* status, unsigned int code) {
+    if (status == nullptr) return;
+    *reinterpret_cast<volatile unsigned int*>(status) = code;
+    __threadfence_system();
+}
 
 CUBF_DEV uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 
@@ -169,7 +177,8 @@ CUBF_DEV void load_pair(const __nv_bfloat16* in, size_t rows, size_t pair, uint8
 CUBF_DEV void group_sync(int g) { asm volatile("bar.sync %0, %1;" ::"r"(1 + g), "r"(kGroupThreads) : "memory"); }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    fwht4096_tc_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, size_t rows, float scale) {
+    fwht4096_tc_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, size_t rows, float scale,
+                       unsigned int* status) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5;
@@ -177,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     GroupSmem& gs = sm.g[grp];
     // the swizzle acts on absolute shared-memory address bits: atoms must be 1 KiB aligned
     const size_t pairs = (smem_addr(smem_raw) & 1023u) ? 0 : (rows + 1) / 2;
-    if (pairs == 0 && rows != 0 && tid == 0) atomicOr(&g_status, 2u);
+    if (pairs == 0 && rows != 0 && tid == 0) record_status(status, 2u);
 
     const size_t first = static_cast<size_t>(blockIdx.x) * kGroups + grp;
     const size_t stride = static_cast<size_t>(gridDim.x) * kGroups;
@@ -359,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // bounded: let outstanding MMA batches drain before TMEM is freed
         mbar_wait(mbar1, ph1);
         mbar_wait(mbar2, ph2);
-        atomicOr(&g_status, 1u);
+        record_status(status, 1u);
     }
     fence_before_sync();
     __syncthreads();
@@ -387,7 +396,8 @@ LaunchShape fwht_tc_shape() {
     return s;
 }
 
-cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream) {
+cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, unsigned int* status,
+                           cudaStream_t stream) {
     using namespace fwht_tc;
     static KernelSetup setup;
     int grid_cap = 0;
@@ -399,16 +409,8 @@ cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float sc
     const std::size_t want = (pairs + kGroups - 1) / kGroups;  // CTAs that have a pair for every group
     const std::size_t grid = want < static_cast<std::size_t>(grid_cap) ? want : static_cast<std::size_t>(grid_cap);
     fwht4096_tc_kernel<<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(
-        static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), rows, scale);
+        static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), rows, scale, status);
     return cudaGetLastError();
-}
-
-unsigned fwht_tc_take_status() {
-    unsigned v = 0;
-    if (cudaMemcpyFromSymbol(&v, fwht_tc::g_status, sizeof(v)) != cudaSuccess) return ~0u;
-    const unsigned zero = 0;
-    cudaMemcpyToSymbol(fwht_tc::g_status, &zero, sizeof(zero));
-    return v;
 }
 
 }  // namespace cubf

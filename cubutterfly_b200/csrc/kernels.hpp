@@ -76,12 +76,14 @@ cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t
 
 // ---- FWHT on the tensor cores (tcgen05) ------------------------------------------
 // 4096-point bf16 rows as H_64 (x) H_64 contractions (csrc/fwht_tc.cu); in may
-// equal out.  fwht_tc_take_status returns (and clears) the kernel's error
-// word: nonzero when a bounded wait expired.
+// equal out.  `status` (nullable; device-visible, normally mapped pinned host
+// memory) receives bit 0 when a bounded MMA-completion wait expired and bit 1
+// when the dynamic shared memory was not 1 KiB aligned (the output is then
+// not written); the kernel only ever sets bits.
 bool fwht_tc_available(int log_n, BwType type);
 LaunchShape fwht_tc_shape();
-cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, cudaStream_t stream);
-unsigned fwht_tc_take_status();
+cudaError_t launch_fwht_tc(const void* in, void* out, std::size_t rows, float scale, unsigned int* status,
+                           cudaStream_t stream);
 
 // ---- structured 2x2 butterfly (csrc/structured.cu) ---------------------------------
 constexpr int kStructuredMaxLog = 30;

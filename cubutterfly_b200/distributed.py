@@ -28,7 +28,6 @@ in CPU tests).
 """
 from __future__ import annotations
 
-import ctypes as ct
 from dataclasses import dataclass
 from typing import Callable, Optional
 
@@ -93,18 +92,13 @@ class _LibraryFft:
 
 class _LibraryTwiddle:
     def __init__(self, lib):
-        fn = lib._dll.cubutterflyB200FourStepTwiddle
-        fn.argtypes = [ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_int,
-                       ct.c_void_p]
-        fn.restype = ct.c_int
-        self.fn, self.lib = fn, lib
+        self.lib = lib
 
     def __call__(self, data: torch.Tensor, rows: int, cols: int, row_offset: int, col_offset: int, n: int,
                  inverse: bool) -> None:
         stream = torch.cuda.current_stream(data.device).cuda_stream
-        status = self.fn(data.data_ptr(), rows, cols, row_offset, col_offset, n, int(inverse), stream)
-        if status:
-            raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
+        self.lib.invoke("B200FourStepTwiddle", data.data_ptr(), rows, cols, row_offset, col_offset, n, int(inverse),
+                        stream)
 
 
 class _LibraryPermute:
@@ -112,32 +106,22 @@ class _LibraryPermute:
     a == self may come from `in_self`, block b == self may go to `out_self`."""
 
     def __init__(self, lib):
-        fn = lib._dll.cubutterflyB200PermuteBlocksC64
-        fn.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t,
-                       ct.c_size_t, ct.c_void_p]
-        fn.restype = ct.c_int
-        self.fn, self.lib = fn, lib
+        self.lib = lib
 
     def __call__(self, x, out, a, b, c, self_index=0, in_self=None, out_self=None):
         stream = torch.cuda.current_stream(x.device).cuda_stream
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
-        status = self.fn(x.data_ptr(), ptr(in_self), out.data_ptr(), ptr(out_self), self_index, a, b, c, stream)
-        if status:
-            raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
+        self.lib.invoke("B200PermuteBlocksC64", x.data_ptr(), ptr(in_self), out.data_ptr(), ptr(out_self),
+                        self_index, a, b, c, stream)
 
 
 class _LibraryTranspose:
     def __init__(self, lib):
-        fn = lib._dll.cubutterflyB200TransposeC64
-        fn.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_size_t, ct.c_size_t, ct.c_size_t, ct.c_void_p]
-        fn.restype = ct.c_int
-        self.fn, self.lib = fn, lib
+        self.lib = lib
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor, rows: int, cols: int) -> None:
         stream = torch.cuda.current_stream(x.device).cuda_stream
-        status = self.fn(x.data_ptr(), out.data_ptr(), 1, rows, cols, stream)
-        if status:
-            raise cb.Error(self.lib._dll.cubutterflyGetLastErrorString().decode(), status)
+        self.lib.invoke("B200TransposeC64", x.data_ptr(), out.data_ptr(), 1, rows, cols, stream)
 
 
 class FourStepFFT:

@@ -1,24 +1,29 @@
 """Prepared word64 RNS NTT plans over caller-owned CUDA buffers.
 
-Mirrors the reference's python/cubutterfly/rns.py:67-170 (Library, Plan,
-Placement, CachePolicy, Error; prepare -> execute -> info -> close) over the
-cubutterflyRns* C ABI of libcubutterfly_b200.so.  Import loads nothing.
-Prepare belongs outside stream capture and timing; execute enqueues the two
-tile passes without copying or synchronising.
+Public names are the reference's (python/cubutterfly/rns.py: ``Library``,
+``Plan``, ``Placement``, ``CachePolicy``, ``Error``); the entry points are the
+cubutterflyRns* C ABI of libcubutterfly_b200.so (include/cuntt/rns_c_api.h).
+
+A plan moves through three states: created (config validated by the C side,
+tables built), prepared (placement and mapping fixed, timed once unless a
+cache answers), closed.  ``prepare`` runs once, outside stream capture and
+timing; ``execute`` only enqueues the tile passes (no copies, no
+synchronisation).  Buffers and streams must outlive the work enqueued on
+them.  Importing this module loads nothing.
 """
 from __future__ import annotations
 
 import ctypes as ct
 import json
-import operator
 import os
-from enum import IntEnum
-from pathlib import Path
+from enum import Enum, IntEnum
 
-from . import default_library_path
+from . import _abi, default_library_path
 
 
 class Error(RuntimeError):
+    """A failed RNS call; `status` is 1 (invalid request) or 2 (runtime failure), None for frontend errors."""
+
     def __init__(self, message, status=None):
         super().__init__(message)
         self.status = status
@@ -35,130 +40,116 @@ class CachePolicy(IntEnum):
     REFRESH = 2
 
 
-def _integer(value, name, maximum):
-    if isinstance(value, bool):
-        raise TypeError(f"{name} must be an integer, not bool")
-    try:
-        value = operator.index(value)
-    except TypeError as exc:
-        raise TypeError(f"{name} must be an integer") from exc
-    if not 0 <= value <= maximum:
-        raise ValueError(f"{name} is outside the ABI range")
-    return value
-
-
-def _pointer(value, name, *, nullable=False, aligned=False):
-    if hasattr(value, "data_ptr"):
-        value = value.data_ptr()
-    if isinstance(value, ct.c_void_p):
-        value = value.value or 0
-    value = _integer(value, name, (1 << (ct.sizeof(ct.c_void_p) * 8)) - 1)
-    if not nullable and not value:
-        raise ValueError(f"{name} must be non-null")
-    if aligned and value % ct.alignment(ct.c_uint64):
-        raise ValueError(f"{name} must be uint64 aligned")
-    return ct.c_void_p(value)
-
-
-def _config_json(config):
-    if isinstance(config, str):
-        config = json.loads(config)
-    if not isinstance(config, dict):
-        raise TypeError("config must be a dict or JSON object string")
-    return json.dumps(config, allow_nan=False, separators=(",", ":")).encode("utf-8")
+_RNS_ABI = """
+Create     s P
+Prepare    p i s i w p
+Execute    p p p p
+InfoJson   p p Z
+Destroy    p
+LastError
+"""
 
 
 class Library:
-    """The RNS entry points of a loaded libcubutterfly_b200.so."""
+    """The cubutterflyRns* entry points of a loaded libcubutterfly_b200.so."""
 
     def __init__(self, path=None):
-        path = Path(path) if path else default_library_path()
-        if not path.exists():
-            raise FileNotFoundError(f"{path} is missing: build it with `python -m cubutterfly_b200._build`")
+        path = path if path is not None else default_library_path()
+        if not os.path.isfile(path):
+            raise FileNotFoundError(f"no cuButterfly library at {path}; build it with "
+                                    "`python -m cubutterfly_b200._build`")
         self._dll = ct.CDLL(os.fspath(path))
-        p = ct.c_void_p
-        sig = {
-            "Create": [ct.c_char_p, ct.POINTER(p)],
-            "Prepare": [p, ct.c_int, ct.c_char_p, ct.c_int, ct.c_uint, p],
-            "Execute": [p, p, p, p],
-            "InfoJson": [p, p, ct.POINTER(ct.c_size_t)],
-            "Destroy": [p],
-            "LastError": [],
-        }
-        for name, args in sig.items():
-            fn = getattr(self._dll, "cubutterflyRns" + name)
-            fn.argtypes = args
-            fn.restype = ct.c_char_p if name == "LastError" else ct.c_int
+        self.fn = _abi.bind(self._dll, "cubutterflyRns", _RNS_ABI, text=("LastError",))
 
-    def _call(self, name, *args):
-        status = getattr(self._dll, "cubutterflyRns" + name)(*args)
+    def invoke(self, name, *args):
+        status = self.fn[name](*args)
         if status:
-            message = self._dll.cubutterflyRnsLastError() or b"RNS operation failed"
-            raise Error(message.decode("utf-8", errors="replace"), status)
+            detail = (self.fn["LastError"]() or b"").decode("utf-8", "replace")
+            raise Error(detail or f"cubutterflyRns{name} failed with status {status}", status)
 
-    def _info(self, handle):
-        size = ct.c_size_t()
-        self._call("InfoJson", handle, None, ct.byref(size))
-        buf = ct.create_string_buffer(size.value)
-        self._call("InfoJson", handle, buf, ct.byref(size))
-        return json.loads(buf.value.decode("utf-8"))
+    def info_json(self, handle) -> dict:
+        return json.loads(_abi.two_call_text(lambda *a: self.invoke("InfoJson", *a), handle))
+
+
+def _payload(config) -> bytes:
+    """The request as compact JSON text (the C parser validates every key)."""
+    doc = json.loads(config) if isinstance(config, (str, bytes)) else config
+    if not isinstance(doc, dict):
+        raise TypeError(f"an RNS config is a JSON object (dict or text), not {type(doc).__name__}")
+    return json.dumps(doc, allow_nan=False, separators=(",", ":")).encode("utf-8")
+
+
+class _State(Enum):
+    CREATED = "created"
+    PREPARED = "prepared"
+    CLOSED = "closed"
 
 
 class Plan:
-    """Owned RNS plan.  prepare() must succeed before execute(); close() explicitly."""
+    """An owned RNS plan.  prepare() once, then execute(); close() releases it
+    (explicitly, or by leaving a `with` block: nothing is freed from a
+    finaliser while GPU work may still reference the plan)."""
 
     def __init__(self, library, config):
         self.library = library
         self._handle = ct.c_void_p()
+        self._state = _State.CREATED
         self._placement = None
-        library._call("Create", _config_json(config), ct.byref(self._handle))
+        library.invoke("Create", _payload(config), ct.byref(self._handle))
         if not self._handle.value:
-            raise Error("RNS Create returned a null plan")
+            self._state = _State.CLOSED
+            raise Error("cubutterflyRnsCreate reported success without a plan")
+
+    def _need(self, *states):
+        if self._state not in states:
+            wanted = " or ".join(s.value for s in states)
+            raise Error(f"RNS plan is {self._state.value}; this call needs a {wanted} plan")
 
     @property
     def native_handle(self):
-        if not self._handle.value:
-            raise Error("RNS plan is closed")
+        self._need(_State.CREATED, _State.PREPARED)
         return self._handle
 
     def prepare(self, *, placement=Placement.SEPARATE, cache_directory=None, policy=CachePolicy.PREFER,
                 repetitions=5, stream=0):
-        handle = self.native_handle
-        if self._placement is not None:
-            raise Error("plan is already prepared; create another plan to retune")
-        placement = Placement(_integer(placement, "placement", 1))
-        policy = CachePolicy(_integer(policy, "policy", 2))
-        repetitions = _integer(repetitions, "repetitions", (1 << 32) - 1)
-        if not repetitions:
-            raise ValueError("repetitions must be positive")
-        directory = b"" if cache_directory is None else os.fsencode(cache_directory)
-        if b"\0" in directory:
-            raise ValueError("cache_directory must not contain NUL")
-        self.library._call("Prepare", handle, int(placement), directory, int(policy), repetitions,
-                           _pointer(stream, "stream", nullable=True))
+        """Fix the placement and the mapping (timed `repetitions` times unless
+        the cache in `cache_directory` answers, per `policy`).  Once per plan."""
+        self._need(_State.CREATED)
+        placement = Placement(_abi.unsigned(placement, "placement", ct.c_int))
+        policy = CachePolicy(_abi.unsigned(policy, "policy", ct.c_int))
+        reps = _abi.unsigned(repetitions, "repetitions", ct.c_uint)
+        if reps < 1:
+            raise ValueError("repetitions: at least one timed repetition is needed")
+        where = os.fsencode(cache_directory) if cache_directory is not None else b""
+        if b"\0" in where:
+            raise ValueError("cache_directory: embedded NUL byte")
+        self.library.invoke("Prepare", self._handle, int(placement), where, int(policy), reps,
+                            _abi.address(stream, "stream"))
         self._placement = placement
+        self._state = _State.PREPARED
         return self
 
     def execute(self, input, output, *, stream=0):
-        handle = self.native_handle
-        if self._placement is None:
-            raise Error("RNS plan must be prepared before execution")
-        src = _pointer(input, "input", aligned=True)
-        dst = _pointer(output, "output", aligned=True)
-        if (src.value == dst.value) != (self._placement == Placement.IN_PLACE):
-            raise ValueError("pointer aliasing does not match prepared placement")
-        self.library._call("Execute", handle, src, dst, _pointer(stream, "stream", nullable=True))
+        """Enqueue the transform of `input` into `output` (device addresses, 8-byte aligned)."""
+        self._need(_State.PREPARED)
+        src = _abi.address(input, "input", nullable=False, align=8)
+        dst = _abi.address(output, "output", nullable=False, align=8)
+        aliased = src.value == dst.value
+        if aliased != (self._placement is Placement.IN_PLACE):
+            raise ValueError(f"the plan was prepared {self._placement.name.lower()}: input and output must "
+                             + ("be the same buffer" if self._placement is Placement.IN_PLACE else "differ"))
+        self.library.invoke("Execute", self._handle, src, dst, _abi.address(stream, "stream"))
 
-    def info(self):
-        return self.library._info(self.native_handle)
+    def info(self) -> dict:
+        return self.library.info_json(self.native_handle)
 
     def close(self):
-        if self._handle.value:
-            self.library._call("Destroy", self._handle)
-            self._handle = ct.c_void_p()
+        if self._state is not _State.CLOSED:
+            handle, self._handle, self._state = self._handle, ct.c_void_p(), _State.CLOSED
+            self.library.invoke("Destroy", handle)
 
     def __enter__(self):
-        self.native_handle
+        self._need(_State.CREATED, _State.PREPARED)
         return self
 
     def __exit__(self, *exc):

@@ -7,8 +7,8 @@ caller's current CUDA stream through plans that are built once per
 (operator, shape, dtype, scale, orders, device, stream) and then reused.
 Execution allocates nothing (workspaces are created with the plan), so the
 calls are CUDA-graph capturable; ``InferenceGraph`` captures a whole
-Tensor -> Tensor function with the contract of the reference's
-``python/cubutterfly/torch_graph.py`` (InferenceGraph, :4-78).
+Tensor -> Tensor function (the consumer the reference serves with
+``python/cubutterfly/torch_graph.py``, same constructor and call).
 
 torch is imported lazily; the library has no CPU fallback and raises when its
 CUDA build is missing.
@@ -175,75 +175,79 @@ def ntt(x, modulus: int, inverse: bool = False, out=None,
 
 
 class InferenceGraph:
-    """Capture a Tensor -> Tensor inference function for one fixed input contract.
+    """A Tensor -> Tensor inference function (for example a Hadamard rotation
+    feeding a model head) replayed as one CUDA graph for one input contract.
 
-    Construction warms the function up on `stream` and captures it in a CUDA
-    graph.  Calls must be serialised on `stream` and use the captured shape,
-    dtype and device; the callable (and any parameters) must stay alive and
-    unchanged, and modules must be in eval mode.  Each call copies its input
-    into the captured buffer, replays the graph and returns a clone of the
-    output (independent storage, asynchronous on `stream`).  Autograd is not
-    supported.  Same contract as the reference's torch_graph.InferenceGraph.
+    `InferenceGraph(function, example, *, stream=None, warmup=3)` fixes the
+    contract (the shape, dtype and CUDA device of `example`) and a capture
+    stream (a new side stream unless given; never the legacy default stream).
+    The function runs `warmup` times there first, which builds and caches
+    every cuButterfly plan it needs, so no plan is created under capture; then
+    it is captured once.  A call, made on the capture stream with a tensor of
+    the contract, stages the value into the graph's static input, replays the
+    graph and returns the static output copied into `out` (or a new tensor):
+    all of it asynchronous on that stream.  The function and its parameters
+    must stay unchanged, torch modules in eval mode; there is no autograd.
     """
 
     def __init__(self, function, example, *, stream=None, warmup=3):
         import torch
 
-        if not isinstance(example, torch.Tensor) or not example.is_cuda:
-            raise ValueError("a CUDA Tensor example is required")
-        if example.requires_grad:
-            raise ValueError("inference input must not require gradients")
-        if warmup < 1:
-            raise ValueError("warmup must be positive")
-        self.torch = torch
+        self._torch = torch
+        if not (isinstance(example, torch.Tensor) and example.is_cuda):
+            raise ValueError("InferenceGraph needs a CUDA Tensor example to fix its input contract")
+        self._key = (tuple(example.shape), example.dtype, example.device)
+        self._reject_grad(example)
+        if int(warmup) < 1:
+            raise ValueError("warmup: at least one eager run must precede the capture")
         self.function = function
-        self.shape, self.dtype, self.device = tuple(example.shape), example.dtype, example.device
-        self.stream = stream if stream is not None else torch.cuda.Stream(device=self.device)
+        self.shape, self.dtype, self.device = self._key
+        self.stream = torch.cuda.Stream(device=self.device) if stream is None else stream
         if torch.device(self.stream.device) != self.device:
-            raise ValueError("capture stream device differs from input device")
+            raise ValueError(f"capture stream is on {self.stream.device}, the example on {self.device}")
         if int(self.stream.cuda_stream) == 0:
-            raise ValueError("capture requires a non-default CUDA stream")
-        self._check_modules()
+            raise ValueError("the legacy default stream cannot be captured; give a side stream")
+        self._require_eval()
         self.stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.stream), torch.inference_mode():
-            self._input = example.clone()
-            for _ in range(warmup):  # builds every plan before capture
-                output = function(self._input)
-            if not isinstance(output, torch.Tensor):
-                raise ValueError("inference function must return one Tensor")
-        self.stream.synchronize()
-        self._graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(self.stream), torch.inference_mode():
+            self._static_in = example.detach().clone()
+            results = [function(self._static_in) for _ in range(int(warmup))]
+            if not isinstance(results[-1], torch.Tensor):
+                raise ValueError(f"the function returned {type(results[-1]).__name__}, not one Tensor")
+            del results
+            self.stream.synchronize()
+            self._graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self._graph, stream=self.stream):
-                self._output = function(self._input)
+                self._static_out = function(self._static_in)
         self.stream.synchronize()
 
-    def _check_modules(self):
-        modules = getattr(self.function, "modules", None)
-        if modules is not None and any(m.training for m in modules()):
-            raise ValueError("all captured modules must be in eval mode")
-
-    def _validate(self, value):
-        torch = self.torch
-        if not isinstance(value, torch.Tensor):
-            raise ValueError("input must be a Tensor")
-        if tuple(value.shape) != self.shape or value.dtype != self.dtype or value.device != self.device:
-            raise ValueError("input shape/dtype/device differs from capture")
+    def _reject_grad(self, value):
         if value.requires_grad:
-            raise ValueError("inference input must not require gradients")
-        if int(torch.cuda.current_stream(self.device).cuda_stream) != int(self.stream.cuda_stream):
-            raise ValueError("call must run on the declared capture stream")
-        self._check_modules()
+            raise ValueError("InferenceGraph is inference only: the input requires grad")
 
-    def __call__(self, value):
-        self._validate(value)
-        with self.torch.inference_mode():
-            self._input.copy_(value)
+    def _require_eval(self):
+        modules = getattr(self.function, "modules", None)
+        if callable(modules) and any(m.training for m in modules()):
+            raise ValueError("put every module of the function in eval mode before capture")
+
+    def __call__(self, value, out=None):
+        torch = self._torch
+        if not isinstance(value, torch.Tensor) or (tuple(value.shape), value.dtype, value.device) != self._key:
+            got = (tuple(value.shape), value.dtype, value.device) if isinstance(value, torch.Tensor) else type(value)
+            raise ValueError(f"input {got} does not match the captured contract {self._key}")
+        self._reject_grad(value)
+        if int(torch.cuda.current_stream(self.device).cuda_stream) != int(self.stream.cuda_stream):
+            raise ValueError("call the graph on its capture stream (with torch.cuda.stream(graph.stream))")
+        self._require_eval()
+        with torch.inference_mode():
+            self._static_in.copy_(value)
             self._graph.replay()
-            return self._output.clone()
+            if out is None:
+                return self._static_out.clone()
+            return out.copy_(self._static_out)
 
     def contract(self):
-        return dict(shape=list(self.shape), dtype=str(self.dtype), device=str(self.device),
-                    stream=int(self.stream.cuda_stream), inference_only=True, serialized_calls=True,
-                    input_copy_included=True,
-                    output_ownership="independent clone per call; clone included in timing")
+        """The captured contract and call semantics, as a dict."""
+        return {"shape": list(self.shape), "dtype": str(self.dtype), "device": str(self.device),
+                "stream": int(self.stream.cuda_stream), "inference_only": True, "serialized_calls": True,
+                "input_copy_included": True, "output": "copied into `out` or a new tensor on every call"}

@@ -52,6 +52,24 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PermuteBlocksC64(const void* i
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input, void* output, size_t batch,
                                                               size_t rows, size_t cols, cudaStream_t stream);
 
+/* Device-side failure status of a plan (no counterpart in the reference ABI;
+ * the reference's kernels never wait on the device).  The tensor-core FWHT
+ * mapping waits on its own MMA completions with bounded waits; when one
+ * expires the launch stops, frees its tensor memory and records bit 0 in the
+ * plan's status word (bit 1: a launch invariant failed), and its output is
+ * invalid.  The next cubutterflyExecute / ExecuteSteady on that plan returns
+ * CUBUTTERFLY_STATUS_BACKEND_ERROR with the reason and clears the word.
+ * GetDeviceStatus reads the word (plan and child plans, OR-ed) without
+ * clearing or synchronising: it is final once the plan's stream has been
+ * synchronised.  Plans of other mappings always read 0. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterflyPlan_t plan, unsigned int* bits);
+
+/* Host-side test hook (no counterpart in the reference ABI): ORs `bits` into
+ * the plan's device status word as a failing launch would, so that callers
+ * can test their handling of the failure path without making a kernel fail.
+ * CUBUTTERFLY_STATUS_NOT_SUPPORTED for plans without a status word. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanInjectDeviceStatus(cubutterflyPlan_t plan, unsigned int bits);
+
 /* Allocation-free complex fp32 FFT (no counterpart in the reference ABI).
  * For callers that cannot allocate device memory -- fixed memory budgets or
  * pools that own every byte, hosts that forbid cudaMalloc/cudaFree on their
@@ -60,11 +78,12 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input
  * cubutterflyCreatePlan/Execute FFT (forward or inverse, optional 1/N,
  * natural order, in place when input == output) with scratch in a 16 MiB
  * device array inside the library: n a power of two in [2^14, 2^21],
- * n * batch <= 2^21 complex values (2^20 for in-place 2^21-point transforms);
- * larger sizes return CUBUTTERFLY_STATUS_INVALID_VALUE.  Pointers 16-byte
- * aligned.  Allocates nothing.  The first call on a device sets up that
- * device (symbol addresses, twiddle upload) and should precede any stream
- * capture.  Every call shares the scratch: calls that overlap on the GPU
+ * n * batch <= 2^21 complex values; in place (input == output) up to
+ * n = 2^20, n = 2^21 out of place only; input and output either equal or
+ * disjoint.  Other sizes return CUBUTTERFLY_STATUS_INVALID_VALUE.  Pointers
+ * 16-byte aligned.  Allocates nothing.  The first call on a device sets up
+ * that device (symbol addresses, twiddle upload, a wait for the upload) and
+ * should precede any stream capture.  Every call shares the scratch: calls that overlap on the GPU
  * race, so serialise them on one stream. */
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FftC2CNoAlloc(const void* input, void* output, size_t n,
                                                                size_t batch, int inverse, int normalize,

@@ -139,27 +139,76 @@ ORACLE_API int cubf_oracle_fft_c64(double* data, size_t n, size_t batch, int inv
     return 0;
 }
 
-/* Direct O(n) evaluation of selected DFT bins in long double, an independent
- * truth for spot checks of very long transforms. */
+/* Selected bins of the DFT of one complex fp32 vector, in long double:
+ * X[k] = sum_j x[j] W^(j k), W = exp(-+2 pi i / n), the definition every FFT
+ * here is held to (the reference's reference_fft, src/butterfly_reference.cpp:
+ * 392-433, computes the same sums by radix-2 stages).  j k is reduced mod n
+ * exactly (incrementally: m += k mod n per term), and W^m is formed from a
+ * two-level table of long-double unit roots, W^m = W^(hi 2^s) W^lo with
+ * m = hi 2^s + lo, so a bin of a 2^30-point vector costs table loads and one
+ * long-double complex product per term (relative error ~1e-19 per term).  Each
+ * bin is summed in fixed chunks on all threads, then the chunk sums in order. */
 ORACLE_API void cubf_oracle_dft_bins(const float* data, size_t n, const size_t* bins, size_t count,
                                      int inverse, double* out) {
     const long double kPi = 3.141592653589793238462643383279502884L;
-#pragma omp parallel for schedule(static)
-    for (size_t i = 0; i < count; ++i) {
-        const size_t k = bins[i];
+    unsigned s = 0;
+    while (((size_t)1 << (2 * s)) < n) ++s; /* 2^s >= sqrt(n) */
+    const size_t lo_n = (size_t)1 << s, hi_n = (n + lo_n - 1) / lo_n;
+    long double* lo = (long double*)malloc(2 * lo_n * sizeof(long double));
+    long double* hi = (long double*)malloc(2 * hi_n * sizeof(long double));
+    enum { kChunks = 256 };
+    long double* part = (long double*)malloc(2 * kChunks * (count ? count : 1) * sizeof(long double));
+    if (!lo || !hi || !part) {
+        free(lo);
+        free(hi);
+        free(part);
+        for (size_t i = 0; i < 2 * count; ++i) out[i] = NAN;
+        return;
+    }
+    const long double sign = inverse ? 2.0L : -2.0L;
+    for (size_t m = 0; m < lo_n; ++m) {
+        const long double a = sign * kPi * (long double)(m % n) / (long double)n;
+        lo[2 * m] = cosl(a);
+        lo[2 * m + 1] = sinl(a);
+    }
+    for (size_t h = 0; h < hi_n; ++h) {
+        const long double a = sign * kPi * (long double)((h * lo_n) % n) / (long double)n;
+        hi[2 * h] = cosl(a);
+        hi[2 * h + 1] = sinl(a);
+    }
+    const size_t chunk = (n + kChunks - 1) / kChunks;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (size_t t = 0; t < count * kChunks; ++t) {
+        const size_t i = t / kChunks, c = t % kChunks;
+        const size_t k = bins[i] % n;
+        const size_t j0 = c * chunk, j1 = j0 + chunk < n ? j0 + chunk : n;
+        size_t m = (size_t)(((u128)j0 * k) % n);
         long double sr = 0, si = 0;
-        for (size_t j = 0; j < n; ++j) {
-            /* reduce j*k mod n exactly before forming the angle */
-            const size_t m = (size_t)(((u128)j * k) % n);
-            const long double ang = (inverse ? 2.0L : -2.0L) * kPi * (long double)m / (long double)n;
-            const long double c = cosl(ang), s = sinl(ang);
+        for (size_t j = j0; j < j1; ++j) {
+            const long double* a = hi + 2 * (m >> s);
+            const long double* b = lo + 2 * (m & (lo_n - 1));
+            const long double c_ = a[0] * b[0] - a[1] * b[1], s_ = a[0] * b[1] + a[1] * b[0];
             const long double xr = data[2 * j], xi = data[2 * j + 1];
-            sr += xr * c - xi * s;
-            si += xr * s + xi * c;
+            sr += xr * c_ - xi * s_;
+            si += xr * s_ + xi * c_;
+            m += k;
+            if (m >= n) m -= n;
+        }
+        part[2 * t] = sr;
+        part[2 * t + 1] = si;
+    }
+    for (size_t i = 0; i < count; ++i) {
+        long double sr = 0, si = 0;
+        for (size_t c = 0; c < kChunks; ++c) {
+            sr += part[2 * (i * kChunks + c)];
+            si += part[2 * (i * kChunks + c) + 1];
         }
         out[2 * i] = (double)sr;
         out[2 * i + 1] = (double)si;
     }
+    free(lo);
+    free(hi);
+    free(part);
 }
 
 /* Direct DFT of any length in long double, rows of n complex doubles:

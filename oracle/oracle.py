@@ -35,12 +35,19 @@ def _ptr(a: np.ndarray):
     return a.ctypes.data_as(ct.c_void_p)
 
 
+def default_reference_root() -> str:
+    """The reference tree: $CUBF_REFERENCE_ROOT, else a `reference` directory
+    beside this repository (absent on hosts that only run the prebuilt files)."""
+    env = os.environ.get("CUBF_REFERENCE_ROOT")
+    return env if env else str(HERE.parent.parent / "reference")
+
+
 def build(reference_root: str | None = None, quiet: bool = True) -> None:
     """Compile the checkers (the reference one only when its sources exist)."""
     import subprocess
 
     targets = ["oracle"]
-    ref = reference_root or os.environ.get("CUBF_REFERENCE_ROOT", "/root/reference")
+    ref = reference_root or default_reference_root()
     if Path(ref, "src", "butterfly_reference.cpp").exists():
         targets.append("ref")
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={ref}", *targets], check=True,

@@ -32,7 +32,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_reference_abi_surface_is_complete():
-    """Every entry point of the reference header (SURVEY 8b list) is declared here."""
+    """Every entry point of the reference header is declared here."""
     reference = """GetStatusString GetLastErrorString GetVersion Create Destroy SetStream GetStream SetLogCallback
     SetCachePath PackRealFp32 ExpandHermitianFp32 CreateDescriptor DestroyDescriptor SetOperator SetDataType SetShape
     SetExecutionMode SetFftTransformType SetFftOutputScale SetOutputScale SetArithmeticPolicy SetOutputRounding

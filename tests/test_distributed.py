@@ -179,6 +179,70 @@ def test_four_step_two_gpus_nccl():
     assert all(err <= 2e-6 for err in results.values()), results
 
 
+def _nccl_worker_full_size(rank, world, port, log_n, q):
+    """Config 4 at its stated size: every rank makes the same seeded 2^log_n
+    input on its own GPU, runs the single-GPU plan on all of it (the
+    reference output), keeps its shard of input and output, then runs the
+    four-step over NCCL on the shard and reports the shard's relative L2."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import cubutterfly_b200 as cb
+        from cubutterfly_b200 import workloads as w
+
+        n = 1 << log_n
+        lo, cnt = shard_range(n, world, rank)
+        x = w.torch_fft_input(n, 1, dev, seed=30).reshape(n, 2)
+        y = torch.empty_like(x)
+        with cb.Plan(cb.load(), cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1),
+                     stream=torch.cuda.current_stream().cuda_stream) as plan:
+            ws = torch.empty(plan.workspace_size(), dtype=torch.uint8, device=dev)
+            plan.set_workspace(ws.data_ptr(), ws.numel())
+            plan.execute(x.data_ptr(), y.data_ptr())
+            torch.cuda.synchronize()
+        del ws
+        mine = x[lo:lo + cnt].clone()
+        want = y[lo:lo + cnt].clone()
+        del x, y
+        torch.cuda.empty_cache()
+        fs = FourStepFFT(n, device=dev)
+        got = fs(mine)
+        torch.cuda.synchronize()
+        fs.close()
+        num = den = 0.0
+        for i in range(0, cnt, 1 << 25):
+            a, b = got[i:i + (1 << 25)].double(), want[i:i + (1 << 25)].double()
+            num += float(torch.sum((a - b) ** 2))
+            den += float(torch.sum(b * b))
+        q.put((rank, (num / den) ** 0.5))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_four_step_two_gpus_config4_full_size():
+    """Config 4 (one 2^30-point FFT) split over two GPUs matches the
+    single-GPU plan on the same input, shard by shard, at 2e-6."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_nccl_worker_full_size, args=(r, 2, port, 30, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    print("four-step 2^30 over 2 GPUs vs single-GPU plan, rel L2 per rank:", results)
+    assert all(err <= 2e-6 for err in results.values()), results
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("rows, cols, row_offset, col_offset, inverse", [
     (64, 4096, 0, 8192, False),     # row path (>= 64 columns), 16 steps per warp

@@ -1,6 +1,8 @@
 """FFT parity on the GPU through the C ABI: rel L2 <= 2e-6 against the oracle
 (reference_fft<Complex32> semantics), plus bit-level checks against the
 golden fixtures made by the reference's own compiled oracle."""
+import os
+
 import numpy as np
 import pytest
 
@@ -216,3 +218,73 @@ def test_fft_fp64_matches_reference_and_composite(lib, oracle, reference, cuda):
     got, name = run(lib, t, x2.reshape(2, -1), cuda)
     want = oracle.fft_c64(np.swapaxes(oracle.fft_c64(x2), 1, 2).copy())
     assert rel_l2(got.reshape(2, 32, 64), np.swapaxes(want, 1, 2)) <= 1e-13, name
+
+
+# ---- config 4: one 2^30-point transform at its stated size -------------------------------
+def _rel_l2_dev(a, b, chunk=1 << 26):
+    """Relative L2 of two equal-shape device tensors, summed in fp64 over chunks."""
+    import torch
+
+    a, b = a.reshape(-1), b.reshape(-1)
+    num = den = 0.0
+    for i in range(0, a.numel(), chunk):
+        x, y = a[i:i + chunk].double(), b[i:i + chunk].double()
+        num += float(torch.sum((x - y) ** 2))
+        den += float(torch.sum(y * y))
+    return (num / den) ** 0.5
+
+
+def test_fft_config4_2e30_single_gpu(lib, oracle, cuda):
+    """Config 4 on one GPU at full size (8 GiB in, 8 GiB out): 16 random bins
+    against the oracle's long-double direct DFT, the inverse round trip, and
+    every output against this library's fp64 FFT (bit-identical to the
+    reference's reference_fft<Complex64> at the sizes the CPU can check)."""
+    import torch
+
+    n = 1 << 30
+    x = w.torch_fft_input(n, 1, cuda, seed=4).reshape(n, 2)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def planned(t, src):
+        with cb.Plan(lib, t, stream=stream) as p:
+            ws = torch.empty(max(p.workspace_size(), 16), dtype=torch.uint8, device=cuda)
+            if p.workspace_size():
+                p.set_workspace(ws.data_ptr(), p.workspace_size())
+            dst = torch.empty(p.output_size() // src.element_size(), dtype=src.dtype, device=cuda)
+            p.execute(src.data_ptr(), dst.data_ptr())
+            torch.cuda.synchronize()
+            return dst.reshape(src.shape), p.algorithm_name()
+
+    y, name = planned(fft_transform(n, 1), x)
+    bins = np.sort(w.rng(78).integers(0, n, size=16))
+    got = y[torch.as_tensor(bins, device=cuda)].cpu().numpy().view(np.complex64).reshape(-1)
+    host_x = x.cpu().numpy().view(np.complex64).reshape(-1)
+    ref = oracle.dft_bins(host_x, bins)
+    del host_x
+    assert rel_l2(got, ref) <= TOL, name
+    back, _ = planned(fft_transform(n, 1, inverse=True, normalize=True), y)
+    assert _rel_l2_dev(back, x) <= TOL
+    del back
+    t64 = cb.Transform(op=cb.Operator.FFT, storage=cb.DataType.COMPLEX_FP64, compute=cb.ComputeType.FP64,
+                       extents=[n], batch=1)
+    y64, name64 = planned(t64, x.double())
+    assert _rel_l2_dev(y, y64) <= TOL, (name, name64)
+
+
+def test_four_step_2e24_matches_the_reference_fft(cuda, reference):
+    """The four-step decomposition (one rank) at 2^24 against the reference's
+    own reference_fft<Complex32> (src/butterfly_reference.cpp:392-473),
+    compiled unchanged into oracle/_ref."""
+    import torch
+
+    from cubutterfly_b200.distributed import FourStepFFT
+
+    n = 1 << 24
+    x = w.fft_input(n, 1, seed=124)[0]
+    fs = FourStepFFT(n, device=cuda)
+    got = fs(torch.from_numpy(x.view(np.float32).reshape(n, 2).copy()).to(cuda))
+    torch.cuda.synchronize()
+    fs.close()
+    got = got.cpu().numpy().view(np.complex64).reshape(-1)
+    want = reference.fft_c32(x[None], threads=os.cpu_count() or 1)[0]
+    assert rel_l2(got, want) <= TOL

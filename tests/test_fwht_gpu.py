@@ -142,6 +142,43 @@ def test_fwht_tcgen05_config1_full_size(lib, oracle, cuda):
     assert np.mean(got == want) > 0.99
 
 
+def test_fwht_tcgen05_device_failure_reaches_the_caller(lib, oracle, cuda):
+    """A failure the tensor-core kernel records on the device (an expired
+    MMA-completion wait) is the status of the next Execute on that plan.  The
+    failure is planted through the host-side hook, never by a failing kernel:
+    the clean launch reports 0, the planted bits make the next Execute return
+    BACKEND_ERROR and are cleared by it, and the plan then runs normally."""
+    import torch
+
+    from gpu_util import from_device, to_device
+
+    bits = w.fwht_input_bits(8, 4096, seed=11)
+    want = oracle.fwht_bf16_final(bits, 1 / 64)
+    with cb.Plan(lib, bf16_transform(4096, 8, 1 / 64), options=TC,
+                 stream=torch.cuda.current_stream().cuda_stream) as plan:
+        assert plan.algorithm_name() == "fwht-tcgen05[6+6]"
+        x = to_device(bits, cuda)
+        y = torch.empty_like(x)
+        plan.execute(x.data_ptr(), y.data_ptr())
+        torch.cuda.synchronize()
+        assert plan.device_status() == 0
+        plan.inject_device_status(1)
+        assert plan.device_status() == 1
+        with pytest.raises(cb.Error) as e:
+            plan.execute(x.data_ptr(), y.data_ptr())
+        assert e.value.status == cb.Status.BACKEND_ERROR
+        assert "completion wait expired" in str(e.value)
+        assert plan.device_status() == 0
+        y.zero_()
+        plan.execute_steady(x.data_ptr(), y.data_ptr())
+        torch.cuda.synchronize()
+        assert np.array_equal(from_device(y, np.uint16, bits.shape), want) or \
+            rel_l2(f32(from_device(y, np.uint16, bits.shape)), f32(want)) <= TOL_BF16
+    with cb.Plan(lib, bf16_transform(4096, 8, 1 / 64), stream=torch.cuda.current_stream().cuda_stream) as simt:
+        if simt.algorithm_name() != "fwht-tcgen05[6+6]":
+            assert simt.device_status() == 0
+
+
 # ---- native stage-storage FWHT (bf16 / fp16 NATIVE compute) --------------------------
 @pytest.mark.parametrize("storage", [cb.DataType.BF16, cb.DataType.FP16])
 @pytest.mark.parametrize("n", [2, 256, 4096, 1 << 14])

@@ -86,26 +86,3 @@ def test_operators_reject_bad_tensors(cuda):
         torch_ops.fwht(x, out=x)  # aliasing
     with pytest.raises(ValueError):
         torch_ops.fft(torch.randn(4, 64, device=cuda))  # not complex
-
-
-@pytest.mark.parametrize("n", [32, 64])
-@pytest.mark.parametrize("scale", [1.0, 0.375, -0.75])
-def test_fused_short_fwht_contract(oracle, cuda, n, scale):
-    """The reference's short FP16 FWHT provider contract
-    (python/cubutterfly/fused_short_fwht.py): FP16 storage, FP32 arithmetic,
-    the caller's scale, one rounding to FP16 (the cases of the reference's
-    tests/test_fwht_final_storage.py)."""
-    from cubutterfly_b200.fused_short_fwht import FusedShortFWHT, descriptor, prepare
-
-    assert prepare()["supported_n"] == [32, 64] and descriptor()["logN"] == [5, 6]
-    x = (w.rng(95, n).integers(-1024, 1025, size=(6, n)).astype(np.float32) / 1024).astype(np.float16)
-    fused = FusedShortFWHT()
-    got = fused(torch.from_numpy(x).to(cuda), scale)
-    torch.cuda.synchronize()
-    want = (oracle.fwht_f64(x.astype(np.float64), normalize=False) * scale).astype(np.float16)
-    assert rel_l2(got.cpu().numpy().astype(np.float64), want.astype(np.float64)) <= 1e-3
-    with pytest.raises(ValueError):
-        fused(torch.zeros((2, 128), dtype=torch.float16, device=cuda), 1.0)
-    v = torch.zeros((2, 32), dtype=torch.float16, device=cuda)
-    with pytest.raises(ValueError):
-        fused(v, 1.0, out=v)

@@ -586,6 +586,9 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline == "auto":
         cpu = cpu_baseline()
+        for name, base in op_cpu_baselines().items():
+            if name in ops:
+                ops[name]["cpu_baseline"] = base
 
     if world > 1:
         dist.barrier()
@@ -690,6 +693,15 @@ def measure_ops(cb, lib, dev, stream, peak, steps, warmup):
         b = 2 * w.NTT_LIMBS * (1 << w.NTT_LOG_N) * 8
         ops["rns_ntt_u64_32x2^16"] = {"gbs": round(b / ms / 1e6, 1), "frac": round(b / ms / 1e6 / peak, 4),
                                       "us": round(ms * 1e3, 2), "algorithm": "b200_two_pass_tile"}
+        # integer roof: the measured rate of the same lazy butterfly from registers
+        import ctypes as ct
+        rate = ct.c_double()
+        lib.invoke("B200NttButterflyPeak", max(qs), ct.byref(rate))
+        butterflies = w.NTT_LIMBS * (1 << (w.NTT_LOG_N - 1)) * w.NTT_LOG_N
+        ops["rns_ntt_u64_32x2^16"].update(
+            butterflies_per_s=round(butterflies / (ms * 1e-3), 1), butterfly_peak_per_s=round(rate.value, 1),
+            imad_frac=round(butterflies / (ms * 1e-3) / rate.value, 4) if rate.value else None,
+            imad_peak_kind="measured: cubutterflyB200NttButterflyPeak (the pass's lazy butterfly from registers)")
     # the same shape as one cyclic single-modulus NTT plan of the main ABI:
     # natural -> bit-reversed (two passes) and natural -> natural (a
     # bit-reversal permutation first)
@@ -717,6 +729,65 @@ def measure_ops(cb, lib, dev, stream, peak, steps, warmup):
                                "us": round(ms * 1e3, 2), "algorithm": p.algorithm_name()}
     del x, y, ws
     return ops
+
+
+def op_cpu_baselines():
+    """The reference's own CPU code (oracle/_ref) on the other configurations,
+    all host threads, each a bounded sample of a second or two: config 0
+    reference_fft<Complex32> over the 1024 transforms; config 2 twist +
+    reference_ntt + bit reversal per limb; config 3 reference_subset_zeta over
+    the 16 transforms; config 4 one 2^24-point reference_fft<Complex32>
+    (the reference runs one transform on one thread), scaled to 2^30 by
+    N log N.  Reported beside each op, never required."""
+    try:
+        import numpy as np
+
+        from cubutterfly_b200 import workloads as w
+        from oracle.oracle import Reference
+
+        if not Reference.available():
+            return {}
+        ref = Reference()
+        threads = os.cpu_count() or 1
+
+        def timed(fn, budget=1.5):
+            fn()
+            t0, reps = time.perf_counter(), 0
+            while reps < 1 or time.perf_counter() - t0 < budget:
+                fn()
+                reps += 1
+            return (time.perf_counter() - t0) / reps, reps
+
+        def entry(nbytes, t, reps, sample, cores=threads):
+            return {"value": round(nbytes / t / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "reference",
+                    "sample": f"{sample}; {reps} repetitions"}
+
+        out = {}
+        x = w.fft_input(w.FFT_N, w.FFT_BATCH, seed=0)
+        t, r = timed(lambda: ref.fft_c32(x, threads=threads))
+        out["fft_c64_4096x1024"] = entry(2 * x.nbytes, t, r, "reference_fft<Complex32>, all 1024 transforms")
+        cfg = w.rns_config()
+        qs = [d["modulus"] for d in cfg["domains"]]
+        v = w.ntt_input(qs, seed=0)
+        t, r = timed(lambda: ref.negacyclic_ntt(v, qs, threads=threads))
+        out["rns_ntt_u64_32x2^16"] = entry(2 * v.nbytes, t, r, "twist + reference_ntt + bit reversal, all 32 limbs")
+        q = 576460756061519873
+        t, r = timed(lambda: ref.ntt_cyclic(v, q, threads=threads))
+        for tag in ("nr", "nn"):
+            out[f"ntt_cyclic_u64_32x2^16_{tag}"] = entry(2 * v.nbytes, t, r, "reference_ntt (natural order), 32 rows")
+        z = w.zeta_input(w.ZETA_LOG_N, w.ZETA_BATCH, seed=0)
+        t, r = timed(lambda: ref.zeta_u32(z, threads=threads), budget=2.0)
+        out["zeta_u32_2^24x16"] = entry(2 * z.nbytes, t, r, "reference_subset_zeta, all 16 transforms")
+        del z
+        big = w.fft_input(1 << 24, 1, seed=4)
+        t, r = timed(lambda: ref.fft_c32(big, threads=1), budget=2.0)
+        t30 = t * (2 ** 30 * 30) / (2 ** 24 * 24)
+        out["fft_c64_2^30"] = entry(2 * 8 * 2 ** 30, t30, r, "one 2^24-point reference_fft<Complex32>, time "
+                                    "scaled by N log N to 2^30", cores=1)
+        return out
+    except Exception as e:  # the baselines are reported, never required
+        return {"error": {"value": None, "unit": "GB/s", "cores": os.cpu_count(), "kind": "unavailable",
+                          "sample": str(e)}}
 
 
 def cpu_baseline():

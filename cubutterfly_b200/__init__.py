@@ -255,6 +255,7 @@ B200FourStepTwiddle        p z z z z z i p
 B200PermuteBlocksC64       p p p p z z z z p
 B200TransposeC64           p p z z z p
 B200FftC2CNoAlloc          p p z z i i p
+B200NttButterflyPeak       q D
 """
 
 

@@ -26,6 +26,7 @@ ARG = {
     "z": ct.c_size_t,
     "Z": ct.POINTER(ct.c_size_t),
     "d": ct.c_double,
+    "D": ct.POINTER(ct.c_double),
     "s": ct.c_char_p,
 }
 

@@ -43,7 +43,8 @@ def _units():
               "--expt-relaxed-constexpr", f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{_json_include()}"]
     units = []
     for name in ("c_api.cpp", "descriptor.cpp", "planner.cpp", "rns_api.cpp", "launch_bitwise_dispatch.cpp",
-                 "launch_ntt_dispatch.cpp", "launch_fft.cu", "noalloc.cu", "fourstep.cu", "bitrev.cu", "fwht_tc.cu", "real_adapter.cu", "real_fft.cu", "structured.cu", "fwht_native.cu", "fft64.cu",
+                 "launch_ntt_dispatch.cpp", "launch_fft.cu", "noalloc.cu", "fourstep.cu", "bitrev.cu", "fwht_tc.cu",
+                 "real_adapter.cu", "real_fft.cu", "calibrate.cu", "structured.cu", "fwht_native.cu", "fft64.cu",
                  "heongpu_adapter.cpp", "bluestein.cu"):
         src = CSRC / name
         obj = OBJ / (src.stem + ".o")

@@ -1996,6 +1996,13 @@ cubutterflyStatus_t cubutterflyCreatePlan(cubutterflyHandle_t handle, cubutterfl
                  : d.rank == 1                                                        ? create_axis(handle, d)
                                                                                       : create_composite(handle, d);
         log_event(handle, CUBUTTERFLY_LOG_INFO, "plan-selected", p->reason);
+        if (p->source == CUBUTTERFLY_SELECTION_STATIC_MODEL) {
+            // no measurement backs this choice on this device: say so, and
+            // how to get one (the reference's "workload-profile-miss" event)
+            log_event(handle, CUBUTTERFLY_LOG_WARNING, "workload-profile-miss",
+                      "no measured mapping for this workload on " + p->hw.name + "; using the static model's " +
+                          p->reason + "; select MEASURE with a cache path to calibrate it");
+        }
         *plan = p.release();
     });
 }

@@ -70,6 +70,14 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanGetDeviceStatus(cubutterfl
  * CUBUTTERFLY_STATUS_NOT_SUPPORTED for plans without a status word. */
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PlanInjectDeviceStatus(cubutterflyPlan_t plan, unsigned int bits);
 
+/* Integer roof of the NTT butterfly (no counterpart in the reference ABI;
+ * a measurement aid).  Runs the forward lazy Cooley-Tukey butterfly of the
+ * NTT tile passes (Shoup product, values in [0, 4q)) from registers on every
+ * SM of the current device and writes the best rate seen, in butterflies per
+ * second, to *per_second.  modulus in [3, 2^62).  Synchronous (about 0.1 s);
+ * call it outside timed regions and stream capture. */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200NttButterflyPeak(unsigned long long modulus, double* per_second);
+
 /* Allocation-free complex fp32 FFT (no counterpart in the reference ABI).
  * For callers that cannot allocate device memory -- fixed memory budgets or
  * pools that own every byte, hosts that forbid cudaMalloc/cudaFree on their

@@ -50,6 +50,9 @@ def build(reference_root: str | None = None, quiet: bool = True) -> None:
     ref = reference_root or default_reference_root()
     if Path(ref, "src", "butterfly_reference.cpp").exists():
         targets.append("ref")
+    lib = HERE.parent / "cubutterfly_b200" / "lib" / "libcubutterfly_b200.so"
+    if Path(ref, "tests", "test_c_api.c").exists() and lib.exists():
+        targets.append("ctest")  # the reference's C API test against the built library
     subprocess.run(["make", "-s", "-C", str(HERE), f"REF={ref}", *targets], check=True,
                    stdout=subprocess.DEVNULL if quiet else None)
 

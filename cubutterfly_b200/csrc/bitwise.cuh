@@ -463,24 +463,26 @@ CUBF_DEV void exchange_groups(typename S::TC (&v)[S::E], typename S::TC* tbuf, u
 // stride 1, log_inner ignored).  `in` and `out` may alias (every tile reads all its elements before
 // writing any).  Floating-point results are multiplied by `scale` before the
 // final narrowing (the FINAL_STORAGE epilogue).
-template <typename Op, typename TS, typename TC, int LOGH, int LOGW, int LOGE>
-__global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
-                                  (512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB > 0
-                                       ? 512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB
-                                       : 1))
-    bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale,
-                        int cache_mode, unsigned prefetch_stride) {
+//
+// tile_pass is the work of one CTA of such a pass: CTA `vblock` of `vgrid`,
+// run by threads vtid = 0 .. TPB-1 with its shared memory at `smem_raw`.  The
+// one-shot kernel below passes blockIdx / threadIdx; the persistent chain
+// kernel passes queue items.  COHERENT reads through L2 only (data that other
+// CTAs of the same launch wrote).
+template <typename Op, typename TS, typename TC, int LOGH, int LOGW, int LOGE, bool COHERENT>
+CUBF_DEV void tile_pass(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale, int cache_mode,
+                        unsigned prefetch_stride, size_t vblock, size_t vgrid, uint32_t vtid,
+                        unsigned char* smem_raw) {
     using S = TileShape<TS, TC, LOGH, LOGW, LOGE>;
     constexpr Groups G = S::G;
     constexpr int LT = S::LT;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
 
-    const int local = threadIdx.x / S::TPT;
-    const uint32_t t = threadIdx.x % S::TPT;
+    const int local = vtid / S::TPT;
+    const uint32_t t = vtid % S::TPT;
     // Contiguous tiles (LOGW == 0) have row stride 1; strided tiles 2^log_inner.
     const int li = LOGW == 0 ? 0 : log_inner;
     const size_t col_blocks = size_t{1} << (li - LOGW);
-    const size_t tile = static_cast<size_t>(blockIdx.x) * S::TILES + local;
+    const size_t tile = vblock * S::TILES + local;
     const bool active = tile < outer * col_blocks;
     const size_t o = active ? tile >> (li - LOGW) : 0;
     const size_t cb = active ? tile & (col_blocks - 1) : 0;
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
             if constexpr (S::V > 1) {
                 Vec16<TS> x;
                 if (active) {
-                    const uint4 w = ld16_hint(tin + addr(e), ld_pol);
+                    const uint4 w = COHERENT ? ld16_hint_cg(tin + addr(e), ld_pol) : ld16_hint(tin + addr(e), ld_pol);
                     x = *reinterpret_cast<const Vec16<TS>*>(&w);
                 } else {
 #pragma unroll
@@ -520,14 +522,15 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
 #pragma unroll
                 for (int i = 0; i < S::V; ++i) v[q * S::V + i] = Convert<TS, TC>::load(x.v[i]);
             } else {
-                v[q] = Convert<TS, TC>::load(active ? tin[addr(e)] : TS{});
+                v[q] = Convert<TS, TC>::load(active ? (COHERENT ? __ldcg(tin + addr(e)) : tin[addr(e)]) : TS{});
             }
         }
     }
     if constexpr (LOGW == 0) {  // loads issued: prefetch the rows of the CTA one resident wave later
         constexpr size_t row_bytes = (size_t{1} << LOGH) * sizeof(TS);
         const size_t rem = outer % S::TILES;
-        prefetch_next_wave(in, S::TILES * row_bytes, (rem ? rem : S::TILES) * row_bytes, prefetch_stride);
+        prefetch_wave_of(in, S::TILES * row_bytes, (rem ? rem : S::TILES) * row_bytes, prefetch_stride, vblock, vgrid,
+                         vtid);
     }
     apply_group<Op, S::LOGE, G.reg[0], G.stage[0]>(v, inverse);
     exchange_groups<Op, S, 1>(v, tbuf, t, inverse);
@@ -576,6 +579,19 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
 #pragma unroll
         for (int r = 0; r < S::E; ++r) tout[addr(tf | OF.v[r])] = narrow(v[r]);
     }
+}
+
+
+template <typename Op, typename TS, typename TC, int LOGH, int LOGW, int LOGE>
+__global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
+                                  (512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB > 0
+                                       ? 512 / TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB
+                                       : 1))
+    bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale,
+                        int cache_mode, unsigned prefetch_stride) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    tile_pass<Op, TS, TC, LOGH, LOGW, LOGE, false>(in, out, outer, log_inner, inverse, scale, cache_mode,
+                                                   prefetch_stride, blockIdx.x, gridDim.x, threadIdx.x, smem_raw);
 }
 
 }  // namespace cubf::bw

@@ -67,31 +67,6 @@ struct cubutterflyPlan {
     unsigned int* status_dev = nullptr;
     cudaStream_t steady_stream = nullptr;
     bool steady_ready = false;
-    // Chained multi-pass bitwise plans over several L2 chunks: the first pass
-    // of chunk c+1 runs on lanes[0] while the later passes of chunk c run on
-    // lanes[1] (fork/join through events on the caller's stream).
-    cudaStream_t lanes[2] = {nullptr, nullptr};
-    cudaEvent_t ev_fork = nullptr, ev_handoff = nullptr, ev_done[2] = {nullptr, nullptr};
-    cudaEvent_t ev_join[2] = {nullptr, nullptr};
-    // Graphs of chunk-overlapped chains, keyed by buffers and mapping (least
-    // recently used evicted), captured on `capture`.
-    struct ChainGraphCache {
-        static constexpr std::size_t kEntries = 4;
-        struct Entry {
-            const void* in;
-            void* out;
-            const cubf::Mapping* mapping;
-            cudaGraphExec_t exec;
-            unsigned long long used;
-        };
-        std::vector<Entry> entries;
-        const void* last_in = nullptr;
-        void* last_out = nullptr;
-        const cubf::Mapping* last_mapping = nullptr;
-        unsigned long long clock = 0;
-    };
-    mutable ChainGraphCache chain_graphs;
-    cudaStream_t capture = nullptr;
     // Rank two and three: packed rank-one child plans.  FFT / NTT: one per
     // axis, innermost first, each run in place on a packed copy of the tensor
     // (axes other than the innermost transposed innermost through a second
@@ -135,12 +110,6 @@ struct cubutterflyPlan {
         if (ntt_block) cudaFree(ntt_block);
         if (real_tw) cudaFree(real_tw);
         if (bluestein_tables) cudaFree(bluestein_tables);
-        for (auto e : {ev_fork, ev_handoff, ev_done[0], ev_done[1], ev_join[0], ev_join[1]})
-            if (e) cudaEventDestroy(e);
-        for (const auto& g : chain_graphs.entries) cudaGraphExecDestroy(g.exec);
-        for (auto l : lanes)
-            if (l) cudaStreamDestroy(l);
-        if (capture) cudaStreamDestroy(capture);
         if (status_host) cudaFreeHost(status_host);
     }
 };
@@ -591,30 +560,35 @@ std::size_t chain_chunk(const cubutterflyPlan& p, const cubf::Mapping& m) {
     return std::max<std::size_t>(1, budget / transform_bytes);
 }
 
-bool chain_overlaps(const cubutterflyPlan& p, const cubf::Mapping& m) {
-    return m.passes.size() > 1 && p.lanes[0] && p.desc.batch > chain_chunk(p, m);
-}
-
 // Bitwise tile passes: the first reads the input, the rest run in place.
+// Multi-pass chains run chunk by chunk (every pass over a chunk of transforms
+// sized to stay in L2, so the intermediate one pass writes is read by the
+// next from L2 instead of HBM).  Two-pass chains over several chunks overlap
+// pass A of chunk c+1 with pass B of chunk c, one launch per step
+// (csrc/chain.cuh); other chains launch pass by pass, chunk by chunk.  All
+// launches go to the caller's stream.
 void enqueue_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
                    cudaStream_t stream, double scale) {
-    // Multi-pass chains run chunk by chunk: every pass over a chunk of
-    // transforms sized to stay in L2, so the intermediate written by one pass
-    // is read by the next from L2 instead of HBM.
     const auto& d = p.desc;
     const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
     const std::size_t n = d.extents[0];
     const std::size_t transform_bytes = n * cubf::bw_type_bytes(p.req.bw_type);
     const bool chained = m.passes.size() > 1;
     const std::size_t chunk = chain_chunk(p, m);
-    const bool overlap = chain_overlaps(p, m);
-    if (overlap) {
-        check_cuda(cudaEventRecord(p.ev_fork, stream), "fork");
-        check_cuda(cudaStreamWaitEvent(p.lanes[0], p.ev_fork, 0), "fork");
-        check_cuda(cudaStreamWaitEvent(p.lanes[1], p.ev_fork, 0), "fork");
+    if (m.passes.size() == 2 && d.batch > chunk &&
+        cubf::bw_chain_available(p.req.bw_op, p.req.bw_type, m.passes[0].log_h, m.passes[1].log_h)) {
+        cubf::BwChain c;
+        c.n = n;
+        c.batch = d.batch;
+        c.chunk = chunk;
+        c.log_h0 = m.passes[0].log_h;
+        c.log_h1 = m.passes[1].log_h;
+        c.inverse = inverse;
+        c.scale = static_cast<float>(scale);
+        check_cuda(cubf::launch_bw_chain(p.req.bw_op, p.req.bw_type, c, in, out, stream), "chain launch");
+        return;
     }
-    std::size_t c = 0;
-    for (std::size_t b0 = 0; b0 < d.batch; b0 += chunk, ++c) {
+    for (std::size_t b0 = 0; b0 < d.batch; b0 += chunk) {
         const std::size_t nb = std::min(chunk, d.batch - b0);
         const void* src = static_cast<const unsigned char*>(in) + b0 * transform_bytes;
         void* dst = static_cast<unsigned char*>(out) + b0 * transform_bytes;
@@ -626,79 +600,12 @@ void enqueue_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const void*
             const std::size_t inner_arg = ps.log_w == 0 ? 1 : inner;
             const std::size_t outer_arg = ps.log_w == 0 ? outer * inner : outer;
             const int mode = !chained ? 0 : (i == 0 ? 1 : (last ? 2 : 3));
-            cudaStream_t s = stream;
-            if (overlap) {
-                s = p.lanes[i == 0 ? 0 : 1];
-                // the first pass runs at most one chunk ahead of the others (L2 holds two chunks)
-                if (i == 0 && c >= 2) check_cuda(cudaStreamWaitEvent(s, p.ev_done[c & 1], 0), "chunk order");
-                if (i == 1) check_cuda(cudaStreamWaitEvent(s, p.ev_handoff, 0), "chunk handoff");
-            }
             check_cuda(cubf::launch_bw({p.req.bw_op, p.req.bw_type, ps.log_h, ps.log_w}, src, dst, outer_arg,
-                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, s),
+                                       inner_arg, inverse, last ? static_cast<float>(scale) : 1.0f, mode, stream),
                        "tile pass launch");
-            if (overlap && i == 0) check_cuda(cudaEventRecord(p.ev_handoff, s), "chunk handoff");
-            if (overlap && last) check_cuda(cudaEventRecord(p.ev_done[c & 1], s), "chunk done");
             src = dst;
         }
     }
-    if (overlap) {
-        check_cuda(cudaEventRecord(p.ev_join[0], p.lanes[0]), "join");
-        check_cuda(cudaEventRecord(p.ev_join[1], p.lanes[1]), "join");
-        check_cuda(cudaStreamWaitEvent(stream, p.ev_join[0], 0), "join");
-        check_cuda(cudaStreamWaitEvent(stream, p.ev_join[1], 0), "join");
-    }
-}
-
-// A chunk-overlapped chain executed twice in a row on the same buffers is
-// captured once into a CUDA graph and from then on launched as that graph:
-// the cross-lane dependencies then resolve on the device instead of through
-// host-enqueued event waits, whose timing let the two lanes settle into
-// slower interleavings.  Returns false where the chain runs directly: no
-// overlap, graphs disabled, the first call on these buffers (which also
-// primes every kernel's launch setup before any capture), or a caller that
-// is itself capturing the stream (the direct enqueue is capturable).
-bool launch_chain_graph(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out,
-                        cudaStream_t stream, double scale) {
-    if (!p.capture || !chain_overlaps(p, m)) return false;
-    cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
-    check_cuda(cudaStreamIsCapturing(stream, &status), "stream capture status");
-    if (status != cudaStreamCaptureStatusNone) return false;
-    auto& cache = p.chain_graphs;
-    ++cache.clock;
-    for (auto& g : cache.entries)
-        if (g.in == in && g.out == out && g.mapping == &m) {
-            g.used = cache.clock;
-            check_cuda(cudaGraphLaunch(g.exec, stream), "chain graph launch");
-            return true;
-        }
-    const bool repeat = cache.last_in == in && cache.last_out == out && cache.last_mapping == &m;
-    cache.last_in = in;
-    cache.last_out = out;
-    cache.last_mapping = &m;
-    if (!repeat) return false;
-    cudaGraph_t graph = nullptr;
-    check_cuda(cudaStreamBeginCapture(p.capture, cudaStreamCaptureModeThreadLocal), "chain capture");
-    try {
-        enqueue_chain(p, m, in, out, p.capture, scale);
-    } catch (...) {
-        cudaStreamEndCapture(p.capture, &graph);
-        if (graph) cudaGraphDestroy(graph);
-        throw;
-    }
-    check_cuda(cudaStreamEndCapture(p.capture, &graph), "chain capture");
-    cudaGraphExec_t exec = nullptr;
-    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    check_cuda(e, "chain graph instantiate");
-    if (cache.entries.size() >= cubutterflyPlan::ChainGraphCache::kEntries) {
-        auto lru = std::min_element(cache.entries.begin(), cache.entries.end(),
-                                    [](const auto& a, const auto& b) { return a.used < b.used; });
-        cudaGraphExecDestroy(lru->exec);
-        cache.entries.erase(lru);
-    }
-    cache.entries.push_back({in, out, &m, exec, cache.clock});
-    check_cuda(cudaGraphLaunch(exec, stream), "chain graph launch");
-    return true;
 }
 
 void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
@@ -771,23 +678,9 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
                    "tensor FWHT launch");
         return;
     }
-    if (!launch_chain_graph(p, m, in, out, stream, scale)) enqueue_chain(p, m, in, out, stream, scale);
+    enqueue_chain(p, m, in, out, stream, scale);
 }
 
-// Streams and events of the chunk-overlapped execution (chained bitwise plans
-// whose batch spans several L2 chunks), and the stream its graphs are
-// captured on.  CUBUTTERFLY_B200_CHUNK_OVERLAP=0 runs every chain on the
-// caller's stream; CUBUTTERFLY_B200_CHAIN_GRAPHS=0 keeps the overlap but
-// enqueues it directly on every call.
-void make_lanes(cubutterflyPlan& p) {
-    if (p.mapping.passes.size() < 2 || p.mapping.passes.front().kind != cubf::PassKind::BitwiseTile) return;
-    if (const char* v = std::getenv("CUBUTTERFLY_B200_CHUNK_OVERLAP"); v && std::string(v) == "0") return;
-    for (auto& l : p.lanes) check_cuda(cudaStreamCreateWithFlags(&l, cudaStreamNonBlocking), "lane stream");
-    for (auto* e : {&p.ev_fork, &p.ev_handoff, &p.ev_done[0], &p.ev_done[1], &p.ev_join[0], &p.ev_join[1]})
-        check_cuda(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "lane event");
-    if (const char* v = std::getenv("CUBUTTERFLY_B200_CHAIN_GRAPHS"); v && std::string(v) == "0") return;
-    check_cuda(cudaStreamCreateWithFlags(&p.capture, cudaStreamNonBlocking), "capture stream");
-}
 
 double time_mapping(cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, cudaStream_t stream,
                     int reps) {
@@ -1077,7 +970,6 @@ std::unique_ptr<cubutterflyPlan> create_rank1(cubutterflyHandle* handle, const c
     }
     build_tables(*p);  // before selection: MEASURE executes the candidates
     select_mapping(handle, *p);
-    make_lanes(*p);
     return p;
 }
 
@@ -2123,7 +2015,8 @@ void report_device_status(cubutterflyPlan& p) {
     clear_device_status(p);
     std::ostringstream o;
     o << "an earlier launch of this plan failed on the device (status bits 0x" << std::hex << bits
-      << "): " << ((bits & 1u) ? "a tensor-core completion wait expired" : "kernel launch invariant violated")
+      << "): "
+      << ((bits & 1u) ? "a tensor-core completion wait expired" : "kernel launch invariant violated")
       << "; that launch's output is invalid";
     throw std::runtime_error(o.str());
 }

@@ -145,6 +145,21 @@ CUBF_DEV void prefetch_next_wave(const void* base, size_t tile_bytes, size_t las
     }
 }
 
+// The same for an explicit (virtual) CTA `block` of `grid` run by threads
+// vtid = 0..: the persistent chain kernel runs tile passes as queue items.
+CUBF_DEV void prefetch_wave_of(const void* base, size_t tile_bytes, size_t last_bytes, unsigned stride,
+                               size_t block, size_t grid, uint32_t vtid) {
+    if (stride == 0 || vtid != 0) return;
+    const size_t next = block + stride;
+    if (next >= grid) return;
+    const size_t bytes = next + 1 == grid ? last_bytes : tile_bytes;
+    const unsigned char* p = static_cast<const unsigned char*>(base) + next * tile_bytes;
+    for (size_t off = 0; off < bytes; off += size_t{1} << 20) {
+        const size_t n = bytes - off < (size_t{1} << 20) ? bytes - off : (size_t{1} << 20);
+        prefetch_l2(p + off, static_cast<uint32_t>(n));
+    }
+}
+
 CUBF_DEV uint64_t l2_policy(bool keep) {
     uint64_t p;
     if (keep)
@@ -158,6 +173,16 @@ CUBF_DEV uint4 ld16_hint(const void* p, uint64_t pol) {
     asm volatile("ld.global.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p), "l"(pol));
+    return r;
+}
+// The same load served by L2 only (not L1): data another CTA wrote earlier in
+// the same kernel (the persistent chain kernel's second pass).
+CUBF_DEV uint4 ld16_hint_cg(const void* p, uint64_t pol) {
+    uint4 r;
+    asm volatile("ld.global.cg.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p), "l"(pol)
+                 : "memory");
     return r;
 }
 CUBF_DEV void st16_hint(void* p, uint4 v, uint64_t pol) {

@@ -74,6 +74,20 @@ LaunchShape bw_shape(const BwVariant& v);
 cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t outer, std::size_t inner,
                       bool inverse, float scale, int cache_mode, cudaStream_t stream);
 
+// Chunk-overlapped two-pass chain (csrc/chain.cuh), zeta operators: pass A
+// over the low log_h0 = bw_max_contiguous_log bits (contiguous tiles), pass B
+// over the remaining log_h1 bits (strided tiles), the batch cut into chunks of
+// `chunk` transforms whose intermediate stays in L2; chunks + 1 launches on
+// `stream`, step k running B of chunk k-1 beside A of chunk k.
+struct BwChain {
+    std::size_t n = 0, batch = 0, chunk = 0;
+    int log_h0 = 0, log_h1 = 0;
+    bool inverse = false;
+    float scale = 1.0f;
+};
+bool bw_chain_available(BwOp op, BwType type, int log_h0, int log_h1);
+cudaError_t launch_bw_chain(BwOp op, BwType type, const BwChain& c, const void* in, void* out, cudaStream_t stream);
+
 // ---- FWHT on the tensor cores (tcgen05) ------------------------------------------
 // 4096-point bf16 rows as H_64 (x) H_64 contractions (csrc/fwht_tc.cu); in may
 // equal out.  `status` (nullable; device-visible, normally mapped pinned host

@@ -7,7 +7,8 @@ namespace cubf {
     LaunchShape bw_unit_##OP##_##TY##_shape(int log_h, int log_w);                                      \
     cudaError_t bw_unit_##OP##_##TY##_launch(int log_h, int log_w, const void* in, void* out,          \
                                              std::size_t outer, std::size_t inner, bool inverse,       \
-                                             float scale, int cache_mode, cudaStream_t stream);
+                                             float scale, int cache_mode, cudaStream_t stream);        \
+    cudaError_t bw_unit_##OP##_##TY##_chain(const BwChain& c, const void* in, void* out, cudaStream_t stream);
 CUBF_DECLARE_UNIT(0, 0)
 CUBF_DECLARE_UNIT(0, 1)
 CUBF_DECLARE_UNIT(0, 2)
@@ -21,27 +22,29 @@ namespace {
 using ShapeFn = LaunchShape (*)(int, int);
 using LaunchFn = cudaError_t (*)(int, int, const void*, void*, std::size_t, std::size_t, bool, float, int,
                                  cudaStream_t);
+using ChainFn = cudaError_t (*)(const BwChain&, const void*, void*, cudaStream_t);
 struct Unit {
     ShapeFn shape;
     LaunchFn launch;
+    ChainFn chain;
 };
 Unit unit_of(BwOp op, BwType type) {
     switch (op) {
         case BwOp::Fwht:
-            if (type == BwType::F32) return {bw_unit_0_0_shape, bw_unit_0_0_launch};
-            if (type == BwType::BF16) return {bw_unit_0_1_shape, bw_unit_0_1_launch};
-            if (type == BwType::F16) return {bw_unit_0_2_shape, bw_unit_0_2_launch};
+            if (type == BwType::F32) return {bw_unit_0_0_shape, bw_unit_0_0_launch, bw_unit_0_0_chain};
+            if (type == BwType::BF16) return {bw_unit_0_1_shape, bw_unit_0_1_launch, bw_unit_0_1_chain};
+            if (type == BwType::F16) return {bw_unit_0_2_shape, bw_unit_0_2_launch, bw_unit_0_2_chain};
             break;
         case BwOp::ZetaSubset:
-            if (type == BwType::U32) return {bw_unit_1_3_shape, bw_unit_1_3_launch};
-            if (type == BwType::U64) return {bw_unit_1_4_shape, bw_unit_1_4_launch};
+            if (type == BwType::U32) return {bw_unit_1_3_shape, bw_unit_1_3_launch, bw_unit_1_3_chain};
+            if (type == BwType::U64) return {bw_unit_1_4_shape, bw_unit_1_4_launch, bw_unit_1_4_chain};
             break;
         case BwOp::ZetaSuperset:
-            if (type == BwType::U32) return {bw_unit_2_3_shape, bw_unit_2_3_launch};
-            if (type == BwType::U64) return {bw_unit_2_4_shape, bw_unit_2_4_launch};
+            if (type == BwType::U32) return {bw_unit_2_3_shape, bw_unit_2_3_launch, bw_unit_2_3_chain};
+            if (type == BwType::U64) return {bw_unit_2_4_shape, bw_unit_2_4_launch, bw_unit_2_4_chain};
             break;
     }
-    return {nullptr, nullptr};
+    return {nullptr, nullptr, nullptr};
 }
 }  // namespace
 
@@ -81,6 +84,17 @@ cudaError_t launch_bw(const BwVariant& v, const void* in, void* out, std::size_t
     const Unit u = unit_of(v.op, v.type);
     if (!u.launch) return cudaErrorInvalidValue;
     return u.launch(v.log_h, v.log_w, in, out, outer, inner, inverse, scale, cache_mode, stream);
+}
+
+bool bw_chain_available(BwOp op, BwType type, int log_h0, int log_h1) {
+    return op != BwOp::Fwht && unit_of(op, type).chain != nullptr && log_h0 == bw_max_contiguous_log(type) &&
+           log_h1 >= 1 && log_h1 <= bw_max_strided_log(type);
+}
+
+cudaError_t launch_bw_chain(BwOp op, BwType type, const BwChain& c, const void* in, void* out, cudaStream_t stream) {
+    const Unit u = unit_of(op, type);
+    if (!u.chain || op == BwOp::Fwht) return cudaErrorInvalidValue;
+    return u.chain(c, in, out, stream);
 }
 
 }  // namespace cubf

@@ -71,42 +71,77 @@ def test_zeta_config3_full_size(lib, oracle, cuda):
     assert np.array_equal(got, oracle.zeta(z)), name
 
 
-def test_zeta_chunk_overlap_graph_replay(lib, oracle, cuda):
-    """A chained plan whose batch spans several L2 chunks, executed again and
-    again: the first call on a buffer pair runs directly, the second captures
-    the chain into a CUDA graph and later calls replay it.  Alternating
-    buffers, and a caller that captures its own stream around the call, give
-    the same bits."""
+def _chain_case(lib, oracle, cuda, log_n, batch, superset=False, inverse=False, dtype=cb.DataType.UINT32,
+                in_place=True, calls=3):
+    """Execute a chained plan `calls` times on fresh copies of one input; every
+    call bit-exact, and the plan's device status stays clean."""
     import json
 
     import torch
 
     from gpu_util import stream_ptr
 
+    if dtype == cb.DataType.UINT32:
+        z = w.zeta_input(log_n, batch, seed=log_n + batch)
+        view = np.uint32
+    else:
+        z = w.rng(37, log_n).integers(0, 2**63, size=(batch, 1 << log_n), dtype=np.uint64)
+        view = np.uint64
+    want = oracle.zeta(z, superset=superset, inverse=inverse)
+    t, _ = zeta_transform(1 << log_n, batch, superset, inverse, dtype, in_place=in_place)
+    src = torch.from_numpy(z.view(np.uint8).reshape(-1).copy()).to(cuda)
+    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
+        assert len(json.loads(plan.mapping_json())["passes"]) == 2, plan.algorithm_name()
+        for _ in range(calls):
+            buf = src.clone()
+            out = buf if in_place else torch.empty_like(buf)
+            plan.execute(buf.data_ptr(), out.data_ptr())
+            torch.cuda.synchronize()
+            assert np.array_equal(out.cpu().numpy().view(view).reshape(z.shape), want)
+        assert plan.device_status() == 0
+
+
+@pytest.mark.parametrize("log_n, batch", [(24, 3), (23, 5), (22, 13), (20, 40), (18, 1100)])
+def test_zeta_chain_kernel_u32(lib, oracle, cuda, log_n, batch):
+    """Two-pass chains whose batch spans several L2 chunks run as one launch
+    per chunk step, pass B of chunk k-1 beside pass A of chunk k: chunk counts
+    from 2 to 23 with a ragged last chunk, strided passes with 256 and with 128
+    threads (two virtual CTAs per CTA)."""
+    _chain_case(lib, oracle, cuda, log_n, batch)
+
+
+@pytest.mark.parametrize("superset, inverse", [(False, True), (True, False), (True, True)])
+def test_zeta_chain_kernel_directions(lib, oracle, cuda, superset, inverse):
+    _chain_case(lib, oracle, cuda, 21, 9, superset=superset, inverse=inverse, in_place=False)
+
+
+def test_zeta_chain_kernel_u64(lib, oracle, cuda):
+    _chain_case(lib, oracle, cuda, 21, 6, dtype=cb.DataType.UINT64, inverse=True)
+
+
+def test_zeta_chain_capturable(lib, oracle, cuda):
+    """A caller capturing its own stream gets the same step launches inside its
+    graph (nothing in the chain synchronises or allocates); replays are
+    bit-exact."""
+    import torch
+
     log_n, batch = 20, 16
     z = w.zeta_input(log_n, batch, seed=21)
     want = oracle.zeta(z)
     t, _ = zeta_transform(1 << log_n, batch, in_place=True)
     src = torch.from_numpy(z.view(np.int32).copy()).to(cuda)
-    bufs = [torch.empty_like(src) for _ in range(2)]
-    with cb.Plan(lib, t, stream=stream_ptr()) as plan:
-        assert len(json.loads(plan.mapping_json())["passes"]) == 2
-        for k in (0, 0, 0, 1, 0, 1, 1, 1, 0):
-            bufs[k].copy_(src)
-            plan.execute(bufs[k].data_ptr(), bufs[k].data_ptr())
-            torch.cuda.synchronize()
-            assert np.array_equal(bufs[k].cpu().numpy().view(np.uint32), want), k
+    buf = torch.empty_like(src)
     side = torch.cuda.Stream()
     with cb.Plan(lib, t, stream=side.cuda_stream) as plan:
         with torch.cuda.stream(side):
-            bufs[0].copy_(src)
-            plan.execute(bufs[0].data_ptr(), bufs[0].data_ptr())
+            buf.copy_(src)
+            plan.execute(buf.data_ptr(), buf.data_ptr())
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=side):
-            plan.execute(bufs[0].data_ptr(), bufs[0].data_ptr())
+            plan.execute(buf.data_ptr(), buf.data_ptr())
         for _ in range(2):
-            bufs[0].copy_(src)
+            buf.copy_(src)
             graph.replay()
             torch.cuda.synchronize()
-            assert np.array_equal(bufs[0].cpu().numpy().view(np.uint32), want)
+            assert np.array_equal(buf.cpu().numpy().view(np.uint32), want)

@@ -54,7 +54,7 @@ struct cubutterflyPlan {
     void* outer_lo = nullptr;  // global FFT: double2 W_N^k, k < 2^split
     void* outer_hi = nullptr;  // global FFT: double2 W_N^(k << split)
     int outer_split = 0;
-    // NTT: one allocation holding the root table, its Shoup quotients, the
+    // NTT: one allocation holding the {root, Shoup quotient} pairs, the
     // per-modulus constants and the per-transform offsets of the tile passes.
     void* ntt_block = nullptr;
     cubf::NttTables ntt_tables{};
@@ -608,6 +608,51 @@ void enqueue_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const void*
     }
 }
 
+// L2-blocked FFT (mapping family "fft-l2-blocked", planner.hpp): each
+// transform of N = V L points runs as V decimated transforms of L points,
+// taken kFftBlockChunk at a time -- their first pass de-interleaves from the
+// input into an L2-resident staging buffer, the rest run there, the last
+// writes the block of results -- then one radix-V pass with Ns = L combines
+// the blocks into the natural-order output.  Workspace: the blocks (N
+// values), then one or two chunk staging buffers.
+void launch_fft_blocked(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
+                        float scale, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    const int log_n = p.req.log_n;
+    const int log_vb = m.passes.back().log_h;
+    const int log_len = log_n - log_vb;
+    const std::size_t n = std::size_t{1} << log_n, len = std::size_t{1} << log_len;
+    const std::size_t chunk = cubf::kFftBlockChunk;
+    auto* ws = static_cast<float2*>(core_ws);
+    float2* blocks = ws;
+    float2* stage[2] = {ws + n, ws + n + chunk * len};
+    const cubf::FftOuterTables outer{p.outer_lo, p.outer_hi, p.outer_split};
+    const std::size_t nsub = m.passes.size() - 1;
+    for (std::size_t b = 0; b < d.batch; ++b) {
+        const float2* src = static_cast<const float2*>(in) + b * n;
+        float2* dst = static_cast<float2*>(out) + b * n;
+        for (std::size_t m0 = 0; m0 < (std::size_t{1} << log_vb); m0 += chunk) {
+            float2* target = blocks + m0 * len;
+            const void* cur = nsub == 1 ? static_cast<void*>(target) : static_cast<void*>(stage[0]);
+            check_cuda(cubf::launch_fft_deinterleave_pass(m.passes[0].log_h, src, const_cast<void*>(cur), log_len, log_vb,
+                                                          m0, p.twiddles, inverse, stream),
+                       "FFT de-interleave pass launch");
+            for (std::size_t i = 1; i < nsub; ++i) {
+                const bool last = i + 1 == nsub;
+                void* next = last ? static_cast<void*>(target) : static_cast<void*>(stage[i & 1]);
+                check_cuda(cubf::launch_fft_global_pass(m.passes[i].log_h, cur, next, log_len, m.passes[i].log_inner,
+                                                        chunk, p.twiddles, outer, false, false, 1.0f, stream, 0, log_vb),
+                           "FFT chunk pass launch");
+                cur = next;
+            }
+        }
+        check_cuda(cubf::launch_fft_global_pass(log_vb, blocks, dst, log_n, log_len, 1, p.twiddles, outer, false,
+                                                inverse, scale, stream, 0, 0, true),
+                   "FFT combining pass launch");
+    }
+}
+
 void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
                  cudaStream_t stream) {
     const auto& d = p.desc;
@@ -639,6 +684,10 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         if (m.passes.front().kind == cubf::PassKind::FftLocal) {
             check_cuda(cubf::launch_fft_local(p.req.log_n, in, out, d.batch, p.twiddles, inverse, scale, stream),
                        "FFT launch");
+            return;
+        }
+        if (m.family == "fft-l2-blocked") {
+            launch_fft_blocked(p, m, in, out, core_ws, scale, stream);
             return;
         }
         // Global passes ping-pong between the output and the workspace so the
@@ -714,8 +763,12 @@ void build_ntt_tables(cubutterflyPlan& p) {
     const std::size_t n = std::size_t{1} << l;
     std::uint64_t root = ma::primitive_root_of_two_power(static_cast<unsigned>(l), q);
     if (d.direction == CUBUTTERFLY_DIRECTION_INVERSE) root = ma::powmod(root, q - 2, q);
-    std::vector<std::uint64_t> words(2 * n + 4);
-    ma::cyclic_root_table(l, q, root, words.data(), words.data() + n);
+    std::vector<std::uint64_t> words(2 * n + 4), roots(n), quots(n);
+    ma::cyclic_root_table(l, q, root, roots.data(), quots.data());
+    for (std::size_t k = 0; k < n; ++k) {  // {root, quotient} pairs
+        words[2 * k] = roots[k];
+        words[2 * k + 1] = quots[k];
+    }
     const std::uint64_t ni = ma::powmod(static_cast<std::uint64_t>(n), q - 2, q);
     words[2 * n + 0] = q;
     words[2 * n + 1] = ni;
@@ -735,7 +788,7 @@ void build_ntt_tables(cubutterflyPlan& p) {
                    "NTT offsets upload");
         p.ntt_polys = reinterpret_cast<const cubf::NttPolyDesc*>(base + words.size());
     }
-    p.ntt_tables = {base, base + n, base + 2 * n, base + 2 * n + 1, base + 2 * n + 2, base + 2 * n + 3};
+    p.ntt_tables = {base, base + 2 * n, base + 2 * n + 1, base + 2 * n + 2, base + 2 * n + 3};
 }
 
 // Per-stage matrices of a structured 2x2 plan: one shared matrix or one per

@@ -270,11 +270,12 @@ __global__ void __launch_bounds__(LocalShape<LOGN>::TPB)
 // stores contiguous.  Outer twiddles come from a fp64 recurrence per column
 // (one two-level table lookup for the start and one for the step, then fp64
 // products), rounded once to fp32.
-template <int LOGR>
+template <int LOGR, int CW = 0>
 struct GlobalPassShape {
     using S = LocalShape<LOGR>;
     static constexpr int R = 1 << LOGR;
-    static constexpr int C = S::T >= 16 ? 16 : 256 / S::T;  // columns per CTA (>= 16)
+    // columns per CTA: CW when given, else >= 16 (runs of >= 128 bytes)
+    static constexpr int C = CW ? CW : (S::T >= 16 ? 16 : 256 / S::T);
     static constexpr int TPB = C * S::T;
     static constexpr int RS = S::PADDED + 1;                 // padded row stride (float2)
     static constexpr int TILE = C * R;
@@ -323,12 +324,15 @@ struct GlobalColumnPasses {
 // Ns scaled by 2^log_v (the caller passes ns_bits including log_v), except
 // that the outer twiddle depends on the transform index (j mod Ns) >> log_v
 // only and is a power of W_N (the outer tables hold W_N).
-template <int LOGR>
-__global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
+//
+// `outer_shift` > 0 serves a transform of 2^log_n points from outer tables of
+// W_M, M = 2^(log_n + outer_shift) (W_N = W_M^(2^outer_shift)).
+template <int LOGR, int CW = 0>
+__global__ void __launch_bounds__(GlobalPassShape<LOGR, CW>::TPB)
     fft_global_pass_kernel(const float2* src, float2* dst, int log_n, int ns_bits, size_t batch,
                            const float2* __restrict__ tw_r, int tw_log_stride, OuterTwiddles outer, int conj_in,
-                           int conj_out, float scale, int log_v, unsigned prefetch_stride) {
-    using G = GlobalPassShape<LOGR>;
+                           int conj_out, float scale, int log_v, unsigned prefetch_stride, int outer_shift) {
+    using G = GlobalPassShape<LOGR, CW>;
     using S = typename G::S;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float2* a = reinterpret_cast<float2*>(smem_raw);
@@ -342,8 +346,8 @@ __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
     const float2* sb = src + bidx * n;
     float2* db = dst + bidx * n;
     const float in_sgn = conj_in ? -1.f : 1.f;
-    const int tshift = log_n - ns_bits - LOGR;  // W_{Ns R}^m = W_N^(m << tshift)
-    const size_t tmask = (n >> log_v) - 1;      // exponents are taken mod N
+    const int tshift = log_n - ns_bits - LOGR + outer_shift;         // W_{Ns R}^m = W_M^(m << tshift)
+    const size_t tmask = (size_t{1} << (log_n - log_v + outer_shift)) - 1;  // exponents are taken mod M
     // 1. coalesced tile load (runs of C elements), outer twiddle applied.
     //    Thread t handles column c = t % C and rows r = t / C + k (TPB / C).
     {
@@ -401,6 +405,63 @@ __global__ void __launch_bounds__(GlobalPassShape<LOGR>::TPB)
                          static_cast<size_t>(k) * ns;
         const float2 x = a[c * G::RS + S::pad(k)];
         __stcs(dcol + o, make_float2(x.x * scale, x.y * out_sgn * scale));
+    }
+}
+
+
+// ---- L2-blocked large transform: first pass of the decimated transforms ------
+//
+// A transform of N = V L points runs as V transforms of L points over the
+// decimated sequences x_m[i] = x[m + V i] (m < V), then one radix-V Stockham
+// pass with Ns = L that combines them (Cooley-Tukey, decimation in time).
+// The V decimated transforms are taken CW at a time, a chunk whose L-point
+// data fits in L2: this kernel runs the first Stockham pass (Ns = 1, radix
+// R = 2^LOGR) of transforms m0 .. m0 + CW - 1 of a chunk, reading x in runs of
+// CW adjacent values (the transforms interleave element by element) and
+// writing each transform's pass output contiguously (dst + (m - m0) L), kept
+// in L2 for the chunk's next pass.  CTA b takes column j = b of every
+// transform of the chunk: rows x_m[j + r L / R], r < R.
+template <int LOGR, int CW>
+__global__ void __launch_bounds__(GlobalPassShape<LOGR, CW>::TPB,
+                                  1024 / GlobalPassShape<LOGR, CW>::TPB > 0 ? 1024 / GlobalPassShape<LOGR, CW>::TPB : 1)
+    fft_deinterleave_pass_kernel(const float2* src, float2* dst, int log_len, int log_v, size_t m0,
+                                 const float2* __restrict__ tw_r, int tw_log_stride, int conj_in) {
+    using G = GlobalPassShape<LOGR, CW>;
+    using S = typename G::S;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* a = reinterpret_cast<float2*>(smem_raw);
+    const auto twt = TwiddleTable<LOGR>::load(a + G::C * G::RS, tw_r, tw_log_stride);
+    const size_t len = size_t{1} << log_len;
+    const size_t cols = len >> LOGR;
+    const size_t j = blockIdx.x;
+    const float in_sgn = conj_in ? -1.f : 1.f;
+    {
+        constexpr int RSTEP = G::TPB / CW;
+        const int c = threadIdx.x % CW;
+        const float2* s = src + m0 + c + (j << log_v);
+#pragma unroll 4
+        for (int r = threadIdx.x / CW; r < G::R; r += RSTEP) {
+            float2 x = __ldcs(s + ((static_cast<size_t>(r) * cols) << log_v));
+            x.y *= in_sgn;
+            a[c * G::RS + S::pad(r)] = x;
+        }
+    }
+    __syncthreads();
+    {
+        const int c = threadIdx.x / S::T;
+        const int th = threadIdx.x % S::T;
+        float2 v[S::E];
+        GlobalColumnPasses<LOGR, 0>::run(v, th, twt, a + c * G::RS);
+    }
+    // y_m[j R + k] -> dst[(m - m0) L + j R + k]: contiguous in k; kept in L2
+    const uint64_t keep = l2_policy(true);
+#pragma unroll 4
+    for (int idx = threadIdx.x; idx < CW * G::R; idx += G::TPB) {
+        const int c = idx >> LOGR, k = idx & (G::R - 1);
+        const float2 x = a[c * G::RS + S::pad(k)];
+        float2* p = dst + static_cast<size_t>(c) * len + j * G::R + k;
+        asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(x.x), "f"(x.y), "l"(keep)
+                     : "memory");
     }
 }
 

@@ -47,9 +47,27 @@ LaunchShape fft_global_pass_shape(int log_r);
 // log_v > 0: 2^log_v interleaved transforms (element n of transform l at
 // n 2^log_v + l) treated as one array of 2^log_n values; ns_bits then
 // includes log_v and `outer` holds W for the transform length 2^(log_n-log_v).
+// `outer_shift` > 0: `outer` holds W for 2^(log_n - log_v + outer_shift)
+// points (one table set serves the shorter transforms of a blocked plan).
+// `narrow`: 8 columns per CTA (64-byte runs, half the shared memory) where
+// fft_global_pass_narrow_available(log_r).
 cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
                                    std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
-                                   bool conj_out, float scale, cudaStream_t stream, int log_v = 0);
+                                   bool conj_out, float scale, cudaStream_t stream, int log_v = 0,
+                                   int outer_shift = 0, bool narrow = false);
+bool fft_global_pass_narrow_available(int log_r);
+LaunchShape fft_global_pass_narrow_shape(int log_r);
+
+// L2-blocked transforms (csrc/fft.cuh, fft_deinterleave_pass_kernel): the
+// first pass (radix 2^log_r, Ns = 1) of transforms m0 .. m0 + 7 of 2^log_v
+// transforms of 2^log_len points interleaved element by element in `src`;
+// each transform's pass output goes contiguously to dst + (m - m0) 2^log_len
+// with an L2 evict-last hint.  log_r in kFftDeinterleaveMinLog .. 10.
+constexpr int kFftBlockChunk = 8;
+constexpr int kFftDeinterleaveMinLog = 8;
+LaunchShape fft_deinterleave_shape(int log_r);
+cudaError_t launch_fft_deinterleave_pass(int log_r, const void* src, void* dst, int log_len, int log_v,
+                                         std::size_t m0, const void* tw1024, bool conj_in, cudaStream_t stream);
 
 // ---- FWHT / zeta tile passes --------------------------------------------------
 enum class BwOp { Fwht = 0, ZetaSubset = 1, ZetaSuperset = 2 };
@@ -176,9 +194,10 @@ struct NttPolyDesc {
     std::uint32_t domain;
     std::uint32_t pad_;
 };
+// root_pairs: [domains][N] pairs {root, Shoup quotient of root} (16 bytes,
+// 16-byte aligned), so one vector load fetches both.
 struct NttTables {
-    const std::uint64_t* roots;
-    const std::uint64_t* quotients;
+    const std::uint64_t* root_pairs;
     const std::uint64_t* moduli;
     const std::uint64_t* n_inv;
     const std::uint64_t* n_inv_q;

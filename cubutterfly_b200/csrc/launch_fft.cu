@@ -76,9 +76,9 @@ struct Table {
 };
 using Local = Table<1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13>;
 
-template <int LOGR>
+template <int LOGR, int CW = 0>
 struct GlobalEntry {
-    using G = fft::GlobalPassShape<LOGR>;
+    using G = fft::GlobalPassShape<LOGR, CW>;
     static LaunchShape shape() {
         LaunchShape s;
         s.threads = G::TPB;
@@ -90,8 +90,8 @@ struct GlobalEntry {
     }
     static cudaError_t launch(const void* src, void* dst, int log_n, int ns_bits, std::size_t batch,
                               const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out,
-                              float scale, cudaStream_t stream, int log_v) {
-        auto kernel = fft::fft_global_pass_kernel<LOGR>;
+                              float scale, cudaStream_t stream, int log_v, int outer_shift) {
+        auto kernel = fft::fft_global_pass_kernel<LOGR, CW>;
         static KernelSetup setup;
         int grid_cap = 0;
         cudaError_t e = setup_kernel(setup, kernel, G::TPB, G::SMEM_BYTES, &grid_cap);
@@ -105,12 +105,12 @@ struct GlobalEntry {
         kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
             static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits, batch,
             static_cast<const float2*>(tw1024), 10 - LOGR, ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v,
-            blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u);
+            blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u, outer_shift);
         return cudaGetLastError();
     }
 };
 using GlobalLaunch = cudaError_t (*)(const void*, void*, int, int, std::size_t, const void*, const FftOuterTables&,
-                                     bool, bool, float, cudaStream_t, int);
+                                     bool, bool, float, cudaStream_t, int, int);
 using GlobalShape = LaunchShape (*)();
 template <int... L>
 struct GlobalTable {
@@ -118,6 +118,41 @@ struct GlobalTable {
     static constexpr GlobalShape shape_fns[] = {GlobalEntry<L>::shape...};
 };
 using Global = GlobalTable<4, 5, 6, 7, 8, 9, 10>;
+// 8-column variants of the large radices (64-byte runs, two CTAs per SM at 2^10)
+template <int... L>
+struct NarrowTable {
+    static constexpr GlobalLaunch launch_fns[] = {GlobalEntry<L, kFftBlockChunk>::launch...};
+    static constexpr GlobalShape shape_fns[] = {GlobalEntry<L, kFftBlockChunk>::shape...};
+};
+using Narrow = NarrowTable<8, 9, 10>;
+
+template <int LOGR>
+struct DeinterleaveEntry {
+    using G = fft::GlobalPassShape<LOGR, kFftBlockChunk>;
+    static LaunchShape shape() { return GlobalEntry<LOGR, kFftBlockChunk>::shape(); }
+    static cudaError_t launch(const void* src, void* dst, int log_len, int log_v, std::size_t m0,
+                              const void* tw1024, bool conj_in, cudaStream_t stream) {
+        auto kernel = fft::fft_deinterleave_pass_kernel<LOGR, kFftBlockChunk>;
+        static KernelSetup setup;
+        int grid_cap = 0;
+        cudaError_t e = setup_kernel(setup, kernel, G::TPB, G::SMEM_BYTES, &grid_cap);
+        if (e != cudaSuccess) return e;
+        if (log_len < LOGR || log_v < 3) return cudaErrorInvalidValue;
+        const std::size_t blocks = std::size_t{1} << (log_len - LOGR);
+        if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
+        kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
+            static_cast<const float2*>(src), static_cast<float2*>(dst), log_len, log_v, m0,
+            static_cast<const float2*>(tw1024), 10 - LOGR, conj_in ? 1 : 0);
+        return cudaGetLastError();
+    }
+};
+template <int... L>
+struct DeinterleaveTable {
+    static constexpr cudaError_t (*launch_fns[])(const void*, void*, int, int, std::size_t, const void*, bool,
+                                                 cudaStream_t) = {DeinterleaveEntry<L>::launch...};
+    static constexpr GlobalShape shape_fns[] = {DeinterleaveEntry<L>::shape...};
+};
+using Deinterleave = DeinterleaveTable<8, 9, 10>;
 
 }  // namespace
 
@@ -128,11 +163,35 @@ LaunchShape fft_global_pass_shape(int log_r) {
 
 cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
                                    std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
-                                   bool conj_out, float scale, cudaStream_t stream, int log_v) {
+                                   bool conj_out, float scale, cudaStream_t stream, int log_v, int outer_shift,
+                                   bool narrow) {
     if (log_r < kFftPassMinLog || log_r > kFftPassMaxLog) return cudaErrorInvalidValue;
-    if (log_v < 0 || log_v > log_n - log_r) return cudaErrorInvalidValue;
+    if (log_v < 0 || log_v > log_n - log_r || outer_shift < 0) return cudaErrorInvalidValue;
+    if (narrow) {
+        if (!fft_global_pass_narrow_available(log_r)) return cudaErrorInvalidValue;
+        return Narrow::launch_fns[log_r - 8](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in, conj_out, scale,
+                                             stream, log_v, outer_shift);
+    }
     return Global::launch_fns[log_r - kFftPassMinLog](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in,
-                                                      conj_out, scale, stream, log_v);
+                                                      conj_out, scale, stream, log_v, outer_shift);
+}
+
+bool fft_global_pass_narrow_available(int log_r) { return log_r >= 8 && log_r <= kFftPassMaxLog; }
+
+LaunchShape fft_global_pass_narrow_shape(int log_r) {
+    return fft_global_pass_narrow_available(log_r) ? Narrow::shape_fns[log_r - 8]() : LaunchShape{};
+}
+
+LaunchShape fft_deinterleave_shape(int log_r) {
+    if (log_r < kFftDeinterleaveMinLog || log_r > kFftPassMaxLog) return {};
+    return Deinterleave::shape_fns[log_r - kFftDeinterleaveMinLog]();
+}
+
+cudaError_t launch_fft_deinterleave_pass(int log_r, const void* src, void* dst, int log_len, int log_v,
+                                         std::size_t m0, const void* tw1024, bool conj_in, cudaStream_t stream) {
+    if (log_r < kFftDeinterleaveMinLog || log_r > kFftPassMaxLog) return cudaErrorInvalidValue;
+    return Deinterleave::launch_fns[log_r - kFftDeinterleaveMinLog](src, dst, log_len, log_v, m0, tw1024, conj_in,
+                                                                    stream);
 }
 
 std::vector<float> fft_local_twiddles(int log_n) {

@@ -22,9 +22,9 @@ constexpr bool kHasStrict = false;
 #endif
 
 ntt::DomainTables device_tables(const NttTables& t) {
-    return {reinterpret_cast<const ntt::u64*>(t.roots),   reinterpret_cast<const ntt::u64*>(t.quotients),
-            reinterpret_cast<const ntt::u64*>(t.moduli),  reinterpret_cast<const ntt::u64*>(t.n_inv),
-            reinterpret_cast<const ntt::u64*>(t.n_inv_q), reinterpret_cast<const ntt::u64*>(t.unit_q)};
+    return {reinterpret_cast<const ntt::u64*>(t.root_pairs), reinterpret_cast<const ntt::u64*>(t.moduli),
+            reinterpret_cast<const ntt::u64*>(t.n_inv),      reinterpret_cast<const ntt::u64*>(t.n_inv_q),
+            reinterpret_cast<const ntt::u64*>(t.unit_q)};
 }
 
 template <int L, bool STRIDED, bool INV, bool LAZY>

@@ -66,8 +66,9 @@ struct PolyDesc {
 };
 
 struct DomainTables {
-    const u64* roots;     // [domains][N] forward: psi^bitrev(i); inverse: psi^-bitrev(i)
-    const u64* quotients; // Shoup quotients of `roots`
+    // [domains][N] pairs {w, floor(w 2^64 / q)}: forward w = psi^bitrev(i),
+    // inverse psi^-bitrev(i); one 16-byte load fetches a root and its quotient
+    const u64* root_pairs;
     const u64* moduli;    // [domains]
     const u64* n_inv;     // [domains] N^-1 mod q (inverse only)
     const u64* n_inv_q;   // Shoup quotient of n_inv
@@ -103,7 +104,7 @@ struct NttGroups {
     static constexpr uint32_t reg(int g) { return lowmask(LOGE) << lo(g); }
 };
 
-template <int B_, int LOGE_, int COLS_, bool STRIDED_, bool INV_, bool LAZY_>
+template <int B_, int LOGE_, int COLS_, bool STRIDED_, bool INV_, bool LAZY_, bool STAGEABLE_ = true>
 struct NttShape {
     static constexpr bool LAZY = LAZY_;
     static constexpr int B = B_;
@@ -124,19 +125,71 @@ struct NttShape {
         else
             return col * (TILE + TILE / 16) + static_cast<int>(i + (i >> 4));
     }
-    static constexpr int SMEM_BYTES = (STRIDED ? TILE * COLS : COLS * (TILE + TILE / 16)) * 8;
-    // Up to 16 residues per thread fit in 64 registers: asking for
-    // 1024 / TPB resident CTAs caps the kernel there, so a 32 x 2^16 pass
-    // (131072 threads) runs as one wave instead of 1.15 (80 registers).
-    static constexpr int MINB = (E <= 16 && TPB <= 1024) ? 1024 / TPB : 1;
+    static constexpr int XCH_BYTES = (STRIDED ? TILE * COLS : COLS * (TILE + TILE / 16)) * 8;
+    // Root pairs a CTA stages into shared memory before its stages run: the
+    // strided pass's tiles all use entries 1 .. 2^B - 1 of the table; the
+    // contiguous pass's COLS tiles use, for local stage ls, COLS 2^ls
+    // consecutive entries from 2^(off+ls) + first_tile 2^ls.
+    // Staged for the strided pass only (2^B - 1 pairs shared by every tile);
+    // the contiguous pass's COLS (2^B - 1) pairs would take a 16-tile CTA's
+    // occupancy from four CTAs per SM to two (measured slower: 53.3 vs 46.5 us
+    // at 32 x 2^16), so its stages read the global pairs, kept L2-resident.
+    static constexpr int STAGE_PAIRS = STRIDED ? (TILE - 1) : COLS * (TILE - 1);
+    static constexpr bool STAGE = STAGEABLE_ && STRIDED;
+    static constexpr int ROOT_PAIRS = STAGE ? STAGE_PAIRS : 0;
+    static constexpr int SMEM_BYTES = XCH_BYTES + ROOT_PAIRS * 16;
+    // Resident CTAs to ask for: as many as the register file holds with up
+    // to 16 residues per thread in 64 registers, but no more than shared
+    // memory admits (the register cap would only cost hoisting).
+    static constexpr int SMEM_CTAS = (227 * 1024) / SMEM_BYTES;
+    static constexpr int REG_CTAS = (E <= 16 && TPB <= 1024) ? 1024 / TPB : 1;
+    static constexpr int MINB = SMEM_CTAS < REG_CTAS ? (SMEM_CTAS > 0 ? SMEM_CTAS : 1) : REG_CTAS;
 };
 
 // Butterflies of group G on the registers of one thread.  i = tpart | (r << lo)
 // is the tile row of register r; the root of the pair at tile bit b (local
 // stage ls = B-1-b forward) is roots[2^(off+ls) + (hi << ls) + (i >> (b+1))].
+// Root pair k with an L2 evict-last hint: the tables (16 bytes per root) stay
+// resident across calls while the coefficient streams pass through.
+CUBF_DEV ulonglong2 load_root_pair(const u64* __restrict__ pairs, u64 k, uint64_t pol) {
+    ulonglong2 r;
+    asm volatile("ld.global.nc.L2::cache_hint.v2.u64 {%0, %1}, [%2], %3;"
+                 : "=l"(r.x), "=l"(r.y)
+                 : "l"(pairs + 2 * k), "l"(pol));
+    return r;
+}
+
+// Coefficient words with an L2 hint (evict-first streams, evict-last for the
+// intermediate the second pass reads back).
+template <typename T>
+CUBF_DEV T load_word(const T* p, uint64_t pol) {
+    if constexpr (sizeof(T) == 8) {
+        unsigned long long v;
+        asm volatile("ld.global.L2::cache_hint.u64 %0, [%1], %2;" : "=l"(v) : "l"(p), "l"(pol));
+        return static_cast<T>(v);
+    } else {
+        unsigned v;
+        asm volatile("ld.global.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+        return static_cast<T>(v);
+    }
+}
+template <typename T>
+CUBF_DEV void store_word(T* p, T v, uint64_t pol) {
+    if constexpr (sizeof(T) == 8)
+        asm volatile("st.global.L2::cache_hint.u64 [%0], %1, %2;" ::"l"(p), "l"(static_cast<unsigned long long>(v)),
+                     "l"(pol)
+                     : "memory");
+    else
+        asm volatile("st.global.L2::cache_hint.u32 [%0], %1, %2;" ::"l"(p), "r"(static_cast<unsigned>(v)), "l"(pol)
+                     : "memory");
+}
+
+// Roots of the tile passes come from the CTA's staged copy in shared memory
+// (`sroots`, laid out as NttShape::ROOT_PAIRS describes); the whole-transform
+// kernel reads the global pairs directly (`sroots` null).
 template <typename S, int G>
-CUBF_DEV void ntt_group(u64 (&v)[S::E], uint32_t tpart, u64 hi, int off, const u64* __restrict__ roots,
-                        const u64* __restrict__ quots, u64 q) {
+CUBF_DEV void ntt_group(u64 (&v)[S::E], uint32_t tpart, u64 hi, int off, const u64* __restrict__ pairs,
+                        uint64_t tab_pol, const ulonglong2* sroots, int col, u64 q) {
     using Gs = typename S::Gs;
     constexpr int LO = Gs::lo(G);
     constexpr uint32_t STAGE = Gs::stage(G);
@@ -150,8 +203,16 @@ CUBF_DEV void ntt_group(u64 (&v)[S::E], uint32_t tpart, u64 hi, int off, const u
 #pragma unroll
             for (int rh = 0; rh < (S::E >> (j + 1)); ++rh) {
                 const u64 k = head + static_cast<u64>(rh);
-                const u64 w = __ldg(roots + k);
-                const u64 wq = __ldg(quots + k);
+                ulonglong2 wp;
+                if (sroots != nullptr) {
+                    const uint32_t x = (tpart >> (b + 1)) + static_cast<uint32_t>(rh);
+                    const int local = S::STRIDED ? (1 << ls) - 1 + static_cast<int>(x)
+                                                 : (S::COLS << ls) - S::COLS + (col << ls) + static_cast<int>(x);
+                    wp = sroots[local];
+                } else {
+                    wp = load_root_pair(pairs, k, tab_pol);
+                }
+                const u64 w = wp.x, wq = wp.y;
 #pragma unroll
                 for (int rl = 0; rl < (1 << j); ++rl) {
                     const int r0 = (rh << (j + 1)) | rl;
@@ -187,7 +248,7 @@ CUBF_DEV void ntt_group(u64 (&v)[S::E], uint32_t tpart, u64 hi, int off, const u
 
 template <typename S, int G>
 CUBF_DEV void ntt_groups(u64 (&v)[S::E], u64* sbuf, int col, uint32_t t, u64 hi, int off,
-                         const u64* __restrict__ roots, const u64* __restrict__ quots, u64 q) {
+                         const u64* __restrict__ pairs, uint64_t tab_pol, const ulonglong2* sroots, u64 q) {
     using Gs = typename S::Gs;
     if constexpr (G < Gs::COUNT) {
         if constexpr (G > 0) {
@@ -204,8 +265,8 @@ CUBF_DEV void ntt_groups(u64 (&v)[S::E], u64* sbuf, int col, uint32_t t, u64 hi,
             for (int r = 0; r < S::E; ++r) v[r] = sbuf[S::sidx(col, tn | ON.v[r])];
         }
         const uint32_t tpart = deposit_rt<lowmask(S::B) & ~Gs::reg(G), S::B>(t);
-        ntt_group<S, G>(v, tpart, hi, off, roots, quots, q);
-        ntt_groups<S, G + 1>(v, sbuf, col, t, hi, off, roots, quots, q);
+        ntt_group<S, G>(v, tpart, hi, off, pairs, tab_pol, sroots, col, q);
+        ntt_groups<S, G + 1>(v, sbuf, col, t, hi, off, pairs, tab_pol, sroots, q);
     }
 }
 
@@ -259,8 +320,36 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB, PassSha
     const uint32_t g = static_cast<uint32_t>(blockIdx.x % GROUPS);
     const PolyDesc pd = polys[p];
     const u64 q = tab.moduli[pd.domain];
-    const u64* roots = tab.roots + static_cast<size_t>(pd.domain) * N;
-    const u64* quots = tab.quotients + static_cast<size_t>(pd.domain) * N;
+    const u64* pairs = tab.root_pairs + 2 * static_cast<size_t>(pd.domain) * N;
+    const uint64_t tab_pol = l2_policy(true);
+    // the first pass streams its input and keeps its output (read back by the
+    // second pass) in L2; the final pass streams both ways
+    const uint64_t ld_pol = l2_policy(false);
+    const uint64_t st_pol = l2_policy(!final_pass);
+    // stage this CTA's root pairs (asynchronous copies, overlapping the
+    // coefficient loads below; the tables are kept in L2 across calls)
+    ulonglong2* sroots = S::STAGE ? reinterpret_cast<ulonglong2*>(smem_raw + S::XCH_BYTES) : nullptr;
+    if constexpr (S::STAGE) {
+        const int off_s = STRIDED ? 0 : L - B;
+        for (int i = threadIdx.x; i < S::ROOT_PAIRS; i += S::TPB) {
+            size_t k;
+            if constexpr (STRIDED) {
+                k = static_cast<size_t>(i) + 1;
+            } else {
+                int ls = 0;
+#pragma unroll
+                for (int s2 = 1; s2 < B; ++s2)
+                    if (i >= (COLS << s2) - COLS) ls = s2;
+                const int j = i - ((COLS << ls) - COLS);
+                k = (size_t{1} << (off_s + ls)) + ((static_cast<size_t>(g) * COLS) << ls) + static_cast<size_t>(j);
+            }
+            const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(sroots + i));
+            asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst),
+                         "l"(pairs + 2 * k), "l"(tab_pol)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     const T* src = in_is_out ? static_cast<const T*>(out) + pd.out_off : in + pd.in_off;
     T* dst = out + pd.out_off;
 
@@ -288,14 +377,18 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB, PassSha
         const uint32_t tp = deposit_rt<lowmask(B) & ~R0, B>(t);
         const T* ts = tsrc + (static_cast<size_t>(tp) << SHIFT);
 #pragma unroll
-        for (int r = 0; r < S::E; ++r) v[r] = static_cast<u64>(ts[static_cast<size_t>(O0.v[r]) << SHIFT]);
+        for (int r = 0; r < S::E; ++r) v[r] = static_cast<u64>(load_word(ts + (static_cast<size_t>(O0.v[r]) << SHIFT), ld_pol));
         if (reduce_input) {
             const u64 uq = tab.unit_q[pd.domain];
 #pragma unroll
             for (int r = 0; r < S::E; ++r) v[r] = reduce_word(v[r], uq, q);
         }
     }
-    ntt_groups<S, 0>(v, sbuf, col, t, hi, off, roots, quots, q);
+    if constexpr (S::STAGE) {
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // every thread's staged roots are visible
+    }
+    ntt_groups<S, 0>(v, sbuf, col, t, hi, off, pairs, tab_pol, sroots, q);
     constexpr uint32_t RF = Gs::reg(Gs::COUNT - 1);
     constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);
     const uint32_t tf = deposit_rt<lowmask(B) & ~RF, B>(t);
@@ -303,8 +396,8 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB, PassSha
     const u64 ni = final_scale ? tab.n_inv[pd.domain] : 0, niq = final_scale ? tab.n_inv_q[pd.domain] : 0;
 #pragma unroll
     for (int r = 0; r < S::E; ++r)
-        td[static_cast<size_t>(OF.v[r]) << SHIFT] =
-            static_cast<T>(final_value<INV, LAZY>(v[r], q, final_pass, final_scale, ni, niq));
+        store_word(td + (static_cast<size_t>(OF.v[r]) << SHIFT),
+                   static_cast<T>(final_value<INV, LAZY>(v[r], q, final_pass, final_scale, ni, niq)), st_pol);
 }
 
 // Whole transforms of 2^L <= 2^11 points as single tiles, COLS transforms
@@ -312,7 +405,7 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB, PassSha
 constexpr int single_log_e(int L) { return L < log_e_for(L) ? L : log_e_for(L); }
 constexpr int single_cols(int L) { return 256 >> (L - single_log_e(L)); }
 template <int L, bool INV, bool LAZY>
-using SingleShape = NttShape<L, single_log_e(L), single_cols(L), false, INV, LAZY>;
+using SingleShape = NttShape<L, single_log_e(L), single_cols(L), false, INV, LAZY, false>;
 
 template <int L, bool INV, bool LAZY, typename T>
 __global__ void __launch_bounds__(SingleShape<L, INV, LAZY>::TPB, SingleShape<L, INV, LAZY>::MINB)
@@ -340,7 +433,7 @@ __global__ void __launch_bounds__(SingleShape<L, INV, LAZY>::TPB, SingleShape<L,
             if (reduce_input) v[r] = reduce_word(v[r], uq, q);
         }
     }
-    ntt_groups<S, 0>(v, sbuf, col, t, 0, 0, tab.roots, tab.quotients, q);
+    ntt_groups<S, 0>(v, sbuf, col, t, 0, 0, tab.root_pairs, l2_policy(true), nullptr, q);
     if (!active) return;
     constexpr uint32_t RF = Gs::reg(Gs::COUNT - 1);
     constexpr Offsets<S::E> OF = make_offsets<S::E>(RF);

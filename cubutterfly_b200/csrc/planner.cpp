@@ -313,6 +313,61 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
     return m;
 }
 
+Mapping fft_blocked_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts) {
+    const Descriptor& d = r.d;
+    require(d.op == CUBUTTERFLY_OPERATOR_FFT && r.log_v == 0 && !r.fft64, "L2-blocked FFT serves packed complex fp32");
+    require(parts.size() >= 2, "L2-blocked FFT needs decimated-transform passes and a combining pass");
+    const int log_vb = parts.back();
+    const int log_len = r.log_n - log_vb;
+    if (!fft_global_pass_narrow_available(log_vb) || parts.front() < kFftDeinterleaveMinLog ||
+        parts.front() > kFftPassMaxLog)
+        throw Unsupported("L2-blocked FFT: first and combining passes must be radix 2^8 .. 2^10");
+    const std::size_t chunk_bytes = std::size_t{kFftBlockChunk} << (log_len + 3);
+    if (static_cast<double>(chunk_bytes) > 0.55 * static_cast<double>(hw.l2_bytes))
+        throw Unsupported("L2-blocked FFT: a chunk of decimated transforms does not fit L2");
+    Mapping m;
+    m.family = "fft-l2-blocked";
+    const double elems = static_cast<double>(d.batch) * std::ldexp(1.0, r.log_n);
+    int ns = 0;
+    for (std::size_t i = 0; i + 1 < parts.size(); ++i) {
+        const int bits = parts[i];
+        require(bits >= kFftPassMinLog && bits <= kFftPassMaxLog, "FFT pass radix must be 2^4 .. 2^10");
+        Pass p;
+        p.kind = i == 0 ? PassKind::FftDeinterleave : PassKind::FftGlobal;
+        p.log_h = bits;
+        p.log_inner = ns;
+        p.shape = i == 0 ? fft_deinterleave_shape(bits) : fft_global_pass_shape(bits);
+        require(fits(p.shape, hw), "FFT pass tile does not fit the device");
+        if ((std::size_t{1} << (log_len - bits)) % static_cast<std::size_t>(p.shape.units_per_cta) != 0 && i > 0)
+            throw Unsupported("L2-blocked FFT: decimated transforms too short for this pass");
+        // only the first pass reads HBM and only the last writes it; the
+        // rest move data through L2 (counted at a quarter of the HBM cost).
+        // Efficiency is what a B200 measured: these passes move 64- and
+        // 128-byte runs at megabyte strides (de-interleave 58 us, chunk pass
+        // 64 us per 64 MiB chunk of a 2^30 transform, about 2.2 TB/s).
+        const bool first = i == 0, last = i + 2 == parts.size();
+        const double share = (first ? 0.5 : 0.125) + (last ? 0.5 : 0.125);
+        const double eff = 0.34;
+        m.predicted_us += share * pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, eff);
+        m.passes.push_back(p);
+        ns += bits;
+    }
+    require(ns == log_len, "L2-blocked FFT passes must cover every stage exactly once");
+    Pass f;
+    f.kind = PassKind::FftGlobalNarrow;
+    f.log_h = log_vb;
+    f.log_inner = log_len;
+    f.shape = fft_global_pass_narrow_shape(log_vb);
+    require(fits(f.shape, hw), "FFT pass tile does not fit the device");
+    // measured: the 8-column radix-2^10 combining pass of 2^30 points, 8.6 ms (2.0 TB/s)
+    m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, log_vb, f.shape.exchanges, 2.5 / 2.0, 0.31);
+    m.passes.push_back(f);
+    // blocks of decimated-transform results (one transform of the batch at a
+    // time), then one or two chunk staging buffers
+    m.workspace_bytes = (std::size_t{8} << r.log_n) + chunk_bytes * (parts.size() > 3 ? 2 : 1);
+    return m;
+}
+
 std::string Mapping::name() const {
     if (!label.empty()) return label;
     std::ostringstream o;
@@ -346,6 +401,8 @@ Json Mapping::to_json() const {
             case PassKind::NativeStage: kernel = "fwht_native_stage"; break;
             case PassKind::Fft64Tile: kernel = "fft64_tile"; break;
             case PassKind::Fft64Stage: kernel = "fft64_column"; break;
+            case PassKind::FftDeinterleave: kernel = "fft_deinterleave_pass"; break;
+            case PassKind::FftGlobalNarrow: kernel = "fft_global_pass_narrow"; break;
             default: break;
         }
         ps.push_back({{"kernel", kernel},
@@ -439,6 +496,19 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
             } catch (const Unsupported&) {
             }
         }
+        // L2-blocked plans of long transforms: V = 2^10 decimated transforms,
+        // their L = N / V points in balanced passes of at most 2^10
+        if (r.log_v == 0 && !r.fft64 && r.log_n >= 24 && r.log_n <= 30) {
+            const int log_len = r.log_n - 10;
+            const int np = (log_len + kFftPassMaxLog - 1) / kFftPassMaxLog;
+            std::vector<int> parts;
+            for (int i = 0; i < np; ++i) parts.push_back(log_len / np + (i < log_len % np ? 1 : 0));
+            parts.push_back(10);
+            try {
+                out.push_back(fft_blocked_mapping(r, hw, parts));
+            } catch (const Unsupported&) {
+            }
+        }
         if (out.empty()) throw Unsupported("no global FFT pass partition fits this transform");
         std::stable_sort(out.begin(), out.end(),
                          [](const Mapping& a, const Mapping& b) { return a.predicted_us < b.predicted_us; });
@@ -499,6 +569,7 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         require(j.at("passes").is_array(), "explicit mapping passes must be an array");
         for (const auto& p : j.at("passes")) parts.push_back(p.at("log_h").get<int>());
         if (j.value("family", "") == "fwht-tcgen05") return parse_core(r, hw, "fwht-tcgen05[6+6]");
+        if (j.value("family", "") == "fft-l2-blocked") return fft_blocked_mapping(r, hw, parts);
     } else {
         std::string body = text;
         const auto lb = body.find('['), rb = body.rfind(']');
@@ -515,6 +586,7 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
     if (r.d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2 || r.fwht_native || r.fft64)
         return enumerate_core(r, hw).front();
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
+        if (text.find("fft-l2-blocked") != std::string::npos) return fft_blocked_mapping(r, hw, parts);
         if (r.log_n > kFftLocalMaxLog || r.log_v > 0) return fft_global_mapping(r, hw, parts);
         require(parts.size() == 1 && parts[0] == r.log_n, "FFT up to 2^13 is one local pass of log N bits");
         return enumerate_core(r, hw).front();

@@ -56,7 +56,9 @@ enum class PassKind {
     NativeTile,
     NativeStage,
     Fft64Tile,
-    Fft64Stage
+    Fft64Stage,
+    FftDeinterleave,  // L2-blocked FFT: first pass of a chunk of decimated transforms
+    FftGlobalNarrow   // L2-blocked FFT: the combining pass (8 columns per CTA)
 };
 
 struct Pass {
@@ -129,6 +131,11 @@ Mapping fwht_tc_mapping(const PlanRequest& r, const HardwareProfile& hw);
 Mapping ntt_mapping(const PlanRequest& r, const HardwareProfile& hw);
 // Multi-pass global FFT with the given radix bits per pass.
 Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts);
+// L2-blocked FFT of long transforms (family "fft-l2-blocked"): parts are the
+// radix bits of the passes of each decimated transform of L = N / V points
+// (the first one the de-interleaving pass), then log V, the radix of the
+// final combining pass.  Two HBM round trips whatever the pass count.
+Mapping fft_blocked_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts);
 // Every legal mapping of the request, ranked best first by the static model.
 std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw);
 // Parse an EXPLICIT mapping: the JSON of Mapping::to_json, or a pass list

@@ -198,7 +198,7 @@ struct cubutterflyRnsPlanOpaque {
     bool needs_scratch = false;
     bool lazy = false;  // every modulus < 2^62: Harvey lazy butterflies
     std::size_t scratch_bytes = 0;
-    DeviceBuffer roots, quots, moduli, n_inv, n_inv_q, polys, polys_scratch, scratch;
+    DeviceBuffer root_pairs, moduli, n_inv, n_inv_q, polys, polys_scratch, scratch;
     cubf::NttTables tables{};
     // Prepare results
     bool cache_hit = false;
@@ -266,12 +266,16 @@ struct cubutterflyRnsPlanOpaque {
             niq[d] = shoup(ni[d], q);
         }
         check(cudaGetDevice(&device), "current device");
-        roots.upload(r.data(), r.size() * 8);
-        quots.upload(rq.data(), rq.size() * 8);
+        std::vector<u64> rp(2 * r.size());
+        for (std::size_t k = 0; k < r.size(); ++k) {
+            rp[2 * k] = r[k];
+            rp[2 * k + 1] = rq[k];
+        }
+        root_pairs.upload(rp.data(), rp.size() * 8);
         moduli.upload(m.data(), m.size() * 8);
         n_inv.upload(ni.data(), ni.size() * 8);
         n_inv_q.upload(niq.data(), niq.size() * 8);
-        tables = {roots.as<u64>(), quots.as<u64>(), moduli.as<u64>(), n_inv.as<u64>(), n_inv_q.as<u64>()};
+        tables = {root_pairs.as<u64>(), moduli.as<u64>(), n_inv.as<u64>(), n_inv_q.as<u64>()};
         std::vector<cubf::NttPolyDesc> pd, ps;
         for (std::size_t p = 0; p < c.polynomials.size(); ++p) {
             const auto& x = c.polynomials[p];

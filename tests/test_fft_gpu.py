@@ -288,3 +288,45 @@ def test_four_step_2e24_matches_the_reference_fft(cuda, reference):
     got = got.cpu().numpy().view(np.complex64).reshape(-1)
     want = reference.fft_c32(x[None], threads=os.cpu_count() or 1)[0]
     assert rel_l2(got, want) <= TOL
+
+
+@pytest.mark.parametrize("log_n, mapping", [(24, "fft-l2-blocked[8+6+10]"), (26, "fft-l2-blocked[8+8+10]"),
+                                            (28, "fft-l2-blocked[9+9+10]"), (27, "fft-l2-blocked[9+8+10]")])
+def test_fft_l2_blocked_plans(lib, oracle, cuda, log_n, mapping):
+    """The L2-blocked plan of long transforms (V = 2^10 decimated transforms
+    taken 8 at a time through L2, then one combining pass; an EXPLICIT or
+    MEASURE choice, not the static default): against the
+    Stockham multi-pass plan on the same input, 8 DFT bins against the
+    oracle's long-double direct DFT, the normalised inverse round trip, and in
+    place; all at rel L2 <= 2e-6."""
+    import torch
+
+    n = 1 << log_n
+    x = w.torch_fft_input(n, 1, cuda, seed=log_n).reshape(n, 2)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def planned(t, src, options=None):
+        with cb.Plan(lib, t, options=options, stream=stream) as p:
+            ws = torch.empty(max(p.workspace_size(), 16), dtype=torch.uint8, device=cuda)
+            if p.workspace_size():
+                p.set_workspace(ws.data_ptr(), p.workspace_size())
+            dst = src if t.in_place else torch.empty_like(src)
+            p.execute(src.data_ptr(), dst.data_ptr())
+            torch.cuda.synchronize()
+            return dst, p.algorithm_name()
+
+    opts = cb.PlanOptions(mapping=mapping)
+    y, name = planned(fft_transform(n, 1), x, opts)
+    assert name.startswith("fft-l2-blocked"), name
+    ref, ref_name = planned(fft_transform(n, 1), x, cb.PlanOptions(mapping="8+8+" + "+".join(
+        str(p) for p in ([log_n - 16] if log_n - 16 <= 10 else [(log_n - 16) // 2, log_n - 16 - (log_n - 16) // 2]))))
+    assert ref_name.startswith("fft-stockham-global"), ref_name
+    assert _rel_l2_dev(y, ref) <= TOL, (name, ref_name)
+    bins = np.sort(w.rng(79, log_n).integers(0, n, size=8))
+    got = y[torch.as_tensor(bins, device=cuda)].cpu().numpy().view(np.complex64).reshape(-1)
+    assert rel_l2(got, oracle.dft_bins(x.cpu().numpy().view(np.complex64).reshape(-1), bins)) <= TOL
+    back, _ = planned(fft_transform(n, 1, inverse=True, normalize=True), y, opts)
+    assert _rel_l2_dev(back, x) <= TOL
+    z = x.clone()
+    z, _ = planned(fft_transform(n, 1, in_place=True), z, opts)
+    assert _rel_l2_dev(z, y) <= TOL

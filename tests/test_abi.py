@@ -174,7 +174,8 @@ def test_planner_single_pass_fwht_and_multipass_fft(lib):
     # blocks of the 2^30 results plus one 64 MiB chunk staging buffer
     assert blocked[0]["workspace_bytes"] == (8 << 30) + (64 << 20)
     assert ms[0]["family"] == "fft-stockham-global"  # measured faster (18.6 vs 24.8 ms on a B200)
-    assert all(p["units_per_cta"] >= 16 for m in ms for p in m["passes"])  # >= 128-byte global runs
+    # >= 128-byte global runs (the blocked plan's narrow passes take 64-byte runs)
+    assert all(p["units_per_cta"] >= 16 for m in ms if m["family"] == "fft-stockham-global" for p in m["passes"])
     ms = rank(lib, cb.Transform(op=cb.Operator.FFT, extents=[1 << 21], batch=1, in_place=True))
     assert ms[0]["workspace_bytes"] == 2 * (8 << 21)  # odd pass count in place: two halves
 

@@ -11,7 +11,9 @@ over all GPUs; every rank transforms its own full batch (weak scaling, no
 data-path collective).  `e2e` repeats the step through the public C ABI with
 host buffers (pinned host -> device copy of the input and device -> host copy
 of both outputs inside the timed region).  `ops` reports the other hot-path
-configurations (FFT, RNS NTT, subset zeta) on the same GPU.
+configurations (FFT, RNS NTT, subset zeta) on the same GPU; `strong_scaling` splits configs 2, 3 and 4 over the ranks
+(limbs 32/P, transforms 16/P, 2^20 FFTs / P, the 2^30 FFT as a four-step
+over NCCL with its per-phase times), each the max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -43,6 +45,8 @@ def parse():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-ops", action="store_true", help="skip the per-op table (FFT, NTT, zeta)")
     p.add_argument("--cpu-baseline", choices=["auto", "skip"], default="auto")
+    p.add_argument("--no-strong", action="store_true",
+                   help="skip the strong-scaled configurations (limbs, zeta transforms, FFT batch, 2^30 FFT)")
     p.add_argument("--only", choices=["fwht4096", "fwht128", "fft", "zeta", "ntt", "fft1g"],
                    help="run just this operator's launches (profiling driver; prints a short JSON line)")
     p.add_argument("--inventory", action="store_true",
@@ -583,6 +587,8 @@ def main():
     traffic = traffic_summary().get("fwht_bf16_4096", {}).get("dram_bytes_per_launch")
     ops = {} if args.no_ops else measure_ops(cb, lib, dev, stream, peak, max(5, args.steps // 2), args.warmup)
 
+    strong = None if args.no_strong else strong_scaling(world, rank, dev, lib, stream)
+
     cpu = None
     if rank == 0 and world == 1 and args.cpu_baseline == "auto":
         cpu = cpu_baseline()
@@ -618,11 +624,128 @@ def main():
             "clocks": clocks.summary(),
             "cpu_baseline": cpu,
             "ops": ops,
+            "strong_scaling": strong,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def strong_scaling(world, rank, dev, lib, stream):
+    """Strong-scaled configurations at this world size, every rank its share
+    of a fixed total, no collective on the data path except the four-step's
+    exchanges: config 2's 32 limbs (each rank only its domains' tables),
+    config 3's 16 transforms, config 4's batch sweep (2^20 transforms of 4096
+    points) and config 4's single 2^30-point transform (the single-GPU plan at
+    one rank, the four-step over NCCL beyond).  Times are CUDA events around
+    a few executions after warm-up, the max over ranks; GB/s count the whole
+    job's input + output once."""
+    import torch
+    import torch.distributed as dist
+
+    import cubutterfly_b200 as cb
+    from cubutterfly_b200 import rns
+    from cubutterfly_b200 import workloads as w
+    from cubutterfly_b200.distributed import FourStepFFT, shard_range, shard_rns_config
+
+    sp = stream.cuda_stream
+    out = {}
+
+    def timed(fn, steps, warmup=2):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # config 2: 32 limbs of 2^16, limbs 32/P per rank
+    cfg = w.rns_config()
+    shard, first, count = shard_rns_config(cfg, world, rank)
+    qs = [d["modulus"] for d in shard["domains"]] if count else []
+    x = w.torch_ntt_input([shard["domains"][p["domain"]]["modulus"] for p in shard["polynomials"]], w.NTT_LOG_N,
+                          dev) if count else None
+    y = torch.empty_like(x) if count else None
+    plan = rns.Plan(rns.Library(), shard) if count else None
+    if plan:
+        plan.prepare(stream=sp, repetitions=1)
+    ms = timed(lambda: plan.execute(x.data_ptr(), y.data_ptr(), stream=sp) if plan else None, 50)
+    total = 2 * w.NTT_LIMBS * (1 << w.NTT_LOG_N) * 8
+    out["rns_ntt_u64_32x2^16"] = {"ms": round(ms, 5), "gbs": round(total / ms / 1e6, 1),
+                                  "per_rank": f"{count} limbs, {len(qs)} domains' tables"}
+    if plan:
+        plan.close()
+    del x, y
+    # config 3: 16 transforms of 2^24, 16/P per rank
+    zs, zc = shard_range(w.ZETA_BATCH, world, rank)
+    z = w.torch_zeta_input(w.ZETA_LOG_N, zc, dev) if zc else None
+    t = cb.Transform(op=cb.Operator.SUBSET_ZETA, storage=cb.DataType.UINT32, extents=[1 << w.ZETA_LOG_N],
+                     batch=max(zc, 1), in_place=True)
+    zp = cb.Plan(lib, t, stream=sp) if zc else None
+    ms = timed(lambda: zp.execute(z.data_ptr(), z.data_ptr()) if zp else None, 5)
+    total = 2 * w.ZETA_BATCH * (1 << w.ZETA_LOG_N) * 4
+    out["zeta_u32_2^24x16"] = {"ms": round(ms, 4), "gbs": round(total / ms / 1e6, 1), "per_rank": f"{zc} transforms"}
+    if zp:
+        zp.close()
+    del z
+    # config 4 batch sweep: 2^20 transforms of 4096 points
+    fs, fc = shard_range(1 << 20, world, rank)
+    xb = w.torch_fft_input(4096, fc, dev, seed=rank)
+    yb = torch.empty_like(xb)
+    fp = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[4096], batch=fc), stream=sp)
+    ms = timed(lambda: fp.execute(xb.data_ptr(), yb.data_ptr()), 3)
+    total = 2 * (1 << 20) * 4096 * 8
+    out["fft_c64_4096x2^20"] = {"ms": round(ms, 4), "gbs": round(total / ms / 1e6, 1), "per_rank": f"{fc} transforms"}
+    fp.close()
+    del xb, yb
+    torch.cuda.empty_cache()
+    # config 4: one 2^30-point transform
+    n = 1 << 30
+    if world == 1:
+        xs = w.torch_fft_input(n, 1, dev, seed=4).reshape(n, 2)
+        ys = torch.empty_like(xs)
+        sp1 = cb.Plan(lib, cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1), stream=sp)
+        ws = torch.empty(sp1.workspace_size(), dtype=torch.uint8, device=dev)
+        sp1.set_workspace(ws.data_ptr(), ws.numel())
+        ms = timed(lambda: sp1.execute(xs.data_ptr(), ys.data_ptr()), 3, warmup=1)
+        entry = {"algorithm": sp1.algorithm_name()}
+        sp1.close()
+        del xs, ys, ws
+    else:
+        g = torch.Generator(device=dev).manual_seed(rank)
+        xs = torch.rand((n // world, 2), generator=g, device=dev, dtype=torch.float32)
+        four = FourStepFFT(n, device=dev)
+        ms = timed(lambda: four(xs), 3, warmup=1)
+        four.record_phases = True
+        four(xs)
+        phases = four.phase_ms()
+        four.record_phases = False
+        if world > 1:
+            keys = sorted(phases)
+            t = torch.tensor([phases[k] for k in keys], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            phases = dict(zip(keys, (float(v) for v in t.tolist())))
+        entry = {"algorithm": f"four-step {four.shape.n1}x{four.shape.n2} over {world} ranks (NCCL)",
+                 "phases_ms": {k: round(v, 3) for k, v in phases.items()},
+                 "limiting_phase": max(phases, key=phases.get) if phases else None}
+        four.close()
+        del xs
+    torch.cuda.empty_cache()
+    entry.update(ms=round(ms, 3), gbs=round(2 * n * 8 / ms / 1e6, 1))
+    out["fft_c64_2^30"] = entry
+    return out
 
 
 def time_launches(fn, stream, steps, warmup):

@@ -46,6 +46,33 @@ def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
     return start, base + (1 if rank < extra else 0)
 
 
+def shard_rns_config(config: dict, world: int, rank: int) -> tuple[dict, int, int]:
+    """`rank`'s share of an RNS request: a contiguous range [first, first +
+    count) of its polynomials (by position), each kept with its own domain.
+
+    The returned request holds only the domains that share uses (renumbered in
+    order of first use), so a GPU builds and keeps only those root tables, and
+    places its polynomials packed in its own buffers: polynomial first + i at
+    input and output offset i * 2^log_n.  Returns (config, first, count); a
+    rank whose share is empty gets count 0 and config None."""
+    polys = config["polynomials"]
+    first, count = shard_range(len(polys), world, rank)
+    if count == 0:
+        return None, first, 0
+    n = 1 << int(config["log_n"])
+    remap: dict[int, int] = {}
+    domains, mine = [], []
+    for i, p in enumerate(polys[first:first + count]):
+        d = int(p["domain"])
+        if d not in remap:
+            remap[d] = len(domains)
+            domains.append(dict(config["domains"][d]))
+        mine.append({"domain": remap[d], "input_offset": i * n, "output_offset": i * n})
+    shard = {k: v for k, v in config.items() if k not in ("domains", "polynomials")}
+    shard["domains"], shard["polynomials"] = domains, mine
+    return shard, first, count
+
+
 def _log2(n: int) -> int:
     if n <= 0 or n & (n - 1):
         raise ValueError("length must be a power of two")
@@ -160,6 +187,27 @@ class FourStepFFT:
             self._transpose = transpose
             self._permute = permute
         self._bufs = None
+        # per-phase CUDA events of the last call when phase timing is on
+        self.record_phases = False
+        self._marks: list[tuple[str, torch.cuda.Event]] = []
+
+    def _mark(self, phase: str) -> None:
+        """Close the current phase (named `phase`) at this point of the stream."""
+        if self.record_phases:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._marks.append((phase, ev))
+
+    def phase_ms(self) -> dict:
+        """Device time per phase of the last call (permute, exchange, fft,
+        twiddle, transpose), summed over its occurrences; synchronises."""
+        if len(self._marks) < 2:
+            return {}
+        self._marks[-1][1].synchronize()
+        out: dict[str, float] = {}
+        for (_, a), (name, b) in zip(self._marks, self._marks[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
 
     def _exchange(self, send: torch.Tensor, recv: torch.Tensor) -> None:
         """Block q of `send` goes to rank q, block q of `recv` comes from rank q,
@@ -189,42 +237,54 @@ class FourStepFFT:
             raise ValueError(f"expected a float32 shard of shape ({s.local}, 2)")
         n1p, n2p = s.n1 // p, s.n2 // p
         buf_a, buf_b, buf_c = self._buffers(x.device)
+        self._marks = []
+        self._mark("start")
         # 1. my rows n1, every rank's column block: block[q][i][j] = A[q N1/P + i][r N2/P + j],
         #    i.e. the N1 x N2/P block of my columns, row-major (my own block is permuted in place)
         if p > 1:
             send, block = buf_a.view(p, n1p, n2p, 2), buf_b.view(p, n1p, n2p, 2)
             self._permute(x, send, n1p, p, n2p, r, out_self=block[r])
+            self._mark("permute")
             self._exchange(send, block)
+            self._mark("exchange")
             block = block.view(s.n1, n2p, 2)
         else:
             block = x.view(s.n1, n2p, 2)
         # 2. column FFTs (length N1) on the block's columns, then W_N^(k1 n2), n2 = r N2/P + j
         spec = buf_c.view(s.n1, n2p, 2)
         self._cols(block, spec)
+        self._mark("fft")
         self._twiddle(spec, s.n1, n2p, 0, r * n2p, s.n, self.inverse)
+        self._mark("twiddle")
         # 3. k1 row blocks as they lie: recv[q][i][j] = C[r N1/P + i][q N2/P + j], then rows of length N2
         if p > 1:
             blocks, recv = spec.view(p, n1p, n2p, 2), buf_a.view(p, n1p, n2p, 2)
             self._exchange(blocks, recv)
+            self._mark("exchange")
             rows = buf_b.view(n1p, p, n2p, 2)
             self._permute(recv, rows, p, n1p, n2p, r, in_self=blocks[r])
+            self._mark("permute")
             rows = rows.view(n1p, s.n2, 2)
             out = buf_c.view(n1p, s.n2, 2)
         else:
             rows, out = spec.view(n1p, s.n2, 2), buf_a.view(n1p, s.n2, 2)
         # 4. row FFTs (length N2): E[i][k2] = X[(r N1/P + i) + N1 k2]
         self._rows(rows, out)
+        self._mark("fft")
         # 5. column blocks k2 in [q N2/P, ...) to rank q: back[q][i][j] = X[(q N1/P + i) + N1 (r N2/P + j)],
         #    an N1 x N2/P block whose transpose is my natural-order shard X[r N/P + j N1 + k1]
         if p > 1:
             send, back = buf_a.view(p, n1p, n2p, 2), buf_b.view(p, n1p, n2p, 2)
             self._permute(out, send, n1p, p, n2p, r, out_self=back[r])
+            self._mark("permute")
             self._exchange(send, back)
+            self._mark("exchange")
             back = back.view(s.n1, n2p, 2)
         else:
             back = out.view(s.n1, n2p, 2)
         result = torch.empty((s.local, 2), dtype=torch.float32, device=x.device)
         self._transpose(back, result, s.n1, n2p)
+        self._mark("transpose")
         return result
 
     def close(self):

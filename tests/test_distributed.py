@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from cubutterfly_b200.distributed import FourStepFFT, FourStepShape, shard_range
+from cubutterfly_b200.distributed import FourStepFFT, FourStepShape, shard_range, shard_rns_config
 
 
 def free_port():
@@ -40,6 +40,77 @@ def test_four_step_shape():
     assert (s.n1, s.n2, s.local) == (1 << 15, 1 << 15, 1 << 27)
     with pytest.raises(ValueError):
         FourStepShape(1 << 4, 8)
+
+
+def test_shard_rns_config_keeps_only_used_domains():
+    """Shares are contiguous by polynomial position; each share carries only
+    the domains its polynomials use, renumbered, and packs its polynomials."""
+    from cubutterfly_b200 import workloads as w
+
+    cfg = w.rns_config(count=4, log_n=12)
+    n = 1 << 12
+    # polynomials in domains 3, 1, 3, 0 at scattered offsets
+    cfg["polynomials"] = [{"domain": d, "input_offset": 9 * n - i * n, "output_offset": i * 2 * n}
+                          for i, d in enumerate([3, 1, 3, 0])]
+    shard, first, count = shard_rns_config(cfg, 2, 0)
+    assert (first, count) == (0, 2)
+    assert [d["modulus"] for d in shard["domains"]] == [cfg["domains"][3]["modulus"], cfg["domains"][1]["modulus"]]
+    assert shard["polynomials"] == [{"domain": 0, "input_offset": 0, "output_offset": 0},
+                                    {"domain": 1, "input_offset": n, "output_offset": n}]
+    shard, first, count = shard_rns_config(cfg, 2, 1)
+    assert (first, count) == (2, 2) and len(shard["domains"]) == 2
+    assert shard_rns_config(cfg, 8, 7) == (None, 4, 0)
+
+
+def _shard_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from cubutterfly_b200 import workloads as w
+        from oracle.oracle import Oracle
+
+        o = Oracle()
+        # RNS limbs: 5 polynomials over the ranks, each rank only its domains
+        cfg = w.rns_config(count=5, log_n=12)
+        xs = w.ntt_input([d["modulus"] for d in cfg["domains"]], log_n=12, seed=5)
+        shard, first, count = shard_rns_config(cfg, world, rank)
+        mine = np.empty((0, 1 << 12), dtype=np.uint64)
+        if count:
+            qs = [shard["domains"][p["domain"]]["modulus"] for p in shard["polynomials"]]
+            roots = [shard["domains"][p["domain"]]["root"] for p in shard["polynomials"]]
+            mine = o.rns_ntt(xs[first:first + count], qs, roots)
+        # zeta transforms: 7 of them over the ranks
+        z = w.zeta_input(10, 7, seed=6)
+        zs, zc = shard_range(7, world, rank)
+        zmine = o.zeta(z[zs:zs + zc])
+        parts = [None] * world
+        dist.all_gather_object(parts, (first, mine, zs, zmine))
+        if rank == 0:
+            ntt_all = np.concatenate([p[1] for p in sorted(parts, key=lambda t: t[0])])
+            want = o.rns_ntt(xs, [d["modulus"] for d in cfg["domains"]], [d["root"] for d in cfg["domains"]])
+            zeta_all = np.concatenate([p[3] for p in sorted(parts, key=lambda t: t[2])])
+            q.put(bool(np.array_equal(ntt_all, want)) and bool(np.array_equal(zeta_all, o.zeta(z))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_limb_and_transform_sharding_gloo(world):
+    """Batch-sharded NTT limbs and zeta transforms: every rank transforms its
+    share (CPU oracle standing in for the GPU plan), rank 0 gathers and finds
+    the whole batch's result, bit-exact."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    ok = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert ok
 
 
 def numpy_fft_factory(inverse, normalize):

@@ -662,6 +662,14 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         launch_ntt(p, m, in, out, stream);
         return;
     }
+    // Caller buffers that are element-aligned but not 16-byte aligned (the
+    // reference accepts any element pointer): complex FFTs and NTTs move whole
+    // elements already; FWHT and zeta take their element-granular kernels
+    // (csrc/unaligned.cu); the stage-storage kernels below have none.
+    const bool vec16 = ((reinterpret_cast<std::uintptr_t>(in) | reinterpret_cast<std::uintptr_t>(out)) & 15) == 0;
+    if (!vec16 && (p.req.fwht_native || d.op == CUBUTTERFLY_OPERATOR_STRUCTURED_2X2))
+        throw cubf::Unsupported(std::string(p.req.fwht_native ? "stage-storage FWHT" : "structured 2x2") +
+                                " plans need 16-byte aligned input and output buffers");
     if (p.req.fwht_native) {
         check_cuda(cubf::launch_fwht_native(d.storage == CUBUTTERFLY_DATA_BF16, p.req.log_n, in, out, d.batch,
                                             inverse && d.normalize_inverse, stream),
@@ -721,6 +729,17 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
     if (d.op == CUBUTTERFLY_OPERATOR_FWHT) {
         scale = d.output_scale;
         if (inverse && d.normalize_inverse) scale /= static_cast<double>(n);
+    }
+    if (!vec16) {
+        if (d.op == CUBUTTERFLY_OPERATOR_FWHT)
+            check_cuda(cubf::launch_fwht_unaligned(p.req.bw_type, p.req.log_n, in, out, d.batch,
+                                                   static_cast<float>(scale), stream),
+                       "element-granular FWHT launch");
+        else
+            check_cuda(cubf::launch_zeta_unaligned(p.req.bw_type, p.req.bw_op == cubf::BwOp::ZetaSuperset,
+                                                   p.req.log_n, in, out, d.batch, inverse, stream),
+                       "element-granular zeta launch");
+        return;
     }
     if (m.passes.front().kind == cubf::PassKind::FwhtTensor) {
         check_cuda(cubf::launch_fwht_tc(in, out, d.batch, static_cast<float>(scale), p.status_dev, stream),
@@ -2059,6 +2078,19 @@ void clear_device_status(cubutterflyPlan& p) {
         if (a.plan) clear_device_status(*a.plan);
 }
 
+// Caller pointers must be aligned to their element (the reference's contract:
+// any element pointer of a cudaMalloc'd buffer); real FFT data moves as
+// float2 pairs, so its real side needs 8 bytes.
+void check_element_alignment(const cubutterflyPlan& p, const void* input, const void* output) {
+    const auto& d = p.desc;
+    std::size_t in_align = cubf::storage_bytes(d.storage), out_align = in_align;
+    if (d.op == CUBUTTERFLY_OPERATOR_FFT && d.fft_type != CUBUTTERFLY_FFT_C2C) in_align = out_align = 8;
+    require(reinterpret_cast<std::uintptr_t>(input) % in_align == 0,
+            "input must be aligned to its element (" + std::to_string(in_align) + " bytes)");
+    require(reinterpret_cast<std::uintptr_t>(output) % out_align == 0,
+            "output must be aligned to its element (" + std::to_string(out_align) + " bytes)");
+}
+
 // A failure that an earlier launch of this plan recorded on the device (a
 // bounded wait that expired: that launch's output is invalid) is the status
 // of the next call on the plan; reporting it clears it.
@@ -2085,8 +2117,7 @@ cubutterflyStatus_t cubutterflyExecute(cubutterflyHandle_t handle, cubutterflyPl
         require(in_place == (input == output),
                 in_place ? "in-place plans require input == output" : "out-of-place plans require input != output");
         require(plan->mapping.workspace_bytes == 0 || plan->workspace != nullptr, "plan workspace is not set");
-        require((reinterpret_cast<std::uintptr_t>(input) | reinterpret_cast<std::uintptr_t>(output)) % 16 == 0,
-                "input and output must be 16-byte aligned (the kernels move 16-byte vectors)");
+        check_element_alignment(*plan, input, output);
         launch_mapping(*plan, plan->mapping, input, output, handle->stream);
         plan->steady_stream = handle->stream;
         plan->steady_ready = true;
@@ -2102,8 +2133,7 @@ cubutterflyStatus_t cubutterflyExecuteSteady(cubutterflyHandle_t handle, cubutte
         const bool in_place = plan->desc.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE;
         require(input != nullptr && output != nullptr && in_place == (input == output),
                 "pointer aliasing does not match the plan placement");
-        require((reinterpret_cast<std::uintptr_t>(input) | reinterpret_cast<std::uintptr_t>(output)) % 16 == 0,
-                "input and output must be 16-byte aligned (the kernels move 16-byte vectors)");
+        check_element_alignment(*plan, input, output);
         launch_mapping(*plan, plan->mapping, input, output, handle->stream);
     });
 }

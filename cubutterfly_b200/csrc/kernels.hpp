@@ -104,6 +104,14 @@ struct BwChain {
     float scale = 1.0f;
 };
 bool bw_chain_available(BwOp op, BwType type, int log_h0, int log_h1);
+
+// Element-granular FWHT (FP32 arithmetic, one rounding to storage; rows of up
+// to 2^14) and zeta (any length) for buffers that are element-aligned but not
+// 16-byte aligned (csrc/unaligned.cu); `in` may equal `out`.
+cudaError_t launch_fwht_unaligned(BwType type, int log_n, const void* in, void* out, std::size_t rows, float scale,
+                                  cudaStream_t stream);
+cudaError_t launch_zeta_unaligned(BwType type, bool superset, int log_n, const void* in, void* out,
+                                  std::size_t batch, bool inverse, cudaStream_t stream);
 cudaError_t launch_bw_chain(BwOp op, BwType type, const BwChain& c, const void* in, void* out, cudaStream_t stream);
 
 // ---- FWHT on the tensor cores (tcgen05) ------------------------------------------
@@ -209,6 +217,7 @@ struct NttVariant {
     bool inverse;         // Gentleman-Sande (bit-reversed in, natural out) vs Cooley-Tukey
     bool lazy;            // Harvey lazy reduction (every modulus < 2^62)
     bool word32 = false;  // 32-bit storage words (moduli < 2^32, always lazy)
+    int split = 0;        // strided pass bits ceil(L/2) + split (0; +-1 where ntt_split_available)
 };
 // One launch of a pass (2^12 .. 2^20: strided or contiguous tile pass over the
 // polynomials of `polys`, a DEVICE array of `count` entries) or of a
@@ -228,7 +237,14 @@ struct NttLaunch {
 constexpr int kNttSingleMaxLog = 11;
 constexpr int kNttMinLog = 12;
 constexpr int kNttMaxLog = 20;
-inline int ntt_pass_bits(int log_n, bool strided) { return strided ? (log_n + 1) / 2 : log_n / 2; }
+inline int ntt_pass_bits(int log_n, bool strided, int split = 0) {
+    return strided ? (log_n + 1) / 2 + split : log_n / 2 - split;
+}
+// Pass-split alternatives (lazy arithmetic, 2^14 .. 2^18, split -1 or +1).
+constexpr int kNttSplitMinLog = 14, kNttSplitMaxLog = 18;
+inline bool ntt_split_available(int log_n, int split, bool lazy) {
+    return split == 0 || (lazy && (split == 1 || split == -1) && log_n >= kNttSplitMinLog && log_n <= kNttSplitMaxLog);
+}
 // Two tile passes exist for 2^12 .. 2^20.
 bool ntt_available(const NttVariant& v);
 // A whole-transform tile exists for 2^1 .. 2^11.

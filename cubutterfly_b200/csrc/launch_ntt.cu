@@ -27,9 +27,9 @@ ntt::DomainTables device_tables(const NttTables& t) {
             reinterpret_cast<const ntt::u64*>(t.unit_q)};
 }
 
-template <int L, bool STRIDED, bool INV, bool LAZY>
+template <int L, bool STRIDED, bool INV, bool LAZY, int D = 0>
 struct Entry {
-    using S = ntt::PassShape<L, STRIDED, INV, LAZY>;
+    using S = ntt::PassShape<L, STRIDED, INV, LAZY, D>;
     static LaunchShape shape() {
         LaunchShape s;
         s.threads = S::TPB;
@@ -40,7 +40,7 @@ struct Entry {
         return s;
     }
     static cudaError_t launch(const NttLaunch& a, cudaStream_t stream) {
-        auto kernel = ntt::ntt_pass_kernel<L, STRIDED, INV, LAZY, Word>;
+        auto kernel = ntt::ntt_pass_kernel<L, STRIDED, INV, LAZY, Word, D>;
         static KernelSetup setup;
         int grid_cap = 0;
         cudaError_t e = setup_kernel(setup, kernel, S::TPB, S::SMEM_BYTES, &grid_cap);
@@ -93,6 +93,11 @@ struct Row {
     static constexpr LaunchFn launch[] = {Entry<L, STRIDED, INV, LAZY>::launch...};
     static constexpr ShapeFn shape[] = {Entry<L, STRIDED, INV, LAZY>::shape...};
 };
+template <int D, bool STRIDED, bool INV, int... L>
+struct SplitRow {
+    static constexpr LaunchFn launch[] = {Entry<L, STRIDED, INV, true, D>::launch...};
+    static constexpr ShapeFn shape[] = {Entry<L, STRIDED, INV, true, D>::shape...};
+};
 template <bool INV, bool LAZY, int... L>
 struct SingleRow {
     static constexpr LaunchFn launch[] = {SingleEntry<L, INV, LAZY>::launch...};
@@ -103,9 +108,35 @@ struct SingleRow {
 static_assert(kNttSingleMaxLog == 11 && kNttMinLog == 12, "instantiated length ranges");
 
 // Pass tables [inverse][strided][lazy]; 32-bit words map strict requests to lazy.
+#define CUBF_NTT_SPLIT_LOGS 14, 15, 16, 17, 18
+static_assert(kNttSplitMinLog == 14 && kNttSplitMaxLog == 18, "instantiated split range");
+
+template <typename Fn, bool FOR_SHAPE>
+Fn pick_split(const NttVariant& v) {
+    const int s = v.log_n - kNttSplitMinLog;
+#define CUBF_PICK(D, STR, INV)                                                             \
+    if constexpr (FOR_SHAPE) return SplitRow<D, STR, INV, CUBF_NTT_SPLIT_LOGS>::shape[s];   \
+    else return SplitRow<D, STR, INV, CUBF_NTT_SPLIT_LOGS>::launch[s];
+    if (v.split > 0) {
+        if (v.strided) {
+            if (v.inverse) { CUBF_PICK(1, true, true) } else { CUBF_PICK(1, true, false) }
+        } else {
+            if (v.inverse) { CUBF_PICK(1, false, true) } else { CUBF_PICK(1, false, false) }
+        }
+    } else {
+        if (v.strided) {
+            if (v.inverse) { CUBF_PICK(-1, true, true) } else { CUBF_PICK(-1, true, false) }
+        } else {
+            if (v.inverse) { CUBF_PICK(-1, false, true) } else { CUBF_PICK(-1, false, false) }
+        }
+    }
+#undef CUBF_PICK
+}
+
 template <typename Fn, bool FOR_SHAPE>
 Fn pick_pass(const NttVariant& v) {
     const bool lazy = v.lazy || !kHasStrict;
+    if (v.split != 0) return pick_split<Fn, FOR_SHAPE>(v);
     const int s = v.log_n - kNttMinLog;
 #define CUBF_PICK(INV, STR)                                                                              \
     if (lazy) {                                                                                          \
@@ -153,12 +184,14 @@ namespace detail {
 #endif
 
 LaunchShape CUBF_NTT_FN(ntt_shape)(const NttVariant& v) {
+    if (!ntt_split_available(v.log_n, v.split, v.lazy || !kHasStrict)) return {};
     if (v.log_n >= kNttMinLog && v.log_n <= kNttMaxLog) return pick_pass<ShapeFn, true>(v)();
     if (v.log_n >= 1 && v.log_n <= kNttSingleMaxLog) return pick_single<ShapeFn, true>(v)();
     return {};
 }
 
 cudaError_t CUBF_NTT_FN(launch_ntt)(const NttVariant& v, const NttLaunch& a, cudaStream_t stream) {
+    if (!ntt_split_available(v.log_n, v.split, v.lazy || !kHasStrict)) return cudaErrorInvalidValue;
     if (v.log_n >= kNttMinLog && v.log_n <= kNttMaxLog) return pick_pass<LaunchFn, false>(v)(a, stream);
     if (v.log_n >= 1 && v.log_n <= kNttSingleMaxLog) return pick_single<LaunchFn, false>(v)(a, stream);
     return cudaErrorInvalidValue;

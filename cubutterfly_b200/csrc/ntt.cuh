@@ -271,19 +271,20 @@ CUBF_DEV void ntt_groups(u64 (&v)[S::E], u64* sbuf, int col, uint32_t t, u64 hi,
 }
 
 // Tile geometry of the two passes of a 2^L transform: the strided pass covers
-// the top ceil(L/2) index bits, the contiguous pass the low floor(L/2) bits.
-constexpr int strided_bits(int L) { return (L + 1) / 2; }
-constexpr int contiguous_bits(int L) { return L / 2; }
+// the top ceil(L/2) + D index bits, the contiguous pass the low floor(L/2) - D
+// bits (D = 0 by default; the RNS tuner also tries D = -1 and +1).
+constexpr int strided_bits(int L, int D = 0) { return (L + 1) / 2 + D; }
+constexpr int contiguous_bits(int L, int D = 0) { return L / 2 - D; }
 constexpr int log_e_for(int b) { return b <= 6 ? 3 : (b <= 8 ? 4 : 5); }
 // Strided passes keep 16 adjacent columns (128-byte rows of uint64) per CTA;
 // contiguous passes pack tiles up to 256 threads.
 constexpr int cols_for(int b, bool strided) {
     return strided ? 16 : ((256 >> (b - log_e_for(b))) > 0 ? (256 >> (b - log_e_for(b))) : 1);
 }
-template <int L, bool STRIDED, bool INV, bool LAZY>
-using PassShape = NttShape<STRIDED ? strided_bits(L) : contiguous_bits(L),
-                           log_e_for(STRIDED ? strided_bits(L) : contiguous_bits(L)),
-                           cols_for(STRIDED ? strided_bits(L) : contiguous_bits(L), STRIDED), STRIDED, INV, LAZY>;
+template <int L, bool STRIDED, bool INV, bool LAZY, int D = 0>
+using PassShape = NttShape<STRIDED ? strided_bits(L, D) : contiguous_bits(L, D),
+                           log_e_for(STRIDED ? strided_bits(L, D) : contiguous_bits(L, D)),
+                           cols_for(STRIDED ? strided_bits(L, D) : contiguous_bits(L, D), STRIDED), STRIDED, INV, LAZY>;
 
 // One tile pass over every polynomial of a 2^L transform.  Forward runs the
 // strided pass (stages 0..B1-1) then the contiguous pass; inverse runs them in
@@ -302,11 +303,11 @@ CUBF_DEV u64 final_value(u64 v, u64 q, bool final_pass, bool scale, u64 ni, u64 
 
 // T is the storage word (unsigned int or u64); `reduce_input` reduces each
 // loaded word modulo q first, so any 64-bit input is accepted.
-template <int L, bool STRIDED, bool INV, bool LAZY, typename T>
-__global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY>::TPB, PassShape<L, STRIDED, INV, LAZY>::MINB)
+template <int L, bool STRIDED, bool INV, bool LAZY, typename T, int D = 0>
+__global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY, D>::TPB, PassShape<L, STRIDED, INV, LAZY, D>::MINB)
     ntt_pass_kernel(const T* in, T* out, const PolyDesc* __restrict__ polys, DomainTables tab, int in_is_out,
                     int final_pass, int final_scale, int reduce_input) {
-    using S = PassShape<L, STRIDED, INV, LAZY>;
+    using S = PassShape<L, STRIDED, INV, LAZY, D>;
     using Gs = typename S::Gs;
     constexpr int B = S::B;
     constexpr int COLS = S::COLS;

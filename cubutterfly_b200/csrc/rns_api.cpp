@@ -196,7 +196,12 @@ struct cubutterflyRnsPlanOpaque {
     bool prepared = false;
     bool in_place = false;
     bool needs_scratch = false;
-    bool lazy = false;  // every modulus < 2^62: Harvey lazy butterflies
+    bool lazy = false;  // every modulus < 2^62: Harvey lazy butterflies allowed
+    // The mapping Prepare chose: pass split (strided bits ceil(L/2) + split)
+    // and arithmetic (lazy or fully reduced Shoup products).
+    int split = 0;
+    bool use_lazy = false;
+    Json candidates = Json::array();  // Prepare's timings, {mapping, kernel_ms}
     std::size_t scratch_bytes = 0;
     DeviceBuffer root_pairs, moduli, n_inv, n_inv_q, polys, polys_scratch, scratch;
     cubf::NttTables tables{};
@@ -206,20 +211,23 @@ struct cubutterflyRnsPlanOpaque {
     std::string source = "unprepared";
     double kernel_ms = 0.0;
 
-    Json mapping_json() const {
+    Json mapping_json() const { return mapping_json_for(split, use_lazy); }
+
+    Json mapping_json_for(int sp, bool lz) const {
         const int l = static_cast<int>(config.log_n);
-        const auto s1 = cubf::ntt_shape({l, true, config.inverse});
-        const auto s2 = cubf::ntt_shape({l, false, config.inverse});
+        const auto s1 = cubf::ntt_shape({l, true, config.inverse, lz, false, sp});
+        const auto s2 = cubf::ntt_shape({l, false, config.inverse, lz, false, sp});
         return {{"schema_version", 1},
                 {"core_family", "b200_two_pass_tile"},
-                {"strided_bits", cubf::ntt_pass_bits(l, true)},
-                {"contiguous_bits", cubf::ntt_pass_bits(l, false)},
+                {"split", sp},
+                {"strided_bits", cubf::ntt_pass_bits(l, true, sp)},
+                {"contiguous_bits", cubf::ntt_pass_bits(l, false, sp)},
                 {"strided_threads", s1.threads},
                 {"contiguous_threads", s2.threads},
                 {"strided_columns", s1.units_per_cta},
                 {"contiguous_tiles", s2.units_per_cta},
                 {"values_per_thread", s1.elems_per_thread},
-                {"arithmetic", lazy ? "shoup-lazy" : "shoup"},
+                {"arithmetic", lz ? "shoup-lazy" : "shoup"},
                 {"order", config.inverse ? "contiguous_then_strided" : "strided_then_contiguous"}};
     }
 
@@ -265,6 +273,7 @@ struct cubutterflyRnsPlanOpaque {
             ni[d] = powmod(static_cast<u64>(n), q - 2, q);
             niq[d] = shoup(ni[d], q);
         }
+        use_lazy = lazy;
         check(cudaGetDevice(&device), "current device");
         std::vector<u64> rp(2 * r.size());
         for (std::size_t k = 0; k < r.size(); ++k) {
@@ -298,7 +307,7 @@ struct cubutterflyRnsPlanOpaque {
         const int l = static_cast<int>(config.log_n);
         const std::size_t count = config.polynomials.size();
         const bool inv = config.inverse;
-        const cubf::NttVariant first{l, !inv, inv, lazy}, second{l, inv, inv, lazy};
+        const cubf::NttVariant first{l, !inv, inv, use_lazy, false, split}, second{l, inv, inv, use_lazy, false, split};
         cubf::NttLaunch a1, a2;
         a1.count = a2.count = count;
         a1.tables = a2.tables = tables;
@@ -476,8 +485,18 @@ int cubutterflyRnsPrepare(cubutterflyRnsPlan plan, int placement, const char* ca
                 in >> rec;
                 if (rec.at("identity") != identity)
                     throw std::runtime_error("RNS cache identity mismatch: " + path);
-                if (rec.at("mapping") != plan->mapping_json())
+                // the record's mapping (split and arithmetic) must be one this
+                // build executes for this request
+                const Json& m = rec.at("mapping");
+                const int sp = m.value("split", 0);
+                const bool lz = m.value("arithmetic", "") == "shoup-lazy";
+                if ((lz && !plan->lazy) || m != plan->mapping_json_for(sp, lz) ||
+                    cubf::ntt_shape({static_cast<int>(plan->config.log_n), true, plan->config.inverse, lz, false, sp})
+                            .threads == 0)
                     throw std::runtime_error("RNS cache mapping is not executable by this build: " + path);
+                plan->split = sp;
+                plan->use_lazy = lz;
+                plan->candidates = rec.value("candidates", Json::array());
                 plan->kernel_ms = rec.at("kernel_ms").get<double>();
                 require(std::isfinite(plan->kernel_ms) && plan->kernel_ms > 0, "invalid RNS cache kernel_ms");
                 plan->cache_hit = true;
@@ -487,7 +506,46 @@ int cubutterflyRnsPrepare(cubutterflyRnsPlan plan, int placement, const char* ca
             }
         }
         if (policy == 1) throw std::runtime_error("required RNS prepared cache record is missing: " + path);
-        plan->kernel_ms = time_plan(*plan, stream, repetitions);
+        // Candidate search: the pass splits this build has for the length
+        // (strided bits ceil(L/2) - 1, + 0, + 1) with lazy arithmetic where
+        // every modulus allows it, and the fully reduced arithmetic at the
+        // default split; each timed with CUDA events over `repetitions`
+        // executions.  The plan's mapping changes only once every candidate
+        // has been timed.
+        const int l = static_cast<int>(plan->config.log_n);
+        std::vector<std::pair<int, bool>> cands;
+        for (const int sp : {0, -1, 1})
+            for (const bool lz : {true, false}) {
+                if (lz && !plan->lazy) continue;
+                if (!cubf::ntt_split_available(l, sp, lz)) continue;
+                if (cubf::ntt_shape({l, true, plan->config.inverse, lz, false, sp}).threads == 0) continue;
+                cands.emplace_back(sp, lz);
+            }
+        const int keep_split = plan->split;
+        const bool keep_lazy = plan->use_lazy;
+        Json timings = Json::array();
+        double best = 0.0;
+        std::pair<int, bool> best_c = cands.front();
+        try {
+            for (const auto& c : cands) {
+                plan->split = c.first;
+                plan->use_lazy = c.second;
+                const double ms = time_plan(*plan, stream, repetitions);
+                timings.push_back({{"mapping", plan->mapping_json()}, {"kernel_ms", ms}});
+                if (timings.size() == 1 || ms < best) {
+                    best = ms;
+                    best_c = c;
+                }
+            }
+        } catch (...) {
+            plan->split = keep_split;
+            plan->use_lazy = keep_lazy;
+            throw;
+        }
+        plan->split = best_c.first;
+        plan->use_lazy = best_c.second;
+        plan->candidates = timings;
+        plan->kernel_ms = best;
         plan->source = path.empty() ? "uncached_event_timing" : "event_timing";
         if (!path.empty()) {
             ::mkdir(dir.c_str(), 0755);
@@ -495,6 +553,7 @@ int cubutterflyRnsPrepare(cubutterflyRnsPlan plan, int placement, const char* ca
                            {"identity", identity},
                            {"mapping", plan->mapping_json()},
                            {"kernel_ms", plan->kernel_ms},
+                           {"candidates", plan->candidates},
                            {"source", plan->source}};
             const std::string tmp = path + ".tmp";
             {
@@ -531,7 +590,8 @@ int cubutterflyRnsInfoJson(cubutterflyRnsPlan plan, char* buffer, size_t* bytes)
                         {"cache_hit", plan->cache_hit},
                         {"cache_key", plan->cache_key},
                         {"source", plan->source},
-                        {"kernel_ms", plan->kernel_ms}};
+                        {"kernel_ms", plan->kernel_ms},
+                        {"candidates", plan->candidates}};
         const std::string text = info.dump();
         const std::size_t capacity = *bytes;
         *bytes = text.size() + 1;

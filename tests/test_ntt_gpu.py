@@ -36,7 +36,7 @@ def test_config2_full_size(oracle, cuda):
     roots = [d["root"] for d in cfg["domains"]]
     x = w.ntt_input(qs)
     got, info = run_rns(cfg, x.reshape(-1), x.size)
-    assert info["prepared"] and info["mapping"]["strided_bits"] == 8
+    assert info["prepared"] and info["mapping"]["strided_bits"] + info["mapping"]["contiguous_bits"] == 16
     assert np.array_equal(got.reshape(x.shape), oracle.rns_ntt(x, qs, roots))
 
 
@@ -151,3 +151,38 @@ def test_round_trip_and_cache(oracle, cuda, tmp_path):
         p2.prepare(cache_directory=str(tmp_path), policy=rns.CachePolicy.REQUIRE, repetitions=2)
         info = p2.info()
         assert info["cache_hit"] and info["kernel_ms"] > 0
+
+
+def test_prepare_searches_candidates_and_each_is_exact(oracle, cuda, tmp_path):
+    """Prepare times every mapping this build has for the request (pass splits
+    8+8, 7+9, 9+7 with lazy arithmetic, and fully reduced arithmetic at 8+8),
+    keeps the fastest, and records all timings.  Each candidate, forced
+    through the plan cache (REQUIRE), is bit-exact against the oracle."""
+    cfg = w.rns_config(count=6, log_n=16)
+    qs = [d["modulus"] for d in cfg["domains"]]
+    roots = [d["root"] for d in cfg["domains"]]
+    x = w.ntt_input(qs, 16, seed=3)
+    want = oracle.rns_ntt(x, qs, roots)
+    lib = rns.Library()
+    stream = torch.cuda.current_stream().cuda_stream
+    with rns.Plan(lib, cfg) as plan:
+        plan.prepare(cache_directory=str(tmp_path), policy=rns.CachePolicy.REFRESH, repetitions=3, stream=stream)
+        info = plan.info()
+    cands = info["candidates"]
+    splits = sorted((c["mapping"]["split"], c["mapping"]["arithmetic"]) for c in cands)
+    assert splits == [(-1, "shoup-lazy"), (0, "shoup"), (0, "shoup-lazy"), (1, "shoup-lazy")]
+    best = min(cands, key=lambda c: c["kernel_ms"])
+    assert info["mapping"] == best["mapping"] and info["kernel_ms"] == best["kernel_ms"]
+    (record_path,) = list(tmp_path.glob("*.json"))
+    record = json.loads(record_path.read_text())
+    for c in cands:
+        record["mapping"] = c["mapping"]
+        record_path.write_text(json.dumps(record))
+        with rns.Plan(lib, cfg) as plan:
+            plan.prepare(cache_directory=str(tmp_path), policy=rns.CachePolicy.REQUIRE, repetitions=3, stream=stream)
+            assert plan.info()["mapping"] == c["mapping"]
+            din = torch.from_numpy(x.view(np.int64).copy()).to(cuda)
+            dout = torch.empty_like(din)
+            plan.execute(din.data_ptr(), dout.data_ptr(), stream=stream)
+            torch.cuda.synchronize()
+            assert np.array_equal(dout.cpu().numpy().view(np.uint64), want), c["mapping"]

@@ -154,8 +154,8 @@ struct LocalShape {
 // load R values per sub-DFT, apply the inter-pass twiddle
 // W_{Ns R}^{(j mod Ns) r} = W_N^{(j mod Ns) r N/(Ns R)}, run the register DFT;
 // then store with the Stockham autosort index.
-template <int LOGN, int P, typename Load>
-CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const TwiddleTable<LOGN>& tw, Load load) {
+template <int LOGN, int P, typename Twiddle, typename Load>
+CUBF_DEV void pass_load_tw(float2 (&v)[LocalShape<LOGN>::E], int th, Twiddle twf, Load load) {
     using S = LocalShape<LOGN>;
     constexpr int RB = S::radix_bits(P);
     constexpr int R = 1 << RB;
@@ -174,13 +174,18 @@ CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const TwiddleT
         if (NS > 1) {
             const int jm = j & (NS - 1);
 #pragma unroll
-            for (int r = 1; r < R; ++r) {
-                const int k = (jm * r) << (LOGN - NSB - RB);
-                v[u * R + r] = cmul(v[u * R + r], tw(k));
-            }
+            for (int r = 1; r < R; ++r) v[u * R + r] = cmul(v[u * R + r], twf(jm, r));
         }
         Dft<R>::run(&v[u * R]);
     }
+}
+
+// twf(jm, r) = W_{Ns R}^{jm r} = W_N^{(jm r) N / (Ns R)} from a TwiddleTable
+template <int LOGN, int P, typename Load>
+CUBF_DEV void pass_load(float2 (&v)[LocalShape<LOGN>::E], int th, const TwiddleTable<LOGN>& tw, Load load) {
+    using S = LocalShape<LOGN>;
+    constexpr int SHIFT = LOGN - S::ns_bits(P) - S::radix_bits(P);
+    pass_load_tw<LOGN, P>(v, th, [&](int jm, int r) { return tw((jm * r) << SHIFT); }, load);
 }
 
 template <int LOGN, int P, typename Store>
@@ -405,6 +410,177 @@ __global__ void __launch_bounds__(GlobalPassShape<LOGR, CW>::TPB)
                          static_cast<size_t>(k) * ns;
         const float2 x = a[c * G::RS + S::pad(k)];
         __stcs(dcol + o, make_float2(x.x * scale, x.y * out_sgn * scale));
+    }
+}
+
+// ---- register-direct global pass ----------------------------------------------
+//
+// The same Stockham pass as fft_global_pass_kernel, for the shapes every plan
+// uses (the first pass, Ns = 1, and passes with Ns >= C), with the tile never
+// staged whole in shared memory: the first in-CTA register phase loads its
+// column values straight from HBM and applies the outer twiddle in registers,
+// the last one writes straight to HBM, and only the exchanges between the
+// in-CTA phases use shared memory (one exchange up to radix 2^8).  A column
+// of R values is served by T = R / 16 threads of 16 values each.  Loads put
+// the C columns of a CTA on consecutive threads, so a warp reads whole
+// C-column runs of two or more rows; stores do the same for Ns >= C (runs of
+// C columns at row stride Ns), and for Ns = 1, where column j's R outputs are
+// contiguous at y[j R], the last phase puts the column's T threads on
+// consecutive lanes (T >= 16: 128-byte runs).  Per point that is one global
+// load, one global store and one shared-memory round trip per exchange,
+// against the staged kernel's three shared-memory round trips and its
+// per-element scatter index arithmetic.
+template <int LOGR, int CW = 0>
+struct GlobalRegShape {
+    using S = LocalShape<LOGR>;
+    static constexpr int R = 1 << LOGR;
+    static constexpr int T = S::T;  // threads per column
+    // columns per CTA: CW when given, else runs of >= 128 bytes
+    static constexpr int C = CW ? CW : (T >= 8 ? 16 : 128 / T);
+    static constexpr int LOG_C = log2_const(C);
+    static constexpr int TPB = C * T;
+    static constexpr int RS = S::PADDED + 1;  // padded column stride (float2)
+    static constexpr bool EXCHANGE = S::NPASS > 1;
+    static constexpr int TILE_BYTES = EXCHANGE ? C * RS * 8 : 0;
+    // W_R^m for m < R (phases with columns on consecutive threads: one
+    // twiddle per half-warp, a broadcast), and for the first pass's last
+    // phase the same values as [r][jm] rows (consecutive jm on consecutive
+    // lanes: conflict-free)
+    static constexpr int TW_BYTES = EXCHANGE ? 2 * R * 8 : 0;
+    static constexpr int SMEM_BYTES = TILE_BYTES + TW_BYTES;
+    static constexpr int MINB = 1024 / TPB;  // 64 registers per thread
+    static_assert(LOGR >= 4 && TPB <= 1024 && TPB >= 128, "register-direct pass radix must be 16..1024");
+};
+
+// In-place in-CTA phases 1 .. NPASS-2 of the register-direct pass; `full`
+// holds W_R^m, m < R.
+template <int LOGR, int P>
+struct GlobalRegMiddle {
+    static CUBF_DEV void run(float2 (&v)[LocalShape<LOGR>::E], int th, const float2* full, float2* col) {
+        using S = LocalShape<LOGR>;
+        if constexpr (P < S::NPASS - 1) {
+            constexpr int SHIFT = LOGR - S::ns_bits(P) - S::radix_bits(P);
+            pass_load_tw<LOGR, P>(v, th, [&](int jm, int r) { return full[(jm * r) << SHIFT]; },
+                                  [&](int i) { return col[S::pad(i)]; });
+            __syncthreads();
+            pass_store<LOGR, P>(v, th, [&](int i, float2 x) { col[S::pad(i)] = x; });
+            __syncthreads();
+            GlobalRegMiddle<LOGR, P + 1>::run(v, th, full, col);
+        }
+    }
+};
+
+// FIRST: Ns = 1 (and no interleaving; T >= 16), the tile's output is C R
+// contiguous values; otherwise Ns >= C.  Offsets within one transform (or one
+// interleaved array) are 32-bit: 2^log_n <= 2^31.
+template <int LOGR, bool FIRST, int CW = 0>
+__global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<LOGR, CW>::MINB)
+    fft_global_reg_kernel(const float2* src, float2* dst, int log_n, int ns_bits, const float2* __restrict__ tw1024,
+                          OuterTwiddles outer, int conj_in, int conj_out, float scale, int log_v,
+                          unsigned prefetch_stride, int outer_shift) {
+    using G = GlobalRegShape<LOGR, CW>;
+    using S = typename G::S;
+    constexpr int RB0 = S::radix_bits(0);
+    constexpr int RA = 1 << RB0;        // radix of the first register phase
+    constexpr int SUB0 = S::E / RA;     // its sub-DFTs per thread
+    constexpr int ROWSTEP = G::R / RA;  // row distance within a first-phase sub-DFT
+    constexpr int PL = S::NPASS - 1;    // last register phase
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* a = reinterpret_cast<float2*>(smem_raw);
+    float2* full = a + G::TILE_BYTES / 8;
+    float2* rows = full + G::R;
+    if constexpr (G::EXCHANGE) {
+        // W_R^m = W_1024^(m 2^(10 - LOGR)); rows[r NsL + jm] = W_R^(jm r) for the last phase
+        constexpr int NSL = 1 << S::ns_bits(PL);
+        for (int m = threadIdx.x; m < G::R; m += G::TPB) {
+            full[m] = __ldg(tw1024 + (m << (10 - LOGR)));
+            const int r = m / NSL, jm = m % NSL;
+            rows[m] = __ldg(tw1024 + (((jm * r) & (G::R - 1)) << (10 - LOGR)));
+        }
+    }
+    const uint32_t cols = 1u << (log_n - LOGR);
+    const uint32_t ctas_per_batch = cols >> G::LOG_C;
+    const size_t bidx = blockIdx.x / ctas_per_batch;
+    const uint32_t j0 = (blockIdx.x % ctas_per_batch) << G::LOG_C;
+    const uint32_t ns = 1u << ns_bits;
+    float2 v[S::E];
+    // phase 0: straight from HBM, columns on consecutive threads
+    const int c0 = threadIdx.x & (G::C - 1);
+    const int th0 = threadIdx.x >> G::LOG_C;
+    {
+        const float2* col = src + (bidx << log_n) + j0 + c0;
+        const uint32_t rstep = ROWSTEP * cols;
+#pragma unroll
+        for (int u = 0; u < SUB0; ++u) {
+            const uint32_t off = static_cast<uint32_t>(th0 + S::T * u) * cols;
+#pragma unroll
+            for (int r = 0; r < RA; ++r) v[u * RA + r] = __ldcs(col + (off + r * rstep));
+        }
+    }
+    if (prefetch_stride != 0 && blockIdx.x + static_cast<size_t>(prefetch_stride) < gridDim.x) {
+        const size_t nb = blockIdx.x + static_cast<size_t>(prefetch_stride);
+        const float2* nsrc = src + ((nb / ctas_per_batch) << log_n) + ((nb % ctas_per_batch) << G::LOG_C);
+        for (int r = threadIdx.x; r < G::R; r += G::TPB) prefetch_l2(nsrc + static_cast<uint32_t>(r) * cols, G::C * 8);
+    }
+    if (conj_in) {
+#pragma unroll
+        for (int i = 0; i < S::E; ++i) v[i].y = -v[i].y;
+    }
+    if (!FIRST && ns_bits > log_v) {
+        // outer twiddle W_{Ns R}^{jm i} of row i = j + r ROWSTEP: a fp64 start
+        // and step per sub-DFT, a fp64 recurrence, each factor rounded once
+        const size_t jm = ((j0 + c0) & (ns - 1)) >> log_v;
+        const int tshift = log_n - ns_bits - LOGR + outer_shift;
+        const size_t tmask = (size_t{1} << (log_n - log_v + outer_shift)) - 1;
+        const double2 step = outer_twiddle_d(outer, ((jm * ROWSTEP) << tshift) & tmask);
+#pragma unroll
+        for (int u = 0; u < SUB0; ++u) {
+            const int j = th0 + S::T * u;
+            double2 w = outer_twiddle_d(outer, ((jm * static_cast<size_t>(j)) << tshift) & tmask);
+#pragma unroll
+            for (int r = 0; r < RA; ++r) {
+                v[u * RA + r] = cmul(v[u * RA + r], make_float2(static_cast<float>(w.x), static_cast<float>(w.y)));
+                if (r + 1 < RA) w = cmul_d(w, step);
+            }
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < SUB0; ++u) Dft<RA>::run(&v[u * RA]);
+    // the output's column base: y[(J / Ns) Ns R + (J mod Ns) + k Ns] with
+    // J = j0 + c, j0 a multiple of C; Ns = 1 reduces it to y[J R + k]
+    float2* dbase = dst + (bidx << log_n) + (((j0 >> ns_bits) << (ns_bits + LOGR)) + (j0 & (ns - 1)));
+    const float out_sgn = conj_out ? -1.f : 1.f;
+    const bool plain = scale == 1.f && !conj_out;
+    auto emit = [&](float2* p, float2 x) {
+        __stcs(p, plain ? x : make_float2(x.x * scale, x.y * out_sgn * scale));
+    };
+    if constexpr (!G::EXCHANGE) {
+        // one register phase (radix 16, Ns >= C): output k of column c0 at k Ns
+        static_assert(!FIRST, "the first pass needs the exchange to reach contiguous runs");
+        float2* d = dbase + c0;
+        pass_store<LOGR, 0>(v, th0, [&](int k, float2 x) { emit(d + static_cast<uint32_t>(k) * ns, x); });
+    } else {
+        pass_store<LOGR, 0>(v, th0, [&](int i, float2 x) { a[c0 * G::RS + S::pad(i)] = x; });
+        __syncthreads();
+        GlobalRegMiddle<LOGR, 1>::run(v, th0, full, a + c0 * G::RS);
+        constexpr int SHIFT = LOGR - S::ns_bits(PL) - S::radix_bits(PL);
+        constexpr int NSL = 1 << S::ns_bits(PL);
+        if constexpr (FIRST) {
+            // a column's threads on consecutive lanes: y[J R + k] in runs of T
+            const int c1 = static_cast<int>(threadIdx.x) / S::T;
+            const int th1 = static_cast<int>(threadIdx.x) % S::T;
+            const float2* col = a + c1 * G::RS;
+            pass_load_tw<LOGR, PL>(v, th1, [&](int jm, int r) { return rows[r * NSL + jm]; },
+                                   [&](int i) { return col[S::pad(i)]; });
+            float2* d = dbase + c1 * G::R;
+            pass_store<LOGR, PL>(v, th1, [&](int k, float2 x) { emit(d + k, x); });
+        } else {
+            const float2* col = a + c0 * G::RS;
+            pass_load_tw<LOGR, PL>(v, th0, [&](int jm, int r) { return full[(jm * r) << SHIFT]; },
+                                   [&](int i) { return col[S::pad(i)]; });
+            float2* d = dbase + c0;
+            pass_store<LOGR, PL>(v, th0, [&](int k, float2 x) { emit(d + static_cast<uint32_t>(k) * ns, x); });
+        }
     }
 }
 

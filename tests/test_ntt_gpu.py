@@ -83,11 +83,14 @@ def test_wide_moduli_strict_path(oracle, cuda, inverse, bits):
     assert np.array_equal(got.reshape(x.shape), want)
 
 
-def test_lazy_path_selected_for_60_bit_moduli(cuda):
+def test_lazy_path_offered_for_60_bit_moduli(cuda):
+    """With every modulus below 2^62 the lazy (Harvey) arithmetic is among the
+    timed candidates, and Prepare keeps whichever candidate was fastest."""
     cfg = w.rns_config(count=2, log_n=12)
     x = w.ntt_input([d["modulus"] for d in cfg["domains"]], 12)
     _, info = run_rns(cfg, x.reshape(-1), x.size)
-    assert info["mapping"]["arithmetic"] == "shoup-lazy"
+    assert "shoup-lazy" in {c["mapping"]["arithmetic"] for c in info["candidates"]}
+    assert info["mapping"] == min(info["candidates"], key=lambda c: c["kernel_ms"])["mapping"]
 
 
 def reference_fixture_config(inverse):

@@ -653,6 +653,58 @@ void launch_fft_blocked(const cubutterflyPlan& p, const cubf::Mapping& m, const 
     }
 }
 
+// L2-chained FFT (mapping family "fft-l2-chain", planner.hpp): passes 0+1
+// and then 2+3 of the Stockham plan, each pair chunk by chunk.  A chunk of a
+// pair is a set of "keys" -- the column bits the two passes share -- chosen
+// so that the second pass of the chunk reads exactly what the first one wrote:
+// pair one (Ns = 1) keys on the columns' high n - b0 - b1 bits, pair two on
+// the low b0 + b1 bits.  The first pass writes the workspace with an L2
+// evict-last policy, the second reads it back from L2 and discards its lines,
+// so each pair reads and writes HBM once.  Tiles of 32 columns; a chunk holds
+// 2^22 values.
+void launch_fft_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
+                      float scale, cudaStream_t stream) {
+    const auto& d = p.desc;
+    const bool inverse = d.direction == CUBUTTERFLY_DIRECTION_INVERSE;
+    const int ln = p.req.log_n;
+    const std::size_t n = std::size_t{1} << ln;
+    const int b0 = m.passes[0].log_h, b1 = m.passes[1].log_h, b2 = m.passes[2].log_h, b3 = m.passes[3].log_h;
+    const int tl = cubf::kFftChainColumnsLog;
+    const cubf::FftOuterTables outer{p.outer_lo, p.outer_hi, p.outer_split};
+    auto pass = [&](int i, const void* src, void* dst, const cubf::FftChunk& c) {
+        const bool last = i == 3;
+        check_cuda(cubf::launch_fft_chain_pass(m.passes[i].log_h, src, dst, ln, m.passes[i].log_inner, p.twiddles,
+                                               outer, inverse && i == 0, inverse && last, last ? scale : 1.0f, c,
+                                               stream),
+                   "FFT chained pass launch");
+    };
+    for (std::size_t b = 0; b < d.batch; ++b) {
+        const float2* src = static_cast<const float2*>(in) + b * n;
+        float2* dst = static_cast<float2*>(out) + b * n;
+        float2* ws = static_cast<float2*>(core_ws);
+        // pair one: key h < 2^(n - b0 - b1); pass 0 columns r 2^(n-b0-b1) + h (r < 2^b1),
+        // pass 1 columns h 2^b0 + k (k < 2^b0)
+        {
+            const int kb = ln - b0 - b1;
+            const int fl = std::min(kb, cubf::kFftChainChunkLog - b0 - b1);
+            for (std::uint32_t h0 = 0; h0 < (1u << kb); h0 += 1u << fl) {
+                pass(0, src, ws, {h0, 1u << (fl - tl), 1u << kb, 1u << b1, false, true});
+                pass(1, ws, dst, {h0 << b0, 1u << (fl + b0 - tl), 0, 1, true, false});
+            }
+        }
+        // pair two: key l < 2^(b0 + b1); pass 2 columns r 2^s + l (r < 2^b3),
+        // pass 3 columns k 2^s + l (k < 2^b2), s = b0 + b1
+        {
+            const int s = b0 + b1;
+            const int fl = std::min(s, cubf::kFftChainChunkLog - b2 - b3);
+            for (std::uint32_t l0 = 0; l0 < (1u << s); l0 += 1u << fl) {
+                pass(2, dst, ws, {l0, 1u << (fl - tl), 1u << s, 1u << b3, false, true});
+                pass(3, ws, dst, {l0, 1u << (fl - tl), 1u << s, 1u << b2, true, false});
+            }
+        }
+    }
+}
+
 void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
                  cudaStream_t stream) {
     const auto& d = p.desc;
@@ -696,6 +748,10 @@ void launch_core(const cubutterflyPlan& p, const cubf::Mapping& m, const void* i
         }
         if (m.family == "fft-l2-blocked") {
             launch_fft_blocked(p, m, in, out, core_ws, scale, stream);
+            return;
+        }
+        if (m.family == "fft-l2-chain") {
+            launch_fft_chain(p, m, in, out, core_ws, scale, stream);
             return;
         }
         // Global passes ping-pong between the output and the workspace so the

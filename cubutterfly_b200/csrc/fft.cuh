@@ -470,14 +470,33 @@ struct GlobalRegMiddle {
     }
 };
 
+// With CHUNKED, a launch covers a chunk of a pass's column tiles (the
+// L2-chained pass pairs of the "fft-l2-chain" plans): tile b of the launch starts at column
+// base + (b mod tiles_per_run) C + (b / tiles_per_run) run_stride of the
+// pass's single transform.  `src_l2`: the source is an intermediate the
+// previous launch left in L2; each 128-byte line is discarded from L2 once
+// its warp holds the values (never written back to HBM).  `dst_l2`: the
+// destination is such an intermediate (stored with an L2 evict-last policy).
+struct RegChunk {
+    uint32_t base;
+    uint32_t tiles_per_run;  // 0: every tile of every transform, in order
+    uint32_t run_stride;
+    int src_l2;
+    int dst_l2;
+};
+
+CUBF_DEV void discard_l2_line(const void* p) {
+    asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
 // FIRST: Ns = 1 (and no interleaving; T >= 16), the tile's output is C R
 // contiguous values; otherwise Ns >= C.  Offsets within one transform (or one
 // interleaved array) are 32-bit: 2^log_n <= 2^31.
-template <int LOGR, bool FIRST, int CW = 0>
+template <int LOGR, bool FIRST, int CW = 0, bool CHUNKED = false>
 __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<LOGR, CW>::MINB)
     fft_global_reg_kernel(const float2* src, float2* dst, int log_n, int ns_bits, const float2* __restrict__ tw1024,
                           OuterTwiddles outer, int conj_in, int conj_out, float scale, int log_v,
-                          unsigned prefetch_stride, int outer_shift) {
+                          unsigned prefetch_stride, int outer_shift, RegChunk chunk) {
     using G = GlobalRegShape<LOGR, CW>;
     using S = typename G::S;
     constexpr int RB0 = S::radix_bits(0);
@@ -500,8 +519,20 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
     }
     const uint32_t cols = 1u << (log_n - LOGR);
     const uint32_t ctas_per_batch = cols >> G::LOG_C;
-    const size_t bidx = blockIdx.x / ctas_per_batch;
-    const uint32_t j0 = (blockIdx.x % ctas_per_batch) << G::LOG_C;
+    // (transform, first column) of tile b of this launch
+    auto tile_origin = [&](size_t b, size_t& t, uint32_t& j) {
+        if (CHUNKED) {
+            t = 0;
+            j = chunk.base + ((static_cast<uint32_t>(b) % chunk.tiles_per_run) << G::LOG_C) +
+                (static_cast<uint32_t>(b) / chunk.tiles_per_run) * chunk.run_stride;
+        } else {
+            t = b / ctas_per_batch;
+            j = static_cast<uint32_t>(b % ctas_per_batch) << G::LOG_C;
+        }
+    };
+    size_t bidx;
+    uint32_t j0;
+    tile_origin(blockIdx.x, bidx, j0);
     const uint32_t ns = 1u << ns_bits;
     float2 v[S::E];
     // phase 0: straight from HBM, columns on consecutive threads
@@ -518,8 +549,10 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
         }
     }
     if (prefetch_stride != 0 && blockIdx.x + static_cast<size_t>(prefetch_stride) < gridDim.x) {
-        const size_t nb = blockIdx.x + static_cast<size_t>(prefetch_stride);
-        const float2* nsrc = src + ((nb / ctas_per_batch) << log_n) + ((nb % ctas_per_batch) << G::LOG_C);
+        size_t nt;
+        uint32_t nj;
+        tile_origin(blockIdx.x + static_cast<size_t>(prefetch_stride), nt, nj);
+        const float2* nsrc = src + (nt << log_n) + nj;
         for (int r = threadIdx.x; r < G::R; r += G::TPB) prefetch_l2(nsrc + static_cast<uint32_t>(r) * cols, G::C * 8);
     }
     if (conj_in) {
@@ -546,13 +579,35 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
     }
 #pragma unroll
     for (int u = 0; u < SUB0; ++u) Dft<RA>::run(&v[u * RA]);
+    if (CHUNKED && chunk.src_l2) {
+        // every value of this warp's lines is in registers: drop the lines
+        // (a warp loads whole 128-byte lines of 16 columns)
+        __syncwarp();
+        if ((c0 & 15) == 0) {
+            const float2* col = src + (bidx << log_n) + j0 + c0;
+            const uint32_t rstep = ROWSTEP * cols;
+#pragma unroll
+            for (int u = 0; u < SUB0; ++u) {
+                const uint32_t off = static_cast<uint32_t>(th0 + S::T * u) * cols;
+#pragma unroll
+                for (int r = 0; r < RA; ++r) discard_l2_line(col + (off + r * rstep));
+            }
+        }
+    }
     // the output's column base: y[(J / Ns) Ns R + (J mod Ns) + k Ns] with
     // J = j0 + c, j0 a multiple of C; Ns = 1 reduces it to y[J R + k]
     float2* dbase = dst + (bidx << log_n) + (((j0 >> ns_bits) << (ns_bits + LOGR)) + (j0 & (ns - 1)));
     const float out_sgn = conj_out ? -1.f : 1.f;
     const bool plain = scale == 1.f && !conj_out;
+    const uint64_t keep = CHUNKED && chunk.dst_l2 ? l2_policy(true) : 0;
     auto emit = [&](float2* p, float2 x) {
-        __stcs(p, plain ? x : make_float2(x.x * scale, x.y * out_sgn * scale));
+        const float2 y = plain ? x : make_float2(x.x * scale, x.y * out_sgn * scale);
+        if (CHUNKED && chunk.dst_l2)
+            asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(y.x), "f"(y.y),
+                         "l"(keep)
+                         : "memory");
+        else
+            __stcs(p, y);
     };
     if constexpr (!G::EXCHANGE) {
         // one register phase (radix 16, Ns >= C): output k of column c0 at k Ns

@@ -51,6 +51,26 @@ LaunchShape fft_global_pass_shape(int log_r);
 // points (one table set serves the shorter transforms of a blocked plan).
 // `narrow`: 8 columns per CTA (64-byte runs, half the shared memory) where
 // fft_global_pass_narrow_available(log_r).
+// A chunk of one Stockham pass's column tiles (the L2-chained pass pairs of
+// the "fft-l2-chain" plans): tile b covers columns base + (b mod tiles_per_run)
+// 32 + (b / tiles_per_run) run_stride of one transform, b < tiles_per_run runs.
+// src_l2: the source is an L2-resident intermediate (its lines are discarded
+// once read); dst_l2: the destination is one (kept in L2).
+struct FftChunk {
+    std::uint32_t base;
+    std::uint32_t tiles_per_run;
+    std::uint32_t run_stride;
+    std::uint32_t runs;
+    bool src_l2;
+    bool dst_l2;
+};
+constexpr int kFftChainMinLog = 6;       // pass radices of the chained plans
+constexpr int kFftChainMaxLog = 8;
+constexpr int kFftChainColumnsLog = 5;   // 32 columns per CTA
+bool fft_chain_pass_available(int log_r);
+cudaError_t launch_fft_chain_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,
+                                  const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
+                                  const FftChunk& chunk, cudaStream_t stream);
 cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
                                    std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
                                    bool conj_out, float scale, cudaStream_t stream, int log_v = 0,

@@ -111,7 +111,7 @@ struct GlobalEntry {
 };
 // Register-direct variants of the same pass (fft.cuh): the first pass of
 // radix >= 2^8, and every pass whose Ns is at least its column count.
-template <int LOGR, bool FIRST, int CW = 0>
+template <int LOGR, bool FIRST, int CW = 0, bool CHUNKED = false>
 struct RegEntry {
     using G = fft::GlobalRegShape<LOGR, CW>;
     static bool eligible(int log_n, int ns_bits, int log_v) {
@@ -122,25 +122,42 @@ struct RegEntry {
     static cudaError_t launch(const void* src, void* dst, int log_n, int ns_bits, std::size_t batch,
                               const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out,
                               float scale, cudaStream_t stream, int log_v, int outer_shift) {
+        const std::size_t blocks = batch * ((std::size_t{1} << (log_n - LOGR)) >> G::LOG_C);
+        return run(src, dst, log_n, ns_bits, blocks, tw1024, outer, conj_in, conj_out, scale, stream, log_v,
+                   outer_shift, fft::RegChunk{0, 0, 0, 0, 0});
+    }
+    // `blocks` tiles; a chunk (tiles_per_run != 0) covers part of one transform
+    static cudaError_t run(const void* src, void* dst, int log_n, int ns_bits, std::size_t blocks,
+                           const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
+                           cudaStream_t stream, int log_v, int outer_shift, const fft::RegChunk& chunk) {
         if constexpr (FIRST && G::T < 16) {
             return cudaErrorInvalidValue;  // never eligible: runs of T < 16 values
         } else {
-        auto kernel = fft::fft_global_reg_kernel<LOGR, FIRST, CW>;
+        auto kernel = fft::fft_global_reg_kernel<LOGR, FIRST, CW, CHUNKED>;
         static KernelSetup setup;
         int grid_cap = 0;
         cudaError_t e = setup_kernel(setup, kernel, G::TPB, G::SMEM_BYTES, &grid_cap);
         if (e != cudaSuccess) return e;
-        const std::size_t blocks = batch * ((std::size_t{1} << (log_n - LOGR)) >> G::LOG_C);
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
         fft::OuterTwiddles ot{static_cast<const double2*>(outer.lo), static_cast<const double2*>(outer.hi),
                               outer.split};
+        // an L2-resident source needs no prefetch
+        const unsigned prefetch =
+            !chunk.src_l2 && blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u;
         kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
             static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits,
-            static_cast<const float2*>(tw1024), ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v,
-            blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u, outer_shift);
+            static_cast<const float2*>(tw1024), ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v, prefetch,
+            outer_shift, chunk);
         return cudaGetLastError();
         }
+    }
+    static cudaError_t chunk_run(const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,
+                                 const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
+                                 const FftChunk& c, cudaStream_t stream) {
+        const fft::RegChunk rc{c.base, c.tiles_per_run, c.run_stride, c.src_l2 ? 1 : 0, c.dst_l2 ? 1 : 0};
+        return run(src, dst, log_n, ns_bits, static_cast<std::size_t>(c.tiles_per_run) * c.runs, tw1024, outer,
+                   conj_in, conj_out, scale, stream, 0, 0, rc);
     }
     static LaunchShape shape() {
         LaunchShape s;
@@ -181,6 +198,16 @@ struct RegWideTable {
     static constexpr GlobalLaunch later_fns[] = {RegEntry<L, false, 32>::launch...};
 };
 using RegWide = RegWideTable<6, 7, 8>;
+template <int... L>
+struct ChainTable {
+    static constexpr cudaError_t (*first_fns[])(const void*, void*, int, int, const void*, const FftOuterTables&,
+                                                bool, bool, float, const FftChunk&, cudaStream_t) = {
+        RegEntry<L, true, 32, true>::chunk_run...};
+    static constexpr cudaError_t (*later_fns[])(const void*, void*, int, int, const void*, const FftOuterTables&,
+                                                bool, bool, float, const FftChunk&, cudaStream_t) = {
+        RegEntry<L, false, 32, true>::chunk_run...};
+};
+using Chain = ChainTable<6, 7, 8>;
 constexpr int kRegWideMinLog = 26;
 
 // 8-column variants of the large radices (64-byte runs, two CTAs per SM at 2^10)
@@ -256,6 +283,20 @@ cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int lo
     return Global::launch_fns[i](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in, conj_out, scale, stream,
                                  log_v, outer_shift);
 }
+
+cudaError_t launch_fft_chain_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,
+                                  const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
+                                  const FftChunk& chunk, cudaStream_t stream) {
+    if (!fft_chain_pass_available(log_r) || log_n > 31 || chunk.tiles_per_run == 0 || chunk.runs == 0)
+        return cudaErrorInvalidValue;
+    const bool first = ns_bits == 0;
+    if (!first && ns_bits < kFftChainColumnsLog) return cudaErrorInvalidValue;
+    const int k = log_r - kFftChainMinLog;
+    return first ? Chain::first_fns[k](src, dst, log_n, ns_bits, tw1024, outer, conj_in, conj_out, scale, chunk, stream)
+                 : Chain::later_fns[k](src, dst, log_n, ns_bits, tw1024, outer, conj_in, conj_out, scale, chunk, stream);
+}
+
+bool fft_chain_pass_available(int log_r) { return log_r >= kFftChainMinLog && log_r <= kFftChainMaxLog; }
 
 bool fft_global_pass_narrow_available(int log_r) { return log_r >= 8 && log_r <= kFftPassMaxLog; }
 

@@ -368,6 +368,51 @@ Mapping fft_blocked_mapping(const PlanRequest& r, const HardwareProfile& hw, con
     return m;
 }
 
+Mapping fft_chain_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts) {
+    const Descriptor& d = r.d;
+    require(d.op == CUBUTTERFLY_OPERATOR_FFT && r.log_v == 0 && !r.fft64, "L2-chained FFT serves packed complex fp32");
+    if (d.placement == CUBUTTERFLY_PLACEMENT_IN_PLACE || r.permute_input || r.staged)
+        throw Unsupported("L2-chained FFT runs out of place on packed natural-order buffers");
+    if (parts.size() != 4) throw Unsupported("L2-chained FFT runs four passes (two chained pairs)");
+    int total = 0;
+    for (int b : parts) {
+        if (!fft_chain_pass_available(b)) throw Unsupported("L2-chained FFT passes are radix 2^6 .. 2^8");
+        total += b;
+    }
+    require(total == r.log_n, "FFT passes must cover every stage exactly once");
+    // the first pass writes whole columns as 128-byte runs of 16 threads
+    if (parts[0] != kFftChainMaxLog) throw Unsupported("L2-chained FFT: the first pass is radix 2^8");
+    // each pair's chunks: 32-column tiles of at least one run
+    const int key1 = r.log_n - parts[0] - parts[1], key2 = parts[0] + parts[1];
+    if (std::min(key1, kFftChainChunkLog - parts[0] - parts[1]) < kFftChainColumnsLog ||
+        std::min(key2, kFftChainChunkLog - parts[2] - parts[3]) < kFftChainColumnsLog)
+        throw Unsupported("L2-chained FFT: transform too short for 32-column chunks");
+    if (static_cast<double>(std::size_t{8} << kFftChainChunkLog) > 0.35 * static_cast<double>(hw.l2_bytes))
+        throw Unsupported("L2-chained FFT: a chunk does not fit L2");
+    Mapping m;
+    m.family = "fft-l2-chain";
+    const double elems = static_cast<double>(d.batch) * std::ldexp(1.0, r.log_n);
+    int ns = 0;
+    for (int bits : parts) {
+        Pass p;
+        p.kind = PassKind::FftChain;
+        p.log_h = bits;
+        p.log_inner = ns;
+        p.shape = fft_global_pass_shape(bits);
+        require(fits(p.shape, hw), "FFT pass tile does not fit the device");
+        // measured on a B200: a 2^22-value chunk pass is ~1.7 waves of CTAs,
+        // so each launch pays its ramp and tail (2^30 points: 1024 launches,
+        // 18.3 ms against 12.7 ms for the Stockham plan; 2^26: 1.05 ms
+        // against 0.68 ms), i.e. each pass at ~0.6 of HBM speed although half
+        // its traffic stays in L2
+        m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, 0.6);
+        m.passes.push_back(p);
+        ns += bits;
+    }
+    m.workspace_bytes = std::size_t{8} << r.log_n;
+    return m;
+}
+
 std::string Mapping::name() const {
     if (!label.empty()) return label;
     std::ostringstream o;
@@ -403,6 +448,7 @@ Json Mapping::to_json() const {
             case PassKind::Fft64Stage: kernel = "fft64_column"; break;
             case PassKind::FftDeinterleave: kernel = "fft_deinterleave_pass"; break;
             case PassKind::FftGlobalNarrow: kernel = "fft_global_pass_narrow"; break;
+            case PassKind::FftChain: kernel = "fft_chain_pass"; break;
             default: break;
         }
         ps.push_back({{"kernel", kernel},
@@ -509,6 +555,16 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
             } catch (const Unsupported&) {
             }
         }
+        // L2-chained plans: radix 2^8 first, the rest in three balanced passes
+        if (r.log_v == 0 && !r.fft64 && r.log_n >= 26 && r.log_n <= 31) {
+            const int rest = r.log_n - kFftChainMaxLog;
+            std::vector<int> parts{kFftChainMaxLog};
+            for (int i = 0; i < 3; ++i) parts.push_back(rest / 3 + (i < rest % 3 ? 1 : 0));
+            try {
+                out.push_back(fft_chain_mapping(r, hw, parts));
+            } catch (const Unsupported&) {
+            }
+        }
         if (out.empty()) throw Unsupported("no global FFT pass partition fits this transform");
         std::stable_sort(out.begin(), out.end(),
                          [](const Mapping& a, const Mapping& b) { return a.predicted_us < b.predicted_us; });
@@ -570,6 +626,7 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         for (const auto& p : j.at("passes")) parts.push_back(p.at("log_h").get<int>());
         if (j.value("family", "") == "fwht-tcgen05") return parse_core(r, hw, "fwht-tcgen05[6+6]");
         if (j.value("family", "") == "fft-l2-blocked") return fft_blocked_mapping(r, hw, parts);
+        if (j.value("family", "") == "fft-l2-chain") return fft_chain_mapping(r, hw, parts);
     } else {
         std::string body = text;
         const auto lb = body.find('['), rb = body.rfind(']');
@@ -587,6 +644,7 @@ Mapping parse_core(const PlanRequest& r, const HardwareProfile& hw, const std::s
         return enumerate_core(r, hw).front();
     if (r.d.op == CUBUTTERFLY_OPERATOR_FFT) {
         if (text.find("fft-l2-blocked") != std::string::npos) return fft_blocked_mapping(r, hw, parts);
+        if (text.find("fft-l2-chain") != std::string::npos) return fft_chain_mapping(r, hw, parts);
         if (r.log_n > kFftLocalMaxLog || r.log_v > 0) return fft_global_mapping(r, hw, parts);
         require(parts.size() == 1 && parts[0] == r.log_n, "FFT up to 2^13 is one local pass of log N bits");
         return enumerate_core(r, hw).front();

@@ -58,6 +58,7 @@ enum class PassKind {
     Fft64Tile,
     Fft64Stage,
     FftDeinterleave,  // L2-blocked FFT: first pass of a chunk of decimated transforms
+    FftChain,         // L2-chained FFT: a pass run chunk by chunk, its pair partner reading it from L2
     FftGlobalNarrow   // L2-blocked FFT: the combining pass (8 columns per CTA)
 };
 
@@ -136,6 +137,14 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
 // (the first one the de-interleaving pass), then log V, the radix of the
 // final combining pass.  Two HBM round trips whatever the pass count.
 Mapping fft_blocked_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts);
+// L2-chained FFT (family "fft-l2-chain"): four Stockham passes of radix
+// 2^6..2^8 run as two pairs; each pair runs chunk by chunk (32 MiB of values),
+// the second pass of a chunk reading the first one's output from L2 and
+// discarding it there, so each pair costs one HBM round trip.  Out of place,
+// packed, natural order.
+Mapping fft_chain_mapping(const PlanRequest& r, const HardwareProfile& hw, const std::vector<int>& parts);
+// Values per chunk of an L2-chained pass pair (32 MiB of complex fp32).
+constexpr int kFftChainChunkLog = 22;
 // Every legal mapping of the request, ranked best first by the static model.
 std::vector<Mapping> enumerate_mappings(const PlanRequest& r, const HardwareProfile& hw);
 // Parse an EXPLICIT mapping: the JSON of Mapping::to_json, or a pass list

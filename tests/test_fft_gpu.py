@@ -330,3 +330,45 @@ def test_fft_l2_blocked_plans(lib, oracle, cuda, log_n, mapping):
     z = x.clone()
     z, _ = planned(fft_transform(n, 1, in_place=True), z, opts)
     assert _rel_l2_dev(z, y) <= TOL
+
+
+@pytest.mark.parametrize("log_n, mapping", [(26, "fft-l2-chain[8+6+6+6]"), (27, "fft-l2-chain[8+7+6+6]"),
+                                            (28, "fft-l2-chain[8+7+7+6]")])
+def test_fft_l2_chain_plans(lib, oracle, cuda, log_n, mapping):
+    """The L2-chained plan (four Stockham passes run as two chunked pairs, the
+    second pass of each chunk reading the first one's output from L2): against
+    the Stockham plan on the same input, 8 DFT bins against the oracle's
+    long-double direct DFT, the normalised inverse round trip, a batch of two
+    transforms, and an in-place request (served by another plan); rel L2 <=
+    2e-6."""
+    import torch
+
+    n = 1 << log_n
+    x = w.torch_fft_input(n, 2, cuda, seed=log_n).reshape(2 * n, 2)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def planned(t, src, options=None):
+        with cb.Plan(lib, t, options=options, stream=stream) as p:
+            ws = torch.empty(max(p.workspace_size(), 16), dtype=torch.uint8, device=cuda)
+            if p.workspace_size():
+                p.set_workspace(ws.data_ptr(), p.workspace_size())
+            dst = src if t.in_place else torch.empty_like(src)
+            p.execute(src.data_ptr(), dst.data_ptr())
+            torch.cuda.synchronize()
+            return dst, p.algorithm_name()
+
+    opts = cb.PlanOptions(mapping=mapping)
+    y, name = planned(fft_transform(n, 2), x, opts)
+    assert name == mapping, name
+    ref, ref_name = planned(fft_transform(n, 2), x, cb.PlanOptions(mapping=mapping.split("[")[1].rstrip("]")))
+    assert ref_name.startswith("fft-stockham-global"), ref_name
+    assert _rel_l2_dev(y, ref) <= TOL, (name, ref_name)
+    bins = np.sort(w.rng(80, log_n).integers(0, n, size=8))
+    got = y[torch.as_tensor(bins + n, device=cuda)].cpu().numpy().view(np.complex64).reshape(-1)
+    assert rel_l2(got, oracle.dft_bins(x[n:].cpu().numpy().view(np.complex64).reshape(-1), bins)) <= TOL
+    back, _ = planned(fft_transform(n, 2, inverse=True, normalize=True), y, opts)
+    assert _rel_l2_dev(back, x) <= TOL
+    z = x.clone()
+    z, zname = planned(fft_transform(n, 2, in_place=True), z)
+    assert not zname.startswith("fft-l2-chain"), zname
+    assert _rel_l2_dev(z, y) <= TOL

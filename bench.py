@@ -13,7 +13,8 @@ host buffers (pinned host -> device copy of the input and device -> host copy
 of both outputs inside the timed region).  `ops` reports the other hot-path
 configurations (FFT, RNS NTT, subset zeta) on the same GPU; `strong_scaling` splits configs 2, 3 and 4 over the ranks
 (limbs 32/P, transforms 16/P, 2^20 FFTs / P, the 2^30 FFT as a four-step
-over NCCL with its per-phase times), each the max over ranks.
+with its per-phase times, exchanges by peer-store kernels over NVLink and by
+NCCL send/recv), each the max over ranks.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 """
@@ -57,6 +58,8 @@ def parse():
                         "transforms of 4096 points split over the ranks (strong scaling)")
     p.add_argument("--log-batch", type=int, default=20, help="fftbatch total batch (log2)")
     p.add_argument("--log-n", type=int, default=30, help="fft4step transform length (log2)")
+    p.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                   help="fft4step exchanges on 2+ GPUs: peer-store kernels over NVLink or NCCL send/recv")
     p.add_argument("--mapping", default="",
                    help="explicit mapping for --only fwht4096 / fft1g and --workload fft4step (1 GPU), "
                         "e.g. 'fwht-tcgen05[6+6]' for the tensor-core FWHT")
@@ -325,8 +328,8 @@ def only_op(args):
 
 def fft4step(args):
     """Config 4: one complex fp32 FFT of 2^log_n points; on one GPU the
-    multi-pass plan, on P GPUs the four-step decomposition with NCCL
-    all-to-alls.  Strong scaling; algorithmic bytes = input + output once."""
+    multi-pass plan, on P GPUs the four-step decomposition (exchanges by
+    --transport).  Strong scaling; algorithmic bytes = input + output once."""
     import torch
     import torch.distributed as dist
 
@@ -356,9 +359,10 @@ def fft4step(args):
         step = lambda: plan.execute(x.data_ptr(), y.data_ptr())  # noqa: E731
         algo = plan.algorithm_name()
     else:
-        fs = FourStepFFT(n, device=dev)
+        fs = FourStepFFT(n, device=dev, transport=args.transport)
         step = lambda: fs(x)  # noqa: E731
-        algo = f"four-step {fs.shape.n1}x{fs.shape.n2} over {world} ranks (NCCL all-to-all x3)"
+        how = {"peer": "peer-store exchange kernels over NVLink", "nccl": "NCCL grouped send/recv"}
+        algo = f"four-step {fs.shape.n1}x{fs.shape.n2} over {world} ranks ({how[args.transport]}, 3 exchanges)"
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -724,23 +728,30 @@ def strong_scaling(world, rank, dev, lib, stream):
         sp1.close()
         del xs, ys, ws
     else:
+        # both exchange transports; the line reports the faster, with the other beside it
         g = torch.Generator(device=dev).manual_seed(rank)
         xs = torch.rand((n // world, 2), generator=g, device=dev, dtype=torch.float32)
-        four = FourStepFFT(n, device=dev)
-        ms = timed(lambda: four(xs), 3, warmup=1)
-        four.record_phases = True
-        four(xs)
-        phases = four.phase_ms()
-        four.record_phases = False
-        if world > 1:
+        runs = {}
+        for transport in ("peer", "nccl"):
+            four = FourStepFFT(n, device=dev, transport=transport)
+            t_ms = timed(lambda: four(xs), 3, warmup=1)
+            four.record_phases = True
+            four(xs)
+            phases = four.phase_ms()
+            four.record_phases = False
             keys = sorted(phases)
             t = torch.tensor([phases[k] for k in keys], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             phases = dict(zip(keys, (float(v) for v in t.tolist())))
-        entry = {"algorithm": f"four-step {four.shape.n1}x{four.shape.n2} over {world} ranks (NCCL)",
+            four.close()
+            runs[transport] = (t_ms, phases)
+        best = min(runs, key=lambda k: runs[k][0])
+        ms, phases = runs[best]
+        how = {"peer": "peer-store exchange kernels over NVLink", "nccl": "NCCL grouped send/recv"}
+        entry = {"algorithm": f"four-step 32768x32768 over {world} ranks ({how[best]})",
                  "phases_ms": {k: round(v, 3) for k, v in phases.items()},
-                 "limiting_phase": max(phases, key=phases.get) if phases else None}
-        four.close()
+                 "limiting_phase": max(phases, key=phases.get) if phases else None,
+                 "other_transport": {k: round(v[0], 3) for k, v in runs.items() if k != best}}
         del xs
     torch.cuda.empty_cache()
     entry.update(ms=round(ms, 3), gbs=round(2 * n * 8 / ms / 1e6, 1))

@@ -256,6 +256,13 @@ B200PermuteBlocksC64       p p p p z z z z p
 B200TransposeC64           p p z z z p
 B200FftC2CNoAlloc          p p z z i i p
 B200NttButterflyPeak       q D
+B200PeerBufferCreate       z P p
+B200PeerBufferOpen         p P
+B200PeerBufferClose        p
+B200PeerBufferDestroy      p
+B200FourStepScatterColumns p p i i z z p
+B200FourStepScatterRows    p p i i z z i p
+B200FourStepScatterTranspose p p i i z z p
 """
 
 

@@ -175,6 +175,14 @@ const Tables& tables_for(int log_n) {
 
 }  // namespace
 
+namespace cubf {
+// W_N^k tables of the four-step twiddles (per device and log N, built once).
+fft::OuterTwiddles fourstep_twiddle_tables(int log_n) {
+    const Tables& t = tables_for(log_n);
+    return fft::OuterTwiddles{t.lo, t.hi, t.split};
+}
+}  // namespace cubf
+
 extern "C" cubutterflyStatus_t cubutterflyB200FourStepTwiddle(void* data, size_t rows, size_t cols,
                                                              size_t row_offset, size_t col_offset, size_t n,
                                                              int inverse, cudaStream_t stream) {

@@ -25,8 +25,17 @@ in CPU tests).
   before use); a rank's own block never enters the exchange -- the block
   permutes read it from, or write it to, its final place.  Inverse transforms use inverse plans and conjugate
   twiddles, normalised by 1/N1 * 1/N2 when requested.
+
+  With transport "peer" the three exchanges are kernels of this library that
+  store every value straight into its destination rank's buffer over NVLink
+  (CUDA IPC mappings of the other ranks' exchange buffers): step 1's permute,
+  step 2's twiddle with step 3's permute, and step 5's permute with the final
+  transpose each become one pass that overlaps the NVLink transfer, and a
+  one-element NCCL all-reduce after each orders the ranks.
 """
 from __future__ import annotations
+
+import ctypes as ct
 
 from dataclasses import dataclass
 from typing import Callable, Optional
@@ -151,6 +160,56 @@ class _LibraryTranspose:
         self.lib.invoke("B200TransposeC64", x.data_ptr(), out.data_ptr(), 1, rows, cols, stream)
 
 
+class _DeviceArray:
+    """A (count, 2) float32 view of device memory this library allocated,
+    for torch.as_tensor (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, count: int):
+        self.__cuda_array_interface__ = {"shape": (count, 2), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class _PeerBuffers:
+    """Exchange buffers of the "peer" transport: `count` buffers of `elems`
+    complex values per rank, each mapped into every other rank's address
+    space (CUDA IPC).  dest[b] lists buffer b of ranks 0..P-1 as this rank
+    sees them; tensors[b] is this rank's own buffer b."""
+
+    def __init__(self, lib, elems: int, count: int, group, world: int, rank: int, device: torch.device):
+        self.lib, self.own, self.opened = lib, [], []
+        handles = torch.zeros((count, 64), dtype=torch.uint8)
+        for b in range(count):
+            ptr, h = ct.c_void_p(), ct.create_string_buffer(64)
+            lib.invoke("B200PeerBufferCreate", elems * 8, ct.byref(ptr), ct.cast(h, ct.c_void_p))
+            self.own.append(ptr.value)
+            handles[b] = torch.frombuffer(bytearray(h.raw), dtype=torch.uint8)
+        gathered = torch.empty((world, count, 64), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(gathered, handles.to(device), group=group)
+        gathered = gathered.cpu()
+        self.dest = []
+        for b in range(count):
+            ptrs = []
+            for q in range(world):
+                if q == rank:
+                    ptrs.append(self.own[b])
+                    continue
+                raw = bytes(gathered[q, b].tolist())
+                mapped = ct.c_void_p()
+                lib.invoke("B200PeerBufferOpen", ct.cast(ct.create_string_buffer(raw, 64), ct.c_void_p),
+                           ct.byref(mapped))
+                self.opened.append(mapped.value)
+                ptrs.append(mapped.value)
+            self.dest.append((ct.c_void_p * world)(*ptrs))
+        self.tensors = [torch.as_tensor(_DeviceArray(p, elems), device=device) for p in self.own]
+
+    def close(self):
+        for p in self.opened:
+            self.lib.invoke("B200PeerBufferClose", p)
+        for p in self.own:
+            self.lib.invoke("B200PeerBufferDestroy", p)
+        self.opened, self.own, self.tensors = [], [], []
+
+
 class FourStepFFT:
     """Distributed single-transform complex fp32 FFT (natural order in and out).
 
@@ -158,14 +217,20 @@ class FourStepFFT:
     (N / P, 2) (interleaved complex).  `local_fft(n, batch, interleaved)`,
     `twiddle`, `transpose` and `permute` may be replaced (CPU tests inject
     reference implementations); by default they are this library's GPU
-    kernels.
+    kernels.  `transport`: "nccl" (grouped send/recv exchanges, a new output
+    tensor per call) or "peer" (peer-store exchange kernels over NVLink, 2, 4
+    or 8 GPU ranks; the output is this object's own buffer, valid until the
+    next call or close()).
     """
 
     def __init__(self, n: int, group=None, inverse: bool = False, normalize: bool = True, lib=None,
                  device: Optional[torch.device] = None,
                  local_fft: Optional[Callable[[int, int, bool], Callable]] = None,
                  twiddle: Optional[Callable] = None, transpose: Optional[Callable] = None,
-                 permute: Optional[Callable] = None):
+                 permute: Optional[Callable] = None, transport: str = "nccl"):
+        if transport not in ("nccl", "peer"):
+            raise ValueError("transport must be 'nccl' or 'peer'")
+        self.transport = transport
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -187,6 +252,13 @@ class FourStepFFT:
             self._transpose = transpose
             self._permute = permute
         self._bufs = None
+        self._peer = None
+        if transport == "peer":
+            if local_fft is not None or self.world not in (2, 4, 8):
+                raise ValueError("the peer transport runs this library's kernels on 2, 4 or 8 GPU ranks")
+            self._lib = lib
+            self._peer = _PeerBuffers(lib, s.local, 3, group, self.world, self.rank, device)
+            self._flag = torch.zeros(1, dtype=torch.float32, device=device)
         # per-phase CUDA events of the last call when phase timing is on
         self.record_phases = False
         self._marks: list[tuple[str, torch.cuda.Event]] = []
@@ -231,10 +303,44 @@ class FourStepFFT:
             self._bufs = [torch.empty(shape, dtype=torch.float32, device=device) for _ in range(3)]
         return self._bufs
 
+    def _peer_call(self, x: torch.Tensor) -> torch.Tensor:
+        s, p, r = self.shape, self.world, self.rank
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        block_buf, rows_buf, result_buf = self._peer.tensors
+        dest = [ct.cast(d, ct.c_void_p) for d in self._peer.dest]
+        spec, out = self._buffers(x.device)[:2]
+
+        def settle(phase):
+            # every rank's peer stores are done before anyone reads them
+            dist.all_reduce(self._flag, group=self.group)
+            self._mark(phase)
+
+        self._marks = []
+        self._mark("start")
+        # 1. my rows' column blocks straight into each rank's N1 x N2/P block
+        self._lib.invoke("B200FourStepScatterColumns", x.data_ptr(), dest[0], p, r, s.n1, s.n2, stream)
+        settle("exchange")
+        # 2. column FFTs (length N1) of my block
+        self._cols(block_buf.view(s.n1, s.n2 // p, 2), spec.view(s.n1, s.n2 // p, 2))
+        self._mark("fft")
+        # 3. twiddle W_N^(k1 n2) and every k1 row block straight into its rank's rows
+        self._lib.invoke("B200FourStepScatterRows", spec.data_ptr(), dest[1], p, r, s.n1, s.n2,
+                         int(self.inverse), stream)
+        settle("exchange")
+        # 4. row FFTs (length N2)
+        self._rows(rows_buf.view(s.n1 // p, s.n2, 2), out.view(s.n1 // p, s.n2, 2))
+        self._mark("fft")
+        # 5. transposed into each rank's natural-order shard
+        self._lib.invoke("B200FourStepScatterTranspose", out.data_ptr(), dest[2], p, r, s.n1, s.n2, stream)
+        settle("exchange")
+        return result_buf
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         s, p, r = self.shape, self.world, self.rank
         if x.shape != (s.local, 2) or x.dtype != torch.float32:
             raise ValueError(f"expected a float32 shard of shape ({s.local}, 2)")
+        if self._peer is not None:
+            return self._peer_call(x)
         n1p, n2p = s.n1 // p, s.n2 // p
         buf_a, buf_b, buf_c = self._buffers(x.device)
         self._marks = []
@@ -292,3 +398,8 @@ class FourStepFFT:
             if hasattr(part, "close"):
                 part.close()
         self._bufs = None
+        if self._peer is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)  # no rank still stores into the buffers
+            self._peer.close()
+            self._peer = None

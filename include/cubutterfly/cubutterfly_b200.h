@@ -52,6 +52,38 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PermuteBlocksC64(const void* i
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input, void* output, size_t batch,
                                                               size_t rows, size_t cols, cudaStream_t stream);
 
+/* Peer buffers and peer-store exchanges of the four-step FFT over P ranks
+ * (no counterpart in the reference ABI; cubutterfly_b200.distributed with
+ * transport "peer").  A rank allocates its exchange buffers with
+ * cubutterflyB200PeerBufferCreate (device memory plus its 64-byte CUDA IPC
+ * handle), sends the handles to the other ranks, which map them with
+ * cubutterflyB200PeerBufferOpen (unmap: ...Close; free: ...Destroy).  The
+ * scatter kernels then read this rank's data once and store every value
+ * straight into its destination rank's buffer (dest[q], q < ranks; dest[rank]
+ * is this rank's own buffer) over NVLink: ordinary stores, no loads from peer
+ * memory.  N = n1 x n2 split over ranks = 2, 4 or 8 (n1p = n1/ranks,
+ * n2p = n2/ranks, powers of two), this rank = `rank`:
+ *   ScatterColumns:   x[i][q n2p + j] (n1p x n2)   -> dest[q][(rank n1p + i) n2p + j]
+ *   ScatterRows:      spec[k1][j] (n1 x n2p) times W_N^(k1 (rank n2p + j)), conjugated when `inverse`,
+ *                                                  -> dest[k1 / n1p][(k1 % n1p) n2 + rank n2p + j]
+ *   ScatterTranspose: out[i][q n2p + j] (n1p x n2) -> dest[q][j n1 + rank n1p + i]
+ * Every buffer holds N / ranks values, 16-byte aligned.  A rank reads what
+ * the others stored only after all of them finished (order them with a
+ * collective). */
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferCreate(size_t bytes, void** ptr, void* ipc_handle);
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferOpen(const void* ipc_handle, void** ptr);
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferClose(void* ptr);
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferDestroy(void* ptr);
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepScatterColumns(const void* x, void* const* dest, int ranks,
+                                                                        int rank, size_t n1, size_t n2,
+                                                                        cudaStream_t stream);
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepScatterRows(const void* spec, void* const* dest, int ranks,
+                                                                     int rank, size_t n1, size_t n2, int inverse,
+                                                                     cudaStream_t stream);
+CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepScatterTranspose(const void* out, void* const* dest,
+                                                                          int ranks, int rank, size_t n1, size_t n2,
+                                                                          cudaStream_t stream);
+
 /* Device-side failure status of a plan (no counterpart in the reference ABI;
  * the reference's kernels never wait on the device).  The tensor-core FWHT
  * mapping waits on its own MMA completions with bounded waits; when one

@@ -314,6 +314,77 @@ def test_four_step_two_gpus_config4_full_size():
     assert all(err <= 2e-6 for err in results.values()), results
 
 
+def _peer_worker(rank, world, port, log_n, inverse, q):
+    """The four-step with peer-store exchanges (transport "peer") against the
+    single-GPU plan on the same seeded input, shard by shard, and against the
+    NCCL transport (same kernels for the FFT stages)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        import cubutterfly_b200 as cb
+        from cubutterfly_b200 import workloads as w
+
+        n = 1 << log_n
+        lo, cnt = shard_range(n, world, rank)
+        x = w.torch_fft_input(n, 1, dev, seed=log_n).reshape(n, 2)
+        y = torch.empty_like(x)
+        t = cb.Transform(op=cb.Operator.FFT, extents=[n], batch=1, inverse=inverse, normalize_inverse=True)
+        with cb.Plan(cb.load(), t, stream=torch.cuda.current_stream().cuda_stream) as plan:
+            ws = torch.empty(max(plan.workspace_size(), 16), dtype=torch.uint8, device=dev)
+            if plan.workspace_size():
+                plan.set_workspace(ws.data_ptr(), plan.workspace_size())
+            plan.execute(x.data_ptr(), y.data_ptr())
+            torch.cuda.synchronize()
+        del ws
+        mine = x[lo:lo + cnt].clone()
+        want = y[lo:lo + cnt].clone()
+        del x, y
+        torch.cuda.empty_cache()
+        errs = {}
+        for transport in ("peer", "nccl"):
+            fs = FourStepFFT(n, device=dev, inverse=inverse, transport=transport)
+            got = fs(mine)
+            got = fs(mine).clone()  # a second call on the same buffers
+            torch.cuda.synchronize()
+            fs.close()
+            num = den = 0.0
+            for i in range(0, cnt, 1 << 25):
+                a, b = got[i:i + (1 << 25)].double(), want[i:i + (1 << 25)].double()
+                num += float(torch.sum((a - b) ** 2))
+                den += float(torch.sum(b * b))
+            errs[transport] = (num / den) ** 0.5
+            del got
+        q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("log_n, inverse", [(24, False), (22, True), (30, False)])
+def test_four_step_two_gpus_peer_transport(log_n, inverse):
+    """The peer-store exchange kernels (NVLink stores into CUDA IPC mappings of
+    the other rank's buffers) give the single-GPU plan's result at 2e-6,
+    forward and inverse, up to config 4's 2^30 points."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, log_n, inverse, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    print(f"four-step 2^{log_n} over 2 GPUs vs single-GPU plan, rel L2 per rank and transport:", results)
+    assert all(err <= 2e-6 for errs in results.values() for err in errs.values()), results
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("rows, cols, row_offset, col_offset, inverse", [
     (64, 4096, 0, 8192, False),     # row path (>= 64 columns), 16 steps per warp

@@ -78,34 +78,47 @@ __global__ void scatter_rows_kernel(const float4* __restrict__ spec, PeerPtrs de
     const size_t i = k1 % n1p;
     const float4* s = spec + ((k1 << log_n2p) + j0) / 2;
     float4* d = reinterpret_cast<float4*>(dest.p[q]) + (i * n2 + col) / 2;
-    for (int t = 0; t < steps; ++t) {
-        const float4 v = __ldcs(s + 32 * t);
-        const float2 a = cubf::fft::cmul(make_float2(v.x, v.y),
-                                         make_float2(static_cast<float>(wa.x), static_cast<float>(sgn * wa.y)));
-        const float2 b = cubf::fft::cmul(make_float2(v.z, v.w),
-                                         make_float2(static_cast<float>(wb.x), static_cast<float>(sgn * wb.y)));
-        d[32 * t] = make_float4(a.x, a.y, b.x, b.y);
-        wa = cubf::fft::cmul_d(wa, step);
-        wb = cubf::fft::cmul_d(wb, step);
+    // four steps' loads in flight before their multiplies and peer stores
+    for (int t0 = 0; t0 < steps; t0 += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = t0 + u < steps ? __ldcs(s + 32 * (t0 + u)) : make_float4(0, 0, 0, 0);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (t0 + u >= steps) break;
+            const float2 a = cubf::fft::cmul(make_float2(v[u].x, v[u].y),
+                                             make_float2(static_cast<float>(wa.x), static_cast<float>(sgn * wa.y)));
+            const float2 b = cubf::fft::cmul(make_float2(v[u].z, v[u].w),
+                                             make_float2(static_cast<float>(wb.x), static_cast<float>(sgn * wb.y)));
+            d[32 * (t0 + u)] = make_float4(a.x, a.y, b.x, b.y);
+            wa = cubf::fft::cmul_d(wa, step);
+            wb = cubf::fft::cmul_d(wb, step);
+        }
     }
     __threadfence_system();
 }
 
-// 32 x 32 tiles of out (n1p x n2, row-major) through shared memory; tile
-// (i0, c0) lies in one destination block (n2p a multiple of 32) and is written
-// as 32 runs of 32 values along i (256-byte runs) in the destination shard.
-__global__ void scatter_transpose_kernel(const float2* __restrict__ out, PeerPtrs dest, int rank, size_t n1,
-                                         size_t n1p, size_t n2p, size_t n2) {
-    __shared__ float2 tile[32][33];
-    const size_t i0 = static_cast<size_t>(blockIdx.y) * 32, c0 = static_cast<size_t>(blockIdx.x) * 32;
+// Tiles of 128 values along i by 32 along k2 through shared memory: read as
+// 256-byte row segments of `out` (n1p x n2, row-major), written as 32 runs of
+// 128 consecutive i (1 KiB each) in the destination shard -- long runs keep
+// the writes that cross NVLink and land in the peer's HBM efficient.  A tile
+// lies in one destination block (n2p a multiple of 32).
+constexpr int kTileI = 128, kTileK = 32;
+__global__ void __launch_bounds__(256) scatter_transpose_kernel(const float2* __restrict__ out, PeerPtrs dest,
+                                                                int rank, size_t n1, size_t n1p, size_t n2p,
+                                                                size_t n2) {
+    __shared__ float2 tile[kTileI][kTileK + 1];
+    const size_t i0 = static_cast<size_t>(blockIdx.y) * kTileI, c0 = static_cast<size_t>(blockIdx.x) * kTileK;
+    const int x = threadIdx.x & 31, y = threadIdx.x >> 5;  // 32 x 8
 #pragma unroll
-    for (int k = 0; k < 32; k += 8) tile[threadIdx.y + k][threadIdx.x] = __ldcs(out + (i0 + threadIdx.y + k) * n2 + c0 + threadIdx.x);
+    for (int r = 0; r < kTileI; r += 8) tile[r + y][x] = __ldcs(out + (i0 + r + y) * n2 + c0 + x);
     __syncthreads();
     const int q = static_cast<int>(c0 / n2p);
     const size_t jb = c0 % n2p;
-    float2* d = dest.p[q] + static_cast<size_t>(rank) * n1p + i0 + threadIdx.x;
+    const int i = threadIdx.x & (kTileI - 1), half = threadIdx.x >> 7;  // two destination rows per pass
+    float2* d = dest.p[q] + static_cast<size_t>(rank) * n1p + i0 + i;
 #pragma unroll
-    for (int k = 0; k < 32; k += 8) d[(jb + threadIdx.y + k) * n1] = tile[threadIdx.x][threadIdx.y + k];
+    for (int k = 0; k < kTileK; k += 2) d[(jb + k + half) * n1] = tile[i][k + half];
     __threadfence_system();
 }
 
@@ -241,14 +254,14 @@ extern "C" cubutterflyStatus_t cubutterflyB200FourStepScatterTranspose(const voi
                                                                       cudaStream_t stream) {
     return guarded([&] {
         const PeerPtrs p = peers_of(dest, ranks, rank);
-        if (!out || !pow2(n1) || !pow2(n2) || n1 < 32 * static_cast<std::size_t>(ranks) ||
-            n2 < 32 * static_cast<std::size_t>(ranks))
-            throw std::invalid_argument("transpose scatter needs power-of-two N1, N2 >= 32 P");
+        if (!out || !pow2(n1) || !pow2(n2) || n1 < kTileI * static_cast<std::size_t>(ranks) ||
+            n2 < kTileK * static_cast<std::size_t>(ranks))
+            throw std::invalid_argument("transpose scatter needs power-of-two N1 >= 128 P and N2 >= 32 P");
         const std::size_t n1p = n1 / ranks, n2p = n2 / ranks;
-        const std::size_t tx = n2 / 32, ty = n1p / 32;
+        const std::size_t tx = n2 / kTileK, ty = n1p / kTileI;
         if (tx > 0x7fffffffULL || ty > 65535) throw std::invalid_argument("transpose scatter grid is too large");
-        scatter_transpose_kernel<<<dim3(static_cast<unsigned>(tx), static_cast<unsigned>(ty)), dim3(32, 8), 0,
-                                   stream>>>(static_cast<const float2*>(out), p, rank, n1, n1p, n2p, n2);
+        scatter_transpose_kernel<<<dim3(static_cast<unsigned>(tx), static_cast<unsigned>(ty)), 256, 0, stream>>>(
+            static_cast<const float2*>(out), p, rank, n1, n1p, n2p, n2);
         check(cudaGetLastError(), "transpose scatter launch");
     });
 }

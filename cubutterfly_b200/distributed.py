@@ -312,27 +312,28 @@ class FourStepFFT:
 
         def settle(phase):
             # every rank's peer stores are done before anyone reads them
-            dist.all_reduce(self._flag, group=self.group)
             self._mark(phase)
+            dist.all_reduce(self._flag, group=self.group)
+            self._mark("sync")
 
         self._marks = []
         self._mark("start")
         # 1. my rows' column blocks straight into each rank's N1 x N2/P block
         self._lib.invoke("B200FourStepScatterColumns", x.data_ptr(), dest[0], p, r, s.n1, s.n2, stream)
-        settle("exchange")
+        settle("exchange_columns")
         # 2. column FFTs (length N1) of my block
         self._cols(block_buf.view(s.n1, s.n2 // p, 2), spec.view(s.n1, s.n2 // p, 2))
         self._mark("fft")
         # 3. twiddle W_N^(k1 n2) and every k1 row block straight into its rank's rows
         self._lib.invoke("B200FourStepScatterRows", spec.data_ptr(), dest[1], p, r, s.n1, s.n2,
                          int(self.inverse), stream)
-        settle("exchange")
+        settle("exchange_rows")
         # 4. row FFTs (length N2)
         self._rows(rows_buf.view(s.n1 // p, s.n2, 2), out.view(s.n1 // p, s.n2, 2))
         self._mark("fft")
         # 5. transposed into each rank's natural-order shard
         self._lib.invoke("B200FourStepScatterTranspose", out.data_ptr(), dest[2], p, r, s.n1, s.n2, stream)
-        settle("exchange")
+        settle("exchange_transpose")
         return result_buf
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:

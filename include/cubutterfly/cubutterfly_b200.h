@@ -67,7 +67,8 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input
  *   ScatterRows:      spec[k1][j] (n1 x n2p) times W_N^(k1 (rank n2p + j)), conjugated when `inverse`,
  *                                                  -> dest[k1 / n1p][(k1 % n1p) n2 + rank n2p + j]
  *   ScatterTranspose: out[i][q n2p + j] (n1p x n2) -> dest[q][j n1 + rank n1p + i]
- * Every buffer holds N / ranks values, 16-byte aligned.  A rank reads what
+ * Every buffer holds N / ranks values, 16-byte aligned; ScatterTranspose needs
+ * n1 >= 128 ranks, ScatterRows n2 >= 64 ranks.  A rank reads what
  * the others stored only after all of them finished (order them with a
  * collective). */
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferCreate(size_t bytes, void** ptr, void* ipc_handle);

@@ -234,6 +234,8 @@ class FourStepFFT:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if transport == "peer" and (local_fft is not None or self.world not in (2, 4, 8)):
+            raise ValueError("the peer transport runs this library's kernels on 2, 4 or 8 GPU ranks")
         self.shape = FourStepShape(n, self.world)
         self.inverse, self.normalize = inverse, normalize
         s = self.shape
@@ -254,8 +256,6 @@ class FourStepFFT:
         self._bufs = None
         self._peer = None
         if transport == "peer":
-            if local_fft is not None or self.world not in (2, 4, 8):
-                raise ValueError("the peer transport runs this library's kernels on 2, 4 or 8 GPU ranks")
             self._lib = lib
             self._peer = _PeerBuffers(lib, s.local, 3, group, self.world, self.rank, device)
             self._flag = torch.zeros(1, dtype=torch.float32, device=device)

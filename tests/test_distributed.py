@@ -42,6 +42,16 @@ def test_four_step_shape():
         FourStepShape(1 << 4, 8)
 
 
+def test_four_step_transport_choices():
+    """The peer transport needs this library's kernels on 2, 4 or 8 GPU
+    ranks; anything else (one process, injected CPU stages) is refused before
+    any buffer is made, as is an unknown transport."""
+    with pytest.raises(ValueError, match="transport"):
+        FourStepFFT(1 << 10, transport="shm")
+    with pytest.raises(ValueError, match="2, 4 or 8"):
+        FourStepFFT(1 << 10, transport="peer", local_fft=lambda n, b, inter: None)
+
+
 def test_shard_rns_config_keeps_only_used_domains():
     """Shares are contiguous by polynomial position; each share carries only
     the domains its polynomials use, renumbered, and packs its polynomials."""

@@ -731,9 +731,13 @@ def strong_scaling(world, rank, dev, lib, stream):
         # both exchange transports; the line reports the faster, with the other beside it
         g = torch.Generator(device=dev).manual_seed(rank)
         xs = torch.rand((n // world, 2), generator=g, device=dev, dtype=torch.float32)
-        runs = {}
+        runs, failed = {}, {}
         for transport in ("peer", "nccl"):
-            four = FourStepFFT(n, device=dev, transport=transport)
+            try:
+                four = FourStepFFT(n, device=dev, transport=transport)
+            except Exception as e:  # e.g. no CUDA IPC between these devices: keep the other transport
+                failed[transport] = str(e)[:200]
+                continue
             t_ms = timed(lambda: four(xs), 3, warmup=1)
             four.record_phases = True
             four(xs)
@@ -752,6 +756,8 @@ def strong_scaling(world, rank, dev, lib, stream):
                  "phases_ms": {k: round(v, 3) for k, v in phases.items()},
                  "limiting_phase": max(phases, key=phases.get) if phases else None,
                  "other_transport": {k: round(v[0], 3) for k, v in runs.items() if k != best}}
+        if failed:
+            entry["unavailable_transport"] = failed
         del xs
     torch.cuda.empty_cache()
     entry.update(ms=round(ms, 3), gbs=round(2 * n * 8 / ms / 1e6, 1))

@@ -297,10 +297,15 @@ Mapping fft_global_mapping(const PlanRequest& r, const HardwareProfile& hw, cons
         const std::size_t cols = std::size_t{1} << (r.log_n + r.log_v - bits);
         if (cols % static_cast<std::size_t>(p.shape.units_per_cta) != 0)
             throw Unsupported("FFT pass of " + std::to_string(bits) + " bits needs more columns than this transform has");
-        // large radices run few, large CTAs whose load, exchange and store
-        // phases overlap poorly (measured: a radix-2^10 pass of 2^30 points
-        // takes 1.5x a radix-2^8 pass, radix-2^9 passes 1.3x)
-        const double eff = p.shape.threads >= 1024 ? 0.45 : (p.shape.threads >= 512 ? 0.6 : 0.85);
+        // Measured on a B200: passes the register-direct kernel takes (a first
+        // pass of radix >= 2^8, later passes with Ns >= 16 columns) run at
+        // 0.8-0.95 of the copy rate up to radix 2^8 (2^30 as 8+7+7+8: 11.2
+        // ms), radix 2^9 at ~0.74, radix 2^10 (one 1024-thread CTA per SM) at
+        // ~0.5; the staged kernel (first passes below radix 2^8, 0 < Ns < 16)
+        // at ~0.55 (2^28 as 7+7+7+7: 3.22 ms, as 8+7+7+6: 2.70 ms).
+        const int nsb = ns + r.log_v;
+        const bool direct = (nsb == 0 && bits >= 8) || nsb >= 4;
+        const double eff = !direct ? 0.55 : (bits >= 10 ? 0.5 : (bits == 9 ? 0.74 : 0.9));
         m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, eff);
         m.passes.push_back(p);
         ns += bits;
@@ -528,14 +533,38 @@ std::vector<Mapping> enumerate_core(const PlanRequest& r, const HardwareProfile&
         if (r.log_n < kFftPassMinLog)
             throw Unsupported("interleaved FFT batches need at least 2^" + std::to_string(kFftPassMinLog) + " points");
         // Multi-pass global Stockham: for each cap on the radix bits of a
-        // pass, ceil(L / cap) passes with balanced radices.
+        // pass, ceil(L / cap) passes with balanced radices; and a radix-2^8
+        // first pass (the register-direct kernel's first pass) followed by
+        // balanced passes in ascending radix.
+        std::vector<std::vector<int>> partitions;
         for (int cap = kFftPassMaxLog; cap >= 7; --cap) {
             const int np = (r.log_n + cap - 1) / cap;
             std::vector<int> parts;
             for (int i = 0; i < np; ++i) parts.push_back(r.log_n / np + (i < r.log_n % np ? 1 : 0));
+            partitions.push_back(parts);
+        }
+        if (r.log_v == 0 && r.log_n >= 8 + kFftPassMinLog) {
+            const int rest = r.log_n - 8;
+            for (int np = (rest + 7) / 8; np <= (rest + 5) / 6; ++np) {
+                std::vector<int> parts;
+                for (int i = 0; i < np; ++i) parts.push_back(rest / np + (i < rest % np ? 1 : 0));
+                std::sort(parts.begin(), parts.end());
+                parts.insert(parts.begin(), 8);
+                // ahead of the balanced partitions: on equal cost the radix-2^8
+                // first pass wins (2^30: 8+7+7+8 11.2 ms, 8+8+7+7 11.55 ms)
+                partitions.insert(partitions.begin() + (np - (rest + 7) / 8), parts);
+            }
+        }
+        for (const auto& parts : partitions) {
+            if (*std::min_element(parts.begin(), parts.end()) < kFftPassMinLog ||
+                *std::max_element(parts.begin(), parts.end()) > kFftPassMaxLog)
+                continue;
             bool dup = false;
-            for (const auto& m : out)
-                if (m.passes.size() == parts.size()) dup = true;
+            for (const auto& m : out) {
+                std::vector<int> have;
+                for (const auto& ps : m.passes) have.push_back(ps.log_h);
+                if (have == parts) dup = true;
+            }
             if (dup) continue;
             try {
                 out.push_back(fft_global_mapping(r, hw, parts));

@@ -66,8 +66,12 @@ __global__ void scatter_rows_kernel(const float4* __restrict__ spec, PeerPtrs de
     const size_t warp = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     const size_t warps_per_row = (n2p >> 6) / static_cast<size_t>(steps);
-    const size_t k1 = warp / warps_per_row;
-    if (k1 >= n1) return;
+    // rows taken round-robin over the destination ranks, so the CTAs in
+    // flight write to every rank at once (local HBM and NVLink together)
+    const size_t slot = warp / warps_per_row;
+    if (slot >= n1) return;
+    const size_t ranks = n1 / n1p;
+    const size_t k1 = (slot % ranks) * n1p + slot / ranks;
     const size_t j0 = (warp % warps_per_row) * static_cast<size_t>(steps) * 64 + 2 * static_cast<size_t>(lane);
     const size_t col = static_cast<size_t>(rank) * n2p + j0;  // n2 index of this thread's first value
     double2 wa = cubf::fft::outer_twiddle_d(tw, (k1 * col) & nmask);
@@ -108,7 +112,11 @@ __global__ void __launch_bounds__(256) scatter_transpose_kernel(const float2* __
                                                                 int rank, size_t n1, size_t n1p, size_t n2p,
                                                                 size_t n2) {
     __shared__ float2 tile[kTileI][kTileK + 1];
-    const size_t i0 = static_cast<size_t>(blockIdx.y) * kTileI, c0 = static_cast<size_t>(blockIdx.x) * kTileK;
+    // column tiles taken round-robin over the destination ranks (adjacent
+    // CTAs write to different ranks)
+    const size_t ranks = n2 / n2p, per_rank = n2p / kTileK;
+    const size_t ct = (blockIdx.x % ranks) * per_rank + blockIdx.x / ranks;
+    const size_t i0 = static_cast<size_t>(blockIdx.y) * kTileI, c0 = ct * kTileK;
     const int x = threadIdx.x & 31, y = threadIdx.x >> 5;  // 32 x 8
 #pragma unroll
     for (int r = 0; r < kTileI; r += 8) tile[r + y][x] = __ldcs(out + (i0 + r + y) * n2 + c0 + x);

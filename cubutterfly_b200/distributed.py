@@ -177,6 +177,14 @@ class _PeerBuffers:
 
     def __init__(self, lib, elems: int, count: int, group, world: int, rank: int, device: torch.device):
         self.lib, self.own, self.opened = lib, [], []
+        try:
+            self._setup(elems, count, group, world, rank, device)
+        except Exception:
+            self.close()  # nothing half-made stays allocated or mapped
+            raise
+
+    def _setup(self, elems, count, group, world, rank, device):
+        lib = self.lib
         handles = torch.zeros((count, 64), dtype=torch.uint8)
         for b in range(count):
             ptr, h = ct.c_void_p(), ct.create_string_buffer(64)
@@ -203,11 +211,12 @@ class _PeerBuffers:
         self.tensors = [torch.as_tensor(_DeviceArray(p, elems), device=device) for p in self.own]
 
     def close(self):
-        for p in self.opened:
-            self.lib.invoke("B200PeerBufferClose", p)
-        for p in self.own:
-            self.lib.invoke("B200PeerBufferDestroy", p)
+        opened, own = self.opened, self.own
         self.opened, self.own, self.tensors = [], [], []
+        for p in opened:
+            self.lib.invoke("B200PeerBufferClose", p)
+        for p in own:
+            self.lib.invoke("B200PeerBufferDestroy", p)
 
 
 class FourStepFFT:

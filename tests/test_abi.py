@@ -567,3 +567,32 @@ def test_cpp_owner_header_on_cpu(tmp_path):
     exe = compile_cpp(ROOT / "tests" / "cpp" / "plan_api_cpu.cpp", tmp_path / "plan_api_cpu")
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
+
+
+def test_peer_transport_entry_points_check_arguments_on_cpu(lib):
+    """The peer-transport extensions refuse bad requests before touching the
+    device: zero-byte buffers, missing handles, rank counts other than 2, 4
+    or 8, ranks out of range, null or unaligned destinations, shapes too small
+    for the kernels' tiles."""
+    import ctypes as ct
+
+    invalid = cb.Status.INVALID_VALUE
+    ptr, handle = ct.c_void_p(), ct.create_string_buffer(64)
+    assert lib.fn["B200PeerBufferCreate"](0, ct.byref(ptr), ct.cast(handle, ct.c_void_p)) == invalid
+    assert lib.fn["B200PeerBufferOpen"](None, ct.byref(ptr)) == invalid
+    assert lib.fn["B200PeerBufferClose"](None) == invalid
+    assert lib.fn["B200PeerBufferDestroy"](None) == invalid
+    two = (ct.c_void_p * 2)(0x10000, 0x20000)
+    dest = ct.cast(two, ct.c_void_p)
+    x = 0x40000
+    scol, srow, stra = (lib.fn[k] for k in ("B200FourStepScatterColumns", "B200FourStepScatterRows",
+                                            "B200FourStepScatterTranspose"))
+    assert scol(x, dest, 3, 0, 1 << 12, 1 << 12, None) == invalid        # 3 ranks
+    assert scol(x, dest, 2, 2, 1 << 12, 1 << 12, None) == invalid        # rank out of range
+    assert scol(x + 8, dest, 2, 0, 1 << 12, 1 << 12, None) == invalid    # unaligned source
+    assert scol(x, dest, 2, 0, 3 << 10, 1 << 12, None) == invalid        # n1 not a power of two
+    bad = (ct.c_void_p * 2)(0x10000, 0x20008)
+    assert scol(x, ct.cast(bad, ct.c_void_p), 2, 0, 1 << 12, 1 << 12, None) == invalid  # unaligned peer
+    assert srow(x, dest, 2, 0, 1 << 12, 64, 0, None) == invalid          # n2 < 64 ranks
+    assert stra(x, dest, 2, 0, 128, 1 << 12, None) == invalid            # n1 < 128 ranks
+    assert b"128" in lib.fn["GetLastErrorString"]()

@@ -260,9 +260,9 @@ B200PeerBufferCreate       z P p
 B200PeerBufferOpen         p P
 B200PeerBufferClose        p
 B200PeerBufferDestroy      p
-B200FourStepScatterColumns p p i i z z p
-B200FourStepScatterRows    p p i i z z i p
-B200FourStepScatterTranspose p p i i z z p
+B200FourStepScatterColumns p p i i z z z z i p
+B200FourStepScatterRows    p p i i z z z z i i p
+B200FourStepScatterTranspose p p i i z z z z i p
 """
 
 

@@ -219,6 +219,15 @@ class _PeerBuffers:
             self.lib.invoke("B200PeerBufferDestroy", p)
 
 
+def _event(stream, record_after=None):
+    """A timing event recorded on `stream` (after `record_after`'s work so far)."""
+    if record_after is not None:
+        stream.wait_stream(record_after)
+    e = torch.cuda.Event(enable_timing=True)
+    e.record(stream)
+    return e
+
+
 class FourStepFFT:
     """Distributed single-transform complex fp32 FFT (natural order in and out).
 
@@ -236,7 +245,7 @@ class FourStepFFT:
                  device: Optional[torch.device] = None,
                  local_fft: Optional[Callable[[int, int, bool], Callable]] = None,
                  twiddle: Optional[Callable] = None, transpose: Optional[Callable] = None,
-                 permute: Optional[Callable] = None, transport: str = "nccl"):
+                 permute: Optional[Callable] = None, transport: str = "nccl", pipeline: bool = True):
         if transport not in ("nccl", "peer"):
             raise ValueError("transport must be 'nccl' or 'peer'")
         self.transport = transport
@@ -268,6 +277,23 @@ class FourStepFFT:
             self._lib = lib
             self._peer = _PeerBuffers(lib, s.local, 3, group, self.world, self.rank, device)
             self._flag = torch.zeros(1, dtype=torch.float32, device=device)
+            self._pipeline = None
+            n1p, n2p = s.n1 // self.world, s.n2 // self.world
+            if pipeline and n2p >= 128 and n1p >= 256:
+                # every stage in two halves: the exchanges (and the
+                # collectives ordering them) on a high-priority stream, the
+                # FFT stages on another, so half of an exchange runs beside
+                # the other half's FFT stage (the overlapped exchange kernels
+                # are bounded to a few CTAs per SM to leave the FFT room)
+                xs = torch.cuda.Stream(device, priority=-2)
+                fs_ = torch.cuda.Stream(device)
+                with torch.cuda.stream(fs_):
+                    cols = _LibraryFft(lib, s.n1, n2p // 2, inverse, normalize, device, interleaved=True)
+                    rows = _LibraryFft(lib, s.n2, n1p // 2, inverse, normalize, device)
+                self._pipeline = ((xs, fs_), [cols], [rows], (self._flag, None))
+                # measured at 2^30 on two GPUs: 1 CTA/SM 15.7 ms, 2: 13.6, 3: 13.2, 4: 13.3, 8: 13.9
+                # (serial schedule: 14.8 ms)
+                self.overlap_ctas_per_sm = 3
         # per-phase CUDA events of the last call when phase timing is on
         self.record_phases = False
         self._marks: list[tuple[str, torch.cuda.Event]] = []
@@ -328,21 +354,89 @@ class FourStepFFT:
         self._marks = []
         self._mark("start")
         # 1. my rows' column blocks straight into each rank's N1 x N2/P block
-        self._lib.invoke("B200FourStepScatterColumns", x.data_ptr(), dest[0], p, r, s.n1, s.n2, stream)
+        self._lib.invoke("B200FourStepScatterColumns", x.data_ptr(), dest[0], p, r, s.n1, s.n2, 0, s.n2 // p, 0,
+                         stream)
         settle("exchange_columns")
         # 2. column FFTs (length N1) of my block
         self._cols(block_buf.view(s.n1, s.n2 // p, 2), spec.view(s.n1, s.n2 // p, 2))
         self._mark("fft")
         # 3. twiddle W_N^(k1 n2) and every k1 row block straight into its rank's rows
-        self._lib.invoke("B200FourStepScatterRows", spec.data_ptr(), dest[1], p, r, s.n1, s.n2,
-                         int(self.inverse), stream)
+        self._lib.invoke("B200FourStepScatterRows", spec.data_ptr(), dest[1], p, r, s.n1, s.n2, 0, s.n2 // p,
+                         int(self.inverse), 0, stream)
         settle("exchange_rows")
         # 4. row FFTs (length N2)
         self._rows(rows_buf.view(s.n1 // p, s.n2, 2), out.view(s.n1 // p, s.n2, 2))
         self._mark("fft")
         # 5. transposed into each rank's natural-order shard
-        self._lib.invoke("B200FourStepScatterTranspose", out.data_ptr(), dest[2], p, r, s.n1, s.n2, stream)
+        self._lib.invoke("B200FourStepScatterTranspose", out.data_ptr(), dest[2], p, r, s.n1, s.n2, 0, s.n1 // p,
+                         0, stream)
         settle("exchange_transpose")
+        return result_buf
+
+    def _peer_pipelined_call(self, x: torch.Tensor) -> torch.Tensor:
+        """The peer transport with every stage in two halves: exchanges on
+        the high-priority stream sx, FFT stages on sf.  Exchange 1's second
+        column half runs beside the first half's column FFT, exchange 2's
+        first half beside the second half's column FFT, and exchange 3's
+        first row half beside the second half's row FFT.  The collectives all
+        run on sx, in the same order on every rank."""
+        s, p, r = self.shape, self.world, self.rank
+        (sx, sf), (cols,), (rows,), (flag, _) = self._pipeline
+        caller = torch.cuda.current_stream(x.device)
+        block_buf, rows_buf, result_buf = self._peer.tensors
+        dest = [ct.cast(d, ct.c_void_p) for d in self._peer.dest]
+        spec, out = self._buffers(x.device)[:2]
+        n1p, n2p = s.n1 // p, s.n2 // p
+        w, m = n2p // 2, n1p // 2
+        inv, lib, k = int(self.inverse), self._lib, self.overlap_ctas_per_sm
+        xsp = sx.cuda_stream
+
+        def rec(stream):
+            e = torch.cuda.Event()
+            e.record(stream)
+            return e
+
+        def settle():
+            with torch.cuda.stream(sx):
+                dist.all_reduce(flag, group=self.group)
+
+        self._marks = []
+        if self.record_phases:
+            self._marks.append(("start", _event(sx, record_after=caller)))
+        sx.wait_stream(caller)
+        blk, sp = block_buf.view(2, s.n1, w, 2), spec.view(2, s.n1, w, 2)
+        rv, ov = rows_buf.view(n1p, s.n2, 2), out.view(n1p, s.n2, 2)
+        # exchange 1, half 0, alone; half 1 beside column FFT half 0
+        lib.invoke("B200FourStepScatterColumns", x.data_ptr(), dest[0], p, r, s.n1, s.n2, 0, w, 0, xsp)
+        settle()
+        sf.wait_event(rec(sx))
+        cols(blk[0], sp[0])
+        e_cf0 = rec(sf)
+        lib.invoke("B200FourStepScatterColumns", x.data_ptr(), dest[0], p, r, s.n1, s.n2, w, w, k, xsp)
+        settle()
+        e_b = rec(sx)
+        # exchange 2, half 0 beside column FFT half 1; half 1 alone
+        sx.wait_event(e_cf0)
+        lib.invoke("B200FourStepScatterRows", sp[0].data_ptr(), dest[1], p, r, s.n1, s.n2, 0, w, inv, k, xsp)
+        sf.wait_event(e_b)
+        cols(blk[1], sp[1])
+        sx.wait_event(rec(sf))
+        lib.invoke("B200FourStepScatterRows", sp[1].data_ptr(), dest[1], p, r, s.n1, s.n2, w, w, inv, 0, xsp)
+        settle()
+        # row FFT halves; exchange 3 half 0 beside row FFT half 1; half 1 alone
+        sf.wait_event(rec(sx))
+        rows(rv[:m], ov[:m])
+        e_rf0 = rec(sf)
+        rows(rv[m:], ov[m:])
+        e_rf1 = rec(sf)
+        sx.wait_event(e_rf0)
+        lib.invoke("B200FourStepScatterTranspose", out.data_ptr(), dest[2], p, r, s.n1, s.n2, 0, m, k, xsp)
+        sx.wait_event(e_rf1)
+        lib.invoke("B200FourStepScatterTranspose", out.data_ptr(), dest[2], p, r, s.n1, s.n2, m, m, 0, xsp)
+        settle()
+        caller.wait_stream(sx)
+        if self.record_phases:
+            self._marks.append(("pipeline", _event(caller)))
         return result_buf
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
@@ -350,6 +444,8 @@ class FourStepFFT:
         if x.shape != (s.local, 2) or x.dtype != torch.float32:
             raise ValueError(f"expected a float32 shard of shape ({s.local}, 2)")
         if self._peer is not None:
+            if self._pipeline is not None:
+                return self._peer_pipelined_call(x)
             return self._peer_call(x)
         n1p, n2p = s.n1 // p, s.n2 // p
         buf_a, buf_b, buf_c = self._buffers(x.device)
@@ -404,7 +500,11 @@ class FourStepFFT:
         return result
 
     def close(self):
-        for part in (self._cols, self._rows):
+        parts = [self._cols, self._rows]
+        if getattr(self, "_pipeline", None) is not None:
+            parts += self._pipeline[1] + self._pipeline[2]
+            self._pipeline = None
+        for part in parts:
             if hasattr(part, "close"):
                 part.close()
         self._bufs = None

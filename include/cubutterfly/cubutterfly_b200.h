@@ -62,11 +62,16 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200TransposeC64(const void* input
  * straight into its destination rank's buffer (dest[q], q < ranks; dest[rank]
  * is this rank's own buffer) over NVLink: ordinary stores, no loads from peer
  * memory.  N = n1 x n2 split over ranks = 2, 4 or 8 (n1p = n1/ranks,
- * n2p = n2/ranks, powers of two), this rank = `rank`:
- *   ScatterColumns:   x[i][q n2p + j] (n1p x n2)   -> dest[q][(rank n1p + i) n2p + j]
- *   ScatterRows:      spec[k1][j] (n1 x n2p) times W_N^(k1 (rank n2p + j)), conjugated when `inverse`,
- *                                                  -> dest[k1 / n1p][(k1 % n1p) n2 + rank n2p + j]
+ * n2p = n2/ranks, powers of two), this rank = `rank`; each call covers a part:
+ * columns j in [c0, c0 + width) of N2/P (ScatterColumns, ScatterRows) or rows
+ * i in [row0, row0 + rows) of n1p (ScatterTranspose); the whole exchange is
+ * c0 = 0, width = n2p, or row0 = 0, rows = n1p:
+ *   ScatterColumns:   x[i][q n2p + j] (n1p x n2)   -> dest[q][c0 n1 + (rank n1p + i) width + j - c0]
+ *   ScatterRows:      spec[k1][j - c0] (n1 x width) times W_N^(k1 (rank n2p + j)), conjugated when
+ *                     `inverse`                    -> dest[k1 / n1p][(k1 % n1p) n2 + rank n2p + j]
  *   ScatterTranspose: out[i][q n2p + j] (n1p x n2) -> dest[q][j n1 + rank n1p + i]
+ * `ctas_per_sm` bounds the launch to that many CTAs per SM (0: 8, the whole
+ * GPU), so a pipelined schedule can run an FFT stage beside it.
  * Every buffer holds N / ranks values, 16-byte aligned; ScatterTranspose needs
  * n1 >= 128 ranks, ScatterRows n2 >= 64 ranks.  A rank reads what
  * the others stored only after all of them finished (order them with a
@@ -76,13 +81,16 @@ CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferOpen(const void* ipc
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferClose(void* ptr);
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200PeerBufferDestroy(void* ptr);
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepScatterColumns(const void* x, void* const* dest, int ranks,
-                                                                        int rank, size_t n1, size_t n2,
+                                                                        int rank, size_t n1, size_t n2, size_t c0,
+                                                                        size_t width, int ctas_per_sm,
                                                                         cudaStream_t stream);
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepScatterRows(const void* spec, void* const* dest, int ranks,
-                                                                     int rank, size_t n1, size_t n2, int inverse,
+                                                                     int rank, size_t n1, size_t n2, size_t c0,
+                                                                     size_t width, int inverse, int ctas_per_sm,
                                                                      cudaStream_t stream);
 CUBUTTERFLYAPI cubutterflyStatus_t cubutterflyB200FourStepScatterTranspose(const void* out, void* const* dest,
                                                                           int ranks, int rank, size_t n1, size_t n2,
+                                                                          size_t row0, size_t rows, int ctas_per_sm,
                                                                           cudaStream_t stream);
 
 /* Device-side failure status of a plan (no counterpart in the reference ABI;

@@ -587,12 +587,18 @@ def test_peer_transport_entry_points_check_arguments_on_cpu(lib):
     x = 0x40000
     scol, srow, stra = (lib.fn[k] for k in ("B200FourStepScatterColumns", "B200FourStepScatterRows",
                                             "B200FourStepScatterTranspose"))
-    assert scol(x, dest, 3, 0, 1 << 12, 1 << 12, None) == invalid        # 3 ranks
-    assert scol(x, dest, 2, 2, 1 << 12, 1 << 12, None) == invalid        # rank out of range
-    assert scol(x + 8, dest, 2, 0, 1 << 12, 1 << 12, None) == invalid    # unaligned source
-    assert scol(x, dest, 2, 0, 3 << 10, 1 << 12, None) == invalid        # n1 not a power of two
+    w = 1 << 11
+    assert scol(x, dest, 3, 0, 1 << 12, 1 << 12, 0, w, 0, None) == invalid        # 3 ranks
+    assert scol(x, dest, 2, 2, 1 << 12, 1 << 12, 0, w, 0, None) == invalid        # rank out of range
+    assert scol(x + 8, dest, 2, 0, 1 << 12, 1 << 12, 0, w, 0, None) == invalid    # unaligned source
+    assert scol(x, dest, 2, 0, 3 << 10, 1 << 12, 0, w, 0, None) == invalid        # n1 not a power of two
+    assert scol(x, dest, 2, 0, 1 << 12, 1 << 12, 512, 1024, 0, None) == invalid   # part not aligned to its width
+    assert scol(x, dest, 2, 0, 1 << 12, 1 << 12, 1024, 2048, 0, None) == invalid  # part past N2/P
     bad = (ct.c_void_p * 2)(0x10000, 0x20008)
-    assert scol(x, ct.cast(bad, ct.c_void_p), 2, 0, 1 << 12, 1 << 12, None) == invalid  # unaligned peer
-    assert srow(x, dest, 2, 0, 1 << 12, 64, 0, None) == invalid          # n2 < 64 ranks
-    assert stra(x, dest, 2, 0, 128, 1 << 12, None) == invalid            # n1 < 128 ranks
+    assert scol(x, ct.cast(bad, ct.c_void_p), 2, 0, 1 << 12, 1 << 12, 0, w, 0, None) == invalid  # unaligned peer
+    assert srow(x, dest, 2, 0, 1 << 12, 64, 0, 32, 0, 0, None) == invalid         # n2 < 64 ranks
+    assert srow(x, dest, 2, 0, 1 << 12, 1 << 12, 0, 32, 0, 0, None) == invalid    # part narrower than 64
+    assert stra(x, dest, 2, 0, 128, 1 << 12, 0, 64, 0, None) == invalid           # n1 < 128 ranks
     assert b"128" in lib.fn["GetLastErrorString"]()
+    assert scol(x, dest, 2, 0, 1 << 12, 1 << 12, 0, w, 33, None) == invalid    # ctas_per_sm out of range
+    assert stra(x, dest, 2, 0, 1 << 12, 1 << 12, 64, 128, 0, None) == invalid     # rows not in 128-row tiles

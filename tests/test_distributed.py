@@ -355,8 +355,10 @@ def _peer_worker(rank, world, port, log_n, inverse, q):
         del x, y
         torch.cuda.empty_cache()
         errs = {}
-        for transport in ("peer", "nccl"):
-            fs = FourStepFFT(n, device=dev, inverse=inverse, transport=transport)
+        for transport, pipeline in (("peer", True), ("peer", False), ("nccl", False)):
+            fs = FourStepFFT(n, device=dev, inverse=inverse, transport=transport, pipeline=pipeline)
+            if transport == "peer":
+                assert (fs._pipeline is not None) == pipeline
             got = fs(mine)
             got = fs(mine).clone()  # a second call on the same buffers
             torch.cuda.synchronize()
@@ -366,7 +368,7 @@ def _peer_worker(rank, world, port, log_n, inverse, q):
                 a, b = got[i:i + (1 << 25)].double(), want[i:i + (1 << 25)].double()
                 num += float(torch.sum((a - b) ** 2))
                 den += float(torch.sum(b * b))
-            errs[transport] = (num / den) ** 0.5
+            errs[transport + ("-pipelined" if pipeline else "")] = (num / den) ** 0.5
             del got
         q.put((rank, errs))
     finally:

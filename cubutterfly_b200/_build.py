@@ -44,7 +44,7 @@ def _units():
     units = []
     for name in ("c_api.cpp", "descriptor.cpp", "planner.cpp", "rns_api.cpp", "launch_bitwise_dispatch.cpp",
                  "launch_ntt_dispatch.cpp", "launch_fft.cu", "noalloc.cu", "fourstep.cu", "bitrev.cu", "fwht_tc.cu",
-                 "real_adapter.cu", "real_fft.cu", "calibrate.cu", "fourstep_peer.cu", "unaligned.cu", "structured.cu", "fwht_native.cu", "fft64.cu",
+                 "real_adapter.cu", "real_fft.cu", "calibrate.cu", "fourstep_peer.cu", "unaligned.cu", "structured.cu", "fwht_native.cu", "fft64.cu", "fft_chain.cu",
                  "heongpu_adapter.cpp", "bluestein.cu"):
         src = CSRC / name
         obj = OBJ / (src.stem + ".o")

@@ -661,7 +661,10 @@ void launch_fft_blocked(const cubutterflyPlan& p, const cubf::Mapping& m, const 
 // the low b0 + b1 bits.  The first pass writes the workspace with an L2
 // evict-last policy, the second reads it back from L2 and discards its lines,
 // so each pair reads and writes HBM once.  Tiles of 32 columns; a chunk holds
-// 2^22 values.
+// 2^22 values.  A pair of C chunks runs as C + 1 chain steps
+// (launch_fft_chain_step, csrc/fft_chain.cu): step k runs the pair's first
+// pass over chunk k beside its second pass over chunk k-1, each step a
+// programmatic dependent launch of the one before.
 void launch_fft_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const void* in, void* out, void* core_ws,
                       float scale, cudaStream_t stream) {
     const auto& d = p.desc;
@@ -671,12 +674,23 @@ void launch_fft_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const vo
     const int b0 = m.passes[0].log_h, b1 = m.passes[1].log_h, b2 = m.passes[2].log_h, b3 = m.passes[3].log_h;
     const int tl = cubf::kFftChainColumnsLog;
     const cubf::FftOuterTables outer{p.outer_lo, p.outer_hi, p.outer_split};
-    auto pass = [&](int i, const void* src, void* dst, const cubf::FftChunk& c) {
+    auto role = [&](int i, const void* src, void* dst, const cubf::FftChunk& c) {
         const bool last = i == 3;
-        check_cuda(cubf::launch_fft_chain_pass(m.passes[i].log_h, src, dst, ln, m.passes[i].log_inner, p.twiddles,
-                                               outer, inverse && i == 0, inverse && last, last ? scale : 1.0f, c,
-                                               stream),
-                   "FFT chained pass launch");
+        return cubf::FftChainRole{src, dst, m.passes[i].log_h, m.passes[i].log_inner, inverse && i == 0,
+                                  inverse && last, last ? scale : 1.0f, c, false};
+    };
+    const cubf::FftChunk none{0, 0, 0, 0, false, false};
+    // one pair over `chunks` chunks: chunk c's A and B roles from make(c)
+    auto pair = [&](std::uint32_t chunks, auto make_a, auto make_b) {
+        for (std::uint32_t k = 0; k <= chunks; ++k) {
+            const cubf::FftChainRole a = k < chunks ? make_a(k) : make_a(0);
+            const cubf::FftChainRole b = k > 0 ? make_b(k - 1) : make_b(0);
+            cubf::FftChainRole ra = a, rb = b;
+            if (k == chunks) ra.chunk = none;
+            if (k == 0) rb.chunk = none;
+            ra.wait = k == 0;  // the pair's first step reads what came before it
+            check_cuda(cubf::launch_fft_chain_step(ra, rb, ln, p.twiddles, outer, stream), "FFT chain step launch");
+        }
     };
     for (std::size_t b = 0; b < d.batch; ++b) {
         const float2* src = static_cast<const float2*>(in) + b * n;
@@ -687,20 +701,30 @@ void launch_fft_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const vo
         {
             const int kb = ln - b0 - b1;
             const int fl = std::min(kb, cubf::kFftChainChunkLog - b0 - b1);
-            for (std::uint32_t h0 = 0; h0 < (1u << kb); h0 += 1u << fl) {
-                pass(0, src, ws, {h0, 1u << (fl - tl), 1u << kb, 1u << b1, false, true});
-                pass(1, ws, dst, {h0 << b0, 1u << (fl + b0 - tl), 0, 1, true, false});
-            }
+            pair(
+                1u << (kb - fl),
+                [&](std::uint32_t c) {
+                    const std::uint32_t h0 = c << fl;
+                    return role(0, src, ws, {h0, 1u << (fl - tl), 1u << kb, 1u << b1, false, true});
+                },
+                [&](std::uint32_t c) {
+                    const std::uint32_t h0 = c << fl;
+                    return role(1, ws, dst, {h0 << b0, 1u << (fl + b0 - tl), 0, 1, true, false});
+                });
         }
         // pair two: key l < 2^(b0 + b1); pass 2 columns r 2^s + l (r < 2^b3),
         // pass 3 columns k 2^s + l (k < 2^b2), s = b0 + b1
         {
             const int s = b0 + b1;
             const int fl = std::min(s, cubf::kFftChainChunkLog - b2 - b3);
-            for (std::uint32_t l0 = 0; l0 < (1u << s); l0 += 1u << fl) {
-                pass(2, dst, ws, {l0, 1u << (fl - tl), 1u << s, 1u << b3, false, true});
-                pass(3, ws, dst, {l0, 1u << (fl - tl), 1u << s, 1u << b2, true, false});
-            }
+            pair(
+                1u << (s - fl),
+                [&](std::uint32_t c) {
+                    return role(2, dst, ws, {c << fl, 1u << (fl - tl), 1u << s, 1u << b3, false, true});
+                },
+                [&](std::uint32_t c) {
+                    return role(3, ws, dst, {c << fl, 1u << (fl - tl), 1u << s, 1u << b2, true, false});
+                });
         }
     }
 }

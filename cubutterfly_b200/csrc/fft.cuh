@@ -492,11 +492,19 @@ CUBF_DEV void discard_l2_line(const void* p) {
 // FIRST: Ns = 1 (and no interleaving; T >= 16), the tile's output is C R
 // contiguous values; otherwise Ns >= C.  Offsets within one transform (or one
 // interleaved array) are 32-bit: 2^log_n <= 2^31.
-template <int LOGR, bool FIRST, int CW = 0, bool CHUNKED = false>
-__global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<LOGR, CW>::MINB)
-    fft_global_reg_kernel(const float2* src, float2* dst, int log_n, int ns_bits, const float2* __restrict__ tw1024,
-                          OuterTwiddles outer, int conj_in, int conj_out, float scale, int log_v,
-                          unsigned prefetch_stride, int outer_shift, RegChunk chunk) {
+//
+// reg_pass_tile is the body of one CTA of the pass: tile `vblock` of a grid
+// of `vgrid` tiles, run by threads tid < TPB over the shared memory at
+// `smem`.  fft_global_reg_kernel runs one tile per CTA; the chain-step kernel
+// (fft_chain_step_kernel) runs tiles of two passes side by side.  ROLE fixes
+// a chunked tile's L2 flags at compile time: 1 the first pass of a chain
+// pair (HBM source, L2-kept destination), 2 the second (L2 source, HBM
+// destination); 0 takes them from `chunk`.
+template <int LOGR, bool FIRST, int CW, bool CHUNKED, int ROLE = 0>
+CUBF_DEV void reg_pass_tile(const float2* src, float2* dst, int log_n, int ns_bits, const float2* __restrict__ tw1024,
+                            const OuterTwiddles& outer, int conj_in, int conj_out, float scale, int log_v,
+                            unsigned prefetch_stride, int outer_shift, const RegChunk& chunk, size_t vblock,
+                            size_t vgrid, int tid, unsigned char* smem_raw) {
     using G = GlobalRegShape<LOGR, CW>;
     using S = typename G::S;
     constexpr int RB0 = S::radix_bits(0);
@@ -504,14 +512,13 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
     constexpr int SUB0 = S::E / RA;     // its sub-DFTs per thread
     constexpr int ROWSTEP = G::R / RA;  // row distance within a first-phase sub-DFT
     constexpr int PL = S::NPASS - 1;    // last register phase
-    extern __shared__ __align__(16) unsigned char smem_raw[];
     float2* a = reinterpret_cast<float2*>(smem_raw);
     float2* full = a + G::TILE_BYTES / 8;
     float2* rows = full + G::R;
     if constexpr (G::EXCHANGE) {
         // W_R^m = W_1024^(m 2^(10 - LOGR)); rows[r NsL + jm] = W_R^(jm r) for the last phase
         constexpr int NSL = 1 << S::ns_bits(PL);
-        for (int m = threadIdx.x; m < G::R; m += G::TPB) {
+        for (int m = tid; m < G::R; m += G::TPB) {
             full[m] = __ldg(tw1024 + (m << (10 - LOGR)));
             const int r = m / NSL, jm = m % NSL;
             rows[m] = __ldg(tw1024 + (((jm * r) & (G::R - 1)) << (10 - LOGR)));
@@ -532,12 +539,12 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
     };
     size_t bidx;
     uint32_t j0;
-    tile_origin(blockIdx.x, bidx, j0);
+    tile_origin(vblock, bidx, j0);
     const uint32_t ns = 1u << ns_bits;
     float2 v[S::E];
     // phase 0: straight from HBM, columns on consecutive threads
-    const int c0 = threadIdx.x & (G::C - 1);
-    const int th0 = threadIdx.x >> G::LOG_C;
+    const int c0 = tid & (G::C - 1);
+    const int th0 = tid >> G::LOG_C;
     {
         const float2* col = src + (bidx << log_n) + j0 + c0;
         const uint32_t rstep = ROWSTEP * cols;
@@ -548,12 +555,12 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
             for (int r = 0; r < RA; ++r) v[u * RA + r] = __ldcs(col + (off + r * rstep));
         }
     }
-    if (prefetch_stride != 0 && blockIdx.x + static_cast<size_t>(prefetch_stride) < gridDim.x) {
+    if (prefetch_stride != 0 && vblock + static_cast<size_t>(prefetch_stride) < vgrid) {
         size_t nt;
         uint32_t nj;
-        tile_origin(blockIdx.x + static_cast<size_t>(prefetch_stride), nt, nj);
+        tile_origin(vblock + static_cast<size_t>(prefetch_stride), nt, nj);
         const float2* nsrc = src + (nt << log_n) + nj;
-        for (int r = threadIdx.x; r < G::R; r += G::TPB) prefetch_l2(nsrc + static_cast<uint32_t>(r) * cols, G::C * 8);
+        for (int r = tid; r < G::R; r += G::TPB) prefetch_l2(nsrc + static_cast<uint32_t>(r) * cols, G::C * 8);
     }
     if (conj_in) {
 #pragma unroll
@@ -579,7 +586,9 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
     }
 #pragma unroll
     for (int u = 0; u < SUB0; ++u) Dft<RA>::run(&v[u * RA]);
-    if (CHUNKED && chunk.src_l2) {
+    const bool src_l2 = CHUNKED && (ROLE == 0 ? chunk.src_l2 != 0 : ROLE == 2);
+    const bool dst_l2 = CHUNKED && (ROLE == 0 ? chunk.dst_l2 != 0 : ROLE == 1);
+    if (src_l2) {
         // every value of this warp's lines is in registers: drop the lines
         // (a warp loads whole 128-byte lines of 16 columns)
         __syncwarp();
@@ -599,10 +608,10 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
     float2* dbase = dst + (bidx << log_n) + (((j0 >> ns_bits) << (ns_bits + LOGR)) + (j0 & (ns - 1)));
     const float out_sgn = conj_out ? -1.f : 1.f;
     const bool plain = scale == 1.f && !conj_out;
-    const uint64_t keep = CHUNKED && chunk.dst_l2 ? l2_policy(true) : 0;
+    const uint64_t keep = dst_l2 ? l2_policy(true) : 0;
     auto emit = [&](float2* p, float2 x) {
         const float2 y = plain ? x : make_float2(x.x * scale, x.y * out_sgn * scale);
-        if (CHUNKED && chunk.dst_l2)
+        if (dst_l2)
             asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(y.x), "f"(y.y),
                          "l"(keep)
                          : "memory");
@@ -622,8 +631,8 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
         constexpr int NSL = 1 << S::ns_bits(PL);
         if constexpr (FIRST) {
             // a column's threads on consecutive lanes: y[J R + k] in runs of T
-            const int c1 = static_cast<int>(threadIdx.x) / S::T;
-            const int th1 = static_cast<int>(threadIdx.x) % S::T;
+            const int c1 = tid / S::T;
+            const int th1 = tid % S::T;
             const float2* col = a + c1 * G::RS;
             pass_load_tw<LOGR, PL>(v, th1, [&](int jm, int r) { return rows[r * NSL + jm]; },
                                    [&](int i) { return col[S::pad(i)]; });
@@ -638,6 +647,18 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
         }
     }
 }
+
+template <int LOGR, bool FIRST, int CW = 0, bool CHUNKED = false>
+__global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<LOGR, CW>::MINB)
+    fft_global_reg_kernel(const float2* src, float2* dst, int log_n, int ns_bits, const float2* __restrict__ tw1024,
+                          OuterTwiddles outer, int conj_in, int conj_out, float scale, int log_v,
+                          unsigned prefetch_stride, int outer_shift, RegChunk chunk) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    reg_pass_tile<LOGR, FIRST, CW, CHUNKED>(src, dst, log_n, ns_bits, tw1024, outer, conj_in, conj_out, scale, log_v,
+                                            prefetch_stride, outer_shift, chunk, blockIdx.x, gridDim.x,
+                                            static_cast<int>(threadIdx.x), smem_raw);
+}
+
 
 
 // ---- L2-blocked large transform: first pass of the decimated transforms ------

@@ -68,9 +68,27 @@ constexpr int kFftChainMinLog = 6;       // pass radices of the chained plans
 constexpr int kFftChainMaxLog = 8;
 constexpr int kFftChainColumnsLog = 5;   // 32 columns per CTA
 bool fft_chain_pass_available(int log_r);
-cudaError_t launch_fft_chain_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,
-                                  const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
-                                  const FftChunk& chunk, cudaStream_t stream);
+// One role of a chain step (csrc/fft_chain.cu): a pass of radix 2^log_r with
+// Ns = 2^ns_bits over one chunk; a chunk with zero runs leaves the role out.
+// Role A (the pair's first pass) writes an L2-kept intermediate and may
+// conjugate its input; role B (the second pass) reads one and may conjugate
+// and scale its output.  `wait`: role A reads what the previous kernel on
+// the stream wrote (role B always does).
+struct FftChainRole {
+    const void* src;
+    void* dst;
+    int log_r;
+    int ns_bits;
+    bool conj_in;
+    bool conj_out;
+    float scale;
+    FftChunk chunk;
+    bool wait;
+};
+// Step k of an L2-chained pass pair: B over chunk k-1 and A over chunk k in
+// one launch (A's radix 2^8 when it is the transform's first pass).
+cudaError_t launch_fft_chain_step(const FftChainRole& a, const FftChainRole& b, int log_n, const void* tw1024,
+                                  const FftOuterTables& outer, cudaStream_t stream);
 cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits,
                                    std::size_t batch, const void* tw1024, const FftOuterTables& outer, bool conj_in,
                                    bool conj_out, float scale, cudaStream_t stream, int log_v = 0,

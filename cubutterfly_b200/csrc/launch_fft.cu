@@ -198,16 +198,6 @@ struct RegWideTable {
     static constexpr GlobalLaunch later_fns[] = {RegEntry<L, false, 32>::launch...};
 };
 using RegWide = RegWideTable<6, 7, 8>;
-template <int... L>
-struct ChainTable {
-    static constexpr cudaError_t (*first_fns[])(const void*, void*, int, int, const void*, const FftOuterTables&,
-                                                bool, bool, float, const FftChunk&, cudaStream_t) = {
-        RegEntry<L, true, 32, true>::chunk_run...};
-    static constexpr cudaError_t (*later_fns[])(const void*, void*, int, int, const void*, const FftOuterTables&,
-                                                bool, bool, float, const FftChunk&, cudaStream_t) = {
-        RegEntry<L, false, 32, true>::chunk_run...};
-};
-using Chain = ChainTable<6, 7, 8>;
 constexpr int kRegWideMinLog = 26;
 
 // 8-column variants of the large radices (64-byte runs, two CTAs per SM at 2^10)
@@ -282,18 +272,6 @@ cudaError_t launch_fft_global_pass(int log_r, const void* src, void* dst, int lo
                                  log_v, outer_shift);
     return Global::launch_fns[i](src, dst, log_n, ns_bits, batch, tw1024, outer, conj_in, conj_out, scale, stream,
                                  log_v, outer_shift);
-}
-
-cudaError_t launch_fft_chain_pass(int log_r, const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,
-                                  const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
-                                  const FftChunk& chunk, cudaStream_t stream) {
-    if (!fft_chain_pass_available(log_r) || log_n > 31 || chunk.tiles_per_run == 0 || chunk.runs == 0)
-        return cudaErrorInvalidValue;
-    const bool first = ns_bits == 0;
-    if (!first && ns_bits < kFftChainColumnsLog) return cudaErrorInvalidValue;
-    const int k = log_r - kFftChainMinLog;
-    return first ? Chain::first_fns[k](src, dst, log_n, ns_bits, tw1024, outer, conj_in, conj_out, scale, chunk, stream)
-                 : Chain::later_fns[k](src, dst, log_n, ns_bits, tw1024, outer, conj_in, conj_out, scale, chunk, stream);
 }
 
 bool fft_chain_pass_available(int log_r) { return log_r >= kFftChainMinLog && log_r <= kFftChainMaxLog; }

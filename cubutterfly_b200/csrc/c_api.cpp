@@ -695,7 +695,10 @@ void launch_fft_chain(const cubutterflyPlan& p, const cubf::Mapping& m, const vo
     for (std::size_t b = 0; b < d.batch; ++b) {
         const float2* src = static_cast<const float2*>(in) + b * n;
         float2* dst = static_cast<float2*>(out) + b * n;
-        float2* ws = static_cast<float2*>(core_ws);
+        // the intermediate starts on a 128-byte line: the second pass of a
+        // pair drops whole lines of it from L2
+        float2* ws = reinterpret_cast<float2*>((reinterpret_cast<std::uintptr_t>(core_ws) + 127) &
+                                               ~std::uintptr_t{127});
         // pair one: key h < 2^(n - b0 - b1); pass 0 columns r 2^(n-b0-b1) + h (r < 2^b1),
         // pass 1 columns h 2^b0 + k (k < 2^b0)
         {

@@ -475,7 +475,7 @@ struct GlobalRegMiddle {
 // base + (b mod tiles_per_run) C + (b / tiles_per_run) run_stride of the
 // pass's single transform.  `src_l2`: the source is an intermediate the
 // previous launch left in L2; each 128-byte line is discarded from L2 once
-// its warp holds the values (never written back to HBM).  `dst_l2`: the
+// the tile holds its values (never written back to HBM).  `dst_l2`: the
 // destination is such an intermediate (stored with an L2 evict-last policy).
 struct RegChunk {
     uint32_t base;
@@ -588,21 +588,17 @@ CUBF_DEV void reg_pass_tile(const float2* src, float2* dst, int log_n, int ns_bi
     for (int u = 0; u < SUB0; ++u) Dft<RA>::run(&v[u * RA]);
     const bool src_l2 = CHUNKED && (ROLE == 0 ? chunk.src_l2 != 0 : ROLE == 2);
     const bool dst_l2 = CHUNKED && (ROLE == 0 ? chunk.dst_l2 != 0 : ROLE == 1);
-    if (src_l2) {
-        // every value of this warp's lines is in registers: drop the lines
-        // (a warp loads whole 128-byte lines of 16 columns)
-        __syncwarp();
-        if ((c0 & 15) == 0) {
-            const float2* col = src + (bidx << log_n) + j0 + c0;
-            const uint32_t rstep = ROWSTEP * cols;
-#pragma unroll
-            for (int u = 0; u < SUB0; ++u) {
-                const uint32_t off = static_cast<uint32_t>(th0 + S::T * u) * cols;
-#pragma unroll
-                for (int r = 0; r < RA; ++r) discard_l2_line(col + (off + r * rstep));
-            }
-        }
-    }
+    // Once every thread of the tile has loaded its values (after the first
+    // exchange's barrier), drop the tile's source lines from L2 without
+    // writing them back: R rows of C = 32 columns, two 128-byte lines per
+    // row, one line per thread (TPB = 2R).  The addresses come from the
+    // thread index, not from the loads, so none stays live across the DFTs
+    // (reusing the load addresses there cost ~100 bytes of spills a thread).
+    static_assert(!CHUNKED || (G::EXCHANGE && G::TPB == 2 * G::R), "chunked tiles discard one line per thread");
+    auto discard_source = [&]() {
+        const uint32_t row = static_cast<uint32_t>(tid) >> 1;
+        discard_l2_line(src + (bidx << log_n) + j0 + row * cols + (static_cast<uint32_t>(tid) & 1u) * 16u);
+    };
     // the output's column base: y[(J / Ns) Ns R + (J mod Ns) + k Ns] with
     // J = j0 + c, j0 a multiple of C; Ns = 1 reduces it to y[J R + k]
     float2* dbase = dst + (bidx << log_n) + (((j0 >> ns_bits) << (ns_bits + LOGR)) + (j0 & (ns - 1)));
@@ -626,6 +622,7 @@ CUBF_DEV void reg_pass_tile(const float2* src, float2* dst, int log_n, int ns_bi
     } else {
         pass_store<LOGR, 0>(v, th0, [&](int i, float2 x) { a[c0 * G::RS + S::pad(i)] = x; });
         __syncthreads();
+        if (src_l2) discard_source();
         GlobalRegMiddle<LOGR, 1>::run(v, th0, full, a + c0 * G::RS);
         constexpr int SHIFT = LOGR - S::ns_bits(PL) - S::radix_bits(PL);
         constexpr int NSL = 1 << S::ns_bits(PL);

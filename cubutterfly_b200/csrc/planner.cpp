@@ -405,16 +405,17 @@ Mapping fft_chain_mapping(const PlanRequest& r, const HardwareProfile& hw, const
         p.log_inner = ns;
         p.shape = fft_global_pass_shape(bits);
         require(fits(p.shape, hw), "FFT pass tile does not fit the device");
-        // measured on a B200: a 2^22-value chunk pass is ~1.7 waves of CTAs,
-        // so each launch pays its ramp and tail (2^30 points: 1024 launches,
-        // 18.3 ms against 12.7 ms for the Stockham plan; 2^26: 1.05 ms
-        // against 0.68 ms), i.e. each pass at ~0.6 of HBM speed although half
-        // its traffic stays in L2
-        m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, 0.6);
+        // measured on a B200 with both passes of a pair in each chain step
+        // (PDL between steps): a pair moves ~1.1x its ideal DRAM bytes (the
+        // intermediate stays in L2), but the steps run at ~2.6-3 TB/s, so the
+        // plan only matches the Stockham plan (2^30: 11.4-11.8 ms against
+        // 11.75; 2^28: 2.79 against 2.71 ms; 2^26: 0.72 against 0.67 ms),
+        // i.e. each pass at ~0.45 of HBM speed on its full traffic
+        m.predicted_us += pass_time_us(hw, elems, 8.0, 8.0, bits, p.shape.exchanges, 2.5 / 2.0, 0.45);
         m.passes.push_back(p);
         ns += bits;
     }
-    m.workspace_bytes = std::size_t{8} << r.log_n;
+    m.workspace_bytes = (std::size_t{8} << r.log_n) + 128;  // the intermediate, aligned up to a 128-byte line
     return m;
 }
 

@@ -372,3 +372,30 @@ def test_fft_l2_chain_plans(lib, oracle, cuda, log_n, mapping):
     z, zname = planned(fft_transform(n, 2, in_place=True), z)
     assert not zname.startswith("fft-l2-chain"), zname
     assert _rel_l2_dev(z, y) <= TOL
+
+
+def test_fft_l2_chain_unaligned_workspace(lib, cuda):
+    """The L2-chained plan drops its intermediate's lines from L2 once read;
+    with a workspace that is 16-byte but not 128-byte aligned the
+    intermediate still starts on a line of its own, so no line shared with
+    other data is dropped: same result as the Stockham plan (rel L2 <= 2e-6)."""
+    import torch
+
+    n = 1 << 26
+    x = w.torch_fft_input(n, 1, cuda, seed=5).reshape(n, 2)
+    stream = torch.cuda.current_stream().cuda_stream
+    with cb.Plan(lib, fft_transform(n, 1), options=cb.PlanOptions(mapping="fft-l2-chain[8+6+6+6]"),
+                 stream=stream) as plan, \
+            cb.Plan(lib, fft_transform(n, 1), options=cb.PlanOptions(mapping="8+6+6+6"), stream=stream) as ref:
+        assert plan.algorithm_name() == "fft-l2-chain[8+6+6+6]"
+        ws = torch.empty(plan.workspace_size() + 16, dtype=torch.uint8, device=cuda)
+        plan.set_workspace(ws.data_ptr() + 16, plan.workspace_size())
+        ref_ws = torch.empty(ref.workspace_size(), dtype=torch.uint8, device=cuda)
+        ref.set_workspace(ref_ws.data_ptr(), ref.workspace_size())
+        y, want = torch.empty_like(x), torch.empty_like(x)
+        ref.execute(x.data_ptr(), want.data_ptr())
+        for _ in range(2):
+            y.zero_()
+            plan.execute(x.data_ptr(), y.data_ptr())
+            torch.cuda.synchronize()
+            assert _rel_l2_dev(y, want) <= TOL

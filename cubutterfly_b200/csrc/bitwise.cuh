@@ -590,6 +590,7 @@ __global__ void __launch_bounds__(TileShape<TS, TC, LOGH, LOGW, LOGE>::TPB,
     bitwise_tile_kernel(const TS* in, TS* out, size_t outer, int log_inner, int inverse, float scale,
                         int cache_mode, unsigned prefetch_stride) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    pdl_begin();
     tile_pass<Op, TS, TC, LOGH, LOGW, LOGE, false>(in, out, outer, log_inner, inverse, scale, cache_mode,
                                                    prefetch_stride, blockIdx.x, gridDim.x, threadIdx.x, smem_raw);
 }

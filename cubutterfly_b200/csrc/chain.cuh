@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(ChainShape<Op, TS, TC, H0, H1, LOGW1, LOGE>::T
     using A = typename K::A;
     using B = typename K::B;
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    pdl_begin();
     const size_t b = blockIdx.x;
     // the step's B CTAs first: they drain chunk k-1 from L2 before the A
     // CTAs that come after them fill it with chunk k

@@ -123,6 +123,20 @@ struct alignas(16) Vec16 {
 // final pass streams its output.
 enum CacheMode : int { kStream = 0, kChainFirst = 1, kChainLast = 2, kChainMiddle = 3 };
 
+// Programmatic dependent launch (launch_dependent in launch_util.cuh): a
+// kernel launched that way may be scheduled while the kernel before it on
+// the stream still runs; pdl_begin() waits until that kernel has completed
+// and its writes are visible, then lets the kernel after this one be
+// scheduled the same way.  Called first, before any global memory access, so
+// the kernel's semantics are those of an ordinary stream-ordered launch; what
+// it gains is the launch and CTA scheduling latency between back-to-back
+// kernels.  Both instructions are no-ops in a kernel launched without the
+// attribute.
+CUBF_DEV void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Bulk prefetch of [p, p + bytes) into L2 (one instruction; p 16-byte
 // aligned, bytes a multiple of 16).  One-shot kernels issue it for the tile
 // the CTA one resident wave later will read, so DRAM keeps streaming while

@@ -651,6 +651,7 @@ __global__ void __launch_bounds__(GlobalRegShape<LOGR, CW>::TPB, GlobalRegShape<
                           OuterTwiddles outer, int conj_in, int conj_out, float scale, int log_v,
                           unsigned prefetch_stride, int outer_shift, RegChunk chunk) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    pdl_begin();
     reg_pass_tile<LOGR, FIRST, CW, CHUNKED>(src, dst, log_n, ns_bits, tw1024, outer, conj_in, conj_out, scale, log_v,
                                             prefetch_stride, outer_shift, chunk, blockIdx.x, gridDim.x,
                                             static_cast<int>(threadIdx.x), smem_raw);

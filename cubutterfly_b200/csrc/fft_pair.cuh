@@ -286,6 +286,7 @@ __global__ void __launch_bounds__(PairShape<LOGN>::TPB, pair_min_blocks<LOGN>())
                     float scale, unsigned prefetch_stride) {
     using S = PairShape<LOGN>;
     extern __shared__ __align__(16) float smem_f[];
+    pdl_begin();
     const int c = threadIdx.x / S::T;
     const int q = threadIdx.x % S::T;
     const size_t row = static_cast<size_t>(blockIdx.x) * S::TPC + c;

@@ -267,6 +267,7 @@ __global__ void __launch_bounds__(FwhtShape<TS, LOGH, LOGE>::TPB, fwht_min_block
     using S = FwhtShape<TS, LOGH, LOGE>;
     static_assert(S::E >= 2 && S::V * sizeof(TS) == 16, "FWHT tiles move 16-byte vectors");
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    pdl_begin();
     const int local = threadIdx.x / S::TPT;
     const uint32_t t = threadIdx.x % S::TPT;
     const size_t row = static_cast<size_t>(blockIdx.x) * S::TILES + local;

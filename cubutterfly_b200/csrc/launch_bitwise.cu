@@ -90,9 +90,8 @@ struct FwhtEntry {
         const std::size_t blocks = (outer + S::TILES - 1) / S::TILES;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
         const unsigned stride = blocks > static_cast<std::size_t>(grid_cap) ? grid_cap : 0;
-        kernel<<<static_cast<unsigned>(blocks), S::TPB, SMEM, stream>>>(static_cast<const TS*>(in),
-                                                                          static_cast<TS*>(out), outer, scale, stride);
-        return cudaGetLastError();
+        return launch_dependent(kernel, static_cast<unsigned>(blocks), S::TPB, SMEM, stream, static_cast<const TS*>(in),
+                                static_cast<TS*>(out), outer, scale, stride);
     }
 };
 #endif
@@ -127,10 +126,9 @@ struct Entry {
         // contiguous passes that stream from DRAM prefetch one resident wave ahead
         const bool streams_in = LOGW == 0 && (cache_mode == kStream || cache_mode == kChainFirst);
         const unsigned stride = streams_in && blocks > static_cast<std::size_t>(grid_cap) ? grid_cap : 0;
-        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-            static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0, scale, cache_mode,
-            stride);
-        return cudaGetLastError();
+        return launch_dependent(kernel, static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream,
+                                static_cast<const TS*>(in), static_cast<TS*>(out), outer, log_inner, inverse ? 1 : 0,
+                                scale, cache_mode, stride);
     }
 };
 
@@ -233,8 +231,9 @@ struct ChainEntry {
                 if (total > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
                 // a half wave ahead while both roles share a step (measured best: 737 vs 760-762 us)
                 st.prefetch_stride = st.b_blocks ? static_cast<unsigned>(grid_cap / 2) : static_cast<unsigned>(grid_cap);
-                kernel<<<static_cast<unsigned>(total), K::TPB, K::SMEM_BYTES, stream>>>(st);
-                if ((e = cudaGetLastError()) != cudaSuccess) return e;
+                if ((e = launch_dependent(kernel, static_cast<unsigned>(total), K::TPB, K::SMEM_BYTES, stream, st)) !=
+                    cudaSuccess)
+                    return e;
             }
             return cudaSuccess;
         }

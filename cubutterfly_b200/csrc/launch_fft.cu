@@ -39,9 +39,9 @@ cudaError_t launch_pair(const void* in, void* out, std::size_t batch, const void
     if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
     // prefetch one resident wave ahead when the grid has more than one wave
     const unsigned stride = blocks > static_cast<std::size_t>(grid_cap) ? grid_cap : 0;
-    kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
-        static_cast<const float4*>(in), static_cast<float4*>(out), batch, table, inverse ? 1 : 0, scale, stride);
-    return cudaGetLastError();
+    return launch_dependent(kernel, static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream,
+                            static_cast<const float4*>(in), static_cast<float4*>(out), batch, table, inverse ? 1 : 0,
+                            scale, stride);
 }
 
 template <int LOGN>
@@ -145,11 +145,10 @@ struct RegEntry {
         // an L2-resident source needs no prefetch
         const unsigned prefetch =
             !chunk.src_l2 && blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u;
-        kernel<<<static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream>>>(
-            static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits,
-            static_cast<const float2*>(tw1024), ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale, log_v, prefetch,
-            outer_shift, chunk);
-        return cudaGetLastError();
+        return launch_dependent(kernel, static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream,
+                                static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits,
+                                static_cast<const float2*>(tw1024), ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale,
+                                log_v, prefetch, outer_shift, chunk);
         }
     }
     static cudaError_t chunk_run(const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,

@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
+#include <utility>
 
 namespace cubf {
 
@@ -55,6 +57,29 @@ cudaError_t setup_kernel(KernelSetup& setup, Kernel kernel, int threads, int sme
     }
     *grid_cap = cap;
     return cudaSuccess;
+}
+
+// Launch as a programmatic dependent of the kernel before it on the stream
+// (cudaLaunchAttributeProgrammaticStreamSerialization): the kernel's CTAs
+// may be scheduled while that kernel finishes, and must call pdl_begin()
+// (common.cuh) before touching global memory.  Between back-to-back kernels
+// of this library -- the passes of one execution, and successive executions
+// -- that hides the launch latency and the CTA ramp behind the previous
+// kernel's tail.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), unsigned grid, unsigned threads, std::size_t smem,
+                             cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace cubf

@@ -49,11 +49,13 @@ struct Entry {
         const std::size_t blocks = a.count * groups;
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
-        return launch_dependent(kernel, static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream,
-                                static_cast<const Word*>(a.in), static_cast<Word*>(a.out),
-                                reinterpret_cast<const ntt::PolyDesc*>(a.polys), device_tables(a.tables),
-                                a.in_is_out ? 1 : 0, a.final_pass ? 1 : 0, a.final_scale ? 1 : 0,
-                                a.reduce_input ? 1 : 0);
+        // an ordinary launch: as a programmatic dependent (launch_dependent)
+        // the two passes measured slower on config 2 (44.5 against 43.2 us)
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+            static_cast<const Word*>(a.in), static_cast<Word*>(a.out),
+            reinterpret_cast<const ntt::PolyDesc*>(a.polys), device_tables(a.tables), a.in_is_out ? 1 : 0,
+            a.final_pass ? 1 : 0, a.final_scale ? 1 : 0, a.reduce_input ? 1 : 0);
+        return cudaGetLastError();
     }
 };
 
@@ -78,9 +80,10 @@ struct SingleEntry {
         const std::size_t blocks = (a.count + S::COLS - 1) / S::COLS;
         if (blocks == 0) return cudaSuccess;
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
-        return launch_dependent(kernel, static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream,
-                                static_cast<const Word*>(a.in), static_cast<Word*>(a.out), a.count,
-                                device_tables(a.tables), a.final_scale ? 1 : 0, a.reduce_input ? 1 : 0);
+        kernel<<<static_cast<unsigned>(blocks), S::TPB, S::SMEM_BYTES, stream>>>(
+            static_cast<const Word*>(a.in), static_cast<Word*>(a.out), a.count, device_tables(a.tables),
+            a.final_scale ? 1 : 0, a.reduce_input ? 1 : 0);
+        return cudaGetLastError();
     }
 };
 

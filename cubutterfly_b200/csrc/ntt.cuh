@@ -320,7 +320,6 @@ __global__ void __launch_bounds__(PassShape<L, STRIDED, INV, LAZY, D>::TPB, Pass
     constexpr size_t GROUPS = (N >> B) / COLS;  // CTAs per polynomial
     extern __shared__ __align__(16) unsigned char smem_raw[];
     u64* sbuf = reinterpret_cast<u64*>(smem_raw);
-    pdl_begin();
 
     const size_t p = blockIdx.x / GROUPS;
     const uint32_t g = static_cast<uint32_t>(blockIdx.x % GROUPS);
@@ -421,7 +420,6 @@ __global__ void __launch_bounds__(SingleShape<L, INV, LAZY>::TPB, SingleShape<L,
     constexpr size_t N = size_t{1} << L;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     u64* sbuf = reinterpret_cast<u64*>(smem_raw);
-    pdl_begin();
     const int col = threadIdx.x / S::TPT;
     const uint32_t t = threadIdx.x % S::TPT;
     const size_t p = static_cast<size_t>(blockIdx.x) * S::COLS + col;

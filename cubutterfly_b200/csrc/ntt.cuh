@@ -151,11 +151,14 @@ struct NttShape {
 // stage ls = B-1-b forward) is roots[2^(off+ls) + (hi << ls) + (i >> (b+1))].
 // Root pair k with an L2 evict-last hint: the tables (16 bytes per root) stay
 // resident across calls while the coefficient streams pass through.
+// The tables are read-only for the kernel's lifetime, so the load is not
+// volatile: the compiler may issue it ahead of the butterflies that come
+// before its use.
 CUBF_DEV ulonglong2 load_root_pair(const u64* __restrict__ pairs, u64 k, uint64_t pol) {
     ulonglong2 r;
-    asm volatile("ld.global.nc.L2::cache_hint.v2.u64 {%0, %1}, [%2], %3;"
-                 : "=l"(r.x), "=l"(r.y)
-                 : "l"(pairs + 2 * k), "l"(pol));
+    asm("ld.global.nc.L2::cache_hint.v2.u64 {%0, %1}, [%2], %3;"
+        : "=l"(r.x), "=l"(r.y)
+        : "l"(pairs + 2 * k), "l"(pol));
     return r;
 }
 

@@ -278,7 +278,11 @@ CUBF_DEV void ntt_groups(u64 (&v)[S::E], u64* sbuf, int col, uint32_t t, u64 hi,
 // bits (D = 0 by default; the RNS tuner also tries D = -1 and +1).
 constexpr int strided_bits(int L, int D = 0) { return (L + 1) / 2 + D; }
 constexpr int contiguous_bits(int L, int D = 0) { return L / 2 - D; }
-constexpr int log_e_for(int b) { return b <= 6 ? 3 : (b <= 8 ? 4 : 5); }
+// 8 residues per thread up to 8-bit passes: 16 registers of values leave room
+// for more resident warps, which hide the root-load and multiply latency
+// better than the fewer exchanges of 16 residues per thread do (config 2,
+// 8+8: 38.9 against 42.4 us); 32 above.
+constexpr int log_e_for(int b) { return b <= 8 ? 3 : 5; }
 // CTAs of 128 threads: strided passes take 8 adjacent columns (64-byte rows
 // of uint64), contiguous passes pack tiles up to 128 threads.  Config 2
 // (32 x 2^16) then runs 1024 CTAs per pass, seven per SM at most, and the

@@ -173,6 +173,10 @@ def test_planner_single_pass_fwht_and_multipass_fft(lib):
     assert blocked and blocked[0]["name"] == "fft-l2-blocked[10+10+10]"
     # blocks of the 2^30 results plus one 64 MiB chunk staging buffer
     assert blocked[0]["workspace_bytes"] == (8 << 30) + (64 << 20)
+    chained = [m for m in ms if m["family"] == "fft-l2-chain"]
+    # the intermediate (aligned up to a 128-byte line: the second pass of a pair drops whole lines of it)
+    assert chained and all(m["workspace_bytes"] == (8 << 30) + 128 for m in chained)
+    assert all(m["passes"][0]["log_h"] == 8 and len(m["passes"]) == 4 for m in chained)
     assert ms[0]["family"] == "fft-stockham-global"  # measured faster (18.6 vs 24.8 ms on a B200)
     # >= 128-byte global runs (the blocked plan's narrow passes take 64-byte runs)
     assert all(p["units_per_cta"] >= 16 for m in ms if m["family"] == "fft-stockham-global" for p in m["passes"])

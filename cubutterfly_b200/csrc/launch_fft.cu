@@ -111,7 +111,7 @@ struct GlobalEntry {
 };
 // Register-direct variants of the same pass (fft.cuh): the first pass of
 // radix >= 2^8, and every pass whose Ns is at least its column count.
-template <int LOGR, bool FIRST, int CW = 0, bool CHUNKED = false>
+template <int LOGR, bool FIRST, int CW = 0>
 struct RegEntry {
     using G = fft::GlobalRegShape<LOGR, CW>;
     static bool eligible(int log_n, int ns_bits, int log_v) {
@@ -126,14 +126,15 @@ struct RegEntry {
         return run(src, dst, log_n, ns_bits, blocks, tw1024, outer, conj_in, conj_out, scale, stream, log_v,
                    outer_shift, fft::RegChunk{0, 0, 0, 0, 0});
     }
-    // `blocks` tiles; a chunk (tiles_per_run != 0) covers part of one transform
+    // `blocks` tiles of the pass (the chained plans run their chunks through
+    // the chain-step kernel of csrc/fft_chain.cu instead)
     static cudaError_t run(const void* src, void* dst, int log_n, int ns_bits, std::size_t blocks,
                            const void* tw1024, const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
                            cudaStream_t stream, int log_v, int outer_shift, const fft::RegChunk& chunk) {
         if constexpr (FIRST && G::T < 16) {
             return cudaErrorInvalidValue;  // never eligible: runs of T < 16 values
         } else {
-        auto kernel = fft::fft_global_reg_kernel<LOGR, FIRST, CW, CHUNKED>;
+        auto kernel = fft::fft_global_reg_kernel<LOGR, FIRST, CW, false>;
         static KernelSetup setup;
         int grid_cap = 0;
         cudaError_t e = setup_kernel(setup, kernel, G::TPB, G::SMEM_BYTES, &grid_cap);
@@ -142,21 +143,12 @@ struct RegEntry {
         if (blocks > 0x7fffffffULL) return cudaErrorInvalidConfiguration;
         fft::OuterTwiddles ot{static_cast<const double2*>(outer.lo), static_cast<const double2*>(outer.hi),
                               outer.split};
-        // an L2-resident source needs no prefetch
-        const unsigned prefetch =
-            !chunk.src_l2 && blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u;
+        const unsigned prefetch = blocks > static_cast<std::size_t>(grid_cap) ? static_cast<unsigned>(grid_cap) : 0u;
         return launch_dependent(kernel, static_cast<unsigned>(blocks), G::TPB, G::SMEM_BYTES, stream,
                                 static_cast<const float2*>(src), static_cast<float2*>(dst), log_n, ns_bits,
                                 static_cast<const float2*>(tw1024), ot, conj_in ? 1 : 0, conj_out ? 1 : 0, scale,
                                 log_v, prefetch, outer_shift, chunk);
         }
-    }
-    static cudaError_t chunk_run(const void* src, void* dst, int log_n, int ns_bits, const void* tw1024,
-                                 const FftOuterTables& outer, bool conj_in, bool conj_out, float scale,
-                                 const FftChunk& c, cudaStream_t stream) {
-        const fft::RegChunk rc{c.base, c.tiles_per_run, c.run_stride, c.src_l2 ? 1 : 0, c.dst_l2 ? 1 : 0};
-        return run(src, dst, log_n, ns_bits, static_cast<std::size_t>(c.tiles_per_run) * c.runs, tw1024, outer,
-                   conj_in, conj_out, scale, stream, 0, 0, rc);
     }
     static LaunchShape shape() {
         LaunchShape s;

@@ -235,6 +235,10 @@ def test_ntt_planner_orders(lib, orders, family, permute):
     assert kinds == (["ntt_pass_strided", "ntt_pass_contiguous"] if family.endswith("ct")
                      else ["ntt_pass_contiguous", "ntt_pass_strided"])
     assert sorted(p["log_h"] for p in m["passes"]) == [8, 8]
+    # 8 residues per thread in passes of up to 8 bits (three register groups, two exchanges): strided
+    # CTAs of 8 columns x 32 threads, contiguous CTAs of 4 tiles x 32 threads
+    assert all(p["elems_per_thread"] == 8 and p["exchanges"] == 2 for p in m["passes"])
+    assert sorted((p["threads"], p["units_per_cta"]) for p in m["passes"]) == [(128, 4), (256, 8)]
 
 
 def test_ntt_planner_lengths_and_words(lib):

@@ -470,13 +470,14 @@ struct GlobalRegMiddle {
     }
 };
 
-// With CHUNKED, a launch covers a chunk of a pass's column tiles (the
-// L2-chained pass pairs of the "fft-l2-chain" plans): tile b of the launch starts at column
-// base + (b mod tiles_per_run) C + (b / tiles_per_run) run_stride of the
-// pass's single transform.  `src_l2`: the source is an intermediate the
-// previous launch left in L2; each 128-byte line is discarded from L2 once
-// the tile holds its values (never written back to HBM).  `dst_l2`: the
-// destination is such an intermediate (stored with an L2 evict-last policy).
+// With CHUNKED, the tiles cover a chunk of a pass's column tiles (the
+// L2-chained pass pairs of the "fft-l2-chain" plans, run by the chain-step
+// kernel of fft_chain.cu): tile b starts at column base + (b mod
+// tiles_per_run) C + (b / tiles_per_run) run_stride of the pass's single
+// transform.  `src_l2`: the source is an intermediate an earlier launch left
+// in L2; each 128-byte line is discarded from L2 once the tile holds its
+// values (never written back to HBM).  `dst_l2`: the destination is such an
+// intermediate (stored with an L2 evict-last policy).
 struct RegChunk {
     uint32_t base;
     uint32_t tiles_per_run;  // 0: every tile of every transform, in order
